@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""Benchmark of the quantised NNUE evaluation hot path on B200.
+
+Workload (one step): the quantised HalfKA NNUE forward of a batch of 65,536
+positions - per position and perspective 2-32 unique active features out of
+11,340, int16 FT of 1024 columns with wraparound, pairwise clipped-ReLU pack
+to 1024 uint8, 16 bucket int8 stacks 1024->16->32->1 - on synthetic inputs
+(SplitMix64 seed 1 + rank for positions, seed 2 for weights).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One JSON line on rank 0.  `value` is device-resident throughput (inputs in HBM,
+L2 flushed between steps); `e2e` is the same metric through the host-buffer C
+ABI call (pinned H2D copy of the step's indices/offsets and D2H of its scores
+inside the timed region).  `--impl reference` times the CPU evaluator (the
+oracle restatement; the Rust reference cannot be built) on all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+BATCH = 65536
+METRIC = "NNUE evals/sec (int8/int16, batch 64K)"
+UNIT = "evals/s"
+WORKLOAD = ("quantized HalfKA NNUE forward: F=11340, int16 FT 11340x1024 shared by 2 perspectives "
+            "(wraparound), 2-32 unique sorted active features per perspective, pairwise clipped-ReLU "
+            "pack to 1024 u8, bucket=(n0-1)/2 of 16 int8 stacks 1024->16->32->1")
+L2_FLUSH_BYTES = 256 << 20
+HBM_FALLBACK_GBS = 6650.0
+# Stack weights and FT bias, read once per batch (16 buckets).
+STACK_BYTES = 16 * (16 * 1024 + 16 * 4 + 32 * 16 + 32 * 4 + 32 + 4) + 2048
+
+
+def algorithmic_bytes(n_positions: int, n_indices: int) -> int:
+    """Bytes one forward must move: every gathered FT row (2 KB) once per use,
+    the uint16 indices, the uint32 offsets, the int32 scores, and the stack
+    weights once per batch."""
+    return n_indices * 2048 + n_indices * 2 + (2 * n_positions + 1) * 4 + n_positions * 4 + STACK_BYTES
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_hbm_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return HBM_FALLBACK_GBS, "fallback"
+
+
+def committed_traffic():
+    """DRAM bytes per launch of the evaluation kernel from the committed ncu
+    summary (profiles/q_eval_kernel.json), scaled to a 65,536-position launch."""
+    path = os.path.join(ROOT, "profiles", "q_eval_kernel.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return int(d["dram_bytes_per_launch_65536"])
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU evaluator on all host threads
+# ---------------------------------------------------------------------------
+def cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def cpu_time_batches(w, pos, threads: int, min_seconds: float, min_reps: int):
+    import oracle
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        st, _ = oracle.q_forward_mt(w, pos, threads)
+        if st != 0:
+            raise RuntimeError(f"oracle status {st}")
+        reps += 1
+        el = time.perf_counter() - t0
+        if reps >= min_reps and el >= min_seconds:
+            return reps, el
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    from chineseai_b200 import synth
+    threads = cpu_threads()
+    w = synth.quantized_weights(2)
+    pos = synth.positions(BATCH, 1)
+    cpu_time_batches(w, pos, threads, 0.0, max(args.warmup, 1))
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        import oracle
+        st, _ = oracle.q_forward_mt(w, pos, threads)
+        times.append(time.perf_counter() - t0)
+        assert st == 0
+    ms = 1e3 * sum(times) / len(times)
+    value = BATCH / (ms / 1e3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": BATCH, "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"full {BATCH}-position batch per step, {threads} OpenMP threads, "
+                                   f"CPU {cpu_cpu_model()}"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import ctypes as C
+
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    from chineseai_b200 import synth
+    from chineseai_b200._lib import check, lib
+    from chineseai_b200.quantized import QuantizedNnue, as_device
+
+    L = lib()
+    w = synth.quantized_weights(2)
+    model = QuantizedNnue(w, device=local)
+    pos = synth.positions(BATCH, 1 + rank)
+    n_idx = len(pos.indices)
+    idx = as_device(pos.indices, dev)
+    off = as_device(pos.offsets, dev)
+    scores = torch.empty(BATCH, dtype=torch.int32, device=dev)
+    ws = model.workspace(BATCH)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    h = model.handle
+
+    def step():
+        check(L.cnnue_q_bucket_sort(h, off.data_ptr(), n_idx, BATCH, ws.data_ptr(), ws.numel(), sp), "sort")
+        mid = torch.cuda.Event(enable_timing=True)
+        mid.record(stream)
+        check(L.cnnue_q_forward_sorted(h, idx.data_ptr(), n_idx, off.data_ptr(), BATCH, scores.data_ptr(),
+                                       ws.data_ptr(), ws.numel(), sp), "forward")
+        return mid
+
+    # correctness of the timed configuration, once, before timing
+    for _ in range(max(args.warmup, 3)):
+        flush.fill_(rank + 1)
+        step()
+    torch.cuda.synchronize(dev)
+    st = C.c_int(0)
+    check(L.cnnue_read_status(ws.data_ptr(), sp, C.byref(st)), "status")
+    check(st.value, "kernel status")
+
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    starts, mids, ends = [], [], []
+    for _ in range(args.steps):
+        flush.fill_(1)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        m = step()
+        e.record(stream)
+        starts.append(s)
+        mids.append(m)
+        ends.append(e)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    kern_ms = [m.elapsed_time(e) for m, e in zip(mids, ends)]
+    total_ms = sum(step_ms)
+    kern_avg = sum(kern_ms) / len(kern_ms)
+
+    # ---- e2e through the host-buffer C ABI call -----------------------------
+    h_idx = torch.empty(n_idx, dtype=torch.int16, pin_memory=True).numpy().view(np.uint16)
+    h_off = torch.empty(len(pos.offsets), dtype=torch.int32, pin_memory=True).numpy().view(np.uint32)
+    h_out = torch.empty(BATCH, dtype=torch.int32, pin_memory=True).numpy()
+    h_idx[:] = pos.indices
+    h_off[:] = pos.offsets
+    for _ in range(max(args.warmup, 3)):
+        model.forward_host(h_idx, h_off, h_out, stream=stream)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.fill_(2)
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        model.forward_host(h_idx, h_off, h_out, stream=stream)  # synchronises the stream
+        e.record(stream)
+        e.synchronize()
+        e2e_ms.append(s.elapsed_time(e))
+    e2e_avg = sum(e2e_ms) / len(e2e_ms)
+    ok = bool(np.array_equal(h_out, scores.cpu().numpy()))
+
+    # ---- max over ranks --------------------------------------------------------
+    stats = torch.tensor([total_ms, kern_avg, e2e_avg, 0.0 if ok else 1.0], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total_ms, kern_avg, e2e_avg, bad = stats.tolist()
+    if bad:
+        raise RuntimeError("host-buffer scores differ from device-resident scores")
+
+    if rank == 0:
+        ms_per_step = total_ms / args.steps
+        value = world * BATCH / (ms_per_step / 1e3)
+        peak, peak_kind = measured_hbm_peak()
+        alg = algorithmic_bytes(BATCH, n_idx)
+        achieved = alg / (kern_avg / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": BATCH, "global_batch": world * BATCH,
+                       "l2": "flushed between steps (256 MiB write)",
+                       "parallelism": f"dp{world} (independent batches, no collective)"},
+            "e2e": {"value": world * BATCH / (e2e_avg / 1e3), "unit": UNIT,
+                    "h2d_bytes_per_step": int(h_idx.nbytes + h_off.nbytes), "d2h_bytes_per_step": int(h_out.nbytes)},
+            "gpu_launches": 3 * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "q_eval_kernel", "achieved": achieved, "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": committed_traffic(), "algorithmic_bytes_per_launch": alg,
+                         "kernel_ms": kern_avg},
+            "clocks": clocks,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            from chineseai_b200 import synth as _s  # noqa: F401
+            threads = cpu_threads()
+            reps, el = cpu_time_batches(w, pos, threads, args.cpu_seconds, 2)
+            line["cpu_baseline"] = {"value": reps * BATCH / el, "unit": UNIT, "cores": threads, "kind": "port",
+                                    "sample": f"{reps} x full {BATCH}-position batch, {threads} OpenMP threads, "
+                                              f"{el:.1f} s, CPU {cpu_cpu_model()}"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,106 @@
+"""ctypes binding of libcnnue.so (the C ABI declared in include/cnnue.h).
+
+The library is loaded from the package directory only.  When it is missing the
+import fails loudly: there is no CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libcnnue.so")
+
+c_void_p = C.c_void_p
+c_int = C.c_int
+c_i64 = C.c_int64
+c_u32 = C.c_uint32
+c_u64 = C.c_uint64
+c_size = C.c_size_t
+P = C.c_void_p  # every buffer crosses the ABI as a plain pointer
+
+
+class QWeights(C.Structure):
+    _fields_ = [(n, c_void_p) for n in (
+        "ft_weight", "ft_bias", "l1_weight", "l1_bias", "l2_weight", "l2_bias", "l3_weight", "l3_bias")]
+
+
+class FWeights(C.Structure):
+    _fields_ = [(n, c_void_p) for n in (
+        "ft_weight", "ft_bias", "l1_weight", "l1_bias", "l2_weight", "l2_bias", "l3_weight", "l3_bias")]
+
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "cnnue_status_string": (C.c_char_p, [c_int]),
+    "cnnue_last_error": (C.c_char_p, []),
+    "cnnue_version": (C.c_char_p, []),
+    "cnnue_q_model_create": (c_int, [C.POINTER(QWeights), c_int, C.POINTER(c_void_p)]),
+    "cnnue_q_model_destroy": (c_int, [c_void_p]),
+    "cnnue_q_workspace_bytes": (c_size, [c_i64]),
+    "cnnue_read_status": (c_int, [P, P, C.POINTER(c_int)]),
+    "cnnue_q_forward": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_q_bucket_sort": (c_int, [c_void_p, P, c_u32, c_i64, P, c_size, P]),
+    "cnnue_q_forward_sorted": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_q_forward_host": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P]),
+    "cnnue_q_forward_acc": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, P, c_size, P]),
+    "cnnue_q_update": (c_int, [c_void_p, P, P, P, c_u32, P, P, c_u32, P, P, c_i64, P, P, P,
+                               c_size, P]),
+    "cnnue_f_model_create": (c_int, [C.POINTER(FWeights), c_int, C.POINTER(c_void_p)]),
+    "cnnue_f_model_destroy": (c_int, [c_void_p]),
+    "cnnue_f_forward": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_feature_pool_fwd": (c_int, [P, P, c_i64, c_i64, c_i64, P, P, P]),
+    "cnnue_feature_pool_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64]),
+    "cnnue_feature_pool_bwd": (c_int, [P, P, c_i64, c_i64, c_i64, P, P, c_size, P]),
+    "cnnue_sparse_pool_fwd": (c_int, [P, c_i64, P, c_i64, c_i64, c_i64, P, P, P]),
+    "cnnue_sparse_pool_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64]),
+    "cnnue_sparse_pool_bwd": (c_int, [P, P, c_i64, c_i64, c_i64, c_i64, P, P, c_size, P]),
+    "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),
+    "cnnue_synth_positions": (c_int, [c_u64, c_i64, c_u32, c_u32, c_u32, P, P, C.POINTER(c_u32)]),
+    "cnnue_synth_q_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),
+    "cnnue_synth_f_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),
+    "cnnue_synth_q_update": (c_int, [c_u64, c_i64, P, P, P, P, C.POINTER(c_u32), P, P,
+                                     C.POINTER(c_u32), P]),
+}
+
+_lib = None
+
+
+class CnnueError(RuntimeError):
+    def __init__(self, status: int, where: str, detail: str = ""):
+        self.status = status
+        msg = f"{where}: {status_string(status)}"
+        if detail:
+            msg += f" ({detail})"
+        super().__init__(msg)
+
+
+def lib() -> C.CDLL:
+    """Loads libcnnue.so (once) and declares every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python -m chineseai_b200.build` "
+            "(the evaluator has no CPU fallback)")
+    handle = C.CDLL(LIB_PATH)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = handle
+    return handle
+
+
+def status_string(status: int) -> str:
+    return lib().cnnue_status_string(status).decode()
+
+
+def last_error() -> str:
+    return lib().cnnue_last_error().decode()
+
+
+def check(status: int, where: str) -> None:
+    if status != 0:
+        raise CnnueError(status, where, last_error())

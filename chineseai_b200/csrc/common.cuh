@@ -1,0 +1,95 @@
+// common.cuh - shared helpers of the cnnue library (status handling, device
+// loads, workspace layout).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stddef.h>
+
+#include "../../include/cnnue.h"
+
+namespace cnnue {
+
+// Sets the calling thread's last-error text and returns `status`.
+int set_error(int status, const char* fmt, ...);
+
+// Maps a CUDA error to CNNUE_ERR_CUDA with the runtime's message.
+int cuda_error(cudaError_t err, const char* what);
+
+#define CNNUE_CUDA_TRY(expr)                                       \
+  do {                                                             \
+    cudaError_t err__ = (expr);                                    \
+    if (err__ != cudaSuccess) return ::cnnue::cuda_error(err__, #expr); \
+  } while (0)
+
+// Checks that `device` is the current device, switching to it if needed.
+int use_device(int device);
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Workspace header shared by every entry point that takes a workspace.
+// The status word is the first 4 bytes; kernels OR CNNUE_STATUS_* bits in.
+struct WorkspaceHeader {
+  uint32_t status;
+  uint32_t pad0[31];
+  uint32_t counts[32];   // per-bucket position counts
+  uint32_t cursors[32];  // per-bucket scatter cursors
+  uint32_t pad1[32];
+};
+static_assert(sizeof(WorkspaceHeader) == 512, "header size");
+
+// Bucket-sort workspace: header, then bucket_of[n] (u8), perm[n] (u32),
+// sorted_bucket[n] (u8), each 256-byte aligned.
+struct WorkspaceView {
+  WorkspaceHeader* hdr;
+  uint8_t* bucket_of;      // [n]
+  uint32_t* perm;          // [n] positions in bucket order
+  uint8_t* sorted_bucket;  // [n] bucket of perm[i]
+};
+size_t bucket_workspace_bytes(int64_t n);
+WorkspaceView carve_workspace(void* ws, int64_t n);
+// Zeroes the header, then buckets the n positions (bucket = min((max(n0,1)-1)
+// >> shift, n_buckets-1), n0 from the offsets or from d_count0) and scatters
+// them into bucket order.  Offsets are validated into the status word.
+int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
+                       int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s);
+// ORs CNNUE_STATUS_BAD_OFFSETS into the workspace status when a CSR offsets
+// array of n_lists lists is not monotone or runs past n_values.
+int launch_offsets_check(const uint32_t* d_offsets, uint32_t n_values, int64_t n_lists, void* ws,
+                         cudaStream_t s);
+
+// RAII switch to a device, restoring the caller's current device.
+struct DeviceGuard {
+  int prev = -1;
+  bool switched = false;
+  int status = CNNUE_OK;
+  explicit DeviceGuard(int device);
+  ~DeviceGuard();
+};
+
+int check_launch_error(const char* what);
+
+// Streaming 16-byte load that bypasses L1 allocation (rows are read once per
+// position; L1 is kept for the per-bucket stack weights).
+__device__ __forceinline__ uint4 ldg_stream16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float4 ldg_stream16f(const void* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Named barrier over `nthreads` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+}  // namespace cnnue

@@ -1,0 +1,83 @@
+"""The AZ-NNUE trunk feature pool and the plain table pool (over the C ABI).
+
+`feature_pool` / `feature_pool_backward` take the roles of the reference's
+Candle ops feature_pool and FeaturePoolGrad (src/az/fused_feature_pool.rs:
+134-148, 214-223); `sparse_pool` / `sparse_pool_backward` those of
+sparse_pool / SparsePoolGrad (:150-163, :276-282).  Items use the reference's
+packing: feature | us_bucket << 11 | them_bucket << 15, 0xffffffff = padding.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import torch
+
+from ._lib import check, lib
+from .quantized import _stream_ptr
+
+POOL_ROWS = 1545
+PADDING_ITEM = 0xFFFFFFFF
+
+
+def pack_feature(feature: int, us_bucket: int, them_bucket: int) -> int:
+    return feature | (us_bucket << 11) | (them_bucket << 15)
+
+
+def _read_word(word: torch.Tensor, stream=None) -> int:
+    st = C.c_int(0)
+    check(lib().cnnue_read_status(word.data_ptr(), _stream_ptr(stream), C.byref(st)), "cnnue_read_status")
+    return st.value
+
+
+def feature_pool(tables: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
+    """tables f32 [1545, H] (cuda), items [B, I] 4-byte (cuda) -> f32 [B, H]."""
+    rows, hidden = tables.shape
+    if rows != POOL_ROWS:
+        raise ValueError(f"feature pool row mismatch: got {rows}, expected {POOL_ROWS}")
+    batch, item_count = items.shape
+    out = torch.empty((batch, hidden), dtype=torch.float32, device=tables.device)
+    status = torch.zeros(64, dtype=torch.int32, device=tables.device)
+    check(lib().cnnue_feature_pool_fwd(tables.data_ptr(), items.data_ptr(), batch, item_count, hidden,
+                                       out.data_ptr(), status.data_ptr(), _stream_ptr(stream)),
+          "cnnue_feature_pool_fwd")
+    check(_read_word(status, stream), "cnnue_feature_pool_fwd (kernel status)")
+    return out
+
+
+def feature_pool_backward(items: torch.Tensor, grad_out: torch.Tensor, stream=None) -> torch.Tensor:
+    """Gradient of feature_pool w.r.t. the tables: f32 [1545, H]."""
+    batch, item_count = items.shape
+    hidden = grad_out.shape[1]
+    grad = torch.empty((POOL_ROWS, hidden), dtype=torch.float32, device=grad_out.device)
+    nbytes = int(lib().cnnue_feature_pool_bwd_workspace_bytes(batch, item_count, hidden))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=grad_out.device)
+    check(lib().cnnue_feature_pool_bwd(items.data_ptr(), grad_out.data_ptr(), batch, item_count, hidden,
+                                       grad.data_ptr(), ws.data_ptr(), nbytes, _stream_ptr(stream)),
+          "cnnue_feature_pool_bwd")
+    check(_read_word(ws, stream), "cnnue_feature_pool_bwd (kernel status)")
+    return grad
+
+
+def sparse_pool(table: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
+    rows, hidden = table.shape
+    batch, item_count = items.shape
+    out = torch.empty((batch, hidden), dtype=torch.float32, device=table.device)
+    status = torch.zeros(64, dtype=torch.int32, device=table.device)
+    check(lib().cnnue_sparse_pool_fwd(table.data_ptr(), rows, items.data_ptr(), batch, item_count, hidden,
+                                      out.data_ptr(), status.data_ptr(), _stream_ptr(stream)),
+          "cnnue_sparse_pool_fwd")
+    check(_read_word(status, stream), "cnnue_sparse_pool_fwd (kernel status)")
+    return out
+
+
+def sparse_pool_backward(items: torch.Tensor, grad_out: torch.Tensor, rows: int, stream=None) -> torch.Tensor:
+    batch, item_count = items.shape
+    hidden = grad_out.shape[1]
+    grad = torch.empty((rows, hidden), dtype=torch.float32, device=grad_out.device)
+    nbytes = int(lib().cnnue_sparse_pool_bwd_workspace_bytes(rows, batch, item_count, hidden))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=grad_out.device)
+    check(lib().cnnue_sparse_pool_bwd(items.data_ptr(), grad_out.data_ptr(), rows, batch, item_count, hidden,
+                                      grad.data_ptr(), ws.data_ptr(), nbytes, _stream_ptr(stream)),
+          "cnnue_sparse_pool_bwd")
+    check(_read_word(ws, stream), "cnnue_sparse_pool_bwd (kernel status)")
+    return grad

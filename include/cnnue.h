@@ -1,0 +1,263 @@
+/*
+ * cnnue.h - C ABI of the B200 (sm_100a) NNUE evaluation library.
+ *
+ * Every entry point returns an int status (CNNUE_OK == 0).  Nothing aborts.
+ * Device buffers are caller-owned device pointers; `stream` is a cudaStream_t
+ * passed as void* (NULL = the legacy default stream).  Entry points that take
+ * device buffers only enqueue work: kernel-side faults in the data (an index
+ * out of range, non-monotone offsets) are recorded in a status word inside the
+ * caller's workspace and reported by cnnue_read_status().  Entry points that
+ * take host buffers synchronise the stream and return that status directly.
+ *
+ * The reference (mycve/chineseai, Rust) has no FFI.  Each function below names
+ * the reference function or Candle custom op it replaces (path:line within the
+ * reference project).  The quantised HalfKA evaluator (cnnue_q_*) and the fp32
+ * HalfKA evaluator (cnnue_f32_*) implement the workload specification the
+ * reference's evaluator API is measured on; their reference anchors are the
+ * evaluator entry points whose role they take.
+ */
+#ifndef CNNUE_H
+#define CNNUE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+enum {
+  CNNUE_OK = 0,
+  CNNUE_ERR_INVALID_ARG = 1,  /* null pointer, negative size, bad enum       */
+  CNNUE_ERR_BAD_INDEX = 2,    /* a feature index >= the feature count        */
+  CNNUE_ERR_BAD_OFFSETS = 3,  /* offsets not monotone or beyond the indices  */
+  CNNUE_ERR_CUDA = 4,         /* a CUDA runtime call failed                  */
+  CNNUE_ERR_WORKSPACE = 5,    /* workspace smaller than cnnue_*_workspace_bytes */
+  CNNUE_ERR_FORMAT = 6,       /* weight file: wrong format tag or tensor size */
+  CNNUE_ERR_IO = 7,           /* weight file cannot be read or written       */
+  CNNUE_ERR_NO_DEVICE = 8,    /* no CUDA device / wrong device ordinal       */
+  CNNUE_ERR_TIMEOUT = 9       /* a bounded device-side wait gave up          */
+};
+
+/* Status bits written by kernels into the workspace status word. */
+#define CNNUE_STATUS_BAD_INDEX 0x1u
+#define CNNUE_STATUS_BAD_OFFSETS 0x2u
+
+const char* cnnue_status_string(int status);
+/* Detail of the last error raised on the calling thread ("" if none). */
+const char* cnnue_last_error(void);
+/* Library version, e.g. "0.1.0". */
+const char* cnnue_version(void);
+
+/* ---- dimensions of the quantised HalfKA network ------------------------ */
+#define CNNUE_Q_FEATURES 11340   /* 9 king squares x 14 piece kinds x 90 squares */
+#define CNNUE_Q_COLS 1024        /* int16 FT columns per perspective            */
+#define CNNUE_Q_HALF 512         /* pairwise pack: column j pairs with j + 512  */
+#define CNNUE_Q_PACKED 1024      /* 2 perspectives x 512 uint8                  */
+#define CNNUE_Q_BUCKETS 16
+#define CNNUE_Q_L1 16
+#define CNNUE_Q_L2 32
+
+/* Host-side weights of the quantised network (all row-major, contiguous).
+ *   ft_weight [11340][1024] int16     ft_bias  [1024] int16
+ *   l1_weight [16][16][1024] int8     l1_bias  [16][16] int32
+ *   l2_weight [16][32][16] int8       l2_bias  [16][32] int32
+ *   l3_weight [16][32] int8           l3_bias  [16] int32
+ * One FT table serves both perspectives. */
+typedef struct cnnue_q_weights {
+  const int16_t* ft_weight;
+  const int16_t* ft_bias;
+  const int8_t* l1_weight;
+  const int32_t* l1_bias;
+  const int8_t* l2_weight;
+  const int32_t* l2_bias;
+  const int8_t* l3_weight;
+  const int32_t* l3_bias;
+} cnnue_q_weights;
+
+typedef struct cnnue_q_model cnnue_q_model;
+
+/* Uploads the weights to `device` and returns a model handle.
+ * Replaces AzNnue::load / AzNnue::random as the evaluator constructor
+ * (src/az.rs:1433-1529): the model owns its device copy of the weights and is
+ * shared read-only by every caller thread. */
+int cnnue_q_model_create(const cnnue_q_weights* weights, int device, cnnue_q_model** out);
+int cnnue_q_model_destroy(cnnue_q_model* model);
+
+/* Bytes of device workspace cnnue_q_forward / cnnue_q_update need for
+ * `n_positions` positions (bucket sort + status word). */
+size_t cnnue_q_workspace_bytes(int64_t n_positions);
+
+/* Reads and clears the status word of a workspace after the work queued on
+ * `stream` has finished (synchronises `stream`).  *status_out receives a
+ * CNNUE_ERR_* code (CNNUE_OK when the kernels saw valid data). */
+int cnnue_read_status(void* d_workspace, void* stream, int* status_out);
+
+/* Full quantised forward of a batch: for every position and perspective the
+ * FT gather-accumulate (int16 wraparound), the pairwise clipped-ReLU pack to
+ * uint8, the bucket selection by the perspective-0 active count and the int8
+ * bucket stack 1024->16->32->1.  Replaces the evaluator entry point
+ * AzNnue::evaluate_with_scratch_output (src/az.rs:1562-1604) and its FT gather
+ * input_embedding_linear_into_slice (src/az.rs:2049-2076).
+ *   d_indices  [n_indices] uint16 feature indices (< 11340)
+ *   d_offsets  [2*n_positions+1] uint32; perspective s of position p owns
+ *              d_indices[d_offsets[2p+s] .. d_offsets[2p+s+1])
+ *   d_scores   [n_positions] int32 output
+ * Two stages, also callable separately: cnnue_q_bucket_sort (groups positions
+ * by bucket into the workspace) and cnnue_q_forward_sorted (the fused
+ * gather/pack/stack kernel over the sorted order). */
+int cnnue_q_forward(const cnnue_q_model* model, const uint16_t* d_indices, uint32_t n_indices,
+                    const uint32_t* d_offsets, int64_t n_positions, int32_t* d_scores,
+                    void* d_workspace, size_t workspace_bytes, void* stream);
+int cnnue_q_bucket_sort(const cnnue_q_model* model, const uint32_t* d_offsets, uint32_t n_indices,
+                        int64_t n_positions, void* d_workspace, size_t workspace_bytes,
+                        void* stream);
+int cnnue_q_forward_sorted(const cnnue_q_model* model, const uint16_t* d_indices,
+                           uint32_t n_indices, const uint32_t* d_offsets, int64_t n_positions,
+                           int32_t* d_scores, void* d_workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Same as cnnue_q_forward with HOST buffers: copies the inputs to the device,
+ * runs the forward and copies the scores back, then synchronises `stream`
+ * and returns the kernels' status.  The model keeps device staging buffers
+ * that grow to the largest batch seen (not thread-safe per model). */
+int cnnue_q_forward_host(cnnue_q_model* model, const uint16_t* h_indices, uint32_t n_indices,
+                         const uint32_t* h_offsets, int64_t n_positions, int32_t* h_scores,
+                         void* stream);
+
+/* Optional: also write the int16 accumulators [n_positions][2][1024] of the
+ * forward (d_acc may be NULL).  Used to check the gather separately. */
+int cnnue_q_forward_acc(const cnnue_q_model* model, const uint16_t* d_indices, uint32_t n_indices,
+                        const uint32_t* d_offsets, int64_t n_positions, int32_t* d_scores,
+                        int16_t* d_acc, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Incremental accumulator update followed by the same pack + bucket stack.
+ * Replaces AzEvalAccumulator::apply_transition_for_perspective
+ * (src/az.rs:439-485) for the quantised network: per perspective either
+ * child = parent - sum(removed rows) + sum(added rows), or, when the
+ * perspective's refresh flag is set (a king move), child = bias + sum(added
+ * rows) with `added` holding the full active list.
+ *   d_parent       [n][2][1024] int16      d_child [n][2][1024] int16 (out)
+ *   d_flags        [2n] uint8, bit 0 = refresh perspective (p, s) at 2p+s
+ *   d_rem_offsets  [2n+1] uint32 into d_rem (uint16)
+ *   d_add_offsets  [2n+1] uint32 into d_add (uint16)
+ *   d_count0       [n] uint8: the child's perspective-0 active count (bucket)
+ *   d_scores       [n] int32 (out) */
+int cnnue_q_update(const cnnue_q_model* model, const int16_t* d_parent, const uint8_t* d_flags,
+                   const uint16_t* d_rem, uint32_t n_rem, const uint32_t* d_rem_offsets,
+                   const uint16_t* d_add, uint32_t n_add, const uint32_t* d_add_offsets,
+                   const uint8_t* d_count0, int64_t n_positions, int16_t* d_child,
+                   int32_t* d_scores, void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ---- fp32 HalfKA network ------------------------------------------------ */
+#define CNNUE_F_FEATURES 11340
+#define CNNUE_F_COLS 256         /* fp32 FT columns per perspective */
+#define CNNUE_F_BUCKETS 8
+/* ft_weight [11340][256], ft_bias [256], l1_weight [8][16][512], l1_bias [8][16],
+ * l2_weight [8][32][16], l2_bias [8][32], l3_weight [8][32], l3_bias [8]. */
+typedef struct cnnue_f_weights {
+  const float* ft_weight;
+  const float* ft_bias;
+  const float* l1_weight;
+  const float* l1_bias;
+  const float* l2_weight;
+  const float* l2_bias;
+  const float* l3_weight;
+  const float* l3_bias;
+} cnnue_f_weights;
+
+typedef struct cnnue_f_model cnnue_f_model;
+int cnnue_f_model_create(const cnnue_f_weights* weights, int device, cnnue_f_model** out);
+int cnnue_f_model_destroy(cnnue_f_model* model);
+/* fp32 forward: FT sum (bias + rows in index order), clipped ReLU [0,1] on the
+ * concatenated 512, bucket = (n0-1)/4 (8 buckets), stack 512->16->32->1 with
+ * clipped ReLU between layers.  Same index/offset layout as cnnue_q_forward.
+ * Replaces the fp32 evaluator path input_embedding_linear_into_slice +
+ * value head (src/az.rs:2049-2076, src/az.rs:2133-2157). */
+int cnnue_f_forward(const cnnue_f_model* model, const uint16_t* d_indices, uint32_t n_indices,
+                    const uint32_t* d_offsets, int64_t n_positions, float* d_out,
+                    void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ---- reference-native feature pool (AZ-NNUE trunk FT) ------------------- */
+#define CNNUE_POOL_ROWS 1545     /* 1260 piece-square + 14 piece + 10 rank + 9 file + 252 king-piece */
+#define CNNUE_POOL_PADDING 0xffffffffu
+
+/* out[b][h] = sum over the non-padding items of row b of the six table rows of
+ * the item (feature, 1260+piece, 1274+rank, 1284+file, 1293+us*14+piece,
+ * 1293+(9+them)*14+piece), summed from 0 in item order, rows in that order.
+ * Item = feature | us_bucket << 11 | them_bucket << 15, 0xffffffff = padding.
+ * An item with a row past the table is skipped and CNNUE_STATUS_BAD_INDEX is
+ * ORed into *d_status (a device word the caller zeroes and reads).
+ * Replaces the Candle op feature_pool / kernel feature_pool_fwd
+ * (src/az/fused_feature_pool.rs:22-49, :134-148, CPU twin :169-198). */
+int cnnue_feature_pool_fwd(const float* d_tables, const uint32_t* d_items, int64_t batch,
+                           int64_t item_count, int64_t hidden, float* d_out, uint32_t* d_status,
+                           void* stream);
+
+/* grad_tables[r][h] = sum of grad_out[b][h] over every (b, item, slot) whose
+ * slot row is r, without atomics: a stable counting sort of the contributions
+ * by row, then a segmented reduction in that order (rows with at most 256
+ * contributions are summed in exactly the reference CPU order; longer rows in
+ * 256-contribution segments combined in order).  Deterministic run to run.
+ * Every row of grad_tables is written.  The workspace's first word is the
+ * status word (read it with cnnue_read_status).
+ * Replaces FeaturePoolGrad / kernel feature_pool_grad
+ * (src/az/fused_feature_pool.rs:51-76, :214-223, CPU twin :231-260). */
+size_t cnnue_feature_pool_bwd_workspace_bytes(int64_t batch, int64_t item_count, int64_t hidden);
+int cnnue_feature_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int64_t batch,
+                           int64_t item_count, int64_t hidden, float* d_grad_tables,
+                           void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* Plain table pool: out[b][h] = sum of table[item][h] over the non-padding
+ * items of row b, in item order (rows >= `rows` are skipped and flagged).
+ * Replaces SparsePool / kernel sparse_pool_fwd
+ * (src/az/fused_feature_pool.rs:78-92, CPU twin :284-309). */
+int cnnue_sparse_pool_fwd(const float* d_table, int64_t rows, const uint32_t* d_items,
+                          int64_t batch, int64_t item_count, int64_t hidden, float* d_out,
+                          uint32_t* d_status, void* stream);
+/* Atomic-free backward of the plain pool (same scheme as the feature pool;
+ * tables up to 16384 rows).  Replaces SparsePoolGrad / kernel sparse_pool_grad
+ * (src/az/fused_feature_pool.rs:94-106, CPU twin :342-370). */
+size_t cnnue_sparse_pool_bwd_workspace_bytes(int64_t rows, int64_t batch, int64_t item_count,
+                                             int64_t hidden);
+int cnnue_sparse_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int64_t rows,
+                          int64_t batch, int64_t item_count, int64_t hidden, float* d_grad_table,
+                          void* d_workspace, size_t workspace_bytes, void* stream);
+
+/* ---- deterministic synthetic workloads (host) --------------------------- */
+/* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is
+ * replaced by the mixed output at every draw. */
+uint64_t cnnue_splitmix64_next(uint64_t* state);
+
+/* Positions: per position and perspective a count n uniform in
+ * [min_active, max_active] and n unique indices uniform in [0, n_features),
+ * sorted ascending.  Writes at most 2*n_positions*max_active indices and
+ * 2*n_positions+1 offsets; returns the index count through *n_indices. */
+int cnnue_synth_positions(uint64_t seed, int64_t n_positions, uint32_t n_features,
+                          uint32_t min_active, uint32_t max_active, uint16_t* h_indices,
+                          uint32_t* h_offsets, uint32_t* n_indices);
+/* Quantised weights from seed: FT uniform in [-127,127], FT bias in [-64,64],
+ * stack weights uniform in [-64,64], stack biases in [-64,64]; the arrays
+ * must have the sizes of cnnue_q_weights. */
+int cnnue_synth_q_weights(uint64_t seed, int16_t* ft_weight, int16_t* ft_bias, int8_t* l1_weight,
+                          int32_t* l1_bias, int8_t* l2_weight, int32_t* l2_bias,
+                          int8_t* l3_weight, int32_t* l3_bias);
+/* fp32 weights: FT N(0, 0.01), FT bias 0, stack N(0, 0.05), stack biases 0
+ * (Box-Muller over the SplitMix64 stream). */
+int cnnue_synth_f_weights(uint64_t seed, float* ft_weight, float* ft_bias, float* l1_weight,
+                          float* l1_bias, float* l2_weight, float* l2_bias, float* l3_weight,
+                          float* l3_bias);
+/* Incremental-update workload: parents uniform in [-2000,2000]; per
+ * perspective 1-2 removed and 1-3 added indices, or with probability 1/20 a
+ * refresh with 2-32 fresh unique sorted indices; child perspective-0 count.
+ * Capacities: h_rem 4n, h_add 64n. */
+int cnnue_synth_q_update(uint64_t seed, int64_t n_positions, int16_t* h_parent, uint8_t* h_flags,
+                         uint16_t* h_rem, uint32_t* h_rem_offsets, uint32_t* n_rem,
+                         uint16_t* h_add, uint32_t* h_add_offsets, uint32_t* n_add,
+                         uint8_t* h_count0);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CNNUE_H */

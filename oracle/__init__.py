@@ -1,0 +1,136 @@
+"""CPU oracle of the NNUE hot path - TEST INFRASTRUCTURE ONLY.
+
+ctypes wrapper of oracle/liboracle.so (built from cnnue_oracle.c by
+oracle/Makefile).  Only tests/, the smoke check and bench.py's CPU-baseline
+leg use it, always as the checker; the product library never calls it.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "liboracle.so")
+
+_lib = None
+
+
+def build() -> str:
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB_PATH
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH) or (
+                os.path.getmtime(os.path.join(HERE, "cnnue_oracle.c")) > os.path.getmtime(LIB_PATH)):
+            build()
+        h = C.CDLL(LIB_PATH)
+        P, i64, u32, i32 = C.c_void_p, C.c_int64, C.c_uint32, C.c_int
+        h.oracle_q_forward.argtypes = [P] * 9 + [u32, P, i64, P, P]
+        h.oracle_q_forward_mt.argtypes = [P] * 9 + [u32, P, i64, P, i32]
+        h.oracle_q_update.argtypes = [P] * 10 + [P, u32, P, P, u32, P, P, i64, P, P, i32]
+        h.oracle_f_forward.argtypes = [P] * 9 + [u32, P, i64, P, P]
+        h.oracle_feature_pool_fwd.argtypes = [P, P, i64, i64, i64, P]
+        h.oracle_feature_pool_bwd.argtypes = [P, P, i64, i64, i64, P]
+        h.oracle_sparse_pool_fwd.argtypes = [P, i64, P, i64, i64, i64, P]
+        h.oracle_sparse_pool_bwd.argtypes = [P, P, i64, i64, i64, i64, P]
+        h.oracle_q_bucket.argtypes = [u32]
+        h.oracle_f_bucket.argtypes = [u32]
+        for name in ("oracle_q_forward", "oracle_q_forward_mt", "oracle_q_update", "oracle_f_forward",
+                     "oracle_feature_pool_fwd", "oracle_feature_pool_bwd", "oracle_sparse_pool_fwd",
+                     "oracle_sparse_pool_bwd", "oracle_q_bucket", "oracle_f_bucket",
+                     "oracle_max_threads"):
+            getattr(h, name).restype = C.c_int
+        _lib = h
+    return _lib
+
+
+def _p(a: np.ndarray) -> int:
+    assert a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data
+
+
+def q_forward(w, pos, with_acc: bool = False):
+    """Quantised forward -> (status, scores int32[n], acc int16[n,2,1024] | None)."""
+    n = pos.n
+    scores = np.zeros(max(n, 1), np.int32)
+    acc = np.zeros((max(n, 1), 2, 1024), np.int16) if with_acc else None
+    arrs = w.arrays()
+    idx = pos.indices if len(pos.indices) else np.zeros(1, np.uint16)
+    st = lib().oracle_q_forward(*[_p(a) for a in arrs], _p(idx), len(pos.indices), _p(pos.offsets), n,
+                                _p(scores), _p(acc) if with_acc else None)
+    return st, scores[:n], (acc[:n] if with_acc else None)
+
+
+def q_forward_mt(w, pos, n_threads: int = 0):
+    n = pos.n
+    scores = np.zeros(max(n, 1), np.int32)
+    st = lib().oracle_q_forward_mt(*[_p(a) for a in w.arrays()], _p(pos.indices), len(pos.indices),
+                                   _p(pos.offsets), n, _p(scores), n_threads)
+    return st, scores[:n]
+
+
+def q_update(w, batch, n_threads: int = 1):
+    n = batch.n
+    child = np.zeros((max(n, 1), 2, 1024), np.int16)
+    scores = np.zeros(max(n, 1), np.int32)
+    rem = batch.rem if len(batch.rem) else np.zeros(1, np.uint16)
+    add = batch.add if len(batch.add) else np.zeros(1, np.uint16)
+    st = lib().oracle_q_update(*[_p(a) for a in w.arrays()], _p(batch.parent), _p(batch.flags), _p(rem),
+                               len(batch.rem), _p(batch.rem_offsets), _p(add), len(batch.add),
+                               _p(batch.add_offsets), _p(batch.count0), n, _p(child), _p(scores),
+                               n_threads)
+    return st, child[:n], scores[:n]
+
+
+def f_forward(w, pos, with_acc: bool = False):
+    n = pos.n
+    out = np.zeros(max(n, 1), np.float32)
+    acc = np.zeros((max(n, 1), 2, 256), np.float32) if with_acc else None
+    idx = pos.indices if len(pos.indices) else np.zeros(1, np.uint16)
+    st = lib().oracle_f_forward(*[_p(a) for a in w.arrays()], _p(idx), len(pos.indices), _p(pos.offsets),
+                                n, _p(out), _p(acc) if with_acc else None)
+    return st, out[:n], (acc[:n] if with_acc else None)
+
+
+def feature_pool_fwd(tables: np.ndarray, items: np.ndarray, hidden: int):
+    batch, item_count = items.shape
+    out = np.zeros((batch, hidden), np.float32)
+    st = lib().oracle_feature_pool_fwd(_p(tables), _p(items), batch, item_count, hidden, _p(out))
+    return st, out
+
+
+def feature_pool_bwd(items: np.ndarray, grad_out: np.ndarray, hidden: int):
+    batch, item_count = items.shape
+    grad = np.zeros((1545, hidden), np.float32)
+    st = lib().oracle_feature_pool_bwd(_p(items), _p(grad_out), batch, item_count, hidden, _p(grad))
+    return st, grad
+
+
+def sparse_pool_fwd(table: np.ndarray, items: np.ndarray):
+    rows, hidden = table.shape
+    batch, item_count = items.shape
+    out = np.zeros((batch, hidden), np.float32)
+    st = lib().oracle_sparse_pool_fwd(_p(table), rows, _p(items), batch, item_count, hidden, _p(out))
+    return st, out
+
+
+def sparse_pool_bwd(items: np.ndarray, grad_out: np.ndarray, rows: int):
+    batch, item_count = items.shape
+    hidden = grad_out.shape[1]
+    grad = np.zeros((rows, hidden), np.float32)
+    st = lib().oracle_sparse_pool_bwd(_p(items), _p(grad_out), rows, batch, item_count, hidden, _p(grad))
+    return st, grad
+
+
+def q_bucket(n0: int) -> int:
+    return lib().oracle_q_bucket(n0)
+
+
+def max_threads() -> int:
+    return lib().oracle_max_threads()

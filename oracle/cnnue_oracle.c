@@ -1,0 +1,404 @@
+/*
+ * cnnue_oracle.c - CPU oracle for the NNUE evaluation hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker the CUDA library is
+ * compared against (tests/, the smoke check and bench.py's CPU-baseline leg).
+ * It is never linked into the product library and the product never falls
+ * back to it.
+ *
+ * Two halves:
+ *
+ * (1) Reference-native restatements, pinned to the reference's own code and
+ *     tests (mycve/chineseai, Rust; cannot be compiled here - no cargo):
+ *       oracle_feature_pool_fwd  <- FeaturePool::cpu_fwd
+ *                                   src/az/fused_feature_pool.rs:169-198,
+ *                                   item_rows :389-403
+ *       oracle_feature_pool_bwd  <- FeaturePoolGrad::cpu_fwd
+ *                                   src/az/fused_feature_pool.rs:231-260
+ *       oracle_sparse_pool_fwd/bwd <- SparsePool / SparsePoolGrad cpu_fwd
+ *                                   src/az/fused_feature_pool.rs:284-309, :342-370
+ *     These are pinned against the reference tests' fixtures
+ *     (src/az/fused_feature_pool.rs:611-686) in tests/test_oracle_pool.py.
+ *
+ * (2) The quantised and fp32 HalfKA networks.  The reference has no code for
+ *     them (it has neither an int16 FT nor a pairwise pack nor bucket stacks);
+ *     they are restated from the workload specification only, so their parity
+ *     is UNPINNED by the reference.  Conventions fixed here (the specification
+ *     leaves them open):
+ *       - one FT table serves both perspectives; acc = bias + sum of rows with
+ *         int16 wraparound (arithmetic mod 2^16);
+ *       - pack: for perspective s and j < 512,
+ *           u8[s*512 + j] = (clamp(acc_s[j],0,127) * clamp(acc_s[j+512],0,127)) >> 7
+ *         (perspective 0 = side to move first);
+ *       - bucket = min((max(n0,1) - 1) >> 1, 15) with n0 the perspective-0
+ *         active count (16 buckets; 8 buckets with >> 2 for fp32);
+ *       - L1 1024->16 int32 + bias, >> 6 (arithmetic), clamp [0,127];
+ *         L2 16->32 the same; L3 32->1 int32 + bias, no shift;
+ *       - fp32: clipped ReLU [0,1] on FT output and between layers, FT sum in
+ *         index order starting from the bias.
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define Q_F 11340
+#define Q_COLS 1024
+#define Q_HALF 512
+#define Q_NB 16
+#define Q_L1 16
+#define Q_L2 32
+
+#define F_COLS 256
+#define F_NB 8
+
+static inline int32_t clampi(int32_t v, int32_t lo, int32_t hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+static inline float clampf(float v, float lo, float hi) {
+  return v < lo ? lo : (v > hi ? hi : v);
+}
+
+int oracle_q_bucket(uint32_t n0) {
+  uint32_t n = n0 < 1 ? 1 : n0;
+  uint32_t b = (n - 1) >> 1;
+  return (int)(b > 15 ? 15 : b);
+}
+
+int oracle_f_bucket(uint32_t n0) {
+  uint32_t n = n0 < 1 ? 1 : n0;
+  uint32_t b = (n - 1) >> 2;
+  return (int)(b > 7 ? 7 : b);
+}
+
+/* acc[j] = bias[j] + sum rows, int16 wraparound. Returns 0, or 2 on a bad index. */
+static int q_accumulate(const int16_t* ft, const int16_t* bias, const uint16_t* idx, uint32_t n,
+                        int16_t* acc) {
+  int status = 0;
+  uint16_t tmp[Q_COLS];
+  for (int j = 0; j < Q_COLS; ++j) tmp[j] = (uint16_t)bias[j];
+  for (uint32_t i = 0; i < n; ++i) {
+    uint32_t f = idx[i];
+    if (f >= Q_F) { status = 2; continue; }
+    const int16_t* row = ft + (size_t)f * Q_COLS;
+    for (int j = 0; j < Q_COLS; ++j) tmp[j] = (uint16_t)(tmp[j] + (uint16_t)row[j]);
+  }
+  memcpy(acc, tmp, sizeof(tmp));
+  return status;
+}
+
+static void q_pack(const int16_t* acc, uint8_t* out512) {
+  for (int j = 0; j < Q_HALF; ++j) {
+    int32_t a = clampi(acc[j], 0, 127);
+    int32_t b = clampi(acc[j + Q_HALF], 0, 127);
+    out512[j] = (uint8_t)((a * b) >> 7);
+  }
+}
+
+static int32_t q_stack(const uint8_t* x, int bucket, const int8_t* l1w, const int32_t* l1b,
+                       const int8_t* l2w, const int32_t* l2b, const int8_t* l3w,
+                       const int32_t* l3b) {
+  int32_t y1[Q_L1], y2[Q_L2];
+  const int8_t* w1 = l1w + (size_t)bucket * Q_L1 * Q_COLS;
+  for (int k = 0; k < Q_L1; ++k) {
+    int32_t s = l1b[bucket * Q_L1 + k];
+    for (int i = 0; i < Q_COLS; ++i) s += (int32_t)w1[k * Q_COLS + i] * (int32_t)x[i];
+    y1[k] = clampi(s >> 6, 0, 127);
+  }
+  const int8_t* w2 = l2w + (size_t)bucket * Q_L2 * Q_L1;
+  for (int m = 0; m < Q_L2; ++m) {
+    int32_t s = l2b[bucket * Q_L2 + m];
+    for (int k = 0; k < Q_L1; ++k) s += (int32_t)w2[m * Q_L1 + k] * y1[k];
+    y2[m] = clampi(s >> 6, 0, 127);
+  }
+  int32_t s = l3b[bucket];
+  for (int m = 0; m < Q_L2; ++m) s += (int32_t)l3w[bucket * Q_L2 + m] * y2[m];
+  return s;
+}
+
+/* Offsets check shared by the batched oracles: 0 ok, 3 bad. */
+static int check_offsets(const uint32_t* offsets, int64_t n_lists, uint32_t n_indices) {
+  if (offsets[0] > n_indices) return 3;
+  for (int64_t i = 0; i < n_lists; ++i) {
+    if (offsets[i] > offsets[i + 1] || offsets[i + 1] > n_indices) return 3;
+  }
+  return 0;
+}
+
+/* Quantised forward over positions [begin, end). */
+static int q_forward_range(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
+                           const int32_t* l1b, const int8_t* l2w, const int32_t* l2b,
+                           const int8_t* l3w, const int32_t* l3b, const uint16_t* idx,
+                           const uint32_t* offsets, int64_t begin, int64_t end, int32_t* scores,
+                           int16_t* acc_out) {
+  int status = 0;
+  int16_t acc[2][Q_COLS];
+  uint8_t x[Q_COLS];
+  for (int64_t p = begin; p < end; ++p) {
+    for (int s = 0; s < 2; ++s) {
+      uint32_t b = offsets[2 * p + s], e = offsets[2 * p + s + 1];
+      int st = q_accumulate(ft, bias, idx + b, e - b, acc[s]);
+      if (st) status = st;
+      q_pack(acc[s], x + s * Q_HALF);
+    }
+    if (acc_out) memcpy(acc_out + (size_t)p * 2 * Q_COLS, acc, sizeof(acc));
+    uint32_t n0 = offsets[2 * p + 1] - offsets[2 * p];
+    scores[p] = q_stack(x, oracle_q_bucket(n0), l1w, l1b, l2w, l2b, l3w, l3b);
+  }
+  return status;
+}
+
+int oracle_q_forward(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
+                     const int32_t* l1b, const int8_t* l2w, const int32_t* l2b,
+                     const int8_t* l3w, const int32_t* l3b, const uint16_t* idx,
+                     uint32_t n_indices, const uint32_t* offsets, int64_t n_positions,
+                     int32_t* scores, int16_t* acc_out) {
+  if (n_positions <= 0) return 0;
+  if (check_offsets(offsets, 2 * n_positions, n_indices)) return 3;
+  return q_forward_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, 0, n_positions,
+                         scores, acc_out);
+}
+
+/* Multi-threaded variant (OpenMP, static split) used as the timed CPU baseline. */
+int oracle_q_forward_mt(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
+                        const int32_t* l1b, const int8_t* l2w, const int32_t* l2b,
+                        const int8_t* l3w, const int32_t* l3b, const uint16_t* idx,
+                        uint32_t n_indices, const uint32_t* offsets, int64_t n_positions,
+                        int32_t* scores, int n_threads) {
+  if (n_positions <= 0) return 0;
+  if (check_offsets(offsets, 2 * n_positions, n_indices)) return 3;
+  int status = 0;
+#ifdef _OPENMP
+  if (n_threads < 1) n_threads = omp_get_max_threads();
+#pragma omp parallel num_threads(n_threads) reduction(| : status)
+  {
+    int t = omp_get_thread_num(), nt = omp_get_num_threads();
+    int64_t chunk = (n_positions + nt - 1) / nt;
+    int64_t b = t * chunk, e = b + chunk < n_positions ? b + chunk : n_positions;
+    if (b < e)
+      status |= q_forward_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, b, e,
+                                scores, NULL);
+  }
+#else
+  (void)n_threads;
+  status = q_forward_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, 0, n_positions,
+                           scores, NULL);
+#endif
+  return status;
+}
+
+int oracle_max_threads(void) {
+#ifdef _OPENMP
+  return omp_get_max_threads();
+#else
+  return 1;
+#endif
+}
+
+/* Incremental update + stack (the same conventions as the forward). */
+static int q_update_range(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
+                          const int32_t* l1b, const int8_t* l2w, const int32_t* l2b,
+                          const int8_t* l3w, const int32_t* l3b, const int16_t* parent,
+                          const uint8_t* flags, const uint16_t* rem, const uint32_t* rem_off,
+                          const uint16_t* add, const uint32_t* add_off, const uint8_t* count0,
+                          int64_t begin, int64_t end, int16_t* child, int32_t* scores) {
+  int status = 0;
+  uint8_t x[Q_COLS];
+  for (int64_t p = begin; p < end; ++p) {
+    for (int s = 0; s < 2; ++s) {
+      int64_t ps = 2 * p + s;
+      uint16_t acc[Q_COLS];
+      const int16_t* par = parent + (size_t)ps * Q_COLS;
+      int refresh = flags[ps] & 1;
+      for (int j = 0; j < Q_COLS; ++j) acc[j] = (uint16_t)(refresh ? bias[j] : par[j]);
+      if (!refresh) {
+        for (uint32_t i = rem_off[ps]; i < rem_off[ps + 1]; ++i) {
+          uint32_t f = rem[i];
+          if (f >= Q_F) { status = 2; continue; }
+          const int16_t* row = ft + (size_t)f * Q_COLS;
+          for (int j = 0; j < Q_COLS; ++j) acc[j] = (uint16_t)(acc[j] - (uint16_t)row[j]);
+        }
+      }
+      for (uint32_t i = add_off[ps]; i < add_off[ps + 1]; ++i) {
+        uint32_t f = add[i];
+        if (f >= Q_F) { status = 2; continue; }
+        const int16_t* row = ft + (size_t)f * Q_COLS;
+        for (int j = 0; j < Q_COLS; ++j) acc[j] = (uint16_t)(acc[j] + (uint16_t)row[j]);
+      }
+      int16_t* out = child + (size_t)ps * Q_COLS;
+      memcpy(out, acc, sizeof(acc));
+      q_pack(out, x + s * Q_HALF);
+    }
+    scores[p] = q_stack(x, oracle_q_bucket(count0[p]), l1w, l1b, l2w, l2b, l3w, l3b);
+  }
+  return status;
+}
+
+int oracle_q_update(const int16_t* ft, const int16_t* bias, const int8_t* l1w, const int32_t* l1b,
+                    const int8_t* l2w, const int32_t* l2b, const int8_t* l3w, const int32_t* l3b,
+                    const int16_t* parent, const uint8_t* flags, const uint16_t* rem,
+                    uint32_t n_rem, const uint32_t* rem_off, const uint16_t* add, uint32_t n_add,
+                    const uint32_t* add_off, const uint8_t* count0, int64_t n_positions,
+                    int16_t* child, int32_t* scores, int n_threads) {
+  if (n_positions <= 0) return 0;
+  if (check_offsets(rem_off, 2 * n_positions, n_rem)) return 3;
+  if (check_offsets(add_off, 2 * n_positions, n_add)) return 3;
+  int status = 0;
+#ifdef _OPENMP
+  if (n_threads < 1) n_threads = 1;
+#pragma omp parallel num_threads(n_threads) reduction(| : status)
+  {
+    int t = omp_get_thread_num(), nt = omp_get_num_threads();
+    int64_t chunk = (n_positions + nt - 1) / nt;
+    int64_t b = t * chunk, e = b + chunk < n_positions ? b + chunk : n_positions;
+    if (b < e)
+      status |= q_update_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, parent, flags, rem,
+                               rem_off, add, add_off, count0, b, e, child, scores);
+  }
+#else
+  (void)n_threads;
+  status = q_update_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, parent, flags, rem, rem_off,
+                          add, add_off, count0, 0, n_positions, child, scores);
+#endif
+  return status;
+}
+
+/* fp32 forward. The FT sum runs in index order from the bias; the stack
+ * layers are plain sequential dot products in double-free fp32. */
+int oracle_f_forward(const float* ft, const float* bias, const float* l1w, const float* l1b,
+                     const float* l2w, const float* l2b, const float* l3w, const float* l3b,
+                     const uint16_t* idx, uint32_t n_indices, const uint32_t* offsets,
+                     int64_t n_positions, float* out, float* acc_out) {
+  if (n_positions <= 0) return 0;
+  if (check_offsets(offsets, 2 * n_positions, n_indices)) return 3;
+  int status = 0;
+  float acc[2][F_COLS], x[2 * F_COLS], h1[16], h2[32];
+  for (int64_t p = 0; p < n_positions; ++p) {
+    for (int s = 0; s < 2; ++s) {
+      for (int j = 0; j < F_COLS; ++j) acc[s][j] = bias[j];
+      for (uint32_t i = offsets[2 * p + s]; i < offsets[2 * p + s + 1]; ++i) {
+        uint32_t f = idx[i];
+        if (f >= Q_F) { status = 2; continue; }
+        const float* row = ft + (size_t)f * F_COLS;
+        for (int j = 0; j < F_COLS; ++j) acc[s][j] += row[j];
+      }
+      for (int j = 0; j < F_COLS; ++j) x[s * F_COLS + j] = clampf(acc[s][j], 0.f, 1.f);
+    }
+    if (acc_out) memcpy(acc_out + (size_t)p * 2 * F_COLS, acc, sizeof(acc));
+    int bucket = oracle_f_bucket(offsets[2 * p + 1] - offsets[2 * p]);
+    for (int k = 0; k < 16; ++k) {
+      float s = l1b[bucket * 16 + k];
+      const float* w = l1w + ((size_t)bucket * 16 + k) * 2 * F_COLS;
+      for (int i = 0; i < 2 * F_COLS; ++i) s += w[i] * x[i];
+      h1[k] = clampf(s, 0.f, 1.f);
+    }
+    for (int m = 0; m < 32; ++m) {
+      float s = l2b[bucket * 32 + m];
+      const float* w = l2w + ((size_t)bucket * 32 + m) * 16;
+      for (int k = 0; k < 16; ++k) s += w[k] * h1[k];
+      h2[m] = clampf(s, 0.f, 1.f);
+    }
+    float s = l3b[bucket];
+    for (int m = 0; m < 32; ++m) s += l3w[bucket * 32 + m] * h2[m];
+    out[p] = s;
+  }
+  return status;
+}
+
+/* ---- reference-native feature pool ------------------------------------- */
+#define POOL_ROWS 1545
+#define POOL_PAD 0xffffffffu
+
+/* item_rows, src/az/fused_feature_pool.rs:389-403.  Returns 1 when every row
+ * lies inside the 1545-row table (the reference indexes the table with these
+ * rows unchecked, so a row past the end is an index panic there). */
+static int pool_item_rows(uint32_t packed, uint32_t rows[6]) {
+  uint32_t feature = packed & 0x7ffu;
+  uint32_t us = (packed >> 11) & 0xfu;
+  uint32_t them = (packed >> 15) & 0xfu;
+  uint32_t piece = feature / 90u, square = feature % 90u;
+  rows[0] = feature;
+  rows[1] = 1260u + piece;
+  rows[2] = 1274u + square / 9u;
+  rows[3] = 1284u + square % 9u;
+  rows[4] = 1293u + us * 14u + piece;
+  rows[5] = 1293u + (9u + them) * 14u + piece;
+  for (int r = 0; r < 6; ++r)
+    if (rows[r] >= POOL_ROWS) return 0;
+  return 1;
+}
+
+/* FeaturePool::cpu_fwd, src/az/fused_feature_pool.rs:169-198: for every item
+ * in order, for every h, out += the six rows in order.  Returns 2 when a row
+ * falls outside the table (the reference would panic on the slice index). */
+int oracle_feature_pool_fwd(const float* tables, const uint32_t* items, int64_t batch,
+                            int64_t item_count, int64_t hidden, float* out) {
+  int status = 0;
+  for (int64_t i = 0; i < batch * hidden; ++i) out[i] = 0.f;
+  for (int64_t b = 0; b < batch; ++b) {
+    for (int64_t i = 0; i < item_count; ++i) {
+      uint32_t packed = items[b * item_count + i];
+      if (packed == POOL_PAD) continue;
+      uint32_t rows[6];
+      if (!pool_item_rows(packed, rows)) { status = 2; continue; }
+      for (int64_t h = 0; h < hidden; ++h) {
+        float* o = &out[b * hidden + h];
+        for (int r = 0; r < 6; ++r) *o += tables[(int64_t)rows[r] * hidden + h];
+      }
+    }
+  }
+  return status;
+}
+
+/* FeaturePoolGrad::cpu_fwd, src/az/fused_feature_pool.rs:231-260: for every
+ * (b, item) in order, for every slot row, grad[row] += grad_out[b]. */
+int oracle_feature_pool_bwd(const uint32_t* items, const float* grad_out, int64_t batch,
+                            int64_t item_count, int64_t hidden, float* grad_tables) {
+  int status = 0;
+  for (int64_t i = 0; i < (int64_t)POOL_ROWS * hidden; ++i) grad_tables[i] = 0.f;
+  for (int64_t b = 0; b < batch; ++b) {
+    for (int64_t i = 0; i < item_count; ++i) {
+      uint32_t packed = items[b * item_count + i];
+      if (packed == POOL_PAD) continue;
+      uint32_t rows[6];
+      if (!pool_item_rows(packed, rows)) { status = 2; continue; }
+      for (int r = 0; r < 6; ++r)
+        for (int64_t h = 0; h < hidden; ++h)
+          grad_tables[(int64_t)rows[r] * hidden + h] += grad_out[b * hidden + h];
+    }
+  }
+  return status;
+}
+
+/* SparsePool::cpu_fwd, src/az/fused_feature_pool.rs:284-309. */
+int oracle_sparse_pool_fwd(const float* table, int64_t rows, const uint32_t* items, int64_t batch,
+                           int64_t item_count, int64_t hidden, float* out) {
+  int status = 0;
+  for (int64_t i = 0; i < batch * hidden; ++i) out[i] = 0.f;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t i = 0; i < item_count; ++i) {
+      uint32_t item = items[b * item_count + i];
+      if (item == POOL_PAD) continue;
+      if ((int64_t)item >= rows) { status = 2; continue; }
+      for (int64_t h = 0; h < hidden; ++h) out[b * hidden + h] += table[(int64_t)item * hidden + h];
+    }
+  return status;
+}
+
+/* SparsePoolGrad::cpu_fwd, src/az/fused_feature_pool.rs:342-370. */
+int oracle_sparse_pool_bwd(const uint32_t* items, const float* grad_out, int64_t rows,
+                           int64_t batch, int64_t item_count, int64_t hidden, float* grad_table) {
+  int status = 0;
+  for (int64_t i = 0; i < rows * hidden; ++i) grad_table[i] = 0.f;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t i = 0; i < item_count; ++i) {
+      uint32_t item = items[b * item_count + i];
+      if (item == POOL_PAD) continue;
+      if ((int64_t)item >= rows) { status = 2; continue; }
+      for (int64_t h = 0; h < hidden; ++h)
+        grad_table[(int64_t)item * hidden + h] += grad_out[b * hidden + h];
+    }
+  return status;
+}

@@ -49,6 +49,7 @@ const char* cnnue_status_string(int status) {
     case CNNUE_ERR_IO: return "I/O error";
     case CNNUE_ERR_NO_DEVICE: return "no such CUDA device";
     case CNNUE_ERR_TIMEOUT: return "device-side wait timed out";
+    case CNNUE_ERR_INTERNAL: return "kernel self-check failed";
     default: return "unknown status";
   }
 }
@@ -69,8 +70,10 @@ int cnnue_read_status(void* d_workspace, void* stream, int* status_out) {
     *status_out = CNNUE_ERR_BAD_OFFSETS;
   else if (word & CNNUE_STATUS_BAD_INDEX)
     *status_out = CNNUE_ERR_BAD_INDEX;
-  else if (word != 0)
+  else if (word & CNNUE_STATUS_TIMEOUT)
     *status_out = CNNUE_ERR_TIMEOUT;
+  else if (word != 0)
+    *status_out = CNNUE_ERR_INTERNAL;
   else
     *status_out = CNNUE_OK;
   if (*status_out != CNNUE_OK)

@@ -3,28 +3,34 @@
 // Work per position: two perspectives x (bias + ~17 gathered int16 rows of
 // 2 KB), the pairwise clipped-ReLU pack to 1024 uint8, then the bucket's int8
 // stack 1024->16->32->1.  The gather dominates (69.6 KB of rows per position
-// against 16 K int8 MACs), so the kernel is built around memory-level
-// parallelism on the FT rows:
+// against 16 K int8 MACs); the FT table (23 MB) stays resident in L2, so the
+// kernel is bound by L2->SM transfer of random 2 KB rows.  On B200 plain
+// 16-byte loads of such rows top out near 10 TB/s per GPU, while 1-D bulk
+// copies (cp.async.bulk, the TMA engine) reach ~16 TB/s when enough warps
+// issue them, so rows travel by bulk copy into shared memory:
 //
-//   * one group of 128 threads (4 warps) evaluates one position; warps 0-1
-//     take perspective 0, warps 2-3 perspective 1.  Thread c of a perspective
-//     owns FT columns [8c, 8c+8) and [512+8c, 512+8c+8): two 16-byte loads per
-//     row, and exactly the two halves its pack needs, so the pack is local;
-//   * rows are streamed with ld.global.nc.L1::no_allocate, kUnroll rows (2 x
-//     kUnroll 16-byte loads per thread) in flight before the adds;
-//   * int16 wraparound is __vadd2/__vsub2 on packed halfword pairs;
-//   * positions are first grouped by bucket (a two-kernel counting sort), and
-//     each group walks a contiguous slice of that order, so the 16 KB of L1
-//     weights of the current bucket live in registers (16 x 8 bytes per
-//     thread) and are reloaded only when the bucket changes;
-//   * L1 = 32 dp4a per thread + a 16-way warp reduce-scatter (16 shuffles) +
-//     a 4-warp sum through shared memory (one named barrier per position,
-//     double-buffered); warp 0 then runs L2/L3 while warps 1-3 move on.
+//   * one CTA = 4 consumer warps evaluating one position at a time plus 4
+//     producer warps; 2 CTAs per SM;
+//   * the producers copy every FT row (2 KB) into a ring of 6 stages x 8
+//     rows of shared memory (full/empty mbarrier pair per stage); each list
+//     of rows (one perspective's active features; for the update also the
+//     parent row and the removed rows) starts a fresh stage, stages are dealt
+//     round-robin to the producer warps and one lane per warp issues;
+//   * consumer thread t owns the 16-byte column chunk t of every row of both
+//     perspectives: per stage one wait, up to 8 shared loads, int16
+//     wraparound adds as __vadd2/__vsub2, one release;
+//   * the pairwise pack pairs chunk t with chunk t^64 (exchanged through
+//     shared memory); L1 = 32 dp4a per thread, a 16-way warp reduce-scatter
+//     and a 4-warp sum; warp 0 then runs L2/L3;
+//   * positions are first grouped by bucket (a two-kernel counting sort) and
+//     each CTA walks a contiguous slice of that order, so the current bucket's
+//     16 KB of L1 weights stay in registers (16 x 8 bytes per thread).
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
 
 #include "common.cuh"
+#include "pipeline.cuh"
 
 namespace cnnue {
 namespace q {
@@ -35,11 +41,6 @@ constexpr int kRowBytes = kCols * 2;
 constexpr int kNB = CNNUE_Q_BUCKETS;
 constexpr int kL1 = CNNUE_Q_L1;
 constexpr int kL2 = CNNUE_Q_L2;
-constexpr int kGroup = 128;
-constexpr int kGroupsPerCta = 2;
-constexpr int kCta = kGroup * kGroupsPerCta;
-constexpr int kUnroll = 8;
-constexpr int kMinBlocks = 2;
 constexpr unsigned kFull = 0xffffffffu;
 
 struct DevWeights {
@@ -73,49 +74,6 @@ __device__ __forceinline__ uint32_t pack_pair(uint32_t lo, uint32_t hi) {
   return p0 | (p1 << 8);
 }
 
-// Adds (kSub: subtracts) the rows listed in idx[begin, end) to this thread's
-// two 16-byte column chunks.  `ftc` points at the thread's low chunk of row 0.
-template <bool kSub>
-__device__ __forceinline__ void gather_rows(const char* __restrict__ ftc,
-                                            const uint16_t* __restrict__ idx, uint32_t begin,
-                                            uint32_t end, uint4& alo, uint4& ahi, int lane,
-                                            uint32_t* status) {
-  for (uint32_t base = begin; base < end; base += 32) {
-    const int cnt = (int)min(32u, end - base);
-    uint32_t my = lane < cnt ? (uint32_t)idx[base + lane] : 0u;
-    const bool bad = lane < cnt && my >= (uint32_t)kF;
-    if (__any_sync(kFull, bad)) {
-      if (bad) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
-    }
-    if (bad) my = 0xffffffffu;
-    for (int r0 = 0; r0 < cnt; r0 += kUnroll) {
-      uint4 vlo[kUnroll], vhi[kUnroll];
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const uint32_t f = __shfl_sync(kFull, my, r0 + u);
-        if (r0 + u < cnt && f != 0xffffffffu) {
-          const char* row = ftc + (size_t)f * kRowBytes;
-          vlo[u] = ldg_stream16(row);
-          vhi[u] = ldg_stream16(row + kRowBytes / 2);
-        } else {
-          vlo[u] = make_uint4(0, 0, 0, 0);
-          vhi[u] = make_uint4(0, 0, 0, 0);
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        if (kSub) {
-          alo = vsub(alo, vlo[u]);
-          ahi = vsub(ahi, vhi[u]);
-        } else {
-          alo = vadd(alo, vlo[u]);
-          ahi = vadd(ahi, vhi[u]);
-        }
-      }
-    }
-  }
-}
-
 struct ForwardArgs {
   DevWeights w;
   const uint16_t* idx;        // forward: active lists; update: added lists
@@ -134,87 +92,341 @@ struct ForwardArgs {
   uint32_t* status;
 };
 
+// ===========================================================================
+// Fused evaluation kernel.  One CTA = one position group: warps 0-3
+// consume, warp 4 produces.  The producer walks the same positions and issues
+// one cp.async.bulk per FT row (2 KB) into a ring of kSlots shared-memory
+// slots (full/empty mbarrier pair per slot), so up to kSlots rows per CTA are
+// in flight without holding registers.  Every consumer thread t owns the
+// 16-byte column chunk t of every row (both perspectives), which balances the
+// two perspectives' row counts across the four warps; the pairwise pack then
+// exchanges the partner half (chunk t^64) through shared memory.
+// Bad feature indices are redirected to an all-zero row kept after the table.
+// ===========================================================================
+constexpr int kStageRows = 8;                    // rows per pipeline stage
+constexpr int kStages = 6;                       // stages in the ring
+constexpr int kSlots = kStages * kStageRows;     // 48 row slots, 96 KB
+constexpr int kProducers = 4;                    // producer warps (one issuing lane each)
+constexpr int kBulkConsumers = 128;
+constexpr int kBulkThreads = kBulkConsumers + 32 * kProducers;
+constexpr int kBulkMinBlocks = 2;
+
+struct BulkSmem {
+  uint8_t ring[kSlots][kRowBytes];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint4 xbuf[kBulkConsumers];
+  int32_t red[2][4][16];
+  uint8_t y1s[16];
+  int abort;
+};
+
+struct Seg {
+  uint32_t beg, cnt;
+};
+
+struct PosDesc {
+  uint32_t pos;
+  int bucket;
+  uint32_t init[2];  // 1: the perspective starts from its parent row
+  Seg rem[2], add[2];
+};
+
+__device__ __forceinline__ Seg clamp_seg(const uint32_t* off, int64_t i, uint32_t n) {
+  const uint32_t b = min(off[i], n);
+  const uint32_t e = min(max(off[i + 1], b), n);
+  return Seg{b, e - b};
+}
+
+template <bool kUpdate>
+__device__ __forceinline__ PosDesc load_desc(const ForwardArgs& a, int64_t i) {
+  PosDesc d;
+  d.pos = a.perm[i];
+  d.bucket = a.sorted_bucket[i];
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t ps = 2 * (int64_t)d.pos + p;
+    d.add[p] = clamp_seg(a.offsets, ps, a.n_idx);
+    if (kUpdate) {
+      const bool refresh = (a.flags[ps] & 1) != 0;
+      d.init[p] = refresh ? 0u : 1u;
+      d.rem[p] = refresh ? Seg{0, 0} : clamp_seg(a.rem_offsets, ps, a.n_rem);
+    } else {
+      d.init[p] = 0;
+      d.rem[p] = Seg{0, 0};
+    }
+  }
+  return d;
+}
+
+__device__ __forceinline__ uint32_t desc_rows(const PosDesc& d) {
+  return d.init[0] + d.rem[0].cnt + d.add[0].cnt + d.init[1] + d.rem[1].cnt + d.add[1].cnt;
+}
+
+// Stage layout.  Each position contributes, per perspective, up to three row
+// lists in this order: the parent row (update only, 1 row), the removed rows
+// (update only, subtracted) and the added/active rows.  Every list starts on
+// a fresh stage of at most kStageRows rows, so a stage never mixes lists and
+// both sides walk stages, not rows.  Stage st lives in ring slots
+// (st % kStages) * kStageRows ... and is issued by producer warp
+// st % kProducers; lane 0 of that warp performs the stage's barrier operations
+// and bulk copies (one bulk copy occupies the issuing warp for ~100 cycles, so
+// issue is spread over several warps).
+__device__ __forceinline__ uint32_t n_stages(uint32_t rows) {
+  return (rows + kStageRows - 1) / kStageRows;
+}
+
+struct Producer {
+  BulkSmem* sm;
+  uint32_t* status;
+  int w;      // producer index
+  int lane;
+  bool ok;    // false once a wait gave up (stop issuing)
+
+  // Lane 0: acquire stage st's slots and announce `rows` rows.
+  __device__ __forceinline__ bool begin_stage(uint32_t st, uint32_t rows) {
+    const uint32_t sidx = st % kStages, use = st / kStages;
+    if (!ok) return false;
+    if (use > 0 && !pipe::mbar_wait(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status)) {
+      ok = false;
+      return false;
+    }
+    pipe::mbar_arrive_expect_tx(&sm->full[sidx], rows * kRowBytes);
+    return true;
+  }
+  __device__ __forceinline__ void copy(uint32_t st, uint32_t j, const char* src) {
+    const uint32_t sidx = st % kStages;
+    pipe::bulk_copy_g2s(sm->ring[sidx * kStageRows + j], src, kRowBytes, &sm->full[sidx]);
+  }
+
+  // Issues this warp's stages of list[seg] (stages st0, st0+1, ...).  `head`
+  // holds lst[seg.beg + lane] for the first 32 entries (prefetched).
+  __device__ __forceinline__ void list(const char* ft, const uint16_t* lst, Seg seg, uint32_t head,
+                                       uint32_t st0) {
+    const uint32_t ns = n_stages(seg.cnt);
+    for (uint32_t k = 0; k < ns; ++k) {
+      const uint32_t st = st0 + k;
+      if ((int)(st % kProducers) != w) continue;
+      const uint32_t first = k * kStageRows;
+      const uint32_t rows = min((uint32_t)kStageRows, seg.cnt - first);
+      uint32_t f = head;
+      if (first >= 32) f = (uint32_t)lane < rows ? lst[seg.beg + first + lane] : 0u;
+      const int src_lane0 = first >= 32 ? 0 : (int)first;
+      if (f >= (uint32_t)kF) {  // bad index -> the zero row (only lanes that hold an entry)
+        atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+        f = kF;
+      }
+      bool go = false;
+      if (lane == 0) go = begin_stage(st, rows);
+      for (uint32_t j = 0; j < rows; ++j) {
+        const uint32_t fj = __shfl_sync(kFull, f, src_lane0 + (int)j);
+        if (lane == 0 && go) copy(st, j, ft + (size_t)fj * kRowBytes);
+      }
+    }
+  }
+};
+
+// Consumer: accumulates the rows of one list into acc (kOp 0 = set from the
+// single parent row, 1 = add, 2 = subtract).  Returns the next stage number.
+template <int kOp>
+__device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint32_t cnt, int t,
+                                                 int lane, uint32_t* status, uint4& acc) {
+  for (uint32_t first = 0; first < cnt; first += kStageRows, ++st) {
+    const uint32_t sidx = st % kStages;
+    const uint32_t rows = min((uint32_t)kStageRows, cnt - first);
+    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status);
+    const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
+    uint4 v[kStageRows];
+#pragma unroll
+    for (int j = 0; j < kStageRows; ++j)
+      v[j] = (uint32_t)j < rows ? *reinterpret_cast<const uint4*>(slot + j * kRowBytes) : make_uint4(0, 0, 0, 0);
+    __syncwarp();
+    if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
+    if (kOp == 0) {
+      acc = v[0];
+    } else {
+      const uint4 s01 = vadd(vadd(v[0], v[1]), vadd(v[2], v[3]));
+      const uint4 s23 = vadd(vadd(v[4], v[5]), vadd(v[6], v[7]));
+      acc = kOp == 1 ? vadd(acc, vadd(s01, s23)) : vsub(acc, vadd(s01, s23));
+    }
+  }
+  return st;
+}
+
+// Lane-parallel descriptor of position i (valid lanes only).
+template <bool kUpdate>
+__device__ __forceinline__ void lane_desc(const ForwardArgs& a, int64_t i, bool valid, PosDesc& d) {
+  if (!valid) {
+    d.pos = 0;
+    d.bucket = 0;
+    d.init[0] = d.init[1] = 0;
+    d.rem[0] = d.rem[1] = d.add[0] = d.add[1] = Seg{0, 0};
+    return;
+  }
+  d = load_desc<kUpdate>(a, i);
+}
+
+__device__ __forceinline__ Seg shfl_seg(Seg s, int src) {
+  return Seg{__shfl_sync(kFull, s.beg, src), __shfl_sync(kFull, s.cnt, src)};
+}
+
+__device__ __forceinline__ PosDesc shfl_desc(const PosDesc& m, int src) {
+  PosDesc d;
+  d.pos = __shfl_sync(kFull, m.pos, src);
+  d.bucket = 0;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    d.init[p] = __shfl_sync(kFull, m.init[p], src);
+    d.rem[p] = shfl_seg(m.rem[p], src);
+    d.add[p] = shfl_seg(m.add[p], src);
+  }
+  return d;
+}
+
+// Prefetched first 32 entries of each index list of one position.
+struct ListHead {
+  uint32_t rem[2], add[2];
+};
+
+template <bool kUpdate>
+__device__ __forceinline__ ListHead load_heads(const ForwardArgs& a, const PosDesc& d, int lane) {
+  ListHead h;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    h.add[p] = (uint32_t)lane < d.add[p].cnt ? a.idx[d.add[p].beg + lane] : 0u;
+    h.rem[p] = kUpdate && (uint32_t)lane < d.rem[p].cnt ? a.rem[d.rem[p].beg + lane] : 0u;
+  }
+  return h;
+}
+
 template <bool kUpdate, bool kWriteAcc>
-__global__ void __launch_bounds__(kCta, kMinBlocks) q_eval_kernel(const ForwardArgs a) {
-  __shared__ int32_t red[kGroupsPerCta][2][4][16];
-  __shared__ __align__(16) uint8_t y1s[kGroupsPerCta][16];
+__global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(const ForwardArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  BulkSmem& sm = *reinterpret_cast<BulkSmem*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  const int g = threadIdx.x / kGroup;
-  const int t = threadIdx.x % kGroup;
-  const int warp = t >> 5, lane = t & 31;
-  const int persp = t >> 6;
-  const int c = t & 63;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      pipe::mbar_init(&sm.full[s], 1);
+      pipe::mbar_init(&sm.empty[s], kBulkConsumers / 32);
+    }
+    sm.abort = 0;
+    pipe::mbar_init_fence();
+  }
+  __syncthreads();
 
-  const int64_t n_groups = (int64_t)gridDim.x * kGroupsPerCta;
-  const int64_t gid = (int64_t)blockIdx.x * kGroupsPerCta + g;
-  const int64_t begin = a.n * gid / n_groups;
-  const int64_t end = a.n * (gid + 1) / n_groups;
+  const int64_t begin = a.n * blockIdx.x / gridDim.x;
+  const int64_t end = a.n * (blockIdx.x + 1) / gridDim.x;
+  const char* ft = (const char*)a.w.ft;
 
-  const char* ftc = (const char*)a.w.ft + c * 16;
-  const uint4 bias_lo = __ldg((const uint4*)((const char*)a.w.bias + c * 16));
-  const uint4 bias_hi = __ldg((const uint4*)((const char*)a.w.bias + kRowBytes / 2 + c * 16));
+  if (warp >= kBulkConsumers / 32) {
+    // ------------------------------ producers -----------------------------
+    Producer pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true};
+    const char* par_lo = (const char*)a.parent;
+    uint32_t st = 0;  // next stage number
+    for (int64_t b0 = begin; b0 < end; b0 += 32) {
+      const int nb = (int)min((int64_t)32, end - b0);
+      PosDesc mine;
+      lane_desc<kUpdate>(a, b0 + lane, lane < nb, mine);
+      PosDesc cur = shfl_desc(mine, 0);
+      ListHead head = load_heads<kUpdate>(a, cur, lane);
+      for (int q = 0; q < nb; ++q) {
+        PosDesc nx = cur;
+        ListHead nhead = head;
+        if (q + 1 < nb) {  // prefetch the next position's lists
+          nx = shfl_desc(mine, q + 1);
+          nhead = load_heads<kUpdate>(a, nx, lane);
+        }
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          if (kUpdate) {
+            if (cur.init[p]) {
+              if ((int)(st % kProducers) == pr.w && lane == 0 && pr.begin_stage(st, 1))
+                pr.copy(st, 0, par_lo + (2 * (int64_t)cur.pos + p) * kRowBytes);
+              st += 1;
+            }
+            pr.list(ft, a.rem, cur.rem[p], head.rem[p], st);
+            st += n_stages(cur.rem[p].cnt);
+          }
+          pr.list(ft, a.idx, cur.add[p], head.add[p], st);
+          st += n_stages(cur.add[p].cnt);
+        }
+        cur = nx;
+        head = nhead;
+      }
+    }
+    // Stay resident until the copies of this warp's last stages have landed
+    // (bounded by the wait limit).
+    if (lane == 0 && st > 0) {
+      const uint32_t first = st > (uint32_t)kStages ? st - kStages : 0u;
+      const unsigned long long t0 = pipe::globaltimer();
+      for (uint32_t k = first; k < st; ++k) {
+        if ((int)(k % kProducers) != pr.w) continue;
+        while (!pipe::mbar_try_wait(&sm.full[k % kStages], (k / kStages) & 1u)) {
+          if (pipe::globaltimer() - t0 > pipe::kWaitLimitNs) break;
+        }
+      }
+    }
+    __syncwarp();
+    return;
+  }
 
+  // -------------------------------- consumers ------------------------------
+  const int t = threadIdx.x;  // chunk t: columns [8t, 8t+8) of every row
+  const uint4 bias = __ldg((const uint4*)((const char*)a.w.bias + t * 16));
   int cur_bucket = -1;
   uint2 w1[kL1];
   uint4 w2row = make_uint4(0, 0, 0, 0);
   int32_t b1v = 0, b2v = 0, w3v = 0, b3v = 0;
   int parity = 0;
+  uint32_t st = 0;  // next stage number
+  PosDesc nxt;
+  if (begin < end) nxt = load_desc<kUpdate>(a, begin);
 
   for (int64_t i = begin; i < end; ++i) {
-    const uint32_t pos = a.perm[i];
-    const int bucket = a.sorted_bucket[i];
-    if (bucket != cur_bucket) {
-      cur_bucket = bucket;
-      const int8_t* w1p = a.w.l1w + (size_t)bucket * kL1 * kCols + persp * (kCols / 2) + 8 * c;
+    const PosDesc d = nxt;
+    if (i + 1 < end) nxt = load_desc<kUpdate>(a, i + 1);
+    if (d.bucket != cur_bucket) {
+      cur_bucket = d.bucket;
+      const int8_t* w1p = a.w.l1w + (size_t)d.bucket * kL1 * kCols + 8 * t;
 #pragma unroll
       for (int k = 0; k < kL1; ++k) w1[k] = __ldg((const uint2*)(w1p + (size_t)k * kCols));
-      w2row = __ldg((const uint4*)(a.w.l2w + ((size_t)bucket * kL2 + lane) * kL1));
-      b2v = __ldg(a.w.l2b + bucket * kL2 + lane);
-      w3v = __ldg(a.w.l3w + bucket * kL2 + lane);
-      b1v = lane < kL1 ? __ldg(a.w.l1b + bucket * kL1 + lane) : 0;
-      b3v = __ldg(a.w.l3b + bucket);
+      w2row = __ldg((const uint4*)(a.w.l2w + ((size_t)d.bucket * kL2 + lane) * kL1));
+      b2v = __ldg(a.w.l2b + d.bucket * kL2 + lane);
+      w3v = __ldg(a.w.l3w + d.bucket * kL2 + lane);
+      b1v = lane < kL1 ? __ldg(a.w.l1b + d.bucket * kL1 + lane) : 0;
+      b3v = __ldg(a.w.l3b + d.bucket);
     }
 
-    // ---- accumulator of this thread's columns --------------------------------
-    const int64_t ps = 2 * (int64_t)pos + persp;
-    uint4 alo, ahi;
-    if (kUpdate) {
-      const bool refresh = (a.flags[ps] & 1) != 0;
-      if (refresh) {
-        alo = bias_lo;
-        ahi = bias_hi;
-      } else {
-        const char* par = (const char*)(a.parent + ps * kCols) + c * 16;
-        alo = __ldg((const uint4*)par);
-        ahi = __ldg((const uint4*)(par + kRowBytes / 2));
-        const uint32_t rb = min(a.rem_offsets[ps], a.n_rem);
-        const uint32_t re = min(max(a.rem_offsets[ps + 1], rb), a.n_rem);
-        gather_rows<true>(ftc, a.rem, rb, re, alo, ahi, lane, a.status);
+    uint4 acc[2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint4 v = bias;
+      if (kUpdate) {
+        st = consume_list<0>(sm, st, d.init[p], t, lane, a.status, v);
+        st = consume_list<2>(sm, st, d.rem[p].cnt, t, lane, a.status, v);
       }
-    } else {
-      alo = bias_lo;
-      ahi = bias_hi;
-    }
-    {
-      const uint32_t ob = min(a.offsets[ps], a.n_idx);
-      const uint32_t oe = min(max(a.offsets[ps + 1], ob), a.n_idx);
-      gather_rows<false>(ftc, a.idx, ob, oe, alo, ahi, lane, a.status);
+      st = consume_list<1>(sm, st, d.add[p].cnt, t, lane, a.status, v);
+      acc[p] = v;
     }
     if (kWriteAcc) {
-      char* out = (char*)(a.acc_out + ps * kCols) + c * 16;
-      *(uint4*)out = alo;
-      *(uint4*)(out + kRowBytes / 2) = ahi;
+      *(uint4*)((char*)(a.acc_out + (2 * (int64_t)d.pos) * kCols) + t * 16) = acc[0];
+      *(uint4*)((char*)(a.acc_out + (2 * (int64_t)d.pos + 1) * kCols) + t * 16) = acc[1];
     }
 
-    // ---- pack + L1 partial sums ----------------------------------------------
-    const uint32_t x0 = pack_pair(alo.x, ahi.x) | (pack_pair(alo.y, ahi.y) << 16);
-    const uint32_t x1 = pack_pair(alo.z, ahi.z) | (pack_pair(alo.w, ahi.w) << 16);
+    // ---- pairwise pack: chunk t pairs with chunk t ^ 64 ----------------------
+    const bool lo = t < 64;
+    sm.xbuf[t] = lo ? acc[1] : acc[0];
+    named_bar_sync(1, kBulkConsumers);
+    const uint4 other = sm.xbuf[t ^ 64];
+    const uint4 plo = lo ? acc[0] : other;  // columns j   of the packed perspective
+    const uint4 phi = lo ? other : acc[1];  // columns j+512
+    const uint32_t x0 = pack_pair(plo.x, phi.x) | (pack_pair(plo.y, phi.y) << 16);
+    const uint32_t x1 = pack_pair(plo.z, phi.z) | (pack_pair(plo.w, phi.w) << 16);
+
     int32_t v[kL1];
 #pragma unroll
     for (int k = 0; k < kL1; ++k) v[k] = __dp4a((int)x1, (int)w1[k].y, __dp4a((int)x0, (int)w1[k].x, 0));
-
-    // Reduce-scatter of the 16 sums over the warp: afterwards lane l holds
-    // the warp total of output k = l >> 1.
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const bool up = lane & 16;
@@ -243,18 +455,17 @@ __global__ void __launch_bounds__(kCta, kMinBlocks) q_eval_kernel(const ForwardA
       v[0] = keep + __shfl_xor_sync(kFull, send, 2);
     }
     v[0] += __shfl_xor_sync(kFull, v[0], 1);
-    if ((lane & 1) == 0) red[g][parity][warp][lane >> 1] = v[0];
-    named_bar_sync(1 + g, kGroup);
+    if ((lane & 1) == 0) sm.red[parity][warp][lane >> 1] = v[0];
+    named_bar_sync(1, kBulkConsumers);
 
-    // ---- L1 epilogue, L2, L3 on warp 0 -------------------------------------
     if (warp == 0) {
       if (lane < kL1) {
-        const int32_t s = b1v + red[g][parity][0][lane] + red[g][parity][1][lane] +
-                          red[g][parity][2][lane] + red[g][parity][3][lane];
-        y1s[g][lane] = (uint8_t)min(max(s >> 6, 0), 127);
+        const int32_t s = b1v + sm.red[parity][0][lane] + sm.red[parity][1][lane] +
+                          sm.red[parity][2][lane] + sm.red[parity][3][lane];
+        sm.y1s[lane] = (uint8_t)min(max(s >> 6, 0), 127);
       }
       __syncwarp();
-      const uint4 y = *(const uint4*)y1s[g];
+      const uint4 y = *(const uint4*)sm.y1s;
       int32_t s2 = b2v;
       s2 = __dp4a((int)y.x, (int)w2row.x, s2);
       s2 = __dp4a((int)y.y, (int)w2row.y, s2);
@@ -264,7 +475,7 @@ __global__ void __launch_bounds__(kCta, kMinBlocks) q_eval_kernel(const ForwardA
       int32_t s3 = (int32_t)(int8_t)w3v * y2;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) s3 += __shfl_xor_sync(kFull, s3, o);
-      if (lane == 0) a.scores[pos] = b3v + s3;
+      if (lane == 0) a.scores[d.pos] = b3v + s3;
       __syncwarp();
     }
     parity ^= 1;
@@ -328,13 +539,16 @@ int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
   a.perm = v.perm;
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
-  const int grid = (int)std::min<int64_t>(m->grid_eval, (n + kGroupsPerCta - 1) / kGroupsPerCta);
+  const int grid = (int)std::min<int64_t>(m->grid_eval, n);
+  const size_t smem = sizeof(BulkSmem);
   if (d_acc)
-    q_eval_kernel<false, true><<<grid, kCta, 0, s>>>(a);
+    q_bulk_kernel<false, true><<<grid, kBulkThreads, smem, s>>>(a);
   else
-    q_eval_kernel<false, false><<<grid, kCta, 0, s>>>(a);
-  return check_launch("q_eval_kernel");
+    q_bulk_kernel<false, false><<<grid, kBulkThreads, smem, s>>>(a);
+  return check_launch("q_bulk_kernel");
 }
+
+bool misaligned16(const void* p) { return p != nullptr && ((uintptr_t)p & 15u) != 0; }
 
 int check_indices_args(const void* idx, uint32_t n_idx, const void* offsets, const void* out,
                        int64_t n) {
@@ -362,7 +576,7 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   DeviceGuard guard(device);
   if (guard.status) return guard.status;
 
-  const size_t sz_ft = (size_t)kF * kCols * 2, sz_bias = kCols * 2;
+  const size_t sz_ft = (size_t)(kF + 1) * kCols * 2, sz_bias = kCols * 2;  // + zero row
   const size_t sz_l1w = (size_t)kNB * kL1 * kCols, sz_l1b = kNB * kL1 * 4;
   const size_t sz_l2w = (size_t)kNB * kL2 * kL1, sz_l2b = kNB * kL2 * 4;
   const size_t sz_l3w = kNB * kL2, sz_l3b = kNB * 4;
@@ -381,13 +595,15 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
     delete m;
     return cuda_error(e, "cudaMalloc(weights)");
   }
-  for (int i = 0; i < 8; ++i) {
-    e = cudaMemcpy((char*)m->blob + offs[i], srcs[i], sizes[i], cudaMemcpyHostToDevice);
-    if (e != cudaSuccess) {
-      cudaFree(m->blob);
-      delete m;
-      return cuda_error(e, "cudaMemcpy(weights)");
-    }
+  e = cudaMemset(m->blob, 0, total);
+  for (int i = 0; i < 8 && e == cudaSuccess; ++i) {
+    const size_t bytes = i == 0 ? (size_t)kF * kCols * 2 : sizes[i];  // row kF stays zero
+    e = cudaMemcpy((char*)m->blob + offs[i], srcs[i], bytes, cudaMemcpyHostToDevice);
+  }
+  if (e != cudaSuccess) {
+    cudaFree(m->blob);
+    delete m;
+    return cuda_error(e, "cudaMemcpy(weights)");
   }
   char* b = (char*)m->blob;
   m->w.ft = (const int16_t*)(b + offs[0]);
@@ -400,11 +616,21 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   m->w.l3b = (const int32_t*)(b + offs[7]);
 
   cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device);
+  const int smem = (int)sizeof(BulkSmem);
+  cudaFuncSetAttribute(q_bulk_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(q_bulk_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaFuncSetAttribute(q_bulk_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   int occ_eval = 0, occ_upd = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_eval_kernel<false, false>, kCta, 0);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_upd, q_eval_kernel<true, true>, kCta, 0);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_bulk_kernel<false, false>, kBulkThreads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_upd, q_bulk_kernel<true, true>, kBulkThreads, smem);
   m->grid_eval = m->sm_count * std::max(occ_eval, 1);
   m->grid_update = m->sm_count * std::max(occ_upd, 1);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFree(m->blob);
+    delete m;
+    return cuda_error(e, "kernel attributes");
+  }
   *out = m;
   return CNNUE_OK;
 }
@@ -452,6 +678,7 @@ int cnnue_q_forward_acc(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t 
   st = check_indices_args(d_idx, n_idx, d_offsets, d_scores, n);
   if (st) return st;
   if (n == 0) return CNNUE_OK;
+  if (misaligned16(d_acc)) return set_error(CNNUE_ERR_INVALID_ARG, "d_acc must be 16-byte aligned");
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
@@ -521,6 +748,8 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   if (!d_parent || !d_flags || !d_rem_offsets || !d_add_offsets || !d_count0 || !d_child ||
       !d_scores || (n_rem && !d_rem) || (n_add && !d_add))
     return set_error(CNNUE_ERR_INVALID_ARG, "null update buffer");
+  if (misaligned16(d_parent) || misaligned16(d_child))
+    return set_error(CNNUE_ERR_INVALID_ARG, "d_parent and d_child must be 16-byte aligned");
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
@@ -547,9 +776,9 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   a.perm = v.perm;
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
-  const int grid = (int)std::min<int64_t>(m->grid_update, (n + kGroupsPerCta - 1) / kGroupsPerCta);
-  q_eval_kernel<true, true><<<grid, kCta, 0, s>>>(a);
-  return check_launch("q_eval_kernel<update>");
+  const int grid = (int)std::min<int64_t>(m->grid_update, n);
+  q_bulk_kernel<true, true><<<grid, kBulkThreads, sizeof(BulkSmem), s>>>(a);
+  return check_launch("q_bulk_kernel<update>");
 }
 
 }  // extern "C"

@@ -37,12 +37,15 @@ enum {
   CNNUE_ERR_FORMAT = 6,       /* weight file: wrong format tag or tensor size */
   CNNUE_ERR_IO = 7,           /* weight file cannot be read or written       */
   CNNUE_ERR_NO_DEVICE = 8,    /* no CUDA device / wrong device ordinal       */
-  CNNUE_ERR_TIMEOUT = 9       /* a bounded device-side wait gave up          */
+  CNNUE_ERR_TIMEOUT = 9,      /* a bounded device-side wait gave up          */
+  CNNUE_ERR_INTERNAL = 10     /* a kernel self-check failed                  */
 };
 
 /* Status bits written by kernels into the workspace status word. */
 #define CNNUE_STATUS_BAD_INDEX 0x1u
 #define CNNUE_STATUS_BAD_OFFSETS 0x2u
+#define CNNUE_STATUS_TIMEOUT 0x4u     /* a bounded device-side wait gave up */
+#define CNNUE_STATUS_INTERNAL 0x8u    /* a kernel self-check failed (access skipped) */
 
 const char* cnnue_status_string(int status);
 /* Detail of the last error raised on the calling thread ("" if none). */

@@ -28,6 +28,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "pipeline.cuh"
@@ -782,3 +783,68 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// No-allocation entry point: the bucket-sort scratch of cnnue_q_forward lives
+// in this file-scope device array instead of a caller workspace.  Host code
+// must not hand `g_noalloc_scratch` itself to a kernel (on the host it is only
+// a stand-in for the device symbol); its device address is looked up once per
+// device with cudaGetSymbolAddress and cached.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CNNUE_Q_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+void* g_noalloc_device_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on `device` (must be current).
+int noalloc_scratch(int device, void** out) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (device < 0 || device >= kNoAllocMaxDevices)
+    return set_error(CNNUE_ERR_NO_DEVICE, "device %d beyond the no-allocation table", device);
+  if (g_noalloc_device_ptr[device] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_error(e, "cudaGetSymbolAddress(no-allocation scratch)");
+    g_noalloc_device_ptr[device] = p;
+  }
+  *out = g_noalloc_device_ptr[device];
+  return CNNUE_OK;
+}
+
+}  // namespace
+
+extern "C" int cnnue_q_forward_noalloc(const cnnue_q_model* m, const uint16_t* d_idx,
+                                       uint32_t n_idx, const uint32_t* d_offsets, int64_t n,
+                                       int32_t* d_scores, void* stream) {
+  if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "model is null");
+  if (n < 0) return set_error(CNNUE_ERR_INVALID_ARG, "n_positions %lld is negative", (long long)n);
+  if (n > CNNUE_Q_NOALLOC_MAX_POSITIONS)
+    return set_error(CNNUE_ERR_INVALID_ARG,
+                     "n_positions %lld exceeds the %d positions the no-allocation entry point's "
+                     "fixed scratch holds; split the batch or call cnnue_q_forward with a workspace",
+                     (long long)n, CNNUE_Q_NOALLOC_MAX_POSITIONS);
+  int st = check_indices_args(d_idx, n_idx, d_offsets, d_scores, n);
+  if (st) return st;
+  if (n == 0) return CNNUE_OK;
+  if (bucket_workspace_bytes(n) > sizeof(g_noalloc_scratch))
+    return set_error(CNNUE_ERR_INTERNAL, "no-allocation scratch smaller than the workspace layout");
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  void* ws = nullptr;
+  st = noalloc_scratch(m->device, &ws);
+  if (st) return st;
+  cudaStream_t s = (cudaStream_t)stream;
+  // launch_sort zeroes the scratch header (status word, bucket counts and
+  // cursors); the rest of the scratch is fully rewritten by every call.
+  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s);
+  if (st) return st;
+  st = launch_eval(m, d_idx, n_idx, d_offsets, n, d_scores, nullptr, ws, s);
+  if (st) return st;
+  int status = CNNUE_OK;
+  st = cnnue_read_status(ws, stream, &status);
+  if (st) return st;
+  return status;
+}

@@ -129,6 +129,35 @@ int cnnue_q_forward_host(cnnue_q_model* model, const uint16_t* h_indices, uint32
                          const uint32_t* h_offsets, int64_t n_positions, int32_t* h_scores,
                          void* stream);
 
+/* No-allocation variant of cnnue_q_forward (no counterpart in the reference).
+ *
+ * For callers that cannot allocate device memory at evaluation time: a search
+ * thread that must not stall on cudaMalloc (which can synchronise the whole
+ * device), or a host process that hands all of its device memory to its own
+ * pool at start-up and has nothing left to give a workspace.  Such a caller
+ * passes only its inputs and outputs; the bucket-sort scratch lives in a
+ * fixed array inside the library (CNNUE_Q_NOALLOC_SCRATCH_BYTES, about 385 KB,
+ * held on every GPU that loads the library until the process exits).
+ *
+ *   - n_positions may be at most CNNUE_Q_NOALLOC_MAX_POSITIONS; larger batches
+ *     are rejected with CNNUE_ERR_INVALID_ARG (split them, or use
+ *     cnnue_q_forward with a workspace).
+ *   - The first call on a device looks up the scratch array's device address
+ *     (once per device, with that device current); make that first call
+ *     before any stream capture.
+ *   - Every call on a device shares the one scratch array, which keeps the
+ *     previous call's contents; each call clears the part that must start at
+ *     zero.  Calls whose GPU work overlaps (other threads, other streams)
+ *     race on the scratch: serialise them.
+ *   - The call waits for its stream and returns the kernels' status
+ *     (CNNUE_ERR_BAD_INDEX / CNNUE_ERR_BAD_OFFSETS on bad data).
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine. */
+#define CNNUE_Q_NOALLOC_MAX_POSITIONS 65536
+#define CNNUE_Q_NOALLOC_SCRATCH_BYTES (512 + 65536 + 4 * 65536 + 65536)
+int cnnue_q_forward_noalloc(const cnnue_q_model* model, const uint16_t* d_indices,
+                            uint32_t n_indices, const uint32_t* d_offsets, int64_t n_positions,
+                            int32_t* d_scores, void* stream);
+
 /* Optional: also write the int16 accumulators [n_positions][2][1024] of the
  * forward (d_acc may be NULL).  Used to check the gather separately. */
 int cnnue_q_forward_acc(const cnnue_q_model* model, const uint16_t* d_indices, uint32_t n_indices,

@@ -73,6 +73,44 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Orders this thread's earlier shared-memory accesses (and what it observed)
+// before its later async-proxy operations on shared memory (bulk copies).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Publishes a monotonic counter after this warp's earlier shared-memory reads
+// (call from one lane after __syncwarp()).
+__device__ __forceinline__ void publish_counter(uint32_t* counter, uint32_t value) {
+  __threadfence_block();
+  *reinterpret_cast<volatile uint32_t*>(counter) = value;
+}
+
+// Waits until every counters[i] (i < n) is >= target.  Bounded like mbar_wait.
+__device__ __forceinline__ bool wait_counters_reach(const uint32_t* counters, int n, uint32_t target,
+                                                    volatile int* abort, uint32_t* status) {
+  const volatile uint32_t* c = reinterpret_cast<const volatile uint32_t*>(counters);
+  unsigned long long t0 = 0;
+  for (uint32_t spin = 0;; ++spin) {
+    bool ok = true;
+    for (int i = 0; i < n; ++i) ok &= c[i] >= target;
+    if (ok) {
+      __threadfence_block();
+      return true;
+    }
+    if (*abort) return false;
+    if (spin == 0) t0 = globaltimer();
+    if ((spin & 63) == 63) {
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort = 1;
+        atomicOr(status, CNNUE_STATUS_TIMEOUT);
+        return false;
+      }
+      __nanosleep(64);
+    }
+  }
+}
+
 // 1-D bulk copy global -> this CTA's shared memory, completing `bytes` of
 // transaction count on `bar` (no multicast).  dst/src 16-byte aligned, bytes a
 // multiple of 16.

@@ -94,28 +94,30 @@ struct ForwardArgs {
 };
 
 // ===========================================================================
-// Fused evaluation kernel.  One CTA = one position group: warps 0-3
-// consume, warp 4 produces.  The producer walks the same positions and issues
-// one cp.async.bulk per FT row (2 KB) into a ring of kSlots shared-memory
-// slots (full/empty mbarrier pair per slot), so up to kSlots rows per CTA are
-// in flight without holding registers.  Every consumer thread t owns the
-// 16-byte column chunk t of every row (both perspectives), which balances the
-// two perspectives' row counts across the four warps; the pairwise pack then
-// exchanges the partner half (chunk t^64) through shared memory.
-// Bad feature indices are redirected to an all-zero row kept after the table.
+// Fused evaluation kernel.  One CTA: 4 consumer warps evaluating one
+// position at a time and kProducers producer warps that copy every FT row
+// (2 KB) by cp.async.bulk into a ring of kSlots shared-memory slots, so up to
+// kSlots rows per CTA are in flight without holding registers.  Every
+// consumer thread t owns the 16-byte column chunk t of every row (both
+// perspectives), which balances the two perspectives' row counts across the
+// four warps; the pairwise pack exchanges the partner half (chunk t^64)
+// through shared memory.  Bad feature indices are redirected to an all-zero
+// row kept after the table.
 // ===========================================================================
 constexpr int kStageRows = 8;                    // rows per pipeline stage
 constexpr int kStages = 6;                       // stages in the ring
 constexpr int kSlots = kStages * kStageRows;     // 48 row slots, 96 KB
 constexpr int kProducers = 4;                    // producer warps (one issuing lane each)
+constexpr int kPrefetch = 4;                     // positions of index lists loaded ahead
+static_assert(kProducers <= kStages, "parity waits on the empty barriers need kProducers <= kStages");
 constexpr int kBulkConsumers = 128;
 constexpr int kBulkThreads = kBulkConsumers + 32 * kProducers;
 constexpr int kBulkMinBlocks = 2;
 
 struct BulkSmem {
   uint8_t ring[kSlots][kRowBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint64_t full[kStages];   // completes when a stage's rows have landed
+  uint64_t empty[kStages];  // completes when all consumer warps released a stage
   uint4 xbuf[kBulkConsumers];
   int32_t red[2][4][16];
   uint8_t y1s[16];
@@ -169,10 +171,13 @@ __device__ __forceinline__ uint32_t desc_rows(const PosDesc& d) {
 // (update only, subtracted) and the added/active rows.  Every list starts on
 // a fresh stage of at most kStageRows rows, so a stage never mixes lists and
 // both sides walk stages, not rows.  Stage st lives in ring slots
-// (st % kStages) * kStageRows ... and is issued by producer warp
-// st % kProducers; lane 0 of that warp performs the stage's barrier operations
-// and bulk copies (one bulk copy occupies the issuing warp for ~100 cycles, so
-// issue is spread over several warps).
+// (st % kStages) * kStageRows ...; lane 0 of its producer warp performs the
+// stage's barrier operations
+// and bulk copies.  Stages are dealt round-robin to the producer warps (stage
+// st belongs to warp st % kProducers), so consecutive stages are issued in
+// parallel; one bulk copy occupies the issuing warp for ~100 cycles.  Every
+// producer warp walks all positions of the CTA's slice; the index lists are
+// prefetched kPrefetch positions ahead.
 __device__ __forceinline__ uint32_t n_stages(uint32_t rows) {
   return (rows + kStageRows - 1) / kStageRows;
 }
@@ -184,7 +189,12 @@ struct Producer {
   int lane;
   bool ok;    // false once a wait gave up (stop issuing)
 
-  // Lane 0: acquire stage st's slots and announce `rows` rows.
+  // Lane 0: wait until stage st's slots are free (all consumer warps released
+  // stage st - kStages), then announce `rows` rows on the stage's barrier.
+  // Parity waits cannot alias here: this warp's previous stage was st -
+  // kProducers, whose own wait already saw stage st - kProducers - kStages
+  // released, and kProducers <= kStages, so the empty barrier is at most one
+  // phase behind the phase waited for.
   __device__ __forceinline__ bool begin_stage(uint32_t st, uint32_t rows) {
     const uint32_t sidx = st % kStages, use = st / kStages;
     if (!ok) return false;
@@ -200,14 +210,14 @@ struct Producer {
     pipe::bulk_copy_g2s(sm->ring[sidx * kStageRows + j], src, kRowBytes, &sm->full[sidx]);
   }
 
-  // Issues this warp's stages of list[seg] (stages st0, st0+1, ...).  `head`
-  // holds lst[seg.beg + lane] for the first 32 entries (prefetched).
+  // Issues this warp's stages among st0, st0+1, ... (the stages of list[seg]).
+  // `head` holds lst[seg.beg + lane] for the first 32 entries (prefetched).
   __device__ __forceinline__ void list(const char* ft, const uint16_t* lst, Seg seg, uint32_t head,
                                        uint32_t st0) {
     const uint32_t ns = n_stages(seg.cnt);
-    for (uint32_t k = 0; k < ns; ++k) {
+    uint32_t k = (uint32_t)((w - (int)(st0 % kProducers) + kProducers) % kProducers);
+    for (; k < ns; k += kProducers) {
       const uint32_t st = st0 + k;
-      if ((int)(st % kProducers) != w) continue;
       const uint32_t first = k * kStageRows;
       const uint32_t rows = min((uint32_t)kStageRows, seg.cnt - first);
       uint32_t f = head;
@@ -252,6 +262,11 @@ __device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint
     }
   }
   return st;
+}
+
+__device__ __forceinline__ uint32_t desc_stages(const PosDesc& d) {
+  return d.init[0] + n_stages(d.rem[0].cnt) + n_stages(d.add[0].cnt) + d.init[1] +
+         n_stages(d.rem[1].cnt) + n_stages(d.add[1].cnt);
 }
 
 // Lane-parallel descriptor of position i (valid lanes only).
@@ -324,20 +339,34 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
     // ------------------------------ producers -----------------------------
     Producer pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true};
     const char* par_lo = (const char*)a.parent;
-    uint32_t st = 0;  // next stage number
+    uint32_t st_base = 0;  // stage number of the batch's first position
     for (int64_t b0 = begin; b0 < end; b0 += 32) {
       const int nb = (int)min((int64_t)32, end - b0);
       PosDesc mine;
       lane_desc<kUpdate>(a, b0 + lane, lane < nb, mine);
-      PosDesc cur = shfl_desc(mine, 0);
-      ListHead head = load_heads<kUpdate>(a, cur, lane);
+      const uint32_t my_ns = lane < nb ? desc_stages(mine) : 0u;
+      uint32_t incl = my_ns;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += x;
+      }
+      const uint32_t excl = incl - my_ns;
+      const uint32_t batch_stages = __shfl_sync(kFull, incl, 31);
+      // index-list heads of positions q .. q+3 (a rotating window)
+      ListHead h0{}, h1{}, h2{}, h3{};
+      if (0 < nb) h0 = load_heads<kUpdate>(a, shfl_desc(mine, 0), lane);
+      if (1 < nb) h1 = load_heads<kUpdate>(a, shfl_desc(mine, 1), lane);
+      if (2 < nb) h2 = load_heads<kUpdate>(a, shfl_desc(mine, 2), lane);
+      if (3 < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, 3), lane);
       for (int q = 0; q < nb; ++q) {
-        PosDesc nx = cur;
-        ListHead nhead = head;
-        if (q + 1 < nb) {  // prefetch the next position's lists
-          nx = shfl_desc(mine, q + 1);
-          nhead = load_heads<kUpdate>(a, nx, lane);
-        }
+        const PosDesc cur = shfl_desc(mine, q);
+        const ListHead head = h0;
+        h0 = h1;
+        h1 = h2;
+        h2 = h3;
+        if (q + kPrefetch < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, q + kPrefetch), lane);
+        uint32_t st = st_base + __shfl_sync(kFull, excl, q);
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           if (kUpdate) {
@@ -352,19 +381,18 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
           pr.list(ft, a.idx, cur.add[p], head.add[p], st);
           st += n_stages(cur.add[p].cnt);
         }
-        cur = nx;
-        head = nhead;
       }
+      st_base += batch_stages;
     }
     // Stay resident until the copies of this warp's last stages have landed
     // (bounded by the wait limit).
-    if (lane == 0 && st > 0) {
-      const uint32_t first = st > (uint32_t)kStages ? st - kStages : 0u;
+    if (lane == 0 && st_base > 0) {
+      const uint32_t first = st_base > (uint32_t)kStages ? st_base - kStages : 0u;
       const unsigned long long t0 = pipe::globaltimer();
-      for (uint32_t k = first; k < st; ++k) {
+      for (uint32_t k = first; k < st_base; ++k) {
         if ((int)(k % kProducers) != pr.w) continue;
         while (!pipe::mbar_try_wait(&sm.full[k % kStages], (k / kStages) & 1u)) {
-          if (pipe::globaltimer() - t0 > pipe::kWaitLimitNs) break;
+          if (sm.abort || pipe::globaltimer() - t0 > pipe::kWaitLimitNs) break;
         }
       }
     }

@@ -121,8 +121,8 @@ def measured_hbm_peak():
 
 def committed_traffic():
     """DRAM bytes per launch of the evaluation kernel from the committed ncu
-    summary (profiles/q_eval_kernel.json), scaled to a 65,536-position launch."""
-    path = os.path.join(ROOT, "profiles", "q_eval_kernel.json")
+    summary (profiles/q_bulk_kernel.json), scaled to a 65,536-position launch."""
+    path = os.path.join(ROOT, "profiles", "q_bulk_kernel.json")
     try:
         with open(path) as f:
             d = json.load(f)
@@ -322,7 +322,7 @@ def run_ours(args):
             "e2e": {"value": world * BATCH / (e2e_avg / 1e3), "unit": UNIT,
                     "h2d_bytes_per_step": int(h_idx.nbytes + h_off.nbytes), "d2h_bytes_per_step": int(h_out.nbytes)},
             "gpu_launches": 3 * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "q_eval_kernel", "achieved": achieved, "peak": peak,
+            "roofline": {"bound": "hbm", "kernel": "q_bulk_kernel", "achieved": achieved, "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                          "traffic": committed_traffic(), "algorithmic_bytes_per_launch": alg,
                          "kernel_ms": kern_avg},

@@ -56,6 +56,12 @@ SIGNATURES = {
     "cnnue_sparse_pool_fwd": (c_int, [P, c_i64, P, c_i64, c_i64, c_i64, P, P, P]),
     "cnnue_sparse_pool_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64]),
     "cnnue_sparse_pool_bwd": (c_int, [P, P, c_i64, c_i64, c_i64, c_i64, P, P, c_size, P]),
+    "cnnue_t_param_count": (c_size, []),
+    "cnnue_t_workspace_bytes": (c_size, [c_i64, c_u32]),
+    "cnnue_t_make_shadow": (c_int, [P, P, P]),
+    "cnnue_t_forward_backward": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, P, c_size, P]),
+    "cnnue_t_adam": (c_int, [P, P, P, P, P, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
+                             c_int, P]),
     "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),
     "cnnue_synth_positions": (c_int, [c_u64, c_i64, c_u32, c_u32, c_u32, P, P, C.POINTER(c_u32)]),
     "cnnue_synth_q_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),

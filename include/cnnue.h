@@ -257,6 +257,42 @@ int cnnue_sparse_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int6
                           int64_t batch, int64_t item_count, int64_t hidden, float* d_grad_table,
                           void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* ---- training step (data parallel), HalfKA network --------------------- */
+/* One rank's step of the fp32-master / bf16-activation form of the quantised
+ * network: FT 11340x1024 (bf16 shadow gathered, fp32 sums), pairwise product
+ * pack x = clamp(a_j,0,1)*clamp(a_j+512,0,1), bucket stacks 1024->16->32->1
+ * with clipped ReLU, loss = mean((sigmoid(score/400) - target)^2).
+ * Flat fp32 parameter layout (CNNUE_T_PARAMS floats):
+ *   ft [11340][1024] | ft_bias [1024] | w1 [16][16][1024] | b1 [16][16] |
+ *   w2 [16][32][16] | b2 [16][32] | w3 [16][32] | b3 [16]
+ * The bf16 shadow covers ft and ft_bias (CNNUE_T_SHADOW elements).
+ * Replaces the reference trainer's batch step GpuTrainer::compute_batch_grads
+ * (src/az/train_gpu_candle.rs:184-219), with the FT backward of
+ * FeaturePoolGrad (src/az/fused_feature_pool.rs:51-76) done without atomics,
+ * and AdamW::step (src/az/train_gpu_candle.rs:159) by plain Adam. */
+#define CNNUE_T_FEATURES 11340
+#define CNNUE_T_SHADOW (11340 * 1024 + 1024)
+#define CNNUE_T_PARAMS (11340 * 1024 + 1024 + 16 * 16 * 1024 + 16 * 16 + 16 * 32 * 16 + 16 * 32 + 16 * 32 + 16)
+size_t cnnue_t_param_count(void);
+size_t cnnue_t_workspace_bytes(int64_t n_positions, uint32_t n_indices);
+/* Writes the bf16 shadow of the FT weights and bias from the fp32 params. */
+int cnnue_t_make_shadow(const float* d_params, uint16_t* d_shadow, void* stream);
+/* Forward + backward of one rank's batch (CSR positions as cnnue_q_forward,
+ * targets fp32 [n]).  Writes the gradient of the rank's mean loss for every
+ * parameter into d_grads (flat layout; no accumulation across calls) and the
+ * mean loss into d_loss[0].  Deterministic: no atomics on floats.  Kernel
+ * status (bad index / offsets) lands in the workspace's first word. */
+int cnnue_t_forward_backward(const float* d_params, const uint16_t* d_shadow,
+                             const uint16_t* d_indices, uint32_t n_indices,
+                             const uint32_t* d_offsets, int64_t n_positions, const float* d_target,
+                             float* d_grads, float* d_loss, void* d_workspace,
+                             size_t workspace_bytes, void* stream);
+/* Adam step over all parameters with gradient grad * grad_scale (e.g. 1/world
+ * after a sum all-reduce); refreshes the bf16 shadow.  step counts from 1. */
+int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, uint16_t* d_shadow,
+                 float grad_scale, float lr, float beta1, float beta2, float eps, int step,
+                 void* stream);
+
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is
  * replaced by the mixed output at every draw. */

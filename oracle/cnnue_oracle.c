@@ -37,6 +37,7 @@
  *       - fp32: clipped ReLU [0,1] on FT output and between layers, FT sum in
  *         index order starting from the bias.
  */
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -401,4 +402,157 @@ int oracle_sparse_pool_bwd(const uint32_t* items, const float* grad_out, int64_t
         grad_table[(int64_t)item * hidden + h] += grad_out[b * hidden + h];
     }
   return status;
+}
+
+/* ---- training step (data-parallel shard of one rank) ------------------- */
+/* Conventions fixed here (the workload specification leaves them open;
+ * parity UNPINNED by the reference, whose trainer differs):
+ *   - FT master weights fp32 [11340][1024], bias fp32 [1024]; the forward
+ *     gathers their bf16 shadow (round-to-nearest-even), sums in fp32 in
+ *     index order starting from the bias, and stores the activation a as bf16;
+ *   - u = clamp(a, 0, 1); x[p*512+j] = bf16(u_p[j] * u_p[j+512]);
+ *   - bucket = min((max(n0,1)-1)>>1, 15); stack fp32: z1 = W1 x + b1,
+ *     h1 = clamp(z1,0,1); z2 = W2 h1 + b2, h2 = clamp(z2,0,1); s = W3 h2 + b3;
+ *   - loss = mean over the rank's batch of (sigmoid(s/400) - t)^2;
+ *   - clamp derivative 1 strictly inside (0,1), else 0; bf16 roundings pass
+ *     gradients straight through; gradients are of the rank's mean loss;
+ *   - Adam (Kingma & Ba): m = b1 m + (1-b1) g, v = b2 v + (1-b2) g^2,
+ *     w -= lr * (m / (1-b1^t)) / (sqrt(v / (1-b2^t)) + eps). */
+#define T_F 11340
+#define T_COLS 1024
+#define T_NB 16
+
+/* float -> bfloat16 -> float, round to nearest even (NaN -> quiet NaN). */
+static inline float bf16_round(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u)
+    u = (u | 0x00400000u) & 0xffff0000u;
+  else
+    u = (u + 0x7fffu + ((u >> 16) & 1u)) & 0xffff0000u;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+
+void oracle_bf16_round_array(const float* in, float* out, int64_t n) {
+  for (int64_t i = 0; i < n; ++i) out[i] = bf16_round(in[i]);
+}
+
+static inline float dclampf01(float z) { return (z > 0.f && z < 1.f) ? 1.f : 0.f; }
+
+/* Forward + backward of one rank's batch.  Gradients are written (not
+ * accumulated) into g_* (same shapes as the parameters); loss_out gets the
+ * mean loss; score_out [n] optional. */
+int oracle_t_grad(const float* ft, const float* ft_bias, const float* w1, const float* b1,
+                  const float* w2, const float* b2, const float* w3, const float* b3,
+                  const uint16_t* idx, uint32_t n_indices, const uint32_t* offsets,
+                  int64_t n, const float* target, float* g_ft, float* g_ft_bias, float* g_w1,
+                  float* g_b1, float* g_w2, float* g_b2, float* g_w3, float* g_b3,
+                  float* loss_out, float* score_out) {
+  if (n <= 0) return 1;
+  if (check_offsets(offsets, 2 * n, n_indices)) return 3;
+  memset(g_ft, 0, sizeof(float) * (size_t)T_F * T_COLS);
+  memset(g_ft_bias, 0, sizeof(float) * T_COLS);
+  memset(g_w1, 0, sizeof(float) * T_NB * 16 * T_COLS);
+  memset(g_b1, 0, sizeof(float) * T_NB * 16);
+  memset(g_w2, 0, sizeof(float) * T_NB * 32 * 16);
+  memset(g_b2, 0, sizeof(float) * T_NB * 32);
+  memset(g_w3, 0, sizeof(float) * T_NB * 32);
+  memset(g_b3, 0, sizeof(float) * T_NB);
+  double loss = 0.0;
+  float a[2 * T_COLS], x[T_COLS], dx[T_COLS], da[2 * T_COLS];
+  int status = 0;
+  for (int64_t b = 0; b < n; ++b) {
+    for (int p = 0; p < 2; ++p) {
+      float* ap = a + p * T_COLS;
+      for (int j = 0; j < T_COLS; ++j) ap[j] = bf16_round(ft_bias[j]);
+      for (uint32_t i = offsets[2 * b + p]; i < offsets[2 * b + p + 1]; ++i) {
+        uint32_t f = idx[i];
+        if (f >= T_F) { status = 2; continue; }
+        const float* row = ft + (size_t)f * T_COLS;
+        for (int j = 0; j < T_COLS; ++j) ap[j] += bf16_round(row[j]);
+      }
+      for (int j = 0; j < T_COLS; ++j) ap[j] = bf16_round(ap[j]);
+      for (int j = 0; j < 512; ++j) x[p * 512 + j] = bf16_round(clampf(ap[j], 0.f, 1.f) * clampf(ap[j + 512], 0.f, 1.f));
+    }
+    const int bk = oracle_q_bucket(offsets[2 * b + 1] - offsets[2 * b]);
+    float z1[16], h1[16], z2[32], h2[32];
+    for (int k = 0; k < 16; ++k) {
+      float s = b1[bk * 16 + k];
+      const float* w = w1 + ((size_t)bk * 16 + k) * T_COLS;
+      for (int i = 0; i < T_COLS; ++i) s += w[i] * x[i];
+      z1[k] = s;
+      h1[k] = clampf(s, 0.f, 1.f);
+    }
+    for (int m = 0; m < 32; ++m) {
+      float s = b2[bk * 32 + m];
+      for (int k = 0; k < 16; ++k) s += w2[(bk * 32 + m) * 16 + k] * h1[k];
+      z2[m] = s;
+      h2[m] = clampf(s, 0.f, 1.f);
+    }
+    float sc = b3[bk];
+    for (int m = 0; m < 32; ++m) sc += w3[bk * 32 + m] * h2[m];
+    if (score_out) score_out[b] = sc;
+    const float sg = 1.f / (1.f + expf(-sc / 400.f));
+    const float d = sg - target[b];
+    loss += (double)d * d;
+    const float gs = 2.f * d * sg * (1.f - sg) / 400.f / (float)n;
+    float dh2[32], dh1[16];
+    g_b3[bk] += gs;
+    for (int m = 0; m < 32; ++m) {
+      g_w3[bk * 32 + m] += gs * h2[m];
+      dh2[m] = gs * w3[bk * 32 + m] * dclampf01(z2[m]);
+      g_b2[bk * 32 + m] += dh2[m];
+    }
+    for (int k = 0; k < 16; ++k) {
+      float s = 0.f;
+      for (int m = 0; m < 32; ++m) {
+        g_w2[(bk * 32 + m) * 16 + k] += dh2[m] * h1[k];
+        s += w2[(bk * 32 + m) * 16 + k] * dh2[m];
+      }
+      dh1[k] = s * dclampf01(z1[k]);
+      g_b1[bk * 16 + k] += dh1[k];
+    }
+    for (int i = 0; i < T_COLS; ++i) dx[i] = 0.f;
+    for (int k = 0; k < 16; ++k) {
+      const float* w = w1 + ((size_t)bk * 16 + k) * T_COLS;
+      float* gw = g_w1 + ((size_t)bk * 16 + k) * T_COLS;
+      for (int i = 0; i < T_COLS; ++i) {
+        gw[i] += dh1[k] * x[i];
+        dx[i] += w[i] * dh1[k];
+      }
+    }
+    for (int p = 0; p < 2; ++p) {
+      const float* ap = a + p * T_COLS;
+      float* dap = da + p * T_COLS;
+      for (int j = 0; j < 512; ++j) {
+        const float g = dx[p * 512 + j];
+        dap[j] = g * clampf(ap[j + 512], 0.f, 1.f) * dclampf01(ap[j]);
+        dap[j + 512] = g * clampf(ap[j], 0.f, 1.f) * dclampf01(ap[j + 512]);
+      }
+      for (int j = 0; j < T_COLS; ++j) g_ft_bias[j] += dap[j];
+      for (uint32_t i = offsets[2 * b + p]; i < offsets[2 * b + p + 1]; ++i) {
+        uint32_t f = idx[i];
+        if (f >= T_F) continue;
+        float* g = g_ft + (size_t)f * T_COLS;
+        for (int j = 0; j < T_COLS; ++j) g[j] += dap[j];
+      }
+    }
+  }
+  *loss_out = (float)(loss / (double)n);
+  return status;
+}
+
+/* One Adam step over a flat parameter array (gradient scaled by grad_scale). */
+void oracle_adam(float* w, float* m, float* v, const float* g, int64_t count, float grad_scale,
+                 float lr, float beta1, float beta2, float eps, int step) {
+  const float c1 = 1.f - powf(beta1, (float)step);
+  const float c2 = 1.f - powf(beta2, (float)step);
+  for (int64_t i = 0; i < count; ++i) {
+    const float gi = g[i] * grad_scale;
+    m[i] = beta1 * m[i] + (1.f - beta1) * gi;
+    v[i] = beta2 * v[i] + (1.f - beta2) * gi * gi;
+    w[i] -= lr * (m[i] / c1) / (sqrtf(v[i] / c2) + eps);
+  }
 }

@@ -1,38 +1,53 @@
 // bucket_sort.cu - groups the positions of a batch by output bucket.
 //
-// Two kernels: (1) the bucket of every position (from the perspective-0
-// active count, or from an explicit count array) with block-aggregated
-// per-bucket counts, and the offsets check; (2) a scatter of position ids into
-// bucket order.  The evaluators then walk that order so the weights of one
-// bucket stay resident while a group of threads evaluates its positions.
+// A stable counting sort in three kernels: (1) the bucket of every position
+// (from the perspective-0 active count, or from an explicit count array) and
+// per-block bucket histograms, plus the offsets check; (2) one CTA turns the
+// histograms into per-block prefixes, bucket totals and bucket starts; (3) a
+// scatter of position ids into bucket order, ranked inside each block with
+// warp match masks, so positions stay in ascending order within a bucket.
+// The evaluators walk that order so the weights of one bucket stay resident;
+// the training step also sums its bucketed gradients in it, which makes them
+// deterministic.
 #include "common.cuh"
 
 namespace cnnue {
 
+namespace {
+constexpr int kSortThreads = 256;
+constexpr unsigned kFull = 0xffffffffu;
+
+inline size_t n_blocks(int64_t n) { return n > 0 ? (size_t)((n + kSortThreads - 1) / kSortThreads) : 0; }
+}  // namespace
+
 size_t bucket_workspace_bytes(int64_t n) {
   size_t nn = n > 0 ? (size_t)n : 0;
-  return sizeof(WorkspaceHeader) + align_up(nn, 256) + align_up(nn * 4, 256) + align_up(nn, 256);
+  return sizeof(WorkspaceHeader) + align_up(nn, 256) + align_up(nn * 4, 256) + align_up(nn, 256) +
+         align_up(n_blocks(n) * 32 * 4, 256);
 }
 
 WorkspaceView carve_workspace(void* ws, int64_t n) {
   WorkspaceView v;
+  const size_t nn = n > 0 ? (size_t)n : 0;
   char* p = (char*)ws;
   v.hdr = (WorkspaceHeader*)p;
   p += sizeof(WorkspaceHeader);
   v.bucket_of = (uint8_t*)p;
-  p += align_up((size_t)(n > 0 ? n : 0), 256);
+  p += align_up(nn, 256);
   v.perm = (uint32_t*)p;
-  p += align_up((size_t)(n > 0 ? n : 0) * 4, 256);
+  p += align_up(nn * 4, 256);
   v.sorted_bucket = (uint8_t*)p;
+  p += align_up(nn, 256);
+  v.block_hist = (uint32_t*)p;
   return v;
 }
 
 namespace {
 
-__global__ void bucket_count_kernel(const uint32_t* __restrict__ offsets, uint32_t n_indices,
-                                    const uint8_t* __restrict__ count0, int64_t n, int shift,
-                                    int max_bucket, uint8_t* __restrict__ bucket_of,
-                                    WorkspaceHeader* __restrict__ hdr) {
+__global__ void __launch_bounds__(kSortThreads) bucket_count_kernel(
+    const uint32_t* __restrict__ offsets, uint32_t n_indices, const uint8_t* __restrict__ count0,
+    int64_t n, int shift, int max_bucket, uint8_t* __restrict__ bucket_of,
+    WorkspaceHeader* __restrict__ hdr, uint32_t* __restrict__ block_hist) {
   __shared__ uint32_t hist[32];
   if (threadIdx.x < 32) hist[threadIdx.x] = 0;
   __syncthreads();
@@ -54,49 +69,65 @@ __global__ void bucket_count_kernel(const uint32_t* __restrict__ offsets, uint32
     const uint32_t nn = n0 < 1u ? 1u : n0;
     const uint32_t b = min((nn - 1u) >> shift, (uint32_t)max_bucket);
     bucket_of[p] = (uint8_t)b;
-    atomicAdd(&hist[b], 1u);
+    atomicAdd(&hist[b], 1u);  // order-free count
   }
   if (bad) atomicOr(&hdr->status, bad);
   __syncthreads();
-  if (threadIdx.x < 32 && hist[threadIdx.x]) atomicAdd(&hdr->counts[threadIdx.x], hist[threadIdx.x]);
+  if (threadIdx.x < 32) block_hist[(size_t)blockIdx.x * 32 + threadIdx.x] = hist[threadIdx.x];
 }
 
-__global__ void offsets_check_kernel(const uint32_t* __restrict__ offsets, uint32_t n_values,
-                                     int64_t n_lists, WorkspaceHeader* __restrict__ hdr) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n_lists) {
-    const uint32_t a = offsets[i], b = offsets[i + 1];
-    if (!(a <= b && b <= n_values)) atomicOr(&hdr->status, CNNUE_STATUS_BAD_OFFSETS);
-  }
-}
-
-__global__ void bucket_scatter_kernel(int64_t n, int n_buckets,
-                                      const uint8_t* __restrict__ bucket_of,
-                                      WorkspaceHeader* __restrict__ hdr,
-                                      uint32_t* __restrict__ perm,
-                                      uint8_t* __restrict__ sorted_bucket) {
-  __shared__ uint32_t base[32], hist[32], block_base[32];
-  if (threadIdx.x < 32) hist[threadIdx.x] = 0;
-  if (threadIdx.x == 0) {
+// One CTA, one warp per bucket: block_hist[blk][b] becomes the number of
+// bucket-b positions in blocks before blk; counts[b] gets the total and
+// cursors[b] the bucket's first slot.
+__global__ void bucket_scan_kernel(uint32_t nblk, int n_buckets, WorkspaceHeader* __restrict__ hdr,
+                                   uint32_t* __restrict__ block_hist) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < n_buckets) {
     uint32_t run = 0;
+    for (uint32_t base = 0; base < nblk; base += 32) {
+      const uint32_t blk = base + lane;
+      const uint32_t v = blk < nblk ? block_hist[(size_t)blk * 32 + warp] : 0u;
+      uint32_t incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t x = __shfl_up_sync(kFull, incl, o);
+        if (lane >= o) incl += x;
+      }
+      if (blk < nblk) block_hist[(size_t)blk * 32 + warp] = run + incl - v;
+      run += __shfl_sync(kFull, incl, 31);
+    }
+    if (lane == 0) hdr->counts[warp] = run;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t start = 0;
     for (int b = 0; b < 32; ++b) {
-      base[b] = run;
-      run += b < n_buckets ? hdr->counts[b] : 0u;
+      hdr->cursors[b] = start;
+      start += b < n_buckets ? hdr->counts[b] : 0u;
     }
   }
+}
+
+__global__ void __launch_bounds__(kSortThreads) bucket_scatter_kernel(
+    int64_t n, const uint8_t* __restrict__ bucket_of, const WorkspaceHeader* __restrict__ hdr,
+    const uint32_t* __restrict__ block_hist, uint32_t* __restrict__ perm,
+    uint8_t* __restrict__ sorted_bucket) {
+  constexpr int kWarps = kSortThreads / 32;
+  __shared__ uint32_t wcount[kWarps][32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < kWarps * 32; i += kSortThreads) (&wcount[0][0])[i] = 0;
   __syncthreads();
   const int64_t p = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  uint32_t b = 0, rank = 0;
-  if (p < n) {
-    b = bucket_of[p];
-    rank = atomicAdd(&hist[b], 1u);
-  }
+  const bool valid = p < n;
+  const uint32_t b = valid ? bucket_of[p] : 32u;
+  const uint32_t peers = __match_any_sync(kFull, b);
+  const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
+  if (valid && lane == __ffs(peers) - 1) wcount[warp][b] = __popc(peers);
   __syncthreads();
-  if (threadIdx.x < 32 && hist[threadIdx.x])
-    block_base[threadIdx.x] = atomicAdd(&hdr->cursors[threadIdx.x], hist[threadIdx.x]);
-  __syncthreads();
-  if (p < n) {
-    const uint32_t slot = base[b] + block_base[b] + rank;
+  if (valid) {
+    uint32_t before = 0;
+    for (int w = 0; w < warp; ++w) before += wcount[w][b];
+    const uint32_t slot = hdr->cursors[b] + block_hist[(size_t)blockIdx.x * 32 + b] + before + rank;
     perm[slot] = (uint32_t)p;
     sorted_bucket[slot] = (uint8_t)b;
   }
@@ -108,20 +139,32 @@ int check_launch(const char* what) {
   return CNNUE_OK;
 }
 
+__global__ void offsets_check_kernel(const uint32_t* __restrict__ offsets, uint32_t n_values,
+                                     int64_t n_lists, WorkspaceHeader* __restrict__ hdr) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n_lists) {
+    const uint32_t a = offsets[i], b = offsets[i + 1];
+    if (!(a <= b && b <= n_values)) atomicOr(&hdr->status, CNNUE_STATUS_BAD_OFFSETS);
+  }
+}
+
 }  // namespace
 
 int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
                        int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s) {
   WorkspaceView v = carve_workspace(ws, n);
   CNNUE_CUDA_TRY(cudaMemsetAsync(v.hdr, 0, sizeof(WorkspaceHeader), s));
-  const int threads = 256;
-  const unsigned blocks = (unsigned)((n + threads - 1) / threads);
-  bucket_count_kernel<<<blocks, threads, 0, s>>>(d_offsets, n_indices, d_count0, n, shift,
-                                                  n_buckets - 1, v.bucket_of, v.hdr);
+  if (n <= 0) return CNNUE_OK;
+  const unsigned blocks = (unsigned)n_blocks(n);
+  bucket_count_kernel<<<blocks, kSortThreads, 0, s>>>(d_offsets, n_indices, d_count0, n, shift,
+                                                      n_buckets - 1, v.bucket_of, v.hdr, v.block_hist);
   int st = check_launch("bucket_count_kernel");
   if (st) return st;
-  bucket_scatter_kernel<<<blocks, threads, 0, s>>>(n, n_buckets, v.bucket_of, v.hdr, v.perm,
-                                                    v.sorted_bucket);
+  bucket_scan_kernel<<<1, 1024, 0, s>>>(blocks, n_buckets, v.hdr, v.block_hist);
+  st = check_launch("bucket_scan_kernel");
+  if (st) return st;
+  bucket_scatter_kernel<<<blocks, kSortThreads, 0, s>>>(n, v.bucket_of, v.hdr, v.block_hist, v.perm,
+                                                        v.sorted_bucket);
   return check_launch("bucket_scatter_kernel");
 }
 

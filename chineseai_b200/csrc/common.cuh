@@ -39,18 +39,22 @@ struct WorkspaceHeader {
 static_assert(sizeof(WorkspaceHeader) == 512, "header size");
 
 // Bucket-sort workspace: header, then bucket_of[n] (u8), perm[n] (u32),
-// sorted_bucket[n] (u8), each 256-byte aligned.
+// sorted_bucket[n] (u8), block_hist[ceil(n/256)][32] (u32), each 256-byte
+// aligned.
 struct WorkspaceView {
-  WorkspaceHeader* hdr;
+  WorkspaceHeader* hdr;    // counts[b] = positions of bucket b, cursors[b] = first slot of b
   uint8_t* bucket_of;      // [n]
-  uint32_t* perm;          // [n] positions in bucket order
+  uint32_t* perm;          // [n] positions in bucket order (ascending within a bucket)
   uint8_t* sorted_bucket;  // [n] bucket of perm[i]
+  uint32_t* block_hist;    // [ceil(n/256)][32] per-block counts, then per-block prefixes
 };
 size_t bucket_workspace_bytes(int64_t n);
 WorkspaceView carve_workspace(void* ws, int64_t n);
 // Zeroes the header, then buckets the n positions (bucket = min((max(n0,1)-1)
 // >> shift, n_buckets-1), n0 from the offsets or from d_count0) and scatters
-// them into bucket order.  Offsets are validated into the status word.
+// them into bucket order, stably (ascending positions within a bucket), so
+// everything computed in that order is deterministic.  Offsets are validated
+// into the status word.
 int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
                        int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s);
 // ORs CNNUE_STATUS_BAD_OFFSETS into the workspace status when a CSR offsets

@@ -136,7 +136,7 @@ int cnnue_q_forward_host(cnnue_q_model* model, const uint16_t* h_indices, uint32
  * device), or a host process that hands all of its device memory to its own
  * pool at start-up and has nothing left to give a workspace.  Such a caller
  * passes only its inputs and outputs; the bucket-sort scratch lives in a
- * fixed array inside the library (CNNUE_Q_NOALLOC_SCRATCH_BYTES, about 385 KB,
+ * fixed array inside the library (CNNUE_Q_NOALLOC_SCRATCH_BYTES, about 417 KB,
  * held on every GPU that loads the library until the process exits).
  *
  *   - n_positions may be at most CNNUE_Q_NOALLOC_MAX_POSITIONS; larger batches
@@ -153,7 +153,7 @@ int cnnue_q_forward_host(cnnue_q_model* model, const uint16_t* h_indices, uint32
  *     (CNNUE_ERR_BAD_INDEX / CNNUE_ERR_BAD_OFFSETS on bad data).
  *   - It calls no cudaMalloc, cudaFree or other allocating routine. */
 #define CNNUE_Q_NOALLOC_MAX_POSITIONS 65536
-#define CNNUE_Q_NOALLOC_SCRATCH_BYTES (512 + 65536 + 4 * 65536 + 65536)
+#define CNNUE_Q_NOALLOC_SCRATCH_BYTES (512 + 65536 + 4 * 65536 + 65536 + 256 * 32 * 4)
 int cnnue_q_forward_noalloc(const cnnue_q_model* model, const uint16_t* d_indices,
                             uint32_t n_indices, const uint32_t* d_offsets, int64_t n_positions,
                             int32_t* d_scores, void* stream);

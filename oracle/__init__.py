@@ -134,3 +134,48 @@ def q_bucket(n0: int) -> int:
 
 def max_threads() -> int:
     return lib().oracle_max_threads()
+
+
+def _t_setup(h):
+    if getattr(h, "_t_ready", False):
+        return
+    P, i64, u32, i32, f32 = C.c_void_p, C.c_int64, C.c_uint32, C.c_int, C.c_float
+    h.oracle_t_grad.argtypes = [P] * 9 + [u32, P, i64, P] + [P] * 8 + [P, P]
+    h.oracle_t_grad.restype = C.c_int
+    h.oracle_adam.argtypes = [P, P, P, P, i64, f32, f32, f32, f32, f32, i32]
+    h.oracle_adam.restype = None
+    h.oracle_bf16_round_array.argtypes = [P, P, i64]
+    h.oracle_bf16_round_array.restype = None
+    h._t_ready = True
+
+
+def t_grad(params: np.ndarray, pos, target: np.ndarray):
+    """Training-step gradients of one rank's batch: (status, loss, flat grads)."""
+    from chineseai_b200.train import LAYOUT, split
+    h = lib()
+    _t_setup(h)
+    p = split(np.ascontiguousarray(params, np.float32))
+    g_flat = np.zeros_like(params, dtype=np.float32)
+    g = split(g_flat)
+    loss = C.c_float(0.0)
+    idx = pos.indices if len(pos.indices) else np.zeros(1, np.uint16)
+    tgt = np.ascontiguousarray(target, np.float32)
+    st = h.oracle_t_grad(*[_p(np.ascontiguousarray(p[n])) for n, _ in LAYOUT], _p(idx), len(pos.indices),
+                         _p(pos.offsets), pos.n, _p(tgt), *[_p(g[n]) for n, _ in LAYOUT], C.byref(loss), None)
+    return st, loss.value, g_flat
+
+
+def adam(w: np.ndarray, m: np.ndarray, v: np.ndarray, g: np.ndarray, grad_scale: float, lr: float,
+         beta1: float, beta2: float, eps: float, step: int) -> None:
+    h = lib()
+    _t_setup(h)
+    h.oracle_adam(_p(w), _p(m), _p(v), _p(g), len(w), grad_scale, lr, beta1, beta2, eps, step)
+
+
+def bf16_round(a: np.ndarray) -> np.ndarray:
+    h = lib()
+    _t_setup(h)
+    a = np.ascontiguousarray(a, np.float32)
+    out = np.empty_like(a)
+    h.oracle_bf16_round_array(_p(a), _p(out), a.size)
+    return out

@@ -24,7 +24,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import threading
 import time
 
 import numpy as np
@@ -343,6 +342,98 @@ def run_ours(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# training-step workload (--workload train; not the headline line)
+# ---------------------------------------------------------------------------
+TRAIN_BATCH = 16384
+TRAIN_METRIC = "training samples/sec (HalfKA FT 11340x1024, batch 16384 per GPU, data parallel)"
+
+
+def run_train(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    from chineseai_b200 import synth, train
+    from chineseai_b200.quantized import as_device
+
+    tr = train.Trainer(train.init_params(3), device=local)
+    pos = synth.positions(TRAIN_BATCH, 1 + rank)
+    t = torch.from_numpy(train.targets(TRAIN_BATCH, 100 + rank)).to(dev)
+    idx, off = as_device(pos.indices, dev), as_device(pos.offsets, dev)
+    n_idx = len(pos.indices)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        tr.forward_backward(idx, n_idx, off, TRAIN_BATCH, t)
+        if ev:
+            ev[1].record(stream)
+        w = train.allreduce_sum_(tr.grads)
+        if ev:
+            ev[2].record(stream)
+        tr.apply_adam(1.0 / w)
+        if ev:
+            ev[3].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if tr.status() != 0:
+        raise RuntimeError("training kernels reported bad input")
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize(dev)
+    sampler.start()
+    time.sleep(0.3)
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+    for k in range(args.steps):
+        step(evs[k])
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    total = sum(e[0].elapsed_time(e[3]) for e in evs)
+    fb = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
+    ar = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
+    ad = sum(e[2].elapsed_time(e[3]) for e in evs) / args.steps
+    stats = torch.tensor([total, fb, ar, ad], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, fb, ar, ad = stats.tolist()
+    loss = float(tr.loss.item())
+    if rank == 0:
+        ms = total / args.steps
+        grad_bytes = 4 * train.param_count()
+        line = {
+            "metric": TRAIN_METRIC, "value": world * TRAIN_BATCH / (ms / 1e3), "unit": "samples/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16/fp32",
+            "data": "synthetic",
+            "config": {"workload": "HalfKA training step: bf16 FT gather, pack, 16 bucket fp32 stacks, "
+                                   "MSE(sigmoid(s/400), t), atomic-free FT backward, NCCL all-reduce, Adam",
+                       "batch_per_gpu": TRAIN_BATCH, "global_batch": world * TRAIN_BATCH,
+                       "parallelism": f"dp{world}", "grad_bytes": grad_bytes},
+            "phases_ms": {"forward_backward": fb, "allreduce": ar, "adam": ad},
+            "allreduce_busbw_gbs": (2 * (world - 1) / world * grad_bytes / (ar / 1e3) / 1e9) if world > 1 else None,
+            "loss": loss, "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -351,11 +442,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["eval", "train"], default="eval",
+                    help="eval: the headline quantised forward; train: the data-parallel training step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.workload == "train":
+        return run_train(args)
     return run_ours(args)
 
 

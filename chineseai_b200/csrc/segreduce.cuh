@@ -111,7 +111,19 @@ __global__ void bwd_chunk_prefix_kernel(int64_t n_chunks, int64_t n_rows, BwdVie
   const int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r >= n_rows) return;
   uint32_t run = 0;
-  for (int64_t c = 0; c < n_chunks; ++c) {
+  int64_t c = 0;
+  // batches of 8 independent loads, then the sequential prefix
+  for (; c + 8 <= n_chunks; c += 8) {
+    uint32_t x[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) x[q] = v.chunk_hist[(c + q) * n_rows + r];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v.chunk_hist[(c + q) * n_rows + r] = run;
+      run += x[q];
+    }
+  }
+  for (; c < n_chunks; ++c) {
     uint32_t* h = v.chunk_hist + c * n_rows + r;
     const uint32_t x = *h;
     *h = run;
@@ -284,16 +296,24 @@ __global__ void bwd_reduce_kernel(const float* __restrict__ grad_out, int64_t hi
   }
 }
 
+// One CTA per row: rows with several units sum their unit partials in unit
+// order (threads over columns); rows without contributions get zeros.
 __global__ void bwd_finalize_kernel(int64_t hidden, int64_t n_rows, BwdView v,
                                     float* __restrict__ grad_table) {
-  const int lane = threadIdx.x & 31;
-  const int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (r >= n_rows) return;
+  const int64_t r = blockIdx.x;
   const uint32_t u0 = v.unit_start[r], u1 = v.unit_start[r + 1];
   if (u1 - u0 == 1) return;
-  for (int64_t h = lane; h < hidden; h += 32) {
+  for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
     float acc = 0.f;
-    for (uint32_t u = u0; u < u1; ++u) acc += v.partial[(int64_t)u * hidden + h];
+    uint32_t u = u0;
+    for (; u + 4 <= u1; u += 4) {
+      float p[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) p[q] = v.partial[(int64_t)(u + q) * hidden + h];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) acc += p[q];
+    }
+    for (; u < u1; ++u) acc += v.partial[(int64_t)u * hidden + h];
     grad_table[r * hidden + h] = acc;
   }
 }
@@ -339,8 +359,7 @@ int launch_bwd(int64_t n_items, const float* grad_out, int64_t hidden, Dec dec, 
     bwd_reduce_kernel<false><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table);
   st = check_launch_error("bwd_reduce_kernel");
   if (st) return st;
-  bwd_finalize_kernel<<<(unsigned)((n_rows * 32 + 255) / 256), 256, 0, s>>>(hidden, n_rows, v,
-                                                                            grad_table);
+  bwd_finalize_kernel<<<(unsigned)n_rows, 256, 0, s>>>(hidden, n_rows, v, grad_table);
   return check_launch_error("bwd_finalize_kernel");
 }
 

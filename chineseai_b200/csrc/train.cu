@@ -356,21 +356,34 @@ __global__ void __launch_bounds__(128) t_w1grad_kernel(const __nv_bfloat16* __re
   float acc[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) acc[k] = 0.f;
+  __shared__ uint32_t poss[32];
   for (uint32_t c0 = 0; c0 < cnt; c0 += 32) {
     const uint32_t m = min(32u, cnt - c0);
     __syncthreads();
+    if (threadIdx.x < m) poss[threadIdx.x] = perm[start + c0 + threadIdx.x];
     for (uint32_t e = threadIdx.x; e < m * 16; e += 128) {
       const uint32_t pos = perm[start + c0 + e / 16];
       dh1s[e / 16][e % 16] = head[(size_t)pos * kHead + kHDH1 + e % 16];
     }
     __syncthreads();
-    for (uint32_t q = 0; q < m; ++q) {
-      const uint32_t pos = perm[start + c0 + q];
-      const __nv_bfloat16* ap = a + (2 * (int64_t)pos + persp) * kCols;
-      const float x = __bfloat162float(__float2bfloat16_rn(clamp01(__bfloat162float(ap[j])) *
-                                                           clamp01(__bfloat162float(ap[j + 512]))));
+    // all 2 x m activation loads of this thread are independent: issue them first
+    __nv_bfloat16 lo[32], hi[32];
 #pragma unroll
-      for (int k = 0; k < 16; ++k) acc[k] += dh1s[q][k] * x;
+    for (uint32_t q = 0; q < 32; ++q) {
+      if (q < m) {
+        const __nv_bfloat16* ap = a + (2 * (int64_t)poss[q] + persp) * kCols;
+        lo[q] = ap[j];
+        hi[q] = ap[j + 512];
+      }
+    }
+#pragma unroll
+    for (uint32_t q = 0; q < 32; ++q) {
+      if (q < m) {
+        const float x = __bfloat162float(__float2bfloat16_rn(clamp01(__bfloat162float(lo[q])) *
+                                                             clamp01(__bfloat162float(hi[q]))));
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc[k] += dh1s[q][k] * x;
+      }
     }
   }
   float* g = grads + kOffW1 + (size_t)bk * 16 * kCols + i;
@@ -378,25 +391,39 @@ __global__ void __launch_bounds__(128) t_w1grad_kernel(const __nv_bfloat16* __re
   for (int k = 0; k < 16; ++k) g[(size_t)k * kCols] = acc[k];
 }
 
-// 4b. dW2, dW3, db1, db2, db3: one CTA per bucket, 512 threads.
+// 4b. dW2, dW3, db1, db2, db3: one CTA per bucket, 512 threads; the head
+//     records of 64 positions at a time are staged in shared memory with
+//     coalesced loads, then summed in bucket order.
 __global__ void __launch_bounds__(512) t_smallgrad_kernel(const float* __restrict__ head,
                                                           const uint32_t* __restrict__ perm,
                                                           const WorkspaceHeader* hdr, float* grads) {
+  constexpr int kChunk = 64;
+  constexpr int kRec = 97;  // h1, dh1, h2, dh2, ds
+  __shared__ float rec[kChunk][kRec];
   const int bk = blockIdx.x, t = threadIdx.x;
   uint32_t start = 0;
   for (int b = 0; b < bk; ++b) start += hdr->counts[b];
   const uint32_t cnt = hdr->counts[bk];
   const int m = t >> 4, k = t & 15;  // dW2[m][k]
   float w2 = 0.f, w3 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-  for (uint32_t q = 0; q < cnt; ++q) {
-    const float* h = head + (size_t)perm[start + q] * kHead;
-    w2 += h[kHDH2 + m] * h[kHH1 + k];
-    if (t < 32) {
-      w3 += h[kHDS] * h[kHH2 + t];
-      b2 += h[kHDH2 + t];
+  for (uint32_t c0 = 0; c0 < cnt; c0 += kChunk) {
+    const uint32_t nq = min((uint32_t)kChunk, cnt - c0);
+    __syncthreads();
+    for (uint32_t e = t; e < nq * kRec; e += 512) {
+      const uint32_t q = e / kRec, f = e % kRec;
+      rec[q][f] = head[(size_t)perm[start + c0 + q] * kHead + f];
     }
-    if (t < 16) b1 += h[kHDH1 + t];
-    if (t == 0) b3 += h[kHDS];
+    __syncthreads();
+    for (uint32_t q = 0; q < nq; ++q) {
+      const float* h = rec[q];
+      w2 += h[kHDH2 + m] * h[kHH1 + k];
+      if (t < 32) {
+        w3 += h[kHDS] * h[kHH2 + t];
+        b2 += h[kHDH2 + t];
+      }
+      if (t < 16) b1 += h[kHDH1 + t];
+      if (t == 0) b3 += h[kHDS];
+    }
   }
   grads[kOffW2 + (size_t)bk * 512 + t] = w2;
   if (t < 32) {

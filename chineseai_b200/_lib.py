@@ -62,6 +62,22 @@ SIGNATURES = {
     "cnnue_t_forward_backward": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, P, c_size, P]),
     "cnnue_t_adam": (c_int, [P, P, P, P, P, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
                              c_int, P]),
+    "cnnue_az_board_from_fen": (c_int, [C.c_char_p, P, C.POINTER(c_int)]),
+    "cnnue_az_features": (c_int, [P, c_int, P, C.POINTER(c_int)]),
+    "cnnue_az_move_items": (c_int, [P, c_int, c_int, c_int, P, P, P, C.POINTER(c_int)]),
+    "cnnue_az_tensor_info": (c_int, [c_int, c_i64, C.POINTER(C.c_char_p), C.POINTER(c_i64)]),
+    "cnnue_az_weights_random": (c_int, [c_i64, c_u64, C.POINTER(c_void_p)]),
+    "cnnue_az_weights_load": (c_int, [C.c_char_p, C.POINTER(c_void_p)]),
+    "cnnue_az_weights_save": (c_int, [c_void_p, C.c_char_p]),
+    "cnnue_az_weights_destroy": (c_int, [c_void_p]),
+    "cnnue_az_weights_hidden": (c_i64, [c_void_p]),
+    "cnnue_az_weights_tensor": (c_int, [c_void_p, c_int, C.POINTER(C.POINTER(C.c_float)), C.POINTER(c_i64)]),
+    "cnnue_az_model_create": (c_int, [c_void_p, c_int, C.POINTER(c_void_p)]),
+    "cnnue_az_model_destroy": (c_int, [c_void_p]),
+    "cnnue_az_workspace_bytes": (c_size, []),
+    "cnnue_az_refresh": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_az_transition": (c_int, [c_void_p, P, P, P, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_az_value": (c_int, [c_void_p, P, P, P, P, c_i64, P, P, P]),
     "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),
     "cnnue_synth_positions": (c_int, [c_u64, c_i64, c_u32, c_u32, c_u32, P, P, C.POINTER(c_u32)]),
     "cnnue_synth_q_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),

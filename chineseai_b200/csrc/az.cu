@@ -1,0 +1,579 @@
+// az.cu - device side of the reference-native AZ-NNUE evaluator: the trunk
+// accumulator refresh, its incremental transition, and the value head.
+//
+// The trunk of one perspective is a sum of fp32 rows of five tables, which the
+// model keeps concatenated as one [1545][H] table (input 0, piece 1260, rank
+// 1274, file 1284, king-piece 1293; the feature-pool layout of
+// src/az/fused_feature_pool.rs:12-19).  Refresh and transition run one warp per
+// item list; lane l owns the columns of chunks l, l+32, ... (a chunk is a
+// float4 when H is a multiple of 4, else one float), so each column is summed
+// by one thread in exactly the reference's row order, one IEEE add or
+// subtract per row, which makes the accumulators bit-identical to the CPU
+// ones.  Row loads of several items are issued before their adds so a warp
+// keeps up to 20 row loads in flight; the table (H = 128: 791 KB) stays in L2.
+//
+// The value head runs one warp per 4 positions: x = ReLU(acc + rule rows),
+// RMSNorm, then lane k computes value units k, k+32, k+64 for all 4 positions
+// from the transposed head weights [H][96] held in shared memory, and the 3
+// logits are warp sums.
+#include <cfloat>
+#include <cstring>
+
+#include "az_weights.h"
+#include "common.cuh"
+
+struct cnnue_az_model {
+  int device = 0;
+  int64_t hidden = 0;
+  void* blob = nullptr;
+  float* trunk = nullptr;   // [1545][H]
+  float* bias = nullptr;    // [H]
+  float* rule = nullptr;    // [7][H]
+  float* head_t = nullptr;  // value_head_hidden transposed, [H][96]
+  float* head_b = nullptr;  // [96]
+  float* head_o = nullptr;  // [3][96]
+};
+
+namespace cnnue {
+namespace {
+
+constexpr int kRows = CNNUE_AZ_TRUNK_ROWS;
+constexpr int kHead = CNNUE_AZ_VALUE_HEAD;
+constexpr int kListWarps = 8;  // warps per CTA of the refresh / transition kernels
+constexpr int kValuePos = 4;   // positions per warp in the value head
+constexpr unsigned kFull = 0xffffffffu;
+
+// Row indices of an item: input, piece, rank, file, king(us), king(them).
+// Returns false (rows all 0) for a feature >= 1260 or a bucket > 8.
+__device__ __forceinline__ bool item_rows(uint32_t item, uint32_t r[6]) {
+  const uint32_t feature = item & 0x7ffu, us = (item >> 11) & 0xfu, them = (item >> 15) & 0xfu;
+  const bool ok = feature < (uint32_t)CNNUE_AZ_INPUT && us <= 8u && them <= 8u && (item >> 19) == 0u;
+  const uint32_t f = ok ? feature : 0u;
+  const uint32_t piece = f / 90u, sq = f - piece * 90u;
+  r[0] = f;
+  r[1] = 1260u + piece;
+  r[2] = 1274u + sq / 9u;
+  r[3] = 1284u + sq % 9u;
+  r[4] = 1293u + (ok ? us : 0u) * 14u + piece;
+  r[5] = 1293u + (9u + (ok ? them : 0u)) * 14u + piece;
+  return ok;
+}
+
+// Columns of one lane: K chunks of VW floats.
+template <int VW, int K>
+struct Cols {
+  float v[K][VW];
+};
+
+template <int VW, int K>
+__device__ __forceinline__ void load_cols(const float* __restrict__ row, int chunks, int lane, Cols<VW, K>& c) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int ch = lane + 32 * k;
+    if (ch < chunks) {
+      if constexpr (VW == 4) {
+        const float4 x = __ldg(reinterpret_cast<const float4*>(row) + ch);
+        c.v[k][0] = x.x;
+        c.v[k][1] = x.y;
+        c.v[k][2] = x.z;
+        c.v[k][3] = x.w;
+      } else {
+        c.v[k][0] = __ldg(row + ch);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < VW; ++e) c.v[k][e] = 0.f;
+    }
+  }
+}
+
+template <int VW, int K>
+__device__ __forceinline__ void store_cols(float* __restrict__ row, int chunks, int lane, const Cols<VW, K>& c) {
+#pragma unroll
+  for (int k = 0; k < K; ++k) {
+    const int ch = lane + 32 * k;
+    if (ch < chunks) {
+      if constexpr (VW == 4) {
+        reinterpret_cast<float4*>(row)[ch] = make_float4(c.v[k][0], c.v[k][1], c.v[k][2], c.v[k][3]);
+      } else {
+        row[ch] = c.v[k][0];
+      }
+    }
+  }
+}
+
+// a += w (kSign > 0) or a -= w, one rounding per element.
+template <int kSign, int VW, int K>
+__device__ __forceinline__ void accumulate(Cols<VW, K>& a, const Cols<VW, K>& w) {
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int e = 0; e < VW; ++e) a.v[k][e] = kSign > 0 ? __fadd_rn(a.v[k][e], w.v[k][e]) : __fsub_rn(a.v[k][e], w.v[k][e]);
+}
+
+// acc += the rows of the items [beg, end) in the reference's refresh order:
+// the input row of every item, then for every item its five structural rows.
+// Returns CNNUE_STATUS_BAD_INDEX if an item was skipped.
+template <int VW, int K>
+__device__ uint32_t add_list(const float* __restrict__ trunk, int H, int chunks, const uint32_t* __restrict__ items,
+                             uint32_t beg, uint32_t end, int lane, Cols<VW, K>& a) {
+  // Rows loaded ahead of their adds, about 32-40 registers of row data.
+  constexpr int kRowRegs = VW * K;
+  constexpr int kIn = 32 / kRowRegs > 0 ? 32 / kRowRegs : 1;            // input rows
+  constexpr int kSt = 40 / (5 * kRowRegs) > 0 ? 40 / (5 * kRowRegs) : 1;  // items of 5 structural rows
+  uint32_t bad = 0;
+  for (int pass = 0; pass < 2; ++pass) {
+    for (uint32_t base = beg; base < end; base += 32) {
+      const uint32_t mine = base + lane < end ? items[base + lane] : 0u;
+      uint32_t r[6];
+      const bool ok = item_rows(mine, r);
+      if (base + lane < end && !ok) bad = CNNUE_STATUS_BAD_INDEX;
+      const uint32_t ok_mask = __ballot_sync(kFull, ok);
+      const int cnt = (int)min(32u, end - base);
+      if (pass == 0) {
+        for (int j0 = 0; j0 < cnt; j0 += kIn) {
+          Cols<VW, K> w[kIn];
+#pragma unroll
+          for (int b = 0; b < kIn; ++b) {
+            const uint32_t row = __shfl_sync(kFull, r[0], (j0 + b) & 31);
+            if (j0 + b < cnt) load_cols(trunk + (size_t)row * H, chunks, lane, w[b]);
+          }
+#pragma unroll
+          for (int b = 0; b < kIn; ++b)
+            if (j0 + b < cnt && ((ok_mask >> (j0 + b)) & 1u)) accumulate<1>(a, w[b]);
+        }
+      } else {
+        for (int j0 = 0; j0 < cnt; j0 += kSt) {
+          Cols<VW, K> w[kSt][5];
+#pragma unroll
+          for (int b = 0; b < kSt; ++b) {
+#pragma unroll
+            for (int s = 0; s < 5; ++s) {
+              const uint32_t row = __shfl_sync(kFull, r[s + 1], (j0 + b) & 31);
+              if (j0 + b < cnt) load_cols(trunk + (size_t)row * H, chunks, lane, w[b][s]);
+            }
+          }
+#pragma unroll
+          for (int b = 0; b < kSt; ++b)
+            if (j0 + b < cnt && ((ok_mask >> (j0 + b)) & 1u))
+#pragma unroll
+              for (int s = 0; s < 5; ++s) accumulate<1>(a, w[b][s]);
+        }
+      }
+    }
+  }
+  return bad;
+}
+
+// a -= 6 rows (kSign < 0) or a += 6 rows of one item, in the order input,
+// piece, rank, file, king(us), king(them).
+template <int kSign, int VW, int K>
+__device__ __forceinline__ uint32_t apply_item(const float* __restrict__ trunk, int H, int chunks, uint32_t item,
+                                               int lane, Cols<VW, K>& a) {
+  if (item == CNNUE_AZ_NO_ITEM) return 0u;
+  uint32_t r[6];
+  if (!item_rows(item, r)) return CNNUE_STATUS_BAD_INDEX;
+  Cols<VW, K> w[6];
+#pragma unroll
+  for (int s = 0; s < 6; ++s) load_cols(trunk + (size_t)r[s] * H, chunks, lane, w[s]);
+#pragma unroll
+  for (int s = 0; s < 6; ++s) accumulate<kSign>(a, w[s]);
+  return 0u;
+}
+
+struct ListArgs {
+  const float* trunk;
+  const float* bias;
+  int H;
+  int chunks;
+  const uint32_t* items;
+  uint32_t n_items;
+  const uint32_t* offsets;
+  int64_t n_lists;
+  // transition only
+  const float* parent;
+  const uint32_t* delta;
+  const uint8_t* refresh;
+  float* out;
+  WorkspaceHeader* hdr;
+};
+
+// One warp per list.  kTransition: parent +- delta rows unless refresh[l].
+template <bool kTransition, int VW, int K>
+__global__ void __launch_bounds__(kListWarps * 32) az_list_kernel(ListArgs p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * kListWarps;
+  uint32_t status = 0;
+  for (int64_t l = (int64_t)blockIdx.x * kListWarps + (threadIdx.x >> 5); l < p.n_lists; l += warps) {
+    Cols<VW, K> a;
+    const bool do_refresh = !kTransition || (p.refresh[l] & 1u);
+    if (do_refresh) {
+      load_cols(p.bias, p.chunks, lane, a);
+      if (p.offsets == nullptr) {
+        status |= CNNUE_STATUS_BAD_OFFSETS;
+      } else {
+        const uint32_t beg = p.offsets[l], end = p.offsets[l + 1];
+        if (beg <= end && end <= p.n_items)
+          status |= add_list(p.trunk, p.H, p.chunks, p.items, beg, end, lane, a);
+        else
+          status |= CNNUE_STATUS_BAD_OFFSETS;
+      }
+    } else {
+      load_cols(p.parent + (size_t)l * p.H, p.chunks, lane, a);
+      const uint32_t from = p.delta[3 * l], captured = p.delta[3 * l + 1], to = p.delta[3 * l + 2];
+      status |= apply_item<-1>(p.trunk, p.H, p.chunks, from, lane, a);
+      status |= apply_item<-1>(p.trunk, p.H, p.chunks, captured, lane, a);
+      status |= apply_item<1>(p.trunk, p.H, p.chunks, to, lane, a);
+    }
+    store_cols(p.out + (size_t)l * p.H, p.chunks, lane, a);
+  }
+  status = __reduce_or_sync(kFull, status);
+  if (lane == 0 && status) atomicOr(&p.hdr->status, status);
+}
+
+template <bool kTransition>
+int launch_list(const ListArgs& a, cudaStream_t s) {
+  const bool vec = a.H % 4 == 0;
+  const int chunks = vec ? a.H / 4 : a.H;
+  const int k = (chunks + 31) / 32;
+  ListArgs p = a;
+  p.chunks = chunks;
+  const int64_t want = (a.n_lists + kListWarps - 1) / kListWarps;
+  const unsigned blocks = (unsigned)(want < 148 * 32 ? want : 148 * 32);
+  const dim3 block(kListWarps * 32);
+  if (vec) {
+    if (k <= 1) az_list_kernel<kTransition, 4, 1><<<blocks, block, 0, s>>>(p);
+    else if (k <= 2) az_list_kernel<kTransition, 4, 2><<<blocks, block, 0, s>>>(p);
+    else az_list_kernel<kTransition, 4, 4><<<blocks, block, 0, s>>>(p);
+  } else {  // H < 128 (checked at model creation)
+    if (k <= 1) az_list_kernel<kTransition, 1, 1><<<blocks, block, 0, s>>>(p);
+    else if (k <= 2) az_list_kernel<kTransition, 1, 2><<<blocks, block, 0, s>>>(p);
+    else az_list_kernel<kTransition, 1, 4><<<blocks, block, 0, s>>>(p);
+  }
+  return check_launch_error(kTransition ? "az_list_kernel<transition>" : "az_list_kernel<refresh>");
+}
+
+// ---- value head ------------------------------------------------------------
+struct ValueArgs {
+  const float* head_t;  // [H][96]
+  const float* head_b;  // [96]
+  const float* head_o;  // [3][96]
+  const float* rule_rows;  // [7][H]
+  int H;
+  const float* acc;
+  const uint8_t* side;
+  const float* rule;
+  const float* threat;
+  int64_t n;
+  float* wdl;
+  float* q;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Dynamic shared memory: head_t [H][96], head_o [3][96], head_b [96], then
+// per warp x [kValuePos][H].
+__global__ void __launch_bounds__(256) az_value_kernel(ValueArgs p) {
+  extern __shared__ float sm[];
+  const int H = p.H, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  float* w_t = sm;
+  float* w_o = w_t + (size_t)H * kHead;
+  float* w_b = w_o + 3 * kHead;
+  float* xs = w_b + kHead + (size_t)warp * kValuePos * H;
+  for (int i = threadIdx.x; i < H * kHead; i += blockDim.x) w_t[i] = p.head_t[i];
+  for (int i = threadIdx.x; i < 3 * kHead; i += blockDim.x) w_o[i] = p.head_o[i];
+  for (int i = threadIdx.x; i < kHead; i += blockDim.x) w_b[i] = p.head_b[i];
+  __syncthreads();
+
+  const int64_t groups = (p.n + kValuePos - 1) / kValuePos;
+  for (int64_t g = (int64_t)blockIdx.x * nwarps + warp; g < groups; g += (int64_t)gridDim.x * nwarps) {
+    // 1. x = ReLU(acc + rule context), then RMSNorm.
+#pragma unroll
+    for (int i = 0; i < kValuePos; ++i) {
+      const int64_t pos = g * kValuePos + i;
+      float* x = xs + i * H;
+      if (pos >= p.n) {
+        for (int c = lane; c < H; c += 32) x[c] = 0.f;
+        continue;
+      }
+      const float* src = p.acc + (p.side ? ((size_t)pos * 2 + (p.side[pos] ? 1 : 0)) : (size_t)pos) * H;
+      float rule[CNNUE_AZ_RULE_CONTEXT];
+#pragma unroll
+      for (int k = 0; k < CNNUE_AZ_RULE_CONTEXT; ++k) rule[k] = p.rule ? p.rule[pos * CNNUE_AZ_RULE_CONTEXT + k] : 0.f;
+      float ss = 0.f;
+      for (int c = lane; c < H; c += 32) {
+        float v = src[c];
+#pragma unroll
+        for (int k = 0; k < CNNUE_AZ_RULE_CONTEXT; ++k)
+          if (rule[k] != 0.f) v = __fadd_rn(v, __fmul_rn(rule[k], p.rule_rows[(size_t)k * H + c]));
+        v = fmaxf(v, 0.f);
+        ss = fmaf(v, v, ss);
+        x[c] = v;
+      }
+      ss = warp_sum(ss);
+      const float inv = 1.0f / sqrtf(ss / (float)H + 1e-6f);
+      for (int c = lane; c < H; c += 32) x[c] *= inv;
+    }
+    __syncwarp();
+    // 2. value units k, k+32, k+64 of the 4 positions.
+    float d[kValuePos][3];
+#pragma unroll
+    for (int i = 0; i < kValuePos; ++i) d[i][0] = d[i][1] = d[i][2] = 0.f;
+    for (int j = 0; j < H; ++j) {
+      const float w0 = w_t[j * kHead + lane], w1 = w_t[j * kHead + lane + 32], w2 = w_t[j * kHead + lane + 64];
+#pragma unroll
+      for (int i = 0; i < kValuePos; ++i) {
+        const float xv = xs[i * H + j];
+        d[i][0] = fmaf(xv, w0, d[i][0]);
+        d[i][1] = fmaf(xv, w1, d[i][1]);
+        d[i][2] = fmaf(xv, w2, d[i][2]);
+      }
+    }
+    // 3. logits, softmax, q.
+    float logit[kValuePos][3];
+#pragma unroll
+    for (int i = 0; i < kValuePos; ++i) {
+      const float v0 = fmaxf(w_b[lane] + d[i][0], 0.f), v1 = fmaxf(w_b[lane + 32] + d[i][1], 0.f),
+                  v2 = fmaxf(w_b[lane + 64] + d[i][2], 0.f);
+#pragma unroll
+      for (int o = 0; o < 3; ++o)
+        logit[i][o] = warp_sum(v0 * w_o[o * kHead + lane] + v1 * w_o[o * kHead + lane + 32] +
+                               v2 * w_o[o * kHead + lane + 64]);
+    }
+#pragma unroll
+    for (int i = 0; i < kValuePos; ++i) {
+      const int64_t pos = g * kValuePos + i;
+      if (lane == i && pos < p.n) {
+        float l[3];
+#pragma unroll
+        for (int o = 0; o < 3; ++o) l[o] = logit[i][o] + (p.threat ? p.threat[pos * 3 + o] : 0.f);
+        const float m = fmaxf(fmaxf(fmaxf(-INFINITY, l[0]), l[1]), l[2]);
+        const float e0 = expf(l[0] - m), e1 = expf(l[1] - m), e2 = expf(l[2] - m);
+        const float sum = fmaxf(e0 + e1 + e2, FLT_MIN);
+        const float p0 = e0 / sum, p1 = e1 / sum, p2 = e2 / sum;
+        p.wdl[pos * 3 + 0] = p0;
+        p.wdl[pos * 3 + 1] = p1;
+        p.wdl[pos * 3 + 2] = p2;
+        p.q[pos] = p0 - p2;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+size_t value_smem_bytes(int64_t H, int warps) {
+  return sizeof(float) * ((size_t)H * kHead + 4 * kHead + (size_t)warps * kValuePos * H);
+}
+
+constexpr size_t kMaxSmem = 227 * 1024;
+
+int value_warps(int64_t H) {
+  int w = 8;
+  while (w > 1 && value_smem_bytes(H, w) > kMaxSmem) w >>= 1;
+  return w;
+}
+
+__global__ void transpose_head_kernel(const float* __restrict__ w, int H, float* __restrict__ wt) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < (int64_t)H * kHead) {
+    const int64_t k = i / H, j = i - k * H;  // w[k][j] -> wt[j][k]
+    wt[j * kHead + k] = w[i];
+  }
+}
+
+// The float4 column path needs 16-byte aligned accumulator rows.
+int check_rows_aligned(int64_t H, const void* a, const char* what) {
+  if (H % 4 == 0 && ((uintptr_t)a & 15u) != 0)
+    return set_error(CNNUE_ERR_INVALID_ARG, "%s must be 16-byte aligned when hidden %% 4 == 0", what);
+  return CNNUE_OK;
+}
+
+}  // namespace
+}  // namespace cnnue
+
+using namespace cnnue;
+
+extern "C" {
+
+size_t cnnue_az_workspace_bytes(void) { return sizeof(WorkspaceHeader); }
+
+int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model** out) {
+  if (!w || !out) return set_error(CNNUE_ERR_INVALID_ARG, "null weights or out");
+  *out = nullptr;
+  const int64_t H = w->hidden;
+  if (H <= 0 || H > CNNUE_AZ_MAX_HIDDEN || (H >= 128 && H % 4 != 0))
+    return set_error(CNNUE_ERR_INVALID_ARG, "hidden %lld: the device model takes 1..127 or multiples of 4 up to %d",
+                     (long long)H, CNNUE_AZ_MAX_HIDDEN);
+  if (value_smem_bytes(H, value_warps(H)) > kMaxSmem)
+    return set_error(CNNUE_ERR_INVALID_ARG, "hidden %lld: value head does not fit in shared memory", (long long)H);
+  DeviceGuard guard(device);
+  if (guard.status) return guard.status;
+  const size_t trunk = align_up(sizeof(float) * kRows * H, 256), vecH = align_up(sizeof(float) * H, 256),
+               rule = align_up(sizeof(float) * 7 * H, 256), head = align_up(sizeof(float) * kHead * H, 256),
+               small = align_up(sizeof(float) * kHead, 256), out3 = align_up(sizeof(float) * 3 * kHead, 256);
+  const size_t staging = align_up(sizeof(float) * kHead * H, 256);
+  auto* m = new (std::nothrow) cnnue_az_model;
+  if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
+  m->device = device;
+  m->hidden = H;
+  cudaError_t e = cudaMalloc(&m->blob, trunk + vecH + rule + head + small + out3 + staging);
+  if (e != cudaSuccess) {
+    delete m;
+    return cuda_error(e, "cudaMalloc(az model)");
+  }
+  char* p = (char*)m->blob;
+  m->trunk = (float*)p;
+  m->bias = (float*)(p += trunk);
+  m->rule = (float*)(p += vecH);
+  m->head_t = (float*)(p += rule);
+  m->head_b = (float*)(p += head);
+  m->head_o = (float*)(p += small);
+  float* stage = (float*)(p += out3);
+  using namespace cnnue::az;
+  const int tables[5] = {kInputHidden, kInputPiece, kInputRank, kInputFile, kInputKingPiece};
+  const int rows[5] = {1260, 14, 10, 9, 252};
+  size_t row = 0;
+  int st = CNNUE_OK;
+  auto copy = [&](void* dst, const std::vector<float>& src, size_t n, const char* what) {
+    if (st) return;
+    if (src.size() != n) {
+      st = set_error(CNNUE_ERR_INVALID_ARG, "tensor %s has %zu elements, expected %zu", what, src.size(), n);
+      return;
+    }
+    const cudaError_t ce = cudaMemcpy(dst, src.data(), n * sizeof(float), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) st = cuda_error(ce, what);
+  };
+  for (int t = 0; t < 5; ++t) {
+    copy(m->trunk + row * H, w->t[tables[t]], (size_t)rows[t] * H, "trunk table");
+    row += rows[t];
+  }
+  copy(m->bias, w->t[kHiddenBias], (size_t)H, "hidden_bias");
+  copy(m->rule, w->t[kRuleContext], (size_t)7 * H, "rule_context_hidden");
+  copy(stage, w->t[kValueHeadHidden], (size_t)kHead * H, "value_head_hidden");
+  copy(m->head_b, w->t[kValueHeadBias], kHead, "value_head_bias");
+  copy(m->head_o, w->t[kValueHeadOutput], 3 * kHead, "value_head_output");
+  if (!st) {
+    const int64_t n = (int64_t)kHead * H;
+    transpose_head_kernel<<<(unsigned)((n + 255) / 256), 256>>>(stage, (int)H, m->head_t);
+    st = check_launch_error("transpose_head_kernel");
+  }
+  if (!st) {
+    // The largest opt-in size, so models of different hidden sizes coexist.
+    const cudaError_t ce =
+        cudaFuncSetAttribute(az_value_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
+    if (ce != cudaSuccess) st = cuda_error(ce, "cudaFuncSetAttribute(az_value_kernel)");
+  }
+  if (!st) {
+    const cudaError_t ce = cudaDeviceSynchronize();
+    if (ce != cudaSuccess) st = cuda_error(ce, "az model upload");
+  }
+  if (st) {
+    cudaFree(m->blob);
+    delete m;
+    return st;
+  }
+  *out = m;
+  return CNNUE_OK;
+}
+
+int cnnue_az_model_destroy(cnnue_az_model* m) {
+  if (!m) return CNNUE_OK;
+  DeviceGuard guard(m->device);
+  if (m->blob) cudaFree(m->blob);
+  delete m;
+  return guard.status;
+}
+
+int cnnue_az_refresh(const cnnue_az_model* m, const uint32_t* d_items, uint32_t n_items, const uint32_t* d_offsets,
+                     int64_t n_lists, float* d_acc, void* ws, size_t ws_bytes, void* stream) {
+  if (!m || !ws || (n_lists > 0 && (!d_offsets || !d_acc || (n_items > 0 && !d_items))) || n_lists < 0)
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, offsets, items or acc, or n_lists < 0");
+  if (ws_bytes < sizeof(WorkspaceHeader))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu", ws_bytes, sizeof(WorkspaceHeader));
+  if (int st = check_rows_aligned(m->hidden, d_acc, "d_acc")) return st;
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n_lists == 0) return CNNUE_OK;
+  ListArgs a{};
+  a.trunk = m->trunk;
+  a.bias = m->bias;
+  a.H = (int)m->hidden;
+  a.items = d_items;
+  a.n_items = n_items;
+  a.offsets = d_offsets;
+  a.n_lists = n_lists;
+  a.out = d_acc;
+  a.hdr = (WorkspaceHeader*)ws;
+  return launch_list<false>(a, s);
+}
+
+int cnnue_az_transition(const cnnue_az_model* m, const float* d_parent, const uint32_t* d_delta,
+                        const uint8_t* d_refresh, const uint32_t* d_items, uint32_t n_items,
+                        const uint32_t* d_offsets, int64_t n_lists, float* d_child, void* ws, size_t ws_bytes,
+                        void* stream) {
+  if (!m || !ws || n_lists < 0 || (n_lists > 0 && (!d_parent || !d_delta || !d_refresh || !d_child)) ||
+      (n_items > 0 && !d_items))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, parent, delta, refresh, child or items");
+  if (ws_bytes < sizeof(WorkspaceHeader))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu", ws_bytes, sizeof(WorkspaceHeader));
+  if (int st = check_rows_aligned(m->hidden, d_parent, "d_parent")) return st;
+  if (int st = check_rows_aligned(m->hidden, d_child, "d_child")) return st;
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n_lists == 0) return CNNUE_OK;
+  ListArgs a{};
+  a.trunk = m->trunk;
+  a.bias = m->bias;
+  a.H = (int)m->hidden;
+  a.items = d_items;
+  a.n_items = n_items;
+  a.offsets = d_offsets;  // NULL: a list with the refresh flag is flagged bad offsets
+  a.n_lists = n_lists;
+  a.parent = d_parent;
+  a.delta = d_delta;
+  a.refresh = d_refresh;
+  a.out = d_child;
+  a.hdr = (WorkspaceHeader*)ws;
+  return launch_list<true>(a, s);
+}
+
+int cnnue_az_value(const cnnue_az_model* m, const float* d_acc, const uint8_t* d_side, const float* d_rule,
+                   const float* d_threat, int64_t n, float* d_wdl, float* d_q, void* stream) {
+  if (!m || n < 0 || (n > 0 && (!d_acc || !d_wdl || !d_q)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, acc, wdl or q, or n < 0");
+  if (n == 0) return CNNUE_OK;
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  ValueArgs a{};
+  a.head_t = m->head_t;
+  a.head_b = m->head_b;
+  a.head_o = m->head_o;
+  a.rule_rows = m->rule;
+  a.H = (int)m->hidden;
+  a.acc = d_acc;
+  a.side = d_side;
+  a.rule = d_rule;
+  a.threat = d_threat;
+  a.n = n;
+  a.wdl = d_wdl;
+  a.q = d_q;
+  const int warps = value_warps(m->hidden);
+  const size_t smem = value_smem_bytes(m->hidden, warps);
+  const int64_t groups = (n + kValuePos - 1) / kValuePos;
+  const int64_t want = (groups + warps - 1) / warps;
+  int per_sm = (int)(kMaxSmem / smem);
+  per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
+  const unsigned blocks = (unsigned)(want < 148 * per_sm ? want : 148 * per_sm);
+  az_value_kernel<<<blocks, warps * 32, smem, (cudaStream_t)stream>>>(a);
+  return check_launch_error("az_value_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,598 @@
+// az_host.cpp - host side of the reference-native AZ-NNUE evaluator.
+//
+// Board parsing (Position::from_fen, src/xiangqi/mod.rs:163-207), the
+// side-relative feature items with their king-palace buckets (src/nnue.rs:25-43,
+// src/az.rs:168-203), the items a move adds and removes
+// (apply_transition_for_perspective, src/az.rs:439-566), deterministic weights
+// (AzNnue::random_with_arch, src/az.rs:1339-1431) and the weight file
+// (AzNnue::save / load / validate, src/az.rs:1437-1529, :2453-2499).
+//
+// The weight file is safetensors: an 8-byte little-endian header length, a
+// JSON header {"name": {"dtype", "shape", "data_offsets"}} padded with spaces
+// to a multiple of 8 bytes, then the raw little-endian tensor bytes.  Files are
+// written with the tensors sorted by name, each tensor's bytes in that order.
+#include <cmath>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/cnnue.h"
+#include "az_weights.h"
+
+namespace cnnue {
+int set_error(int status, const char* fmt, ...);
+}
+
+namespace {
+
+using cnnue::set_error;
+
+constexpr int kSq = CNNUE_AZ_SQUARES;
+constexpr int kDenseMoves = 2086;  // DENSE_MOVE_SPACE (src/az.rs:60, checked by :3344-3352)
+
+// One tensor of az_weight_tensors!: rows x cols, a dimension of -1 meaning H.
+struct TensorSpec {
+  const char* name;
+  int64_t rows;  // -1 = H; 0 = a 1-D tensor of `cols`
+  int64_t cols;  // -1 = H
+};
+
+constexpr TensorSpec kSpecs[CNNUE_AZ_TENSORS] = {
+    {"input_hidden", 1260, -1},
+    {"input_piece_hidden", 14, -1},
+    {"input_rank_hidden", 10, -1},
+    {"input_file_hidden", 9, -1},
+    {"input_king_piece_hidden", 252, -1},
+    {"rule_context_hidden", 7, -1},
+    {"hidden_bias", 0, -1},
+    {"value_head_hidden", 96, -1},
+    {"value_head_bias", 0, 96},
+    {"value_head_output", 3, 96},
+    {"value_threat_embedding", 57702, 64},
+    {"value_threat_output", 3, 128},
+    {"policy_threat_context", 16, 128},
+    {"policy_move_bias", 0, kDenseMoves},
+    {"policy_consequence_output", 0, 32},
+    {"policy_context_hidden", 16, -1},
+    {"policy_move_context", kDenseMoves, 16},
+    {"policy_accumulator_hidden", 32, -1},
+    {"policy_accumulator_move", kDenseMoves, 32},
+    {"policy_sparse_table", 0, 2396815},
+    {"policy_sparse_factor", 0, 199458},
+    {"policy_tactical", 0, 934976},
+};
+
+inline int64_t dim(int64_t d, int64_t h) { return d < 0 ? h : d; }
+
+std::vector<int64_t> shape_of(int i, int64_t h) {
+  const TensorSpec& s = kSpecs[i];
+  if (s.rows == 0) return {dim(s.cols, h)};
+  return {dim(s.rows, h), dim(s.cols, h)};
+}
+
+int64_t count_of(int i, int64_t h) {
+  int64_t n = 1;
+  for (int64_t d : shape_of(i, h)) n *= d;
+  return n;
+}
+
+// ---- SplitMix64 as the reference defines it (src/az.rs:3146-3176) ----------
+struct SplitMix {
+  uint64_t state;
+  uint64_t next() {
+    uint64_t v = state + 0x9E3779B97F4A7C15ull;
+    v = (v ^ (v >> 30)) * 0xBF58476D1CE4E5B9ull;
+    v = (v ^ (v >> 27)) * 0x94D049BB133111EBull;
+    state = v ^ (v >> 31);
+    return state;
+  }
+  float unit_f32() { return (float)((double)(next() >> 11) * (1.0 / 9007199254740992.0)); }
+  float weight(float scale) { return (unit_f32() * 2.0f - 1.0f) * scale; }
+};
+
+// ---- board helpers ---------------------------------------------------------
+inline int canonical_square(int perspective, int sq) { return perspective == 0 ? sq : kSq - 1 - sq; }
+
+// canonical_general_bucket (src/az.rs:194-203).
+inline int general_bucket(int piece_index, int sq) {
+  const int o = piece_index < 7 ? sq : kSq - 1 - sq;
+  int file = o % 9, rank = o / 9;
+  file = file < 3 ? 3 : (file > 5 ? 5 : file);
+  rank = rank < 7 ? 7 : (rank > 9 ? 9 : rank);
+  return (rank - 7) * 3 + (file - 3);
+}
+
+inline bool piece_ok(int v) { return v >= -7 && v <= 7; }
+
+// Feature of the piece `v` on `sq` for `perspective` (src/nnue.rs:25-28).
+inline uint32_t feature_of(int v, int sq, int perspective) {
+  const int color = v > 0 ? 0 : 1, kind = (v > 0 ? v : -v) - 1;
+  const int piece_index = (color == perspective ? 0 : 7) + kind;
+  return (uint32_t)(piece_index * kSq + canonical_square(perspective, sq));
+}
+
+// (us, them) buckets of a board for a perspective: the last general of each
+// side in scan order, 4 when absent (canonical_general_buckets_from_features).
+void buckets_of(const int8_t* board, int perspective, int* us, int* them) {
+  *us = 4;
+  *them = 4;
+  for (int sq = 0; sq < kSq; ++sq) {
+    const int v = board[sq];
+    if (v == 0 || (v > 0 ? v : -v) != 1) continue;
+    const uint32_t f = feature_of(v, sq, perspective);
+    const int piece_index = (int)f / kSq, csq = (int)f % kSq;
+    if (piece_index == 0) *us = general_bucket(0, csq);
+    if (piece_index == 7) *them = general_bucket(7, csq);
+  }
+}
+
+inline uint32_t pack(uint32_t feature, int us, int them) {
+  return feature | ((uint32_t)us << 11) | ((uint32_t)them << 15);
+}
+
+int check_board(const int8_t* board) {
+  if (board == nullptr) return set_error(CNNUE_ERR_INVALID_ARG, "null board");
+  for (int sq = 0; sq < kSq; ++sq)
+    if (!piece_ok(board[sq]))
+      return set_error(CNNUE_ERR_INVALID_ARG, "board[%d] = %d is not a piece code", sq, board[sq]);
+  return CNNUE_OK;
+}
+
+int features(const int8_t* board, int perspective, uint32_t* items) {
+  int us, them, n = 0;
+  buckets_of(board, perspective, &us, &them);
+  for (int sq = 0; sq < kSq; ++sq)
+    if (board[sq] != 0) items[n++] = pack(feature_of(board[sq], sq, perspective), us, them);
+  return n;
+}
+
+// ---- a minimal JSON reader for the safetensors header ---------------------
+struct Json {
+  enum Kind { Null, Bool, Number, String, Array, Object } kind = Null;
+  double number = 0.0;
+  bool integral = false;
+  int64_t integer = 0;
+  std::string str;
+  std::vector<Json> items;
+  std::vector<std::pair<std::string, Json>> fields;
+  const Json* get(const char* key) const {
+    for (const auto& f : fields)
+      if (f.first == key) return &f.second;
+    return nullptr;
+  }
+};
+
+struct JsonParser {
+  const char* p;
+  const char* end;
+  int depth = 0;
+  bool fail = false;
+
+  void ws() {
+    while (p < end && (*p == ' ' || *p == '\t' || *p == '\n' || *p == '\r')) ++p;
+  }
+  bool lit(const char* s) {
+    const size_t n = strlen(s);
+    if ((size_t)(end - p) < n || memcmp(p, s, n) != 0) return false;
+    p += n;
+    return true;
+  }
+  bool string(std::string& out) {
+    if (p >= end || *p != '"') return false;
+    ++p;
+    while (p < end && *p != '"') {
+      if (*p == '\\') {
+        if (++p >= end) return false;
+        switch (*p) {
+          case '"': out += '"'; break;
+          case '\\': out += '\\'; break;
+          case '/': out += '/'; break;
+          case 'b': out += '\b'; break;
+          case 'f': out += '\f'; break;
+          case 'n': out += '\n'; break;
+          case 'r': out += '\r'; break;
+          case 't': out += '\t'; break;
+          case 'u':  // kept verbatim: tensor names of this format are ASCII
+            if (end - p < 5) return false;
+            out.append(p - 1, 6);
+            p += 4;
+            break;
+          default: return false;
+        }
+        ++p;
+      } else {
+        out += *p++;
+      }
+    }
+    if (p >= end) return false;
+    ++p;
+    return true;
+  }
+  bool value(Json& v) {
+    if (++depth > 64) return false;
+    ws();
+    if (p >= end) return false;
+    bool ok = true;
+    if (*p == '{') {
+      v.kind = Json::Object;
+      ++p;
+      ws();
+      if (p < end && *p == '}') {
+        ++p;
+      } else {
+        for (;;) {
+          ws();
+          std::string key;
+          if (!string(key)) { ok = false; break; }
+          ws();
+          if (p >= end || *p != ':') { ok = false; break; }
+          ++p;
+          Json child;
+          if (!value(child)) { ok = false; break; }
+          v.fields.emplace_back(std::move(key), std::move(child));
+          ws();
+          if (p < end && *p == ',') { ++p; continue; }
+          if (p < end && *p == '}') { ++p; break; }
+          ok = false;
+          break;
+        }
+      }
+    } else if (*p == '[') {
+      v.kind = Json::Array;
+      ++p;
+      ws();
+      if (p < end && *p == ']') {
+        ++p;
+      } else {
+        for (;;) {
+          Json child;
+          if (!value(child)) { ok = false; break; }
+          v.items.push_back(std::move(child));
+          ws();
+          if (p < end && *p == ',') { ++p; continue; }
+          if (p < end && *p == ']') { ++p; break; }
+          ok = false;
+          break;
+        }
+      }
+    } else if (*p == '"') {
+      v.kind = Json::String;
+      ok = string(v.str);
+    } else if (lit("true")) {
+      v.kind = Json::Bool;
+      v.number = 1;
+    } else if (lit("false")) {
+      v.kind = Json::Bool;
+    } else if (lit("null")) {
+      v.kind = Json::Null;
+    } else {
+      const char* s = p;
+      while (p < end && (strchr("+-.eE", *p) != nullptr || (*p >= '0' && *p <= '9'))) ++p;
+      if (p == s) return false;
+      std::string text(s, p);
+      char* stop = nullptr;
+      v.kind = Json::Number;
+      v.number = strtod(text.c_str(), &stop);
+      ok = stop != nullptr && *stop == '\0';
+      v.integral = text.find_first_of(".eE") == std::string::npos;
+      if (v.integral) v.integer = strtoll(text.c_str(), nullptr, 10);
+    }
+    --depth;
+    return ok;
+  }
+};
+
+struct FileCloser {
+  void operator()(FILE* f) const {
+    if (f) fclose(f);
+  }
+};
+using File = std::unique_ptr<FILE, FileCloser>;
+
+int read_file(const char* path, std::vector<char>& bytes) {
+  File f(fopen(path, "rb"));
+  if (!f) return set_error(CNNUE_ERR_IO, "cannot open %s for reading", path);
+  if (fseek(f.get(), 0, SEEK_END) != 0) return set_error(CNNUE_ERR_IO, "cannot seek %s", path);
+  const long size = ftell(f.get());
+  if (size < 0 || fseek(f.get(), 0, SEEK_SET) != 0) return set_error(CNNUE_ERR_IO, "cannot size %s", path);
+  try {
+    bytes.resize((size_t)size);
+  } catch (const std::bad_alloc&) {
+    return set_error(CNNUE_ERR_IO, "out of host memory reading %s", path);
+  }
+  if (size > 0 && fread(bytes.data(), 1, (size_t)size, f.get()) != (size_t)size)
+    return set_error(CNNUE_ERR_IO, "short read on %s", path);
+  return CNNUE_OK;
+}
+
+struct TensorRef {
+  std::string dtype;
+  std::vector<int64_t> shape;
+  uint64_t begin = 0, end = 0;
+};
+
+// Parses a safetensors file into name -> tensor; checks offsets and sizes.
+int parse_safetensors(const std::vector<char>& bytes, std::map<std::string, TensorRef>& out,
+                      const char** data) {
+  if (bytes.size() < 8) return set_error(CNNUE_ERR_FORMAT, "safetensors file shorter than its header length");
+  uint64_t n = 0;
+  for (int i = 7; i >= 0; --i) n = (n << 8) | (uint8_t)bytes[i];
+  if (n > bytes.size() - 8) return set_error(CNNUE_ERR_FORMAT, "safetensors header length %llu past the file end",
+                                             (unsigned long long)n);
+  JsonParser parser{bytes.data() + 8, bytes.data() + 8 + n};
+  Json root;
+  if (!parser.value(root) || root.kind != Json::Object)
+    return set_error(CNNUE_ERR_FORMAT, "safetensors header is not a JSON object");
+  parser.ws();
+  if (parser.p != parser.end) return set_error(CNNUE_ERR_FORMAT, "trailing bytes in the safetensors header");
+  const uint64_t data_len = bytes.size() - 8 - n;
+  *data = bytes.data() + 8 + n;
+  for (const auto& f : root.fields) {
+    if (f.first == "__metadata__") continue;
+    const Json& t = f.second;
+    const Json* dt = t.get("dtype");
+    const Json* sh = t.get("shape");
+    const Json* off = t.get("data_offsets");
+    if (t.kind != Json::Object || !dt || dt->kind != Json::String || !sh || sh->kind != Json::Array || !off ||
+        off->kind != Json::Array || off->items.size() != 2)
+      return set_error(CNNUE_ERR_FORMAT, "safetensors entry `%s` is malformed", f.first.c_str());
+    TensorRef r;
+    r.dtype = dt->str;
+    for (const Json& d : sh->items) {
+      if (d.kind != Json::Number || !d.integral || d.integer < 0)
+        return set_error(CNNUE_ERR_FORMAT, "tensor `%s` has a bad shape", f.first.c_str());
+      r.shape.push_back(d.integer);
+    }
+    for (int k = 0; k < 2; ++k)
+      if (off->items[k].kind != Json::Number || !off->items[k].integral || off->items[k].integer < 0)
+        return set_error(CNNUE_ERR_FORMAT, "tensor `%s` has bad data_offsets", f.first.c_str());
+    r.begin = (uint64_t)off->items[0].integer;
+    r.end = (uint64_t)off->items[1].integer;
+    if (r.begin > r.end || r.end > data_len)
+      return set_error(CNNUE_ERR_FORMAT, "tensor `%s` data_offsets [%llu, %llu) outside the %llu data bytes",
+                       f.first.c_str(), (unsigned long long)r.begin, (unsigned long long)r.end,
+                       (unsigned long long)data_len);
+    out[f.first] = std::move(r);
+  }
+  return CNNUE_OK;
+}
+
+// Loads one F32 tensor, flattened (load_candle_f32_tensor, src/az.rs:222-239).
+int load_f32(const std::map<std::string, TensorRef>& tensors, const char* data, const char* name,
+             std::vector<float>& out) {
+  auto it = tensors.find(name);
+  if (it == tensors.end()) return set_error(CNNUE_ERR_FORMAT, "cannot find tensor %s", name);
+  const TensorRef& r = it->second;
+  if (r.dtype != "F32") return set_error(CNNUE_ERR_FORMAT, "tensor `%s` is %s, expected F32", name, r.dtype.c_str());
+  uint64_t n = 1;
+  for (int64_t d : r.shape) n *= (uint64_t)d;
+  if (r.end - r.begin != n * 4)
+    return set_error(CNNUE_ERR_FORMAT, "tensor `%s`: %llu data bytes for %llu elements", name,
+                     (unsigned long long)(r.end - r.begin), (unsigned long long)n);
+  out.resize(n);
+  if (n) memcpy(out.data(), data + r.begin, n * 4);
+  return CNNUE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cnnue_az_board_from_fen(const char* fen, int8_t* board, int* side) {
+  if (!fen || !board || !side) return set_error(CNNUE_ERR_INVALID_ARG, "null fen, board or side");
+  int8_t b[kSq] = {0};
+  const char* p = fen;
+  while (*p == ' ' || *p == '\t') ++p;
+  int rank = 0, file = 0;
+  for (; *p && *p != ' ' && *p != '\t'; ++p) {
+    const char c = *p;
+    if (c == '/') {
+      if (file != 9) return set_error(CNNUE_ERR_FORMAT, "rank %d does not contain 9 files", rank);
+      if (++rank >= 10) return set_error(CNNUE_ERR_FORMAT, "expected 10 ranks in FEN");
+      file = 0;
+      continue;
+    }
+    if (c >= '0' && c <= '9') {
+      file += c - '0';
+      continue;
+    }
+    const char l = (c >= 'A' && c <= 'Z') ? (char)(c - 'A' + 'a') : c;
+    int kind;
+    switch (l) {
+      case 'k': kind = 0; break;
+      case 'a': kind = 1; break;
+      case 'b': case 'e': kind = 2; break;
+      case 'n': case 'h': kind = 3; break;
+      case 'r': kind = 4; break;
+      case 'c': kind = 5; break;
+      case 'p': kind = 6; break;
+      default: return set_error(CNNUE_ERR_FORMAT, "invalid piece: %c", c);
+    }
+    if (file >= 9) return set_error(CNNUE_ERR_FORMAT, "file overflow in FEN");
+    b[rank * 9 + file] = (int8_t)((c >= 'A' && c <= 'Z') ? kind + 1 : -(kind + 1));
+    ++file;
+  }
+  if (rank != 9) return set_error(CNNUE_ERR_FORMAT, "expected 10 ranks in FEN");
+  if (file != 9) return set_error(CNNUE_ERR_FORMAT, "rank %d does not contain 9 files", rank);
+  while (*p == ' ' || *p == '\t') ++p;
+  int s = 0;
+  if (*p) {
+    const char* q = p;
+    while (*q && *q != ' ' && *q != '\t') ++q;
+    const std::string tok(p, q);
+    if (tok == "w" || tok == "r") s = 0;
+    else if (tok == "b") s = 1;
+    else return set_error(CNNUE_ERR_FORMAT, "invalid side to move: %s", tok.c_str());
+  }
+  memcpy(board, b, sizeof(b));
+  *side = s;
+  return CNNUE_OK;
+}
+
+int cnnue_az_features(const int8_t* board, int perspective, uint32_t* items, int* count) {
+  if (!items || !count) return set_error(CNNUE_ERR_INVALID_ARG, "null items or count");
+  if (perspective != 0 && perspective != 1) return set_error(CNNUE_ERR_INVALID_ARG, "perspective %d", perspective);
+  int st = check_board(board);
+  if (st) return st;
+  *count = features(board, perspective, items);
+  return CNNUE_OK;
+}
+
+int cnnue_az_move_items(const int8_t* board, int from, int to, int perspective, uint32_t* delta,
+                        uint8_t* refresh, uint32_t* items, int* count) {
+  if (!delta || !refresh || !items || !count)
+    return set_error(CNNUE_ERR_INVALID_ARG, "null delta, refresh, items or count");
+  if (perspective != 0 && perspective != 1) return set_error(CNNUE_ERR_INVALID_ARG, "perspective %d", perspective);
+  int st = check_board(board);
+  if (st) return st;
+  if (from < 0 || from >= kSq || to < 0 || to >= kSq || from == to)
+    return set_error(CNNUE_ERR_INVALID_ARG, "move %d -> %d", from, to);
+  if (board[from] == 0) return set_error(CNNUE_ERR_INVALID_ARG, "no piece on square %d", from);
+  int8_t after[kSq];
+  memcpy(after, board, sizeof(after));
+  after[to] = after[from];
+  after[from] = 0;
+  int us0, them0, us1, them1;
+  buckets_of(board, perspective, &us0, &them0);
+  buckets_of(after, perspective, &us1, &them1);
+  delta[0] = delta[1] = delta[2] = CNNUE_AZ_NO_ITEM;
+  if (us0 != us1 || them0 != them1) {
+    *refresh = 1;
+    *count = features(after, perspective, items);
+    return CNNUE_OK;
+  }
+  *refresh = 0;
+  *count = 0;
+  delta[0] = pack(feature_of(board[from], from, perspective), us0, them0);
+  if (board[to] != 0) delta[1] = pack(feature_of(board[to], to, perspective), us0, them0);
+  delta[2] = pack(feature_of(board[from], to, perspective), us1, them1);
+  return CNNUE_OK;
+}
+
+int cnnue_az_tensor_info(int index, int64_t hidden, const char** name, int64_t* count) {
+  if (index < 0 || index >= CNNUE_AZ_TENSORS) return set_error(CNNUE_ERR_INVALID_ARG, "tensor index %d", index);
+  if (hidden <= 0) return set_error(CNNUE_ERR_INVALID_ARG, "hidden %lld", (long long)hidden);
+  if (name) *name = kSpecs[index].name;
+  if (count) *count = count_of(index, hidden);
+  return CNNUE_OK;
+}
+
+int cnnue_az_weights_random(int64_t hidden, uint64_t seed, cnnue_az_weights** out) {
+  if (!out) return set_error(CNNUE_ERR_INVALID_ARG, "null out");
+  *out = nullptr;
+  if (hidden <= 0 || hidden > (1 << 20)) return set_error(CNNUE_ERR_INVALID_ARG, "invalid hidden_size %lld", (long long)hidden);
+  std::unique_ptr<cnnue_az_weights> w(new (std::nothrow) cnnue_az_weights);
+  if (!w) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
+  w->hidden = hidden;
+  try {
+    for (int i = 0; i < CNNUE_AZ_TENSORS; ++i) w->t[i].assign((size_t)count_of(i, hidden), 0.0f);
+  } catch (const std::bad_alloc&) {
+    return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
+  }
+  // Draw order of random_with_arch: input_hidden, value_head_hidden,
+  // value_threat_embedding, policy_context_hidden, policy_accumulator_hidden;
+  // every other tensor starts at zero.
+  SplitMix rng{seed};
+  const float head_scale = std::sqrt(2.0f / (float)hidden) * 0.5f;
+  for (float& x : w->t[0]) x = rng.weight(0.015f);
+  for (float& x : w->t[7]) x = rng.weight(head_scale);
+  for (float& x : w->t[10]) x = rng.weight(0.02f);
+  for (float& x : w->t[15]) x = rng.weight(head_scale);
+  for (float& x : w->t[17]) x = rng.weight(head_scale);
+  *out = w.release();
+  return CNNUE_OK;
+}
+
+int cnnue_az_weights_load(const char* path, cnnue_az_weights** out) {
+  if (!path || !out) return set_error(CNNUE_ERR_INVALID_ARG, "null path or out");
+  *out = nullptr;
+  std::vector<char> bytes;
+  int st = read_file(path, bytes);
+  if (st) return st;
+  std::map<std::string, TensorRef> tensors;
+  const char* data = nullptr;
+  if ((st = parse_safetensors(bytes, tensors, &data))) return st;
+  std::vector<float> version;
+  if ((st = load_f32(tensors, data, "az_model_format_version", version))) return st;
+  if (version.empty()) return set_error(CNNUE_ERR_FORMAT, "missing AZ model format");
+  if (version[0] != CNNUE_AZ_FORMAT_VERSION)
+    return set_error(CNNUE_ERR_FORMAT, "unsupported AZ model format %g; expected v%g", (double)version[0],
+                     (double)CNNUE_AZ_FORMAT_VERSION);
+  std::unique_ptr<cnnue_az_weights> w(new (std::nothrow) cnnue_az_weights);
+  if (!w) return set_error(CNNUE_ERR_IO, "out of host memory");
+  if ((st = load_f32(tensors, data, "hidden_bias", w->t[6]))) return st;
+  w->hidden = (int64_t)w->t[6].size();
+  if (w->hidden == 0) return set_error(CNNUE_ERR_FORMAT, "aznnue arch invalid: invalid hidden_size 0");
+  for (int i = 0; i < CNNUE_AZ_TENSORS; ++i) {
+    if (i != 6 && (st = load_f32(tensors, data, kSpecs[i].name, w->t[i]))) return st;
+    const int64_t expected = count_of(i, w->hidden);
+    if ((int64_t)w->t[i].size() != expected)
+      return set_error(CNNUE_ERR_FORMAT, "az model tensor `%s` length mismatch: got %lld, expected %lld",
+                       kSpecs[i].name, (long long)w->t[i].size(), (long long)expected);
+  }
+  *out = w.release();
+  return CNNUE_OK;
+}
+
+int cnnue_az_weights_save(const cnnue_az_weights* w, const char* path) {
+  if (!w || !path) return set_error(CNNUE_ERR_INVALID_ARG, "null weights or path");
+  struct Entry {
+    std::vector<int64_t> shape;
+    const float* data;
+    uint64_t n;
+  };
+  static const float kVersion = CNNUE_AZ_FORMAT_VERSION;
+  std::map<std::string, Entry> entries;
+  entries["az_model_format_version"] = Entry{{1}, &kVersion, 1};
+  for (int i = 0; i < CNNUE_AZ_TENSORS; ++i)
+    entries[kSpecs[i].name] = Entry{shape_of(i, w->hidden), w->t[i].data(), (uint64_t)w->t[i].size()};
+  std::string header = "{";
+  uint64_t offset = 0;
+  bool first = true;
+  for (const auto& e : entries) {
+    if (!first) header += ",";
+    first = false;
+    header += "\"" + e.first + "\":{\"dtype\":\"F32\",\"shape\":[";
+    for (size_t d = 0; d < e.second.shape.size(); ++d) {
+      if (d) header += ",";
+      header += std::to_string(e.second.shape[d]);
+    }
+    header += "],\"data_offsets\":[" + std::to_string(offset) + "," + std::to_string(offset + 4 * e.second.n) + "]}";
+    offset += 4 * e.second.n;
+  }
+  header += "}";
+  while (header.size() % 8) header += ' ';
+  File f(fopen(path, "wb"));
+  if (!f) return set_error(CNNUE_ERR_IO, "cannot open %s for writing", path);
+  uint8_t len[8];
+  for (int i = 0; i < 8; ++i) len[i] = (uint8_t)((uint64_t)header.size() >> (8 * i));
+  bool ok = fwrite(len, 1, 8, f.get()) == 8 && fwrite(header.data(), 1, header.size(), f.get()) == header.size();
+  for (const auto& e : entries)
+    ok = ok && (e.second.n == 0 || fwrite(e.second.data, 4, e.second.n, f.get()) == e.second.n);
+  FILE* raw = f.release();
+  ok = (fclose(raw) == 0) && ok;
+  if (!ok) return set_error(CNNUE_ERR_IO, "short write on %s", path);
+  return CNNUE_OK;
+}
+
+int cnnue_az_weights_destroy(cnnue_az_weights* w) {
+  delete w;
+  return CNNUE_OK;
+}
+
+int64_t cnnue_az_weights_hidden(const cnnue_az_weights* w) { return w ? w->hidden : 0; }
+
+int cnnue_az_weights_tensor(cnnue_az_weights* w, int index, float** data, int64_t* count) {
+  if (!w || !data) return set_error(CNNUE_ERR_INVALID_ARG, "null weights or data");
+  if (index < 0 || index >= CNNUE_AZ_TENSORS) return set_error(CNNUE_ERR_INVALID_ARG, "tensor index %d", index);
+  *data = w->t[index].data();
+  if (count) *count = (int64_t)w->t[index].size();
+  return CNNUE_OK;
+}
+
+}  // extern "C"

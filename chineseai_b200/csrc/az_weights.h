@@ -1,0 +1,31 @@
+// az_weights.h - host weights of the AZ-NNUE evaluator, shared by the host
+// code (az_host.cpp) and the device model (az.cu).
+#pragma once
+
+#include <vector>
+
+#include "../../include/cnnue.h"
+
+// The 22 fp32 tensors of az_weight_tensors! (src/az.rs:241-278) in that order.
+struct cnnue_az_weights {
+  int64_t hidden = 0;
+  std::vector<float> t[CNNUE_AZ_TENSORS];
+};
+
+namespace cnnue {
+namespace az {
+// Tensor positions in cnnue_az_weights::t.
+enum Tensor {
+  kInputHidden = 0,
+  kInputPiece = 1,
+  kInputRank = 2,
+  kInputFile = 3,
+  kInputKingPiece = 4,
+  kRuleContext = 5,
+  kHiddenBias = 6,
+  kValueHeadHidden = 7,
+  kValueHeadBias = 8,
+  kValueHeadOutput = 9,
+};
+}  // namespace az
+}  // namespace cnnue

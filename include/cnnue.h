@@ -293,6 +293,112 @@ int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, 
                  float grad_scale, float lr, float beta1, float beta2, float eps, int step,
                  void* stream);
 
+/* ---- reference-native AZ-NNUE evaluator (src/az.rs, src/nnue.rs) -------- */
+/* Squares are rank * 9 + file with rank 0 the first rank of a FEN (Black's
+ * back rank), as src/xiangqi/geom.rs:28-30.  A board is int8_t[90]: 0 empty,
+ * +(kind+1) Red, -(kind+1) Black, kind = General 0, Advisor 1, Elephant 2,
+ * Horse 3, Rook 4, Cannon 5, Soldier 6 (piece_kind_index,
+ * src/xiangqi/types.rs:206-216).  Perspective / side: 0 Red, 1 Black.
+ * An item packs one piece of one perspective as feature | us_bucket << 11 |
+ * them_bucket << 15 (pack_feature, src/az/fused_feature_pool.rs:130-132):
+ * feature = (own ? 0 : 7 + kind) * 90 + canonical square (sq for Red,
+ * 89 - sq for Black), buckets = the king-palace buckets of both generals
+ * (src/az.rs:168-203), 4 when a general is absent. */
+#define CNNUE_AZ_SQUARES 90
+#define CNNUE_AZ_INPUT 1260          /* 14 piece kinds x 90 squares            */
+#define CNNUE_AZ_TRUNK_ROWS 1545     /* input 1260 + piece 14 + rank 10 + file 9 + king-piece 252 */
+#define CNNUE_AZ_VALUE_HEAD 96
+#define CNNUE_AZ_RULE_CONTEXT 7
+#define CNNUE_AZ_WDL 3
+#define CNNUE_AZ_TENSORS 22
+#define CNNUE_AZ_MAX_HIDDEN 512
+#define CNNUE_AZ_NO_ITEM 0xffffffffu
+#define CNNUE_AZ_FORMAT_VERSION 20.0f /* az_model_format_version (src/version.rs:5) */
+
+/* FEN board field and side (src/xiangqi/mod.rs:163-207): ranks split by '/',
+ * digits skip files, letters k a b/e n/h r c p, uppercase Red; side "w"/"r"
+ * Red, "b" Black, missing = Red.  CNNUE_ERR_FORMAT on a malformed FEN. */
+int cnnue_az_board_from_fen(const char* fen, int8_t* board, int* side);
+/* Items of one perspective in board-scan order (fill_sparse_features_az,
+ * src/nnue.rs:31-43, with refresh_perspective's perspective,
+ * src/az.rs:413-426).  items holds 90; *count gets the piece count. */
+int cnnue_az_features(const int8_t* board, int perspective, uint32_t* items, int* count);
+/* What apply_transition_for_perspective (src/az.rs:439-485) adds and removes
+ * for the move from -> to on `board` (the position before the move): if the
+ * perspective's (us, them) bucket pair changes, *refresh = 1 and items/count
+ * get the child's features; else *refresh = 0 and delta = {moved piece at
+ * from, captured piece at to or CNNUE_AZ_NO_ITEM, moved piece at to}. */
+int cnnue_az_move_items(const int8_t* board, int from, int to, int perspective, uint32_t* delta,
+                        uint8_t* refresh, uint32_t* items, int* count);
+
+/* Host weights: the 22 fp32 tensors of az_weight_tensors! (src/az.rs:241-278)
+ * in that order, row-major. */
+typedef struct cnnue_az_weights cnnue_az_weights;
+/* Name and element count of tensor `index` at hidden size `hidden`. */
+int cnnue_az_tensor_info(int index, int64_t hidden, const char** name, int64_t* count);
+/* AzNnue::random(hidden, seed) (src/az.rs:1339-1431): the same SplitMix64
+ * draws in the same order, so the tensors equal the reference's. */
+int cnnue_az_weights_random(int64_t hidden, uint64_t seed, cnnue_az_weights** out);
+/* AzNnue::load / save (src/az.rs:1437-1529, validate :2453-2499): a
+ * safetensors file of F32 tensors named as az_weight_tensors! plus
+ * az_model_format_version = [20.0].  CNNUE_ERR_IO if the file cannot be read
+ * or written, CNNUE_ERR_FORMAT for a bad header, a missing tensor, another
+ * dtype, a wrong format tag or a length mismatch (the hidden size comes from
+ * hidden_bias). */
+int cnnue_az_weights_load(const char* path, cnnue_az_weights** out);
+int cnnue_az_weights_save(const cnnue_az_weights* weights, const char* path);
+int cnnue_az_weights_destroy(cnnue_az_weights* weights);
+int64_t cnnue_az_weights_hidden(const cnnue_az_weights* weights);
+/* Host view of tensor `index` (writable; a model created later sees edits). */
+int cnnue_az_weights_tensor(cnnue_az_weights* weights, int index, float** data, int64_t* count);
+
+/* Device copy of the trunk (the 5 input tables concatenated as [1545][H],
+ * hidden_bias, rule_context_hidden) and the value head.  Hidden sizes 1..127
+ * and multiples of 4 up to 512. */
+typedef struct cnnue_az_model cnnue_az_model;
+int cnnue_az_model_create(const cnnue_az_weights* weights, int device, cnnue_az_model** out);
+int cnnue_az_model_destroy(cnnue_az_model* model);
+/* Workspace of the AZ entry points (the status word). */
+size_t cnnue_az_workspace_bytes(void);
+
+/* Accumulator refresh of n_lists item lists (CSR: offsets[n_lists+1] into
+ * d_items): acc[l] = hidden_bias, + the input row of every item in list
+ * order, + for every item its piece, rank, file, king-piece(us) and
+ * king-piece(them) rows, one fp32 add per row per column in exactly that
+ * order (input_embedding_linear_into_slice, src/az.rs:2049-2076, and
+ * add_factorized_structure_into, :1920-2042), so the result is bit-identical
+ * to the reference.  acc is [n_lists][H]; the two perspectives of a node are
+ * two consecutive lists ([2][H], AzEvalAccumulator::refresh, src/az.rs:384-411).
+ * An item with feature >= 1260 or a bucket > 8 is skipped and flagged
+ * CNNUE_STATUS_BAD_INDEX; bad offsets are flagged CNNUE_STATUS_BAD_OFFSETS. */
+int cnnue_az_refresh(const cnnue_az_model* model, const uint32_t* d_items, uint32_t n_items,
+                     const uint32_t* d_offsets, int64_t n_lists, float* d_acc, void* d_workspace,
+                     size_t workspace_bytes, void* stream);
+/* Incremental accumulator update per list (apply_transition_for_perspective,
+ * src/az.rs:439-485; add_canonical_piece_contribution, :509-566): if
+ * d_refresh[l] & 1, child[l] = the refresh of list l of d_items/d_offsets;
+ * else child[l] = parent[l] - 6 rows(delta[3l]) - 6 rows(delta[3l+1], unless
+ * CNNUE_AZ_NO_ITEM) + 6 rows(delta[3l+2]), each item's rows in the order
+ * input, piece, rank, file, king(us), king(them): bit-identical to the
+ * reference.  d_items may be NULL when no list refreshes. */
+int cnnue_az_transition(const cnnue_az_model* model, const float* d_parent, const uint32_t* d_delta,
+                        const uint8_t* d_refresh, const uint32_t* d_items, uint32_t n_items,
+                        const uint32_t* d_offsets, int64_t n_lists, float* d_child,
+                        void* d_workspace, size_t workspace_bytes, void* stream);
+/* Value of n positions from side-to-move accumulators: x = acc (+ the rule
+ * context rows scaled by d_rule[p][k] for non-zero entries,
+ * add_rule_context_to_hidden src/az.rs:1903-1918), ReLU, RMSNorm with eps
+ * 1e-6 (src/az.rs:3020-3040, :3110-3126), value head 96 ReLU units, 3 logits
+ * (+ d_threat[p][k] when not NULL), softmax, q = W - L
+ * (value_wdl_from_hidden_into, src/az.rs:2133-2157; softmax_fixed3,
+ * :2563-2575).  With d_side == NULL d_acc is [n][H]; else it is [n][2][H]
+ * (both perspectives of a node) and position p reads perspective d_side[p].
+ * d_rule ([n][7]) and d_threat ([n][3]) may be NULL.  Writes d_wdl [n][3]
+ * and d_q [n] (AzEvalOutput). */
+int cnnue_az_value(const cnnue_az_model* model, const float* d_acc, const uint8_t* d_side,
+                   const float* d_rule, const float* d_threat, int64_t n, float* d_wdl, float* d_q,
+                   void* stream);
+
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is
  * replaced by the mixed output at every draw. */

@@ -179,3 +179,88 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
     out = np.empty_like(a)
     h.oracle_bf16_round_array(_p(a), _p(out), a.size)
     return out
+
+
+# ---- AZ-NNUE (reference-native) ---------------------------------------------
+def _az_setup(h):
+    if getattr(h, "_az_ready", False):
+        return
+    P, i64, i32, u64 = C.c_void_p, C.c_int64, C.c_int, C.c_uint64
+    h.oracle_az_tensor_elements.argtypes = [i32, i32]
+    h.oracle_az_tensor_elements.restype = i64
+    h.oracle_az_random.argtypes = [i32, u64, P]
+    h.oracle_az_random.restype = None
+    h.oracle_az_features.argtypes = [P, i32, P]
+    h.oracle_az_features.restype = i32
+    h.oracle_az_refresh.argtypes = [P, P, i32, P, P, i64, P]
+    h.oracle_az_refresh.restype = i32
+    h.oracle_az_transition.argtypes = [P, P, i32, P, P, P, P, P, i64, P]
+    h.oracle_az_transition.restype = i32
+    h.oracle_az_value.argtypes = [P, P, P, P, i32, P, P, P, i64, P, P]
+    h.oracle_az_value.restype = None
+    h._az_ready = True
+
+
+def _az():
+    h = lib()
+    _az_setup(h)
+    return h
+
+
+def az_random(hidden: int, seed: int):
+    """AzNnue::random(hidden, seed) restated: the 22 tensors, flat float32."""
+    h = _az()
+    arrays = [np.zeros(h.oracle_az_tensor_elements(i, hidden), np.float32) for i in range(22)]
+    ptrs = (C.c_void_p * 22)(*[a.ctypes.data for a in arrays])
+    h.oracle_az_random(hidden, seed, ptrs)
+    return arrays
+
+
+def az_features(board: np.ndarray, perspective: int) -> np.ndarray:
+    items = np.zeros(90, np.uint32)
+    b = np.ascontiguousarray(board, np.int8)
+    n = _az().oracle_az_features(_p(b), perspective, _p(items))
+    return items[:n].copy()
+
+
+def az_trunk(tensors) -> tuple:
+    """(trunk [1545][H], bias [H]) from the 22 tensors."""
+    trunk = np.ascontiguousarray(np.concatenate([np.asarray(tensors[i], np.float32).reshape(-1) for i in range(5)]))
+    return trunk, np.ascontiguousarray(np.asarray(tensors[6], np.float32).reshape(-1))
+
+
+def az_refresh(tensors, hidden: int, items: np.ndarray, offsets: np.ndarray):
+    trunk, bias = az_trunk(tensors)
+    n_lists = len(offsets) - 1
+    acc = np.zeros((max(n_lists, 1), hidden), np.float32)
+    it = np.ascontiguousarray(items, np.uint32) if len(items) else np.zeros(1, np.uint32)
+    st = _az().oracle_az_refresh(_p(trunk), _p(bias), hidden, _p(it), _p(np.ascontiguousarray(offsets, np.uint32)),
+                                 n_lists, _p(acc))
+    return st, acc[:n_lists]
+
+
+def az_transition(tensors, hidden: int, parent: np.ndarray, delta: np.ndarray, refresh: np.ndarray,
+                  items: np.ndarray, offsets: np.ndarray):
+    trunk, bias = az_trunk(tensors)
+    n_lists = len(refresh)
+    child = np.zeros((max(n_lists, 1), hidden), np.float32)
+    it = np.ascontiguousarray(items, np.uint32) if len(items) else np.zeros(1, np.uint32)
+    st = _az().oracle_az_transition(_p(trunk), _p(bias), hidden, _p(np.ascontiguousarray(parent, np.float32)),
+                                    _p(np.ascontiguousarray(delta, np.uint32)),
+                                    _p(np.ascontiguousarray(refresh, np.uint8)), _p(it),
+                                    _p(np.ascontiguousarray(offsets, np.uint32)), n_lists, _p(child))
+    return st, child[:n_lists]
+
+
+def az_value(tensors, hidden: int, hidden_rows: np.ndarray, rule=None, threat=None):
+    """(wdl [n][3], q [n]) from side-to-move accumulators [n][H]."""
+    n = hidden_rows.shape[0]
+    wdl = np.zeros((max(n, 1), 3), np.float32)
+    q = np.zeros(max(n, 1), np.float32)
+    f = [np.ascontiguousarray(np.asarray(tensors[i], np.float32).reshape(-1)) for i in (5, 7, 8, 9)]
+    r = None if rule is None else np.ascontiguousarray(rule, np.float32)
+    t = None if threat is None else np.ascontiguousarray(threat, np.float32)
+    _az().oracle_az_value(_p(f[0]), _p(f[1]), _p(f[2]), _p(f[3]), hidden,
+                          _p(np.ascontiguousarray(hidden_rows, np.float32)), None if r is None else _p(r),
+                          None if t is None else _p(t), n, _p(wdl), _p(q))
+    return wdl[:n], q[:n]

@@ -37,6 +37,7 @@
  *       - fp32: clipped ReLU [0,1] on FT output and between layers, FT sum in
  *         index order starting from the bias.
  */
+#include <float.h>
 #include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
@@ -554,5 +555,214 @@ void oracle_adam(float* w, float* m, float* v, const float* g, int64_t count, fl
     m[i] = beta1 * m[i] + (1.f - beta1) * gi;
     v[i] = beta2 * v[i] + (1.f - beta2) * gi * gi;
     w[i] -= lr * (m[i] / c1) / (sqrtf(v[i] / c2) + eps);
+  }
+}
+
+/* ---- AZ-NNUE, the reference's own network (reference-native) ----------- */
+/* Restates src/nnue.rs:25-43 (features), src/az.rs:155-203 (buckets,
+ * structural rows), :1339-1431 (AzNnue::random), :2049-2076 + :1920-2042
+ * (FT gather order: bias, every input row in feature order, then for every
+ * feature its piece, rank, file, king(us), king(them) rows), :439-566
+ * (incremental transition), :1903-1918 (rule context), :3020-3126 (ReLU,
+ * RMSNorm eps 1e-6), :2133-2157 + :2563-2575 (value head, WDL softmax). */
+#define AZ_SQ 90
+#define AZ_INPUT 1260
+#define AZ_ROWS 1545
+#define AZ_VALUE 96
+
+static uint64_t az_mix(uint64_t v) {
+  v += 0x9E3779B97F4A7C15ull;
+  uint64_t m = v;
+  m = (m ^ (m >> 30)) * 0xBF58476D1CE4E5B9ull;
+  m = (m ^ (m >> 27)) * 0x94D049BB133111EBull;
+  return m ^ (m >> 31);
+}
+
+/* SplitMix64::unit_f32 / weight, src/az.rs:3161-3168. */
+static float az_weight(uint64_t* st, float scale) {
+  *st = az_mix(*st);
+  const float u = (float)((double)(*st >> 11) * (1.0 / 9007199254740992.0));
+  return (u * 2.0f - 1.0f) * scale;
+}
+
+/* Tensor element counts in az_weight_tensors! order (src/az.rs:241-278). */
+int64_t oracle_az_tensor_elements(int i, int h) {
+  static const int64_t fixed[22] = {0, 0, 0, 0, 0, 0, 0, 0, 96, 3 * 96, 57702LL * 64, 3 * 128,
+                                    16 * 128, 2086, 32, 0, 2086 * 16, 0, 2086 * 32, 2396815,
+                                    199458, 934976};
+  switch (i) {
+    case 0: return 1260LL * h;
+    case 1: return 14LL * h;
+    case 2: return 10LL * h;
+    case 3: return 9LL * h;
+    case 4: return 252LL * h;
+    case 5: return 7LL * h;
+    case 6: return h;
+    case 7: return 96LL * h;
+    case 15: return 16LL * h;
+    case 17: return 32LL * h;
+    default: return (i >= 0 && i < 22) ? fixed[i] : -1;
+  }
+}
+
+/* AzNnue::random_with_arch, src/az.rs:1339-1431: tensors[i] must hold
+ * oracle_az_tensor_elements(i, h) floats; draws in the reference's order. */
+void oracle_az_random(int h, uint64_t seed, float** t) {
+  for (int i = 0; i < 22; ++i) memset(t[i], 0, sizeof(float) * (size_t)oracle_az_tensor_elements(i, h));
+  uint64_t st = seed;
+  const float hs = sqrtf(2.0f / (float)(h > 1 ? h : 1)) * 0.5f;
+  for (int64_t i = 0; i < 1260LL * h; ++i) t[0][i] = az_weight(&st, 0.015f);
+  for (int64_t i = 0; i < 96LL * h; ++i) t[7][i] = az_weight(&st, hs);
+  for (int64_t i = 0; i < 57702LL * 64; ++i) t[10][i] = az_weight(&st, 0.02f);
+  for (int64_t i = 0; i < 16LL * h; ++i) t[15][i] = az_weight(&st, hs);
+  for (int64_t i = 0; i < 32LL * h; ++i) t[17][i] = az_weight(&st, hs);
+}
+
+/* canonical_general_bucket, src/az.rs:194-203. */
+static int az_bucket(int piece_index, int sq) {
+  const int o = piece_index < 7 ? sq : AZ_SQ - 1 - sq;
+  int f = o % 9, r = o / 9;
+  f = f < 3 ? 3 : (f > 5 ? 5 : f);
+  r = r < 7 ? 7 : (r > 9 ? 9 : r);
+  return (r - 7) * 3 + (f - 3);
+}
+
+/* Features of one perspective (src/nnue.rs:25-43 with the perspective in
+ * place of the side to move, as refresh_perspective does, src/az.rs:413-426),
+ * packed feature | us << 11 | them << 15 with the king buckets of
+ * canonical_general_buckets_from_features (src/az.rs:168-184).  board: 0
+ * empty, +1..+7 Red kind+1, -1..-7 Black kind+1.  Returns the count. */
+int oracle_az_features(const int8_t* board, int perspective, uint32_t* items) {
+  int n = 0, us = 4, them = 4;
+  uint32_t feat[AZ_SQ];
+  for (int sq = 0; sq < AZ_SQ; ++sq) {
+    const int v = board[sq];
+    if (v == 0) continue;
+    const int color = v > 0 ? 0 : 1, kind = (v > 0 ? v : -v) - 1;
+    const int piece_index = (color == perspective ? 0 : 7) + kind;
+    const int csq = perspective == 0 ? sq : AZ_SQ - 1 - sq;
+    feat[n++] = (uint32_t)(piece_index * AZ_SQ + csq);
+  }
+  for (int i = 0; i < n; ++i) {
+    const int pi = (int)feat[i] / AZ_SQ, s = (int)feat[i] % AZ_SQ;
+    if (pi == 0) us = az_bucket(0, s);
+    if (pi == 7) them = az_bucket(7, s);
+  }
+  for (int i = 0; i < n; ++i) items[i] = feat[i] | ((uint32_t)us << 11) | ((uint32_t)them << 15);
+  return n;
+}
+
+/* The six trunk rows of an item (offsets into the concatenated [1545][H]
+ * trunk table: input 0, piece 1260, rank 1274, file 1284, king-piece 1293). */
+static int az_rows(uint32_t item, int rows[6]) {
+  const int feature = item & 0x7ff, us = (item >> 11) & 0xf, them = (item >> 15) & 0xf;
+  if (feature >= AZ_INPUT || us > 8 || them > 8) return 0;
+  const int piece = feature / 90, sq = feature % 90;
+  rows[0] = feature;
+  rows[1] = 1260 + piece;
+  rows[2] = 1274 + sq / 9;
+  rows[3] = 1284 + sq % 9;
+  rows[4] = 1293 + us * 14 + piece;
+  rows[5] = 1293 + (9 + them) * 14 + piece;
+  return 1;
+}
+
+/* input_embedding_linear_into_slice for each list: acc = bias, + input row of
+ * every item, + its five structural rows per item (in item order).  table =
+ * [1545][H] concatenation.  Returns 2 on a bad item (skipped). */
+int oracle_az_refresh(const float* table, const float* bias, int h, const uint32_t* items,
+                      const uint32_t* offsets, int64_t n_lists, float* acc) {
+  int status = 0;
+  for (int64_t l = 0; l < n_lists; ++l) {
+    float* a = acc + l * h;
+    for (int j = 0; j < h; ++j) a[j] = bias[j];
+    for (uint32_t i = offsets[l]; i < offsets[l + 1]; ++i) {
+      int r[6];
+      if (!az_rows(items[i], r)) { status = 2; continue; }
+      for (int j = 0; j < h; ++j) a[j] += table[(int64_t)r[0] * h + j];
+    }
+    for (uint32_t i = offsets[l]; i < offsets[l + 1]; ++i) {
+      int r[6];
+      if (!az_rows(items[i], r)) continue;
+      for (int k = 1; k < 6; ++k)
+        for (int j = 0; j < h; ++j) a[j] += table[(int64_t)r[k] * h + j];
+    }
+  }
+  return status;
+}
+
+/* apply_transition_for_perspective (src/az.rs:439-485): refresh[l] -> the
+ * refresh of list l; else child = parent - rows(from) - rows(captured)
+ * + rows(to), each item's six rows in order (add_canonical_piece_contribution,
+ * src/az.rs:509-566).  delta[3l..3l+2] = from, captured (or 0xffffffff), to. */
+int oracle_az_transition(const float* table, const float* bias, int h, const float* parent,
+                         const uint32_t* delta, const uint8_t* refresh, const uint32_t* items,
+                         const uint32_t* offsets, int64_t n_lists, float* child) {
+  int status = 0;
+  for (int64_t l = 0; l < n_lists; ++l) {
+    float* c = child + l * h;
+    if (refresh[l] & 1) {
+      status |= oracle_az_refresh(table, bias, h, items, offsets + l, 1, c);
+      continue;
+    }
+    for (int j = 0; j < h; ++j) c[j] = parent[l * h + j];
+    for (int q = 0; q < 3; ++q) {
+      const uint32_t it = delta[3 * l + q];
+      if (it == 0xffffffffu) continue;
+      int r[6];
+      if (!az_rows(it, r)) { status = 2; continue; }
+      for (int k = 0; k < 6; ++k)
+        for (int j = 0; j < h; ++j) {
+          const float w = table[(int64_t)r[k] * h + j];
+          c[j] = q < 2 ? c[j] - w : c[j] + w;
+        }
+    }
+  }
+  return status;
+}
+
+/* Value of side-to-move accumulators: + rule context (non-zero entries,
+ * src/az.rs:1903-1918), ReLU, RMSNorm (eps 1e-6), value head 96 ReLU units,
+ * 3 WDL logits + threat logits, softmax, q = W - L.  rule [n][7] and threat
+ * [n][3] may be NULL. */
+void oracle_az_value(const float* rule_rows, const float* vh, const float* vb, const float* vo, int h,
+                     const float* hidden, const float* rule, const float* threat, int64_t n,
+                     float* wdl, float* q) {
+  float x[4096], v[AZ_VALUE];
+  if (h > 4096) return;
+  for (int64_t p = 0; p < n; ++p) {
+    for (int j = 0; j < h; ++j) x[j] = hidden[p * h + j];
+    if (rule)
+      for (int k = 0; k < 7; ++k) {
+        const float r = rule[p * 7 + k];
+        if (r == 0.f) continue;
+        for (int j = 0; j < h; ++j) x[j] += r * rule_rows[k * h + j];
+      }
+    float ss = 0.f;
+    for (int j = 0; j < h; ++j) {
+      x[j] = x[j] > 0.f ? x[j] : 0.f;
+      ss += x[j] * x[j];
+    }
+    const float inv = 1.f / sqrtf(ss / (float)h + 1e-6f);
+    for (int j = 0; j < h; ++j) x[j] *= inv;
+    for (int k = 0; k < AZ_VALUE; ++k) {
+      float s = vb[k];
+      for (int j = 0; j < h; ++j) s += vh[k * h + j] * x[j];
+      v[k] = s > 0.f ? s : 0.f;
+    }
+    float lg[3];
+    for (int o = 0; o < 3; ++o) {
+      float s = 0.f;
+      for (int k = 0; k < AZ_VALUE; ++k) s += vo[o * AZ_VALUE + k] * v[k];
+      lg[o] = s + (threat ? threat[p * 3 + o] : 0.f);
+    }
+    float mx = lg[0] > lg[1] ? lg[0] : lg[1];
+    mx = mx > lg[2] ? mx : lg[2];
+    float e[3];
+    for (int o = 0; o < 3; ++o) e[o] = expf(lg[o] - mx);
+    float sum = e[0] + e[1] + e[2];
+    if (sum < FLT_MIN) sum = FLT_MIN; /* .max(f32::MIN_POSITIVE) */
+    for (int o = 0; o < 3; ++o) wdl[p * 3 + o] = e[o] / sum;
+    q[p] = wdl[p * 3] - wdl[p * 3 + 2];
   }
 }

@@ -1,0 +1,190 @@
+"""GPU parity of the reference-native AZ-NNUE evaluator against the oracle.
+
+Refresh and transition are bit-identical to the oracle (the reference's row
+order, one fp32 add per row per column); the value head is within 1e-4 of it
+(the reference's dot products run in another summation order).  Cases: board
+lists of random positions, ragged synthetic lists (empty, > 32 items), hidden
+sizes on both the float4 and the scalar column paths, bad items and offsets,
+in-place transitions, the reference's incremental-equals-refresh walk
+(src/az.rs:3470-3495) and its neutral-initial-value check
+(src/az.rs:3354-3363)."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from chineseai_b200 import az
+from chineseai_b200.quantized import as_device
+
+from ._azutil import random_item_lists, trained_like
+
+pytestmark = pytest.mark.gpu
+
+_MODELS = {}
+
+
+def _model(hidden, seed=20260807):
+    key = (hidden, seed)
+    if key not in _MODELS:
+        w = az.AzWeights.random(hidden, seed)
+        trained_like(w, seed % 1000)
+        _MODELS[key] = (w, w.tensors(), az.AzModel(w, device=0))
+    return _MODELS[key]
+
+
+def _dev(a):
+    return as_device(np.ascontiguousarray(a), torch.device("cuda", 0))
+
+
+@pytest.mark.parametrize("hidden", [128, 256, 512, 32, 16, 100, 4, 7])
+def test_refresh_bit_exact_on_boards(hidden):
+    w, tensors, model = _model(hidden)
+    boards = az.random_boards(700, seed=hidden)
+    items, offsets = az.node_lists(boards)
+    acc = model.refresh(_dev(items), _dev(offsets))
+    assert model.read_status() == 0
+    st, ref = oracle.az_refresh(tensors, hidden, items, offsets)
+    assert st == 0
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("hidden", [128, 20])
+def test_refresh_bit_exact_on_ragged_lists(hidden):
+    w, tensors, model = _model(hidden)
+    lists = random_item_lists(1500, seed=5, max_len=90)
+    items, offsets = az.pack_lists(lists)
+    acc = model.refresh(_dev(items), _dev(offsets))
+    assert model.read_status() == 0
+    st, ref = oracle.az_refresh(tensors, hidden, items, offsets)
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+    # an empty list is the hidden bias
+    np.testing.assert_array_equal(acc[0].cpu().numpy(), w.tensor("hidden_bias"))
+
+
+def test_refresh_flags_bad_items_and_skips_them():
+    w, tensors, model = _model(128)
+    lists = random_item_lists(64, seed=6, max_len=40, empty_every=1000)
+    lists[3][2] = 1300                      # feature >= 1260
+    lists[10][0] = 5 | (9 << 11)            # us bucket 9
+    lists[20][5] = 7 | (3 << 11) | (12 << 15)  # them bucket 12
+    items, offsets = az.pack_lists(lists)
+    acc = model.refresh(_dev(items), _dev(offsets))
+    assert model.read_status() == 2  # CNNUE_ERR_BAD_INDEX
+    st, ref = oracle.az_refresh(tensors, 128, items, offsets)
+    assert st == 2
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+    bad = offsets.copy()
+    bad[5] = bad[6] + 1  # not monotone
+    model.refresh(_dev(items), _dev(bad))
+    assert model.read_status() == 3  # CNNUE_ERR_BAD_OFFSETS
+    assert model.read_status() == 0  # read clears
+
+
+def _moves(boards, seed):
+    rng = np.random.default_rng(seed)
+    deltas, refresh, lists, afters = [], [], [], []
+    for b in boards:
+        frm, to = az.random_move(b, rng)
+        afters.append(az.apply_move(b, frm, to))
+        for p in (0, 1):
+            m = az.move_items(b, frm, to, p)
+            deltas.append(m.delta)
+            refresh.append(m.refresh)
+            lists.append(m.items)
+    items, offsets = az.pack_lists(lists)
+    return np.stack(deltas), np.array(refresh, np.uint8), items, offsets, np.stack(afters)
+
+
+@pytest.mark.parametrize("hidden", [128, 512, 16, 7])
+def test_transition_bit_exact(hidden):
+    w, tensors, model = _model(hidden)
+    boards = az.random_boards(800, seed=100 + hidden)
+    p_items, p_off = az.node_lists(boards)
+    parent = model.refresh(_dev(p_items), _dev(p_off))
+    delta, refresh, items, offsets, afters = _moves(boards, seed=hidden)
+    assert 0 < refresh.sum() < len(refresh)
+    child = model.transition(parent, _dev(delta), _dev(refresh), _dev(items), _dev(offsets))
+    assert model.read_status() == 0
+    st, ref = oracle.az_transition(tensors, hidden, parent.cpu().numpy(), delta, refresh, items, offsets)
+    assert st == 0
+    np.testing.assert_array_equal(child.cpu().numpy(), ref)
+    # in place gives the same bits
+    model.transition(parent, _dev(delta), _dev(refresh), _dev(items), _dev(offsets), out=parent)
+    np.testing.assert_array_equal(parent.cpu().numpy(), ref)
+    # and the incremental child is the refresh of the child board within 2e-5
+    full = model.refresh(*[_dev(a) for a in az.node_lists(afters)])
+    assert (parent - full).abs().max().item() < 2e-5
+
+
+def test_transition_without_refresh_lists_takes_null_items():
+    w, tensors, model = _model(128)
+    boards = az.random_boards(300, seed=77)
+    parent = model.refresh(*[_dev(a) for a in az.node_lists(boards)])
+    delta, refresh, items, offsets, _ = _moves(boards, seed=78)
+    keep = refresh == 0
+    delta, parent_k = delta[keep], parent[torch.from_numpy(keep).cuda()]
+    zeros = np.zeros(len(delta), np.uint8)
+    child = model.transition(parent_k, _dev(delta), _dev(zeros))
+    assert model.read_status() == 0
+    st, ref = oracle.az_transition(tensors, 128, parent_k.cpu().numpy(), delta, zeros, np.zeros(0, np.uint32),
+                                   np.zeros(len(delta) + 1, np.uint32))
+    np.testing.assert_array_equal(child.cpu().numpy(), ref)
+    # a refresh flag with no item lists is reported, not read
+    zeros[0] = 1
+    model.transition(parent_k, _dev(delta), _dev(zeros))
+    assert model.read_status() == 3
+
+
+def test_incremental_walk_matches_refresh():
+    """src/az.rs:3470-3495 on the device: 32 moves from the start position."""
+    w, tensors, model = _model(128)
+    rng = np.random.default_rng(21)
+    board, _ = az.board_from_fen(az.STARTPOS)
+    acc = model.refresh(*[_dev(a) for a in az.node_lists(board[None])])
+    for ply in range(32):
+        frm, to = az.random_move(board, rng, side=ply % 2)
+        ms = [az.move_items(board, frm, to, p) for p in (0, 1)]
+        r_items, r_off = az.pack_lists([m.items for m in ms])
+        acc = model.transition(acc, _dev(np.stack([m.delta for m in ms])),
+                               _dev(np.array([m.refresh for m in ms], np.uint8)), _dev(r_items), _dev(r_off))
+        board = az.apply_move(board, frm, to)
+        full = model.refresh(*[_dev(a) for a in az.node_lists(board[None])])
+        assert (acc - full).abs().max().item() < 2e-5
+    assert model.read_status() == 0
+
+
+@pytest.mark.parametrize("hidden", [128, 512, 32, 7])
+def test_value_matches_oracle(hidden):
+    w, tensors, model = _model(hidden)
+    boards = az.random_boards(1001, seed=200 + hidden)
+    acc = model.refresh(*[_dev(a) for a in az.node_lists(boards)])
+    rng = np.random.default_rng(hidden)
+    side = rng.integers(0, 2, len(boards)).astype(np.uint8)
+    rule = (rng.random((len(boards), 7)) * (rng.random((len(boards), 7)) < 0.4)).astype(np.float32)
+    threat = rng.standard_normal((len(boards), 3)).astype(np.float32)
+    wdl, q = model.value(acc, side=_dev(side), rule=_dev(rule), threat=_dev(threat))
+    a = acc.cpu().numpy().reshape(len(boards), 2, hidden)
+    stm = a[np.arange(len(boards)), side]
+    ref_wdl, ref_q = oracle.az_value(tensors, hidden, stm, rule, threat)
+    np.testing.assert_allclose(wdl.cpu().numpy(), ref_wdl, atol=1e-4, rtol=0)
+    np.testing.assert_allclose(q.cpu().numpy(), ref_q, atol=1e-4, rtol=0)
+    assert np.abs(ref_q).max() > 0.05  # the head is not trivially neutral here
+    # [n][H] layout without rule or threat
+    wdl2, q2 = model.value(torch.from_numpy(stm).cuda())
+    r2_wdl, r2_q = oracle.az_value(tensors, hidden, stm)
+    np.testing.assert_allclose(q2.cpu().numpy(), r2_q, atol=1e-4, rtol=0)
+    np.testing.assert_allclose(wdl2.sum(1).cpu().numpy(), 1.0, atol=1e-5)
+
+
+def test_random_init_value_is_neutral():
+    """src/az.rs:3354-3363: AzNnue::random(512, 20260409) evaluates startpos to 0."""
+    w = az.AzWeights.random(512, 20260409)
+    model = az.AzModel(w, device=0)
+    try:
+        board, side = az.board_from_fen(az.STARTPOS)
+        acc = model.refresh(*[_dev(a) for a in az.node_lists(board[None])])
+        wdl, q = model.value(acc, side=_dev(np.array([side], np.uint8)))
+        assert abs(q.item()) < 1e-6
+        np.testing.assert_allclose(wdl.cpu().numpy(), 1.0 / 3.0, atol=1e-6)
+    finally:
+        model.close()

@@ -78,6 +78,13 @@ SIGNATURES = {
     "cnnue_az_refresh": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_az_transition": (c_int, [c_void_p, P, P, P, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_az_value": (c_int, [c_void_p, P, P, P, P, c_i64, P, P, P]),
+    "cnnue_az_quantize": (c_int, [c_void_p]),
+    "cnnue_az_quant_table": (c_int, [c_void_p, c_int, C.POINTER(c_void_p), C.POINTER(c_i64),
+                                     C.POINTER(C.c_float)]),
+    "cnnue_az_quant_flags": (c_int, [c_void_p, C.POINTER(c_int), C.POINTER(c_int)]),
+    "cnnue_az_dense_moves": (c_int, [P, P]),
+    "cnnue_az_policy_refresh": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_az_policy_transition": (c_int, [c_void_p, P, P, P, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),
     "cnnue_synth_positions": (c_int, [c_u64, c_i64, c_u32, c_u32, c_u32, P, P, C.POINTER(c_u32)]),
     "cnnue_synth_q_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),

@@ -38,6 +38,19 @@ NO_ITEM = 0xFFFFFFFF
 FORMAT_VERSION = 20.0
 STARTPOS = "rnbakabnr/9/1c5c1/p1p1p1p1p/9/9/P1P1P1P1P/1C5C1/9/RNBAKABNR w"
 
+# Quantised tables (cnnue_az_quant_table).
+Q_POLICY_FEATURE, Q_POLICY_MOVE, Q_POLICY_SPARSE, Q_VALUE_THREAT, Q_MOVED_DELTA, Q_CAPTURE = range(6)
+DENSE_MOVES = 2086
+
+
+def dense_moves() -> Tuple[np.ndarray, np.ndarray]:
+    """(dense_to_sparse uint16[2086], sparse_to_dense uint16[8100])."""
+    d2s = np.zeros(DENSE_MOVES, np.uint16)
+    s2d = np.zeros(SQUARES * SQUARES, np.uint16)
+    check(lib().cnnue_az_dense_moves(d2s.ctypes.data, s2d.ctypes.data), "cnnue_az_dense_moves")
+    return d2s, s2d
+
+
 # Piece codes of a board: +(kind+1) Red, -(kind+1) Black.
 GENERAL, ADVISOR, ELEPHANT, HORSE, ROOK, CANNON, SOLDIER = range(7)
 
@@ -93,6 +106,30 @@ class AzWeights:
 
     def tensors(self) -> List[np.ndarray]:
         return [self.tensor(i) for i in range(N_TENSORS)]
+
+    def quantize(self) -> None:
+        """Rebuilds the quantised tables after tensor edits (the reference's
+        rebuild_* steps, src/az.rs:2201-2342)."""
+        check(lib().cnnue_az_quantize(self._h), "cnnue_az_quantize")
+
+    def quant_table(self, which: int) -> Tuple[np.ndarray, float]:
+        """(copy of quantised table `which` (Q_*), its scale)."""
+        data = C.c_void_p()
+        count = C.c_int64()
+        scale = C.c_float()
+        check(lib().cnnue_az_quant_table(self._h, which, C.byref(data), C.byref(count), C.byref(scale)),
+              "cnnue_az_quant_table")
+        ctype, dtype = (C.c_int8, np.int8) if which < 4 else (C.c_int32, np.int32)
+        arr = np.ctypeslib.as_array(C.cast(data, C.POINTER(ctype)), shape=(count.value,)).astype(dtype)
+        shapes = {Q_POLICY_FEATURE: (1546, 32), Q_POLICY_MOVE: (2086, 32), Q_VALUE_THREAT: (57702, 64),
+                  Q_MOVED_DELTA: (2086, 14), Q_CAPTURE: (2086, 14)}
+        return arr.reshape(shapes.get(which, (count.value,))), scale.value
+
+    def quant_flags(self) -> Tuple[bool, bool]:
+        """(value_threat_active, policy_tactical_active)."""
+        a, b = C.c_int(), C.c_int()
+        check(lib().cnnue_az_quant_flags(self._h, C.byref(a), C.byref(b)), "cnnue_az_quant_flags")
+        return bool(a.value), bool(b.value)
 
     @property
     def handle(self) -> C.c_void_p:
@@ -272,6 +309,29 @@ class AzModel:
                                         self._ptr(items) if n_items else None, n_items, self._ptr(offsets),
                                         n_lists, out.data_ptr(), self._ws.data_ptr(), self._ws.numel(),
                                         self._stream(stream)), "cnnue_az_transition")
+        return out
+
+    def policy_refresh(self, items, offsets, out=None, stream=None):
+        """int16 policy accumulators [n_lists][32] from CSR item lists."""
+        torch = self._torch
+        n_lists = offsets.numel() - 1
+        if out is None:
+            out = torch.empty((n_lists, 32), dtype=torch.int16, device=self.device)
+        check(lib().cnnue_az_policy_refresh(self._h, self._ptr(items) if items.numel() else None, items.numel(),
+                                            offsets.data_ptr(), n_lists, out.data_ptr(), self._ws.data_ptr(),
+                                            self._ws.numel(), self._stream(stream)), "cnnue_az_policy_refresh")
+        return out
+
+    def policy_transition(self, parent, delta, refresh, items=None, offsets=None, out=None, stream=None):
+        torch = self._torch
+        n_lists = refresh.numel()
+        if out is None:
+            out = torch.empty((n_lists, 32), dtype=torch.int16, device=self.device)
+        n_items = 0 if items is None else items.numel()
+        check(lib().cnnue_az_policy_transition(self._h, parent.data_ptr(), delta.data_ptr(), refresh.data_ptr(),
+                                               self._ptr(items) if n_items else None, n_items, self._ptr(offsets),
+                                               n_lists, out.data_ptr(), self._ws.data_ptr(), self._ws.numel(),
+                                               self._stream(stream)), "cnnue_az_policy_transition")
         return out
 
     def value(self, acc, side=None, rule=None, threat=None, stream=None):

@@ -32,6 +32,7 @@ struct cnnue_az_model {
   float* head_t = nullptr;  // value_head_hidden transposed, [H][96]
   float* head_b = nullptr;  // [96]
   float* head_o = nullptr;  // [3][96]
+  int8_t* policy_q = nullptr;  // quantised policy feature rows [1546][32]
 };
 
 namespace cnnue {
@@ -385,6 +386,125 @@ __global__ void transpose_head_kernel(const float* __restrict__ w, int H, float*
   }
 }
 
+// ---- int16 policy accumulator ----------------------------------------------
+// 4 lists per warp, 8 lanes per list; lane s of a list owns ranks 4s..4s+3 as
+// two words of int16 pairs.  The int8 table is widened into shared memory as
+// [1546][16] words, so one row add is one 8-byte shared load and two
+// saturating pair adds (__vaddss2 / __vsubss2).
+constexpr int kPolicyWarps = 8;
+constexpr size_t kPolicySmem = (size_t)CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK * 2;
+
+struct PolicyArgs {
+  const int8_t* q;
+  const uint32_t* items;
+  uint32_t n_items;
+  const uint32_t* offsets;
+  int64_t n_lists;
+  const int16_t* parent;
+  const uint32_t* delta;
+  const uint8_t* refresh;
+  int16_t* out;
+  WorkspaceHeader* hdr;
+};
+
+__device__ __forceinline__ uint32_t widen2(uint32_t b) {  // int8 bytes 0,1 -> int16 pair
+  return (uint32_t)(uint16_t)(int16_t)(int8_t)(b & 0xffu) | ((uint32_t)(uint16_t)(int16_t)(int8_t)((b >> 8) & 0xffu) << 16);
+}
+
+template <int kSign>
+__device__ __forceinline__ void policy_row(const uint2* __restrict__ tab, uint32_t row, int sub, uint32_t& a0, uint32_t& a1) {
+  const uint2 w = tab[row * 8 + sub];
+  if (kSign > 0) {
+    a0 = __vaddss2(a0, w.x);
+    a1 = __vaddss2(a1, w.y);
+  } else {
+    a0 = __vsubss2(a0, w.x);
+    a1 = __vsubss2(a1, w.y);
+  }
+}
+
+template <int kSign>
+__device__ __forceinline__ void policy_item(const uint2* __restrict__ tab, const uint32_t r[6], int sub, uint32_t& a0,
+                                            uint32_t& a1) {
+#pragma unroll
+  for (int k = 0; k < 6; ++k) policy_row<kSign>(tab, r[k], sub, a0, a1);
+}
+
+template <bool kTransition>
+__global__ void __launch_bounds__(kPolicyWarps * 32) az_policy_kernel(PolicyArgs p) {
+  extern __shared__ uint2 ptab[];  // [1546][8] uint2 = [1546][32] int16
+  const uint32_t* q32 = reinterpret_cast<const uint32_t*>(p.q);
+  uint32_t* t32 = reinterpret_cast<uint32_t*>(ptab);
+  for (int i = threadIdx.x; i < CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK / 4; i += blockDim.x) {
+    const uint32_t v = __ldg(q32 + i);
+    t32[2 * i] = widen2(v);
+    t32[2 * i + 1] = widen2(v >> 16);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, group = lane >> 3, sub = lane & 7;
+  const unsigned gmask = 0xffu << (8 * group);
+  uint32_t status = 0;
+  const int64_t stride = (int64_t)gridDim.x * kPolicyWarps * 4;
+  for (int64_t base = ((int64_t)blockIdx.x * kPolicyWarps + (threadIdx.x >> 5)) * 4; base < p.n_lists; base += stride) {
+    const int64_t l = base + group;
+    if (l < p.n_lists) {
+      uint32_t a0 = 0, a1 = 0;
+      const bool do_refresh = !kTransition || (p.refresh[l] & 1u);
+      if (do_refresh) {
+        policy_row<1>(ptab, CNNUE_AZ_POLICY_ROWS - 1, sub, a0, a1);  // bias row
+        uint32_t beg = 0, end = 0;
+        if (p.offsets == nullptr) {
+          status |= CNNUE_STATUS_BAD_OFFSETS;
+        } else {
+          beg = p.offsets[l];
+          end = p.offsets[l + 1];
+          if (!(beg <= end && end <= p.n_items)) {
+            status |= CNNUE_STATUS_BAD_OFFSETS;
+            beg = end = 0;
+          }
+        }
+        for (uint32_t b = beg; b < end; b += 8) {
+          const uint32_t mine = b + sub < end ? p.items[b + sub] : 0u;
+          const uint32_t cnt = min(8u, end - b);
+          for (uint32_t k = 0; k < cnt; ++k) {
+            const uint32_t it = __shfl_sync(gmask, mine, (int)k, 8);
+            uint32_t r[6];
+            if (item_rows(it, r)) policy_item<1>(ptab, r, sub, a0, a1);
+            else status |= CNNUE_STATUS_BAD_INDEX;
+          }
+        }
+      } else {
+        const uint2 par = reinterpret_cast<const uint2*>(p.parent + l * CNNUE_AZ_POLICY_RANK)[sub];
+        a0 = par.x;
+        a1 = par.y;
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          const uint32_t it = p.delta[3 * l + d];
+          if (it == CNNUE_AZ_NO_ITEM) continue;
+          uint32_t r[6];
+          if (!item_rows(it, r)) {
+            status |= CNNUE_STATUS_BAD_INDEX;
+            continue;
+          }
+          if (d < 2) policy_item<-1>(ptab, r, sub, a0, a1);
+          else policy_item<1>(ptab, r, sub, a0, a1);
+        }
+      }
+      reinterpret_cast<uint2*>(p.out + l * CNNUE_AZ_POLICY_RANK)[sub] = make_uint2(a0, a1);
+    }
+  }
+  status = __reduce_or_sync(kFull, status);
+  if (lane == 0 && status) atomicOr(&p.hdr->status, status);
+}
+
+template <bool kTransition>
+int launch_policy(const PolicyArgs& a, cudaStream_t s) {
+  const int64_t want = (a.n_lists + 4 * kPolicyWarps - 1) / (4 * kPolicyWarps);
+  const unsigned blocks = (unsigned)(want < 148 * 2 ? want : 148 * 2);
+  az_policy_kernel<kTransition><<<blocks, kPolicyWarps * 32, kPolicySmem, s>>>(a);
+  return check_launch_error(kTransition ? "az_policy_kernel<transition>" : "az_policy_kernel<refresh>");
+}
+
 // The float4 column path needs 16-byte aligned accumulator rows.
 int check_rows_aligned(int64_t H, const void* a, const char* what) {
   if (H % 4 == 0 && ((uintptr_t)a & 15u) != 0)
@@ -416,11 +536,14 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
                rule = align_up(sizeof(float) * 7 * H, 256), head = align_up(sizeof(float) * kHead * H, 256),
                small = align_up(sizeof(float) * kHead, 256), out3 = align_up(sizeof(float) * 3 * kHead, 256);
   const size_t staging = align_up(sizeof(float) * kHead * H, 256);
+  const size_t policy = align_up((size_t)CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK, 256);
+  if (w->q8[0].size() != (size_t)CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK)
+    return set_error(CNNUE_ERR_INVALID_ARG, "weights have no quantised policy table (run cnnue_az_quantize)");
   auto* m = new (std::nothrow) cnnue_az_model;
   if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
   m->device = device;
   m->hidden = H;
-  cudaError_t e = cudaMalloc(&m->blob, trunk + vecH + rule + head + small + out3 + staging);
+  cudaError_t e = cudaMalloc(&m->blob, trunk + vecH + rule + head + small + out3 + policy + staging);
   if (e != cudaSuccess) {
     delete m;
     return cuda_error(e, "cudaMalloc(az model)");
@@ -432,7 +555,8 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
   m->head_t = (float*)(p += rule);
   m->head_b = (float*)(p += head);
   m->head_o = (float*)(p += small);
-  float* stage = (float*)(p += out3);
+  m->policy_q = (int8_t*)(p += out3);
+  float* stage = (float*)(p += policy);
   using namespace cnnue::az;
   const int tables[5] = {kInputHidden, kInputPiece, kInputRank, kInputFile, kInputKingPiece};
   const int rows[5] = {1260, 14, 10, 9, 252};
@@ -457,6 +581,10 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
   copy(m->head_b, w->t[kValueHeadBias], kHead, "value_head_bias");
   copy(m->head_o, w->t[kValueHeadOutput], 3 * kHead, "value_head_output");
   if (!st) {
+    const cudaError_t ce = cudaMemcpy(m->policy_q, w->q8[0].data(), w->q8[0].size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) st = cuda_error(ce, "policy table");
+  }
+  if (!st) {
     const int64_t n = (int64_t)kHead * H;
     transpose_head_kernel<<<(unsigned)((n + 255) / 256), 256>>>(stage, (int)H, m->head_t);
     st = check_launch_error("transpose_head_kernel");
@@ -466,6 +594,11 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
     const cudaError_t ce =
         cudaFuncSetAttribute(az_value_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kMaxSmem);
     if (ce != cudaSuccess) st = cuda_error(ce, "cudaFuncSetAttribute(az_value_kernel)");
+  }
+  for (int k = 0; k < 2 && !st; ++k) {
+    const cudaError_t ce = cudaFuncSetAttribute(k ? az_policy_kernel<true> : az_policy_kernel<false>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPolicySmem);
+    if (ce != cudaSuccess) st = cuda_error(ce, "cudaFuncSetAttribute(az_policy_kernel)");
   }
   if (!st) {
     const cudaError_t ce = cudaDeviceSynchronize();
@@ -574,6 +707,60 @@ int cnnue_az_value(const cnnue_az_model* m, const float* d_acc, const uint8_t* d
   const unsigned blocks = (unsigned)(want < 148 * per_sm ? want : 148 * per_sm);
   az_value_kernel<<<blocks, warps * 32, smem, (cudaStream_t)stream>>>(a);
   return check_launch_error("az_value_kernel");
+}
+
+int cnnue_az_policy_refresh(const cnnue_az_model* m, const uint32_t* d_items, uint32_t n_items,
+                            const uint32_t* d_offsets, int64_t n_lists, int16_t* d_acc, void* ws, size_t ws_bytes,
+                            void* stream) {
+  if (!m || !ws || n_lists < 0 || (n_lists > 0 && (!d_offsets || !d_acc || (n_items > 0 && !d_items))))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, offsets, items or acc, or n_lists < 0");
+  if (ws_bytes < sizeof(WorkspaceHeader))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu", ws_bytes, sizeof(WorkspaceHeader));
+  if ((uintptr_t)d_acc & 7u) return set_error(CNNUE_ERR_INVALID_ARG, "d_acc must be 8-byte aligned");
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n_lists == 0) return CNNUE_OK;
+  PolicyArgs a{};
+  a.q = m->policy_q;
+  a.items = d_items;
+  a.n_items = n_items;
+  a.offsets = d_offsets;
+  a.n_lists = n_lists;
+  a.out = d_acc;
+  a.hdr = (WorkspaceHeader*)ws;
+  return launch_policy<false>(a, s);
+}
+
+int cnnue_az_policy_transition(const cnnue_az_model* m, const int16_t* d_parent, const uint32_t* d_delta,
+                               const uint8_t* d_refresh, const uint32_t* d_items, uint32_t n_items,
+                               const uint32_t* d_offsets, int64_t n_lists, int16_t* d_child, void* ws,
+                               size_t ws_bytes, void* stream) {
+  if (!m || !ws || n_lists < 0 || (n_lists > 0 && (!d_parent || !d_delta || !d_refresh || !d_child)) ||
+      (n_items > 0 && !d_items))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, parent, delta, refresh, child or items");
+  if (ws_bytes < sizeof(WorkspaceHeader))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu", ws_bytes, sizeof(WorkspaceHeader));
+  if (((uintptr_t)d_parent | (uintptr_t)d_child) & 7u)
+    return set_error(CNNUE_ERR_INVALID_ARG, "d_parent and d_child must be 8-byte aligned");
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n_lists == 0) return CNNUE_OK;
+  PolicyArgs a{};
+  a.q = m->policy_q;
+  a.items = d_items;
+  a.n_items = n_items;
+  a.offsets = d_offsets;
+  a.n_lists = n_lists;
+  a.parent = d_parent;
+  a.delta = d_delta;
+  a.refresh = d_refresh;
+  a.out = d_child;
+  a.hdr = (WorkspaceHeader*)ws;
+  return launch_policy<true>(a, s);
 }
 
 }  // extern "C"

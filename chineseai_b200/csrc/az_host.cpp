@@ -11,6 +11,7 @@
 // JSON header {"name": {"dtype", "shape", "data_offsets"}} padded with spaces
 // to a multiple of 8 bytes, then the raw little-endian tensor bytes.  Files are
 // written with the tensors sorted by name, each tensor's bytes in that order.
+#include <algorithm>
 #include <cmath>
 #include <cstdio>
 #include <cstdlib>
@@ -379,9 +380,198 @@ int load_f32(const std::map<std::string, TensorRef>& tensors, const char* data, 
   return CNNUE_OK;
 }
 
+// ---- quantised tables (src/az.rs:2201-2342) --------------------------------
+constexpr int kRank = CNNUE_AZ_POLICY_RANK;
+
+// dot_product (src/az.rs:2730-2766) as it runs on x86-64 with AVX2 and FMA:
+// n >= 64 uses dot_product_avx2_fma (:2880-2922), four 8-lane fused
+// accumulators over 32-float chunks, combined (a0 + a1) + (a2 + a3) per lane,
+// the 8 lanes summed in order, then the tail; shorter rows use four scalar
+// accumulators, (s0 + s1) + (s2 + s3), then the tail.
+float reference_dot(const float* l, const float* r, int64_t n) {
+  if (n >= 64) {
+    float acc[4][8] = {};
+    const int64_t chunks = n / 32;
+    for (int64_t c = 0; c < chunks; ++c)
+      for (int a = 0; a < 4; ++a)
+        for (int k = 0; k < 8; ++k) {
+          const int64_t i = c * 32 + a * 8 + k;
+          acc[a][k] = std::fma(l[i], r[i], acc[a][k]);
+        }
+    float sum = 0.0f;
+    for (int k = 0; k < 8; ++k) sum += (acc[0][k] + acc[1][k]) + (acc[2][k] + acc[3][k]);
+    for (int64_t i = chunks * 32; i < n; ++i) sum += l[i] * r[i];
+    return sum;
+  }
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t chunks = n / 4;
+  for (int64_t c = 0; c < chunks; ++c)
+    for (int k = 0; k < 4; ++k) s[k] += l[4 * c + k] * r[4 * c + k];
+  float sum = (s[0] + s[1]) + (s[2] + s[3]);
+  for (int64_t i = chunks * 4; i < n; ++i) sum += l[i] * r[i];
+  return sum;
+}
+
+// Symmetric per-tensor int8 quantisation; returns the scale.
+float quantize_i8(const float* x, size_t n, std::vector<int8_t>& q) {
+  float mx = 0.f;
+  for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, std::fabs(x[i]));
+  const float scale = std::fmax(mx / 127.0f, 1.0e-12f);
+  q.resize(n);
+  for (size_t i = 0; i < n; ++i) {
+    const float v = std::round(x[i] / scale);
+    q[i] = std::isnan(v) ? (int8_t)0 : (int8_t)std::fmin(std::fmax(v, -127.f), 127.f);
+  }
+  return scale;
+}
+
+bool advisor_point(int r, int f) {
+  return ((r == 0 || r == 2 || r == 7 || r == 9) && (f == 3 || f == 5)) || ((r == 1 || r == 8) && f == 4);
+}
+bool elephant_point(int r, int f) {
+  return ((r == 0 || r == 9 || r == 4 || r == 5) && (f == 2 || f == 6)) ||
+         ((r == 2 || r == 7) && (f == 0 || f == 4 || f == 8));
+}
+// is_valid_policy_move (src/az.rs:3206-3237).
+bool policy_move(int from, int to) {
+  const int ff = from % 9, fr = from / 9, tf = to % 9, tr = to / 9;
+  const int df = std::abs(tf - ff), dr = std::abs(tr - fr);
+  if (df == 0 || dr == 0) return true;
+  if (df + dr == 3 && df != 0 && dr != 0) return true;  // horse step
+  if (df == 1 && dr == 1) return advisor_point(fr, ff) && advisor_point(tr, tf);
+  if (df == 2 && dr == 2) return elephant_point(fr, ff) && elephant_point(tr, tf);
+  return false;
+}
+
+const std::vector<uint16_t>& dense_moves() {
+  static const std::vector<uint16_t> moves = [] {
+    std::vector<uint16_t> m;
+    for (int from = 0; from < kSq; ++from)
+      for (int to = 0; to < kSq; ++to)
+        if (from != to && policy_move(from, to)) m.push_back((uint16_t)(from * kSq + to));
+    return m;
+  }();
+  return moves;
+}
+
+int quantize(cnnue_az_weights& w) {
+  const int64_t h = w.hidden;
+  const auto& moves = dense_moves();
+  if ((int)moves.size() != kDenseMoves) return set_error(CNNUE_ERR_INTERNAL, "dense move space %zu", moves.size());
+  // 1546 trunk rows projected on policy_accumulator_hidden.
+  std::vector<float> projected;
+  projected.reserve((size_t)CNNUE_AZ_POLICY_ROWS * kRank);
+  const float* proj = w.t[17].data();
+  for (int t : {0, 1, 2, 3, 4, 6}) {
+    const std::vector<float>& table = w.t[t];
+    for (size_t row = 0; row * h < table.size(); ++row)
+      for (int j = 0; j < kRank; ++j) projected.push_back(reference_dot(table.data() + row * h, proj + j * h, h));
+  }
+  w.scale[0] = quantize_i8(projected.data(), projected.size(), w.q8[0]);
+  w.scale[1] = quantize_i8(w.t[18].data(), w.t[18].size(), w.q8[1]);
+  // policy_sparse_factor folded into the main part of policy_sparse_table,
+  // factor order of policy_sparse_factor_indices (src/az.rs:789-813).
+  std::vector<float> folded(w.t[19]);
+  const int64_t move_piece = (int64_t)kDenseMoves * 14, move_king = (int64_t)kDenseMoves * 81, piece_king = 14 * 81;
+  const int64_t distance_off = move_piece + move_king + piece_king, approach_off = distance_off + 14 * 6;
+  const float* factor = w.t[20].data();
+  for (int m = 0; m < kDenseMoves; ++m) {
+    const int from = moves[m] / kSq, to = moves[m] % kSq;
+    for (int piece = 0; piece < 14; ++piece)
+      for (int us = 0; us < 9; ++us)
+        for (int them = 0; them < 9; ++them) {
+          // policy_king_distance_buckets (src/az.rs:841-859): Manhattan
+          // distances from the opponent general's palace square.
+          const int king = kSq - 1 - ((7 + them / 3) * 9 + 3 + them % 3);
+          const int before = std::abs(from / 9 - king / 9) + std::abs(from % 9 - king % 9);
+          const int after = std::abs(to / 9 - king / 9) + std::abs(to % 9 - king % 9);
+          const int approach = std::min(std::max(before - after, -2), 2) + 2;
+          const int distance = std::min(after, 5);
+          const int pair = us * 9 + them;
+          float& main = folded[(size_t)((((int64_t)m * 14 + piece) * 9 + us) * 9 + them)];
+          main += factor[(int64_t)m * 14 + piece];
+          main += factor[move_piece + (int64_t)m * 81 + pair];
+          main += factor[move_piece + move_king + piece * 81 + pair];
+          main += factor[distance_off + piece * 6 + distance];
+          main += factor[approach_off + piece * 5 + approach];
+        }
+  }
+  w.scale[2] = quantize_i8(folded.data(), folded.size(), w.q8[2]);
+  // moved-piece delta and capture caches in the int8 feature and move spaces.
+  w.q32[0].assign((size_t)kDenseMoves * 14, 0);
+  w.q32[1].assign((size_t)kDenseMoves * 14, 0);
+  const int8_t* fq = w.q8[0].data();
+  const int8_t* mq = w.q8[1].data();
+  for (int m = 0; m < kDenseMoves; ++m) {
+    const int from = moves[m] / kSq, to = moves[m] % kSq;
+    for (int piece = 0; piece < 14; ++piece) {
+      int32_t delta = 0, cap = 0;
+      for (int j = 0; j < kRank; ++j) {
+        const int32_t wt = mq[m * kRank + j];
+        const int32_t tq = fq[(piece * kSq + to) * kRank + j], fr = fq[(piece * kSq + from) * kRank + j];
+        delta += (tq - fr) * wt;
+        cap += tq * wt;
+      }
+      w.q32[0][(size_t)m * 14 + piece] = delta;
+      w.q32[1][(size_t)m * 14 + piece] = cap;
+    }
+  }
+  auto any = [](const std::vector<float>& v) {
+    for (float x : v)
+      if (x != 0.f) return true;
+    return false;
+  };
+  w.value_threat_active = any(w.t[11]) || any(w.t[12]);
+  w.policy_tactical_active = any(w.t[21]);
+  w.scale[3] = quantize_i8(w.t[10].data(), w.t[10].size(), w.q8[3]);
+  return CNNUE_OK;
+}
+
 }  // namespace
 
 extern "C" {
+
+int cnnue_az_quantize(cnnue_az_weights* w) {
+  if (!w) return set_error(CNNUE_ERR_INVALID_ARG, "null weights");
+  try {
+    return quantize(*w);
+  } catch (const std::bad_alloc&) {
+    return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
+  }
+}
+
+int cnnue_az_quant_table(const cnnue_az_weights* w, int which, const void** data, int64_t* count, float* scale) {
+  if (!w || !data) return set_error(CNNUE_ERR_INVALID_ARG, "null weights or data");
+  if (which < 0 || which > CNNUE_AZ_Q_CAPTURE) return set_error(CNNUE_ERR_INVALID_ARG, "quantised table %d", which);
+  if (which < 4) {
+    *data = w->q8[which].data();
+    if (count) *count = (int64_t)w->q8[which].size();
+    if (scale) *scale = w->scale[which];
+  } else {
+    *data = w->q32[which - 4].data();
+    if (count) *count = (int64_t)w->q32[which - 4].size();
+    if (scale) *scale = 1.f;
+  }
+  return CNNUE_OK;
+}
+
+int cnnue_az_quant_flags(const cnnue_az_weights* w, int* value_threat_active, int* policy_tactical_active) {
+  if (!w) return set_error(CNNUE_ERR_INVALID_ARG, "null weights");
+  if (value_threat_active) *value_threat_active = w->value_threat_active;
+  if (policy_tactical_active) *policy_tactical_active = w->policy_tactical_active;
+  return CNNUE_OK;
+}
+
+int cnnue_az_dense_moves(uint16_t* dense_to_sparse, uint16_t* sparse_to_dense) {
+  const auto& moves = dense_moves();
+  if (dense_to_sparse) std::copy(moves.begin(), moves.end(), dense_to_sparse);
+  if (sparse_to_dense) {
+    std::fill(sparse_to_dense, sparse_to_dense + kSq * kSq, (uint16_t)0xffff);
+    for (size_t i = 0; i < moves.size(); ++i) sparse_to_dense[moves[i]] = (uint16_t)i;
+  }
+  return CNNUE_OK;
+}
+
 
 int cnnue_az_board_from_fen(const char* fen, int8_t* board, int* side) {
   if (!fen || !board || !side) return set_error(CNNUE_ERR_INVALID_ARG, "null fen, board or side");
@@ -504,6 +694,7 @@ int cnnue_az_weights_random(int64_t hidden, uint64_t seed, cnnue_az_weights** ou
   for (float& x : w->t[10]) x = rng.weight(0.02f);
   for (float& x : w->t[15]) x = rng.weight(head_scale);
   for (float& x : w->t[17]) x = rng.weight(head_scale);
+  if (int st = cnnue_az_quantize(w.get())) return st;
   *out = w.release();
   return CNNUE_OK;
 }
@@ -535,6 +726,7 @@ int cnnue_az_weights_load(const char* path, cnnue_az_weights** out) {
       return set_error(CNNUE_ERR_FORMAT, "az model tensor `%s` length mismatch: got %lld, expected %lld",
                        kSpecs[i].name, (long long)w->t[i].size(), (long long)expected);
   }
+  if ((st = cnnue_az_quantize(w.get()))) return st;
   *out = w.release();
   return CNNUE_OK;
 }

@@ -352,6 +352,40 @@ int64_t cnnue_az_weights_hidden(const cnnue_az_weights* weights);
 /* Host view of tensor `index` (writable; a model created later sees edits). */
 int cnnue_az_weights_tensor(cnnue_az_weights* weights, int index, float** data, int64_t* count);
 
+/* Quantised tables (rebuild_policy_accumulator_quantization,
+ * rebuild_value_threat_quantization, rebuild_policy_tactical,
+ * src/az.rs:2201-2342).  cnnue_az_weights_random and _load build them, as
+ * AzNnue::random and ::load do; after editing tensors call
+ * cnnue_az_quantize again.  Symmetric per-tensor int8: scale = max(max|x| /
+ * 127, 1e-12), q = clamp(round(x / scale), -127, 127), round half away from
+ * zero.  The policy feature rows are the 1546 rows (1260 input, 14 piece,
+ * 10 rank, 9 file, 252 king-piece, 1 hidden_bias) projected on the 32 rows of
+ * policy_accumulator_hidden with the reference's x86-64 AVX2/FMA dot product
+ * summation order (dot_product, src/az.rs:2730-2766, :2880-2922), so the
+ * tables are bit-identical to the reference's on that platform. */
+#define CNNUE_AZ_Q_POLICY_FEATURE 0  /* int8  [1546][32]   */
+#define CNNUE_AZ_Q_POLICY_MOVE 1     /* int8  [2086][32]   */
+#define CNNUE_AZ_Q_POLICY_SPARSE 2   /* int8  [2396815], sparse factors folded in */
+#define CNNUE_AZ_Q_VALUE_THREAT 3    /* int8  [57702][64]  */
+#define CNNUE_AZ_Q_MOVED_DELTA 4     /* int32 [2086][14]   */
+#define CNNUE_AZ_Q_CAPTURE 5         /* int32 [2086][14]   */
+#define CNNUE_AZ_DENSE_MOVES 2086
+#define CNNUE_AZ_POLICY_RANK 32
+#define CNNUE_AZ_POLICY_ROWS 1546
+int cnnue_az_quantize(cnnue_az_weights* weights);
+/* Host view of quantised table `which`; *scale gets its scale (1 for the
+ * int32 caches).  Element size: 1 byte for the int8 tables, 4 for int32. */
+int cnnue_az_quant_table(const cnnue_az_weights* weights, int which, const void** data, int64_t* count,
+                         float* scale);
+/* value_threat_active, policy_tactical_active (src/az.rs:2202-2206, :2223-2225). */
+int cnnue_az_quant_flags(const cnnue_az_weights* weights, int* value_threat_active,
+                         int* policy_tactical_active);
+/* The dense policy move space (move_map, src/az.rs:3261-3285): the 2086
+ * from * 90 + to pairs of is_valid_policy_move (:3206-3237) in from-major
+ * order; sparse_to_dense[8100] gets the inverse, 0xffff for invalid pairs.
+ * Either pointer may be NULL. */
+int cnnue_az_dense_moves(uint16_t* dense_to_sparse, uint16_t* sparse_to_dense);
+
 /* Device copy of the trunk (the 5 input tables concatenated as [1545][H],
  * hidden_bias, rule_context_hidden) and the value head.  Hidden sizes 1..127
  * and multiples of 4 up to 512. */
@@ -398,6 +432,24 @@ int cnnue_az_transition(const cnnue_az_model* model, const float* d_parent, cons
 int cnnue_az_value(const cnnue_az_model* model, const float* d_acc, const uint8_t* d_side,
                    const float* d_rule, const float* d_threat, int64_t n, float* d_wdl, float* d_q,
                    void* stream);
+
+/* int16 policy accumulators [n_lists][32] (quantized_policy_accumulator,
+ * src/az.rs:2344-2365): the bias row, then for every item its 6 rows of the
+ * CNNUE_AZ_Q_POLICY_FEATURE table (input, piece, rank, file, king(us),
+ * king(them)), each row add saturating to int16 in that order
+ * (add_quantized_policy_row, :2439-2451): bit-identical to the reference.
+ * Same lists, status and skipping rules as cnnue_az_refresh. */
+int cnnue_az_policy_refresh(const cnnue_az_model* model, const uint32_t* d_items, uint32_t n_items,
+                            const uint32_t* d_offsets, int64_t n_lists, int16_t* d_acc,
+                            void* d_workspace, size_t workspace_bytes, void* stream);
+/* apply_quantized_policy_transition (src/az.rs:2367-2409): parent minus the
+ * rows of delta[3l] and delta[3l+1], plus those of delta[3l+2], saturating per
+ * row, or the refresh of list l where d_refresh[l] & 1.  child may be parent. */
+int cnnue_az_policy_transition(const cnnue_az_model* model, const int16_t* d_parent,
+                               const uint32_t* d_delta, const uint8_t* d_refresh,
+                               const uint32_t* d_items, uint32_t n_items, const uint32_t* d_offsets,
+                               int64_t n_lists, int16_t* d_child, void* d_workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is

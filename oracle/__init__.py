@@ -264,3 +264,69 @@ def az_value(tensors, hidden: int, hidden_rows: np.ndarray, rule=None, threat=No
                           _p(np.ascontiguousarray(hidden_rows, np.float32)), None if r is None else _p(r),
                           None if t is None else _p(t), n, _p(wdl), _p(q))
     return wdl[:n], q[:n]
+
+
+def _azq_setup(h):
+    if getattr(h, "_azq_ready", False):
+        return
+    P, i64, i32 = C.c_void_p, C.c_int64, C.c_int
+    h.oracle_az_dense_moves.argtypes = [P]
+    h.oracle_az_dense_moves.restype = i32
+    h.oracle_az_quantize.argtypes = [i32, P] + [P] * 8
+    h.oracle_az_quantize.restype = i32
+    h.oracle_az_policy_refresh.argtypes = [P, P, P, i64, P]
+    h.oracle_az_policy_refresh.restype = i32
+    h.oracle_az_policy_transition.argtypes = [P, P, P, P, P, P, i64, P]
+    h.oracle_az_policy_transition.restype = i32
+    h._azq_ready = True
+
+
+def _azq():
+    h = _az()
+    _azq_setup(h)
+    return h
+
+
+def az_dense_moves() -> np.ndarray:
+    out = np.zeros(8100, np.uint16)
+    n = _azq().oracle_az_dense_moves(_p(out))
+    return out[:n].copy()
+
+
+def az_quantize(tensors, hidden: int) -> dict:
+    """rebuild_policy_accumulator_quantization + rebuild_value_threat_quantization restated."""
+    flat = [np.ascontiguousarray(np.asarray(t, np.float32).reshape(-1)) for t in tensors]
+    ptrs = (C.c_void_p * 22)(*[a.ctypes.data for a in flat])
+    out = {"policy_feature": np.zeros((1546, 32), np.int8), "policy_move": np.zeros((2086, 32), np.int8),
+           "policy_sparse": np.zeros(2396815, np.int8), "moved_delta": np.zeros((2086, 14), np.int32),
+           "capture": np.zeros((2086, 14), np.int32), "value_threat": np.zeros((57702, 64), np.int8)}
+    scales = np.zeros(4, np.float32)
+    flags = np.zeros(2, np.int32)
+    st = _azq().oracle_az_quantize(hidden, ptrs, *[_p(out[k]) for k in ("policy_feature", "policy_move",
+                                                                        "policy_sparse", "moved_delta", "capture",
+                                                                        "value_threat")], _p(scales), _p(flags))
+    assert st == 0
+    out["scales"] = scales
+    out["flags"] = flags
+    return out
+
+
+def az_policy_refresh(feature_q: np.ndarray, items: np.ndarray, offsets: np.ndarray):
+    n_lists = len(offsets) - 1
+    acc = np.zeros((max(n_lists, 1), 32), np.int16)
+    it = np.ascontiguousarray(items, np.uint32) if len(items) else np.zeros(1, np.uint32)
+    st = _azq().oracle_az_policy_refresh(_p(np.ascontiguousarray(feature_q, np.int8)), _p(it),
+                                         _p(np.ascontiguousarray(offsets, np.uint32)), n_lists, _p(acc))
+    return st, acc[:n_lists]
+
+
+def az_policy_transition(feature_q, parent, delta, refresh, items, offsets):
+    n_lists = len(refresh)
+    child = np.zeros((max(n_lists, 1), 32), np.int16)
+    it = np.ascontiguousarray(items, np.uint32) if len(items) else np.zeros(1, np.uint32)
+    st = _azq().oracle_az_policy_transition(_p(np.ascontiguousarray(feature_q, np.int8)),
+                                            _p(np.ascontiguousarray(parent, np.int16)),
+                                            _p(np.ascontiguousarray(delta, np.uint32)),
+                                            _p(np.ascontiguousarray(refresh, np.uint8)), _p(it),
+                                            _p(np.ascontiguousarray(offsets, np.uint32)), n_lists, _p(child))
+    return st, child[:n_lists]

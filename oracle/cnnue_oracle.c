@@ -766,3 +766,220 @@ void oracle_az_value(const float* rule_rows, const float* vh, const float* vb, c
     q[p] = wdl[p * 3] - wdl[p * 3 + 2];
   }
 }
+
+/* ---- AZ-NNUE quantised policy accumulator (reference-native) ------------ */
+/* dot_product (src/az.rs:2730-2766) as it runs on x86-64 with AVX2 and FMA:
+ * length >= 64 -> 4 x 8-lane FMA accumulators over 32-float chunks, lanes
+ * combined (a0+a1)+(a2+a3), summed left to right, then the tail with separate
+ * multiply and add (dot_product_avx2_fma, :2880-2922); shorter -> 4 scalar
+ * accumulators (sum0+sum1)+(sum2+sum3) then the tail. */
+static float az_dot(const float* l, const float* r, int n) {
+  if (n >= 64) {
+    float acc[4][8];
+    memset(acc, 0, sizeof(acc));
+    const int chunks = n / 32;
+    for (int c = 0; c < chunks; ++c)
+      for (int a = 0; a < 4; ++a)
+        for (int k = 0; k < 8; ++k) acc[a][k] = fmaf(l[c * 32 + a * 8 + k], r[c * 32 + a * 8 + k], acc[a][k]);
+    float sum = 0.0f;
+    for (int k = 0; k < 8; ++k) {
+      const float v = (acc[0][k] + acc[1][k]) + (acc[2][k] + acc[3][k]);
+      sum += v;
+    }
+    for (int i = chunks * 32; i < n; ++i) {
+      const float p = l[i] * r[i];
+      sum += p;
+    }
+    return sum;
+  }
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  const int chunks = n / 4;
+  for (int c = 0; c < chunks; ++c) {
+    float p0 = l[4 * c] * r[4 * c], p1 = l[4 * c + 1] * r[4 * c + 1];
+    float p2 = l[4 * c + 2] * r[4 * c + 2], p3 = l[4 * c + 3] * r[4 * c + 3];
+    s0 += p0;
+    s1 += p1;
+    s2 += p2;
+    s3 += p3;
+  }
+  float sum = (s0 + s1) + (s2 + s3);
+  for (int i = chunks * 4; i < n; ++i) {
+    const float p = l[i] * r[i];
+    sum += p;
+  }
+  return sum;
+}
+
+/* Symmetric int8 quantisation of x[n] (src/az.rs:2250-2262): scale =
+ * max(max|x| / 127, 1e-12), q = clamp(round(x / scale), -127, 127) with
+ * round half away from zero and NaN -> 0. */
+static float az_quantize(const float* x, int64_t n, int8_t* q) {
+  float mx = 0.f;
+  for (int64_t i = 0; i < n; ++i) {
+    const float a = fabsf(x[i]);
+    if (a > mx) mx = a; /* f32::max ignores NaN */
+  }
+  float scale = mx / 127.0f;
+  if (!(scale >= 1.0e-12f)) scale = 1.0e-12f;
+  for (int64_t i = 0; i < n; ++i) {
+    float v = roundf(x[i] / scale);
+    if (v != v) v = 0.f;
+    v = v < -127.f ? -127.f : (v > 127.f ? 127.f : v);
+    q[i] = (int8_t)v;
+  }
+  return scale;
+}
+
+/* is_valid_policy_move (src/az.rs:3178-3238) */
+static int az_advisor_pos(int r, int f) {
+  return (r == 0 && (f == 3 || f == 5)) || (r == 1 && f == 4) || (r == 2 && (f == 3 || f == 5)) ||
+         (r == 7 && (f == 3 || f == 5)) || (r == 8 && f == 4) || (r == 9 && (f == 3 || f == 5));
+}
+static int az_elephant_pos(int r, int f) {
+  return ((r == 0 || r == 9) && (f == 2 || f == 6)) || ((r == 2 || r == 7) && (f == 0 || f == 4 || f == 8)) ||
+         ((r == 4 || r == 5) && (f == 2 || f == 6));
+}
+static int az_valid_move(int from, int to) {
+  const int ff = from % 9, fr = from / 9, tf = to % 9, tr = to / 9;
+  const int df = abs(tf - ff), dr = abs(tr - fr);
+  if (df == 0 || dr == 0) return 1;
+  if ((df == 1 && dr == 2) || (df == 2 && dr == 1)) return 1;
+  if (df == 1 && dr == 1 && az_advisor_pos(fr, ff) && az_advisor_pos(tr, tf)) return 1;
+  if (df == 2 && dr == 2 && az_elephant_pos(fr, ff) && az_elephant_pos(tr, tf)) return 1;
+  return 0;
+}
+
+/* move_map (src/az.rs:3261-3285): dense index -> from * 90 + to. */
+int oracle_az_dense_moves(uint16_t* dense_to_sparse) {
+  int n = 0;
+  for (int from = 0; from < 90; ++from)
+    for (int to = 0; to < 90; ++to)
+      if (from != to && az_valid_move(from, to)) dense_to_sparse[n++] = (uint16_t)(from * 90 + to);
+  return n;
+}
+
+/* rebuild_policy_accumulator_quantization + rebuild_value_threat_quantization
+ * (src/az.rs:2201-2342).  t = the 22 tensors.  Outputs: feature_q
+ * [1546][32], move_q [2086][32], sparse_q [2396815], moved_delta / capture
+ * [2086][14] (int32), threat_q [57702][64]; scales[4] = feature, move,
+ * sparse, threat; flags[2] = value_threat_active, policy_tactical_active. */
+int oracle_az_quantize(int h, const float* const* t, int8_t* feature_q, int8_t* move_q, int8_t* sparse_q,
+                       int32_t* moved_delta, int32_t* capture, int8_t* threat_q, float* scales, int* flags) {
+  const int rank = 32, moves = 2086;
+  float* projected = (float*)malloc(sizeof(float) * 1546 * rank);
+  if (!projected) return 1;
+  const int tables[6] = {0, 1, 2, 3, 4, 6};
+  const int rows_of[6] = {1260, 14, 10, 9, 252, 1};
+  int64_t o = 0;
+  for (int k = 0; k < 6; ++k)
+    for (int r = 0; r < rows_of[k]; ++r)
+      for (int j = 0; j < rank; ++j) projected[o++] = az_dot(t[tables[k]] + (int64_t)r * h, t[17] + (int64_t)j * h, h);
+  scales[0] = az_quantize(projected, 1546 * rank, feature_q);
+  free(projected);
+  scales[1] = az_quantize(t[18], (int64_t)moves * rank, move_q);
+  /* fold the sparse factors into the main table */
+  const int64_t main_size = (int64_t)moves * 14 * 81, sparse_size = 2396815;
+  float* folded = (float*)malloc(sizeof(float) * sparse_size);
+  if (!folded) return 1;
+  memcpy(folded, t[19], sizeof(float) * sparse_size);
+  uint16_t d2s[2086];
+  oracle_az_dense_moves(d2s);
+  const int64_t mp = (int64_t)moves * 14, mk = (int64_t)moves * 81, pk = 14 * 81, dist = 14 * 6;
+  for (int m = 0; m < moves; ++m) {
+    const int from = d2s[m] / 90, to = d2s[m] % 90;
+    for (int piece = 0; piece < 14; ++piece)
+      for (int us = 0; us < 9; ++us)
+        for (int them = 0; them < 9; ++them) {
+          const int64_t main = (((int64_t)m * 14 + piece) * 9 + us) * 9 + them;
+          const int pair = us * 9 + them;
+          /* policy_king_distance_buckets (src/az.rs:841-859) */
+          const int king = 89 - ((7 + them / 3) * 9 + (3 + them % 3));
+          const int before = abs(from / 9 - king / 9) + abs(from % 9 - king % 9);
+          const int after = abs(to / 9 - king / 9) + abs(to % 9 - king % 9);
+          int approach = before - after;
+          approach = (approach < -2 ? -2 : (approach > 2 ? 2 : approach)) + 2;
+          const int distance = after < 5 ? after : 5;
+          const int64_t f[5] = {(int64_t)m * 14 + piece, mp + (int64_t)m * 81 + pair, mp + mk + piece * 81 + pair,
+                                mp + mk + pk + piece * 6 + distance, mp + mk + pk + dist + piece * 5 + approach};
+          for (int k = 0; k < 5; ++k) folded[main] += t[20][f[k]];
+        }
+  }
+  (void)main_size;
+  scales[2] = az_quantize(folded, sparse_size, sparse_q);
+  free(folded);
+  for (int m = 0; m < moves; ++m) {
+    const int from = d2s[m] / 90, to = d2s[m] % 90;
+    for (int piece = 0; piece < 14; ++piece) {
+      int32_t md = 0, cap = 0;
+      for (int j = 0; j < rank; ++j) {
+        const int32_t w = move_q[m * rank + j];
+        const int32_t tq = feature_q[(piece * 90 + to) * rank + j], fq = feature_q[(piece * 90 + from) * rank + j];
+        md += (tq - fq) * w;
+        cap += tq * w;
+      }
+      moved_delta[m * 14 + piece] = md;
+      capture[m * 14 + piece] = cap;
+    }
+  }
+  int threat_active = 0, tactical_active = 0;
+  for (int i = 0; i < 3 * 128 && !threat_active; ++i) threat_active = t[11][i] != 0.f;
+  for (int i = 0; i < 16 * 128 && !threat_active; ++i) threat_active = t[12][i] != 0.f;
+  for (int64_t i = 0; i < 934976 && !tactical_active; ++i) tactical_active = t[21][i] != 0.f;
+  scales[3] = az_quantize(t[10], 57702LL * 64, threat_q);
+  flags[0] = threat_active;
+  flags[1] = tactical_active;
+  return 0;
+}
+
+/* Saturating int16 row add (add_quantized_policy_row, src/az.rs:2439-2451). */
+static void az_policy_row(int16_t* acc, const int8_t* q, int row, int sign) {
+  for (int j = 0; j < 32; ++j) {
+    int v = (int)acc[j] + sign * (int)q[row * 32 + j];
+    acc[j] = (int16_t)(v < -32768 ? -32768 : (v > 32767 ? 32767 : v));
+  }
+}
+
+static void az_policy_piece(int16_t* acc, const int8_t* q, const int rows[6], int sign) {
+  for (int k = 0; k < 6; ++k) az_policy_row(acc, q, rows[k], sign);
+}
+
+/* quantized_policy_accumulator (src/az.rs:2344-2365): bias row 1545, then
+ * every item's 6 rows, per item.  Returns 2 if an item was skipped. */
+int oracle_az_policy_refresh(const int8_t* feature_q, const uint32_t* items, const uint32_t* offsets,
+                             int64_t n_lists, int16_t* acc) {
+  int status = 0;
+  for (int64_t l = 0; l < n_lists; ++l) {
+    int16_t* a = acc + l * 32;
+    memset(a, 0, 64);
+    az_policy_row(a, feature_q, 1545, 1);
+    for (uint32_t i = offsets[l]; i < offsets[l + 1]; ++i) {
+      int r[6];
+      if (!az_rows(items[i], r)) { status = 2; continue; }
+      az_policy_piece(a, feature_q, r, 1);
+    }
+  }
+  return status;
+}
+
+/* apply_quantized_policy_transition (src/az.rs:2367-2409). */
+int oracle_az_policy_transition(const int8_t* feature_q, const int16_t* parent, const uint32_t* delta,
+                                const uint8_t* refresh, const uint32_t* items, const uint32_t* offsets,
+                                int64_t n_lists, int16_t* child) {
+  int status = 0;
+  for (int64_t l = 0; l < n_lists; ++l) {
+    if (refresh[l] & 1) {
+      status |= oracle_az_policy_refresh(feature_q, items, offsets + l, 1, child + l * 32);
+      continue;
+    }
+    int16_t* c = child + l * 32;
+    memcpy(c, parent + l * 32, 64);
+    for (int q = 0; q < 3; ++q) {
+      const uint32_t it = delta[3 * l + q];
+      if (it == 0xffffffffu) continue;
+      int r[6];
+      if (!az_rows(it, r)) { status = 2; continue; }
+      az_policy_piece(c, feature_q, r, q < 2 ? -1 : 1);
+    }
+  }
+  return status;
+}

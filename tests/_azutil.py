@@ -34,3 +34,14 @@ def random_item_lists(n_lists: int, seed: int, max_len: int = 70, empty_every: i
         them = rng.integers(0, 9, n, dtype=np.uint32)
         lists.append((f | (us << 11) | (them << 15)).astype(np.uint32))
     return lists
+
+
+def trained_policy(weights: "az.AzWeights", seed: int) -> None:
+    """Seeded values for the policy tensors the quantiser reads (move table,
+    sparse table and factors) and a re-quantisation."""
+    rng = np.random.default_rng(seed)
+    for name, scale in (("policy_accumulator_move", 1.0), ("policy_sparse_table", 0.1),
+                        ("policy_sparse_factor", 0.1)):
+        t = weights.tensor(name)
+        t[...] = rng.standard_normal(t.shape).astype(np.float32) * np.float32(scale)
+    weights.quantize()

@@ -227,3 +227,81 @@ def test_device_model_rejects_bad_hidden_sizes_without_a_gpu():
     assert lib().cnnue_az_model_create(w.handle, 0, C.byref(h)) == 1
     w = az.AzWeights.random(516, 1)
     assert lib().cnnue_az_model_create(w.handle, 0, C.byref(h)) == 1
+
+
+def test_dense_move_space_matches_enumeration():
+    """src/az.rs:3344-3352: 2086 dense moves, dense <-> sparse inverse."""
+    d2s, s2d = az.dense_moves()
+    assert len(d2s) == 2086
+    np.testing.assert_array_equal(d2s, oracle.az_dense_moves())
+    assert all(s2d[d2s[i]] == i for i in range(2086))
+    assert (s2d != 0xFFFF).sum() == 2086
+    # rook lines from a corner: 8 + 9 targets; a horse step and a palace diagonal exist
+    assert sum(1 for s in d2s if s // 90 == 0) == 17 + 2  # + the horse steps to (1,2) and (2,1)
+    assert s2d[76 * 90 + 84] != 0xFFFF and s2d[84 * 90 + 76] != 0xFFFF  # palace diagonal (9,3) <-> (8,4)
+    assert s2d[84 * 90 + 74] == 0xFFFF  # (9,3) -> (8,2) is no palace diagonal
+
+
+@pytest.mark.parametrize("hidden,seed", [(128, 20260817), (16, 7), (100, 3)])
+def test_quantised_tables_match_oracle(hidden, seed):
+    from ._azutil import trained_policy
+    w = az.AzWeights.random(hidden, seed)
+    trained_like(w, seed % 97)
+    trained_policy(w, seed % 89)
+    ref = oracle.az_quantize(w.tensors(), hidden)
+    for which, name in enumerate(["policy_feature", "policy_move", "policy_sparse", "value_threat",
+                                  "moved_delta", "capture"]):
+        got, scale = w.quant_table(which)
+        np.testing.assert_array_equal(got.reshape(-1), ref[name].reshape(-1), err_msg=name)
+        if which < 4:
+            assert scale == ref["scales"][which], name
+    assert list(w.quant_flags()) == [bool(x) for x in ref["flags"]]
+
+
+def test_quantised_policy_rows_follow_float64_projection():
+    """Independent pin of the projection: q = round(x / scale) of the float64
+    dot products, except within 1e-3 of a rounding boundary."""
+    w = az.AzWeights.random(128, 20260817)
+    trained_like(w, 4)
+    w.quantize()
+    t = w.tensors()
+    rows = np.concatenate([t[i].astype(np.float64) for i in (0, 1, 2, 3, 4)] + [t[6][None].astype(np.float64)])
+    proj = rows @ t[17].astype(np.float64).T  # [1546][32]
+    q, scale = w.quant_table(az.Q_POLICY_FEATURE)
+    assert abs(scale - np.abs(proj).max() / 127) < 1e-6 * scale * 127
+    x = proj / scale
+    frac = np.abs(x - np.floor(x) - 0.5)
+    safe = frac > 1e-3
+    expect = np.clip(np.sign(x) * np.floor(np.abs(x) + 0.5), -127, 127)
+    np.testing.assert_array_equal(q[safe], expect[safe])
+    assert safe.mean() > 0.99
+
+
+def test_random_init_quantisation_flags_and_zero_rows():
+    w = az.AzWeights.random(128, 20260817)
+    assert w.quant_flags() == (False, False)  # zero threat and tactical outputs
+    q, _ = w.quant_table(az.Q_POLICY_FEATURE)
+    assert not q[1260:].any()  # structural and bias rows are zero at init
+    assert q[:1260].any()
+
+
+def test_policy_accumulator_incremental_equals_refresh_on_the_oracle():
+    """src/az.rs:3497-3527 on the oracle: exact equality over 32 moves."""
+    from ._azutil import trained_policy
+    w = az.AzWeights.random(128, 20260817)
+    trained_like(w, 2)
+    trained_policy(w, 3)
+    fq, _ = w.quant_table(az.Q_POLICY_FEATURE)
+    rng = np.random.default_rng(5)
+    board, _ = az.board_from_fen(az.STARTPOS)
+    st, acc = oracle.az_policy_refresh(fq, *az.node_lists(board[None]))
+    assert st == 0
+    for ply in range(32):
+        frm, to = az.random_move(board, rng, side=ply % 2)
+        ms = [az.move_items(board, frm, to, p) for p in (0, 1)]
+        r_items, r_off = az.pack_lists([m.items for m in ms])
+        st, acc = oracle.az_policy_transition(fq, acc, np.stack([m.delta for m in ms]),
+                                              np.array([m.refresh for m in ms], np.uint8), r_items, r_off)
+        board = az.apply_move(board, frm, to)
+        st2, full = oracle.az_policy_refresh(fq, *az.node_lists(board[None]))
+        np.testing.assert_array_equal(acc, full)

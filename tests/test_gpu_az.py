@@ -188,3 +188,105 @@ def test_random_init_value_is_neutral():
         np.testing.assert_allclose(wdl.cpu().numpy(), 1.0 / 3.0, atol=1e-6)
     finally:
         model.close()
+
+
+# ---- int16 policy accumulator (bit-exact) -----------------------------------
+_POLICY = {}
+
+
+def _policy_model():
+    if "m" not in _POLICY:
+        from ._azutil import trained_policy
+        w = az.AzWeights.random(128, 20260817)
+        trained_like(w, 31)
+        trained_policy(w, 32)
+        fq, _ = w.quant_table(az.Q_POLICY_FEATURE)
+        _POLICY["m"] = (w, fq, az.AzModel(w, device=0))
+    return _POLICY["m"]
+
+
+def test_policy_refresh_bit_exact():
+    w, fq, model = _policy_model()
+    boards = az.random_boards(1500, seed=41)
+    items, offsets = az.node_lists(boards)
+    acc = model.policy_refresh(_dev(items), _dev(offsets))
+    assert model.read_status() == 0
+    st, ref = oracle.az_policy_refresh(fq, items, offsets)
+    assert st == 0
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+
+
+def _hottest_item(fq):
+    """The packed item whose 6 policy rows have the largest |sum| at one rank."""
+    q = fq.astype(np.int32)
+    f = np.arange(1260)
+    piece, sq = f // 90, f % 90
+    base = q[f] + q[1260 + piece] + q[1274 + sq // 9] + q[1284 + sq % 9]  # [1260][32]
+    best, best_item = -1, 0
+    for us in range(9):
+        for them in range(9):
+            tot = base + q[1293 + us * 14 + piece] + q[1293 + (9 + them) * 14 + piece]
+            i = int(np.argmax(np.abs(tot).max(axis=1)))
+            v = int(np.abs(tot[i]).max())
+            if v > best:
+                best, best_item = v, i | (us << 11) | (them << 15)
+    assert best * 90 > 32767
+    return np.uint32(best_item)
+
+
+def test_policy_refresh_saturates_like_the_reference():
+    """Lists of 90 copies of the item whose rows hold +-127 push int16 past its
+    range; each row add clamps, in order, as add_quantized_policy_row does."""
+    w, fq, model = _policy_model()
+    hot = _hottest_item(fq)
+    lists = random_item_lists(300, seed=42, max_len=90)
+    for i in range(0, 300, 3):
+        lists[i] = np.full(90, hot, np.uint32)
+    items, offsets = az.pack_lists(lists)
+    acc = model.policy_refresh(_dev(items), _dev(offsets))
+    st, ref = oracle.az_policy_refresh(fq, items, offsets)
+    assert model.read_status() == 0 and st == 0
+    assert (np.abs(ref.astype(np.int32)) == 32767).any() or (ref == -32768).any()
+    np.testing.assert_array_equal(acc.cpu().numpy(), ref)
+    # transitions from saturated parents
+    delta = np.tile(np.array([hot, az.NO_ITEM, hot], np.uint32), (len(lists), 1))
+    delta[1::2, 1] = hot
+    refresh = np.zeros(len(lists), np.uint8)
+    child = model.policy_transition(acc, _dev(delta), _dev(refresh))
+    st, ref2 = oracle.az_policy_transition(fq, ref, delta, refresh, np.zeros(0, np.uint32),
+                                           np.zeros(len(lists) + 1, np.uint32))
+    np.testing.assert_array_equal(child.cpu().numpy(), ref2)
+
+
+def test_policy_transition_bit_exact_and_in_place():
+    w, fq, model = _policy_model()
+    boards = az.random_boards(1200, seed=43)
+    parent = model.policy_refresh(*[_dev(a) for a in az.node_lists(boards)])
+    delta, refresh, items, offsets, afters = _moves(boards, seed=44)
+    child = model.policy_transition(parent, _dev(delta), _dev(refresh), _dev(items), _dev(offsets))
+    assert model.read_status() == 0
+    st, ref = oracle.az_policy_transition(fq, parent.cpu().numpy(), delta, refresh, items, offsets)
+    np.testing.assert_array_equal(child.cpu().numpy(), ref)
+    model.policy_transition(parent, _dev(delta), _dev(refresh), _dev(items), _dev(offsets), out=parent)
+    np.testing.assert_array_equal(parent.cpu().numpy(), ref)
+    # equals the refresh of the child boards exactly (no saturation at <= 32 pieces)
+    full = model.policy_refresh(*[_dev(a) for a in az.node_lists(afters)])
+    assert torch.equal(parent, full)
+
+
+def test_policy_walk_matches_refresh_exactly():
+    """src/az.rs:3497-3527 on the device."""
+    w, fq, model = _policy_model()
+    rng = np.random.default_rng(45)
+    board, _ = az.board_from_fen(az.STARTPOS)
+    acc = model.policy_refresh(*[_dev(a) for a in az.node_lists(board[None])])
+    for ply in range(32):
+        frm, to = az.random_move(board, rng, side=ply % 2)
+        ms = [az.move_items(board, frm, to, p) for p in (0, 1)]
+        r_items, r_off = az.pack_lists([m.items for m in ms])
+        acc = model.policy_transition(acc, _dev(np.stack([m.delta for m in ms])),
+                                      _dev(np.array([m.refresh for m in ms], np.uint8)), _dev(r_items), _dev(r_off))
+        board = az.apply_move(board, frm, to)
+        full = model.policy_refresh(*[_dev(a) for a in az.node_lists(board[None])])
+        assert torch.equal(acc, full)
+    assert model.read_status() == 0

@@ -85,6 +85,12 @@ SIGNATURES = {
     "cnnue_az_dense_moves": (c_int, [P, P]),
     "cnnue_az_policy_refresh": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_az_policy_transition": (c_int, [c_void_p, P, P, P, P, c_u32, P, c_i64, P, P, c_size, P]),
+    "cnnue_rn_model_create": (c_int, [C.c_void_p, c_int, C.POINTER(c_void_p)]),
+    "cnnue_rn_model_destroy": (c_int, [c_void_p]),
+    "cnnue_rn_workspace_bytes": (c_size, [c_i64]),
+    "cnnue_rn_forward": (c_int, [c_void_p, P, c_i64, P, P, P, P, c_size, P]),
+    "cnnue_synth_rn_weights": (c_int, [c_u64] + [P] * 14),
+    "cnnue_synth_rn_planes": (c_int, [c_u64, c_i64, P]),
     "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),
     "cnnue_synth_positions": (c_int, [c_u64, c_i64, c_u32, c_u32, c_u32, P, P, C.POINTER(c_u32)]),
     "cnnue_synth_q_weights": (c_int, [c_u64, P, P, P, P, P, P, P, P]),

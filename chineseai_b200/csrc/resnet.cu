@@ -1,0 +1,618 @@
+// resnet.cu - AlphaZero policy/value ResNet inference for MCTS leaf batches
+// (the dense tensor-core part of the evaluator).
+//
+// Trunk: 21 3x3 convolutions (stem 15->128, 10 residual blocks of two
+// 128->128), each an implicit GEMM on the 5th-generation tensor cores:
+// rows = board squares of the batch (M = 90 B), columns = 128 output
+// channels, K = 9 taps x input channels.  Activations are bf16, square-major
+// ([B*90][C], channels contiguous); the stem input is packed to 64 channels.
+//
+// rn_conv_kernel, one CTA per 128 x 128 output tile, 6 warps:
+//   warp 4     allocates the 128 TMEM columns of the fp32 accumulator and
+//              loads each 64-wide K block: the A tile (one tap, 64 channels
+//              of 128 squares) with one 2-D TMA of the tap-shifted row range
+//              (square-major rows make a tap a constant row shift), the B tile
+//              with one bulk copy of weights pre-tiled in the same 128-byte
+//              swizzled K-major layout;
+//   warps 0-3  zero the rows whose tap leaves the board (a row is one
+//              128-byte line of the swizzled tile), then are the epilogue
+//              (TMEM -> registers, + bias (+ residual), ReLU, bf16, store);
+//   warp 5     one thread issues tcgen05.mma (M128 N128 K16, 4 per K block)
+//              and commits each stage back to its producers.
+// A 3-stage ring of (16 KB A + 16 KB B) stages with three mbarriers each
+// (loaded, ready, empty); every wait is bounded (1 s) and reports
+// CNNUE_STATUS_TIMEOUT.  No load uses cluster multicast.
+//
+// Heads, fp32 on CUDA cores: rn_head_prep_kernel (1x1 convs to 2 policy and
+// 1 value planes, value FC 90 -> 256 -> 1 with tanh, 8 boards per CTA),
+// rn_policy_fc_kernel (FC 180 -> 2086 as a tiled GEMM, 32 boards x 128 moves
+// per CTA), rn_softmax_kernel (one warp per board).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include <cstring>
+#include <new>
+#include <vector>
+
+#include "common.cuh"
+#include "pipeline.cuh"
+#include "tcgen05.cuh"
+
+namespace cnnue {
+namespace rn {
+namespace {
+
+constexpr int kSq = 90;
+constexpr int kC = CNNUE_RN_CHANNELS;
+constexpr int kMoves = CNNUE_RN_MOVES;
+constexpr int kConvs = 1 + 2 * CNNUE_RN_BLOCKS;
+constexpr int kTileM = 128;
+constexpr int kTileBytes = 128 * 64 * 2;  // 128 rows x 64 bf16
+constexpr int kStages = 3;
+constexpr int kConvThreads = 192;
+constexpr int kStemKb = 9;   // 9 taps x 64 (packed) channels / 64
+constexpr int kBlockKb = 18; // 9 taps x 128 channels / 64
+constexpr int kHeadBoards = 8;
+
+inline size_t conv_tile_offset(int conv) { return conv == 0 ? 0 : (size_t)kStemKb + (size_t)(conv - 1) * kBlockKb; }
+constexpr size_t kTotalKb = kStemKb + (size_t)(kConvs - 1) * kBlockKb;
+
+struct ConvSmem {
+  alignas(1024) uint8_t a[kStages][kTileBytes];
+  alignas(1024) uint8_t b[kStages][kTileBytes];
+  uint64_t loaded[kStages];  // A (TMA) and B (bulk copy) bytes landed
+  uint64_t ready[kStages];   // off-board rows of A zeroed
+  uint64_t empty[kStages];   // the stage's MMAs completed
+  uint64_t accum;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// Byte offset of (row, k) inside a 128 x 64 bf16 tile in the 128B-swizzled
+// K-major layout: row r is the 128-byte line r, its 16-byte chunk c is stored
+// at chunk position c ^ (r % 8).
+__host__ __device__ constexpr uint32_t tile_offset(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k >> 3) ^ row) & 7) << 4) + (k & 7) * 2);
+}
+
+template <int CIN>
+__global__ void __launch_bounds__(kConvThreads) rn_conv_kernel(const __grid_constant__ CUtensorMap tmap_in,
+                                                               const uint8_t* __restrict__ wtiles,
+                                                               const float* __restrict__ bias,
+                                                               const __nv_bfloat16* __restrict__ resid,
+                                                               __nv_bfloat16* __restrict__ out, int M,
+                                                               uint32_t* status) {
+  constexpr int kKbPerTap = CIN / 64;
+  constexpr int kKb = 9 * kKbPerTap;
+  extern __shared__ uint8_t smem_raw[];
+  ConvSmem& sm = *reinterpret_cast<ConvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m0 = blockIdx.x * kTileM;
+
+  if (warp == 4) {
+    tc::tmem_alloc(pipe::smem_addr(&sm.tmem_base), 128);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      pipe::mbar_init(&sm.loaded[s], 1);
+      pipe::mbar_init(&sm.ready[s], 128);
+      pipe::mbar_init(&sm.empty[s], 1);
+    }
+    pipe::mbar_init(&sm.accum, 1);
+    sm.abort = 0;
+    pipe::mbar_init_fence();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp < 4) {
+    // ---- edge fix-up: the TMA copied rows m0+shift .. m0+shift+127 of the
+    // activations; row t whose tap leaves the board must read zeros.
+    const int row = tid, m = m0 + row;
+    const int p = (m < M ? m : 0) % kSq, r = p / 9, f = p - (p / 9) * 9;
+    for (int kb = 0; kb < kKb; ++kb) {
+      const int s = kb % kStages, u = kb / kStages;
+      if (!pipe::mbar_wait(&sm.loaded[s], u & 1, &sm.abort, status)) break;
+      const int tap = kb / kKbPerTap;
+      const int r2 = r + tap / 3 - 1, f2 = f + tap % 3 - 1;
+      if (m < M && (r2 < 0 || r2 > 9 || f2 < 0 || f2 > 8)) {
+        uint8_t* line = sm.a[s] + row * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<uint4*>(line + (((i + row) & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+      }
+      pipe::fence_proxy_async_smem();
+      pipe::mbar_arrive(&sm.ready[s]);
+    }
+    // ---- epilogue: TMEM lane = row.
+    const bool ok = pipe::mbar_wait(&sm.accum, 0, &sm.abort, status);
+    tc::fence_after_sync();
+    const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
+    const bool active = ok && m < M;
+#pragma unroll 1
+    for (int j = 0; j < 4; ++j) {
+      uint32_t v[32];
+      __syncwarp();  // converged for the .sync.aligned TMEM load
+      tc::tmem_ld32(taddr + 32 * j, v);
+      tc::wait_ld();
+      if (!active) continue;
+      float res[32];
+      if (resid != nullptr) {
+        const uint4* rp = reinterpret_cast<const uint4*>(resid + (size_t)m * kC + 32 * j);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = __ldg(rp + q);
+          const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat162 h2 = *reinterpret_cast<const __nv_bfloat162*>(&ws[e]);
+            res[8 * q + 2 * e] = __bfloat162float(h2.x);
+            res[8 * q + 2 * e + 1] = __bfloat162float(h2.y);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) res[i] = 0.f;
+      }
+      uint32_t packed[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        float x0 = __uint_as_float(v[2 * i]) + __ldg(bias + 32 * j + 2 * i) + res[2 * i];
+        float x1 = __uint_as_float(v[2 * i + 1]) + __ldg(bias + 32 * j + 2 * i + 1) + res[2 * i + 1];
+        x0 = fmaxf(x0, 0.f);
+        x1 = fmaxf(x1, 0.f);
+        const __nv_bfloat162 h2 = __floats2bfloat162_rn(x0, x1);
+        packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
+      }
+      uint4* op = reinterpret_cast<uint4*>(out + (size_t)m * kC + 32 * j);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        op[q] = make_uint4(packed[4 * q], packed[4 * q + 1], packed[4 * q + 2], packed[4 * q + 3]);
+    }
+  } else if (warp == 4) {
+    // ---- loads: A by one 2-D TMA of the tap-shifted rows (zeros past the
+    // buffer's ends), B by one bulk copy of the pre-tiled weights.
+    if (lane == 0) {
+      for (int kb = 0; kb < kKb; ++kb) {
+        const int s = kb % kStages, u = kb / kStages;
+        if (u > 0 && !pipe::mbar_wait(&sm.empty[s], (u - 1) & 1, &sm.abort, status)) break;
+        const int tap = kb / kKbPerTap, c0 = (kb % kKbPerTap) * 64;
+        const int shift = (tap / 3 - 1) * 9 + (tap % 3 - 1);
+        pipe::mbar_arrive_expect_tx(&sm.loaded[s], 2 * kTileBytes);
+        tc::tma_load_2d(pipe::smem_addr(sm.a[s]), &tmap_in, c0, m0 + shift, pipe::smem_addr(&sm.loaded[s]));
+        pipe::bulk_copy_g2s(sm.b[s], wtiles + (size_t)kb * kTileBytes, kTileBytes, &sm.loaded[s]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- MMA issuer.
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(128, 128);
+      for (int kb = 0; kb < kKb; ++kb) {
+        const int s = kb % kStages, u = kb / kStages;
+        if (!pipe::mbar_wait(&sm.ready[s], u & 1, &sm.abort, status)) break;
+        tc::fence_after_sync();
+        const uint32_t a0 = pipe::smem_addr(sm.a[s]), b0 = pipe::smem_addr(sm.b[s]);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint64_t ad = tc::smem_desc(a0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+          const uint64_t bd = tc::smem_desc(b0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+          tc::mma_bf16(tmem, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+        }
+        tc::commit(pipe::smem_addr(&sm.empty[s]));
+      }
+      tc::commit(pipe::smem_addr(&sm.accum));
+    }
+    __syncwarp();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 4) tc::tmem_dealloc(tmem, 128);
+}
+
+// [B][15][90] bf16 planes -> [B*90][64] bf16, channels 15..63 zero.
+__global__ void rn_pack_kernel(const __nv_bfloat16* __restrict__ planes, int64_t B, __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * kSq) return;
+  const int64_t b = i / kSq;
+  const int p = (int)(i - b * kSq);
+  uint32_t w[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) w[k] = 0u;
+#pragma unroll
+  for (int c = 0; c < CNNUE_RN_PLANES; ++c) {
+    const uint16_t v = reinterpret_cast<const uint16_t*>(planes)[(b * CNNUE_RN_PLANES + c) * kSq + p];
+    w[c >> 1] |= (uint32_t)v << (16 * (c & 1));
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + i * 64);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
+struct HeadArgs {
+  const __nv_bfloat16* trunk;  // [B*90][128]
+  const float* pcw;            // [2][128]
+  const float* pcb;            // [2]
+  const float* pfw_t;          // [180][2086]
+  const float* pfb;            // [2086]
+  const float* vcw;            // [128]
+  const float* vcb;            // [1]
+  const float* v1w_t;          // [90][256]
+  const float* v1b;            // [256]
+  const float* v2w;            // [256]
+  const float* v2b;            // [1]
+  int64_t B;
+  float* logits;  // [B][2086] or null
+  float* probs;   // [B][2086]
+  float* value;   // [B]
+};
+
+constexpr int kHeadThreads = 256;
+
+// 1x1 convs of 8 boards (policy planes to pc [B][180], value plane) and the
+// value MLP 90 -> 256 -> 1 with tanh.
+__global__ void __launch_bounds__(kHeadThreads) rn_head_prep_kernel(HeadArgs a, float* __restrict__ pc_out) {
+  __shared__ float vc[kHeadBoards][kSq];
+  __shared__ float red[kHeadBoards][kHeadThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b0 = (int64_t)blockIdx.x * kHeadBoards;
+  for (int i = tid; i < kHeadBoards * kSq; i += kHeadThreads) {
+    const int bl = i / kSq, p = i - bl * kSq;
+    const int64_t b = b0 + bl;
+    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+    if (b < a.B) {
+      const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(a.trunk + (size_t)(b * kSq + p) * kC);
+#pragma unroll 8
+      for (int c2 = 0; c2 < kC / 2; ++c2) {
+        const float2 x = __bfloat1622float2(row[c2]);
+        s0 = fmaf(x.x, __ldg(a.pcw + 2 * c2), s0);
+        s0 = fmaf(x.y, __ldg(a.pcw + 2 * c2 + 1), s0);
+        s1 = fmaf(x.x, __ldg(a.pcw + kC + 2 * c2), s1);
+        s1 = fmaf(x.y, __ldg(a.pcw + kC + 2 * c2 + 1), s1);
+        s2 = fmaf(x.x, __ldg(a.vcw + 2 * c2), s2);
+        s2 = fmaf(x.y, __ldg(a.vcw + 2 * c2 + 1), s2);
+      }
+      pc_out[b * 2 * kSq + p] = fmaxf(s0 + a.pcb[0], 0.f);
+      pc_out[b * 2 * kSq + kSq + p] = fmaxf(s1 + a.pcb[1], 0.f);
+    }
+    vc[bl][p] = fmaxf(s2 + a.vcb[0], 0.f);
+  }
+  __syncthreads();
+  float hsum[kHeadBoards];
+#pragma unroll
+  for (int bl = 0; bl < kHeadBoards; ++bl) hsum[bl] = 0.f;
+  for (int p = 0; p < kSq; ++p) {
+    const float w = __ldg(a.v1w_t + (size_t)p * 256 + tid);
+#pragma unroll
+    for (int bl = 0; bl < kHeadBoards; ++bl) hsum[bl] = fmaf(vc[bl][p], w, hsum[bl]);
+  }
+  const float w2 = __ldg(a.v2w + tid), b1 = __ldg(a.v1b + tid);
+#pragma unroll
+  for (int bl = 0; bl < kHeadBoards; ++bl) {
+    float v = fmaxf(hsum[bl] + b1, 0.f) * w2;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[bl][warp] = v;
+  }
+  __syncthreads();
+  if (tid < kHeadBoards && b0 + tid < a.B) {
+    float v = 0.f;
+    for (int w = 0; w < kHeadThreads / 32; ++w) v += red[tid][w];
+    a.value[b0 + tid] = tanhf(v + a.v2b[0]);
+  }
+}
+
+// Policy FC logits[B][2086] = pc[B][180] . W^T + b: CTA tile 32 boards x 128
+// moves, K staged in smem in chunks of 36; thread = 4 boards x 4 moves.
+constexpr int kFcBoards = 32, kFcMoves = 128, kFcK = 36;
+__global__ void __launch_bounds__(256) rn_policy_fc_kernel(const float* __restrict__ pc,
+                                                           const float* __restrict__ pfw_t,
+                                                           const float* __restrict__ pfb, int64_t B,
+                                                           float* __restrict__ logits) {
+  __shared__ float xs[kFcK][kFcBoards + 1];
+  __shared__ float ws[kFcK][kFcMoves];
+  const int tid = threadIdx.x;
+  const int64_t b0 = (int64_t)blockIdx.x * kFcBoards;
+  const int j0 = blockIdx.y * kFcMoves;
+  const int tb = (tid >> 5) * 4, tj = (tid & 31) * 4;  // 8 x 4 boards, 32 x 4 moves
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < 2 * kSq; k0 += kFcK) {
+    for (int i = tid; i < kFcK * kFcBoards; i += 256) {
+      const int bl = i / kFcK, k = i - bl * kFcK;
+      xs[k][bl] = b0 + bl < B ? pc[(b0 + bl) * 2 * kSq + k0 + k] : 0.f;
+    }
+    for (int i = tid; i < kFcK * kFcMoves; i += 256) {
+      const int k = i / kFcMoves, jj = i - k * kFcMoves;
+      ws[k][jj] = j0 + jj < kMoves ? __ldg(pfw_t + (size_t)(k0 + k) * kMoves + j0 + jj) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 6
+    for (int k = 0; k < kFcK; ++k) {
+      float x[4], w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) x[i] = xs[k][tb + i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w[i] = ws[k][tj + i];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(x[i], w[q], acc[i][q]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int64_t b = b0 + tb + i;
+    if (b >= B) continue;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int j = j0 + tj + q;
+      if (j < kMoves) logits[b * kMoves + j] = acc[i][q] + __ldg(pfb + j);
+    }
+  }
+}
+
+// Softmax over the 2086 logits of a board, one warp per board.
+__global__ void __launch_bounds__(256) rn_softmax_kernel(const float* __restrict__ logits, int64_t B,
+                                                         float* __restrict__ probs) {
+  const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;
+  const float* row = logits + b * kMoves;
+  float m = -INFINITY;
+  for (int j = lane; j < kMoves; j += 32) m = fmaxf(m, row[j]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.f;
+  for (int j = lane; j < kMoves; j += 32) s += expf(row[j] - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float inv = 1.f / s;
+  for (int j = lane; j < kMoves; j += 32) probs[b * kMoves + j] = expf(row[j] - m) * inv;
+}
+
+// Host: fp32 -> bf16 bits, round to nearest even.
+inline uint16_t to_bf16(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);  // quiet NaN
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// One conv's weights (OIHW [128][cin][3][3]) as K-block tiles of the UMMA
+// layout: K index = tap * cin_pad + channel; channels >= cin are zero.
+void tile_conv(const float* w, int cin, int cin_pad, uint8_t* dst) {
+  const int kb_per_tap = cin_pad / 64;
+  for (int kb = 0; kb < 9 * kb_per_tap; ++kb) {
+    const int tap = kb / kb_per_tap, c0 = (kb % kb_per_tap) * 64;
+    const int kh = tap / 3, kw = tap % 3;
+    uint8_t* tile = dst + (size_t)kb * kTileBytes;
+    for (int n = 0; n < kC; ++n)
+      for (int k = 0; k < 64; ++k) {
+        const int c = c0 + k;
+        const float v = c < cin ? w[((n * cin + c) * 3 + kh) * 3 + kw] : 0.f;
+        const uint16_t h = to_bf16(v);
+        std::memcpy(tile + tile_offset(n, k), &h, 2);
+      }
+  }
+}
+
+size_t conv_smem_bytes() { return sizeof(ConvSmem) + 1024; }
+
+// cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map of an activation buffer [M][cin] bf16 read in boxes of 128 rows
+// x 64 channels with the 128-byte swizzle; rows outside [0, M) read zeros.
+int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  if (!fn) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {(cuuint64_t)cin, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)cin * 2};
+  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return CNNUE_OK;
+}
+
+}  // namespace
+}  // namespace rn
+}  // namespace cnnue
+
+struct cnnue_rn_model {
+  int device = 0;
+  void* blob = nullptr;
+  uint8_t* tiles = nullptr;  // [kTotalKb][16 KB]
+  float* conv_bias = nullptr;  // [21][128]
+  float* head = nullptr;       // heads, see HeadArgs
+  cnnue::rn::HeadArgs h{};
+};
+
+using namespace cnnue;
+using namespace cnnue::rn;
+
+extern "C" {
+
+size_t cnnue_rn_workspace_bytes(int64_t batch) {
+  const size_t m = batch > 0 ? (size_t)batch * kSq : 0;
+  const size_t b = batch > 0 ? (size_t)batch : 0;
+  return sizeof(WorkspaceHeader) + align_up(m * 64 * 2, 256) + 3 * align_up(m * kC * 2, 256) +
+         align_up(b * 2 * kSq * 4, 256) + align_up(b * kMoves * 4, 256);
+}
+
+int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model** out) {
+  if (!w || !out || !w->stem_w || !w->stem_b || !w->block_w || !w->block_b || !w->policy_conv_w ||
+      !w->policy_conv_b || !w->policy_fc_w || !w->policy_fc_b || !w->value_conv_w || !w->value_conv_b ||
+      !w->value_fc1_w || !w->value_fc1_b || !w->value_fc2_w || !w->value_fc2_b)
+    return set_error(CNNUE_ERR_INVALID_ARG, "null weights");
+  *out = nullptr;
+  DeviceGuard guard(device);
+  if (guard.status) return guard.status;
+  // host staging: tiles, biases, heads (transposed where the kernel reads columns)
+  std::vector<uint8_t> tiles(kTotalKb * kTileBytes);
+  tile_conv(w->stem_w, CNNUE_RN_PLANES, 64, tiles.data());
+  for (int j = 0; j < 2 * CNNUE_RN_BLOCKS; ++j)
+    tile_conv(w->block_w + (size_t)j * kC * kC * 9, kC, kC, tiles.data() + conv_tile_offset(1 + j) * kTileBytes);
+  std::vector<float> bias((size_t)kConvs * kC);
+  std::memcpy(bias.data(), w->stem_b, sizeof(float) * kC);
+  std::memcpy(bias.data() + kC, w->block_b, sizeof(float) * 2 * CNNUE_RN_BLOCKS * kC);
+  const size_t n_pfw = (size_t)2 * kSq * kMoves, n_v1 = (size_t)kSq * 256;
+  std::vector<float> head(2 * kC + 2 + n_pfw + kMoves + kC + 1 + n_v1 + 256 + 256 + 1);
+  float* hp = head.data();
+  float* pcw = hp; std::memcpy(pcw, w->policy_conv_w, sizeof(float) * 2 * kC); hp += 2 * kC;
+  float* pcb = hp; std::memcpy(pcb, w->policy_conv_b, sizeof(float) * 2); hp += 2;
+  float* pfw_t = hp;
+  for (int j = 0; j < kMoves; ++j)
+    for (int k = 0; k < 2 * kSq; ++k) pfw_t[(size_t)k * kMoves + j] = w->policy_fc_w[(size_t)j * 2 * kSq + k];
+  hp += n_pfw;
+  float* pfb = hp; std::memcpy(pfb, w->policy_fc_b, sizeof(float) * kMoves); hp += kMoves;
+  float* vcw = hp; std::memcpy(vcw, w->value_conv_w, sizeof(float) * kC); hp += kC;
+  float* vcb = hp; vcb[0] = w->value_conv_b[0]; hp += 1;
+  float* v1w_t = hp;
+  for (int i = 0; i < 256; ++i)
+    for (int p = 0; p < kSq; ++p) v1w_t[(size_t)p * 256 + i] = w->value_fc1_w[(size_t)i * kSq + p];
+  hp += n_v1;
+  float* v1b = hp; std::memcpy(v1b, w->value_fc1_b, sizeof(float) * 256); hp += 256;
+  float* v2w = hp; std::memcpy(v2w, w->value_fc2_w, sizeof(float) * 256); hp += 256;
+  float* v2b = hp; v2b[0] = w->value_fc2_b[0];
+
+  auto* m = new (std::nothrow) cnnue_rn_model;
+  if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
+  m->device = device;
+  const size_t t_bytes = align_up(tiles.size(), 1024), b_bytes = align_up(bias.size() * 4, 256);
+  const size_t h_bytes = align_up(head.size() * 4, 256);
+  cudaError_t e = cudaMalloc(&m->blob, t_bytes + b_bytes + h_bytes);
+  if (e != cudaSuccess) {
+    delete m;
+    return cuda_error(e, "cudaMalloc(resnet model)");
+  }
+  m->tiles = (uint8_t*)m->blob;
+  m->conv_bias = (float*)((char*)m->blob + t_bytes);
+  m->head = (float*)((char*)m->blob + t_bytes + b_bytes);
+  int st = CNNUE_OK;
+  if ((e = cudaMemcpy(m->tiles, tiles.data(), tiles.size(), cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->conv_bias, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess ||
+      (e = cudaMemcpy(m->head, head.data(), head.size() * 4, cudaMemcpyHostToDevice)) != cudaSuccess)
+    st = cuda_error(e, "resnet weight upload");
+  if (!st) {
+    const int smem = (int)conv_smem_bytes();
+    if ((e = cudaFuncSetAttribute(rn_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+            cudaSuccess ||
+        (e = cudaFuncSetAttribute(rn_conv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
+            cudaSuccess)
+      st = cuda_error(e, "cudaFuncSetAttribute(rn_conv_kernel)");
+  }
+  if (st) {
+    cudaFree(m->blob);
+    delete m;
+    return st;
+  }
+  float* dh = m->head;
+  auto off = [&](const float* host_ptr) { return dh + (host_ptr - head.data()); };
+  m->h.pcw = off(pcw);
+  m->h.pcb = off(pcb);
+  m->h.pfw_t = off(pfw_t);
+  m->h.pfb = off(pfb);
+  m->h.vcw = off(vcw);
+  m->h.vcb = off(vcb);
+  m->h.v1w_t = off(v1w_t);
+  m->h.v1b = off(v1b);
+  m->h.v2w = off(v2w);
+  m->h.v2b = off(v2b);
+  *out = m;
+  return CNNUE_OK;
+}
+
+int cnnue_rn_model_destroy(cnnue_rn_model* m) {
+  if (!m) return CNNUE_OK;
+  DeviceGuard guard(m->device);
+  if (m->blob) cudaFree(m->blob);
+  delete m;
+  return guard.status;
+}
+
+int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t batch, float* d_probs,
+                     float* d_logits, float* d_value, void* ws, size_t ws_bytes, void* stream) {
+  if (!m || !ws || batch < 0 || (batch > 0 && (!d_planes || !d_probs || !d_value)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, planes, probs or value, or batch < 0");
+  if (batch > (int64_t)1 << 22) return set_error(CNNUE_ERR_INVALID_ARG, "batch %lld too large", (long long)batch);
+  if (ws_bytes < cnnue_rn_workspace_bytes(batch))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, cnnue_rn_workspace_bytes(batch));
+  if ((uintptr_t)d_planes & 1u) return set_error(CNNUE_ERR_INVALID_ARG, "planes must be 2-byte aligned");
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (batch == 0) return CNNUE_OK;
+  const int M = (int)(batch * kSq);
+  char* p = (char*)ws + sizeof(WorkspaceHeader);
+  auto* in64 = (__nv_bfloat16*)p;
+  p += align_up((size_t)M * 64 * 2, 256);
+  __nv_bfloat16* act[3];
+  for (int i = 0; i < 3; ++i) {
+    act[i] = (__nv_bfloat16*)p;
+    p += align_up((size_t)M * kC * 2, 256);
+  }
+  float* pc = (float*)p;
+  p += align_up((size_t)batch * 2 * kSq * 4, 256);
+  float* logits = d_logits ? d_logits : (float*)p;
+  uint32_t* status = &((WorkspaceHeader*)ws)->status;
+  rn_pack_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, in64);
+  if (int st = check_launch_error("rn_pack_kernel")) return st;
+  const unsigned tiles = (unsigned)((M + kTileM - 1) / kTileM);
+  const size_t smem = conv_smem_bytes();
+  CUtensorMap map_in, map_act[3];
+  if (int st = make_act_map(&map_in, in64, 64, M)) return st;
+  for (int i = 0; i < 3; ++i)
+    if (int st = make_act_map(&map_act[i], act[i], kC, M)) return st;
+  rn_conv_kernel<64><<<tiles, kConvThreads, smem, s>>>(map_in, m->tiles, m->conv_bias, nullptr, act[0], M, status);
+  if (int st = check_launch_error("rn_conv_kernel<64>")) return st;
+  int x = 0;
+  for (int blk = 0; blk < CNNUE_RN_BLOCKS; ++blk) {
+    const int h = (x + 1) % 3, y = (x + 2) % 3;
+    const int c1 = 1 + 2 * blk, c2 = c1 + 1;
+    rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map_act[x], m->tiles + conv_tile_offset(c1) * kTileBytes,
+                                                         m->conv_bias + c1 * kC, nullptr, act[h], M, status);
+    if (int st = check_launch_error("rn_conv_kernel<128>")) return st;
+    rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map_act[h], m->tiles + conv_tile_offset(c2) * kTileBytes,
+                                                         m->conv_bias + c2 * kC, act[x], act[y], M, status);
+    if (int st = check_launch_error("rn_conv_kernel<128>")) return st;
+    x = y;
+  }
+  HeadArgs h = m->h;
+  h.trunk = act[x];
+  h.B = batch;
+  h.logits = logits;
+  h.probs = d_probs;
+  h.value = d_value;
+  rn_head_prep_kernel<<<(unsigned)((batch + kHeadBoards - 1) / kHeadBoards), kHeadThreads, 0, s>>>(h, pc);
+  if (int st = check_launch_error("rn_head_prep_kernel")) return st;
+  const dim3 fc_grid((unsigned)((batch + kFcBoards - 1) / kFcBoards), (kMoves + kFcMoves - 1) / kFcMoves);
+  rn_policy_fc_kernel<<<fc_grid, 256, 0, s>>>(pc, h.pfw_t, h.pfb, batch, logits);
+  if (int st = check_launch_error("rn_policy_fc_kernel")) return st;
+  rn_softmax_kernel<<<(unsigned)((batch + 7) / 8), 256, 0, s>>>(logits, batch, d_probs);
+  return check_launch_error("rn_softmax_kernel");
+}
+
+}  // extern "C"

@@ -7,6 +7,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdint>
+#include <cstring>
 #include <vector>
 
 #include "../../include/cnnue.h"
@@ -166,6 +167,68 @@ int cnnue_synth_q_update(uint64_t seed, int64_t n_positions, int16_t* h_parent, 
   }
   *n_rem = nr;
   *n_add = na;
+  return CNNUE_OK;
+}
+
+// bf16 value of f, round to nearest even (finite inputs).
+static float bf16_value(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+int cnnue_synth_rn_weights(uint64_t seed, float* stem_w, float* stem_b, float* block_w, float* block_b,
+                           float* policy_conv_w, float* policy_conv_b, float* policy_fc_w, float* policy_fc_b,
+                           float* value_conv_w, float* value_conv_b, float* value_fc1_w, float* value_fc1_b,
+                           float* value_fc2_w, float* value_fc2_b) {
+  if (!stem_w || !stem_b || !block_w || !block_b || !policy_conv_w || !policy_conv_b || !policy_fc_w ||
+      !policy_fc_b || !value_conv_w || !value_conv_b || !value_fc1_w || !value_fc1_b || !value_fc2_w ||
+      !value_fc2_b)
+    return CNNUE_ERR_INVALID_ARG;
+  Rng rng{seed};
+  auto fill = [&](float* dst, size_t n, double std) {
+    for (size_t i = 0; i < n; ++i) dst[i] = bf16_value((float)(rng.normal() * std));
+  };
+  const int C = CNNUE_RN_CHANNELS;
+  fill(stem_w, (size_t)C * CNNUE_RN_PLANES * 9, std::sqrt(2.0 / (CNNUE_RN_PLANES * 9)));
+  fill(stem_b, C, 0.02);
+  for (int j = 0; j < 2 * CNNUE_RN_BLOCKS; ++j)
+    fill(block_w + (size_t)j * C * C * 9, (size_t)C * C * 9, std::sqrt(2.0 / (C * 9)) * (j % 2 ? 0.25 : 1.0));
+  fill(block_b, (size_t)2 * CNNUE_RN_BLOCKS * C, 0.02);
+  fill(policy_conv_w, 2 * C, std::sqrt(2.0 / C));
+  fill(policy_conv_b, 2, 0.02);
+  fill(policy_fc_w, (size_t)CNNUE_RN_MOVES * 180, std::sqrt(1.0 / 180));
+  fill(policy_fc_b, CNNUE_RN_MOVES, 0.02);
+  fill(value_conv_w, C, std::sqrt(2.0 / C));
+  fill(value_conv_b, 1, 0.02);
+  fill(value_fc1_w, (size_t)256 * 90, std::sqrt(1.0 / 90));
+  fill(value_fc1_b, 256, 0.02);
+  fill(value_fc2_w, 256, std::sqrt(1.0 / 256));
+  fill(value_fc2_b, 1, 0.02);
+  return CNNUE_OK;
+}
+
+int cnnue_synth_rn_planes(uint64_t seed, int64_t batch, uint16_t* planes) {
+  if (batch < 0 || (batch > 0 && !planes)) return CNNUE_ERR_INVALID_ARG;
+  std::memset(planes, 0, sizeof(uint16_t) * (size_t)batch * CNNUE_RN_PLANES * 90);
+  Rng rng{seed};
+  const uint16_t one = 0x3f80;  // bf16 1.0
+  for (int64_t b = 0; b < batch; ++b) {
+    uint16_t* pl = planes + (size_t)b * CNNUE_RN_PLANES * 90;
+    bool used[90] = {};
+    const uint32_t k = rng.below(33);
+    for (uint32_t i = 0; i < k; ++i) {
+      uint32_t sq = rng.below(90);
+      while (used[sq]) sq = (sq + 1) % 90;
+      used[sq] = true;
+      pl[rng.below(14) * 90 + sq] = one;
+    }
+    if (rng.below(2))
+      for (int sq = 0; sq < 90; ++sq) pl[14 * 90 + sq] = one;
+  }
   return CNNUE_OK;
 }
 

@@ -451,6 +451,50 @@ int cnnue_az_policy_transition(const cnnue_az_model* model, const int16_t* d_par
                                int64_t n_lists, int16_t* d_child, void* d_workspace,
                                size_t workspace_bytes, void* stream);
 
+/* ---- AlphaZero policy/value ResNet for MCTS leaf batches ---------------- */
+/* No counterpart in the reference's code (its evaluator is the AZ-NNUE
+ * above); this is the dense network of the workload specification, evaluated
+ * where the reference evaluates leaves (AzNnue::evaluate_with_scratch_output,
+ * src/az.rs:1562-1604; MCTS leaf batches, src/az/alphazero.rs:388-521).
+ * Input planes bf16 [B][15][10][9]: 14 piece planes and a side-to-move plane.
+ * Trunk: conv 3x3 15->128 + bias, ReLU; 10 residual blocks h = ReLU(conv1(x)
+ * + b1), x = ReLU(conv2(h) + b2 + x) (BN folded into weights and biases);
+ * activations stored as bf16 after every layer, sums in fp32 on the tensor
+ * cores.  Policy: ReLU(conv1x1 128->2 + b), flattened channel-major (c * 90 +
+ * square), FC 180->2086, softmax.  Value: ReLU(conv1x1 128->1 + b), FC
+ * 90->256 + ReLU, FC 256->1, tanh.  Heads in fp32. */
+#define CNNUE_RN_PLANES 15
+#define CNNUE_RN_CHANNELS 128
+#define CNNUE_RN_BLOCKS 10
+#define CNNUE_RN_MOVES 2086
+typedef struct cnnue_rn_weights {   /* host fp32, PyTorch layouts; conv weights
+                                       are rounded to bf16 on upload */
+  const float* stem_w;         /* [128][15][3][3]            */
+  const float* stem_b;         /* [128]                      */
+  const float* block_w;        /* [10][2][128][128][3][3]    */
+  const float* block_b;        /* [10][2][128]               */
+  const float* policy_conv_w;  /* [2][128]                   */
+  const float* policy_conv_b;  /* [2]                        */
+  const float* policy_fc_w;    /* [2086][180]                */
+  const float* policy_fc_b;    /* [2086]                     */
+  const float* value_conv_w;   /* [128]                      */
+  const float* value_conv_b;   /* [1]                        */
+  const float* value_fc1_w;    /* [256][90]                  */
+  const float* value_fc1_b;    /* [256]                      */
+  const float* value_fc2_w;    /* [256]                      */
+  const float* value_fc2_b;    /* [1]                        */
+} cnnue_rn_weights;
+typedef struct cnnue_rn_model cnnue_rn_model;
+int cnnue_rn_model_create(const cnnue_rn_weights* weights, int device, cnnue_rn_model** out);
+int cnnue_rn_model_destroy(cnnue_rn_model* model);
+size_t cnnue_rn_workspace_bytes(int64_t batch);
+/* d_planes bf16 bits [B][15][90]; writes d_probs [B][2086] (softmax),
+ * d_logits [B][2086] (may be NULL) and d_value [B] (tanh).  A bounded wait
+ * that gives up is reported through the workspace status word. */
+int cnnue_rn_forward(const cnnue_rn_model* model, const uint16_t* d_planes, int64_t batch, float* d_probs,
+                     float* d_logits, float* d_value, void* d_workspace, size_t workspace_bytes,
+                     void* stream);
+
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is
  * replaced by the mixed output at every draw. */
@@ -478,6 +522,20 @@ int cnnue_synth_f_weights(uint64_t seed, float* ft_weight, float* ft_bias, float
  * perspective 1-2 removed and 1-3 added indices, or with probability 1/20 a
  * refresh with 2-32 fresh unique sorted indices; child perspective-0 count.
  * Capacities: h_rem 4n, h_add 64n. */
+/* ResNet weights (sizes of cnnue_rn_weights, writable arrays): conv weights
+ * He-normal N(0, sqrt(2 / fan_in)), the second conv of each block scaled by
+ * 1/4 (a small residual branch keeps activations bounded through 10 blocks),
+ * conv biases N(0, 0.02), FC weights N(0, sqrt(1 / fan_in)), FC biases
+ * N(0, 0.02); every value rounded to a bf16 value. */
+int cnnue_synth_rn_weights(uint64_t seed, float* stem_w, float* stem_b, float* block_w, float* block_b,
+                           float* policy_conv_w, float* policy_conv_b, float* policy_fc_w,
+                           float* policy_fc_b, float* value_conv_w, float* value_conv_b,
+                           float* value_fc1_w, float* value_fc1_b, float* value_fc2_w,
+                           float* value_fc2_b);
+/* Input planes bf16 bits [B][15][90]: per board k uniform in [0,32] pieces on
+ * distinct squares, each of a kind uniform over the 14 piece planes; plane 14
+ * all ones with probability 1/2 (side to move). */
+int cnnue_synth_rn_planes(uint64_t seed, int64_t batch, uint16_t* planes);
 int cnnue_synth_q_update(uint64_t seed, int64_t n_positions, int16_t* h_parent, uint8_t* h_flags,
                          uint16_t* h_rem, uint32_t* h_rem_offsets, uint32_t* n_rem,
                          uint16_t* h_add, uint32_t* h_add_offsets, uint32_t* n_add,

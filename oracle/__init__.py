@@ -330,3 +330,23 @@ def az_policy_transition(feature_q, parent, delta, refresh, items, offsets):
                                             _p(np.ascontiguousarray(refresh, np.uint8)), _p(it),
                                             _p(np.ascontiguousarray(offsets, np.uint32)), n_lists, _p(child))
     return st, child[:n_lists]
+
+
+def rn_forward(weights, planes_bits: np.ndarray, with_trunk: bool = False):
+    """ResNet forward restated on the CPU: (logits, probs, value_pre, value, trunk|None)."""
+    h = lib()
+    if not getattr(h, "_rn_ready", False):
+        h.oracle_rn_forward.argtypes = [C.c_void_p] * 15 + [C.c_int64] + [C.c_void_p] * 5
+        h.oracle_rn_forward.restype = None
+        h._rn_ready = True
+    B = planes_bits.shape[0]
+    planes = np.ascontiguousarray((planes_bits.astype(np.uint32) << 16).view(np.float32).reshape(B, 15, 90))
+    arrs = weights.arrays()
+    logits = np.zeros((max(B, 1), 2086), np.float32)
+    probs = np.zeros((max(B, 1), 2086), np.float32)
+    vpre = np.zeros(max(B, 1), np.float32)
+    value = np.zeros(max(B, 1), np.float32)
+    trunk = np.zeros((max(B, 1), 128, 90), np.float32) if with_trunk else None
+    h.oracle_rn_forward(*[_p(a) for a in arrs], _p(planes), B, _p(logits), _p(probs), _p(vpre), _p(value),
+                        _p(trunk) if with_trunk else None)
+    return logits[:B], probs[:B], vpre[:B], value[:B], (trunk[:B] if with_trunk else None)

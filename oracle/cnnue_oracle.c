@@ -983,3 +983,102 @@ int oracle_az_policy_transition(const int8_t* feature_q, const int16_t* parent, 
   }
   return status;
 }
+
+/* ---- C5: AlphaZero policy/value ResNet (workload specification) -------- */
+/* Conventions (the specification leaves them open; the CUDA path follows
+ * them): planes [B][15][10][9] (14 piece planes + side to move); stem conv
+ * 3x3 15->128, pad 1, + bias, ReLU; 10 blocks h = ReLU(conv1(x) + b1),
+ * x = ReLU(conv2(h) + b2 + x); policy head p = ReLU(conv1x1(x, 128->2) + b)
+ * flattened channel-major (c * 90 + square) -> FC 180 -> 2086 logits ->
+ * softmax; value head v = ReLU(conv1x1(x, 128->1) + b) -> FC 90 -> 256 + ReLU
+ * -> FC 256 -> 1 -> tanh.  Weights are bf16 values (BN folded into conv
+ * weights and biases); every trunk activation is rounded to bf16 after its
+ * layer (the stored dtype), sums are fp32; the heads run in fp32 on the bf16
+ * trunk output.  Conv weights OIHW: w[o][c][kh][kw]. */
+#define RN_C 128
+#define RN_SQ 90
+#define RN_MOVES 2086
+
+static void rn_conv3(const float* in, int cin, const float* w, const float* b, const float* resid, float* out) {
+  for (int o = 0; o < RN_C; ++o)
+    for (int p = 0; p < RN_SQ; ++p) {
+      const int r = p / 9, f = p % 9;
+      float s = 0.f;
+      for (int c = 0; c < cin; ++c)
+        for (int kh = 0; kh < 3; ++kh) {
+          const int rr = r + kh - 1;
+          if (rr < 0 || rr > 9) continue;
+          for (int kw = 0; kw < 3; ++kw) {
+            const int ff = f + kw - 1;
+            if (ff < 0 || ff > 8) continue;
+            s += in[c * RN_SQ + rr * 9 + ff] * w[((o * cin + c) * 3 + kh) * 3 + kw];
+          }
+        }
+      s += b[o];
+      if (resid) s += resid[o * RN_SQ + p];
+      out[o * RN_SQ + p] = bf16_round(s > 0.f ? s : 0.f);
+    }
+}
+
+void oracle_rn_forward(const float* stem_w, const float* stem_b, const float* block_w, const float* block_b,
+                       const float* pcw, const float* pcb, const float* pfw, const float* pfb, const float* vcw,
+                       const float* vcb, const float* v1w, const float* v1b, const float* v2w, const float* v2b,
+                       const float* planes, int64_t batch, float* logits, float* probs, float* value_pre,
+                       float* value, float* trunk) {
+#pragma omp parallel for schedule(dynamic, 1)
+  for (int64_t bi = 0; bi < batch; ++bi) {
+    float* x = (float*)malloc(sizeof(float) * RN_C * RN_SQ);
+    float* h = (float*)malloc(sizeof(float) * RN_C * RN_SQ);
+    float* y = (float*)malloc(sizeof(float) * RN_C * RN_SQ);
+    rn_conv3(planes + bi * 15 * RN_SQ, 15, stem_w, stem_b, NULL, x);
+    for (int blk = 0; blk < 10; ++blk) {
+      const float* w1 = block_w + (size_t)(2 * blk) * RN_C * RN_C * 9;
+      const float* w2 = block_w + (size_t)(2 * blk + 1) * RN_C * RN_C * 9;
+      rn_conv3(x, RN_C, w1, block_b + (2 * blk) * RN_C, NULL, h);
+      rn_conv3(h, RN_C, w2, block_b + (2 * blk + 1) * RN_C, x, y);
+      float* t = x;
+      x = y;
+      y = t;
+    }
+    if (trunk) memcpy(trunk + bi * RN_C * RN_SQ, x, sizeof(float) * RN_C * RN_SQ);
+    float pc[2 * RN_SQ], vc[RN_SQ], hid[256];
+    for (int o = 0; o < 2; ++o)
+      for (int p = 0; p < RN_SQ; ++p) {
+        float s = 0.f;
+        for (int c = 0; c < RN_C; ++c) s += x[c * RN_SQ + p] * pcw[o * RN_C + c];
+        s += pcb[o];
+        pc[o * RN_SQ + p] = s > 0.f ? s : 0.f;
+      }
+    for (int p = 0; p < RN_SQ; ++p) {
+      float s = 0.f;
+      for (int c = 0; c < RN_C; ++c) s += x[c * RN_SQ + p] * vcw[c];
+      s += vcb[0];
+      vc[p] = s > 0.f ? s : 0.f;
+    }
+    float* lg = logits + bi * RN_MOVES;
+    float mx = -INFINITY;
+    for (int j = 0; j < RN_MOVES; ++j) {
+      float s = 0.f;
+      for (int k = 0; k < 2 * RN_SQ; ++k) s += pc[k] * pfw[j * 2 * RN_SQ + k];
+      lg[j] = s + pfb[j];
+      if (lg[j] > mx) mx = lg[j];
+    }
+    double sum = 0.0;
+    for (int j = 0; j < RN_MOVES; ++j) sum += exp((double)(lg[j] - mx));
+    for (int j = 0; j < RN_MOVES; ++j) probs[bi * RN_MOVES + j] = (float)(exp((double)(lg[j] - mx)) / sum);
+    for (int i = 0; i < 256; ++i) {
+      float s = 0.f;
+      for (int p = 0; p < RN_SQ; ++p) s += vc[p] * v1w[i * RN_SQ + p];
+      s += v1b[i];
+      hid[i] = s > 0.f ? s : 0.f;
+    }
+    float s = 0.f;
+    for (int i = 0; i < 256; ++i) s += hid[i] * v2w[i];
+    s += v2b[0];
+    value_pre[bi] = s;
+    value[bi] = tanhf(s);
+    free(x);
+    free(h);
+    free(y);
+  }
+}

@@ -434,6 +434,251 @@ def run_train(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# ResNet policy/value inference (--workload resnet; not the headline line)
+# ---------------------------------------------------------------------------
+RN_BATCH = 1024
+RN_FLOPS_PER_BOARD = (90 * 128 * 135 * 2 + 20 * 90 * 128 * 1152 * 2 + 2 * 180 * 2086 + 90 * 128 * 3 * 2
+                      + 2 * 90 * 256 + 2 * 256)
+
+
+def measured_bf16_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d.get("bf16_tflops")), "measured"
+    except Exception:
+        return 1590.0, "fallback"
+
+
+def _device_loop(step, steps, dev, stream):
+    """Events around each step on `stream`; returns the summed milliseconds."""
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for a, b in evs:
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    return sum(a.elapsed_time(b) for a, b in evs)
+
+
+def run_resnet(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    from chineseai_b200 import resnet
+
+    w = resnet.ResNetWeights.synthetic(5)
+    model = resnet.ResNetModel(w, device=local)
+    planes = resnet.synthetic_planes(RN_BATCH, 6 + rank)
+    d_planes = torch.from_numpy(planes.view(np.int16)).to(dev)
+    h_planes = torch.from_numpy(planes.view(np.int16)).pin_memory()
+    h_probs = torch.empty((RN_BATCH, resnet.MOVES), dtype=torch.float32).pin_memory()
+    h_value = torch.empty(RN_BATCH, dtype=torch.float32).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step():
+        model.forward(d_planes)
+
+    def step_e2e():
+        d_planes.copy_(h_planes, non_blocking=True)
+        probs, _, value = model.forward(d_planes)
+        h_probs.copy_(probs, non_blocking=True)
+        h_value.copy_(value, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+        step_e2e()
+    torch.cuda.synchronize(dev)
+    if model.read_status() != 0:
+        raise RuntimeError("resnet kernels reported a timeout")
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    total = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        total += _device_loop(step, 1, dev, stream)
+    clocks = sampler.stop()
+    e2e_total = _device_loop(step_e2e, args.steps, dev, stream)
+    stats = torch.tensor([total, e2e_total], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, e2e_total = stats.tolist()
+    if rank == 0:
+        ms = total / args.steps
+        peak, peak_kind = measured_bf16_peak()
+        achieved = RN_FLOPS_PER_BOARD * RN_BATCH / (ms / 1e3) / 1e12
+        line = {
+            "metric": "AlphaZero ResNet leaf evaluations/sec (policy 2086 + value, batch 1024)",
+            "value": world * RN_BATCH / (ms / 1e3), "unit": "boards/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": "ResNet 10x128 (stem 3x3 15->128, 10 residual blocks), policy FC 180->2086 + "
+                                   "softmax, value 90->256->1 tanh; input bf16 [1024][15][10][9]",
+                       "batch_per_gpu": RN_BATCH, "parallelism": f"replicas{world}",
+                       "l2": "flushed (256 MiB write) before each timed step"},
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "scope": "whole forward (21 tcgen05 convs + heads), algorithmic FLOPs"},
+            "e2e": {"value": world * RN_BATCH / (e2e_total / args.steps / 1e3), "unit": "boards/s",
+                    "h2d_bytes_per_step": planes.nbytes,
+                    "d2h_bytes_per_step": RN_BATCH * resnet.MOVES * 4 + RN_BATCH * 4},
+            "clocks": clocks, "gpu_launches": 26 * args.steps,
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            sample = 8
+            t0 = time.time()
+            reps = 0
+            while time.time() - t0 < min(args.cpu_seconds, 10.0) or reps == 0:
+                oracle.rn_forward(w, planes[:sample])
+                reps += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": reps * sample / el, "unit": "boards/s", "cores": cpu_threads(),
+                                    "kind": "port", "sample": f"{reps} x {sample} boards of the same batch"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# Reference-native AZ-NNUE evaluation (--workload az; not the headline line)
+# ---------------------------------------------------------------------------
+AZ_POSITIONS = 65536
+
+
+def run_az(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    from chineseai_b200 import az
+    from chineseai_b200.quantized import as_device
+
+    w = az.AzWeights.random(128, 20260807)
+    model = az.AzModel(w, device=local)
+    base = az.random_boards(4096, seed=1 + rank, keep=0.9)
+    reps = AZ_POSITIONS // len(base)
+    items0, offsets0 = az.node_lists(base)
+    lens = np.diff(offsets0)
+    items = np.tile(items0, reps)
+    offsets = np.concatenate([[0], np.cumsum(np.tile(lens, reps))]).astype(np.uint32)
+    side = np.tile((np.arange(len(base)) % 2).astype(np.uint8), reps)
+    d_items, d_off, d_side = as_device(items, dev), as_device(offsets, dev), as_device(side, dev)
+    acc = torch.empty((2 * AZ_POSITIONS, 128), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    h_items = torch.from_numpy(items.view(np.int32)).pin_memory()
+    h_off = torch.from_numpy(offsets.view(np.int32)).pin_memory()
+    h_wdl = torch.empty((AZ_POSITIONS, 3), dtype=torch.float32).pin_memory()
+    h_q = torch.empty(AZ_POSITIONS, dtype=torch.float32).pin_memory()
+
+    def step():
+        model.refresh(d_items, d_off, out=acc)
+        return model.value(acc, side=d_side)
+
+    def step_e2e():
+        d_items.copy_(h_items, non_blocking=True)
+        d_off.copy_(h_off, non_blocking=True)
+        wdl, q = step()
+        h_wdl.copy_(wdl, non_blocking=True)
+        h_q.copy_(q, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step()
+        step_e2e()
+    torch.cuda.synchronize(dev)
+    if model.read_status() != 0:
+        raise RuntimeError("az kernels reported bad input")
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    total = refresh_ms = 0.0
+    for _ in range(args.steps):
+        flush.zero_()
+        refresh_ms += _device_loop(lambda: model.refresh(d_items, d_off, out=acc), 1, dev, stream)
+        flush.zero_()
+        total += _device_loop(step, 1, dev, stream)
+    clocks = sampler.stop()
+    e2e_total = _device_loop(step_e2e, args.steps, dev, stream)
+    stats = torch.tensor([total, e2e_total, refresh_ms], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, e2e_total, refresh_ms = stats.tolist()
+    if rank == 0:
+        ms = total / args.steps
+        r_ms = refresh_ms / args.steps
+        n_items = len(items)
+        alg = (2 * AZ_POSITIONS + 6 * n_items) * 128 * 4 + n_items * 4 + offsets.nbytes + 2 * AZ_POSITIONS * 128 * 4
+        peak, peak_kind = measured_hbm_peak()
+        achieved = alg / (r_ms / 1e3) / 1e9
+        line = {
+            "metric": "AZ-NNUE evaluations/sec (trunk refresh of both perspectives + value head, H=128)",
+            "value": world * AZ_POSITIONS / (ms / 1e3), "unit": "positions/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "AzNnue::random(128, 20260807); 65,536 synthetic boards (~29 pieces), "
+                                   "refresh bit-identical to the reference, value head WDL",
+                       "batch_per_gpu": AZ_POSITIONS, "parallelism": f"replicas{world}",
+                       "l2": "flushed (256 MiB write) before each timed step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "scope": "az_list_kernel (refresh), algorithmic bytes; rows are L2-resident"},
+            "e2e": {"value": world * AZ_POSITIONS / (e2e_total / args.steps / 1e3), "unit": "positions/s",
+                    "h2d_bytes_per_step": items.nbytes + offsets.nbytes,
+                    "d2h_bytes_per_step": AZ_POSITIONS * 16},
+            "clocks": clocks, "gpu_launches": 2 * args.steps,
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            tensors = w.tensors()
+            sample = 4096
+            s_off = offsets[: 2 * sample + 1]
+            s_items = items[: s_off[-1]]
+            t0 = time.time()
+            n_rep = 0
+            while time.time() - t0 < min(args.cpu_seconds, 10.0) or n_rep == 0:
+                _, a = oracle.az_refresh(tensors, 128, s_items, s_off)
+                oracle.az_value(tensors, 128, a.reshape(sample, 2, 128)[np.arange(sample), side[:sample]])
+                n_rep += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": n_rep * sample / el, "unit": "positions/s", "cores": 1,
+                                    "kind": "port", "sample": f"{n_rep} x {sample} positions, single thread"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -442,8 +687,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["eval", "train"], default="eval",
-                    help="eval: the headline quantised forward; train: the data-parallel training step")
+    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az"], default="eval",
+                    help="eval: the headline quantised forward; train: the data-parallel training step; "
+                         "resnet: AlphaZero ResNet leaf batch; az: reference-native AZ-NNUE evaluation")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -451,6 +697,10 @@ def main():
         return run_reference(args)
     if args.workload == "train":
         return run_train(args)
+    if args.workload == "resnet":
+        return run_resnet(args)
+    if args.workload == "az":
+        return run_az(args)
     return run_ours(args)
 
 

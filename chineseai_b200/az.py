@@ -164,6 +164,21 @@ def features(board: np.ndarray, perspective: int) -> np.ndarray:
     return items[:n.value].copy()
 
 
+THREAT_VOCAB = 57702
+THREAT_MAX = 256
+
+
+def threat_features(board: np.ndarray, side: int) -> np.ndarray:
+    """Threat-table rows of the side to move (value_threat_index of every
+    attack on an occupied square, source-square order)."""
+    b = np.ascontiguousarray(board, np.int8)
+    out = np.zeros(THREAT_MAX, np.uint32)
+    n = C.c_int()
+    check(lib().cnnue_az_threat_features(b.ctypes.data, side, out.ctypes.data, C.byref(n)),
+          "cnnue_az_threat_features")
+    return out[:n.value].copy()
+
+
 @dataclass
 class MoveItems:
     refresh: bool
@@ -332,6 +347,18 @@ class AzModel:
                                                self._ptr(items) if n_items else None, n_items, self._ptr(offsets),
                                                n_lists, out.data_ptr(), self._ws.data_ptr(), self._ws.numel(),
                                                self._stream(stream)), "cnnue_az_policy_transition")
+        return out
+
+    def threat_logits(self, features, offsets, out=None, stream=None):
+        """Threat logits [n][3] from CSR threat features (device uint32)."""
+        torch = self._torch
+        n = offsets.numel() - 1
+        if out is None:
+            out = torch.empty((n, 3), dtype=torch.float32, device=self.device)
+        check(lib().cnnue_az_threat_logits(self._h, self._ptr(features) if features.numel() else None,
+                                           features.numel(), offsets.data_ptr(), n, out.data_ptr(),
+                                           self._ws.data_ptr(), self._ws.numel(), self._stream(stream)),
+              "cnnue_az_threat_logits")
         return out
 
     def value(self, acc, side=None, rule=None, threat=None, stream=None):

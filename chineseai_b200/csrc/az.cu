@@ -33,6 +33,9 @@ struct cnnue_az_model {
   float* head_b = nullptr;  // [96]
   float* head_o = nullptr;  // [3][96]
   int8_t* policy_q = nullptr;  // quantised policy feature rows [1546][32]
+  int8_t* threat_q = nullptr;  // quantised threat embedding [57702][64]
+  float* threat_out = nullptr; // value_threat_output [3][128]
+  float threat_scale = 1.f;
 };
 
 namespace cnnue {
@@ -505,6 +508,71 @@ int launch_policy(const PolicyArgs& a, cudaStream_t s) {
   return check_launch_error(kTransition ? "az_policy_kernel<transition>" : "az_policy_kernel<refresh>");
 }
 
+// ---- threat logits (value_threat_logits, src/az.rs:2078-2120) -------------
+// One warp per position: lane l owns threat ranks 2l, 2l+1 as one word of an
+// int16 pair; each feature row (64 int8) is widened and added with wrapping
+// (__vadd2, as the reference's epi16 adds), which makes the sum independent
+// of the feature order.  Then act = clamp(acc * scale, 0, 1) and act^2 go to
+// shared memory and lanes 0-2 form the three logits with the reference's
+// x86-64 AVX2/FMA dot-product order (four 8-lane fused accumulators over
+// 32-element chunks, lanes combined (a0 + a1) + (a2 + a3), then summed).
+constexpr int kThreatWarps = 8;
+
+__global__ void __launch_bounds__(kThreatWarps * 32) az_threat_kernel(
+    const int8_t* __restrict__ table, float scale, const float* __restrict__ out_w,
+    const uint32_t* __restrict__ features, uint32_t n_features, const uint32_t* __restrict__ offsets, int64_t n,
+    float* __restrict__ logits, WorkspaceHeader* hdr) {
+  __shared__ float act[kThreatWarps][2 * CNNUE_AZ_THREAT_RANK];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t status = 0;
+  for (int64_t p = (int64_t)blockIdx.x * kThreatWarps + warp; p < n; p += (int64_t)gridDim.x * kThreatWarps) {
+    const uint32_t beg = offsets[p], end = offsets[p + 1];
+    uint32_t acc = 0;
+    if (beg <= end && end <= n_features) {
+      for (uint32_t i = beg; i < end; ++i) {
+        const uint32_t f = features[i];
+        if (f >= (uint32_t)CNNUE_AZ_THREAT_VOCAB) {
+          status |= CNNUE_STATUS_BAD_INDEX;
+          continue;
+        }
+        const uint16_t two = __ldg(reinterpret_cast<const uint16_t*>(table + (size_t)f * CNNUE_AZ_THREAT_RANK) + lane);
+        acc = __vadd2(acc, widen2(two));
+      }
+    } else {
+      status |= CNNUE_STATUS_BAD_OFFSETS;
+    }
+    const float x0 = fminf(fmaxf(__fmul_rn((float)(int16_t)(acc & 0xffffu), scale), 0.f), 1.f);
+    const float x1 = fminf(fmaxf(__fmul_rn((float)(int16_t)(acc >> 16), scale), 0.f), 1.f);
+    float* a = act[warp];
+    a[2 * lane] = x0;
+    a[2 * lane + 1] = x1;
+    a[CNNUE_AZ_THREAT_RANK + 2 * lane] = __fmul_rn(x0, x0);
+    a[CNNUE_AZ_THREAT_RANK + 2 * lane + 1] = __fmul_rn(x1, x1);
+    __syncwarp();
+    if (lane < 3) {
+      const float* w = out_w + lane * 2 * CNNUE_AZ_THREAT_RANK;
+      float part[4][8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 8; ++k) part[q][k] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) part[q][k] = fmaf(a[c * 32 + q * 8 + k], __ldg(w + c * 32 + q * 8 + k), part[q][k]);
+      float sum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) sum = __fadd_rn(sum, __fadd_rn(__fadd_rn(part[0][k], part[1][k]), __fadd_rn(part[2][k], part[3][k])));
+      logits[p * 3 + lane] = sum;
+    }
+    __syncwarp();
+  }
+  status = __reduce_or_sync(kFull, status);
+  if (lane == 0 && status) atomicOr(&hdr->status, status);
+}
+
 // The float4 column path needs 16-byte aligned accumulator rows.
 int check_rows_aligned(int64_t H, const void* a, const char* what) {
   if (H % 4 == 0 && ((uintptr_t)a & 15u) != 0)
@@ -537,13 +605,18 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
                small = align_up(sizeof(float) * kHead, 256), out3 = align_up(sizeof(float) * 3 * kHead, 256);
   const size_t staging = align_up(sizeof(float) * kHead * H, 256);
   const size_t policy = align_up((size_t)CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK, 256);
+  const size_t threat = align_up((size_t)CNNUE_AZ_THREAT_VOCAB * CNNUE_AZ_THREAT_RANK, 256);
+  const size_t threat_out = align_up(sizeof(float) * 3 * 2 * CNNUE_AZ_THREAT_RANK, 256);
+  if (w->q8[3].size() != (size_t)CNNUE_AZ_THREAT_VOCAB * CNNUE_AZ_THREAT_RANK)
+    return set_error(CNNUE_ERR_INVALID_ARG, "weights have no quantised threat table (run cnnue_az_quantize)");
   if (w->q8[0].size() != (size_t)CNNUE_AZ_POLICY_ROWS * CNNUE_AZ_POLICY_RANK)
     return set_error(CNNUE_ERR_INVALID_ARG, "weights have no quantised policy table (run cnnue_az_quantize)");
   auto* m = new (std::nothrow) cnnue_az_model;
   if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
   m->device = device;
   m->hidden = H;
-  cudaError_t e = cudaMalloc(&m->blob, trunk + vecH + rule + head + small + out3 + policy + staging);
+  cudaError_t e =
+      cudaMalloc(&m->blob, trunk + vecH + rule + head + small + out3 + policy + threat + threat_out + staging);
   if (e != cudaSuccess) {
     delete m;
     return cuda_error(e, "cudaMalloc(az model)");
@@ -556,7 +629,10 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
   m->head_b = (float*)(p += head);
   m->head_o = (float*)(p += small);
   m->policy_q = (int8_t*)(p += out3);
-  float* stage = (float*)(p += policy);
+  m->threat_q = (int8_t*)(p += policy);
+  m->threat_out = (float*)(p += threat);
+  m->threat_scale = w->scale[3];
+  float* stage = (float*)(p += threat_out);
   using namespace cnnue::az;
   const int tables[5] = {kInputHidden, kInputPiece, kInputRank, kInputFile, kInputKingPiece};
   const int rows[5] = {1260, 14, 10, 9, 252};
@@ -584,6 +660,11 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
     const cudaError_t ce = cudaMemcpy(m->policy_q, w->q8[0].data(), w->q8[0].size(), cudaMemcpyHostToDevice);
     if (ce != cudaSuccess) st = cuda_error(ce, "policy table");
   }
+  if (!st) {
+    const cudaError_t ce = cudaMemcpy(m->threat_q, w->q8[3].data(), w->q8[3].size(), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) st = cuda_error(ce, "threat table");
+  }
+  copy(m->threat_out, w->t[11], 3 * 2 * CNNUE_AZ_THREAT_RANK, "value_threat_output");
   if (!st) {
     const int64_t n = (int64_t)kHead * H;
     transpose_head_kernel<<<(unsigned)((n + 255) / 256), 256>>>(stage, (int)H, m->head_t);
@@ -761,6 +842,25 @@ int cnnue_az_policy_transition(const cnnue_az_model* m, const int16_t* d_parent,
   a.out = d_child;
   a.hdr = (WorkspaceHeader*)ws;
   return launch_policy<true>(a, s);
+}
+
+int cnnue_az_threat_logits(const cnnue_az_model* m, const uint32_t* d_features, uint32_t n_features,
+                           const uint32_t* d_offsets, int64_t n, float* d_logits, void* ws, size_t ws_bytes,
+                           void* stream) {
+  if (!m || !ws || n < 0 || (n > 0 && (!d_offsets || !d_logits)) || (n_features > 0 && !d_features))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, offsets, features or logits, or n < 0");
+  if (ws_bytes < sizeof(WorkspaceHeader))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu", ws_bytes, sizeof(WorkspaceHeader));
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n == 0) return CNNUE_OK;
+  const int64_t want = (n + kThreatWarps - 1) / kThreatWarps;
+  const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+  az_threat_kernel<<<blocks, kThreatWarps * 32, 0, s>>>(m->threat_q, m->threat_scale, m->threat_out, d_features,
+                                                        n_features, d_offsets, n, d_logits, (WorkspaceHeader*)ws);
+  return check_launch_error("az_threat_kernel");
 }
 
 }  // extern "C"

@@ -527,9 +527,210 @@ int quantize(cnnue_az_weights& w) {
   return CNNUE_OK;
 }
 
+// ---- threat features (src/az.rs:577-742; src/xiangqi/mod.rs:286-389) -------
+constexpr int kPieces = 14;
+
+// threat_reachable_square (src/az.rs:663-697), canonical coordinates: own
+// pieces (index < 7) live at the high ranks.
+bool threat_reachable(int piece, int square) {
+  const int rank = square / 9, file = square % 9;
+  const bool ours = piece < 7;
+  switch (piece % 7) {
+    case 0: return file >= 3 && file <= 5 && (ours ? rank >= 7 : rank <= 2);
+    case 1:
+      return ours ? ((rank == 7 || rank == 9) && (file == 3 || file == 5)) || (rank == 8 && file == 4)
+                  : ((rank == 0 || rank == 2) && (file == 3 || file == 5)) || (rank == 1 && file == 4);
+    case 2:
+      return ours ? (rank == 5 && (file == 2 || file == 6)) || (rank == 7 && (file == 0 || file == 4 || file == 8)) ||
+                        (rank == 9 && (file == 2 || file == 6))
+                  : (rank == 0 && (file == 2 || file == 6)) || (rank == 2 && (file == 0 || file == 4 || file == 8)) ||
+                        (rank == 4 && (file == 2 || file == 6));
+    case 6:
+      return ours ? rank <= 4 || ((rank == 5 || rank == 6) && file % 2 == 0)
+                  : rank >= 5 || ((rank == 3 || rank == 4) && file % 2 == 0);
+    default: return true;
+  }
+}
+
+struct ThreatMap {
+  std::vector<uint32_t> relation;  // [14][90][90] -> first slot, or UINT32_MAX
+  uint8_t attacked[90][kPieces];   // slot offset of the attacked piece, 255 = impossible
+  uint32_t vocab = 0;
+};
+
+// threat_relation_map and threat_attacked_offsets (src/az.rs:577-716): the
+// (attacker, source, target) relations a piece could ever have, in attacker,
+// source, target order, each followed by one slot per piece that can stand on
+// the target.
+const ThreatMap& threat_map() {
+  static const ThreatMap map = [] {
+    ThreatMap m;
+    m.relation.assign((size_t)kPieces * kSq * kSq, UINT32_MAX);
+    uint32_t next = 0;
+    for (int attacker = 0; attacker < kPieces; ++attacker) {
+      const bool ours = attacker < 7;
+      const int kind = attacker % 7;
+      for (int source = 0; source < kSq; ++source) {
+        if (!threat_reachable(attacker, source)) continue;
+        const int rank = source / 9, file = source % 9;
+        int targets[18], n = 0;
+        if (kind == 4 || kind == 5) {
+          for (int t = 0; t < kSq; ++t)
+            if (t != source && (t / 9 == rank || t % 9 == file)) targets[n++] = t;
+        } else {
+          static const int general[4][2] = {{0, -1}, {0, 1}, {-1, 0}, {1, 0}};
+          static const int advisor[4][2] = {{-1, -1}, {1, -1}, {-1, 1}, {1, 1}};
+          static const int elephant[4][2] = {{-2, -2}, {2, -2}, {-2, 2}, {2, 2}};
+          static const int horse[8][2] = {{-1, -2}, {1, -2}, {-1, 2}, {1, 2}, {-2, -1}, {-2, 1}, {2, -1}, {2, 1}};
+          static const int soldier_home_ours[1][2] = {{0, -1}};
+          static const int soldier_home_theirs[1][2] = {{0, 1}};
+          static const int soldier_across_ours[3][2] = {{0, -1}, {-1, 0}, {1, 0}};
+          static const int soldier_across_theirs[3][2] = {{0, 1}, {-1, 0}, {1, 0}};
+          const int(*steps)[2] = nullptr;
+          int ns = 0;
+          switch (kind) {
+            case 0: steps = general; ns = 4; break;
+            case 1: steps = advisor; ns = 4; break;
+            case 2: steps = elephant; ns = 4; break;
+            case 3: steps = horse; ns = 8; break;
+            default:
+              if (ours && rank <= 4) { steps = soldier_across_ours; ns = 3; }
+              else if (!ours && rank >= 5) { steps = soldier_across_theirs; ns = 3; }
+              else if (ours) { steps = soldier_home_ours; ns = 1; }
+              else { steps = soldier_home_theirs; ns = 1; }
+          }
+          for (int i = 0; i < ns; ++i) {
+            const int tf = file + steps[i][0], tr = rank + steps[i][1];
+            if (tf < 0 || tf > 8 || tr < 0 || tr > 9) continue;
+            if ((kind == 0 || kind == 1) && (tf < 3 || tf > 5 || (ours ? tr < 7 : tr > 2))) continue;
+            if (kind == 2 && (ours ? tr < 5 : tr > 4)) continue;
+            targets[n++] = tr * 9 + tf;
+          }
+        }
+        for (int i = 0; i < n; ++i) {
+          m.relation[((size_t)attacker * kSq + source) * kSq + targets[i]] = next;
+          for (int piece = 0; piece < kPieces; ++piece) next += threat_reachable(piece, targets[i]) ? 1 : 0;
+        }
+      }
+    }
+    for (int sq = 0; sq < kSq; ++sq) {
+      uint8_t k = 0;
+      for (int piece = 0; piece < kPieces; ++piece) m.attacked[sq][piece] = threat_reachable(piece, sq) ? k++ : 255;
+    }
+    m.vocab = next;
+    return m;
+  }();
+  return map;
+}
+
+// value_threat_index (src/az.rs:718-742).
+uint32_t threat_index(int perspective, int source, int attacker_code, int target, int attacked_code) {
+  const ThreatMap& m = threat_map();
+  auto piece_index = [&](int code) {
+    const int color = code > 0 ? 0 : 1, kind = (code > 0 ? code : -code) - 1;
+    return (color == perspective ? 0 : 7) + kind;
+  };
+  const int a = piece_index(attacker_code), v = piece_index(attacked_code);
+  const int cs = canonical_square(perspective, source), ct = canonical_square(perspective, target);
+  const uint32_t base = m.relation[((size_t)a * kSq + cs) * kSq + ct];
+  if (base == UINT32_MAX) return UINT32_MAX;
+  const uint8_t off = m.attacked[ct][v];
+  if (off == 255) return UINT32_MAX;
+  return base + off;
+}
+
+// Position::visit_occupied_attacks (src/xiangqi/mod.rs:286-389): every piece
+// attacking an occupied square, sources in square order.
+template <class Visit>
+void visit_attacks(const int8_t* b, Visit&& visit) {
+  auto inside = [](int f, int r) { return f >= 0 && f < 9 && r >= 0 && r < 10; };
+  for (int source = 0; source < kSq; ++source) {
+    const int v = b[source];
+    if (v == 0) continue;
+    const int kind = (v > 0 ? v : -v) - 1;
+    const bool red = v > 0;
+    const int file = source % 9, rank = source / 9;
+    auto step = [&](int df, int dr) {
+      const int tf = file + df, tr = rank + dr;
+      if (inside(tf, tr) && b[tr * 9 + tf] != 0) visit(source, v, tr * 9 + tf, (int)b[tr * 9 + tf]);
+    };
+    auto in_palace = [&](int f, int r) { return f >= 3 && f <= 5 && (red ? r >= 7 : r <= 2); };
+    static const int ortho[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+    switch (kind) {
+      case 0:
+        for (auto& d : ortho)
+          if (inside(file + d[0], rank + d[1]) && in_palace(file + d[0], rank + d[1])) step(d[0], d[1]);
+        break;
+      case 1: {
+        static const int diag[4][2] = {{-1, -1}, {-1, 1}, {1, -1}, {1, 1}};
+        for (auto& d : diag)
+          if (inside(file + d[0], rank + d[1]) && in_palace(file + d[0], rank + d[1])) step(d[0], d[1]);
+        break;
+      }
+      case 2: {
+        static const int el[4][2] = {{-2, -2}, {-2, 2}, {2, -2}, {2, 2}};
+        for (auto& d : el) {
+          const int tf = file + d[0], tr = rank + d[1];
+          if (inside(tf, tr) && (red ? tr >= 5 : tr <= 4) && b[(rank + d[1] / 2) * 9 + file + d[0] / 2] == 0)
+            step(d[0], d[1]);
+        }
+        break;
+      }
+      case 3: {
+        static const int hs[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                     {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+        for (auto& h : hs)
+          if (inside(file + h[2], rank + h[3]) && inside(file + h[0], rank + h[1]) &&
+              b[(rank + h[1]) * 9 + file + h[0]] == 0)
+            step(h[2], h[3]);
+        break;
+      }
+      case 4:
+      case 5:
+        for (auto& d : ortho) {
+          int tf = file + d[0], tr = rank + d[1], occupied = 0;
+          while (inside(tf, tr)) {
+            const int t = tr * 9 + tf;
+            if (b[t] != 0) {
+              ++occupied;
+              if (kind == 4 || occupied == 2) {
+                visit(source, v, t, (int)b[t]);
+                break;
+              }
+            }
+            tf += d[0];
+            tr += d[1];
+          }
+        }
+        break;
+      default:
+        step(0, red ? -1 : 1);
+        if (red ? rank <= 4 : rank >= 5) {
+          step(-1, 0);
+          step(1, 0);
+        }
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int cnnue_az_threat_vocab(void) { return (int)threat_map().vocab; }
+
+int cnnue_az_threat_features(const int8_t* board, int perspective, uint32_t* features, int* count) {
+  if (!features || !count) return set_error(CNNUE_ERR_INVALID_ARG, "null features or count");
+  if (perspective != 0 && perspective != 1) return set_error(CNNUE_ERR_INVALID_ARG, "perspective %d", perspective);
+  if (int st = check_board(board)) return st;
+  int n = 0;
+  visit_attacks(board, [&](int source, int attacker, int target, int attacked) {
+    const uint32_t f = threat_index(perspective, source, attacker, target, attacked);
+    if (f != UINT32_MAX && n < CNNUE_AZ_THREAT_MAX) features[n++] = f;
+  });
+  *count = n;
+  return CNNUE_OK;
+}
 
 int cnnue_az_quantize(cnnue_az_weights* w) {
   if (!w) return set_error(CNNUE_ERR_INVALID_ARG, "null weights");

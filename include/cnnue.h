@@ -331,6 +331,20 @@ int cnnue_az_features(const int8_t* board, int perspective, uint32_t* items, int
 int cnnue_az_move_items(const int8_t* board, int from, int to, int perspective, uint32_t* delta,
                         uint8_t* refresh, uint32_t* items, int* count);
 
+/* Threat features of the side to move (value_threat_logits' accumulation,
+ * src/az.rs:2078-2101): for every piece attacking an occupied square
+ * (Position::visit_occupied_attacks, src/xiangqi/mod.rs:286-389, sources in
+ * square order) the index of value_threat_index (src/az.rs:718-742) into the
+ * 57,702-row threat table; relations outside threat_relation_map
+ * (src/az.rs:577-661) are skipped.  features holds CNNUE_AZ_THREAT_MAX. */
+#define CNNUE_AZ_THREAT_VOCAB 57702
+#define CNNUE_AZ_THREAT_RANK 64
+#define CNNUE_AZ_THREAT_MAX 256
+int cnnue_az_threat_features(const int8_t* board, int perspective, uint32_t* features, int* count);
+/* Size of the enumerated threat vocabulary (57,702 when the enumeration is
+ * the reference's; the reference asserts the same count). */
+int cnnue_az_threat_vocab(void);
+
 /* Host weights: the 22 fp32 tensors of az_weight_tensors! (src/az.rs:241-278)
  * in that order, row-major. */
 typedef struct cnnue_az_weights cnnue_az_weights;
@@ -432,6 +446,17 @@ int cnnue_az_transition(const cnnue_az_model* model, const float* d_parent, cons
 int cnnue_az_value(const cnnue_az_model* model, const float* d_acc, const uint8_t* d_side,
                    const float* d_rule, const float* d_threat, int64_t n, float* d_wdl, float* d_q,
                    void* stream);
+
+/* Threat logits [n][3] of n positions (value_threat_logits, src/az.rs:
+ * 2078-2120): acc[64] = wrapping int16 sum of the CNNUE_AZ_Q_VALUE_THREAT rows
+ * of the position's threat features (CSR: offsets[n+1] into d_features),
+ * act = clamp(acc * scale, 0, 1), logits = value_threat_output . (act ||
+ * act^2) in the reference's dot-product order: bit-identical.  Feed them to
+ * cnnue_az_value as d_threat when value_threat_active (else the reference
+ * adds zeros).  A feature >= 57,702 is skipped and flagged BAD_INDEX. */
+int cnnue_az_threat_logits(const cnnue_az_model* model, const uint32_t* d_features, uint32_t n_features,
+                           const uint32_t* d_offsets, int64_t n, float* d_logits, void* d_workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* int16 policy accumulators [n_lists][32] (quantized_policy_accumulator,
  * src/az.rs:2344-2365): the bias row, then for every item its 6 rows of the

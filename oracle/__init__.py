@@ -350,3 +350,36 @@ def rn_forward(weights, planes_bits: np.ndarray, with_trunk: bool = False):
     h.oracle_rn_forward(*[_p(a) for a in arrs], _p(planes), B, _p(logits), _p(probs), _p(vpre), _p(value),
                         _p(trunk) if with_trunk else None)
     return logits[:B], probs[:B], vpre[:B], value[:B], (trunk[:B] if with_trunk else None)
+
+
+def _azt():
+    h = _az()
+    if not getattr(h, "_azt_ready", False):
+        h.oracle_az_threat_vocab.restype = C.c_int
+        h.oracle_az_threat_features.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
+        h.oracle_az_threat_features.restype = C.c_int
+        h.oracle_az_threat_logits.argtypes = [C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
+                                              C.c_int64, C.c_void_p]
+        h.oracle_az_threat_logits.restype = C.c_int
+        h._azt_ready = True
+    return h
+
+
+def az_threat_vocab() -> int:
+    return _azt().oracle_az_threat_vocab()
+
+
+def az_threat_features(board: np.ndarray, side: int) -> np.ndarray:
+    out = np.zeros(256, np.uint32)
+    n = _azt().oracle_az_threat_features(_p(np.ascontiguousarray(board, np.int8)), side, _p(out))
+    return out[:n].copy()
+
+
+def az_threat_logits(table: np.ndarray, scale: float, out_w: np.ndarray, features: np.ndarray, offsets: np.ndarray):
+    n = len(offsets) - 1
+    logits = np.zeros((max(n, 1), 3), np.float32)
+    f = np.ascontiguousarray(features, np.uint32) if len(features) else np.zeros(1, np.uint32)
+    st = _azt().oracle_az_threat_logits(_p(np.ascontiguousarray(table, np.int8)), scale,
+                                        _p(np.ascontiguousarray(out_w, np.float32)), _p(f),
+                                        _p(np.ascontiguousarray(offsets, np.uint32)), n, _p(logits))
+    return st, logits[:n]

@@ -1082,3 +1082,172 @@ void oracle_rn_forward(const float* stem_w, const float* stem_b, const float* bl
     free(y);
   }
 }
+
+/* ---- AZ-NNUE threat features and logits (reference-native) -------------- */
+/* threat_reachable_square (src/az.rs:663-697), canonical squares. */
+static int az_reach(int piece, int sq) {
+  const int r = sq / 9, f = sq % 9, own = piece < 7;
+  switch (piece % 7) {
+    case 0: return f >= 3 && f <= 5 && (own ? r >= 7 : r <= 2);
+    case 1:
+      if (own) return (r == 7 && (f == 3 || f == 5)) || (r == 8 && f == 4) || (r == 9 && (f == 3 || f == 5));
+      return (r == 0 && (f == 3 || f == 5)) || (r == 1 && f == 4) || (r == 2 && (f == 3 || f == 5));
+    case 2:
+      if (own)
+        return (r == 5 && (f == 2 || f == 6)) || (r == 7 && (f == 0 || f == 4 || f == 8)) || (r == 9 && (f == 2 || f == 6));
+      return (r == 0 && (f == 2 || f == 6)) || (r == 2 && (f == 0 || f == 4 || f == 8)) || (r == 4 && (f == 2 || f == 6));
+    case 6:
+      if (own) return r <= 4 || ((r == 5 || r == 6) && f % 2 == 0);
+      return r >= 5 || ((r == 3 || r == 4) && f % 2 == 0);
+    default: return 1;
+  }
+}
+
+static uint32_t* az_rel = NULL; /* [14*90*90] */
+static uint8_t az_att[90][14];
+static uint32_t az_vocab = 0;
+
+/* threat_relation_map + threat_attacked_offsets (src/az.rs:577-716). */
+static void az_threat_init(void) {
+  if (az_rel) return;
+  uint32_t* rel = (uint32_t*)malloc(sizeof(uint32_t) * 14 * 90 * 90);
+  for (int i = 0; i < 14 * 90 * 90; ++i) rel[i] = 0xffffffffu;
+  uint32_t next = 0;
+  for (int a = 0; a < 14; ++a) {
+    const int own = a < 7, kind = a % 7;
+    for (int src = 0; src < 90; ++src) {
+      if (!az_reach(a, src)) continue;
+      const int r = src / 9, f = src % 9;
+      int tg[18], n = 0;
+      if (kind == 4 || kind == 5) {
+        for (int t = 0; t < 90; ++t)
+          if (t != src && (t / 9 == r || t % 9 == f)) tg[n++] = t;
+      } else {
+        int st[8][2], ns = 0;
+#define AZ_ST(x, y) (st[ns][0] = (x), st[ns][1] = (y), ++ns)
+        if (kind == 0) { AZ_ST(0, -1); AZ_ST(0, 1); AZ_ST(-1, 0); AZ_ST(1, 0); }
+        else if (kind == 1) { AZ_ST(-1, -1); AZ_ST(1, -1); AZ_ST(-1, 1); AZ_ST(1, 1); }
+        else if (kind == 2) { AZ_ST(-2, -2); AZ_ST(2, -2); AZ_ST(-2, 2); AZ_ST(2, 2); }
+        else if (kind == 3) { AZ_ST(-1, -2); AZ_ST(1, -2); AZ_ST(-1, 2); AZ_ST(1, 2); AZ_ST(-2, -1); AZ_ST(-2, 1); AZ_ST(2, -1); AZ_ST(2, 1); }
+        else if (own && r <= 4) { AZ_ST(0, -1); AZ_ST(-1, 0); AZ_ST(1, 0); }
+        else if (!own && r >= 5) { AZ_ST(0, 1); AZ_ST(-1, 0); AZ_ST(1, 0); }
+        else if (own) { AZ_ST(0, -1); }
+        else { AZ_ST(0, 1); }
+#undef AZ_ST
+        for (int i = 0; i < ns; ++i) {
+          const int tf = f + st[i][0], tr = r + st[i][1];
+          if (tf < 0 || tf > 8 || tr < 0 || tr > 9) continue;
+          if ((kind == 0 || kind == 1) && (tf < 3 || tf > 5 || (own ? tr < 7 : tr > 2))) continue;
+          if (kind == 2 && (own ? tr < 5 : tr > 4)) continue;
+          tg[n++] = tr * 9 + tf;
+        }
+      }
+      for (int i = 0; i < n; ++i) {
+        rel[(a * 90 + src) * 90 + tg[i]] = next;
+        for (int p = 0; p < 14; ++p) next += (uint32_t)az_reach(p, tg[i]);
+      }
+    }
+  }
+  for (int sq = 0; sq < 90; ++sq) {
+    int k = 0;
+    for (int p = 0; p < 14; ++p) az_att[sq][p] = az_reach(p, sq) ? (uint8_t)k++ : 255;
+  }
+  az_vocab = next;
+  az_rel = rel;
+}
+
+int oracle_az_threat_vocab(void) {
+  az_threat_init();
+  return (int)az_vocab;
+}
+
+static void az_threat_push(int persp, int src, int attacker, int tgt, int attacked, uint32_t* out, int* n) {
+  const int ai = ((attacker > 0 ? 0 : 1) == persp ? 0 : 7) + (attacker > 0 ? attacker : -attacker) - 1;
+  const int vi = ((attacked > 0 ? 0 : 1) == persp ? 0 : 7) + (attacked > 0 ? attacked : -attacked) - 1;
+  const int cs = persp == 0 ? src : 89 - src, ct = persp == 0 ? tgt : 89 - tgt;
+  const uint32_t base = az_rel[(ai * 90 + cs) * 90 + ct];
+  if (base == 0xffffffffu || az_att[ct][vi] == 255) return;
+  if (*n < 256) out[(*n)++] = base + az_att[ct][vi];
+}
+
+/* visit_occupied_attacks (src/xiangqi/mod.rs:286-389) + value_threat_index
+ * (src/az.rs:718-742).  Returns the feature count. */
+int oracle_az_threat_features(const int8_t* b, int persp, uint32_t* out) {
+  az_threat_init();
+  int n = 0;
+#define IN(x, y) ((x) >= 0 && (x) < 9 && (y) >= 0 && (y) < 10)
+#define HIT(x, y) do { if (IN(x, y) && b[(y) * 9 + (x)]) az_threat_push(persp, s, v, (y) * 9 + (x), b[(y) * 9 + (x)], out, &n); } while (0)
+  for (int s = 0; s < 90; ++s) {
+    const int v = b[s];
+    if (!v) continue;
+    const int kind = (v > 0 ? v : -v) - 1, red = v > 0, f = s % 9, r = s / 9;
+    if (kind == 0 || kind == 1) {
+      static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+      static const int d[4][2] = {{-1, -1}, {-1, 1}, {1, -1}, {1, 1}};
+      for (int i = 0; i < 4; ++i) {
+        const int tf = f + (kind ? d[i][0] : o[i][0]), tr = r + (kind ? d[i][1] : o[i][1]);
+        if (IN(tf, tr) && tf >= 3 && tf <= 5 && (red ? tr >= 7 : tr <= 2)) HIT(tf, tr);
+      }
+    } else if (kind == 2) {
+      static const int e[4][2] = {{-2, -2}, {-2, 2}, {2, -2}, {2, 2}};
+      for (int i = 0; i < 4; ++i) {
+        const int tf = f + e[i][0], tr = r + e[i][1];
+        if (IN(tf, tr) && (red ? tr >= 5 : tr <= 4) && !b[(r + e[i][1] / 2) * 9 + f + e[i][0] / 2]) HIT(tf, tr);
+      }
+    } else if (kind == 3) {
+      static const int h[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                  {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+      for (int i = 0; i < 8; ++i)
+        if (IN(f + h[i][2], r + h[i][3]) && IN(f + h[i][0], r + h[i][1]) && !b[(r + h[i][1]) * 9 + f + h[i][0]])
+          HIT(f + h[i][2], r + h[i][3]);
+    } else if (kind == 4 || kind == 5) {
+      static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+      for (int i = 0; i < 4; ++i) {
+        int tf = f + o[i][0], tr = r + o[i][1], occ = 0;
+        while (IN(tf, tr)) {
+          if (b[tr * 9 + tf]) {
+            ++occ;
+            if (kind == 4 || occ == 2) {
+              az_threat_push(persp, s, v, tr * 9 + tf, b[tr * 9 + tf], out, &n);
+              break;
+            }
+          }
+          tf += o[i][0];
+          tr += o[i][1];
+        }
+      }
+    } else {
+      HIT(f, r + (red ? -1 : 1));
+      if (red ? r <= 4 : r >= 5) {
+        HIT(f - 1, r);
+        HIT(f + 1, r);
+      }
+    }
+  }
+#undef HIT
+#undef IN
+  return n;
+}
+
+/* value_threat_logits activation and output (src/az.rs:2103-2119). */
+int oracle_az_threat_logits(const int8_t* table, float scale, const float* out_w, const uint32_t* features,
+                            const uint32_t* offsets, int64_t n, float* logits) {
+  int status = 0;
+  for (int64_t p = 0; p < n; ++p) {
+    int16_t acc[64];
+    memset(acc, 0, sizeof(acc));
+    for (uint32_t i = offsets[p]; i < offsets[p + 1]; ++i) {
+      if (features[i] >= 57702u) { status = 2; continue; }
+      for (int j = 0; j < 64; ++j) acc[j] = (int16_t)(uint16_t)((uint16_t)acc[j] + (uint16_t)(int16_t)table[(size_t)features[i] * 64 + j]);
+    }
+    float act[128];
+    for (int j = 0; j < 64; ++j) {
+      float v = (float)acc[j] * scale;
+      v = v < 0.f ? 0.f : (v > 1.f ? 1.f : v);
+      act[j] = v;
+      act[64 + j] = v * v;
+    }
+    for (int o = 0; o < 3; ++o) logits[p * 3 + o] = az_dot(act, out_w + o * 128, 128);
+  }
+  return status;
+}

@@ -305,3 +305,33 @@ def test_policy_accumulator_incremental_equals_refresh_on_the_oracle():
         board = az.apply_move(board, frm, to)
         st2, full = oracle.az_policy_refresh(fq, *az.node_lists(board[None]))
         np.testing.assert_array_equal(acc, full)
+
+
+def test_threat_vocabulary_is_the_reference_size():
+    """threat_relation_map enumerates exactly VALUE_THREAT_VOCAB = 57,702
+    slots (src/az.rs:106, asserted at :656) - in the library and the oracle."""
+    from chineseai_b200._lib import lib
+    assert lib().cnnue_az_threat_vocab() == 57702
+    assert oracle.az_threat_vocab() == 57702
+
+
+def test_threat_features_of_the_start_position():
+    """Start position, Red to move: 4 cannon-over-screen attacks on the
+    opposing horses, 8 rook contacts (own horse and pawn), 4 general contacts
+    (own advisors) - 16 relations."""
+    board, side = az.board_from_fen(az.STARTPOS)
+    f = az.threat_features(board, side)
+    assert len(f) == 16 and len(set(f.tolist())) == 16
+    np.testing.assert_array_equal(f, oracle.az_threat_features(board, side))
+    # colour symmetry: the mirrored position seen by Black gives the same rows
+    mirrored = -board[::-1].copy()
+    np.testing.assert_array_equal(np.sort(az.threat_features(mirrored, 1)), np.sort(f))
+
+
+def test_threat_features_match_oracle_on_random_boards():
+    boards = az.random_boards(300, seed=17)
+    for b in boards:
+        for side in (0, 1):
+            got = az.threat_features(b, side)
+            np.testing.assert_array_equal(got, oracle.az_threat_features(b, side))
+            assert (got < 57702).all()

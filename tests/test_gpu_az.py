@@ -290,3 +290,38 @@ def test_policy_walk_matches_refresh_exactly():
         full = model.policy_refresh(*[_dev(a) for a in az.node_lists(board[None])])
         assert torch.equal(acc, full)
     assert model.read_status() == 0
+
+
+# ---- threat logits (bit-exact) ---------------------------------------------
+def test_threat_logits_bit_exact_and_value_with_threat():
+    w = az.AzWeights.random(128, 20260807)
+    trained_like(w, 51)
+    rng = np.random.default_rng(52)
+    out = w.tensor("value_threat_output")
+    out[...] = rng.standard_normal(out.shape).astype(np.float32) * np.float32(0.5)
+    emb = w.tensor("value_threat_embedding")
+    emb *= np.float32(20.0)  # larger rows: activations reach the clamp and the int16 sums wrap sometimes
+    w.quantize()
+    assert w.quant_flags()[0]
+    table, scale = w.quant_table(az.Q_VALUE_THREAT)
+    model = az.AzModel(w, device=0)
+    try:
+        boards = az.random_boards(1500, seed=53)
+        side = rng.integers(0, 2, len(boards)).astype(np.uint8)
+        lists = [az.threat_features(b, int(s)) for b, s in zip(boards, side)]
+        lists[7] = np.zeros(0, np.uint32)  # no attacks
+        lists[9] = np.tile(lists[9], 40) if len(lists[9]) else np.full(200, 5, np.uint32)  # long: wraps
+        feats, offs = az.pack_lists(lists)
+        logits = model.threat_logits(_dev(feats), _dev(offs))
+        assert model.read_status() == 0
+        st, ref = oracle.az_threat_logits(table, scale, w.tensor("value_threat_output"), feats, offs)
+        assert st == 0
+        np.testing.assert_array_equal(logits.cpu().numpy(), ref)
+        # the value head with these threat logits agrees with the oracle's
+        acc = model.refresh(*[_dev(a) for a in az.node_lists(boards)])
+        wdl, q = model.value(acc, side=_dev(side), threat=logits)
+        a = acc.cpu().numpy().reshape(len(boards), 2, 128)[np.arange(len(boards)), side]
+        r_wdl, r_q = oracle.az_value(w.tensors(), 128, a, None, ref)
+        np.testing.assert_allclose(q.cpu().numpy(), r_q, atol=1e-4, rtol=0)
+    finally:
+        model.close()

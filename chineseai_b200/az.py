@@ -179,6 +179,38 @@ def threat_features(board: np.ndarray, side: int) -> np.ndarray:
     return out[:n.value].copy()
 
 
+def policy_moves(board: np.ndarray, side: int, moves: np.ndarray) -> np.ndarray:
+    """Per-move records uint32 [n][2] for the policy logits (moves: [n][2]
+    absolute from/to squares)."""
+    b = np.ascontiguousarray(board, np.int8)
+    mv = np.ascontiguousarray(moves, np.uint8).reshape(-1, 2)
+    info = np.zeros((max(len(mv), 1), 2), np.uint32)
+    check(lib().cnnue_az_policy_moves(b.ctypes.data, side, mv.ctypes.data, len(mv), info.ctypes.data),
+          "cnnue_az_policy_moves")
+    return info[:len(mv)].copy()
+
+
+def pseudo_moves(board: np.ndarray, side: int, rng: np.random.Generator, k: int) -> np.ndarray:
+    """Up to k distinct from/to pairs of `side`'s pieces onto empty or enemy
+    squares that lie in the dense policy move space (stand-ins for a move
+    list; rules legality is not needed by the arithmetic)."""
+    _, s2d = dense_moves()
+    own = np.flatnonzero((board > 0) if side == 0 else (board < 0))
+    out = []
+    for _ in range(8 * k):
+        if len(out) == k or len(own) == 0:
+            break
+        frm = int(rng.choice(own))
+        to = int(rng.integers(0, SQUARES))
+        if to == frm or (board[to] != 0 and (board[to] > 0) == (board[frm] > 0)):
+            continue
+        cf, ct = (frm, to) if side == 0 else (89 - frm, 89 - to)
+        if s2d[cf * SQUARES + ct] == 0xFFFF or (frm, to) in out:
+            continue
+        out.append((frm, to))
+    return np.array(out, np.uint8).reshape(-1, 2)
+
+
 @dataclass
 class MoveItems:
     refresh: bool
@@ -360,6 +392,30 @@ class AzModel:
                                            self._ws.data_ptr(), self._ws.numel(), self._stream(stream)),
               "cnnue_az_threat_logits")
         return out
+
+    def evaluate(self, acc, side=None, rule=None, threat_features=None, threat_offsets=None, policy_acc=None,
+                 move_info=None, move_offsets=None, stream=None):
+        """evaluate_incremental_with_scratch_output for a batch: (wdl, q,
+        logits or None).  acc/policy_acc are node layouts with `side`."""
+        torch = self._torch
+        n = side.numel() if side is not None else acc.numel() // self.hidden
+        wdl = torch.empty((n, 3), dtype=torch.float32, device=self.device)
+        q = torch.empty(n, dtype=torch.float32, device=self.device)
+        logits = None
+        n_moves = 0
+        if move_info is not None:
+            n_moves = move_info.numel() // 2
+            logits = torch.empty(n_moves, dtype=torch.float32, device=self.device)
+        need = int(lib().cnnue_az_evaluate_workspace_bytes(self._h, n))
+        if self._ws.numel() < need:
+            self._ws = torch.zeros(need, dtype=torch.uint8, device=self.device)
+        n_tf = 0 if threat_features is None else threat_features.numel()
+        check(lib().cnnue_az_evaluate(self._h, acc.data_ptr(), self._ptr(side), self._ptr(rule),
+                                      self._ptr(threat_features) if n_tf else None, n_tf, self._ptr(threat_offsets),
+                                      self._ptr(policy_acc), self._ptr(move_info), n_moves, self._ptr(move_offsets),
+                                      n, wdl.data_ptr(), q.data_ptr(), self._ptr(logits), self._ws.data_ptr(),
+                                      self._ws.numel(), self._stream(stream)), "cnnue_az_evaluate")
+        return wdl, q, logits
 
     def value(self, acc, side=None, rule=None, threat=None, stream=None):
         """(wdl [n][3], q [n]) of side-to-move accumulators: acc [n][H], or with

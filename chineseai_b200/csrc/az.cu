@@ -36,6 +36,20 @@ struct cnnue_az_model {
   int8_t* threat_q = nullptr;  // quantised threat embedding [57702][64]
   float* threat_out = nullptr; // value_threat_output [3][128]
   float threat_scale = 1.f;
+  // policy head (evaluate_prepared_hidden_with_context, src/az.rs:1766-1887)
+  float* ps_scores = nullptr;      // [1260] piece-square consequence scores
+  float* move_bias = nullptr;      // [2086]
+  float* move_context = nullptr;   // [2086][16]
+  float* context_hidden = nullptr; // [16][H]
+  float* threat_context = nullptr; // [16][128]
+  int8_t* move_q = nullptr;        // [2086][32]
+  int32_t* moved_delta = nullptr;  // [2086][14]
+  int32_t* capture = nullptr;      // [2086][14]
+  int8_t* sparse_q = nullptr;      // [2396815]
+  float* tactical = nullptr;       // [934976]
+  float feature_scale = 1.f, move_scale = 1.f, sparse_scale = 1.f;
+  int threat_active = 0, tactical_active = 0;
+  void* policy_blob = nullptr;
 };
 
 namespace cnnue {
@@ -271,6 +285,7 @@ struct ValueArgs {
   int64_t n;
   float* wdl;
   float* q;
+  float* x_out;  // optional [n][H]: the normalised hidden the policy head reads
 };
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -320,7 +335,10 @@ __global__ void __launch_bounds__(256) az_value_kernel(ValueArgs p) {
       }
       ss = warp_sum(ss);
       const float inv = 1.0f / sqrtf(ss / (float)H + 1e-6f);
-      for (int c = lane; c < H; c += 32) x[c] *= inv;
+      for (int c = lane; c < H; c += 32) {
+        x[c] *= inv;
+        if (p.x_out) p.x_out[(size_t)pos * H + c] = x[c];
+      }
     }
     __syncwarp();
     // 2. value units k, k+32, k+64 of the 4 positions.
@@ -521,7 +539,7 @@ constexpr int kThreatWarps = 8;
 __global__ void __launch_bounds__(kThreatWarps * 32) az_threat_kernel(
     const int8_t* __restrict__ table, float scale, const float* __restrict__ out_w,
     const uint32_t* __restrict__ features, uint32_t n_features, const uint32_t* __restrict__ offsets, int64_t n,
-    float* __restrict__ logits, WorkspaceHeader* hdr) {
+    float* __restrict__ logits, float* __restrict__ act_out, WorkspaceHeader* hdr) {
   __shared__ float act[kThreatWarps][2 * CNNUE_AZ_THREAT_RANK];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   uint32_t status = 0;
@@ -549,6 +567,10 @@ __global__ void __launch_bounds__(kThreatWarps * 32) az_threat_kernel(
     a[CNNUE_AZ_THREAT_RANK + 2 * lane] = __fmul_rn(x0, x0);
     a[CNNUE_AZ_THREAT_RANK + 2 * lane + 1] = __fmul_rn(x1, x1);
     __syncwarp();
+    if (act_out) {
+      float* o = act_out + (size_t)p * 2 * CNNUE_AZ_THREAT_RANK;
+      for (int i = lane; i < 2 * CNNUE_AZ_THREAT_RANK; i += 32) o[i] = a[i];
+    }
     if (lane < 3) {
       const float* w = out_w + lane * 2 * CNNUE_AZ_THREAT_RANK;
       float part[4][8];
@@ -571,6 +593,169 @@ __global__ void __launch_bounds__(kThreatWarps * 32) az_threat_kernel(
   }
   status = __reduce_or_sync(kFull, status);
   if (lane == 0 && status) atomicOr(&hdr->status, status);
+}
+
+// ---- policy logits (evaluate_prepared_hidden_with_context) -----------------
+// One warp per position.  Lanes 0-15 form the 16 context values (normalised
+// hidden . policy_context_hidden[c], + threat activation .
+// policy_threat_context[c] when the threat branch is active); then each lane
+// takes moves j = lane, lane + 32, ... and sums the six terms in the
+// reference's order: move bias, piece-square consequence, context . move
+// context, quantised accumulator, folded sparse table, tactical table.
+constexpr int kPolicyLogitWarps = 8;
+constexpr int64_t kSparseMain = (int64_t)CNNUE_AZ_DENSE_MOVES * 14 * 81;
+constexpr int64_t kTacticalExact = (int64_t)CNNUE_AZ_DENSE_MOVES * 7 * 64;
+
+struct PolicyLogitArgs {
+  const float* x;          // [n][H] normalised hidden
+  const float* threat_act; // [n][128] or null
+  const int16_t* pacc;     // [n][32] or [n][2][32] with side
+  const uint8_t* side;
+  const uint32_t* info;    // [moves][2]
+  uint32_t n_moves;
+  const uint32_t* offsets; // [n+1]
+  int64_t n;
+  int H;
+  float* logits;
+  WorkspaceHeader* hdr;
+  // model tables
+  const float* ps;
+  const float* bias;
+  const float* mctx;
+  const float* pch;
+  const float* ptc;
+  const int8_t* mq;
+  const int32_t* mdelta;
+  const int32_t* mcap;
+  const int8_t* sq;
+  const float* tac;
+  float fscale, mscale, sscale;
+  int tactical_active;
+};
+
+__global__ void __launch_bounds__(kPolicyLogitWarps * 32) az_policy_logits_kernel(PolicyLogitArgs a) {
+  __shared__ float ctx[kPolicyLogitWarps][16];
+  __shared__ int16_t pacc[kPolicyLogitWarps][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  uint32_t status = 0;
+  for (int64_t p = (int64_t)blockIdx.x * kPolicyLogitWarps + warp; p < a.n; p += (int64_t)gridDim.x * kPolicyLogitWarps) {
+    if (lane < 16) {
+      const float* x = a.x + (size_t)p * a.H;
+      const float* w = a.pch + (size_t)lane * a.H;
+      float c = 0.f;
+      for (int j = 0; j < a.H; ++j) c = fmaf(__ldg(x + j), __ldg(w + j), c);
+      if (a.threat_act) {
+        const float* t = a.threat_act + (size_t)p * 2 * CNNUE_AZ_THREAT_RANK;
+        const float* tw = a.ptc + lane * 2 * CNNUE_AZ_THREAT_RANK;
+        float d = 0.f;
+        for (int j = 0; j < 2 * CNNUE_AZ_THREAT_RANK; ++j) d = fmaf(__ldg(t + j), __ldg(tw + j), d);
+        c += d;
+      }
+      ctx[warp][lane] = c;
+    }
+    const int16_t* prow = a.pacc + (a.side ? ((size_t)p * 2 + (a.side[p] ? 1 : 0)) : (size_t)p) * 32;
+    pacc[warp][lane] = prow[lane];
+    __syncwarp();
+    const uint32_t beg = a.offsets[p], end = a.offsets[p + 1];
+    if (!(beg <= end && end <= a.n_moves)) {
+      status |= CNNUE_STATUS_BAD_OFFSETS;
+    } else {
+      for (uint32_t j = beg + lane; j < end; j += 32) {
+        const uint32_t w0 = a.info[2 * j], w1 = a.info[2 * j + 1];
+        const uint32_t dense = w0 & 0xfffu, moved = (w0 >> 12) & 15u, cap = (w0 >> 16) & 15u, sig = (w0 >> 20) & 63u;
+        const uint32_t cf = w1 & 127u, ct = (w1 >> 7) & 127u, us = (w1 >> 14) & 15u, them = (w1 >> 18) & 15u;
+        if (dense >= (uint32_t)CNNUE_AZ_DENSE_MOVES || moved >= 14u || (cap >= 14u && cap != 15u) || cf >= 90u ||
+            ct >= 90u || us > 8u || them > 8u) {
+          status |= CNNUE_STATUS_BAD_INDEX;
+          a.logits[j] = 0.f;
+          continue;
+        }
+        // piece-square consequence: scores[to] - scores[from] - scores[captured]
+        float ps = __fsub_rn(__ldg(a.ps + moved * 90 + ct), __ldg(a.ps + moved * 90 + cf));
+        ps = __fsub_rn(ps, cap < 14u ? __ldg(a.ps + cap * 90 + ct) : 0.f);
+        // context . move_context[dense]: dot_product's scalar path (16 < 64)
+        const float* mc = a.mctx + dense * 16;
+        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int k = 0; k < 4; ++k) s4[k] = __fadd_rn(s4[k], __fmul_rn(ctx[warp][4 * c + k], __ldg(mc + 4 * c + k)));
+        const float cdot = __fadd_rn(__fadd_rn(s4[0], s4[1]), __fadd_rn(s4[2], s4[3]));
+        // quantised accumulator . move row (exact integers)
+        int32_t v = 0;
+        const int8_t* mrow = a.mq + dense * 32;
+#pragma unroll
+        for (int k = 0; k < 32; ++k) v += (int32_t)pacc[warp][k] * (int32_t)__ldg(mrow + k);
+        v += __ldg(a.mdelta + dense * 14 + moved);
+        if (cap < 14u) v -= __ldg(a.mcap + dense * 14 + cap);
+        const float accl = __fmul_rn(__fmul_rn((float)v, a.fscale), a.mscale);
+        // folded sparse table
+        const int64_t main = (((int64_t)dense * 14 + moved) * 9 + us) * 9 + them;
+        const int64_t capi = kSparseMain + (int64_t)dense * 15 + (cap < 14u ? cap : 14u);
+        const float sparse = __fmul_rn((float)((int32_t)__ldg(a.sq + main) + (int32_t)__ldg(a.sq + capi)), a.sscale);
+        float tactical = 0.f;
+        if (a.tactical_active && moved < 7u) {
+          const int64_t exact = ((int64_t)dense * 7 + moved) * 64 + sig;
+          const int64_t factor = kTacticalExact + (int64_t)moved * 64 + sig;
+          tactical = __fadd_rn(__ldg(a.tac + exact), __ldg(a.tac + factor));
+        }
+        float logit = __fadd_rn(__ldg(a.bias + dense), ps);
+        logit = __fadd_rn(logit, cdot);
+        logit = __fadd_rn(logit, accl);
+        logit = __fadd_rn(logit, sparse);
+        logit = __fadd_rn(logit, tactical);
+        a.logits[j] = logit;
+      }
+    }
+    __syncwarp();
+  }
+  status = __reduce_or_sync(kFull, status);
+  if (lane == 0 && status) atomicOr(&a.hdr->status, status);
+}
+
+// Device copy of the policy-head tables (one allocation).
+int upload_policy(const cnnue_az_weights& w, cnnue_az_model* m) {
+  using namespace cnnue::az;
+  const int64_t H = w.hidden;
+  const int D = CNNUE_AZ_DENSE_MOVES;
+  if (w.ps_scores.size() != (size_t)CNNUE_AZ_INPUT || w.q8[1].size() != (size_t)D * 32 ||
+      w.q8[2].size() != (size_t)2396815 || w.q32[0].size() != (size_t)D * 14 || w.q32[1].size() != (size_t)D * 14)
+    return set_error(CNNUE_ERR_INVALID_ARG, "weights have no quantised policy tables (run cnnue_az_quantize)");
+  struct Part {
+    const void* src;
+    size_t bytes;
+    void** dst;
+  };
+  Part parts[] = {
+      {w.ps_scores.data(), w.ps_scores.size() * 4, (void**)&m->ps_scores},
+      {w.t[13].data(), w.t[13].size() * 4, (void**)&m->move_bias},
+      {w.t[16].data(), w.t[16].size() * 4, (void**)&m->move_context},
+      {w.t[15].data(), w.t[15].size() * 4, (void**)&m->context_hidden},
+      {w.t[12].data(), w.t[12].size() * 4, (void**)&m->threat_context},
+      {w.q8[1].data(), w.q8[1].size(), (void**)&m->move_q},
+      {w.q32[0].data(), w.q32[0].size() * 4, (void**)&m->moved_delta},
+      {w.q32[1].data(), w.q32[1].size() * 4, (void**)&m->capture},
+      {w.q8[2].data(), w.q8[2].size(), (void**)&m->sparse_q},
+      {w.t[21].data(), w.t[21].size() * 4, (void**)&m->tactical},
+  };
+  if (w.t[15].size() != (size_t)16 * H) return set_error(CNNUE_ERR_INVALID_ARG, "policy_context_hidden size");
+  size_t total = 0;
+  for (const Part& p : parts) total += align_up(p.bytes, 256);
+  cudaError_t e = cudaMalloc(&m->policy_blob, total);
+  if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(az policy tables)");
+  char* p = (char*)m->policy_blob;
+  for (const Part& part : parts) {
+    *part.dst = p;
+    if ((e = cudaMemcpy(p, part.src, part.bytes, cudaMemcpyHostToDevice)) != cudaSuccess)
+      return cuda_error(e, "az policy table upload");
+    p += align_up(part.bytes, 256);
+  }
+  m->feature_scale = w.scale[0];
+  m->move_scale = w.scale[1];
+  m->sparse_scale = w.scale[2];
+  m->threat_active = w.value_threat_active;
+  m->tactical_active = w.policy_tactical_active;
+  return CNNUE_OK;
 }
 
 // The float4 column path needs 16-byte aligned accumulator rows.
@@ -665,6 +850,7 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
     if (ce != cudaSuccess) st = cuda_error(ce, "threat table");
   }
   copy(m->threat_out, w->t[11], 3 * 2 * CNNUE_AZ_THREAT_RANK, "value_threat_output");
+  if (!st) st = upload_policy(*w, m);
   if (!st) {
     const int64_t n = (int64_t)kHead * H;
     transpose_head_kernel<<<(unsigned)((n + 255) / 256), 256>>>(stage, (int)H, m->head_t);
@@ -687,6 +873,7 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
   }
   if (st) {
     cudaFree(m->blob);
+    if (m->policy_blob) cudaFree(m->policy_blob);
     delete m;
     return st;
   }
@@ -697,6 +884,7 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
 int cnnue_az_model_destroy(cnnue_az_model* m) {
   if (!m) return CNNUE_OK;
   DeviceGuard guard(m->device);
+  if (m->policy_blob) cudaFree(m->policy_blob);
   if (m->blob) cudaFree(m->blob);
   delete m;
   return guard.status;
@@ -859,8 +1047,111 @@ int cnnue_az_threat_logits(const cnnue_az_model* m, const uint32_t* d_features, 
   const int64_t want = (n + kThreatWarps - 1) / kThreatWarps;
   const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
   az_threat_kernel<<<blocks, kThreatWarps * 32, 0, s>>>(m->threat_q, m->threat_scale, m->threat_out, d_features,
-                                                        n_features, d_offsets, n, d_logits, (WorkspaceHeader*)ws);
+                                                        n_features, d_offsets, n, d_logits, nullptr,
+                                                        (WorkspaceHeader*)ws);
   return check_launch_error("az_threat_kernel");
+}
+
+size_t cnnue_az_evaluate_workspace_bytes(const cnnue_az_model* m, int64_t n) {
+  if (!m || n < 0) return 0;
+  return sizeof(WorkspaceHeader) + align_up((size_t)n * m->hidden * 4, 256) + align_up((size_t)n * 3 * 4, 256) +
+         align_up((size_t)n * 2 * CNNUE_AZ_THREAT_RANK * 4, 256);
+}
+
+int cnnue_az_evaluate(const cnnue_az_model* m, const float* d_acc, const uint8_t* d_side, const float* d_rule,
+                      const uint32_t* d_threat_features, uint32_t n_threat_features, const uint32_t* d_threat_offsets,
+                      const int16_t* d_policy_acc, const uint32_t* d_move_info, uint32_t n_moves,
+                      const uint32_t* d_move_offsets, int64_t n, float* d_wdl, float* d_q, float* d_logits, void* ws,
+                      size_t ws_bytes, void* stream) {
+  if (!m || !ws || n < 0 || (n > 0 && (!d_acc || !d_wdl || !d_q)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null model, workspace, acc, wdl or q, or n < 0");
+  if (d_move_info && (!d_move_offsets || !d_logits || !d_policy_acc))
+    return set_error(CNNUE_ERR_INVALID_ARG, "moves need offsets, logits and the policy accumulators");
+  if (d_threat_features && !d_threat_offsets) return set_error(CNNUE_ERR_INVALID_ARG, "threat features need offsets");
+  if (ws_bytes < cnnue_az_evaluate_workspace_bytes(m, n))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes, cnnue_az_evaluate_workspace_bytes(m, n));
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  if (n == 0) return CNNUE_OK;
+  char* p = (char*)ws + sizeof(WorkspaceHeader);
+  float* x = (float*)p;
+  p += align_up((size_t)n * m->hidden * 4, 256);
+  float* tlogits = (float*)p;
+  p += align_up((size_t)n * 3 * 4, 256);
+  float* tact = (float*)p;
+  WorkspaceHeader* hdr = (WorkspaceHeader*)ws;
+  // 1. threat branch, when the model has one (value_threat_active)
+  const bool threat = d_threat_offsets != nullptr && m->threat_active;
+  if (threat) {
+    const int64_t want = (n + kThreatWarps - 1) / kThreatWarps;
+    const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+    az_threat_kernel<<<blocks, kThreatWarps * 32, 0, s>>>(m->threat_q, m->threat_scale, m->threat_out,
+                                                          d_threat_features, n_threat_features, d_threat_offsets, n,
+                                                          tlogits, tact, hdr);
+    if (int st = check_launch_error("az_threat_kernel")) return st;
+  }
+  // 2. value head, keeping the normalised hidden for the policy head
+  {
+    ValueArgs a{};
+    a.head_t = m->head_t;
+    a.head_b = m->head_b;
+    a.head_o = m->head_o;
+    a.rule_rows = m->rule;
+    a.H = (int)m->hidden;
+    a.acc = d_acc;
+    a.side = d_side;
+    a.rule = d_rule;
+    a.threat = threat ? tlogits : nullptr;
+    a.n = n;
+    a.wdl = d_wdl;
+    a.q = d_q;
+    a.x_out = x;
+    const int warps = value_warps(m->hidden);
+    const size_t smem = value_smem_bytes(m->hidden, warps);
+    const int64_t groups = (n + kValuePos - 1) / kValuePos;
+    const int64_t want = (groups + warps - 1) / warps;
+    int per_sm = (int)(kMaxSmem / smem);
+    per_sm = per_sm < 1 ? 1 : (per_sm > 4 ? 4 : per_sm);
+    const unsigned blocks = (unsigned)(want < 148 * per_sm ? want : 148 * per_sm);
+    az_value_kernel<<<blocks, warps * 32, smem, s>>>(a);
+    if (int st = check_launch_error("az_value_kernel")) return st;
+  }
+  // 3. policy logits of the listed moves
+  if (d_move_info) {
+    PolicyLogitArgs a{};
+    a.x = x;
+    a.threat_act = threat ? tact : nullptr;
+    a.pacc = d_policy_acc;
+    a.side = d_side;
+    a.info = d_move_info;
+    a.n_moves = n_moves;
+    a.offsets = d_move_offsets;
+    a.n = n;
+    a.H = (int)m->hidden;
+    a.logits = d_logits;
+    a.hdr = hdr;
+    a.ps = m->ps_scores;
+    a.bias = m->move_bias;
+    a.mctx = m->move_context;
+    a.pch = m->context_hidden;
+    a.ptc = m->threat_context;
+    a.mq = m->move_q;
+    a.mdelta = m->moved_delta;
+    a.mcap = m->capture;
+    a.sq = m->sparse_q;
+    a.tac = m->tactical;
+    a.fscale = m->feature_scale;
+    a.mscale = m->move_scale;
+    a.sscale = m->sparse_scale;
+    a.tactical_active = m->tactical_active;
+    const int64_t want = (n + kPolicyLogitWarps - 1) / kPolicyLogitWarps;
+    const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+    az_policy_logits_kernel<<<blocks, kPolicyLogitWarps * 32, 0, s>>>(a);
+    if (int st = check_launch_error("az_policy_logits_kernel")) return st;
+  }
+  return CNNUE_OK;
 }
 
 }  // extern "C"

@@ -521,6 +521,10 @@ int quantize(cnnue_az_weights& w) {
       if (x != 0.f) return true;
     return false;
   };
+  // piece-square consequence scores over the first min(32, H) columns.
+  const int64_t cs = h < 32 ? h : 32;
+  w.ps_scores.resize(CNNUE_AZ_INPUT);
+  for (int f = 0; f < CNNUE_AZ_INPUT; ++f) w.ps_scores[f] = reference_dot(w.t[0].data() + f * h, w.t[14].data(), cs);
   w.value_threat_active = any(w.t[11]) || any(w.t[12]);
   w.policy_tactical_active = any(w.t[21]);
   w.scale[3] = quantize_i8(w.t[10].data(), w.t[10].size(), w.q8[3]);
@@ -713,9 +717,237 @@ void visit_attacks(const int8_t* b, Visit&& visit) {
   }
 }
 
+// ---- policy move records (src/az.rs:1766-1887) ------------------------------
+// Board helpers in absolute coordinates; colour 0 = Red (positive codes).
+inline int color_of(int v) { return v > 0 ? 0 : 1; }
+inline int kind_of(int v) { return (v > 0 ? v : -v) - 1; }
+inline bool on_board(int f, int r) { return f >= 0 && f < 9 && r >= 0 && r < 10; }
+inline bool palace(int color, int f, int r) { return f >= 3 && f <= 5 && (color == 0 ? r >= 7 : r <= 2); }
+
+int general_of(const int8_t* b, int color) {
+  int g = -1;
+  for (int sq = 0; sq < kSq; ++sq)
+    if (b[sq] != 0 && kind_of(b[sq]) == 0 && color_of(b[sq]) == color) g = sq;  // last in scan order
+  return g;
+}
+
+// Position::attacked_squares_mask (src/xiangqi/mod.rs:391-484) as a 90-entry
+// flag array: squares attacked by `by`, empty or not.
+void attacked_squares(const int8_t* b, int by, uint8_t* mask) {
+  std::memset(mask, 0, kSq);
+  auto mark = [&](int f, int r) {
+    if (on_board(f, r)) mask[r * 9 + f] = 1;
+  };
+  const int enemy_general = general_of(b, 1 - by);
+  for (int sq = 0; sq < kSq; ++sq) {
+    const int v = b[sq];
+    if (v == 0 || color_of(v) != by) continue;
+    const int f = sq % 9, r = sq / 9;
+    switch (kind_of(v)) {
+      case 0: {
+        static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+        for (auto& d : o)
+          if (on_board(f + d[0], r + d[1]) && palace(by, f + d[0], r + d[1])) mark(f + d[0], r + d[1]);
+        if (enemy_general >= 0 && enemy_general % 9 == f) {
+          bool clear = true;
+          const int lo = std::min(r, enemy_general / 9), hi = std::max(r, enemy_general / 9);
+          for (int rr = lo + 1; rr < hi; ++rr) clear &= b[rr * 9 + f] == 0;
+          if (clear) mask[enemy_general] = 1;
+        }
+        break;
+      }
+      case 1: {
+        static const int d4[4][2] = {{-1, -1}, {-1, 1}, {1, -1}, {1, 1}};
+        for (auto& d : d4)
+          if (on_board(f + d[0], r + d[1]) && palace(by, f + d[0], r + d[1])) mark(f + d[0], r + d[1]);
+        break;
+      }
+      case 2: {
+        static const int e[4][2] = {{-2, -2}, {-2, 2}, {2, -2}, {2, 2}};
+        for (auto& d : e) {
+          const int tf = f + d[0], tr = r + d[1];
+          if (on_board(tf, tr) && (by == 0 ? tr >= 5 : tr <= 4) && b[(r + d[1] / 2) * 9 + f + d[0] / 2] == 0)
+            mark(tf, tr);
+        }
+        break;
+      }
+      case 3: {
+        static const int hs[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                     {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+        for (auto& h : hs)
+          if (on_board(f + h[2], r + h[3]) && b[(r + h[1]) * 9 + f + h[0]] == 0) mark(f + h[2], r + h[3]);
+        break;
+      }
+      case 4:
+      case 5: {
+        static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+        const bool rook = kind_of(v) == 4;
+        for (auto& d : o) {
+          int tf = f + d[0], tr = r + d[1], blockers = 0;
+          while (on_board(tf, tr)) {
+            const bool occupied = b[tr * 9 + tf] != 0;
+            if (rook) {
+              mark(tf, tr);
+              if (occupied) break;
+            } else {
+              if (blockers == 1) mark(tf, tr);  // beyond the screen, up to the next piece
+              if (occupied && ++blockers == 2) break;
+            }
+            tf += d[0];
+            tr += d[1];
+          }
+        }
+        break;
+      }
+      default:
+        mark(f, r + (by == 0 ? -1 : 1));
+        if (by == 0 ? r <= 4 : r >= 5) {
+          mark(f - 1, r);
+          mark(f + 1, r);
+        }
+    }
+  }
+}
+
+// Position::gives_check_after_move_fast (src/xiangqi/mod.rs:763-1012).
+bool gives_check(const int8_t* b, int side, int from, int to) {
+  const int g = general_of(b, 1 - side);
+  if (g < 0 || b[from] == 0) return false;
+  const int moving = b[from];
+  auto occ = [&](int sq) -> int { return sq == from ? 0 : (sq == to ? moving : (int)b[sq]); };
+  auto between = [&](int a, int c) -> int {  // pieces strictly between, INT_MAX-like if not aligned
+    if (a % 9 == c % 9) {
+      int n = 0;
+      for (int r = std::min(a / 9, c / 9) + 1; r < std::max(a / 9, c / 9); ++r) n += occ(r * 9 + a % 9) != 0;
+      return n;
+    }
+    if (a / 9 == c / 9) {
+      int n = 0;
+      for (int f = std::min(a % 9, c % 9) + 1; f < std::max(a % 9, c % 9); ++f) n += occ((a / 9) * 9 + f) != 0;
+      return n;
+    }
+    return 1 << 20;
+  };
+  // piece_attacks_virtual (src/xiangqi/mod.rs:920-979) of the moved piece.
+  {
+    const int pf = to % 9, pr = to / 9, tf = g % 9, tr = g / 9, df = tf - pf, dr = tr - pr;
+    const int color = color_of(moving);
+    bool hit = false;
+    switch (kind_of(moving)) {
+      case 0:
+        hit = (std::abs(df) + std::abs(dr) == 1 && palace(color, tf, tr)) ||
+              (pf == tf && occ(g) != 0 && kind_of(occ(g)) == 0 && color_of(occ(g)) != color && between(to, g) == 0);
+        break;
+      case 1: hit = std::abs(df) == 1 && std::abs(dr) == 1 && palace(color, tf, tr); break;
+      case 2:
+        hit = std::abs(df) == 2 && std::abs(dr) == 2 && (color == 0 ? tr >= 5 : tr <= 4) &&
+              occ(((pr + tr) / 2) * 9 + (pf + tf) / 2) == 0;
+        break;
+      case 3: {
+        static const int hs[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                     {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+        for (auto& h : hs)
+          if (df == h[2] && dr == h[3]) {
+            hit = occ((pr + h[1]) * 9 + pf + h[0]) == 0;
+            break;
+          }
+        break;
+      }
+      case 4: hit = (pf == tf || pr == tr) && between(to, g) == 0; break;
+      case 5: hit = (pf == tf || pr == tr) && between(to, g) == 1; break;
+      default:
+        hit = (tf == pf && tr == pr + (color == 0 ? -1 : 1)) ||
+              ((color == 0 ? tr <= 4 : tr >= 5) && tr == pr && std::abs(df) == 1);
+    }
+    if (hit) return true;
+  }
+  // discovered checks along the orthogonal rays through from or to.
+  static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+  const int gf = g % 9, gr = g / 9;
+  auto on_ray = [&](int q, int df, int dr) {
+    const int qf = q % 9, qr = q / 9;
+    return dr == 0 ? (qr == gr && (qf - gf) * df > 0) : (qf == gf && (qr - gr) * dr > 0);
+  };
+  for (auto& d : o) {
+    if (!on_ray(from, d[0], d[1]) && !on_ray(to, d[0], d[1])) continue;
+    int nf = gf + d[0], nr = gr + d[1];
+    bool screen = false;
+    while (on_board(nf, nr)) {
+      const int p = occ(nr * 9 + nf);
+      if (p != 0) {
+        if (!screen) {
+          if (color_of(p) == side && (kind_of(p) == 4 || (kind_of(p) == 0 && d[0] == 0))) return true;
+          screen = true;
+        } else if (color_of(p) == side && kind_of(p) == 5) {
+          return true;
+        } else {
+          break;
+        }
+      }
+      nf += d[0];
+      nr += d[1];
+    }
+  }
+  // a horse or elephant whose leg / eye was `from` (leaper_revealed_*, :845-918).
+  static const int hs[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                               {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+  for (auto& h : hs) {
+    const int of = gf - h[2], orr = gr - h[3];
+    if (!on_board(of, orr) || !on_board(of + h[0], orr + h[1])) continue;
+    const int p = occ(orr * 9 + of);
+    if ((orr + h[1]) * 9 + of + h[0] == from && p != 0 && kind_of(p) == 3 && color_of(p) == side) return true;
+  }
+  static const int es[4][4] = {{1, 1, 2, 2}, {1, -1, 2, -2}, {-1, 1, -2, 2}, {-1, -1, -2, -2}};
+  for (auto& e : es) {
+    const int of = gf - e[2], orr = gr - e[3];
+    if (!on_board(of, orr) || !on_board(of + e[0], orr + e[1])) continue;
+    const int p = occ(orr * 9 + of);
+    if ((orr + e[1]) * 9 + of + e[0] == from && p != 0 && kind_of(p) == 2 && color_of(p) == side &&
+        (side == 0 ? gr >= 5 : gr <= 4))
+      return true;
+  }
+  return false;
+}
+
 }  // namespace
 
 extern "C" {
+
+int cnnue_az_policy_moves(const int8_t* board, int side, const uint8_t* moves, int n_moves, uint32_t* info) {
+  if (!moves || !info || n_moves < 0) return set_error(CNNUE_ERR_INVALID_ARG, "null moves or info");
+  if (side != 0 && side != 1) return set_error(CNNUE_ERR_INVALID_ARG, "side %d", side);
+  if (int st = check_board(board)) return st;
+  static const std::vector<uint16_t> s2d = [] {
+    std::vector<uint16_t> v(kSq * kSq, 0xffff);
+    const auto& d = dense_moves();
+    for (size_t i = 0; i < d.size(); ++i) v[d[i]] = (uint16_t)i;
+    return v;
+  }();
+  uint8_t opp[kSq], own[kSq];
+  attacked_squares(board, 1 - side, opp);
+  attacked_squares(board, side, own);
+  int us, them;
+  buckets_of(board, side, &us, &them);
+  int status = CNNUE_OK;
+  for (int i = 0; i < n_moves; ++i) {
+    const int from = moves[2 * i], to = moves[2 * i + 1];
+    if (from >= kSq || to >= kSq || board[from] == 0) {
+      status = set_error(CNNUE_ERR_INVALID_ARG, "move %d: %d -> %d has no piece to move", i, from, to);
+      info[2 * i] = info[2 * i + 1] = 0xffffffffu;
+      continue;
+    }
+    const int cf = canonical_square(side, from), ct = canonical_square(side, to);
+    const uint32_t dense = s2d[cf * kSq + ct];
+    const int moved = (color_of(board[from]) == side ? 0 : 7) + kind_of(board[from]);
+    const int captured = board[to] != 0 ? (color_of(board[to]) == side ? 0 : 7) + kind_of(board[to]) : 15;
+    const uint32_t sig = (uint32_t)opp[from] | (uint32_t)opp[to] << 1 | (uint32_t)own[from] << 2 |
+                         (uint32_t)own[to] << 3 | (uint32_t)(board[to] != 0) << 4 |
+                         (uint32_t)gives_check(board, side, from, to) << 5;
+    info[2 * i] = (dense == 0xffff ? 0xfffu : dense) | (uint32_t)moved << 12 | (uint32_t)captured << 16 | sig << 20;
+    info[2 * i + 1] = (uint32_t)cf | (uint32_t)ct << 7 | (uint32_t)us << 14 | (uint32_t)them << 18;
+  }
+  return status;
+}
 
 int cnnue_az_threat_vocab(void) { return (int)threat_map().vocab; }
 

@@ -17,6 +17,9 @@ struct cnnue_az_weights {
   float scale[4] = {1.f, 1.f, 1.f, 1.f};
   int value_threat_active = 0;
   int policy_tactical_active = 0;
+  // fill_policy_piece_square_scores (src/az.rs:2189-2199): input_hidden row
+  // prefix . policy_consequence_output, one score per piece-square feature.
+  std::vector<float> ps_scores;
 };
 
 namespace cnnue {

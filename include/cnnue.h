@@ -345,6 +345,18 @@ int cnnue_az_threat_features(const int8_t* board, int perspective, uint32_t* fea
  * the reference's; the reference asserts the same count). */
 int cnnue_az_threat_vocab(void);
 
+/* Per-move records for the policy logits (the per-move inputs of
+ * evaluate_prepared_hidden_with_context, src/az.rs:1766-1887), side to move
+ * `side`.  moves[2i], moves[2i+1] = from, to squares (absolute).  info[2i] =
+ * dense move index of the canonical move (12 bits, 0xfff when not in the
+ * dense space) | moved piece index << 12 | captured piece index << 16 (15 =
+ * none) | tactical signature << 20 (bits: from attacked by the opponent, to
+ * attacked, from defended, to defended, capture, gives check:
+ * attacked_squares_mask, src/xiangqi/mod.rs:391-484, and
+ * gives_check_after_move_fast, :763-1012); info[2i+1] = canonical from |
+ * canonical to << 7 | us bucket << 14 | them bucket << 18. */
+int cnnue_az_policy_moves(const int8_t* board, int side, const uint8_t* moves, int n_moves, uint32_t* info);
+
 /* Host weights: the 22 fp32 tensors of az_weight_tensors! (src/az.rs:241-278)
  * in that order, row-major. */
 typedef struct cnnue_az_weights cnnue_az_weights;
@@ -457,6 +469,27 @@ int cnnue_az_value(const cnnue_az_model* model, const float* d_acc, const uint8_
 int cnnue_az_threat_logits(const cnnue_az_model* model, const uint32_t* d_features, uint32_t n_features,
                            const uint32_t* d_offsets, int64_t n, float* d_logits, void* d_workspace,
                            size_t workspace_bytes, void* stream);
+
+/* The evaluator entry point evaluate_incremental_with_scratch_output
+ * (src/az.rs:1606-1652) for n positions: side-to-move hidden from d_acc (+
+ * rule context), ReLU, RMSNorm, value head with the threat logits of
+ * d_threat_features (CSR; used when the model's value_threat_active is set)
+ * -> d_wdl [n][3], d_q [n]; then, when d_move_info is given, the policy
+ * logits of the listed moves (records of cnnue_az_policy_moves, CSR by
+ * d_move_offsets) from the side-to-move policy accumulators d_policy_acc
+ * (int16 [n][32], or [n][2][32] with d_side) -> d_logits [n_moves]
+ * (evaluate_prepared_hidden_with_scratch + _with_context, src/az.rs:
+ * 1738-1887: move bias + piece-square consequence + context . move context
+ * + quantised accumulator + folded sparse table + tactical table, summed in
+ * that order).  The workspace holds the normalised hidden and the threat
+ * activations between the kernels. */
+size_t cnnue_az_evaluate_workspace_bytes(const cnnue_az_model* model, int64_t n);
+int cnnue_az_evaluate(const cnnue_az_model* model, const float* d_acc, const uint8_t* d_side,
+                      const float* d_rule, const uint32_t* d_threat_features, uint32_t n_threat_features,
+                      const uint32_t* d_threat_offsets, const int16_t* d_policy_acc,
+                      const uint32_t* d_move_info, uint32_t n_moves, const uint32_t* d_move_offsets,
+                      int64_t n, float* d_wdl, float* d_q, float* d_logits, void* d_workspace,
+                      size_t workspace_bytes, void* stream);
 
 /* int16 policy accumulators [n_lists][32] (quantized_policy_accumulator,
  * src/az.rs:2344-2365): the bias row, then for every item its 6 rows of the

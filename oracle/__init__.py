@@ -196,7 +196,7 @@ def _az_setup(h):
     h.oracle_az_refresh.restype = i32
     h.oracle_az_transition.argtypes = [P, P, i32, P, P, P, P, P, i64, P]
     h.oracle_az_transition.restype = i32
-    h.oracle_az_value.argtypes = [P, P, P, P, i32, P, P, P, i64, P, P]
+    h.oracle_az_value.argtypes = [P, P, P, P, i32, P, P, P, i64, P, P, P]
     h.oracle_az_value.restype = None
     h._az_ready = True
 
@@ -252,17 +252,21 @@ def az_transition(tensors, hidden: int, parent: np.ndarray, delta: np.ndarray, r
     return st, child[:n_lists]
 
 
-def az_value(tensors, hidden: int, hidden_rows: np.ndarray, rule=None, threat=None):
-    """(wdl [n][3], q [n]) from side-to-move accumulators [n][H]."""
+def az_value(tensors, hidden: int, hidden_rows: np.ndarray, rule=None, threat=None, with_x: bool = False):
+    """(wdl [n][3], q [n]) from side-to-move accumulators [n][H]; with_x adds
+    the normalised hidden [n][H] the policy head reads."""
     n = hidden_rows.shape[0]
     wdl = np.zeros((max(n, 1), 3), np.float32)
     q = np.zeros(max(n, 1), np.float32)
+    x = np.zeros((max(n, 1), hidden), np.float32) if with_x else None
     f = [np.ascontiguousarray(np.asarray(tensors[i], np.float32).reshape(-1)) for i in (5, 7, 8, 9)]
     r = None if rule is None else np.ascontiguousarray(rule, np.float32)
     t = None if threat is None else np.ascontiguousarray(threat, np.float32)
     _az().oracle_az_value(_p(f[0]), _p(f[1]), _p(f[2]), _p(f[3]), hidden,
                           _p(np.ascontiguousarray(hidden_rows, np.float32)), None if r is None else _p(r),
-                          None if t is None else _p(t), n, _p(wdl), _p(q))
+                          None if t is None else _p(t), n, _p(wdl), _p(q), _p(x) if with_x else None)
+    if with_x:
+        return wdl[:n], q[:n], x[:n]
     return wdl[:n], q[:n]
 
 
@@ -359,7 +363,12 @@ def _azt():
         h.oracle_az_threat_features.argtypes = [C.c_void_p, C.c_int, C.c_void_p]
         h.oracle_az_threat_features.restype = C.c_int
         h.oracle_az_threat_logits.argtypes = [C.c_void_p, C.c_float, C.c_void_p, C.c_void_p, C.c_void_p,
-                                              C.c_int64, C.c_void_p]
+                                              C.c_int64, C.c_void_p, C.c_void_p]
+        h.oracle_az_policy_moves.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_void_p]
+        h.oracle_az_policy_moves.restype = C.c_int
+        h.oracle_az_policy_logits.argtypes = [C.c_void_p, C.c_int] + [C.c_void_p] * 5 + [C.c_int] + \
+            [C.c_void_p] * 5 + [C.c_int64, C.c_void_p]
+        h.oracle_az_policy_logits.restype = C.c_int
         h.oracle_az_threat_logits.restype = C.c_int
         h._azt_ready = True
     return h
@@ -375,11 +384,40 @@ def az_threat_features(board: np.ndarray, side: int) -> np.ndarray:
     return out[:n].copy()
 
 
-def az_threat_logits(table: np.ndarray, scale: float, out_w: np.ndarray, features: np.ndarray, offsets: np.ndarray):
+def az_threat_logits(table: np.ndarray, scale: float, out_w: np.ndarray, features: np.ndarray, offsets: np.ndarray,
+                     with_act: bool = False):
     n = len(offsets) - 1
     logits = np.zeros((max(n, 1), 3), np.float32)
+    act = np.zeros((max(n, 1), 128), np.float32) if with_act else None
     f = np.ascontiguousarray(features, np.uint32) if len(features) else np.zeros(1, np.uint32)
     st = _azt().oracle_az_threat_logits(_p(np.ascontiguousarray(table, np.int8)), scale,
                                         _p(np.ascontiguousarray(out_w, np.float32)), _p(f),
-                                        _p(np.ascontiguousarray(offsets, np.uint32)), n, _p(logits))
+                                        _p(np.ascontiguousarray(offsets, np.uint32)), n, _p(logits),
+                                        _p(act) if with_act else None)
+    if with_act:
+        return st, logits[:n], act[:n]
     return st, logits[:n]
+
+
+def az_policy_moves(board: np.ndarray, side: int, moves: np.ndarray) -> np.ndarray:
+    mv = np.ascontiguousarray(moves, np.uint8).reshape(-1, 2)
+    info = np.zeros((max(len(mv), 1), 2), np.uint32)
+    _azt().oracle_az_policy_moves(_p(np.ascontiguousarray(board, np.int8)), side, _p(mv), len(mv), _p(info))
+    return info[:len(mv)]
+
+
+def az_policy_logits(tensors, hidden: int, quant: dict, tactical_active: bool, x, act, pacc, info, offsets):
+    """Per-move policy logits restated (quant = az_quantize's output)."""
+    flat = [np.ascontiguousarray(np.asarray(t, np.float32).reshape(-1)) for t in tensors]
+    ptrs = (C.c_void_p * 22)(*[a.ctypes.data for a in flat])
+    n = len(offsets) - 1
+    logits = np.zeros(max(int(offsets[-1]), 1), np.float32)
+    _azt().oracle_az_policy_logits(ptrs, hidden, _p(quant["policy_move"]), _p(quant["policy_sparse"]),
+                                   _p(quant["moved_delta"]), _p(quant["capture"]),
+                                   _p(np.ascontiguousarray(quant["scales"], np.float32)), int(tactical_active),
+                                   _p(np.ascontiguousarray(x, np.float32)),
+                                   None if act is None else _p(np.ascontiguousarray(act, np.float32)),
+                                   _p(np.ascontiguousarray(pacc, np.int16)),
+                                   _p(np.ascontiguousarray(info, np.uint32)),
+                                   _p(np.ascontiguousarray(offsets, np.uint32)), n, _p(logits))
+    return logits[:int(offsets[-1])]

@@ -727,7 +727,7 @@ int oracle_az_transition(const float* table, const float* bias, int h, const flo
  * [n][3] may be NULL. */
 void oracle_az_value(const float* rule_rows, const float* vh, const float* vb, const float* vo, int h,
                      const float* hidden, const float* rule, const float* threat, int64_t n,
-                     float* wdl, float* q) {
+                     float* wdl, float* q, float* x_out) {
   float x[4096], v[AZ_VALUE];
   if (h > 4096) return;
   for (int64_t p = 0; p < n; ++p) {
@@ -745,6 +745,7 @@ void oracle_az_value(const float* rule_rows, const float* vh, const float* vb, c
     }
     const float inv = 1.f / sqrtf(ss / (float)h + 1e-6f);
     for (int j = 0; j < h; ++j) x[j] *= inv;
+    if (x_out) memcpy(x_out + p * h, x, sizeof(float) * h);
     for (int k = 0; k < AZ_VALUE; ++k) {
       float s = vb[k];
       for (int j = 0; j < h; ++j) s += vh[k * h + j] * x[j];
@@ -1231,7 +1232,7 @@ int oracle_az_threat_features(const int8_t* b, int persp, uint32_t* out) {
 
 /* value_threat_logits activation and output (src/az.rs:2103-2119). */
 int oracle_az_threat_logits(const int8_t* table, float scale, const float* out_w, const uint32_t* features,
-                            const uint32_t* offsets, int64_t n, float* logits) {
+                            const uint32_t* offsets, int64_t n, float* logits, float* act_out) {
   int status = 0;
   for (int64_t p = 0; p < n; ++p) {
     int16_t acc[64];
@@ -1248,6 +1249,235 @@ int oracle_az_threat_logits(const int8_t* table, float scale, const float* out_w
       act[64 + j] = v * v;
     }
     for (int o = 0; o < 3; ++o) logits[p * 3 + o] = az_dot(act, out_w + o * 128, 128);
+    if (act_out) memcpy(act_out + p * 128, act, sizeof(act));
   }
   return status;
+}
+
+/* ---- AZ-NNUE policy logits (reference-native) --------------------------- */
+static int az_gen(const int8_t* b, int color) {
+  int g = -1;
+  for (int sq = 0; sq < 90; ++sq)
+    if (b[sq] == (color == 0 ? 1 : -1)) g = sq;
+  return g;
+}
+
+/* attacked_squares_mask (src/xiangqi/mod.rs:391-484) as flags. */
+static void az_attacked(const int8_t* b, int by, uint8_t* m) {
+  memset(m, 0, 90);
+#define INB(x, y) ((x) >= 0 && (x) < 9 && (y) >= 0 && (y) < 10)
+  const int eg = az_gen(b, 1 - by);
+  for (int s = 0; s < 90; ++s) {
+    const int v = b[s];
+    if (!v || (v > 0 ? 0 : 1) != by) continue;
+    const int k = (v > 0 ? v : -v) - 1, f = s % 9, r = s / 9;
+    if (k == 0 || k == 1) {
+      for (int df = -1; df <= 1; ++df)
+        for (int dr = -1; dr <= 1; ++dr) {
+          const int ortho = (df == 0) != (dr == 0), diag = df != 0 && dr != 0;
+          if (!(k == 0 ? ortho : diag)) continue;
+          const int tf = f + df, tr = r + dr;
+          if (INB(tf, tr) && tf >= 3 && tf <= 5 && (by == 0 ? tr >= 7 : tr <= 2)) m[tr * 9 + tf] = 1;
+        }
+      if (k == 0 && eg >= 0 && eg % 9 == f) {
+        int clear = 1;
+        const int lo = r < eg / 9 ? r : eg / 9, hi = r < eg / 9 ? eg / 9 : r;
+        for (int rr = lo + 1; rr < hi; ++rr) clear &= b[rr * 9 + f] == 0;
+        if (clear) m[eg] = 1;
+      }
+    } else if (k == 2) {
+      for (int df = -2; df <= 2; df += 4)
+        for (int dr = -2; dr <= 2; dr += 4) {
+          const int tf = f + df, tr = r + dr;
+          if (INB(tf, tr) && (by == 0 ? tr >= 5 : tr <= 4) && !b[(r + dr / 2) * 9 + f + df / 2]) m[tr * 9 + tf] = 1;
+        }
+    } else if (k == 3) {
+      static const int h[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                  {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+      for (int i = 0; i < 8; ++i)
+        if (INB(f + h[i][2], r + h[i][3]) && !b[(r + h[i][1]) * 9 + f + h[i][0]]) m[(r + h[i][3]) * 9 + f + h[i][2]] = 1;
+    } else if (k == 4 || k == 5) {
+      static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+      for (int i = 0; i < 4; ++i) {
+        int tf = f + o[i][0], tr = r + o[i][1], seen = 0;
+        for (; INB(tf, tr); tf += o[i][0], tr += o[i][1]) {
+          const int occ = b[tr * 9 + tf] != 0;
+          if (k == 4) {
+            m[tr * 9 + tf] = 1;
+            if (occ) break;
+          } else {
+            if (seen) m[tr * 9 + tf] = 1;
+            if (occ) {
+              if (seen) break;
+              seen = 1;
+            }
+          }
+        }
+      }
+    } else {
+      const int fwd = by == 0 ? -1 : 1;
+      if (INB(f, r + fwd)) m[(r + fwd) * 9 + f] = 1;
+      if (by == 0 ? r <= 4 : r >= 5) {
+        if (INB(f - 1, r)) m[r * 9 + f - 1] = 1;
+        if (INB(f + 1, r)) m[r * 9 + f + 1] = 1;
+      }
+    }
+  }
+}
+
+/* gives_check_after_move_fast (src/xiangqi/mod.rs:763-1012). */
+static int az_vocc(const int8_t* b, int from, int to, int sq) { return sq == from ? 0 : (sq == to ? b[from] : b[sq]); }
+static int az_between(const int8_t* b, int from, int to, int a, int c) {
+  int n = 0;
+  if (a % 9 == c % 9) {
+    for (int r = (a < c ? a : c) / 9 + 1; r < (a < c ? c : a) / 9; ++r) n += az_vocc(b, from, to, r * 9 + a % 9) != 0;
+    return n;
+  }
+  if (a / 9 == c / 9) {
+    const int lo = a % 9 < c % 9 ? a % 9 : c % 9, hi = a % 9 < c % 9 ? c % 9 : a % 9;
+    for (int f = lo + 1; f < hi; ++f) n += az_vocc(b, from, to, (a / 9) * 9 + f) != 0;
+    return n;
+  }
+  return 1000;
+}
+
+static int az_gives_check(const int8_t* b, int side, int from, int to) {
+  const int g = az_gen(b, 1 - side);
+  if (g < 0 || !b[from]) return 0;
+  const int mv = b[from], color = mv > 0 ? 0 : 1, kind = (mv > 0 ? mv : -mv) - 1;
+  const int pf = to % 9, pr = to / 9, gf = g % 9, gr = g / 9, df = gf - pf, dr = gr - pr;
+  const int adf = df < 0 ? -df : df, adr = dr < 0 ? -dr : dr;
+  int hit = 0;
+  if (kind == 0) {
+    const int og = az_vocc(b, from, to, g);
+    hit = (adf + adr == 1 && gf >= 3 && gf <= 5 && (color == 0 ? gr >= 7 : gr <= 2)) ||
+          (pf == gf && og && (og > 0 ? og : -og) == 1 && (og > 0 ? 0 : 1) != color && az_between(b, from, to, to, g) == 0);
+  } else if (kind == 1) {
+    hit = adf == 1 && adr == 1 && gf >= 3 && gf <= 5 && (color == 0 ? gr >= 7 : gr <= 2);
+  } else if (kind == 2) {
+    hit = adf == 2 && adr == 2 && (color == 0 ? gr >= 5 : gr <= 4) && !az_vocc(b, from, to, ((pr + gr) / 2) * 9 + (pf + gf) / 2);
+  } else if (kind == 3) {
+    static const int h[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                                {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+    for (int i = 0; i < 8; ++i)
+      if (df == h[i][2] && dr == h[i][3]) {
+        hit = !az_vocc(b, from, to, (pr + h[i][1]) * 9 + pf + h[i][0]);
+        break;
+      }
+  } else if (kind == 4) {
+    hit = (pf == gf || pr == gr) && az_between(b, from, to, to, g) == 0;
+  } else if (kind == 5) {
+    hit = (pf == gf || pr == gr) && az_between(b, from, to, to, g) == 1;
+  } else {
+    hit = (gf == pf && gr == pr + (color == 0 ? -1 : 1)) || ((color == 0 ? gr <= 4 : gr >= 5) && gr == pr && adf == 1);
+  }
+  if (hit) return 1;
+  static const int o[4][2] = {{1, 0}, {-1, 0}, {0, 1}, {0, -1}};
+  for (int i = 0; i < 4; ++i) {
+    const int odf = o[i][0], odr = o[i][1];
+    const int on_from = odr == 0 ? (from / 9 == gr && (from % 9 - gf) * odf > 0) : (from % 9 == gf && (from / 9 - gr) * odr > 0);
+    const int on_to = odr == 0 ? (to / 9 == gr && (to % 9 - gf) * odf > 0) : (to % 9 == gf && (to / 9 - gr) * odr > 0);
+    if (!on_from && !on_to) continue;
+    int screen = 0;
+    for (int nf = gf + odf, nr = gr + odr; INB(nf, nr); nf += odf, nr += odr) {
+      const int p = az_vocc(b, from, to, nr * 9 + nf);
+      if (!p) continue;
+      const int pc = p > 0 ? 0 : 1, pk = (p > 0 ? p : -p) - 1;
+      if (!screen) {
+        if (pc == side && (pk == 4 || (pk == 0 && odf == 0))) return 1;
+        screen = 1;
+      } else if (pc == side && pk == 5) {
+        return 1;
+      } else {
+        break;
+      }
+    }
+  }
+  static const int h[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
+                              {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
+  for (int i = 0; i < 8; ++i) {
+    const int of = gf - h[i][2], orr = gr - h[i][3];
+    if (!INB(of, orr) || !INB(of + h[i][0], orr + h[i][1])) continue;
+    const int p = az_vocc(b, from, to, orr * 9 + of);
+    if ((orr + h[i][1]) * 9 + of + h[i][0] == from && p == (side == 0 ? 4 : -4)) return 1;
+  }
+  static const int e[4][4] = {{1, 1, 2, 2}, {1, -1, 2, -2}, {-1, 1, -2, 2}, {-1, -1, -2, -2}};
+  for (int i = 0; i < 4; ++i) {
+    const int of = gf - e[i][2], orr = gr - e[i][3];
+    if (!INB(of, orr) || !INB(of + e[i][0], orr + e[i][1])) continue;
+    const int p = az_vocc(b, from, to, orr * 9 + of);
+    if ((orr + e[i][1]) * 9 + of + e[i][0] == from && p == (side == 0 ? 3 : -3) && (side == 0 ? gr >= 5 : gr <= 4)) return 1;
+  }
+#undef INB
+  return 0;
+}
+
+/* The per-move records of cnnue_az_policy_moves, restated. */
+int oracle_az_policy_moves(const int8_t* b, int side, const uint8_t* moves, int n, uint32_t* info) {
+  uint16_t d2s[2086], s2d[8100];
+  oracle_az_dense_moves(d2s);
+  for (int i = 0; i < 8100; ++i) s2d[i] = 0xffff;
+  for (int i = 0; i < 2086; ++i) s2d[d2s[i]] = (uint16_t)i;
+  uint8_t opp[90], own[90];
+  az_attacked(b, 1 - side, opp);
+  az_attacked(b, side, own);
+  uint32_t items[90];
+  const int cnt = oracle_az_features(b, side, items);
+  const uint32_t us = cnt ? (items[0] >> 11) & 15 : 4, them = cnt ? (items[0] >> 15) & 15 : 4;
+  for (int i = 0; i < n; ++i) {
+    const int from = moves[2 * i], to = moves[2 * i + 1];
+    const int cf = side == 0 ? from : 89 - from, ct = side == 0 ? to : 89 - to;
+    const int v = b[from], c = b[to];
+    const uint32_t dense = s2d[cf * 90 + ct] == 0xffff ? 0xfffu : s2d[cf * 90 + ct];
+    const uint32_t moved = (uint32_t)(((v > 0 ? 0 : 1) == side ? 0 : 7) + (v > 0 ? v : -v) - 1);
+    const uint32_t cap = c ? (uint32_t)(((c > 0 ? 0 : 1) == side ? 0 : 7) + (c > 0 ? c : -c) - 1) : 15u;
+    const uint32_t sig = opp[from] | opp[to] << 1 | own[from] << 2 | own[to] << 3 | (c != 0) << 4 |
+                         (uint32_t)az_gives_check(b, side, from, to) << 5;
+    info[2 * i] = dense | moved << 12 | cap << 16 | sig << 20;
+    info[2 * i + 1] = (uint32_t)cf | (uint32_t)ct << 7 | us << 14 | them << 18;
+  }
+  return 0;
+}
+
+/* evaluate_prepared_hidden_with_context (src/az.rs:1766-1887) per move.
+ * t = the 22 tensors; q = the oracle's quantised tables (feature, move,
+ * sparse, moved delta, capture); x [n][h] normalised hidden; act [n][128]
+ * threat activations or NULL; pacc [n][32]. */
+int oracle_az_policy_logits(const float* const* t, int h, const int8_t* move_q, const int8_t* sparse_q,
+                            const int32_t* mdelta, const int32_t* mcap, const float* scales, int tactical_active,
+                            const float* x, const float* act, const int16_t* pacc, const uint32_t* info,
+                            const uint32_t* offsets, int64_t n, float* logits) {
+  float ps[1260];
+  const int cs = h < 32 ? h : 32;
+  for (int f = 0; f < 1260; ++f) ps[f] = az_dot(t[0] + (int64_t)f * h, t[14], cs);
+  for (int64_t p = 0; p < n; ++p) {
+    float ctx[16];
+    for (int c = 0; c < 16; ++c) {
+      ctx[c] = az_dot(x + p * h, t[15] + (int64_t)c * h, h);
+      if (act) ctx[c] += az_dot(act + p * 128, t[12] + c * 128, 128);
+    }
+    for (uint32_t j = offsets[p]; j < offsets[p + 1]; ++j) {
+      const uint32_t w0 = info[2 * j], w1 = info[2 * j + 1];
+      const uint32_t dense = w0 & 0xfff, moved = (w0 >> 12) & 15, cap = (w0 >> 16) & 15, sig = (w0 >> 20) & 63;
+      const uint32_t cf = w1 & 127, ct = (w1 >> 7) & 127, us = (w1 >> 14) & 15, them = (w1 >> 18) & 15;
+      float psl = ps[moved * 90 + ct] - ps[moved * 90 + cf];
+      psl = psl - (cap < 14 ? ps[cap * 90 + ct] : 0.f);
+      const float cdot = az_dot(ctx, t[16] + dense * 16, 16);
+      int32_t v = 0;
+      for (int k = 0; k < 32; ++k) v += (int32_t)pacc[p * 32 + k] * (int32_t)move_q[dense * 32 + k];
+      v += mdelta[dense * 14 + moved];
+      if (cap < 14) v -= mcap[dense * 14 + cap];
+      const float accl = (float)v * scales[0] * scales[1];
+      const int64_t main = (((int64_t)dense * 14 + moved) * 9 + us) * 9 + them;
+      const int64_t capi = 2086LL * 14 * 81 + dense * 15 + (cap < 14 ? cap : 14);
+      const float sparse = (float)((int32_t)sparse_q[main] + (int32_t)sparse_q[capi]) * scales[2];
+      float tactical = 0.f;
+      if (tactical_active) {
+        const int64_t exact = ((int64_t)dense * 7 + moved) * 64 + sig, factor = 2086LL * 7 * 64 + moved * 64 + sig;
+        tactical = t[21][exact] + t[21][factor];
+      }
+      logits[j] = t[13][dense] + psl + cdot + accl + sparse + tactical;
+    }
+  }
+  return 0;
 }

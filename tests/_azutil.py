@@ -45,3 +45,16 @@ def trained_policy(weights: "az.AzWeights", seed: int) -> None:
         t = weights.tensor(name)
         t[...] = rng.standard_normal(t.shape).astype(np.float32) * np.float32(scale)
     weights.quantize()
+
+
+def full_policy(weights: "az.AzWeights", seed: int) -> None:
+    """Seeded values for every policy-head and threat tensor, so each term of
+    the policy logit and both optional branches (threat, tactical) are live."""
+    rng = np.random.default_rng(seed)
+    for name, scale in (("policy_move_bias", 0.3), ("policy_consequence_output", 0.3),
+                        ("policy_move_context", 0.3), ("policy_accumulator_move", 1.0),
+                        ("policy_sparse_table", 0.1), ("policy_sparse_factor", 0.1), ("policy_tactical", 0.2),
+                        ("value_threat_output", 0.5), ("policy_threat_context", 0.2)):
+        t = weights.tensor(name)
+        t[...] = rng.standard_normal(t.shape).astype(np.float32) * np.float32(scale)
+    weights.quantize()

@@ -335,3 +335,37 @@ def test_threat_features_match_oracle_on_random_boards():
             got = az.threat_features(b, side)
             np.testing.assert_array_equal(got, oracle.az_threat_features(b, side))
             assert (got < 57702).all()
+
+
+def _check_bit(fen, frm, to):
+    board, side = az.board_from_fen(fen)
+    mv = np.array([[frm, to]], np.uint8)
+    info = az.policy_moves(board, side, mv)
+    np.testing.assert_array_equal(info, oracle.az_policy_moves(board, side, mv))
+    return (int(info[0, 0]) >> 25) & 1
+
+
+def test_gives_check_known_answers():
+    """gives_check_after_move_fast (src/xiangqi/mod.rs:763-831) on hand-made
+    positions: a rook onto the general's open file, a cannon with exactly one
+    screen, the facing generals rule, and a quiet rook move."""
+    assert _check_bit("3k5/9/9/9/9/R8/9/9/9/4K4 w", 45, 48) == 1
+    assert _check_bit("3k5/9/9/9/9/R8/9/9/9/4K4 w", 45, 46) == 0
+    assert _check_bit("3k5/3p5/9/9/9/C8/9/9/9/4K4 w", 45, 48) == 1
+    assert _check_bit("3k5/9/9/9/9/9/9/9/9/4K4 w", 85, 84) == 1
+    # discovered: moving the screen away from a rook's file
+    assert _check_bit("3k5/9/9/9/3P5/9/9/3R5/9/4K4 w", 39, 40) == 1
+
+
+def test_policy_move_records_match_oracle():
+    rng = np.random.default_rng(2)
+    boards = az.random_boards(200, seed=21)
+    n = 0
+    for b in boards:
+        for side in (0, 1):
+            mv = az.pseudo_moves(b, side, rng, 25)
+            if len(mv) == 0:
+                continue
+            np.testing.assert_array_equal(az.policy_moves(b, side, mv), oracle.az_policy_moves(b, side, mv))
+            n += len(mv)
+    assert n > 5000

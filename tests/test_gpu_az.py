@@ -325,3 +325,46 @@ def test_threat_logits_bit_exact_and_value_with_threat():
         np.testing.assert_allclose(q.cpu().numpy(), r_q, atol=1e-4, rtol=0)
     finally:
         model.close()
+
+
+# ---- the full evaluator entry point (value + threat + policy logits) --------
+def test_evaluate_matches_oracle_with_every_branch_live():
+    from ._azutil import full_policy
+    w = az.AzWeights.random(128, 20260819)
+    trained_like(w, 61)
+    full_policy(w, 62)
+    assert w.quant_flags() == (True, True)
+    t = w.tensors()
+    quant = oracle.az_quantize(t, 128)
+    model = az.AzModel(w, device=0)
+    try:
+        rng = np.random.default_rng(63)
+        boards = az.random_boards(600, seed=64)
+        side = rng.integers(0, 2, len(boards)).astype(np.uint8)
+        acc = model.refresh(*[_dev(a) for a in az.node_lists(boards)])
+        pacc = model.policy_refresh(*[_dev(a) for a in az.node_lists(boards)])
+        tf, to = az.pack_lists([az.threat_features(b, int(s)) for b, s in zip(boards, side)])
+        move_lists = [az.pseudo_moves(b, int(s), rng, 40) for b, s in zip(boards, side)]
+        infos = [az.policy_moves(b, int(s), m) for b, s, m in zip(boards, side, move_lists)]
+        offs = np.zeros(len(boards) + 1, np.uint32)
+        offs[1:] = np.cumsum([len(i) for i in infos])
+        info = np.concatenate(infos).astype(np.uint32)
+        rule = (rng.random((len(boards), 7)) * (rng.random((len(boards), 7)) < 0.3)).astype(np.float32)
+        wdl, q, logits = model.evaluate(acc, side=_dev(side), rule=_dev(rule), threat_features=_dev(tf),
+                                        threat_offsets=_dev(to), policy_acc=pacc, move_info=_dev(info),
+                                        move_offsets=_dev(offs))
+        assert model.read_status() == 0
+        # oracle: threat logits + activations, value with the normalised hidden, policy logits
+        a = acc.cpu().numpy().reshape(len(boards), 2, 128)[np.arange(len(boards)), side]
+        pa = pacc.cpu().numpy().reshape(len(boards), 2, 32)[np.arange(len(boards)), side]
+        st, tl, act = oracle.az_threat_logits(quant["value_threat"], float(quant["scales"][3]), t[11], tf, to,
+                                              with_act=True)
+        r_wdl, r_q, x = oracle.az_value(t, 128, a, rule, tl, with_x=True)
+        r_logits = oracle.az_policy_logits(t, 128, quant, True, x, act, pa, info, offs)
+        np.testing.assert_allclose(q.cpu().numpy(), r_q, atol=1e-4, rtol=0)
+        np.testing.assert_allclose(wdl.cpu().numpy(), r_wdl, atol=1e-4, rtol=0)
+        g = logits.cpu().numpy()
+        assert np.abs(r_logits).max() > 1.0
+        np.testing.assert_allclose(g, r_logits, atol=1e-4, rtol=1e-5)
+    finally:
+        model.close()

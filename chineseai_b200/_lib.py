@@ -95,6 +95,7 @@ SIGNATURES = {
     "cnnue_rn_model_destroy": (c_int, [c_void_p]),
     "cnnue_rn_workspace_bytes": (c_size, [c_i64]),
     "cnnue_rn_forward": (c_int, [c_void_p, P, c_i64, P, P, P, P, c_size, P]),
+    "cnnue_rn_set_conv_kernel": (c_int, [c_void_p, c_int]),
     "cnnue_synth_rn_weights": (c_int, [c_u64] + [P] * 14),
     "cnnue_synth_rn_planes": (c_int, [c_u64, c_i64, P]),
     "cnnue_splitmix64_next": (c_u64, [C.POINTER(c_u64)]),

@@ -216,6 +216,217 @@ __global__ void __launch_bounds__(kConvThreads) rn_conv_kernel(const __grid_cons
   if (warp == 4) tc::tmem_dealloc(tmem, 128);
 }
 
+// ---- persistent variant: two M tiles per K block, double-buffered TMEM ----
+// One CTA per SM loops over pairs of 128-row tiles.  Per K block the loader
+// issues two A boxes (one per tile) and one B tile, so each 16 KB weight tile
+// feeds 8 MMAs; a 4-stage ring of 48 KB stages hides load latency, and the
+// two 256-column TMEM buffers let the epilogue of one pair overlap the main
+// loop of the next.  Warps: 0 loader, 1 MMA issuer (and TMEM owner), 2-5
+// edge fix-up (rows t and 128 + t), 6-13 epilogue (warps 6-9 the first tile,
+// 10-13 the second; TMEM lane quadrant w % 4), with the bias in shared memory
+// and each row's residual loads issued before its TMEM reads.
+constexpr int kPStages = 4;
+constexpr int kPThreads = 448;  // 14 warps
+
+struct PConvSmem {
+  alignas(1024) uint8_t a[kPStages][2][kTileBytes];
+  alignas(1024) uint8_t b[kPStages][kTileBytes];
+  uint64_t loaded[kPStages];
+  uint64_t ready[kPStages];
+  uint64_t empty[kPStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  float bias[CNNUE_RN_CHANNELS];
+  uint32_t tmem_base;
+  int abort;
+};
+
+template <int CIN>
+__global__ void __launch_bounds__(kPThreads, 1) rn_pconv_kernel(const __grid_constant__ CUtensorMap tmap_in,
+                                                               const uint8_t* __restrict__ wtiles,
+                                                               const float* __restrict__ bias,
+                                                               const __nv_bfloat16* __restrict__ resid,
+                                                               __nv_bfloat16* __restrict__ out, int M,
+                                                               uint32_t* status) {
+  constexpr int kKbPerTap = CIN / 64;
+  constexpr int kKb = 9 * kKbPerTap;
+  extern __shared__ uint8_t smem_raw[];
+  PConvSmem& sm = *reinterpret_cast<PConvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_pairs = (M + 2 * kTileM - 1) / (2 * kTileM);
+
+  if (warp == 1) {
+    tc::tmem_alloc(pipe::smem_addr(&sm.tmem_base), 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kPStages; ++s) {
+      pipe::mbar_init(&sm.loaded[s], 1);
+      pipe::mbar_init(&sm.ready[s], 128);
+      pipe::mbar_init(&sm.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      pipe::mbar_init(&sm.acc_full[b], 1);
+      pipe::mbar_init(&sm.acc_empty[b], 256);
+    }
+    sm.abort = 0;
+    pipe::mbar_init_fence();
+  }
+  if (tid < kC) sm.bias[tid] = bias[tid];
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---- loader
+    if (lane == 0) {
+      uint32_t g = 0;
+      for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x) {
+        const int m0 = pair * 2 * kTileM;
+        for (int kb = 0; kb < kKb; ++kb, ++g) {
+          const uint32_t s = g % kPStages, u = g / kPStages;
+          if (u > 0 && !pipe::mbar_wait(&sm.empty[s], (u - 1) & 1, &sm.abort, status)) goto done_load;
+          const int tap = kb / kKbPerTap, c0 = (kb % kKbPerTap) * 64;
+          const int shift = (tap / 3 - 1) * 9 + (tap % 3 - 1);
+          pipe::mbar_arrive_expect_tx(&sm.loaded[s], 3 * kTileBytes);
+          tc::tma_load_2d(pipe::smem_addr(sm.a[s][0]), &tmap_in, c0, m0 + shift, pipe::smem_addr(&sm.loaded[s]));
+          tc::tma_load_2d(pipe::smem_addr(sm.a[s][1]), &tmap_in, c0, m0 + kTileM + shift,
+                          pipe::smem_addr(&sm.loaded[s]));
+          pipe::bulk_copy_g2s(sm.b[s], wtiles + (size_t)kb * kTileBytes, kTileBytes, &sm.loaded[s]);
+        }
+      }
+    done_load:;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(128, 128);
+      uint32_t g = 0;
+      int it = 0;
+      for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x, ++it) {
+        const int buf = it & 1, use = it >> 1;
+        if (use > 0 && !pipe::mbar_wait(&sm.acc_empty[buf], (use - 1) & 1, &sm.abort, status)) break;
+        tc::fence_after_sync();
+        const uint32_t d0 = tmem + (uint32_t)(buf * 256), d1 = d0 + 128;
+        bool ok = true;
+        for (int kb = 0; kb < kKb; ++kb, ++g) {
+          const uint32_t s = g % kPStages, u = g / kPStages;
+          if (!pipe::mbar_wait(&sm.ready[s], u & 1, &sm.abort, status)) {
+            ok = false;
+            break;
+          }
+          tc::fence_after_sync();
+          const uint32_t a0 = pipe::smem_addr(sm.a[s][0]), a1 = pipe::smem_addr(sm.a[s][1]);
+          const uint32_t b0 = pipe::smem_addr(sm.b[s]);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bd = tc::smem_desc(b0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+            tc::mma_bf16(d0, tc::smem_desc(a0 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
+            tc::mma_bf16(d1, tc::smem_desc(a1 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
+          }
+          tc::commit(pipe::smem_addr(&sm.empty[s]));
+        }
+        tc::commit(pipe::smem_addr(&sm.acc_full[buf]));
+        if (!ok) break;
+      }
+    }
+    __syncwarp();
+  } else if (warp < 6) {
+    // ---- edge fix-up: rows t and 128 + t of the two A boxes
+    const int t = tid - 64;
+    int r[2], f[2];
+    bool live[2];
+    uint32_t g = 0;
+    for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int m = pair * 2 * kTileM + h * kTileM + t;
+        live[h] = m < M;
+        const int p = (live[h] ? m : 0) % kSq;
+        r[h] = p / 9;
+        f[h] = p - r[h] * 9;
+      }
+      bool ok = true;
+      for (int kb = 0; kb < kKb; ++kb, ++g) {
+        const uint32_t s = g % kPStages, u = g / kPStages;
+        if (!pipe::mbar_wait(&sm.loaded[s], u & 1, &sm.abort, status)) {
+          ok = false;
+          break;
+        }
+        const int tap = kb / kKbPerTap;
+        const int dr = tap / 3 - 1, df = tap % 3 - 1;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r2 = r[h] + dr, f2 = f[h] + df;
+          if (live[h] && (r2 < 0 || r2 > 9 || f2 < 0 || f2 > 8)) {
+            uint8_t* line = sm.a[s][h] + t * 128;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4*>(line + (((i + t) & 7) << 4)) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        pipe::fence_proxy_async_smem();
+        pipe::mbar_arrive(&sm.ready[s]);
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ---- epilogue: warps 6-9 tile 0, 10-13 tile 1; TMEM lane quadrant w % 4
+    const int h = (warp - 6) >> 2, q = warp & 3, row = q * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16);
+    int it = 0;
+    for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x, ++it) {
+      const int buf = it & 1, use = it >> 1;
+      const int m = pair * 2 * kTileM + h * kTileM + row;
+      // residual row first: its 16 loads overlap the accumulator wait
+      uint4 rv[16];
+      const bool in_range = m < M;
+      if (resid != nullptr && in_range) {
+        const uint4* rp = reinterpret_cast<const uint4*>(resid + (size_t)m * kC);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rv[i] = __ldg(rp + i);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) rv[i] = make_uint4(0u, 0u, 0u, 0u);
+      }
+      const bool ok = pipe::mbar_wait(&sm.acc_full[buf], use & 1, &sm.abort, status);
+      tc::fence_after_sync();
+      const bool active = ok && in_range;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t v[32];
+        __syncwarp();
+        tc::tmem_ld32(lane_addr + (uint32_t)(buf * 256 + h * 128 + 32 * j), v);
+        tc::wait_ld();
+        if (!active) continue;
+        uint32_t packed[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t rw = (&rv[4 * j].x)[i];
+          const float2 r2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw));
+          const float x0 = __uint_as_float(v[2 * i]) + sm.bias[32 * j + 2 * i] + r2.x;
+          const float x1 = __uint_as_float(v[2 * i + 1]) + sm.bias[32 * j + 2 * i + 1] + r2.y;
+          const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaxf(x0, 0.f), fmaxf(x1, 0.f));
+          packed[i] = *reinterpret_cast<const uint32_t*>(&h2);
+        }
+        uint4* op = reinterpret_cast<uint4*>(out + (size_t)m * kC + 32 * j);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq)
+          op[qq] = make_uint4(packed[4 * qq], packed[4 * qq + 1], packed[4 * qq + 2], packed[4 * qq + 3]);
+      }
+      tc::fence_before_sync();
+      pipe::mbar_arrive(&sm.acc_empty[buf]);
+      if (!ok) break;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
 // [B][15][90] bf16 planes -> [B*90][64] bf16, channels 15..63 zero.
 __global__ void rn_pack_kernel(const __nv_bfloat16* __restrict__ planes, int64_t B, __nv_bfloat16* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -405,6 +616,7 @@ void tile_conv(const float* w, int cin, int cin_pad, uint8_t* dst) {
 }
 
 size_t conv_smem_bytes() { return sizeof(ConvSmem) + 1024; }
+size_t pconv_smem_bytes() { return sizeof(PConvSmem) + 1024; }
 
 // cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -442,6 +654,8 @@ int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M) {
 
 struct cnnue_rn_model {
   int device = 0;
+  int sms = 148;
+  int persistent = 1;  // 1: rn_pconv_kernel, 0: the one-tile-per-CTA rn_conv_kernel
   void* blob = nullptr;
   uint8_t* tiles = nullptr;  // [kTotalKb][16 KB]
   float* conv_bias = nullptr;  // [21][128]
@@ -520,8 +734,16 @@ int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model*
     if ((e = cudaFuncSetAttribute(rn_conv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
             cudaSuccess ||
         (e = cudaFuncSetAttribute(rn_conv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)) !=
-            cudaSuccess)
+            cudaSuccess ||
+        (e = cudaFuncSetAttribute(rn_pconv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)pconv_smem_bytes())) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(rn_pconv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)pconv_smem_bytes())) != cudaSuccess)
       st = cuda_error(e, "cudaFuncSetAttribute(rn_conv_kernel)");
+    int sms = 0;
+    if (!st && (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
+      st = cuda_error(e, "cudaDeviceGetAttribute");
+    m->sms = sms > 0 ? sms : 148;
   }
   if (st) {
     cudaFree(m->blob);
@@ -586,18 +808,28 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   if (int st = make_act_map(&map_in, in64, 64, M)) return st;
   for (int i = 0; i < 3; ++i)
     if (int st = make_act_map(&map_act[i], act[i], kC, M)) return st;
-  rn_conv_kernel<64><<<tiles, kConvThreads, smem, s>>>(map_in, m->tiles, m->conv_bias, nullptr, act[0], M, status);
-  if (int st = check_launch_error("rn_conv_kernel<64>")) return st;
+  const int pairs = (M + 2 * kTileM - 1) / (2 * kTileM);
+  const unsigned pgrid = (unsigned)(pairs < m->sms ? pairs : m->sms);
+  const size_t psmem = pconv_smem_bytes();
+  auto conv = [&](bool stem, const CUtensorMap& map, int c, const __nv_bfloat16* resid, __nv_bfloat16* dst) {
+    const uint8_t* wt = m->tiles + conv_tile_offset(c) * kTileBytes;
+    const float* b = m->conv_bias + c * kC;
+    if (m->persistent) {
+      if (stem) rn_pconv_kernel<64><<<pgrid, kPThreads, psmem, s>>>(map, wt, b, resid, dst, M, status);
+      else rn_pconv_kernel<128><<<pgrid, kPThreads, psmem, s>>>(map, wt, b, resid, dst, M, status);
+    } else {
+      if (stem) rn_conv_kernel<64><<<tiles, kConvThreads, smem, s>>>(map, wt, b, resid, dst, M, status);
+      else rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map, wt, b, resid, dst, M, status);
+    }
+    return check_launch_error("rn conv");
+  };
+  if (int st = conv(true, map_in, 0, nullptr, act[0])) return st;
   int x = 0;
   for (int blk = 0; blk < CNNUE_RN_BLOCKS; ++blk) {
     const int h = (x + 1) % 3, y = (x + 2) % 3;
     const int c1 = 1 + 2 * blk, c2 = c1 + 1;
-    rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map_act[x], m->tiles + conv_tile_offset(c1) * kTileBytes,
-                                                         m->conv_bias + c1 * kC, nullptr, act[h], M, status);
-    if (int st = check_launch_error("rn_conv_kernel<128>")) return st;
-    rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map_act[h], m->tiles + conv_tile_offset(c2) * kTileBytes,
-                                                         m->conv_bias + c2 * kC, act[x], act[y], M, status);
-    if (int st = check_launch_error("rn_conv_kernel<128>")) return st;
+    if (int st = conv(false, map_act[x], c1, nullptr, act[h])) return st;
+    if (int st = conv(false, map_act[h], c2, act[x], act[y])) return st;
     x = y;
   }
   HeadArgs h = m->h;
@@ -613,6 +845,12 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   if (int st = check_launch_error("rn_policy_fc_kernel")) return st;
   rn_softmax_kernel<<<(unsigned)((batch + 7) / 8), 256, 0, s>>>(logits, batch, d_probs);
   return check_launch_error("rn_softmax_kernel");
+}
+
+int cnnue_rn_set_conv_kernel(cnnue_rn_model* m, int persistent) {
+  if (!m || (persistent != 0 && persistent != 1)) return set_error(CNNUE_ERR_INVALID_ARG, "model or kernel choice");
+  m->persistent = persistent;
+  return CNNUE_OK;
 }
 
 }  // extern "C"

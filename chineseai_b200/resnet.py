@@ -98,6 +98,10 @@ class ResNetModel:
     def handle(self):
         return self._h
 
+    def set_conv_kernel(self, persistent: bool) -> None:
+        """Chooses the persistent conv kernel (default) or the one-tile-per-CTA one."""
+        check(lib().cnnue_rn_set_conv_kernel(self._h, 1 if persistent else 0), "cnnue_rn_set_conv_kernel")
+
     def workspace(self, batch: int):
         need = int(lib().cnnue_rn_workspace_bytes(batch))
         if self._ws is None or self._ws.numel() < need:

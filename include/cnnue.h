@@ -552,6 +552,10 @@ size_t cnnue_rn_workspace_bytes(int64_t batch);
 int cnnue_rn_forward(const cnnue_rn_model* model, const uint16_t* d_planes, int64_t batch, float* d_probs,
                      float* d_logits, float* d_value, void* d_workspace, size_t workspace_bytes,
                      void* stream);
+/* Conv kernel choice: 1 (default) the persistent kernel (one CTA per SM, two
+ * 128-row tiles per K block sharing each weight tile, double-buffered TMEM),
+ * 0 the one-tile-per-CTA kernel.  Both compute the same results. */
+int cnnue_rn_set_conv_kernel(cnnue_rn_model* model, int persistent);
 
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is

@@ -56,6 +56,12 @@ SIGNATURES = {
     "cnnue_sparse_pool_fwd": (c_int, [P, c_i64, P, c_i64, c_i64, c_i64, P, P, P]),
     "cnnue_sparse_pool_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64]),
     "cnnue_sparse_pool_bwd": (c_int, [P, P, c_i64, c_i64, c_i64, c_i64, P, P, c_size, P]),
+    "cnnue_policy_fused_fwd": (c_int, [P, P, P, c_i64, c_i64, P, P, P]),
+    "cnnue_policy_fused_bwd_workspace_bytes": (c_size, [c_i64, c_i64]),
+    "cnnue_policy_fused_bwd": (c_int, [P, P, P, P, c_i64, c_i64, P, P, P, c_size, P]),
+    "cnnue_policy_table_fwd": (c_int, [P, c_i64, P, c_i64, c_int, P, P, P]),
+    "cnnue_policy_table_bwd_workspace_bytes": (c_size, [c_i64, c_int]),
+    "cnnue_policy_table_bwd": (c_int, [P, P, c_i64, c_int, c_i64, P, P, c_size, P]),
     "cnnue_t_param_count": (c_size, []),
     "cnnue_t_workspace_bytes": (c_size, [c_i64, c_u32]),
     "cnnue_t_make_shadow": (c_int, [P, P, P]),

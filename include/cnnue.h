@@ -257,6 +257,56 @@ int cnnue_sparse_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int6
                           int64_t batch, int64_t item_count, int64_t hidden, float* d_grad_table,
                           void* d_workspace, size_t workspace_bytes, void* stream);
 
+/* ---- AZ-NNUE policy-head training ops ------------------------------------
+ * fused_policy: one logit per (board, move slot) from the 182,886-float
+ * policy table (sections: consequence rows [1260][32] at 0, consequence
+ * weights [32] at 40320, move bias [2086] at 40352, move context [2086][16]
+ * at 42438, accumulator feature rows [1260][32] at 75814, accumulator move
+ * factors [2086][32] at 116134), the board context [B][48] (16 move-context
+ * values, then 32 accumulator values) and i64 items [B][M] packed as
+ * move | from << 12 | to << 23 | captured << 34 | move_valid << 45 |
+ * capture_valid << 46 | policy_valid << 47 (src/az/fused_policy.rs:10-35,
+ * :146-157).  Items without policy_valid give 0; an item whose move or
+ * feature indices fall outside their sections gives 0 and ORs
+ * CNNUE_STATUS_BAD_INDEX into *d_status.  Terms are added one product at a
+ * time in the CPU twin's order, so logits equal it bit for bit.
+ * Replaces FusedPolicy (src/az/fused_policy.rs:159-245, CPU twin :178-241). */
+#define CNNUE_POLICY_TABLE_LEN 182886
+#define CNNUE_POLICY_CONTEXT 48
+int cnnue_policy_fused_fwd(const float* d_tables, const float* d_context, const int64_t* d_items,
+                           int64_t batch, int64_t moves, float* d_out, uint32_t* d_status,
+                           void* stream);
+/* Backward of fused_policy: d_grad_tables [182886] and d_grad_context [B][48]
+ * are overwritten.  No atomics: grad_context[b] adds its board's moves in
+ * order; every table contribution is summed per entry in item order by a
+ * stable radix sort of (entry, contribution) pairs (entries hit by at most
+ * 256 contributions equal the CPU twin bit for bit, longer runs are summed in
+ * ordered units of 256).  Bad items are flagged in the workspace status.
+ * Synchronises the stream (the sort's run counts are read back).
+ * Replaces FusedPolicyGrad (src/az/fused_policy.rs:263-371, CPU twin :287-366,
+ * CUDA kernel fused_policy_grad :73-126, which uses atomicAdd). */
+size_t cnnue_policy_fused_bwd_workspace_bytes(int64_t batch, int64_t moves);
+int cnnue_policy_fused_bwd(const float* d_tables, const float* d_context, const int64_t* d_items,
+                           const float* d_grad_out, int64_t batch, int64_t moves, float* d_grad_tables,
+                           float* d_grad_context, void* d_workspace, size_t workspace_bytes,
+                           void* stream);
+
+/* Sparse / tactical policy table lookup: out[o] = sum over k < terms of
+ * table[indices[o * terms + k]] in order (terms = 7 for sparse_policy, 2 for
+ * tactical_policy); an index outside [0, table_len) is skipped and flagged.
+ * Replaces SparsePolicy (src/az/fused_sparse_policy.rs:56-110, CPU twin :86-107). */
+int cnnue_policy_table_fwd(const float* d_table, int64_t table_len, const int64_t* d_indices,
+                           int64_t outputs, int terms, float* d_out, uint32_t* d_status,
+                           void* stream);
+/* Its backward: d_grad_table[j] = sum of grad_out[o] over every (o, k) with
+ * indices[o * terms + k] == j, in (o, k) order, without atomics (the same
+ * sorted scatter as cnnue_policy_fused_bwd).  Replaces SparsePolicyGrad
+ * (src/az/fused_sparse_policy.rs:112-175, CPU twin :138-165). */
+size_t cnnue_policy_table_bwd_workspace_bytes(int64_t outputs, int terms);
+int cnnue_policy_table_bwd(const int64_t* d_indices, const float* d_grad_out, int64_t outputs,
+                           int terms, int64_t table_len, float* d_grad_table, void* d_workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* ---- training step (data parallel), HalfKA network --------------------- */
 /* One rank's step of the fp32-master / bf16-activation form of the quantised
  * network: FT 11340x1024 (bf16 shadow gathered, fp32 sums), pairwise product

@@ -39,11 +39,17 @@ def lib() -> C.CDLL:
         h.oracle_feature_pool_bwd.argtypes = [P, P, i64, i64, i64, P]
         h.oracle_sparse_pool_fwd.argtypes = [P, i64, P, i64, i64, i64, P]
         h.oracle_sparse_pool_bwd.argtypes = [P, P, i64, i64, i64, i64, P]
+        h.oracle_policy_fused_fwd.argtypes = [P, P, P, i64, i64, P]
+        h.oracle_policy_fused_bwd.argtypes = [P, P, P, P, i64, i64, P, P]
+        h.oracle_policy_table_fwd.argtypes = [P, i64, P, i64, i32, P]
+        h.oracle_policy_table_bwd.argtypes = [P, P, i64, i32, i64, P]
         h.oracle_q_bucket.argtypes = [u32]
         h.oracle_f_bucket.argtypes = [u32]
         for name in ("oracle_q_forward", "oracle_q_forward_mt", "oracle_q_update", "oracle_f_forward",
                      "oracle_feature_pool_fwd", "oracle_feature_pool_bwd", "oracle_sparse_pool_fwd",
                      "oracle_sparse_pool_bwd", "oracle_q_bucket", "oracle_f_bucket",
+                     "oracle_policy_fused_fwd", "oracle_policy_fused_bwd", "oracle_policy_table_fwd",
+                     "oracle_policy_table_bwd",
                      "oracle_max_threads"):
             getattr(h, name).restype = C.c_int
         _lib = h
@@ -125,6 +131,53 @@ def sparse_pool_bwd(items: np.ndarray, grad_out: np.ndarray, rows: int):
     hidden = grad_out.shape[1]
     grad = np.zeros((rows, hidden), np.float32)
     st = lib().oracle_sparse_pool_bwd(_p(items), _p(grad_out), rows, batch, item_count, hidden, _p(grad))
+    return st, grad
+
+
+POLICY_TABLE_LEN = 182886
+POLICY_CONTEXT = 48
+
+
+def policy_fused_fwd(tables: np.ndarray, context: np.ndarray, items: np.ndarray):
+    """FusedPolicy forward restated -> (status, logits [B][M])."""
+    batch, moves = items.shape
+    out = np.zeros((max(batch, 1), max(moves, 1)), np.float32)
+    st = lib().oracle_policy_fused_fwd(_p(np.ascontiguousarray(tables, np.float32)),
+                                       _p(np.ascontiguousarray(context, np.float32)),
+                                       _p(np.ascontiguousarray(items, np.int64)), batch, moves, _p(out))
+    return st, out[:batch, :moves]
+
+
+def policy_fused_bwd(tables: np.ndarray, context: np.ndarray, items: np.ndarray, grad_out: np.ndarray):
+    """FusedPolicyGrad restated -> (status, grad_tables [182886], grad_context [B][48])."""
+    batch, moves = items.shape
+    gt = np.zeros(POLICY_TABLE_LEN, np.float32)
+    gc = np.zeros((max(batch, 1), POLICY_CONTEXT), np.float32)
+    st = lib().oracle_policy_fused_bwd(_p(np.ascontiguousarray(tables, np.float32)),
+                                       _p(np.ascontiguousarray(context, np.float32)),
+                                       _p(np.ascontiguousarray(items, np.int64)),
+                                       _p(np.ascontiguousarray(grad_out, np.float32)), batch, moves, _p(gt),
+                                       _p(gc))
+    return st, gt, gc[:batch]
+
+
+def policy_table_fwd(table: np.ndarray, indices: np.ndarray):
+    """SparsePolicy forward restated; indices [..., terms] -> (status, out [...])."""
+    terms = indices.shape[-1]
+    flat = np.ascontiguousarray(indices, np.int64).reshape(-1, terms)
+    out = np.zeros(max(len(flat), 1), np.float32)
+    st = lib().oracle_policy_table_fwd(_p(np.ascontiguousarray(table, np.float32)), len(table), _p(flat),
+                                       len(flat), terms, _p(out))
+    return st, out[:len(flat)].reshape(indices.shape[:-1])
+
+
+def policy_table_bwd(indices: np.ndarray, grad_out: np.ndarray, table_len: int):
+    """SparsePolicyGrad restated -> (status, grad_table [table_len])."""
+    terms = indices.shape[-1]
+    flat = np.ascontiguousarray(indices, np.int64).reshape(-1, terms)
+    g = np.ascontiguousarray(grad_out, np.float32).reshape(-1)
+    grad = np.zeros(table_len, np.float32)
+    st = lib().oracle_policy_table_bwd(_p(flat), _p(g), len(flat), terms, table_len, _p(grad))
     return st, grad
 
 

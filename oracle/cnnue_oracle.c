@@ -19,6 +19,13 @@
  *                                   src/az/fused_feature_pool.rs:284-309, :342-370
  *     These are pinned against the reference tests' fixtures
  *     (src/az/fused_feature_pool.rs:611-686) in tests/test_oracle_pool.py.
+ *       oracle_policy_fused_fwd/bwd <- FusedPolicy / FusedPolicyGrad cpu_fwd
+ *                                   src/az/fused_policy.rs:178-241, :287-366
+ *       oracle_policy_table_fwd/bwd <- SparsePolicy / SparsePolicyGrad cpu_fwd
+ *                                   src/az/fused_sparse_policy.rs:86-107, :138-165
+ *     The fused policy twin is checked against the reference test's inputs
+ *     (src/az/fused_policy.rs:536-572) by hand-derived values in
+ *     tests/test_oracle_policy.py.
  *
  * (2) The quantised and fp32 HalfKA networks.  The reference has no code for
  *     them (it has neither an int16 FT nor a pairwise pack nor bucket stacks);
@@ -401,6 +408,153 @@ int oracle_sparse_pool_bwd(const uint32_t* items, const float* grad_out, int64_t
       if ((int64_t)item >= rows) { status = 2; continue; }
       for (int64_t h = 0; h < hidden; ++h)
         grad_table[(int64_t)item * hidden + h] += grad_out[b * hidden + h];
+    }
+  return status;
+}
+
+/* ---- policy-head training ops ------------------------------------------- */
+/* Item fields and table offsets, src/az/fused_policy.rs:10-35. */
+#define POL_TABLE_LEN 182886
+#define POL_CONSEQUENCE 40320
+#define POL_BIAS 40352
+#define POL_CONTEXT 42438
+#define POL_ACC_FEATURE 75814
+#define POL_ACC_MOVE 116134
+#define POL_CTX 48
+
+typedef struct {
+  int policy, move, capture;
+  int64_t mv, from, to, cap;
+} pol_item;
+
+static pol_item pol_decode(int64_t packed_s) {
+  uint64_t p = (uint64_t)packed_s;
+  pol_item it;
+  it.policy = (int)((p >> 47) & 1u);
+  it.move = (int)((p >> 45) & 1u);
+  it.capture = (int)((p >> 46) & 1u);
+  it.mv = (int64_t)(p & 0xfffu);
+  it.from = (int64_t)((p >> 12) & 0x7ffu);
+  it.to = (int64_t)((p >> 23) & 0x7ffu);
+  it.cap = (int64_t)((p >> 34) & 0x7ffu);
+  return it;
+}
+
+/* The Rust twin indexes its slices and panics past the end; here such an
+ * item is skipped and reported (status 2). */
+static int pol_in_range(const pol_item* it) {
+  return it->mv < 2086 && (!it->move || (it->from < 1260 && it->to < 1260 && (!it->capture || it->cap < 1260)));
+}
+
+/* FusedPolicy::cpu_fwd, src/az/fused_policy.rs:178-241. */
+int oracle_policy_fused_fwd(const float* t, const float* context, const int64_t* items, int64_t batch,
+                            int64_t moves, float* out) {
+  int status = 0;
+  for (int64_t i = 0; i < batch * moves; ++i) {
+    out[i] = 0.f;
+    pol_item it = pol_decode(items[i]);
+    if (!it.policy) continue;
+    if (!pol_in_range(&it)) { status = 2; continue; }
+    float value = t[POL_BIAS + it.mv];
+    if (it.move) {
+      const float* c = context + (i / moves) * POL_CTX;
+      for (int h = 0; h < 32; ++h) {
+        float delta = t[it.to * 32 + h] - t[it.from * 32 + h];
+        if (it.capture) delta -= t[it.cap * 32 + h];
+        value += delta * t[POL_CONSEQUENCE + h];
+      }
+      for (int h = 0; h < 16; ++h) value += c[h] * t[POL_CONTEXT + it.mv * 16 + h];
+      for (int h = 0; h < 32; ++h) {
+        float after = c[16 + h] + t[POL_ACC_FEATURE + it.to * 32 + h] - t[POL_ACC_FEATURE + it.from * 32 + h];
+        if (it.capture) after -= t[POL_ACC_FEATURE + it.cap * 32 + h];
+        value += after * t[POL_ACC_MOVE + it.mv * 32 + h];
+      }
+    }
+    out[i] = value;
+  }
+  return status;
+}
+
+/* FusedPolicyGrad::cpu_fwd, src/az/fused_policy.rs:287-366: one pass over the
+ * items in order, every contribution added as it is met. */
+int oracle_policy_fused_bwd(const float* t, const float* context, const int64_t* items, const float* grad_out,
+                            int64_t batch, int64_t moves, float* grad_t, float* grad_c) {
+  int status = 0;
+  for (int64_t i = 0; i < POL_TABLE_LEN; ++i) grad_t[i] = 0.f;
+  for (int64_t i = 0; i < batch * POL_CTX; ++i) grad_c[i] = 0.f;
+  for (int64_t i = 0; i < batch * moves; ++i) {
+    pol_item it = pol_decode(items[i]);
+    if (!it.policy) continue;
+    if (!pol_in_range(&it)) { status = 2; continue; }
+    const float g = grad_out[i];
+    grad_t[POL_BIAS + it.mv] += g;
+    if (!it.move) continue;
+    const int64_t b = i / moves;
+    const float* c = context + b * POL_CTX;
+    float* gc = grad_c + b * POL_CTX;
+    for (int h = 0; h < 32; ++h) {
+      const float w = t[POL_CONSEQUENCE + h];
+      float delta = t[it.to * 32 + h] - t[it.from * 32 + h];
+      grad_t[it.to * 32 + h] += g * w;
+      grad_t[it.from * 32 + h] -= g * w;
+      if (it.capture) {
+        delta -= t[it.cap * 32 + h];
+        grad_t[it.cap * 32 + h] -= g * w;
+      }
+      grad_t[POL_CONSEQUENCE + h] += g * delta;
+    }
+    for (int h = 0; h < 16; ++h) {
+      const int64_t ci = POL_CONTEXT + it.mv * 16 + h;
+      grad_t[ci] += g * c[h];
+      gc[h] += g * t[ci];
+    }
+    for (int h = 0; h < 32; ++h) {
+      const int64_t mf = POL_ACC_MOVE + it.mv * 32 + h;
+      const float w = t[mf];
+      const int64_t ti = POL_ACC_FEATURE + it.to * 32 + h, fi = POL_ACC_FEATURE + it.from * 32 + h;
+      float after = c[16 + h] + t[ti] - t[fi];
+      gc[16 + h] += g * w;
+      grad_t[ti] += g * w;
+      grad_t[fi] -= g * w;
+      if (it.capture) {
+        const int64_t cpi = POL_ACC_FEATURE + it.cap * 32 + h;
+        after -= t[cpi];
+        grad_t[cpi] -= g * w;
+      }
+      grad_t[mf] += g * after;
+    }
+  }
+  return status;
+}
+
+/* SparsePolicy::cpu_fwd, src/az/fused_sparse_policy.rs:86-107 (terms = 7 for
+ * the sparse table, 2 for the tactical one).  Rust's f32 Sum folds from
+ * -0.0, the exact additive identity. */
+int oracle_policy_table_fwd(const float* table, int64_t table_len, const int64_t* indices, int64_t outputs,
+                            int terms, float* out) {
+  int status = 0;
+  for (int64_t o = 0; o < outputs; ++o) {
+    float s = -0.f;
+    for (int k = 0; k < terms; ++k) {
+      const int64_t j = indices[o * terms + k];
+      if (j < 0 || j >= table_len) { status = 2; continue; }
+      s += table[j];
+    }
+    out[o] = s;
+  }
+  return status;
+}
+
+/* SparsePolicyGrad::cpu_fwd, src/az/fused_sparse_policy.rs:138-165. */
+int oracle_policy_table_bwd(const int64_t* indices, const float* grad_out, int64_t outputs, int terms,
+                            int64_t table_len, float* grad_table) {
+  int status = 0;
+  for (int64_t j = 0; j < table_len; ++j) grad_table[j] = 0.f;
+  for (int64_t o = 0; o < outputs; ++o)
+    for (int k = 0; k < terms; ++k) {
+      const int64_t j = indices[o * terms + k];
+      if (j < 0 || j >= table_len) { status = 2; continue; }
+      grad_table[j] += grad_out[o];
     }
   return status;
 }

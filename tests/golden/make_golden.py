@@ -5,7 +5,8 @@ seeds 1 and 2) by hashes of what they produce, and (b) the oracle's outputs
 on small batches of every path, so a change in either shows up as a fixture
 mismatch.  The feature-pool and sparse-pool cases use the exact fixtures of
 the reference's own tests (src/az/fused_feature_pool.rs:611-686: ramp tables,
-hand-packed items, gradient of sum_all).
+hand-packed items, gradient of sum_all); the fused-policy case those of
+src/az/fused_policy.rs:536-572.
 
 Run from the repository root:  python tests/golden/make_golden.py
 """
@@ -50,6 +51,30 @@ def sparse_fixture():
     return table.astype(np.float32), items
 
 
+def pack_policy_item(move_index, from_, to, captured, move_valid, capture_valid):
+    """pack_policy_item, src/az/fused_policy.rs:146-157 (policy_valid set)."""
+    return (move_index | from_ << 12 | to << 23 | captured << 34 | int(move_valid) << 45
+            | int(capture_valid) << 46 | 1 << 47)
+
+
+def policy_fixture():
+    """The fused-policy test inputs of src/az/fused_policy.rs:536-572: ramp
+    tables ((i % 97) - 48) * 0.001, context (i - 12) * 0.01 for two boards,
+    six items (a capture, a quiet move, padding, a bias-only item, two more);
+    the gradient is that of sum_all (all-ones output gradient)."""
+    i = np.arange(182886)
+    tables = (np.float32(1) * (i % 97).astype(np.float32) - np.float32(48.0)) * np.float32(0.001)
+    c = np.arange(2 * 48)
+    context = ((c.astype(np.float32) - np.float32(12.0)) * np.float32(0.01)).reshape(2, 48)
+    items = np.array([pack_policy_item(3, 10, 11, 20, True, True),
+                      pack_policy_item(7, 30, 40, 0, True, False),
+                      0,
+                      pack_policy_item(3, 0, 0, 0, False, False),
+                      pack_policy_item(100, 500, 501, 0, True, False),
+                      pack_policy_item(7, 30, 40, 20, True, True)], dtype=np.int64).reshape(2, 3)
+    return tables.astype(np.float32), context.astype(np.float32), items
+
+
 def main():
     out = {}
     qw = synth.quantized_weights(2)
@@ -91,6 +116,15 @@ def main():
     st, sg = oracle.sparse_pool_bwd(sitems, np.ones((2, 7), np.float32), 11)
     assert st == 0
     out["sparse_items"], out["sparse_fwd"], out["sparse_bwd"] = sitems, sf, sg
+
+    ptab, pctx, pitems = policy_fixture()
+    st, pol = oracle.policy_fused_fwd(ptab, pctx, pitems)
+    assert st == 0
+    st, pgt, pgc = oracle.policy_fused_bwd(ptab, pctx, pitems, np.ones((2, 3), np.float32))
+    assert st == 0
+    nz = np.flatnonzero(pgt)
+    out["policy_fwd"], out["policy_grad_idx"], out["policy_grad_val"] = pol, nz, pgt[nz]
+    out["policy_grad_context"] = pgc
 
     path = os.path.join(HERE, "golden.npz")
     np.savez_compressed(path, **out)

@@ -24,9 +24,14 @@
 // The summation order is fixed by the input alone, so results are
 // deterministic run to run; a row with at most kSeg contributions is summed in
 // exactly the reference CPU order.
+//
+// Tables of more than kSegMaxRows rows (the 57,702-row threat table) whose
+// per-chunk histograms would not fit in shared memory take the radix-sorted
+// row scatter of scatter.cuh instead: same order, same exactness.
 #include <algorithm>
 
 #include "common.cuh"
+#include "scatter.cuh"
 #include "segreduce.cuh"
 
 namespace cnnue {
@@ -154,6 +159,25 @@ int launch_fwd(const float* table, const uint32_t* items, int64_t batch, int64_t
   return check_launch_error("pool_fwd_kernel");
 }
 
+constexpr int64_t kSegMaxRows = 16384;  // shared-memory row histogram of a chunk
+
+// Plain-pool items as scatter keys: padding and out-of-range rows map to the
+// drop key `rows` (out-of-range ones are flagged).
+__global__ void plain_keys_kernel(const uint32_t* __restrict__ items, int64_t n, int64_t rows,
+                                  uint32_t* __restrict__ keys, uint32_t* status) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const uint32_t it = items[i];
+    const bool pad = it == kPad, ok = (int64_t)it < rows;
+    if (!pad && !ok) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+    keys[i] = (!pad && ok) ? it : (uint32_t)rows;
+  }
+}
+
+inline size_t sorted_bwd_bytes(int64_t n_items, int64_t hidden) {
+  return sizeof(WorkspaceHeader) + align_up((size_t)std::max<int64_t>(n_items, 1) * 4, 256) +
+         scat::workspace_bytes(n_items, hidden);
+}
+
 int check_shape(int64_t batch, int64_t item_count, int64_t hidden) {
   if (batch < 0 || item_count < 0 || hidden <= 0)
     return set_error(CNNUE_ERR_INVALID_ARG, "bad shape batch=%lld items=%lld hidden=%lld",
@@ -218,6 +242,7 @@ int cnnue_sparse_pool_fwd(const float* d_table, int64_t rows, const uint32_t* d_
 size_t cnnue_sparse_pool_bwd_workspace_bytes(int64_t rows, int64_t batch, int64_t item_count,
                                              int64_t hidden) {
   if (rows <= 0 || batch < 0 || item_count < 0 || hidden <= 0) return 0;
+  if (rows > kSegMaxRows) return sorted_bwd_bytes(batch * item_count, hidden);
   return seg::bwd_bytes(batch * item_count, 1, rows, hidden);
 }
 
@@ -226,12 +251,26 @@ int cnnue_sparse_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int6
                           void* d_workspace, size_t workspace_bytes, void* stream) {
   int st = check_shape(batch, item_count, hidden);
   if (st) return st;
-  if (rows <= 0 || rows > 16384)
-    return set_error(CNNUE_ERR_INVALID_ARG, "sparse pool backward supports 1..16384 rows");
+  if (rows <= 0 || rows >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "bad rows");
   if (!d_grad_table || !d_workspace || (batch && !d_grad_out) || (batch * item_count && !d_items))
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer");
-  if (workspace_bytes < seg::bwd_bytes(batch * item_count, 1, rows, hidden))
+  if (workspace_bytes < cnnue_sparse_pool_bwd_workspace_bytes(rows, batch, item_count, hidden))
     return set_error(CNNUE_ERR_WORKSPACE, "workspace too small");
+  if (rows > kSegMaxRows) {
+    cudaStream_t s = (cudaStream_t)stream;
+    const int64_t n = batch * item_count;
+    CNNUE_CUDA_TRY(cudaMemsetAsync(d_workspace, 0, sizeof(WorkspaceHeader), s));
+    uint32_t* status = &((WorkspaceHeader*)d_workspace)->status;
+    uint32_t* keys = (uint32_t*)((char*)d_workspace + sizeof(WorkspaceHeader));
+    void* scratch = (char*)keys + align_up((size_t)std::max<int64_t>(n, 1) * 4, 256);
+    if (n > 0) {
+      const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
+      plain_keys_kernel<<<g, 256, 0, s>>>(d_items, n, rows, keys, status);
+      if (int e = check_launch_error("plain_keys_kernel")) return e;
+    }
+    return scat::launch_scatter_add_rows(keys, d_grad_out, (uint32_t)item_count, hidden, n, rows, d_grad_table,
+                                         scratch, s);
+  }
   PlainDecoder dec{rows, d_items, item_count};
   return seg::launch_bwd(batch * item_count, d_grad_out, hidden, dec, d_grad_table, d_workspace,
                          (cudaStream_t)stream);

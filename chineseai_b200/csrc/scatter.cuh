@@ -17,6 +17,10 @@
 //      each key adds its units' partials in order.  A key with at most 256
 //      contributions is thus summed exactly in contribution order; longer
 //      runs are still deterministic.  Keys with no contribution read zero.
+// The row form (launch_scatter_add_rows) does the same for whole table rows:
+// a contribution adds a `hidden`-wide row of values, one warp sums a unit
+// with its lanes over the columns, and a key with a single unit is written
+// directly.
 #pragma once
 
 #include "common.cuh"
@@ -235,31 +239,97 @@ __global__ void run_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t
   }
 }
 
-// Workspace of launch_scatter_add for n contributions.
-inline size_t workspace_bytes(int64_t n) {
+// Row form: one warp per unit; lanes walk the columns 32 at a time.  A
+// unit that is its run's only one writes the table row directly.
+__global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx,
+                                     const float* __restrict__ values, uint32_t div, int64_t hidden,
+                                     const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ unit_off,
+                                     uint32_t n_runs, uint32_t n_units, int64_t n, int64_t n_keys,
+                                     float* __restrict__ partial, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n_units; u += warps) {
+    uint32_t lo = 0, hi = n_runs - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (unit_off[mid] <= (uint32_t)u) lo = mid;
+      else hi = mid - 1;
+    }
+    const uint32_t r = lo;
+    const uint32_t rbeg = run_start[r], rend = r + 1 < n_runs ? run_start[r + 1] : (uint32_t)n;
+    const uint32_t u1 = r + 1 < n_runs ? unit_off[r + 1] : n_units;
+    const uint32_t beg = rbeg + ((uint32_t)u - unit_off[r]) * kUnit;
+    const uint32_t end = min(rend, beg + kUnit);
+    const uint32_t key = keys[rbeg];
+    float* dst;
+    if (u1 - unit_off[r] == 1) {
+      if ((int64_t)key >= n_keys) continue;  // dropped contributions
+      dst = out + (int64_t)key * hidden;
+    } else {
+      dst = partial + u * hidden;
+    }
+    for (int64_t h = lane; h < hidden; h += 32) {
+      float s = 0.f;
+      uint32_t j = beg;
+      for (; j + 8 <= end; j += 8) {
+        float v[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[k] = __ldg(values + (int64_t)(__ldg(idx + j + k) / div) * hidden + h);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += v[k];
+      }
+      for (; j < end; ++j) s += __ldg(values + (int64_t)(__ldg(idx + j) / div) * hidden + h);
+      dst[h] = s;
+    }
+  }
+}
+
+// Runs of several units add their partial rows in order (one thread per
+// (run, column); single-unit runs were written by unit_sum_rows_kernel).
+__global__ void run_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ run_start,
+                                    const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
+                                    const float* __restrict__ partial, int64_t hidden, int64_t n_keys,
+                                    float* __restrict__ out) {
+  const int64_t total = (int64_t)n_runs * hidden;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = q / hidden, h = q - r * hidden;
+    const uint32_t u0 = unit_off[r], u1 = r + 1 < n_runs ? unit_off[r + 1] : n_units;
+    if (u1 - u0 < 2) continue;
+    const uint32_t k = keys[run_start[r]];
+    if ((int64_t)k >= n_keys) continue;
+    float s = partial[(int64_t)u0 * hidden + h];
+    for (uint32_t u = u0 + 1; u < u1; ++u) s += partial[(int64_t)u * hidden + h];
+    out[(int64_t)k * hidden + h] = s;
+  }
+}
+
+// Workspace of launch_scatter_add(_rows) for n contributions of `hidden`
+// values each.
+inline size_t workspace_bytes(int64_t n, int64_t hidden = 1) {
   const size_t nn = (size_t)(n > 0 ? n : 1);
   const int64_t nb = n_blocks(n > 0 ? n : 1);
   size_t b = 4 * align_up(nn * 4, 256);                       // keys / idx ping-pong
   b += align_up((size_t)nb * kDigits * 4, 256);               // histograms
   b += scan_bytes(std::max<int64_t>((int64_t)nb * kDigits, (int64_t)nn));  // scan scratch
   b += 3 * align_up((nn + 1) * 4, 256);                       // flags / run starts / unit offsets
-  b += align_up((nn + 1) * 4, 256);                           // unit partials
+  b += align_up((nn + 1) * 4 * (size_t)hidden, 256);          // unit partials
   b += 256;
   return b;
 }
 
-// out[k] = sum over i (in index order, in units of 256 per key) of
-// values[i / div] with keys[i] == k; keys nobody hits read 0.  Every key must
-// be <= n_keys (the sort covers only those bits); key n_keys marks a
-// contribution to drop (callers map padding and out-of-range indices to it).
-// Synchronises `s` twice (run and unit counts).
-int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, int64_t n, int64_t n_keys,
-                       float* out, void* ws, cudaStream_t s) {
-  const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_keys + 255) / 256, 148 * 8));
-  zero_kernel<<<zb, 256, 0, s>>>(out, n_keys);
-  if (int st = check_launch_error("scatter zero")) return st;
-  if (n <= 0) return CNNUE_OK;
-  if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
+// The sorted contributions and their runs and units.
+struct Runs {
+  const uint32_t* keys;   // [n] sorted keys
+  const uint32_t* idx;    // [n] contribution index of each sorted slot
+  uint32_t* run_start;    // [n_runs]
+  uint32_t* unit_off;     // [n_runs] first unit of each run
+  float* partial;         // unit partials
+  uint32_t n_runs = 0, n_units = 0;
+};
+
+// Sorts (key, contribution) pairs stably by key and finds runs and units;
+// synchronises `s` twice (run and unit counts).  Requires 0 < n < 2^32 - 1.
+int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s, Runs* out) {
   const size_t nn = (size_t)n;
   const int64_t nb = n_blocks(n);
   char* p = (char*)ws;
@@ -277,7 +347,7 @@ int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, 
   uint32_t* flag = (uint32_t*)take((nn + 1) * 4);
   uint32_t* rstart = (uint32_t*)take((nn + 1) * 4);
   uint32_t* uoff = (uint32_t*)take((nn + 1) * 4);
-  float* partial = (float*)take((nn + 1) * 4);
+  out->partial = (float*)p;
   const int passes = key_passes(n_keys + 1);
   const uint32_t* kin = keys;
   const uint32_t* iin = nullptr;
@@ -315,12 +385,60 @@ int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, 
   if (int st = launch_scan(uoff, n_runs, aux, s)) return st;
   CNNUE_CUDA_TRY(cudaMemcpyAsync(&n_units, uoff + n_runs - 1, 4, cudaMemcpyDeviceToHost, s));
   CNNUE_CUDA_TRY(cudaStreamSynchronize(s));
-  n_units += last_units;
-  const unsigned ub = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_units + 255) / 256, 148 * 16));
-  unit_sum_kernel<<<ub, 256, 0, s>>>(iin, values, div, rstart, uoff, n_runs, n_units, n, partial);
+  out->keys = kin;
+  out->idx = iin;
+  out->run_start = rstart;
+  out->unit_off = uoff;
+  out->n_runs = n_runs;
+  out->n_units = n_units + last_units;
+  return CNNUE_OK;
+}
+
+// out[k] = sum over i (in index order, in units of 256 per key) of
+// values[i / div] with keys[i] == k; keys nobody hits read 0.  Every key must
+// be <= n_keys (the sort covers only those bits); key n_keys marks a
+// contribution to drop (callers map padding and out-of-range indices to it).
+// Synchronises `s` twice (run and unit counts).
+int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, int64_t n, int64_t n_keys,
+                       float* out, void* ws, cudaStream_t s) {
+  const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_keys + 255) / 256, 148 * 8));
+  zero_kernel<<<zb, 256, 0, s>>>(out, n_keys);
+  if (int st = check_launch_error("scatter zero")) return st;
+  if (n <= 0) return CNNUE_OK;
+  if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
+  Runs r;
+  if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
+  const unsigned ub = (unsigned)std::max<int64_t>(1, std::min<int64_t>((r.n_units + 255) / 256, 148 * 16));
+  unit_sum_kernel<<<ub, 256, 0, s>>>(r.idx, values, div, r.run_start, r.unit_off, r.n_runs, r.n_units, n,
+                                     r.partial);
   if (int st = check_launch_error("scatter unit sums")) return st;
-  run_sum_kernel<<<rb, 256, 0, s>>>(kin, rstart, uoff, n_runs, n_units, partial, n_keys, out);
+  const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((r.n_runs + 255) / 256, 148 * 16));
+  run_sum_kernel<<<rb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, n_keys, out);
   return check_launch_error("scatter run sums");
+}
+
+// Row form: out[k][h] = sum over i (same order) of values[(i / div) * hidden
+// + h] with keys[i] == k, for a table out[n_keys][hidden].
+int launch_scatter_add_rows(const uint32_t* keys, const float* values, uint32_t div, int64_t hidden, int64_t n,
+                            int64_t n_keys, float* out, void* ws, cudaStream_t s) {
+  const int64_t total = n_keys * hidden;
+  const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
+  zero_kernel<<<zb, 256, 0, s>>>(out, total);
+  if (int st = check_launch_error("scatter zero")) return st;
+  if (n <= 0) return CNNUE_OK;
+  if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
+  Runs r;
+  if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
+  const unsigned ub =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_units * 32 + 255) / 256, 148 * 16));
+  unit_sum_rows_kernel<<<ub, 256, 0, s>>>(r.keys, r.idx, values, div, hidden, r.run_start, r.unit_off, r.n_runs,
+                                          r.n_units, n, n_keys, r.partial, out);
+  if (int st = check_launch_error("scatter unit row sums")) return st;
+  const unsigned rb =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_runs * hidden + 255) / 256, 148 * 16));
+  run_sum_rows_kernel<<<rb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, hidden,
+                                         n_keys, out);
+  return check_launch_error("scatter run row sums");
 }
 
 }  // namespace

@@ -248,8 +248,10 @@ int cnnue_feature_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int
 int cnnue_sparse_pool_fwd(const float* d_table, int64_t rows, const uint32_t* d_items,
                           int64_t batch, int64_t item_count, int64_t hidden, float* d_out,
                           uint32_t* d_status, void* stream);
-/* Atomic-free backward of the plain pool (same scheme as the feature pool;
- * tables up to 16384 rows).  Replaces SparsePoolGrad / kernel sparse_pool_grad
+/* Atomic-free backward of the plain pool (same scheme as the feature pool up
+ * to 16384 rows; larger tables such as the 57,702-row threat table use a
+ * radix-sorted row scatter with the same order).  Synchronises the stream for
+ * tables of more than 16384 rows.  Replaces SparsePoolGrad / kernel sparse_pool_grad
  * (src/az/fused_feature_pool.rs:94-106, CPU twin :342-370). */
 size_t cnnue_sparse_pool_bwd_workspace_bytes(int64_t rows, int64_t batch, int64_t item_count,
                                              int64_t hidden);

@@ -14,6 +14,7 @@ from tests.golden.make_golden import pool_fixture, sparse_fixture
 pytestmark = pytest.mark.gpu
 GOLDEN = os.path.join(os.path.dirname(__file__), "golden", "golden.npz")
 dev = torch.device("cuda", 0)
+PAD_ITEM = 0xFFFFFFFF
 
 
 def t(a):
@@ -92,3 +93,42 @@ def test_bad_item_is_flagged():
     items = np.array([[0 | (15 << 15)]], np.uint32)
     with pytest.raises(CnnueError):
         pool.feature_pool(t(tables), t(items))
+
+
+@pytest.mark.parametrize("batch,item_count,hidden,seed", [(5, 9, 64, 1), (512, 48, 64, 2), (128, 30, 128, 3)])
+def test_threat_table_backward(batch, item_count, hidden, seed):
+    """The 57,702-row threat table (past the shared-memory histogram): bit
+    exact wherever a row takes at most 256 contributions, deterministic."""
+    rows = 57702
+    rng = np.random.default_rng(seed)
+    items = rng.integers(0, rows, size=(batch, item_count)).astype(np.uint32)
+    items[:, -3:] = PAD_ITEM
+    items[0, :5] = 4242  # a row hit repeatedly inside one batch row
+    if batch >= 512:
+        items[:, 0] = 7  # a row with `batch` (> 256) contributions
+    grad_out = rng.standard_normal((batch, hidden)).astype(np.float32)
+    table = rng.standard_normal((rows, hidden)).astype(np.float32)
+    st, ref_fwd = oracle.sparse_pool_fwd(table, items)
+    assert st == 0
+    np.testing.assert_array_equal(pool.sparse_pool(t(table), t(items)).cpu().numpy(), ref_fwd)
+    g1 = pool.sparse_pool_backward(t(items), t(grad_out), rows).cpu().numpy()
+    g2 = pool.sparse_pool_backward(t(items), t(grad_out), rows).cpu().numpy()
+    np.testing.assert_array_equal(g1, g2)
+    st, ref = oracle.sparse_pool_bwd(items, grad_out, rows)
+    assert st == 0
+    counts = np.bincount(items[items != PAD_ITEM].astype(np.int64), minlength=rows)
+    exact = counts <= 256
+    np.testing.assert_array_equal(g1[exact], ref[exact])
+    if not exact.all():
+        mag = np.zeros((rows, hidden))
+        valid = items != PAD_ITEM
+        np.add.at(mag, items[valid].astype(np.int64), np.abs(np.repeat(grad_out, item_count, 0)[valid.reshape(-1)]))
+        err = np.abs(g1[~exact].astype(np.float64) - ref[~exact])
+        assert np.all(err <= 2 * counts[~exact, None] * 2.0**-23 * mag[~exact])
+
+
+def test_threat_table_backward_bad_row_flagged():
+    from chineseai_b200._lib import CnnueError
+    items = np.array([[3, 57702]], np.uint32)
+    with pytest.raises(CnnueError):
+        pool.sparse_pool_backward(t(items), t(np.ones((1, 64), np.float32)), 57702)

@@ -20,6 +20,7 @@
 #include <memory>
 #include <new>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/cnnue.h"
@@ -909,6 +910,194 @@ bool gives_check(const int8_t* b, int side, int from, int to) {
   return false;
 }
 
+// ---- training batch packer (PackedBatch::from_indices, src/az/dataloader.rs:113-336)
+constexpr int64_t kSparseTable = 2396815;    // POLICY_SPARSE_TABLE_SIZE (src/az.rs:77-78)
+constexpr int64_t kSparseMain = 2086 * 14 * 81;
+constexpr int64_t kTacticalExact = 2086 * 7 * 64;  // POLICY_TACTICAL_EXACT_SIZE (src/az.rs:66-67)
+constexpr int64_t kTacticalSize = kTacticalExact + 7 * 64;
+constexpr float kPolicyMask = -1.0e9f;       // POLICY_MASK_VALUE (src/az/dataloader.rs:22)
+constexpr uint32_t kPad = 0xffffffffu;
+
+struct RowDims {
+  int features = 0, moves = 0, threats = 0;
+};
+
+// The canonical position of a sample (Position::from_canonical_piece_squares,
+// src/xiangqi/mod.rs:112-157): own pieces (index < 7) Red, others Black, Red
+// to move; board_features[sq] = the feature standing on sq (-1 if none).
+void sample_board(const uint16_t* f, int n, int8_t* board, int* board_features) {
+  std::memset(board, 0, kSq);
+  for (int sq = 0; sq < kSq; ++sq) board_features[sq] = -1;
+  for (int k = 0; k < n; ++k) {
+    if (f[k] >= CNNUE_AZ_INPUT) continue;
+    const int pi = f[k] / kSq, sq = f[k] % kSq;
+    board[sq] = (int8_t)(pi < 7 ? pi + 1 : -(pi - 7 + 1));
+    board_features[sq] = f[k];
+  }
+}
+
+// canonical_general_buckets_from_features (src/az.rs:168-184): the last
+// general of each side in feature order.
+void sample_buckets(const uint16_t* f, int n, int* us, int* them) {
+  *us = 4;
+  *them = 4;
+  for (int k = 0; k < n; ++k) {
+    if (f[k] >= CNNUE_AZ_INPUT) continue;
+    const int pi = f[k] / kSq, sq = f[k] % kSq;
+    if (pi == 0) *us = general_bucket(0, sq);
+    if (pi == 7) *them = general_bucket(7, sq);
+  }
+}
+
+// value_threat_features (src/az/dataloader.rs:307-326).
+int sample_threats(const int8_t* board, uint32_t* out) {
+  int n = 0;
+  visit_attacks(board, [&](int source, int attacker, int target, int attacked) {
+    const uint32_t f = threat_index(0, source, attacker, target, attacked);
+    if (f != UINT32_MAX && n < CNNUE_AZ_THREAT_MAX) out[n++] = f;
+  });
+  return n;
+}
+
+// policy_king_distance_buckets (src/az.rs:841-859).
+void king_distance(int from, int to, int them, int* distance, int* approach) {
+  const int king = kSq - 1 - ((7 + them / 3) * 9 + 3 + them % 3);
+  const int before = std::abs(from / 9 - king / 9) + std::abs(from % 9 - king % 9);
+  const int after = std::abs(to / 9 - king / 9) + std::abs(to % 9 - king % 9);
+  *approach = std::min(std::max(before - after, -2), 2) + 2;
+  *distance = std::min(after, 5);
+}
+
+void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowDims& dims,
+              const uint32_t* threats, int n_threats, const cnnue_az_packed* o) {
+  const uint16_t* f = s->features + s->feature_offsets[sample];
+  const int nf = (int)(s->feature_offsets[sample + 1] - s->feature_offsets[sample]);
+  const int F = dims.features, M = dims.moves, T = dims.threats;
+  int us, them;
+  sample_buckets(f, nf, &us, &them);
+  // pack_features (:193-205): padding where a feature is out of range
+  uint32_t* fi = o->feature_items + row * F;
+  for (int k = 0; k < F; ++k) fi[k] = k < nf && f[k] < CNNUE_AZ_INPUT ? pack(f[k], us, them) : kPad;
+  uint32_t* ti = o->value_threat_indices + row * T;
+  for (int k = 0; k < T; ++k) ti[k] = k < n_threats ? threats[k] : kPad;
+  // pack_policy (:207-305)
+  int8_t board[kSq];
+  int bf[kSq];
+  sample_board(f, nf, board, bf);
+  uint8_t opp[kSq], own[kSq];
+  attacked_squares(board, 1, opp);
+  attacked_squares(board, 0, own);
+  const auto& moves = dense_moves();
+  int64_t* items = o->policy_items + row * M;
+  int64_t* sparse = o->policy_sparse_indices + row * M * 7;
+  int64_t* tactical = o->policy_tactical_indices + row * M * 2;
+  float* targets = o->policy_targets + row * M;
+  float* mask = o->policy_mask + row * M;
+  for (int k = 0; k < M; ++k) {
+    items[k] = 0;
+    targets[k] = 0.f;
+    mask[k] = kPolicyMask;
+    for (int j = 0; j < 7; ++j) sparse[k * 7 + j] = kSparseTable - 1;
+    tactical[k * 2] = tactical[k * 2 + 1] = kTacticalSize;
+  }
+  const uint32_t m0 = s->move_offsets[sample], m1 = s->move_offsets[sample + 1];
+  int off = 0;
+  for (uint32_t j = m0; j < m1; ++j) {
+    const int mi = s->move_indices[j];
+    if (mi >= kDenseMoves) continue;
+    const float target = s->policy[j];
+    targets[off] = std::fmax(target, 0.f);
+    mask[off] = 0.f;
+    const int from = moves[mi] / kSq, to = moves[mi] % kSq;
+    const int mf = bf[from];
+    const bool move_valid = mf >= 0 && mf / kSq < 7;
+    int64_t cf = 0, ct = 0, cc = 0;
+    bool capture = false;
+    if (move_valid) {
+      cf = mf;
+      ct = (int64_t)(mf / kSq) * kSq + to;
+      if (bf[to] >= 0) {
+        cc = bf[to];
+        capture = true;
+      }
+    }
+    // pack_policy_item (src/az/fused_policy.rs:146-157)
+    items[off] = (int64_t)((uint64_t)mi | (uint64_t)cf << 12 | (uint64_t)ct << 23 | (uint64_t)cc << 34 |
+                           (uint64_t)move_valid << 45 | (uint64_t)capture << 46 | (uint64_t)1 << 47);
+    if (move_valid) {
+      const int piece = mf / kSq;
+      const int pair = us * 9 + them;
+      int64_t* sp = sparse + off * 7;
+      // policy_sparse_main_index / _capture_index / _factor_indices (src/az.rs:763-813)
+      sp[0] = (((int64_t)mi * 14 + piece) * 9 + us) * 9 + them;
+      sp[1] = kSparseMain + (int64_t)mi * 15 + (capture ? cc / kSq : 14);
+      int distance, approach;
+      king_distance(from, to, them, &distance, &approach);
+      const int64_t move_piece = (int64_t)kDenseMoves * 14, move_king = (int64_t)kDenseMoves * 81;
+      const int64_t distance_off = move_piece + move_king + 14 * 81;
+      sp[2] = kSparseTable + (int64_t)mi * 14 + piece;
+      sp[3] = kSparseTable + move_piece + (int64_t)mi * 81 + pair;
+      sp[4] = kSparseTable + move_piece + move_king + piece * 81 + pair;
+      sp[5] = kSparseTable + distance_off + piece * 6 + distance;
+      sp[6] = kSparseTable + distance_off + 14 * 6 + piece * 5 + approach;
+      // policy_tactical_indices (src/az.rs:815-839)
+      const int64_t sig = (int64_t)opp[from] | (int64_t)opp[to] << 1 | (int64_t)own[from] << 2 |
+                          (int64_t)own[to] << 3 | (int64_t)capture << 4 |
+                          (int64_t)gives_check(board, 0, from, to) << 5;
+      tactical[off * 2] = ((int64_t)mi * 7 + piece) * 64 + sig;
+      tactical[off * 2 + 1] = kTacticalExact + piece * 64 + sig;
+    }
+    ++off;
+  }
+  // normalize_policy_targets (:432-446)
+  if (off > 0) {
+    float sum = 0.f;
+    for (int k = 0; k < off; ++k) sum += targets[k];
+    if (std::isfinite(sum) && sum > 1.0e-12f) {
+      for (int k = 0; k < off; ++k) targets[k] = std::fmax(targets[k] / sum, 0.f);
+    } else {
+      const float uniform = 1.0f / (float)off;
+      for (int k = 0; k < off; ++k) targets[k] = uniform;
+    }
+  }
+  // normalize_wdl_target (src/az.rs:2586-2599)
+  float w[3];
+  for (int k = 0; k < 3; ++k) w[k] = std::fmax(s->value_wdl[sample * 3 + k], 0.f);
+  const float wsum = w[0] + w[1] + w[2];
+  if (std::isfinite(wsum) && wsum > 1.0e-6f) {
+    for (int k = 0; k < 3; ++k) o->value_wdl[row * 3 + k] = w[k] / wsum;
+  } else {
+    o->value_wdl[row * 3] = 0.f;
+    o->value_wdl[row * 3 + 1] = 1.f;
+    o->value_wdl[row * 3 + 2] = 0.f;
+  }
+  o->values[row] = std::min(std::max(s->value[sample], -1.0f), 1.0f);
+  for (int k = 0; k < CNNUE_AZ_RULE_CONTEXT; ++k)
+    o->rule_context[row * CNNUE_AZ_RULE_CONTEXT + k] = s->rule_context[sample * CNNUE_AZ_RULE_CONTEXT + k];
+  o->policy_weights[row] = std::fmax(s->policy_weight[sample], 0.f);
+  o->value_weights[row] = std::fmax(s->value_weight[sample], 0.f);
+  const uint32_t ply = s->ply[sample];
+  const int phase = ply < 40 ? 0 : (ply < 120 ? 1 : 2);
+  for (int k = 0; k < 3; ++k) o->value_phase_masks[row * 3 + k] = k == phase ? 1.f : 0.f;
+}
+
+template <class Fn>
+void parallel_rows(int64_t n, int n_threads, Fn&& fn) {
+  int t = n_threads > 0 ? n_threads : (int)std::min<unsigned>(std::max(1u, std::thread::hardware_concurrency()), 16u);
+  t = (int)std::min<int64_t>(t, std::max<int64_t>(n / 16, 1));
+  if (t <= 1) {
+    for (int64_t i = 0; i < n; ++i) fn(i);
+    return;
+  }
+  std::vector<std::thread> pool;
+  pool.reserve(t);
+  for (int k = 0; k < t; ++k)
+    pool.emplace_back([&, k] {
+      for (int64_t i = n * k / t; i < n * (k + 1) / t; ++i) fn(i);
+    });
+  for (auto& th : pool) th.join();
+}
+
 }  // namespace
 
 extern "C" {
@@ -1217,6 +1406,58 @@ int cnnue_az_weights_tensor(cnnue_az_weights* w, int index, float** data, int64_
   if (index < 0 || index >= CNNUE_AZ_TENSORS) return set_error(CNNUE_ERR_INVALID_ARG, "tensor index %d", index);
   *data = w->t[index].data();
   if (count) *count = (int64_t)w->t[index].size();
+  return CNNUE_OK;
+}
+
+int cnnue_az_pack_batch(const cnnue_az_samples* s, const int64_t* rows, int64_t batch, int64_t cap_features,
+                        int64_t cap_moves, int64_t cap_threats, cnnue_az_packed* out, int n_threads) {
+  if (!s || !out || batch < 0) return set_error(CNNUE_ERR_INVALID_ARG, "null samples/out or negative batch");
+  if (s->n < 0 || (s->n > 0 && (!s->feature_offsets || !s->move_offsets)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "samples without offsets");
+  for (int64_t r = 0; r < batch; ++r) {
+    const int64_t i = rows ? rows[r] : r;
+    if (i < 0 || i >= s->n) return set_error(CNNUE_ERR_INVALID_ARG, "batch row %lld: sample %lld of %lld",
+                                             (long long)r, (long long)i, (long long)s->n);
+  }
+  // pass 1: per-row counts and threat features (the batch maxima set the strides)
+  std::vector<RowDims> dims(batch);
+  std::vector<uint32_t> threats((size_t)batch * CNNUE_AZ_THREAT_MAX);
+  parallel_rows(batch, n_threads, [&](int64_t r) {
+    const int64_t i = rows ? rows[r] : r;
+    const uint16_t* f = s->features + s->feature_offsets[i];
+    const int nf = (int)(s->feature_offsets[i + 1] - s->feature_offsets[i]);
+    int8_t board[kSq];
+    int bf[kSq];
+    sample_board(f, nf, board, bf);
+    dims[r].features = nf;
+    dims[r].threats = sample_threats(board, threats.data() + (size_t)r * CNNUE_AZ_THREAT_MAX);
+    int m = 0;
+    for (uint32_t j = s->move_offsets[i]; j < s->move_offsets[i + 1]; ++j) m += s->move_indices[j] < kDenseMoves;
+    dims[r].moves = m;
+  });
+  RowDims mx;
+  mx.features = mx.moves = mx.threats = 1;  // .max(1) (:116-136)
+  for (const RowDims& d : dims) {
+    mx.features = std::max(mx.features, d.features);
+    mx.moves = std::max(mx.moves, d.moves);
+    mx.threats = std::max(mx.threats, d.threats);
+  }
+  out->batch = batch;
+  out->max_features = mx.features;
+  out->max_policy_moves = mx.moves;
+  out->max_value_threats = mx.threats;
+  if (mx.features > cap_features || mx.moves > cap_moves || mx.threats > cap_threats)
+    return set_error(CNNUE_ERR_WORKSPACE, "batch needs %d features, %d moves, %d threats per row", mx.features,
+                     mx.moves, mx.threats);
+  if (batch == 0) return CNNUE_OK;
+  if (!out->feature_items || !out->value_threat_indices || !out->policy_items || !out->policy_sparse_indices ||
+      !out->policy_tactical_indices || !out->policy_targets || !out->policy_mask || !out->value_wdl ||
+      !out->values || !out->rule_context || !out->policy_weights || !out->value_weights || !out->value_phase_masks)
+    return set_error(CNNUE_ERR_INVALID_ARG, "null output array");
+  parallel_rows(batch, n_threads, [&](int64_t r) {
+    const int64_t i = rows ? rows[r] : r;
+    pack_row(s, i, r, mx, threats.data() + (size_t)r * CNNUE_AZ_THREAT_MAX, dims[r].threats, out);
+  });
   return CNNUE_OK;
 }
 

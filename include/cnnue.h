@@ -397,7 +397,64 @@ int cnnue_az_threat_features(const int8_t* board, int perspective, uint32_t* fea
  * the reference's; the reference asserts the same count). */
 int cnnue_az_threat_vocab(void);
 
-/* Per-move records for the policy logits (the per-move inputs of
+/* ---- AZ-NNUE training batch packer ---------------------------------------
+ * Training samples (the AzTrainingSample fields the packer reads) in CSR
+ * form: features (canonical side-to-move piece-square features, as stored
+ * by the self-play writer) per sample, its move_indices (dense move space;
+ * >= 2086 are skipped) with their policy targets alongside, value_wdl [n][3],
+ * value [n], rule_context [n][7], policy_weight [n], value_weight [n], ply [n]. */
+typedef struct cnnue_az_samples {
+  int64_t n;
+  const uint16_t* features;
+  const uint32_t* feature_offsets; /* [n + 1] */
+  const uint16_t* move_indices;
+  const float* policy;
+  const uint32_t* move_offsets;    /* [n + 1] */
+  const float* value_wdl;
+  const float* value;
+  const float* rule_context;
+  const float* policy_weight;
+  const float* value_weight;
+  const uint32_t* ply;
+} cnnue_az_samples;
+/* The packed batch (PackedBatch, src/az/dataloader.rs:92-111): row-major
+ * arrays with the batch's own strides F = max_features, M = max_policy_moves,
+ * T = max_value_threats (each at least 1):
+ *   feature_items u32 [B][F] (pack_feature items, 0xffffffff padding),
+ *   value_threat_indices u32 [B][T], policy_items i64 [B][M] (fused_policy
+ *   items, 0 padding), policy_sparse_indices i64 [B][M][7] (padding 2396814),
+ *   policy_tactical_indices i64 [B][M][2] (padding 934976), policy_targets
+ *   f32 [B][M] (normalised), policy_mask f32 [B][M] (0 or -1e9), value_wdl
+ *   f32 [B][3] (normalised), values f32 [B] (clamped to [-1,1]), rule_context
+ *   f32 [B][7], policy_weights / value_weights f32 [B], value_phase_masks f32
+ *   [B][3] (ply < 40, < 120, else). */
+typedef struct cnnue_az_packed {
+  int64_t batch, max_features, max_policy_moves, max_value_threats; /* written by the packer */
+  uint32_t* feature_items;
+  uint32_t* value_threat_indices;
+  int64_t* policy_items;
+  int64_t* policy_sparse_indices;
+  int64_t* policy_tactical_indices;
+  float* policy_targets;
+  float* policy_mask;
+  float* value_wdl;
+  float* values;
+  float* rule_context;
+  float* policy_weights;
+  float* value_weights;
+  float* value_phase_masks;
+} cnnue_az_packed;
+/* Packs the samples rows[0..batch) (rows NULL = 0..batch) on n_threads host
+ * threads (<= 0: up to 16).  The output arrays must hold the capacities
+ * cap_features / cap_moves / cap_threats per row; the dims actually used are
+ * written to out first, and CNNUE_ERR_WORKSPACE is returned (nothing else
+ * written) when a capacity is too small.  Replaces PackedBatch::from_indices
+ * (src/az/dataloader.rs:113-336). */
+int cnnue_az_pack_batch(const cnnue_az_samples* samples, const int64_t* rows, int64_t batch,
+                        int64_t cap_features, int64_t cap_moves, int64_t cap_threats,
+                        cnnue_az_packed* out, int n_threads);
+
+/* Per-move records for the policy logits/* Per-move records for the policy logits (the per-move inputs of
  * evaluate_prepared_hidden_with_context, src/az.rs:1766-1887), side to move
  * `side`.  moves[2i], moves[2i+1] = from, to squares (absolute).  info[2i] =
  * dense move index of the canonical move (12 bits, 0xfff when not in the

@@ -62,6 +62,8 @@ SIGNATURES = {
     "cnnue_policy_table_fwd": (c_int, [P, c_i64, P, c_i64, c_int, P, P, P]),
     "cnnue_policy_table_bwd_workspace_bytes": (c_size, [c_i64, c_int]),
     "cnnue_policy_table_bwd": (c_int, [P, P, c_i64, c_int, c_i64, P, P, c_size, P]),
+    "cnnue_adamw": (c_int, [P, P, P, P, c_i64, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double,
+                            c_i64, P]),
     "cnnue_t_param_count": (c_size, []),
     "cnnue_t_workspace_bytes": (c_size, [c_i64, c_u32]),
     "cnnue_t_make_shadow": (c_int, [P, P, P]),

@@ -195,3 +195,205 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
         value_wdl=bufs["value_wdl"][:batch], values=bufs["values"][:batch],
         rule_context=bufs["rule_context"][:batch], policy_weights=bufs["policy_weights"][:batch],
         value_weights=bufs["value_weights"][:batch], value_phase_masks=bufs["value_phase_masks"][:batch])
+
+
+# ---- the training step --------------------------------------------------------
+# Leaves of the flat parameter buffer: (name, first tensor, last tensor, shape).
+# Tensors 0-4 form the [1545, H] feature table of feature_pool, 19-20 the
+# sparse policy table, and the tactical table (last) carries one constant
+# zero after it (the Tensor::zeros(1) of candle_model.rs:133-139).
+_LEAVES = [
+    ("feature_tables", 0, 4, lambda h: (1545, h)),
+    ("rule_context_hidden", 5, 5, lambda h: (RULE_CONTEXT, h)),
+    ("hidden_bias", 6, 6, lambda h: (h,)),
+    ("value_head_hidden", 7, 7, lambda h: (96, h)),
+    ("value_head_bias", 8, 8, lambda h: (96,)),
+    ("value_head_output", 9, 9, lambda h: (3, 96)),
+    ("value_threat_embedding", 10, 10, lambda h: (57702, 64)),
+    ("value_threat_output", 11, 11, lambda h: (3, 128)),
+    ("policy_threat_context", 12, 12, lambda h: (16, 128)),
+    ("policy_move_bias", 13, 13, lambda h: (DENSE_MOVES,)),
+    ("policy_consequence_output", 14, 14, lambda h: (32,)),
+    ("policy_context_hidden", 15, 15, lambda h: (16, h)),
+    ("policy_move_context", 16, 16, lambda h: (DENSE_MOVES, 16)),
+    ("policy_accumulator_hidden", 17, 17, lambda h: (32, h)),
+    ("policy_accumulator_move", 18, 18, lambda h: (DENSE_MOVES, 32)),
+    ("sparse_tables", 19, 20, lambda h: (SPARSE_TABLE + SPARSE_FACTOR,)),
+    ("tactical_table", 21, 21, lambda h: (TACTICAL + 1,)),
+]
+_ALIGN = 64  # floats: every leaf starts on a 256-byte boundary
+
+
+@dataclass
+class TrainStats:
+    """AzTrainStats of one batch (src/az/train_gpu_candle.rs:271-300): sums
+    over the batch (loss = weighted CE sum, not yet divided by the batch)."""
+    loss: float
+    value_loss: float
+    policy_ce: float
+    value_pred_sum: float
+    value_pred_sq_sum: float
+    value_target_sum: float
+    value_target_sq_sum: float
+    value_pred_target_sum: float
+    value_error_sq_sum: float
+    samples: int
+    phase: np.ndarray  # [3][7]: samples, pred, pred^2, target, target^2, pred*target, error^2 sums
+
+
+class AzTrainer:
+    """GpuTrainer (src/az/train_gpu_candle.rs:15-160) on one CUDA device."""
+
+    def __init__(self, weights: "az.AzWeights", lr: float = 1e-3, device: int = 0, weight_decay: float = 1e-4,
+                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8):
+        import torch
+        self.torch = torch
+        self.hidden = h = weights.hidden
+        self.device = torch.device("cuda", device)
+        self.lr, self.beta1, self.beta2, self.eps, self.weight_decay = lr, beta1, beta2, eps, weight_decay
+        self.step_count = 0
+        sizes = [az.tensor_info(i, h)[1] for i in range(az.N_TENSORS)]
+        starts = np.concatenate([[0], np.cumsum(sizes)])
+        layout, pos = [], 0
+        for name, first, last, shape in _LEAVES:
+            n = int(starts[last + 1] - starts[first]) + (1 if name == "tactical_table" else 0)
+            layout.append((name, first, last, shape(h), pos, n))
+            pos = pos + n if name == "tactical_table" else (pos + n + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.n_params = pos - 1  # AdamW covers everything but the tactical table's constant zero
+        host = np.zeros(pos, np.float32)
+        for name, first, last, shape, off, n in layout:
+            host[off:off + int(starts[last + 1] - starts[first])] = np.concatenate(
+                [weights.tensor(i).reshape(-1) for i in range(first, last + 1)])
+        self.flat = torch.from_numpy(host).to(self.device)
+        self.grad = torch.zeros_like(self.flat)
+        self.m = torch.zeros(self.n_params, dtype=torch.float32, device=self.device)
+        self.v = torch.zeros_like(self.m)
+        self._layout = layout
+        self.params = {}
+        for name, first, last, shape, off, n in layout:
+            p = torch.nn.Parameter(self.flat[off:off + n].view(shape))
+            p.grad = self.grad[off:off + n].view(shape)
+            self.params[name] = p
+        self._wdl_q = torch.tensor([1.0, 0.0, -1.0], device=self.device)
+
+    # -- data ---------------------------------------------------------------
+    def to_device(self, b: PackedBatch) -> dict:
+        """BatchTensors::from_packed (src/az/candle_model.rs:173-233)."""
+        torch = self.torch
+
+        def t(a):
+            a = np.ascontiguousarray(a)
+            if a.dtype == np.uint32:
+                a = a.view(np.int32)
+            return torch.from_numpy(a).to(self.device, non_blocking=True)
+        return {f.name: t(getattr(b, f.name)) for f in fields(PackedBatch)}
+
+    # -- model ----------------------------------------------------------------
+    def forward(self, bt: dict):
+        """AzCandleModel::forward (src/az/candle_model.rs:46-147) ->
+        (value_logits [B, 3], policy_logits [B, M])."""
+        from . import policy as pol
+        from . import pool
+        torch = self.torch
+        P = self.params
+        h = self.hidden
+        ft = P["feature_tables"]
+        board_pre = pool.feature_pool(ft, bt["feature_items"]) + P["hidden_bias"]
+        accumulator_context = board_pre @ P["policy_accumulator_hidden"].t()
+        rule_pre = bt["rule_context"] @ P["rule_context_hidden"]
+        sparse_hidden = torch.relu(board_pre + rule_pre)
+        rms = torch.sqrt((sparse_hidden * sparse_hidden).mean(1, keepdim=True) + 1.0e-6)
+        hidden = sparse_hidden / rms
+        value_head = torch.relu(hidden @ P["value_head_hidden"].t() + P["value_head_bias"])
+        value_logits = value_head @ P["value_head_output"].t()
+        threat_acc = pool.sparse_pool(P["value_threat_embedding"], bt["value_threat_indices"])
+        threat_act = threat_acc.clamp(0.0, 1.0)
+        threat_pair = torch.cat([threat_act, threat_act * threat_act], 1)
+        value_logits = value_logits + threat_pair @ P["value_threat_output"].t()
+        input_hidden = ft[:1260]
+        cs = min(32, h)
+        psp = input_hidden[:, :cs]
+        if cs < 32:
+            psp = torch.cat([psp, psp.new_zeros(1260, 32 - cs)], 1)
+        policy_context = hidden @ P["policy_context_hidden"].t() + threat_pair @ P["policy_threat_context"].t()
+        policy_context = torch.cat([policy_context, accumulator_context], 1)
+        accumulator_feature = input_hidden @ P["policy_accumulator_hidden"].t()
+        tables = torch.cat([psp.reshape(-1), P["policy_consequence_output"], P["policy_move_bias"],
+                            P["policy_move_context"].reshape(-1), accumulator_feature.reshape(-1),
+                            P["policy_accumulator_move"].reshape(-1)])
+        policy_logits = pol.fused_policy(tables, policy_context, bt["policy_items"])
+        policy_logits = policy_logits + pol.sparse_policy(P["sparse_tables"], bt["policy_sparse_indices"])
+        policy_logits = policy_logits + pol.tactical_policy(P["tactical_table"], bt["policy_tactical_indices"])
+        return value_logits, policy_logits
+
+    def loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0):
+        """compute_batch_loss (src/az/train_gpu_candle.rs:221-305) -> (loss
+        tensor = weighted CE sum / B, metrics tensor [30])."""
+        torch = self.torch
+        value_logits, policy_logits = self.forward(bt)
+        value_log_probs = torch.log_softmax(value_logits, 1)
+        value = (value_log_probs.exp() @ self._wdl_q)
+        value_ce_ps = (bt["value_wdl"] * value_log_probs * -1.0).sum(1)
+        log_policy = torch.log_softmax(policy_logits + bt["policy_mask"], 1)
+        policy_ce_ps = (bt["policy_targets"] * log_policy * -1.0).sum(1)
+        weighted_value = (value_ce_ps * bt["value_weights"]).sum() * max(value_weight, 0.0)
+        weighted_policy = (policy_ce_ps * bt["policy_weights"]).sum() * max(policy_weight, 0.0)
+        loss_sum = weighted_value + weighted_policy
+        batch = bt["values"].shape[0]
+        loss = loss_sum / batch
+        with torch.no_grad():
+            target = bt["values"]
+            err = value - target
+            per = torch.stack([value, value * value, target, target * target, value * target, err * err], 1)
+            phase = bt["value_phase_masks"].t() @ torch.cat([torch.ones_like(value)[:, None], per], 1)  # [3, 7]
+            metrics = torch.cat([torch.stack([loss_sum, value_ce_ps.sum(), policy_ce_ps.sum()]), per.sum(0),
+                                 phase.reshape(-1)])
+        return loss, metrics
+
+    def step(self, batch: PackedBatch, value_weight: float = 1.0, policy_weight: float = 1.0) -> TrainStats:
+        """One train_batch_single (src/az/train_gpu_candle.rs:145-160):
+        forward, loss, backward, AdamW."""
+        bt = self.to_device(batch)
+        self.grad.zero_()
+        loss, metrics = self.loss(bt, value_weight, policy_weight)
+        loss.backward()
+        self.step_count += 1
+        check(lib().cnnue_adamw(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(), self.grad.data_ptr(),
+                                self.n_params, self.lr, self.beta1, self.beta2, self.eps, self.weight_decay,
+                                self.step_count, self.torch.cuda.current_stream(self.device).cuda_stream),
+              "cnnue_adamw")
+        m = metrics.cpu().numpy()
+        return TrainStats(*[float(x) for x in m[:9]], samples=batch.batch_size, phase=m[9:].reshape(3, 7))
+
+    # -- weights ------------------------------------------------------------------
+    def tensors(self) -> list:
+        """The 22 weight tensors (host numpy copies) in the reference layout."""
+        h = self.hidden
+        host = self.flat.cpu().numpy()
+        out = []
+        for name, first, last, shape, off, n in self._layout:
+            pos = off
+            for i in range(first, last + 1):
+                k = az.tensor_info(i, h)[1]
+                out.append(host[pos:pos + k].reshape(az.tensor_shape(i, h)).copy())
+                pos += k
+        return out
+
+    def copy_to(self, weights: "az.AzWeights") -> None:
+        """copy_to_model (src/az/train_gpu_candle.rs:162-164); re-quantises."""
+        for i, t in enumerate(self.tensors()):
+            weights.tensor(i)[...] = t
+        weights.quantize()
+
+    def gradients(self) -> list:
+        """The last step's gradients as 22 host arrays (reference layout)."""
+        h = self.hidden
+        host = self.grad.cpu().numpy()
+        out = []
+        for name, first, last, shape, off, n in self._layout:
+            pos = off
+            for i in range(first, last + 1):
+                k = az.tensor_info(i, h)[1]
+                out.append(host[pos:pos + k].reshape(az.tensor_shape(i, h)).copy())
+                pos += k
+        return out

@@ -1,0 +1,118 @@
+// optim.cu - the AdamW step of the AZ-NNUE trainer over a flat fp32
+// parameter buffer, in one memory-bound pass (28 bytes per parameter: read
+// parameter, moments and gradient, write parameter and moments).
+//
+// The arithmetic restates candle-nn's AdamW::step (candle-nn 0.10, the
+// optimizer of src/az/train_gpu_candle.rs:113-122, :159; decoupled weight
+// decay after Loshchilov & Hutter) operation for operation in fp32:
+//   m' = (m*b1 + 0) + (g*(1-b1) + 0)
+//   v' = (v*b2 + 0) + ((g*g)*(1-b2) + 0)
+//   m^ = m'*sm + 0,  v^ = v'*sv + 0       sm = 1/(1-b1^t), sv = 1/(1-b2^t)
+//   p' = (p*(1-lr*wd) + 0) - ((m^ / (sqrt(v^)*1 + eps))*lr + 0)
+// where each "x*a + c" is one of candle's affine maps (a and c rounded to
+// fp32, no fused multiply-add) and the scalar factors are formed in double
+// (b^t by repeated squaring, as LLVM's powi runtime does) before rounding.
+#include "common.cuh"
+
+namespace cnnue {
+namespace opt {
+namespace {
+
+struct AdamWScalars {
+  float b1, omb1, b2, omb2, sm, sv, decay, lr, eps;
+};
+
+__device__ __forceinline__ float affine(float x, float a, float c) { return __fadd_rn(__fmul_rn(x, a), c); }
+
+__device__ __forceinline__ void adamw_one(float& p, float& m, float& v, float g, const AdamWScalars& k) {
+  const float nm = __fadd_rn(affine(m, k.b1, 0.f), affine(g, k.omb1, 0.f));
+  const float nv = __fadd_rn(affine(v, k.b2, 0.f), affine(__fmul_rn(g, g), k.omb2, 0.f));
+  const float mh = affine(nm, k.sm, 0.f);
+  const float vh = affine(nv, k.sv, 0.f);
+  const float den = affine(__fsqrt_rn(vh), 1.f, k.eps);
+  const float step = affine(__fdiv_rn(mh, den), k.lr, 0.f);
+  p = __fsub_rn(affine(p, k.decay, 0.f), step);
+  m = nm;
+  v = nv;
+}
+
+__global__ void __launch_bounds__(256) adamw_vec4_kernel(float4* __restrict__ p, float4* __restrict__ m,
+                                                         float4* __restrict__ v, const float4* __restrict__ g,
+                                                         int64_t n4, AdamWScalars k) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float4 pp = p[i], mm = m[i], vv = v[i];
+    const float4 gg = __ldg(g + i);
+    adamw_one(pp.x, mm.x, vv.x, gg.x, k);
+    adamw_one(pp.y, mm.y, vv.y, gg.y, k);
+    adamw_one(pp.z, mm.z, vv.z, gg.z, k);
+    adamw_one(pp.w, mm.w, vv.w, gg.w, k);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+  }
+}
+
+__global__ void adamw_scalar_kernel(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
+                                    const float* __restrict__ g, int64_t begin, int64_t n, AdamWScalars k) {
+  for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x)
+    adamw_one(p[i], m[i], v[i], g[i], k);
+}
+
+// b^e for e >= 0 by repeated squaring (the powi runtime routine).
+double powi(double b, int64_t e) {
+  double r = 1.0;
+  while (true) {
+    if (e & 1) r *= b;
+    e /= 2;
+    if (e == 0) break;
+    b *= b;
+  }
+  return r;
+}
+
+}  // namespace
+}  // namespace opt
+}  // namespace cnnue
+
+using namespace cnnue;
+using namespace cnnue::opt;
+
+extern "C" {
+
+int cnnue_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n, double lr, double beta1,
+                double beta2, double eps, double weight_decay, int64_t step, void* stream) {
+  if (n < 0 || (n > 0 && (!d_params || !d_m || !d_v || !d_grads)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
+  if (step < 1) return set_error(CNNUE_ERR_INVALID_ARG, "step must be >= 1");
+  if (n == 0) return CNNUE_OK;
+  AdamWScalars k;
+  k.b1 = (float)beta1;
+  k.omb1 = (float)(1.0 - beta1);
+  k.b2 = (float)beta2;
+  k.omb2 = (float)(1.0 - beta2);
+  k.sm = (float)(1.0 / (1.0 - powi(beta1, step)));
+  k.sv = (float)(1.0 / (1.0 - powi(beta2, step)));
+  k.decay = (float)(1.0 - lr * weight_decay);
+  k.lr = (float)lr;
+  k.eps = (float)eps;
+  cudaStream_t s = (cudaStream_t)stream;
+  const bool aligned = ((uintptr_t)d_params | (uintptr_t)d_m | (uintptr_t)d_v | (uintptr_t)d_grads) % 16 == 0;
+  int64_t done = 0;
+  if (aligned && n >= 4) {
+    const int64_t n4 = n / 4;
+    const unsigned blocks = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    adamw_vec4_kernel<<<blocks, 256, 0, s>>>((float4*)d_params, (float4*)d_m, (float4*)d_v, (const float4*)d_grads,
+                                            n4, k);
+    if (int st = check_launch_error("adamw_vec4_kernel")) return st;
+    done = n4 * 4;
+  }
+  if (done < n) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((n - done + 255) / 256, 148 * 8);
+    adamw_scalar_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, done, n, k);
+    if (int st = check_launch_error("adamw_scalar_kernel")) return st;
+  }
+  return CNNUE_OK;
+}
+
+}  // extern "C"

@@ -29,8 +29,41 @@ def _read_word(word: torch.Tensor, stream=None) -> int:
     return st.value
 
 
+class _FeaturePool(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, tables, items):
+        ctx.save_for_backward(items)
+        return _feature_pool_fwd(tables, items)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        (items,) = ctx.saved_tensors
+        return feature_pool_backward(items, grad_out.contiguous()), None
+
+
+class _SparsePool(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, table, items):
+        ctx.save_for_backward(items)
+        ctx.rows = table.shape[0]
+        return _sparse_pool_fwd(table, items)
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        (items,) = ctx.saved_tensors
+        return sparse_pool_backward(items, grad_out.contiguous(), ctx.rows), None
+
+
 def feature_pool(tables: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
-    """tables f32 [1545, H] (cuda), items [B, I] 4-byte (cuda) -> f32 [B, H]."""
+    """tables f32 [1545, H] (cuda), items [B, I] 4-byte (cuda) -> f32 [B, H].
+    Differentiable in `tables` (backward: feature_pool_backward) when called
+    on the current stream."""
+    if stream is None and torch.is_grad_enabled() and tables.requires_grad:
+        return _FeaturePool.apply(tables, items)
+    return _feature_pool_fwd(tables, items, stream)
+
+
+def _feature_pool_fwd(tables: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
     rows, hidden = tables.shape
     if rows != POOL_ROWS:
         raise ValueError(f"feature pool row mismatch: got {rows}, expected {POOL_ROWS}")
@@ -59,6 +92,14 @@ def feature_pool_backward(items: torch.Tensor, grad_out: torch.Tensor, stream=No
 
 
 def sparse_pool(table: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
+    """table f32 [R, H], items [B, I] 4-byte row indices (0xffffffff padding)
+    -> f32 [B, H]; differentiable in `table` like feature_pool."""
+    if stream is None and torch.is_grad_enabled() and table.requires_grad:
+        return _SparsePool.apply(table, items)
+    return _sparse_pool_fwd(table, items, stream)
+
+
+def _sparse_pool_fwd(table: torch.Tensor, items: torch.Tensor, stream=None) -> torch.Tensor:
     rows, hidden = table.shape
     batch, item_count = items.shape
     out = torch.empty((batch, hidden), dtype=torch.float32, device=table.device)

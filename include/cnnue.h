@@ -345,6 +345,16 @@ int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, 
                  float grad_scale, float lr, float beta1, float beta2, float eps, int step,
                  void* stream);
 
+/* AdamW step over n fp32 parameters (flat buffer) with moments m, v, as
+ * candle-nn's AdamW::step (the AZ trainer's optimizer, lr / betas / eps /
+ * weight decay as src/az/train_gpu_candle.rs:113-122), operation for
+ * operation in fp32: m' = m*b1 + g*(1-b1); v' = v*b2 + g*g*(1-b2);
+ * p' = p*(1 - lr*wd) - lr * (m'/(1-b1^t)) / (sqrt(v'/(1-b2^t)) + eps).
+ * step counts from 1.  One pass, no atomics. */
+int cnnue_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n, double lr,
+                double beta1, double beta2, double eps, double weight_decay, int64_t step,
+                void* stream);
+
 /* ---- reference-native AZ-NNUE evaluator (src/az.rs, src/nnue.rs) -------- */
 /* Squares are rank * 9 + file with rank 0 the first rank of a FEN (Black's
  * back rank), as src/xiangqi/geom.rs:28-30.  A board is int8_t[90]: 0 empty,

@@ -43,13 +43,15 @@ def lib() -> C.CDLL:
         h.oracle_policy_fused_bwd.argtypes = [P, P, P, P, i64, i64, P, P]
         h.oracle_policy_table_fwd.argtypes = [P, i64, P, i64, i32, P]
         h.oracle_policy_table_bwd.argtypes = [P, P, i64, i32, i64, P]
+        h.oracle_adamw.argtypes = [P, P, P, P, i64, C.c_double, C.c_double, C.c_double, C.c_double,
+                                    C.c_double, i64]
         h.oracle_q_bucket.argtypes = [u32]
         h.oracle_f_bucket.argtypes = [u32]
         for name in ("oracle_q_forward", "oracle_q_forward_mt", "oracle_q_update", "oracle_f_forward",
                      "oracle_feature_pool_fwd", "oracle_feature_pool_bwd", "oracle_sparse_pool_fwd",
                      "oracle_sparse_pool_bwd", "oracle_q_bucket", "oracle_f_bucket",
                      "oracle_policy_fused_fwd", "oracle_policy_fused_bwd", "oracle_policy_table_fwd",
-                     "oracle_policy_table_bwd",
+                     "oracle_policy_table_bwd", "oracle_adamw",
                      "oracle_max_threads"):
             getattr(h, name).restype = C.c_int
         _lib = h
@@ -179,6 +181,14 @@ def policy_table_bwd(indices: np.ndarray, grad_out: np.ndarray, table_len: int):
     grad = np.zeros(table_len, np.float32)
     st = lib().oracle_policy_table_bwd(_p(flat), _p(g), len(flat), terms, table_len, _p(grad))
     return st, grad
+
+
+def adamw(p, m, v, g, lr, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=1e-4, step=1):
+    """candle-nn AdamW step restated, in place on float32 arrays p, m, v."""
+    for a in (p, m, v):
+        assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    g = np.ascontiguousarray(g, np.float32)
+    return lib().oracle_adamw(_p(p), _p(m), _p(v), _p(g), p.size, lr, beta1, beta2, eps, weight_decay, step)
 
 
 def q_bucket(n0: int) -> int:

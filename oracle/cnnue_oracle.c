@@ -559,6 +559,40 @@ int oracle_policy_table_bwd(const int64_t* indices, const float* grad_out, int64
   return status;
 }
 
+/* ---- AdamW (candle-nn AdamW::step, the AZ trainer's optimizer) ---------- */
+/* Parity of this restatement with candle itself is unpinned (candle cannot be
+ * run here); the CUDA kernel is held to it bit for bit.  Each "x*a + c" is one
+ * of candle's fp32 affine maps; b^t by repeated squaring (the powi runtime). */
+static double oracle_powi(double b, int64_t e) {
+  double r = 1.0;
+  for (;;) {
+    if (e & 1) r *= b;
+    e /= 2;
+    if (e == 0) break;
+    b *= b;
+  }
+  return r;
+}
+
+int oracle_adamw(float* p, float* m, float* v, const float* g, int64_t n, double lr, double beta1, double beta2,
+                 double eps, double wd, int64_t step) {
+  const float b1 = (float)beta1, omb1 = (float)(1.0 - beta1), b2 = (float)beta2, omb2 = (float)(1.0 - beta2);
+  const float sm = (float)(1.0 / (1.0 - oracle_powi(beta1, step)));
+  const float sv = (float)(1.0 / (1.0 - oracle_powi(beta2, step)));
+  const float decay = (float)(1.0 - lr * wd), flr = (float)lr, feps = (float)eps;
+  for (int64_t i = 0; i < n; ++i) {
+    const float gi = g[i];
+    const float nm = (m[i] * b1 + 0.f) + (gi * omb1 + 0.f);
+    const float nv = (v[i] * b2 + 0.f) + ((gi * gi) * omb2 + 0.f);
+    const float mh = nm * sm + 0.f, vh = nv * sv + 0.f;
+    const float den = sqrtf(vh) * 1.f + feps;
+    p[i] = (p[i] * decay + 0.f) - ((mh / den) * flr + 0.f);
+    m[i] = nm;
+    v[i] = nv;
+  }
+  return 0;
+}
+
 /* ---- training step (data-parallel shard of one rank) ------------------- */
 /* Conventions fixed here (the workload specification leaves them open;
  * parity UNPINNED by the reference, whose trainer differs):

@@ -4,11 +4,18 @@
 //
 // Forward kernels keep the CPU twins' operation order (one product and one
 // add per term, no fused multiply-add), so outputs are bit-identical to them.
-// Backward passes are atomic-free: every scalar contribution to the table
-// gradient becomes a (table entry, value) pair, summed per entry in
-// contribution order by the deterministic scatter (scatter.cuh); the context
-// gradient of a board is summed over its moves in order by one thread per
-// (board, context column).
+// Backward passes are atomic-free and deterministic (scatter.cuh):
+//   - fused_policy: the table gradient splits by section.  Feature rows (the
+//     consequence rows and the accumulator feature rows, 1260 x 32 each) take
+//     one radix sort of up to three keys per item (to, from, captured) and a
+//     64-wide row sum per key; move rows (bias, move context, accumulator
+//     move factors) one sort by move index and a 49-wide row sum; the 32
+//     consequence weights, hit by every item, an ordered reduction in chunks
+//     of 256 items.  Values are formed on the fly from the item, in the CPU
+//     twin's operation order.  The context gradient of a board is summed over
+//     its moves in order by one thread per (board, context column);
+//   - sparse / tactical: scalar (entry, output) pairs through the scalar
+//     scatter.
 #include "common.cuh"
 #include "scatter.cuh"
 
@@ -24,7 +31,6 @@ constexpr int kPolicyValidBit = kCaptureValidBit + 1;        // 47
 constexpr uint32_t kConsequence = 40320, kBias = 40352, kContext = 42438, kAccFeature = 75814, kAccMove = 116134;
 constexpr uint32_t kTableLen = CNNUE_POLICY_TABLE_LEN;
 constexpr int kCtx = CNNUE_POLICY_CONTEXT;  // 16 move context + 32 accumulator context
-constexpr int kMaxContrib = 1 + 4 * 32 + 16 + 4 * 32;  // table contributions of one item
 
 struct Item {
   bool policy, move, capture;
@@ -85,70 +91,133 @@ __global__ void fused_fwd_kernel(const float* __restrict__ t, const float* __res
   }
 }
 
-// Table contributions of item i, kMaxContrib slots (unused slots get key
-// kTableLen, dropped by the scatter as "no table entry").
-__global__ void fused_contrib_kernel(const float* __restrict__ t, const float* __restrict__ ctx,
-                                     const int64_t* __restrict__ items, const float* __restrict__ g_out,
-                                     int64_t batch, int64_t moves, uint32_t* __restrict__ keys,
-                                     float* __restrict__ vals, uint32_t* status) {
-  const int64_t n = batch * moves;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    uint32_t* k = keys + i * kMaxContrib;
-    float* v = vals + i * kMaxContrib;
-    int c = 0;
+constexpr uint32_t kFeatureKeys = CNNUE_AZ_INPUT;  // drop key of the feature-row sort
+constexpr uint32_t kMoveKeys = CNNUE_AZ_DENSE_MOVES;
+constexpr int kConsChunk = 256;  // items per ordered chunk of the consequence-weight sums
+
+__device__ __forceinline__ bool live_move(const Item& it) { return it.policy && it.move && in_range(it); }
+
+// Feature-row keys: contribution e = 3 i + slot (slot 0 to, 1 from, 2 captured).
+__global__ void fused_feature_keys_kernel(const int64_t* __restrict__ items, int64_t n, uint32_t* __restrict__ keys,
+                                          uint32_t* status) {
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < 3 * n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = e / 3;
+    const int slot = (int)(e - 3 * i);
     const Item it = decode(items[i]);
-    const bool ok = it.policy && in_range(it);
-    if (it.policy && !ok) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
-    if (ok) {
-      const float g = g_out[i];
-      k[c] = kBias + it.mv;
-      v[c++] = g;
-      if (it.move) {
-        const float* cx = ctx + (i / moves) * kCtx;
-        for (int h = 0; h < 32; ++h) {
-          const float w = t[kConsequence + h];
-          float delta = __fsub_rn(t[it.to * 32 + h], t[it.from * 32 + h]);
-          const float gw = __fmul_rn(g, w);
-          k[c] = it.to * 32 + h;
-          v[c++] = gw;
-          k[c] = it.from * 32 + h;
-          v[c++] = -gw;
-          if (it.capture) {
-            delta = __fsub_rn(delta, t[it.cap * 32 + h]);
-            k[c] = it.cap * 32 + h;
-            v[c++] = -gw;
+    if (slot == 0 && it.policy && !in_range(it)) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+    uint32_t k = kFeatureKeys;
+    if (live_move(it)) {
+      if (slot == 0) k = it.to;
+      else if (slot == 1) k = it.from;
+      else if (it.capture) k = it.cap;
+    }
+    keys[e] = k;
+  }
+}
+
+__global__ void fused_move_keys_kernel(const int64_t* __restrict__ items, int64_t n, uint32_t* __restrict__ keys) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const Item it = decode(items[i]);
+    keys[i] = it.policy && in_range(it) ? it.mv : kMoveKeys;
+  }
+}
+
+// Column h < 32: consequence row; h >= 32: accumulator feature row.
+struct FeatureVal {
+  const float* t;
+  const int64_t* items;
+  const float* g;
+  __device__ __forceinline__ float operator()(uint32_t e, int64_t h) const {
+    const uint32_t i = e / 3u, slot = e - 3u * i;
+    const Item it = decode(__ldg(items + i));
+    const float w = h < 32 ? __ldg(t + kConsequence + h) : __ldg(t + kAccMove + it.mv * 32 + (h - 32));
+    const float gw = __fmul_rn(__ldg(g + i), w);
+    return slot == 0 ? gw : -gw;  // grad[from] -= g*w is grad[from] + (-(g*w)), exactly
+  }
+};
+struct FeatureOut {
+  float* gt;
+  __device__ __forceinline__ float& operator()(uint32_t key, int64_t h) const {
+    return h < 32 ? gt[key * 32 + h] : gt[kAccFeature + key * 32 + (h - 32)];
+  }
+};
+
+// Column 0: move bias; 1..16: move context; 17..48: accumulator move factors.
+struct MoveVal {
+  const float* t;
+  const float* ctx;
+  const int64_t* items;
+  const float* g;
+  int64_t moves;
+  __device__ __forceinline__ float operator()(uint32_t i, int64_t h) const {
+    const float gi = __ldg(g + i);
+    if (h == 0) return gi;
+    const Item it = decode(__ldg(items + i));
+    if (!it.move) return 0.f;  // adds +0: partial sums here never hold -0
+    const float* c = ctx + (i / moves) * kCtx;
+    if (h <= 16) return __fmul_rn(gi, __ldg(c + h - 1));
+    const int64_t hh = h - 17;
+    float after = __fsub_rn(__fadd_rn(__ldg(c + 16 + hh), __ldg(t + kAccFeature + it.to * 32 + hh)),
+                            __ldg(t + kAccFeature + it.from * 32 + hh));
+    if (it.capture) after = __fsub_rn(after, __ldg(t + kAccFeature + it.cap * 32 + hh));
+    return __fmul_rn(gi, after);
+  }
+};
+struct MoveOut {
+  float* gt;
+  __device__ __forceinline__ float& operator()(uint32_t key, int64_t h) const {
+    if (h == 0) return gt[kBias + key];
+    if (h <= 16) return gt[kContext + key * 16 + (h - 1)];
+    return gt[kAccMove + key * 32 + (h - 17)];
+  }
+};
+
+// Consequence weights: chunk c of kConsChunk items summed in item order per
+// column (8 items' loads in flight); a single chunk writes the result.
+__global__ void cons_chunk_kernel(const float* __restrict__ t, const int64_t* __restrict__ items,
+                                  const float* __restrict__ g, int64_t n, int64_t n_chunks, float* __restrict__ partial,
+                                  float* __restrict__ gt) {
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < n_chunks * 32;
+       q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = q >> 5;
+    const int h = (int)(q & 31);
+    const int64_t i0 = c * kConsChunk, i1 = min(n, i0 + kConsChunk);
+    float s = 0.f;
+    for (int64_t i = i0; i < i1; i += 8) {
+      float v[8];
+      bool live[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        live[k] = false;
+        v[k] = 0.f;
+        if (i + k < i1) {
+          const Item it = decode(__ldg(items + i + k));
+          if (live_move(it)) {
+            float delta = __fsub_rn(__ldg(t + it.to * 32 + h), __ldg(t + it.from * 32 + h));
+            if (it.capture) delta = __fsub_rn(delta, __ldg(t + it.cap * 32 + h));
+            v[k] = __fmul_rn(__ldg(g + i + k), delta);
+            live[k] = true;
           }
-          k[c] = kConsequence + h;
-          v[c++] = __fmul_rn(g, delta);
-        }
-        for (int h = 0; h < 16; ++h) {
-          k[c] = kContext + it.mv * 16 + h;
-          v[c++] = __fmul_rn(g, cx[h]);
-        }
-        for (int h = 0; h < 32; ++h) {
-          const uint32_t mf = kAccMove + it.mv * 32 + h;
-          const float w = t[mf];
-          float after = __fsub_rn(__fadd_rn(cx[16 + h], t[kAccFeature + it.to * 32 + h]), t[kAccFeature + it.from * 32 + h]);
-          const float gw = __fmul_rn(g, w);
-          k[c] = kAccFeature + it.to * 32 + h;
-          v[c++] = gw;
-          k[c] = kAccFeature + it.from * 32 + h;
-          v[c++] = -gw;
-          if (it.capture) {
-            after = __fsub_rn(after, t[kAccFeature + it.cap * 32 + h]);
-            k[c] = kAccFeature + it.cap * 32 + h;
-            v[c++] = -gw;
-          }
-          k[c] = mf;
-          v[c++] = __fmul_rn(g, after);
         }
       }
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (live[k]) s = __fadd_rn(s, v[k]);
     }
-    for (; c < kMaxContrib; ++c) {
-      k[c] = kTableLen;
-      v[c] = 0.f;
-    }
+    if (n_chunks == 1) gt[kConsequence + h] = s;
+    else partial[c * 32 + h] = s;
   }
+}
+
+// Chunk partials of one column: lane l sums chunks l, l+32, ... in order,
+// then the lanes combine in a fixed butterfly.  One warp per column.
+__global__ void cons_final_kernel(const float* __restrict__ partial, int64_t n_chunks, float* __restrict__ gt) {
+  const int h = blockIdx.x, lane = threadIdx.x;
+  float s = 0.f;
+  for (int64_t c = lane; c < n_chunks; c += 32) s = __fadd_rn(s, partial[c * 32 + h]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if (lane == 0) gt[kConsequence + h] = s;
 }
 
 // grad_context[b][col]: the board's moves in order (one thread per (b, col)).
@@ -219,8 +288,11 @@ int cnnue_policy_fused_fwd(const float* d_tables, const float* d_context, const 
 }
 
 size_t cnnue_policy_fused_bwd_workspace_bytes(int64_t batch, int64_t moves) {
-  const int64_t n = std::max<int64_t>(batch * moves, 0) * kMaxContrib;
-  return sizeof(WorkspaceHeader) + align_up((size_t)n * 4, 256) * 2 + scat::workspace_bytes(n);
+  const int64_t n = std::max<int64_t>(batch * moves, 0);
+  const int64_t chunks = std::max<int64_t>((n + kConsChunk - 1) / kConsChunk, 1);
+  return sizeof(WorkspaceHeader) + align_up((size_t)std::max<int64_t>(3 * n, 1) * 4, 256) +
+         align_up((size_t)std::max<int64_t>(n, 1) * 4, 256) + align_up((size_t)chunks * 32 * 4, 256) +
+         std::max(scat::workspace_bytes(3 * n, 64), scat::workspace_bytes(n, 49));
 }
 
 int cnnue_policy_fused_bwd(const float* d_tables, const float* d_context, const int64_t* d_items,
@@ -232,26 +304,41 @@ int cnnue_policy_fused_bwd(const float* d_tables, const float* d_context, const 
   if (ws_bytes < cnnue_policy_fused_bwd_workspace_bytes(batch, moves))
     return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu < %zu bytes", ws_bytes,
                      cnnue_policy_fused_bwd_workspace_bytes(batch, moves));
-  const int64_t n = batch * moves * kMaxContrib;
-  if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "batch x moves too large");
+  const int64_t n = batch * moves;
+  if (3 * n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "batch x moves too large");
   cudaStream_t s = (cudaStream_t)stream;
   CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  CNNUE_CUDA_TRY(cudaMemsetAsync(d_grad_tables, 0, sizeof(float) * kTableLen, s));
+  if (n == 0) return CNNUE_OK;
   uint32_t* status = &((WorkspaceHeader*)ws)->status;
   char* p = (char*)ws + sizeof(WorkspaceHeader);
-  uint32_t* keys = (uint32_t*)p;
+  uint32_t* fkeys = (uint32_t*)p;
+  p += align_up((size_t)(3 * n) * 4, 256);
+  uint32_t* mkeys = (uint32_t*)p;
   p += align_up((size_t)n * 4, 256);
-  float* vals = (float*)p;
-  p += align_up((size_t)n * 4, 256);
-  if (batch * moves > 0) {
-    fused_contrib_kernel<<<grid_for(batch * moves), 256, 0, s>>>(d_tables, d_context, d_items, d_grad_out, batch,
-                                                                moves, keys, vals, status);
-    if (int st = check_launch_error("fused_contrib_kernel")) return st;
-    fused_ctx_grad_kernel<<<grid_for(batch * kCtx), 256, 0, s>>>(d_tables, d_items, d_grad_out, batch, moves,
-                                                                d_grad_context);
-    if (int st = check_launch_error("fused_ctx_grad_kernel")) return st;
+  const int64_t chunks = (n + kConsChunk - 1) / kConsChunk;
+  float* cons_partial = (float*)p;
+  p += align_up((size_t)chunks * 32 * 4, 256);
+  fused_feature_keys_kernel<<<grid_for(3 * n), 256, 0, s>>>(d_items, n, fkeys, status);
+  if (int st = check_launch_error("fused_feature_keys_kernel")) return st;
+  fused_move_keys_kernel<<<grid_for(n), 256, 0, s>>>(d_items, n, mkeys);
+  if (int st = check_launch_error("fused_move_keys_kernel")) return st;
+  fused_ctx_grad_kernel<<<grid_for(batch * kCtx), 256, 0, s>>>(d_tables, d_items, d_grad_out, batch, moves,
+                                                              d_grad_context);
+  if (int st = check_launch_error("fused_ctx_grad_kernel")) return st;
+  cons_chunk_kernel<<<grid_for(chunks * 32), 256, 0, s>>>(d_tables, d_items, d_grad_out, n, chunks, cons_partial,
+                                                          d_grad_tables);
+  if (int st = check_launch_error("cons_chunk_kernel")) return st;
+  if (chunks > 1) {
+    cons_final_kernel<<<32, 32, 0, s>>>(cons_partial, chunks, d_grad_tables);
+    if (int st = check_launch_error("cons_final_kernel")) return st;
   }
-  // unused slots carry key kTableLen, which the scatter drops
-  return scat::launch_scatter_add(keys, vals, 1, n, kTableLen, d_grad_tables, p, s);
+  // the two row sorts share the scatter workspace (stream order separates them)
+  if (int st = scat::launch_scatter_rows(fkeys, FeatureVal{d_tables, d_items, d_grad_out}, FeatureOut{d_grad_tables},
+                                         64, 3 * n, kFeatureKeys, p, s))
+    return st;
+  return scat::launch_scatter_rows(mkeys, MoveVal{d_tables, d_context, d_items, d_grad_out, moves},
+                                   MoveOut{d_grad_tables}, 49, n, kMoveKeys, p, s);
 }
 
 int cnnue_policy_table_fwd(const float* d_table, int64_t table_len, const int64_t* d_indices, int64_t outputs,

@@ -240,12 +240,13 @@ __global__ void run_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t
 }
 
 // Row form: one warp per unit; lanes walk the columns 32 at a time.  A
-// unit that is its run's only one writes the table row directly.
-__global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx,
-                                     const float* __restrict__ values, uint32_t div, int64_t hidden,
-                                     const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ unit_off,
-                                     uint32_t n_runs, uint32_t n_units, int64_t n, int64_t n_keys,
-                                     float* __restrict__ partial, float* __restrict__ out) {
+// unit that is its run's only one writes the table row directly.  Val(e, h)
+// gives column h of contribution e; Out(key, h) the output element.
+template <class Val, class Out>
+__global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx, Val val,
+                                     int64_t hidden, const uint32_t* __restrict__ run_start,
+                                     const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
+                                     int64_t n, int64_t n_keys, float* __restrict__ partial, Out out) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n_units; u += warps) {
@@ -261,35 +262,31 @@ __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const ui
     const uint32_t beg = rbeg + ((uint32_t)u - unit_off[r]) * kUnit;
     const uint32_t end = min(rend, beg + kUnit);
     const uint32_t key = keys[rbeg];
-    float* dst;
-    if (u1 - unit_off[r] == 1) {
-      if ((int64_t)key >= n_keys) continue;  // dropped contributions
-      dst = out + (int64_t)key * hidden;
-    } else {
-      dst = partial + u * hidden;
-    }
+    const bool single = u1 - unit_off[r] == 1;
+    if ((int64_t)key >= n_keys) continue;  // dropped contributions: never evaluated
     for (int64_t h = lane; h < hidden; h += 32) {
       float s = 0.f;
       uint32_t j = beg;
       for (; j + 8 <= end; j += 8) {
         float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = __ldg(values + (int64_t)(__ldg(idx + j + k) / div) * hidden + h);
+        for (int k = 0; k < 8; ++k) v[k] = val(__ldg(idx + j + k), h);
 #pragma unroll
         for (int k = 0; k < 8; ++k) s += v[k];
       }
-      for (; j < end; ++j) s += __ldg(values + (int64_t)(__ldg(idx + j) / div) * hidden + h);
-      dst[h] = s;
+      for (; j < end; ++j) s += val(__ldg(idx + j), h);
+      if (single) out(key, h) = s;
+      else partial[u * hidden + h] = s;
     }
   }
 }
 
 // Runs of several units add their partial rows in order (one thread per
 // (run, column); single-unit runs were written by unit_sum_rows_kernel).
+template <class Out>
 __global__ void run_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ run_start,
                                     const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
-                                    const float* __restrict__ partial, int64_t hidden, int64_t n_keys,
-                                    float* __restrict__ out) {
+                                    const float* __restrict__ partial, int64_t hidden, int64_t n_keys, Out out) {
   const int64_t total = (int64_t)n_runs * hidden;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = q / hidden, h = q - r * hidden;
@@ -299,9 +296,25 @@ __global__ void run_sum_rows_kernel(const uint32_t* __restrict__ keys, const uin
     if ((int64_t)k >= n_keys) continue;
     float s = partial[(int64_t)u0 * hidden + h];
     for (uint32_t u = u0 + 1; u < u1; ++u) s += partial[(int64_t)u * hidden + h];
-    out[(int64_t)k * hidden + h] = s;
+    out(k, h) = s;
   }
 }
+
+// Values of a plain row-major buffer: contribution e adds row e / div.
+struct BufferRows {
+  const float* values;
+  uint32_t div;
+  int64_t hidden;
+  __device__ __forceinline__ float operator()(uint32_t e, int64_t h) const {
+    return __ldg(values + (int64_t)(e / div) * hidden + h);
+  }
+};
+// A dense row-major table out[key][hidden].
+struct DenseRows {
+  float* out;
+  int64_t hidden;
+  __device__ __forceinline__ float& operator()(uint32_t key, int64_t h) const { return out[(int64_t)key * hidden + h]; }
+};
 
 // Workspace of launch_scatter_add(_rows) for n contributions of `hidden`
 // values each.
@@ -417,28 +430,39 @@ int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, 
   return check_launch_error("scatter run sums");
 }
 
-// Row form: out[k][h] = sum over i (same order) of values[(i / div) * hidden
-// + h] with keys[i] == k, for a table out[n_keys][hidden].
-int launch_scatter_add_rows(const uint32_t* keys, const float* values, uint32_t div, int64_t hidden, int64_t n,
-                            int64_t n_keys, float* out, void* ws, cudaStream_t s) {
-  const int64_t total = n_keys * hidden;
-  const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
-  zero_kernel<<<zb, 256, 0, s>>>(out, total);
-  if (int st = check_launch_error("scatter zero")) return st;
+// Row form over functors: for every key k < n_keys hit by a contribution,
+// out(k, h) = sum over contributions e with keys[e] == k (in order, units of
+// 256) of val(e, h).  Rows nobody hits are not written (the caller zeroes
+// them); keys must be <= n_keys, key n_keys is dropped.
+template <class Val, class Out>
+int launch_scatter_rows(const uint32_t* keys, Val val, Out out, int64_t hidden, int64_t n, int64_t n_keys, void* ws,
+                        cudaStream_t s) {
   if (n <= 0) return CNNUE_OK;
   if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
   Runs r;
   if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
   const unsigned ub =
       (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_units * 32 + 255) / 256, 148 * 16));
-  unit_sum_rows_kernel<<<ub, 256, 0, s>>>(r.keys, r.idx, values, div, hidden, r.run_start, r.unit_off, r.n_runs,
-                                          r.n_units, n, n_keys, r.partial, out);
+  unit_sum_rows_kernel<<<ub, 256, 0, s>>>(r.keys, r.idx, val, hidden, r.run_start, r.unit_off, r.n_runs, r.n_units,
+                                          n, n_keys, r.partial, out);
   if (int st = check_launch_error("scatter unit row sums")) return st;
   const unsigned rb =
       (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_runs * hidden + 255) / 256, 148 * 16));
   run_sum_rows_kernel<<<rb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, hidden,
                                          n_keys, out);
   return check_launch_error("scatter run row sums");
+}
+
+// Dense form: out[k][h] = sum over i (same order) of values[(i / div) *
+// hidden + h] with keys[i] == k, for a table out[n_keys][hidden] (zeroed
+// first).
+int launch_scatter_add_rows(const uint32_t* keys, const float* values, uint32_t div, int64_t hidden, int64_t n,
+                            int64_t n_keys, float* out, void* ws, cudaStream_t s) {
+  const int64_t total = n_keys * hidden;
+  const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, 148 * 8));
+  zero_kernel<<<zb, 256, 0, s>>>(out, total);
+  if (int st = check_launch_error("scatter zero")) return st;
+  return launch_scatter_rows(keys, BufferRows{values, div, hidden}, DenseRows{out, hidden}, hidden, n, n_keys, ws, s);
 }
 
 }  // namespace

@@ -280,11 +280,13 @@ int cnnue_policy_fused_fwd(const float* d_tables, const float* d_context, const 
                            void* stream);
 /* Backward of fused_policy: d_grad_tables [182886] and d_grad_context [B][48]
  * are overwritten.  No atomics: grad_context[b] adds its board's moves in
- * order; every table contribution is summed per entry in item order by a
- * stable radix sort of (entry, contribution) pairs (entries hit by at most
- * 256 contributions equal the CPU twin bit for bit, longer runs are summed in
- * ordered units of 256).  Bad items are flagged in the workspace status.
- * Synchronises the stream (the sort's run counts are read back).
+ * order; table entries are summed in item order through stable radix sorts of
+ * the feature rows (to, from, captured) and move rows each item touches.  An
+ * entry with at most 256 contributions equals the CPU twin bit for bit; the
+ * 32 consequence weights (every move item contributes) do when the batch has
+ * at most 256 items.  Longer sums run in ordered units of 256: deterministic.
+ * Bad items are flagged in the workspace status.  Synchronises the stream
+ * (the sorts' run counts are read back).
  * Replaces FusedPolicyGrad (src/az/fused_policy.rs:263-371, CPU twin :287-366,
  * CUDA kernel fused_policy_grad :73-126, which uses atomicAdd). */
 size_t cnnue_policy_fused_bwd_workspace_bytes(int64_t batch, int64_t moves);

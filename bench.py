@@ -679,6 +679,128 @@ def run_az(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# AZ-NNUE training step (--workload az-train; not the headline line)
+# ---------------------------------------------------------------------------
+AZ_TRAIN_BATCH = 1024  # the reference's default batch (src/az_loop_config.rs:115)
+AZ_TRAIN_CAPS = (40, 96, 96)  # fixed per-row widths: features, policy moves, threats
+
+
+def run_az_train(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    from chineseai_b200 import az, az_train
+
+    B = AZ_TRAIN_BATCH
+    w = az.AzWeights.random(128, 20260807)
+    samples = az_train.random_samples(4 * B, seed=1 + rank)
+    t0 = time.time()
+    batches = [az_train.pack_batch(samples, np.arange(k * B, (k + 1) * B), caps=AZ_TRAIN_CAPS, fixed=True)
+               for k in range(4)]
+    pack_ms = (time.time() - t0) / 4 * 1e3
+    tr = az_train.AzTrainer(w, lr=1e-3, device=local, graph=True)
+    for i in range(max(args.warmup, 3)):
+        tr.step(batches[i % 4])
+    # kernels of one step: a profiled eager step of a twin trainer (outside the timed region)
+    from torch.profiler import ProfilerActivity, profile
+    twin = az_train.AzTrainer(w, lr=1e-3, device=local)
+    twin.step(batches[0])
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        twin.step(batches[1])
+        torch.cuda.synchronize(dev)
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours_per_step = sum(1 for n in names if "cnnue" in n)
+    all_per_step = sum(1 for n in names if not n.startswith("Memcpy") and not n.startswith("Memset"))
+    del twin
+    stream = torch.cuda.current_stream(dev)
+    # device-resident: replays of the captured step on a batch already in HBM
+    tr.to_device(batches[0])
+    torch.cuda.synchronize(dev)
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    total = _device_loop(tr._graph.replay, args.steps, dev, stream)
+    clocks = sampler.stop()
+    # end to end: AzTrainer.step on host batches (pinned staging + H2D, metrics back)
+    e2e_total = _device_loop(lambda: tr.step(batches[np.random.randint(4)]), args.steps, dev, stream)
+    # AdamW alone (the one kernel with a clean roofline: 28 bytes per parameter)
+    adam_ms = _device_loop(
+        lambda: az_train.lib().cnnue_adamw(tr.flat.data_ptr(), tr.m.data_ptr(), tr.v.data_ptr(),
+                                           tr.grad.data_ptr(), tr.n_params, 1e-9, 0.9, 0.999, 1e-8, 0.0,
+                                           tr.step_count + 1, stream.cuda_stream), args.steps, dev, stream)
+    stats = torch.tensor([total, e2e_total, adam_ms], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, e2e_total, adam_ms = stats.tolist()
+    if rank == 0:
+        ms = total / args.steps
+        a_ms = adam_ms / args.steps
+        peak, peak_kind = measured_hbm_peak()
+        adam_bytes = 28 * tr.n_params
+        achieved = adam_bytes / (a_ms / 1e3) / 1e9
+        b0 = batches[0]
+        h2d = sum(np.asarray(getattr(b0, f)).nbytes for f in
+                  ("feature_items", "value_threat_indices", "policy_items", "policy_sparse_indices",
+                   "policy_tactical_indices", "policy_targets", "policy_mask", "value_wdl", "values",
+                   "rule_context", "policy_weights", "value_weights", "value_phase_masks"))
+        line = {
+            "metric": "AZ-NNUE training samples/sec (forward, WDL + masked policy CE, backward, AdamW; H=128)",
+            "value": world * B / (ms / 1e3), "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "AzNnue::random(128, 20260807); batch 1024 synthetic self-play samples "
+                                   "(random boards, pseudo moves, gamma visit targets), fixed widths "
+                                   f"{AZ_TRAIN_CAPS}; one CUDA-graph step", "batch_per_gpu": B,
+                       "parallelism": f"replicas{world}", "host_pack_ms_per_batch": pack_ms,
+                       "l2": "not flushed: the step's inputs and parameters (~33 MB) are L2-sized"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "scope": f"adamw_vec4_kernel alone: 28 B x {tr.n_params} parameters per launch, "
+                                  f"{a_ms * 1e3:.1f} us"},
+            "e2e": {"value": world * B / (e2e_total / args.steps / 1e3), "unit": "samples/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": 31 * 4},
+            "clocks": clocks, "gpu_launches": ours_per_step * args.steps,
+            "kernels_per_step": {"ours": ours_per_step, "all": all_per_step},
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            from oracle import az_train_ref
+            torch.set_num_threads(cpu_threads())
+            sample = 64
+            sb = az_train.pack_batch(samples, np.arange(sample))
+            tensors = w.tensors()
+            t0 = time.time()
+            n_rep = 0
+            while time.time() - t0 < min(args.cpu_seconds, 15.0) or n_rep == 0:
+                _, grads = az_train_ref.gradients(tensors, sb, dtype=torch.float32)
+                flat_p = np.concatenate([t.reshape(-1) for t in tensors]).astype(np.float32)
+                flat_g = np.concatenate([g.reshape(-1) for g in grads]).astype(np.float32)
+                oracle.adamw(flat_p, np.zeros_like(flat_p), np.zeros_like(flat_p), flat_g, 1e-3, step=1)
+                n_rep += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": n_rep * sample / el, "unit": "samples/s", "cores": cpu_threads(),
+                                    "kind": "port",
+                                    "sample": f"{n_rep} steps of {sample} samples: torch-CPU restatement "
+                                              "(fp32 autograd) + the oracle's AdamW"}
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -687,9 +809,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az"], default="eval",
+    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az", "az-train"], default="eval",
                     help="eval: the headline quantised forward; train: the data-parallel training step; "
-                         "resnet: AlphaZero ResNet leaf batch; az: reference-native AZ-NNUE evaluation")
+                         "resnet: AlphaZero ResNet leaf batch; az: reference-native AZ-NNUE evaluation; "
+                         "az-train: the AZ-NNUE training step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -701,6 +824,8 @@ def main():
         return run_resnet(args)
     if args.workload == "az":
         return run_az(args)
+    if args.workload == "az-train":
+        return run_az_train(args)
     return run_ours(args)
 
 

@@ -152,8 +152,10 @@ def _samples_struct(s: Samples, keep: list) -> _CSamples:
 
 
 def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: int = 0,
-               caps=(96, 160, 256)) -> PackedBatch:
-    """Packs samples[rows] (all samples when rows is None) with the native packer."""
+               caps=(96, 160, 256), fixed: bool = False) -> PackedBatch:
+    """Packs samples[rows] (all samples when rows is None) with the native
+    packer.  fixed=True: the arrays take the `caps` widths whatever the batch
+    needs (CnnueError if it needs more), for a trainer with a captured step."""
     keep: list = []
     cs = _samples_struct(samples, keep)
     if rows is None:
@@ -174,9 +176,9 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
             "policy_weights": np.empty(b, np.float32), "value_weights": np.empty(b, np.float32),
             "value_phase_masks": np.empty((b, 3), np.float32)}
         out = _CPacked(0, 0, 0, 0, *[bufs[k].ctypes.data for k in _PACKED_FIELDS])
-        st = lib().cnnue_az_pack_batch(C.byref(cs), rptr, batch, F, M, T, C.byref(out), n_threads)
+        st = lib().cnnue_az_pack_batch(C.byref(cs), rptr, batch, F, M, T, int(fixed), C.byref(out), n_threads)
         need = (out.max_features, out.max_policy_moves, out.max_value_threats)
-        if st == 5 and any(n > c for n, c in zip(need, caps)):  # CNNUE_ERR_WORKSPACE: grow and retry
+        if st == 5 and not fixed and any(n > c for n, c in zip(need, caps)):  # CNNUE_ERR_WORKSPACE: grow, retry
             caps = tuple(max(n, c) for n, c in zip(need, caps))
             continue
         check(st, "cnnue_az_pack_batch")
@@ -198,6 +200,15 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
 
 
 # ---- the training step --------------------------------------------------------
+def _raise_status(word: int, where: str) -> None:
+    """The kernels' status bits as cnnue_read_status maps them."""
+    if word == 0:
+        return
+    from ._lib import CnnueError
+    code = 3 if word & 2 else (2 if word & 1 else (9 if word & 4 else 10))
+    raise CnnueError(code, where, f"kernel status word 0x{word:x}")
+
+
 # Leaves of the flat parameter buffer: (name, first tensor, last tensor, shape).
 # Tensors 0-4 form the [1545, H] feature table of feature_pool, 19-20 the
 # sparse policy table, and the tactical table (last) carries one constant
@@ -242,12 +253,22 @@ class TrainStats:
 
 
 class AzTrainer:
-    """GpuTrainer (src/az/train_gpu_candle.rs:15-160) on one CUDA device."""
+    """GpuTrainer (src/az/train_gpu_candle.rs:15-160) on one CUDA device.
+
+    graph=True captures the whole step (forward, loss, backward, AdamW) in a
+    CUDA graph once a batch shape repeats (batches packed with fixed=True all
+    share one shape), and replays it; the first step of each new shape runs
+    eagerly.  The AdamW step counter and learning rate live in device memory
+    (cnnue_adamw_device), so replays advance them."""
 
     def __init__(self, weights: "az.AzWeights", lr: float = 1e-3, device: int = 0, weight_decay: float = 1e-4,
-                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8):
+                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False):
         import torch
         self.torch = torch
+        self.use_graph = graph
+        self._graph = None
+        self._graph_key = None
+        self._last_key = None
         self.hidden = h = weights.hidden
         self.device = torch.device("cuda", device)
         self.lr, self.beta1, self.beta2, self.eps, self.weight_decay = lr, beta1, beta2, eps, weight_decay
@@ -275,18 +296,50 @@ class AzTrainer:
             p.grad = self.grad[off:off + n].view(shape)
             self.params[name] = p
         self._wdl_q = torch.tensor([1.0, 0.0, -1.0], device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._pinned = None
+        self._arena = None
+        # cnnue_adamw_state: lr, beta1, beta2, eps, weight_decay (f64), step (i64), 12 floats
+        state = np.zeros(12, np.float64)
+        state[:5] = [lr, beta1, beta2, eps, weight_decay]
+        self.adam_state = torch.from_numpy(state.view(np.uint8).copy()).to(self.device)
+
+    def set_learning_rate(self, lr: float) -> None:
+        """GpuTrainer::set_learning_rate (src/az/train_gpu_candle.rs:134-136)."""
+        self.lr = lr
+        self.adam_state[:8].copy_(self.torch.from_numpy(np.array([lr], np.float64).view(np.uint8)))
 
     # -- data ---------------------------------------------------------------
     def to_device(self, b: PackedBatch) -> dict:
-        """BatchTensors::from_packed (src/az/candle_model.rs:173-233)."""
+        """BatchTensors::from_packed (src/az/candle_model.rs:173-233): the
+        batch's arrays staged in one pinned host buffer and sent in one copy;
+        the device tensors are views of one device buffer (valid until the
+        next call)."""
         torch = self.torch
-
-        def t(a):
-            a = np.ascontiguousarray(a)
+        arrays, offsets, total = [], [], 0
+        for f in fields(PackedBatch):
+            a = np.ascontiguousarray(getattr(b, f.name))
             if a.dtype == np.uint32:
                 a = a.view(np.int32)
-            return torch.from_numpy(a).to(self.device, non_blocking=True)
-        return {f.name: t(getattr(b, f.name)) for f in fields(PackedBatch)}
+            arrays.append((f.name, a))
+            offsets.append(total)
+            total += (a.nbytes + 255) // 256 * 256
+        if self._pinned is None or self._pinned.numel() < total:
+            self._pinned = torch.empty(total, dtype=torch.uint8, pin_memory=True)
+            self._arena = torch.empty(total, dtype=torch.uint8, device=self.device)
+        host = self._pinned.numpy()
+        for (name, a), off in zip(arrays, offsets):
+            host[off:off + a.nbytes] = a.reshape(-1).view(np.uint8)
+        self._arena[:total].copy_(self._pinned[:total], non_blocking=True)
+        self._last_h2d = total
+        dt = {np.dtype(np.int32): torch.int32, np.dtype(np.int64): torch.int64, np.dtype(np.float32): torch.float32}
+        return {name: self._arena[off:off + a.nbytes].view(dt[a.dtype]).view(a.shape)
+                for (name, a), off in zip(arrays, offsets)}
+
+    @property
+    def h2d_bytes(self) -> int:
+        """Bytes of the last batch's host-to-device copy."""
+        return 0 if self._pinned is None else int(self._last_h2d)
 
     # -- model ----------------------------------------------------------------
     def forward(self, bt: dict):
@@ -298,7 +351,8 @@ class AzTrainer:
         P = self.params
         h = self.hidden
         ft = P["feature_tables"]
-        board_pre = pool.feature_pool(ft, bt["feature_items"]) + P["hidden_bias"]
+        st = self.status
+        board_pre = pool.feature_pool(ft, bt["feature_items"], status=st) + P["hidden_bias"]
         accumulator_context = board_pre @ P["policy_accumulator_hidden"].t()
         rule_pre = bt["rule_context"] @ P["rule_context_hidden"]
         sparse_hidden = torch.relu(board_pre + rule_pre)
@@ -306,7 +360,7 @@ class AzTrainer:
         hidden = sparse_hidden / rms
         value_head = torch.relu(hidden @ P["value_head_hidden"].t() + P["value_head_bias"])
         value_logits = value_head @ P["value_head_output"].t()
-        threat_acc = pool.sparse_pool(P["value_threat_embedding"], bt["value_threat_indices"])
+        threat_acc = pool.sparse_pool(P["value_threat_embedding"], bt["value_threat_indices"], status=st)
         threat_act = threat_acc.clamp(0.0, 1.0)
         threat_pair = torch.cat([threat_act, threat_act * threat_act], 1)
         value_logits = value_logits + threat_pair @ P["value_threat_output"].t()
@@ -321,9 +375,9 @@ class AzTrainer:
         tables = torch.cat([psp.reshape(-1), P["policy_consequence_output"], P["policy_move_bias"],
                             P["policy_move_context"].reshape(-1), accumulator_feature.reshape(-1),
                             P["policy_accumulator_move"].reshape(-1)])
-        policy_logits = pol.fused_policy(tables, policy_context, bt["policy_items"])
-        policy_logits = policy_logits + pol.sparse_policy(P["sparse_tables"], bt["policy_sparse_indices"])
-        policy_logits = policy_logits + pol.tactical_policy(P["tactical_table"], bt["policy_tactical_indices"])
+        policy_logits = pol.fused_policy(tables, policy_context, bt["policy_items"], st)
+        policy_logits = policy_logits + pol.sparse_policy(P["sparse_tables"], bt["policy_sparse_indices"], st)
+        policy_logits = policy_logits + pol.tactical_policy(P["tactical_table"], bt["policy_tactical_indices"], st)
         return value_logits, policy_logits
 
     def loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0):
@@ -350,20 +404,47 @@ class AzTrainer:
                                  phase.reshape(-1)])
         return loss, metrics
 
-    def step(self, batch: PackedBatch, value_weight: float = 1.0, policy_weight: float = 1.0) -> TrainStats:
-        """One train_batch_single (src/az/train_gpu_candle.rs:145-160):
-        forward, loss, backward, AdamW."""
-        bt = self.to_device(batch)
+    def _step_body(self, bt: dict, value_weight: float, policy_weight: float):
         self.grad.zero_()
+        self.status.zero_()
         loss, metrics = self.loss(bt, value_weight, policy_weight)
         loss.backward()
+        check(lib().cnnue_adamw_device(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                                       self.grad.data_ptr(), self.n_params, self.adam_state.data_ptr(),
+                                       self.torch.cuda.current_stream(self.device).cuda_stream),
+              "cnnue_adamw_device")
+        return self.torch.cat([metrics, self.status.float()])
+
+    def step(self, batch: PackedBatch, value_weight: float = 1.0, policy_weight: float = 1.0) -> TrainStats:
+        """One train_batch_single (src/az/train_gpu_candle.rs:145-160):
+        forward, loss, backward, AdamW; one host synchronisation, at the end
+        (metrics and the kernels' status word come back together).  A bad
+        index in the batch raises CnnueError after the step."""
+        torch = self.torch
+        bt = self.to_device(batch)
         self.step_count += 1
-        check(lib().cnnue_adamw(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(), self.grad.data_ptr(),
-                                self.n_params, self.lr, self.beta1, self.beta2, self.eps, self.weight_decay,
-                                self.step_count, self.torch.cuda.current_stream(self.device).cuda_stream),
-              "cnnue_adamw")
-        m = metrics.cpu().numpy()
-        return TrainStats(*[float(x) for x in m[:9]], samples=batch.batch_size, phase=m[9:].reshape(3, 7))
+        key = (tuple((k, tuple(v.shape)) for k, v in bt.items()), self._arena.data_ptr(), value_weight,
+               policy_weight)
+        if not self.use_graph:
+            out = self._step_body(bt, value_weight, policy_weight)
+        elif self._graph is not None and key == self._graph_key:
+            self._graph.replay()
+            out = self._graph_out
+        elif key == self._last_key:  # the shape repeats: capture it, then replay this step
+            self._graph = None
+            g = torch.cuda.CUDAGraph()
+            torch.cuda.synchronize(self.device)
+            with torch.cuda.graph(g):
+                self._graph_out = self._step_body(bt, value_weight, policy_weight)
+            self._graph, self._graph_key = g, key
+            g.replay()
+            out = self._graph_out
+        else:
+            out = self._step_body(bt, value_weight, policy_weight)
+        self._last_key = key
+        m = out.cpu().numpy()
+        _raise_status(int(m[-1]), "AzTrainer.step")
+        return TrainStats(*[float(x) for x in m[:9]], samples=batch.batch_size, phase=m[9:30].reshape(3, 7))
 
     # -- weights ------------------------------------------------------------------
     def tensors(self) -> list:

@@ -1410,7 +1410,8 @@ int cnnue_az_weights_tensor(cnnue_az_weights* w, int index, float** data, int64_
 }
 
 int cnnue_az_pack_batch(const cnnue_az_samples* s, const int64_t* rows, int64_t batch, int64_t cap_features,
-                        int64_t cap_moves, int64_t cap_threats, cnnue_az_packed* out, int n_threads) {
+                        int64_t cap_moves, int64_t cap_threats, int fixed_strides, cnnue_az_packed* out,
+                        int n_threads) {
   if (!s || !out || batch < 0) return set_error(CNNUE_ERR_INVALID_ARG, "null samples/out or negative batch");
   if (s->n < 0 || (s->n > 0 && (!s->feature_offsets || !s->move_offsets)))
     return set_error(CNNUE_ERR_INVALID_ARG, "samples without offsets");
@@ -1449,6 +1450,14 @@ int cnnue_az_pack_batch(const cnnue_az_samples* s, const int64_t* rows, int64_t 
   if (mx.features > cap_features || mx.moves > cap_moves || mx.threats > cap_threats)
     return set_error(CNNUE_ERR_WORKSPACE, "batch needs %d features, %d moves, %d threats per row", mx.features,
                      mx.moves, mx.threats);
+  if (fixed_strides) {  // the capacities are the strides (static shapes for a captured step)
+    mx.features = (int)cap_features;
+    mx.moves = (int)cap_moves;
+    mx.threats = (int)cap_threats;
+    out->max_features = cap_features;
+    out->max_policy_moves = cap_moves;
+    out->max_value_threats = cap_threats;
+  }
   if (batch == 0) return CNNUE_OK;
   if (!out->feature_items || !out->value_threat_indices || !out->policy_items || !out->policy_sparse_indices ||
       !out->policy_tactical_indices || !out->policy_targets || !out->policy_mask || !out->value_wdl ||

@@ -12,6 +12,12 @@
 // where each "x*a + c" is one of candle's affine maps (a and c rounded to
 // fp32, no fused multiply-add) and the scalar factors are formed in double
 // (b^t by repeated squaring, as LLVM's powi runtime does) before rounding.
+//
+// Two entry points: cnnue_adamw takes the step and hyper-parameters from the
+// host; cnnue_adamw_device keeps them in device memory and advances the step
+// there, so a CUDA graph that contains it replays correctly step after step.
+#include <cstring>
+
 #include "common.cuh"
 
 namespace cnnue {
@@ -21,6 +27,7 @@ namespace {
 struct AdamWScalars {
   float b1, omb1, b2, omb2, sm, sv, decay, lr, eps;
 };
+static_assert(sizeof(AdamWScalars) == sizeof(((cnnue_adamw_state*)nullptr)->scalars), "scalar block");
 
 __device__ __forceinline__ float affine(float x, float a, float c) { return __fadd_rn(__fmul_rn(x, a), c); }
 
@@ -36,9 +43,12 @@ __device__ __forceinline__ void adamw_one(float& p, float& m, float& v, float g,
   v = nv;
 }
 
+// The scalars come by value (host form) or from device memory (device form,
+// written by adamw_prepare_kernel); `kd` non-null selects the latter.
 __global__ void __launch_bounds__(256) adamw_vec4_kernel(float4* __restrict__ p, float4* __restrict__ m,
                                                          float4* __restrict__ v, const float4* __restrict__ g,
-                                                         int64_t n4, AdamWScalars k) {
+                                                         int64_t n4, AdamWScalars k, const AdamWScalars* kd) {
+  if (kd) k = *kd;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     float4 pp = p[i], mm = m[i], vv = v[i];
     const float4 gg = __ldg(g + i);
@@ -53,14 +63,16 @@ __global__ void __launch_bounds__(256) adamw_vec4_kernel(float4* __restrict__ p,
 }
 
 __global__ void adamw_scalar_kernel(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
-                                    const float* __restrict__ g, int64_t begin, int64_t n, AdamWScalars k) {
+                                    const float* __restrict__ g, int64_t begin, int64_t n, AdamWScalars k,
+                                    const AdamWScalars* kd) {
+  if (kd) k = *kd;
   for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
     adamw_one(p[i], m[i], v[i], g[i], k);
 }
 
 // b^e for e >= 0 by repeated squaring (the powi runtime routine).
-double powi(double b, int64_t e) {
+__host__ __device__ double powi(double b, int64_t e) {
   double r = 1.0;
   while (true) {
     if (e & 1) r *= b;
@@ -69,6 +81,62 @@ double powi(double b, int64_t e) {
     b *= b;
   }
   return r;
+}
+
+// The scalar factors in double, rounded once to fp32.  Every double
+// operation is spelled out (no contraction), so host and device forms agree.
+__host__ __device__ AdamWScalars make_scalars(double lr, double beta1, double beta2, double eps, double wd,
+                                              int64_t step) {
+#ifdef __CUDA_ARCH__
+#define DSUB(a, b) __dsub_rn(a, b)
+#define DMUL(a, b) __dmul_rn(a, b)
+#define DDIV(a, b) __ddiv_rn(a, b)
+#else
+#define DSUB(a, b) ((a) - (b))
+#define DMUL(a, b) ((a) * (b))
+#define DDIV(a, b) ((a) / (b))
+#endif
+  AdamWScalars k;
+  k.b1 = (float)beta1;
+  k.omb1 = (float)DSUB(1.0, beta1);
+  k.b2 = (float)beta2;
+  k.omb2 = (float)DSUB(1.0, beta2);
+  k.sm = (float)DDIV(1.0, DSUB(1.0, powi(beta1, step)));
+  k.sv = (float)DDIV(1.0, DSUB(1.0, powi(beta2, step)));
+  k.decay = (float)DSUB(1.0, DMUL(lr, wd));
+  k.lr = (float)lr;
+  k.eps = (float)eps;
+#undef DSUB
+#undef DMUL
+#undef DDIV
+  return k;
+}
+
+// Device form: advances the step counter and forms this step's scalars.
+__global__ void adamw_prepare_kernel(cnnue_adamw_state* st) {
+  st->step += 1;
+  const AdamWScalars k = make_scalars(st->lr, st->beta1, st->beta2, st->eps, st->weight_decay, st->step);
+  memcpy(st->scalars, &k, sizeof(k));
+}
+
+int launch_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n, const AdamWScalars& k,
+                 const AdamWScalars* kd, cudaStream_t s) {
+  const bool aligned = ((uintptr_t)d_params | (uintptr_t)d_m | (uintptr_t)d_v | (uintptr_t)d_grads) % 16 == 0;
+  int64_t done = 0;
+  if (aligned && n >= 4) {
+    const int64_t n4 = n / 4;
+    const unsigned blocks = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    adamw_vec4_kernel<<<blocks, 256, 0, s>>>((float4*)d_params, (float4*)d_m, (float4*)d_v, (const float4*)d_grads,
+                                            n4, k, kd);
+    if (int st = check_launch_error("adamw_vec4_kernel")) return st;
+    done = n4 * 4;
+  }
+  if (done < n) {
+    const unsigned blocks = (unsigned)std::min<int64_t>((n - done + 255) / 256, 148 * 8);
+    adamw_scalar_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, done, n, k, kd);
+    if (int st = check_launch_error("adamw_scalar_kernel")) return st;
+  }
+  return CNNUE_OK;
 }
 
 }  // namespace
@@ -86,33 +154,19 @@ int cnnue_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, i
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
   if (step < 1) return set_error(CNNUE_ERR_INVALID_ARG, "step must be >= 1");
   if (n == 0) return CNNUE_OK;
-  AdamWScalars k;
-  k.b1 = (float)beta1;
-  k.omb1 = (float)(1.0 - beta1);
-  k.b2 = (float)beta2;
-  k.omb2 = (float)(1.0 - beta2);
-  k.sm = (float)(1.0 / (1.0 - powi(beta1, step)));
-  k.sv = (float)(1.0 / (1.0 - powi(beta2, step)));
-  k.decay = (float)(1.0 - lr * weight_decay);
-  k.lr = (float)lr;
-  k.eps = (float)eps;
+  return launch_adamw(d_params, d_m, d_v, d_grads, n, make_scalars(lr, beta1, beta2, eps, weight_decay, step),
+                      nullptr, (cudaStream_t)stream);
+}
+
+int cnnue_adamw_device(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n,
+                       cnnue_adamw_state* d_state, void* stream) {
+  if (n < 0 || !d_state || (n > 0 && (!d_params || !d_m || !d_v || !d_grads)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
   cudaStream_t s = (cudaStream_t)stream;
-  const bool aligned = ((uintptr_t)d_params | (uintptr_t)d_m | (uintptr_t)d_v | (uintptr_t)d_grads) % 16 == 0;
-  int64_t done = 0;
-  if (aligned && n >= 4) {
-    const int64_t n4 = n / 4;
-    const unsigned blocks = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
-    adamw_vec4_kernel<<<blocks, 256, 0, s>>>((float4*)d_params, (float4*)d_m, (float4*)d_v, (const float4*)d_grads,
-                                            n4, k);
-    if (int st = check_launch_error("adamw_vec4_kernel")) return st;
-    done = n4 * 4;
-  }
-  if (done < n) {
-    const unsigned blocks = (unsigned)std::min<int64_t>((n - done + 255) / 256, 148 * 8);
-    adamw_scalar_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, done, n, k);
-    if (int st = check_launch_error("adamw_scalar_kernel")) return st;
-  }
-  return CNNUE_OK;
+  adamw_prepare_kernel<<<1, 1, 0, s>>>(d_state);
+  if (int st = check_launch_error("adamw_prepare_kernel")) return st;
+  if (n == 0) return CNNUE_OK;
+  return launch_adamw(d_params, d_m, d_v, d_grads, n, AdamWScalars{}, (const AdamWScalars*)d_state->scalars, s);
 }
 
 }  // extern "C"

@@ -17,6 +17,9 @@
 //      each key adds its units' partials in order.  A key with at most 256
 //      contributions is thus summed exactly in contribution order; longer
 //      runs are still deterministic.  Keys with no contribution read zero.
+// Nothing is read back to the host: run and unit counts stay in device
+// memory and the kernels after them loop up to those counts, so a scatter is
+// asynchronous and can be captured in a CUDA graph.
 // The row form (launch_scatter_add_rows) does the same for whole table rows:
 // a contribution adds a `hidden`-wide row of values, one warp sums a unit
 // with its lanes over the columns, and a key with a single unit is written
@@ -173,10 +176,11 @@ __global__ void zero_kernel(float* __restrict__ out, int64_t n) {
     out[i] = 0.f;
 }
 
-// flag[i] = 1 at the start of a run of equal keys (later scanned to run ids).
+// flag[i] = 1 at the start of a run of equal keys, flag[n] = 0 (scanned to
+// run ids; the scan's entry n is then the run count).
 __global__ void run_flag_kernel(const uint32_t* __restrict__ keys, int64_t n, uint32_t* __restrict__ flag) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
-    flag[i] = (i == 0 || keys[i] != keys[i - 1]) ? 1u : 0u;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i <= n; i += (int64_t)gridDim.x * blockDim.x)
+    flag[i] = i == n ? 0u : ((i == 0 || keys[i] != keys[i - 1]) ? 1u : 0u);
 }
 
 // After the scan flag[i] is the number of runs starting before i; run starts
@@ -187,11 +191,18 @@ __global__ void run_start_kernel(const uint32_t* __restrict__ keys, int64_t n, c
     if (i == 0 || keys[i] != keys[i - 1]) run_start[run_of[i]] = (uint32_t)i;
 }
 
-__global__ void run_units_kernel(const uint32_t* __restrict__ run_start, uint32_t n_runs, int64_t n,
-                                 uint32_t* __restrict__ units) {
-  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_runs; r += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t beg = run_start[r], end = r + 1 < n_runs ? run_start[r + 1] : (uint32_t)n;
-    units[r] = (end - beg + kUnit - 1) / kUnit;
+// units[r] = the unit count of run r (0 past the last run, up to entry n;
+// the scan's entry n is then the unit count).
+__global__ void run_units_kernel(const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ n_runs_d,
+                                 int64_t n, uint32_t* __restrict__ units) {
+  const uint32_t n_runs = *n_runs_d;
+  for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r <= n; r += (int64_t)gridDim.x * blockDim.x) {
+    if (r < n_runs) {
+      const uint32_t beg = run_start[r], end = r + 1 < n_runs ? run_start[r + 1] : (uint32_t)n;
+      units[r] = (end - beg + kUnit - 1) / kUnit;
+    } else {
+      units[r] = 0;
+    }
   }
 }
 
@@ -199,7 +210,9 @@ __global__ void run_units_kernel(const uint32_t* __restrict__ run_start, uint32_
 // issued eight at a time.
 __global__ void unit_sum_kernel(const uint32_t* __restrict__ idx, const float* __restrict__ values, uint32_t div,
                                 const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ unit_off,
-                                uint32_t n_runs, uint32_t n_units, int64_t n, float* __restrict__ partial) {
+                                const uint32_t* __restrict__ n_runs_d, const uint32_t* __restrict__ n_units_d,
+                                int64_t n, float* __restrict__ partial) {
+  const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < n_units; u += (int64_t)gridDim.x * blockDim.x) {
     // the run of unit u: last r with unit_off[r] <= u
     uint32_t lo = 0, hi = n_runs - 1;
@@ -228,8 +241,10 @@ __global__ void unit_sum_kernel(const uint32_t* __restrict__ idx, const float* _
 
 // Each run adds its unit partials in order and writes its key.
 __global__ void run_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ run_start,
-                               const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
-                               const float* __restrict__ partial, int64_t n_keys, float* __restrict__ out) {
+                               const uint32_t* __restrict__ unit_off, const uint32_t* __restrict__ n_runs_d,
+                               const uint32_t* __restrict__ n_units_d, const float* __restrict__ partial,
+                               int64_t n_keys, float* __restrict__ out) {
+  const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_runs; r += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t k = keys[run_start[r]];
     const uint32_t u0 = unit_off[r], u1 = r + 1 < n_runs ? unit_off[r + 1] : n_units;
@@ -245,8 +260,10 @@ __global__ void run_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t
 template <class Val, class Out>
 __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx, Val val,
                                      int64_t hidden, const uint32_t* __restrict__ run_start,
-                                     const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
-                                     int64_t n, int64_t n_keys, float* __restrict__ partial, Out out) {
+                                     const uint32_t* __restrict__ unit_off, const uint32_t* __restrict__ n_runs_d,
+                                     const uint32_t* __restrict__ n_units_d, int64_t n, int64_t n_keys,
+                                     float* __restrict__ partial, Out out) {
+  const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
   for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n_units; u += warps) {
@@ -285,8 +302,10 @@ __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const ui
 // (run, column); single-unit runs were written by unit_sum_rows_kernel).
 template <class Out>
 __global__ void run_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ run_start,
-                                    const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t n_units,
-                                    const float* __restrict__ partial, int64_t hidden, int64_t n_keys, Out out) {
+                                    const uint32_t* __restrict__ unit_off, const uint32_t* __restrict__ n_runs_d,
+                                    const uint32_t* __restrict__ n_units_d, const float* __restrict__ partial,
+                                    int64_t hidden, int64_t n_keys, Out out) {
+  const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   const int64_t total = (int64_t)n_runs * hidden;
   for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = q / hidden, h = q - r * hidden;
@@ -323,7 +342,7 @@ inline size_t workspace_bytes(int64_t n, int64_t hidden = 1) {
   const int64_t nb = n_blocks(n > 0 ? n : 1);
   size_t b = 4 * align_up(nn * 4, 256);                       // keys / idx ping-pong
   b += align_up((size_t)nb * kDigits * 4, 256);               // histograms
-  b += scan_bytes(std::max<int64_t>((int64_t)nb * kDigits, (int64_t)nn));  // scan scratch
+  b += scan_bytes(std::max<int64_t>((int64_t)nb * kDigits, (int64_t)nn + 1));  // scan scratch
   b += 3 * align_up((nn + 1) * 4, 256);                       // flags / run starts / unit offsets
   b += align_up((nn + 1) * 4 * (size_t)hidden, 256);          // unit partials
   b += 256;
@@ -337,11 +356,12 @@ struct Runs {
   uint32_t* run_start;    // [n_runs]
   uint32_t* unit_off;     // [n_runs] first unit of each run
   float* partial;         // unit partials
-  uint32_t n_runs = 0, n_units = 0;
+  const uint32_t* n_runs;   // device word: number of runs
+  const uint32_t* n_units;  // device word: number of units
 };
 
-// Sorts (key, contribution) pairs stably by key and finds runs and units;
-// synchronises `s` twice (run and unit counts).  Requires 0 < n < 2^32 - 1.
+// Sorts (key, contribution) pairs stably by key and finds runs and units
+// (counts left in device memory).  Requires 0 < n < 2^32 - 1.
 int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s, Runs* out) {
   const size_t nn = (size_t)n;
   const int64_t nb = n_blocks(n);
@@ -356,7 +376,7 @@ int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStr
   uint32_t* i0 = (uint32_t*)take(nn * 4);
   uint32_t* i1 = (uint32_t*)take(nn * 4);
   uint32_t* hist = (uint32_t*)take((size_t)nb * kDigits * 4);
-  uint32_t* aux = (uint32_t*)take(scan_bytes(std::max<int64_t>((int64_t)nb * kDigits, (int64_t)nn)));
+  uint32_t* aux = (uint32_t*)take(scan_bytes(std::max<int64_t>((int64_t)nb * kDigits, (int64_t)nn + 1)));
   uint32_t* flag = (uint32_t*)take((nn + 1) * 4);
   uint32_t* rstart = (uint32_t*)take((nn + 1) * 4);
   uint32_t* uoff = (uint32_t*)take((nn + 1) * 4);
@@ -378,32 +398,21 @@ int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStr
     kout = kout == k0 ? k1 : k0;
     iout = iout == i0 ? i1 : i0;
   }
-  const unsigned gb = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  const unsigned gb = (unsigned)std::min<int64_t>((n + 256) / 256, 148 * 16);
   run_flag_kernel<<<gb, 256, 0, s>>>(kin, n, flag);
   if (int st = check_launch_error("scatter flags")) return st;
-  // run ids: exclusive scan of the flags; the run count is the last id + its flag
-  uint32_t last_flag = 0, n_runs = 0;
-  CNNUE_CUDA_TRY(cudaMemcpyAsync(&last_flag, flag + n - 1, 4, cudaMemcpyDeviceToHost, s));
-  if (int st = launch_scan(flag, n, aux, s)) return st;
-  CNNUE_CUDA_TRY(cudaMemcpyAsync(&n_runs, flag + n - 1, 4, cudaMemcpyDeviceToHost, s));
-  CNNUE_CUDA_TRY(cudaStreamSynchronize(s));
-  n_runs += last_flag;
+  if (int st = launch_scan(flag, n + 1, aux, s)) return st;  // run ids; flag[n] = run count
   run_start_kernel<<<gb, 256, 0, s>>>(kin, n, flag, rstart);
   if (int st = check_launch_error("scatter run starts")) return st;
-  const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_runs + 255) / 256, 148 * 16));
-  run_units_kernel<<<rb, 256, 0, s>>>(rstart, n_runs, n, uoff);
+  run_units_kernel<<<gb, 256, 0, s>>>(rstart, flag + n, n, uoff);
   if (int st = check_launch_error("scatter run units")) return st;
-  uint32_t last_units = 0, n_units = 0;
-  CNNUE_CUDA_TRY(cudaMemcpyAsync(&last_units, uoff + n_runs - 1, 4, cudaMemcpyDeviceToHost, s));
-  if (int st = launch_scan(uoff, n_runs, aux, s)) return st;
-  CNNUE_CUDA_TRY(cudaMemcpyAsync(&n_units, uoff + n_runs - 1, 4, cudaMemcpyDeviceToHost, s));
-  CNNUE_CUDA_TRY(cudaStreamSynchronize(s));
+  if (int st = launch_scan(uoff, n + 1, aux, s)) return st;  // unit offsets; uoff[n] = unit count
   out->keys = kin;
   out->idx = iin;
   out->run_start = rstart;
   out->unit_off = uoff;
-  out->n_runs = n_runs;
-  out->n_units = n_units + last_units;
+  out->n_runs = flag + n;
+  out->n_units = uoff + n;
   return CNNUE_OK;
 }
 
@@ -411,7 +420,6 @@ int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStr
 // values[i / div] with keys[i] == k; keys nobody hits read 0.  Every key must
 // be <= n_keys (the sort covers only those bits); key n_keys marks a
 // contribution to drop (callers map padding and out-of-range indices to it).
-// Synchronises `s` twice (run and unit counts).
 int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, int64_t n, int64_t n_keys,
                        float* out, void* ws, cudaStream_t s) {
   const unsigned zb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_keys + 255) / 256, 148 * 8));
@@ -421,12 +429,12 @@ int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, 
   if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
   Runs r;
   if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
-  const unsigned ub = (unsigned)std::max<int64_t>(1, std::min<int64_t>((r.n_units + 255) / 256, 148 * 16));
-  unit_sum_kernel<<<ub, 256, 0, s>>>(r.idx, values, div, r.run_start, r.unit_off, r.n_runs, r.n_units, n,
+  // grids for the upper bounds (units, runs <= n); the kernels stop at the counts
+  const unsigned gb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
+  unit_sum_kernel<<<gb, 256, 0, s>>>(r.idx, values, div, r.run_start, r.unit_off, r.n_runs, r.n_units, n,
                                      r.partial);
   if (int st = check_launch_error("scatter unit sums")) return st;
-  const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((r.n_runs + 255) / 256, 148 * 16));
-  run_sum_kernel<<<rb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, n_keys, out);
+  run_sum_kernel<<<gb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, n_keys, out);
   return check_launch_error("scatter run sums");
 }
 
@@ -441,13 +449,12 @@ int launch_scatter_rows(const uint32_t* keys, Val val, Out out, int64_t hidden, 
   if (n >= (int64_t)UINT32_MAX) return set_error(CNNUE_ERR_INVALID_ARG, "too many contributions");
   Runs r;
   if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
-  const unsigned ub =
-      (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_units * 32 + 255) / 256, 148 * 16));
+  // grids for the upper bounds (units, runs <= n); the kernels stop at the counts
+  const unsigned ub = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n * 32 + 255) / 256, 148 * 16));
   unit_sum_rows_kernel<<<ub, 256, 0, s>>>(r.keys, r.idx, val, hidden, r.run_start, r.unit_off, r.n_runs, r.n_units,
                                           n, n_keys, r.partial, out);
   if (int st = check_launch_error("scatter unit row sums")) return st;
-  const unsigned rb =
-      (unsigned)std::max<int64_t>(1, std::min<int64_t>(((int64_t)r.n_runs * hidden + 255) / 256, 148 * 16));
+  const unsigned rb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n * hidden + 255) / 256, 148 * 16));
   run_sum_rows_kernel<<<rb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, hidden,
                                          n_keys, out);
   return check_launch_error("scatter run row sums");

@@ -356,6 +356,18 @@ int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, 
 int cnnue_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n, double lr,
                 double beta1, double beta2, double eps, double weight_decay, int64_t step,
                 void* stream);
+/* The same step with its hyper-parameters and step counter in device memory
+ * (so a captured CUDA graph replays it step after step): the call advances
+ * d_state->step by one on the device, then applies AdamW with the new step.
+ * The host may rewrite lr (set_learning_rate) between replays. */
+typedef struct cnnue_adamw_state {
+  double lr, beta1, beta2, eps, weight_decay;
+  int64_t step;        /* steps taken; 0 before the first */
+  float scalars[9];    /* written by the device: this step's fp32 factors */
+  float pad[3];
+} cnnue_adamw_state;
+int cnnue_adamw_device(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n,
+                       cnnue_adamw_state* d_state, void* stream);
 
 /* ---- reference-native AZ-NNUE evaluator (src/az.rs, src/nnue.rs) -------- */
 /* Squares are rank * 9 + file with rank 0 the first rank of a FEN (Black's
@@ -460,10 +472,12 @@ typedef struct cnnue_az_packed {
  * threads (<= 0: up to 16).  The output arrays must hold the capacities
  * cap_features / cap_moves / cap_threats per row; the dims actually used are
  * written to out first, and CNNUE_ERR_WORKSPACE is returned (nothing else
- * written) when a capacity is too small.  Replaces PackedBatch::from_indices
+ * written) when a capacity is too small.  With fixed_strides the capacities
+ * themselves are the strides (extra columns hold the padding values), so
+ * every batch has the same shapes.  Replaces PackedBatch::from_indices
  * (src/az/dataloader.rs:113-336). */
 int cnnue_az_pack_batch(const cnnue_az_samples* samples, const int64_t* rows, int64_t batch,
-                        int64_t cap_features, int64_t cap_moves, int64_t cap_threats,
+                        int64_t cap_features, int64_t cap_moves, int64_t cap_threats, int fixed_strides,
                         cnnue_az_packed* out, int n_threads);
 
 /* Per-move records for the policy logits/* Per-move records for the policy logits (the per-move inputs of

@@ -99,3 +99,36 @@ def test_copy_back_round_trip(tmp_path):
     w2 = az.AzWeights.load(str(path))
     for a, c in zip(tr.tensors(), w2.tensors()):
         np.testing.assert_array_equal(a, c)
+
+
+def test_bad_batch_raises_after_step():
+    from chineseai_b200._lib import CnnueError
+    w, b = make(32, 8, 5)
+    b.policy_items[0, 0] = (3000 | 1 << 47)  # a move index past the 2086-move space
+    tr = az_train.AzTrainer(w, lr=1e-3)
+    with pytest.raises(CnnueError):
+        tr.step(b)
+
+
+def test_graph_steps_equal_eager_steps():
+    """The captured step replays exactly what the eager step computes, step
+    after step (device-side AdamW counter), on fixed-shape batches."""
+    w, _ = make(64, 8, 12)
+    s = az_train.random_samples(256, 13)
+    batches = [az_train.pack_batch(s, np.arange(k * 64, (k + 1) * 64), caps=(40, 96, 96), fixed=True)
+               for k in range(4)]
+    eager = az_train.AzTrainer(w, lr=2e-3)
+    graph = az_train.AzTrainer(w, lr=2e-3, graph=True)
+    for k in range(6):
+        b = batches[k % 4]
+        se, sg = eager.step(b), graph.step(b)
+        assert se.loss == sg.loss, (k, se.loss, sg.loss)
+    assert graph._graph is not None
+    for a, c in zip(eager.tensors(), graph.tensors()):
+        np.testing.assert_array_equal(a, c)
+    graph.set_learning_rate(1e-4)
+    eager.set_learning_rate(1e-4)
+    eager.step(batches[0])
+    graph.step(batches[0])
+    for a, c in zip(eager.tensors(), graph.tensors()):
+        np.testing.assert_array_equal(a, c)

@@ -112,24 +112,32 @@ class _CSamples(C.Structure):
 
 @dataclass
 class PackedBatch:
-    """PackedBatch (src/az/dataloader.rs:92-111) as numpy arrays."""
+    """PackedBatch (src/az/dataloader.rs:92-111) as numpy arrays.  A compact
+    batch carries policy_signature / king_buckets instead of the sparse,
+    tactical and mask arrays (None), which the GPU rebuilds."""
     feature_items: np.ndarray           # u32 [B, F]
     value_threat_indices: np.ndarray    # u32 [B, T]
     policy_items: np.ndarray            # i64 [B, M]
-    policy_sparse_indices: np.ndarray   # i64 [B, M, 7]
-    policy_tactical_indices: np.ndarray  # i64 [B, M, 2]
+    policy_sparse_indices: Optional[np.ndarray]    # i64 [B, M, 7]
+    policy_tactical_indices: Optional[np.ndarray]  # i64 [B, M, 2]
     policy_targets: np.ndarray          # f32 [B, M]
-    policy_mask: np.ndarray             # f32 [B, M]
+    policy_mask: Optional[np.ndarray]   # f32 [B, M]
     value_wdl: np.ndarray               # f32 [B, 3]
     values: np.ndarray                  # f32 [B]
     rule_context: np.ndarray            # f32 [B, 7]
     policy_weights: np.ndarray          # f32 [B]
     value_weights: np.ndarray           # f32 [B]
     value_phase_masks: np.ndarray       # f32 [B, 3]
+    policy_signature: Optional[np.ndarray] = None  # u8 [B, M] (compact)
+    king_buckets: Optional[np.ndarray] = None      # u8 [B] us | them << 4 (compact)
 
     @property
     def batch_size(self) -> int:
         return self.values.shape[0]
+
+    @property
+    def compact(self) -> bool:
+        return self.policy_sparse_indices is None
 
 
 _PACKED_FIELDS = [f.name for f in fields(PackedBatch)]
@@ -152,10 +160,13 @@ def _samples_struct(s: Samples, keep: list) -> _CSamples:
 
 
 def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: int = 0,
-               caps=(96, 160, 256), fixed: bool = False) -> PackedBatch:
+               caps=(96, 160, 256), fixed: bool = False, compact: bool = False) -> PackedBatch:
     """Packs samples[rows] (all samples when rows is None) with the native
     packer.  fixed=True: the arrays take the `caps` widths whatever the batch
-    needs (CnnueError if it needs more), for a trainer with a captured step."""
+    needs (CnnueError if it needs more), for a trainer with a captured step.
+    compact=True: per-move tactical signatures and per-row king buckets
+    instead of the 7 + 2 int64 lookup indices and the mask (the trainer
+    rebuilds those on the GPU: about a fifth of the bytes to send)."""
     keep: list = []
     cs = _samples_struct(samples, keep)
     if rows is None:
@@ -174,8 +185,14 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
             "policy_mask": np.empty((b, M), np.float32), "value_wdl": np.empty((b, 3), np.float32),
             "values": np.empty(b, np.float32), "rule_context": np.empty((b, RULE_CONTEXT), np.float32),
             "policy_weights": np.empty(b, np.float32), "value_weights": np.empty(b, np.float32),
-            "value_phase_masks": np.empty((b, 3), np.float32)}
-        out = _CPacked(0, 0, 0, 0, *[bufs[k].ctypes.data for k in _PACKED_FIELDS])
+            "value_phase_masks": np.empty((b, 3), np.float32),
+            "policy_signature": np.empty((b, M), np.uint8), "king_buckets": np.empty(b, np.uint8)}
+        if compact:
+            for k in ("policy_sparse_indices", "policy_tactical_indices", "policy_mask"):
+                bufs[k] = None
+        else:
+            bufs["policy_signature"] = bufs["king_buckets"] = None
+        out = _CPacked(0, 0, 0, 0, *[None if bufs[k] is None else bufs[k].ctypes.data for k in _PACKED_FIELDS])
         st = lib().cnnue_az_pack_batch(C.byref(cs), rptr, batch, F, M, T, int(fixed), C.byref(out), n_threads)
         need = (out.max_features, out.max_policy_moves, out.max_value_threats)
         if st == 5 and not fixed and any(n > c for n, c in zip(need, caps)):  # CNNUE_ERR_WORKSPACE: grow, retry
@@ -186,6 +203,8 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
     F, M, T = need
 
     def cut(a, width, extra=()):
+        if a is None:
+            return None
         flat = a.reshape(-1)[: batch * width * int(np.prod(extra or (1,)))]
         return flat.reshape((batch, width) + tuple(extra))
 
@@ -196,7 +215,9 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
         policy_targets=cut(bufs["policy_targets"], M), policy_mask=cut(bufs["policy_mask"], M),
         value_wdl=bufs["value_wdl"][:batch], values=bufs["values"][:batch],
         rule_context=bufs["rule_context"][:batch], policy_weights=bufs["policy_weights"][:batch],
-        value_weights=bufs["value_weights"][:batch], value_phase_masks=bufs["value_phase_masks"][:batch])
+        value_weights=bufs["value_weights"][:batch], value_phase_masks=bufs["value_phase_masks"][:batch],
+        policy_signature=cut(bufs["policy_signature"], M),
+        king_buckets=None if bufs["king_buckets"] is None else bufs["king_buckets"][:batch])
 
 
 # ---- the training step --------------------------------------------------------
@@ -318,6 +339,8 @@ class AzTrainer:
         torch = self.torch
         arrays, offsets, total = [], [], 0
         for f in fields(PackedBatch):
+            if getattr(b, f.name) is None:
+                continue
             a = np.ascontiguousarray(getattr(b, f.name))
             if a.dtype == np.uint32:
                 a = a.view(np.int32)
@@ -332,9 +355,30 @@ class AzTrainer:
             host[off:off + a.nbytes] = a.reshape(-1).view(np.uint8)
         self._arena[:total].copy_(self._pinned[:total], non_blocking=True)
         self._last_h2d = total
-        dt = {np.dtype(np.int32): torch.int32, np.dtype(np.int64): torch.int64, np.dtype(np.float32): torch.float32}
+        dt = {np.dtype(np.int32): torch.int32, np.dtype(np.int64): torch.int64, np.dtype(np.float32): torch.float32,
+              np.dtype(np.uint8): torch.uint8}
         return {name: self._arena[off:off + a.nbytes].view(dt[a.dtype]).view(a.shape)
                 for (name, a), off in zip(arrays, offsets)}
+
+    def expand(self, bt: dict) -> dict:
+        """A compact batch's sparse / tactical indices and mask, rebuilt on the
+        GPU (cnnue_az_expand_policy_indices); full batches pass through."""
+        if "policy_signature" not in bt:
+            return bt
+        torch = self.torch
+        items = bt["policy_items"]
+        B, M = items.shape
+        sparse = torch.empty((B, M, 7), dtype=torch.int64, device=self.device)
+        tactical = torch.empty((B, M, 2), dtype=torch.int64, device=self.device)
+        mask = torch.empty((B, M), dtype=torch.float32, device=self.device)
+        check(lib().cnnue_az_expand_policy_indices(items.data_ptr(), bt["policy_signature"].data_ptr(),
+                                                   bt["king_buckets"].data_ptr(), B, M, sparse.data_ptr(),
+                                                   tactical.data_ptr(), mask.data_ptr(),
+                                                   torch.cuda.current_stream(self.device).cuda_stream),
+              "cnnue_az_expand_policy_indices")
+        out = dict(bt)
+        out.update(policy_sparse_indices=sparse, policy_tactical_indices=tactical, policy_mask=mask)
+        return out
 
     @property
     def h2d_bytes(self) -> int:
@@ -407,7 +451,7 @@ class AzTrainer:
     def _step_body(self, bt: dict, value_weight: float, policy_weight: float):
         self.grad.zero_()
         self.status.zero_()
-        loss, metrics = self.loss(bt, value_weight, policy_weight)
+        loss, metrics = self.loss(self.expand(bt), value_weight, policy_weight)
         loss.backward()
         check(lib().cnnue_adamw_device(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
                                        self.grad.data_ptr(), self.n_params, self.adam_state.data_ptr(),

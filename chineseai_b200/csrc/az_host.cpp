@@ -988,14 +988,21 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
   attacked_squares(board, 1, opp);
   attacked_squares(board, 0, own);
   const auto& moves = dense_moves();
+  const bool compact = o->policy_sparse_indices == nullptr;
   int64_t* items = o->policy_items + row * M;
-  int64_t* sparse = o->policy_sparse_indices + row * M * 7;
-  int64_t* tactical = o->policy_tactical_indices + row * M * 2;
   float* targets = o->policy_targets + row * M;
-  float* mask = o->policy_mask + row * M;
+  int64_t* sparse = compact ? nullptr : o->policy_sparse_indices + row * M * 7;
+  int64_t* tactical = compact ? nullptr : o->policy_tactical_indices + row * M * 2;
+  float* mask = compact ? nullptr : o->policy_mask + row * M;
+  uint8_t* signature = compact ? o->policy_signature + row * M : nullptr;
+  if (compact) o->king_buckets[row] = (uint8_t)(us | them << 4);
   for (int k = 0; k < M; ++k) {
     items[k] = 0;
     targets[k] = 0.f;
+    if (compact) {
+      signature[k] = 0;
+      continue;
+    }
     mask[k] = kPolicyMask;
     for (int j = 0; j < 7; ++j) sparse[k * 7 + j] = kSparseTable - 1;
     tactical[k * 2] = tactical[k * 2 + 1] = kTacticalSize;
@@ -1007,7 +1014,7 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
     if (mi >= kDenseMoves) continue;
     const float target = s->policy[j];
     targets[off] = std::fmax(target, 0.f);
-    mask[off] = 0.f;
+    if (!compact) mask[off] = 0.f;
     const int from = moves[mi] / kSq, to = moves[mi] % kSq;
     const int mf = bf[from];
     const bool move_valid = mf >= 0 && mf / kSq < 7;
@@ -1024,7 +1031,10 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
     // pack_policy_item (src/az/fused_policy.rs:146-157)
     items[off] = (int64_t)((uint64_t)mi | (uint64_t)cf << 12 | (uint64_t)ct << 23 | (uint64_t)cc << 34 |
                            (uint64_t)move_valid << 45 | (uint64_t)capture << 46 | (uint64_t)1 << 47);
-    if (move_valid) {
+    if (move_valid && compact) {
+      signature[off] = (uint8_t)(opp[from] | opp[to] << 1 | own[from] << 2 | own[to] << 3 | (int)capture << 4 |
+                                 (int)gives_check(board, 0, from, to) << 5);
+    } else if (move_valid) {
       const int piece = mf / kSq;
       const int pair = us * 9 + them;
       int64_t* sp = sparse + off * 7;
@@ -1459,10 +1469,14 @@ int cnnue_az_pack_batch(const cnnue_az_samples* s, const int64_t* rows, int64_t 
     out->max_value_threats = cap_threats;
   }
   if (batch == 0) return CNNUE_OK;
-  if (!out->feature_items || !out->value_threat_indices || !out->policy_items || !out->policy_sparse_indices ||
-      !out->policy_tactical_indices || !out->policy_targets || !out->policy_mask || !out->value_wdl ||
-      !out->values || !out->rule_context || !out->policy_weights || !out->value_weights || !out->value_phase_masks)
+  const bool compact = !out->policy_sparse_indices && !out->policy_tactical_indices && !out->policy_mask;
+  if (!out->feature_items || !out->value_threat_indices || !out->policy_items || !out->policy_targets ||
+      !out->value_wdl || !out->values || !out->rule_context || !out->policy_weights || !out->value_weights ||
+      !out->value_phase_masks)
     return set_error(CNNUE_ERR_INVALID_ARG, "null output array");
+  if (compact ? (!out->policy_signature || !out->king_buckets)
+              : (!out->policy_sparse_indices || !out->policy_tactical_indices || !out->policy_mask))
+    return set_error(CNNUE_ERR_INVALID_ARG, "give all of sparse/tactical/mask, or the compact signature + buckets");
   parallel_rows(batch, n_threads, [&](int64_t r) {
     const int64_t i = rows ? rows[r] : r;
     pack_row(s, i, r, mx, threats.data() + (size_t)r * CNNUE_AZ_THREAT_MAX, dims[r].threats, out);

@@ -266,6 +266,53 @@ __global__ void index_keys_kernel(const int64_t* __restrict__ idx, int64_t n, in
   }
 }
 
+// Compact packed batch -> the policy lookups' index arrays (src/az.rs:763-859).
+constexpr int64_t kSparseTable = 2396815, kSparseMain = 2086LL * 14 * 81;
+constexpr int64_t kTacticalExact = 2086LL * 7 * 64, kTacticalSize = kTacticalExact + 7 * 64;
+
+__global__ void expand_indices_kernel(const int64_t* __restrict__ items, const uint8_t* __restrict__ signature,
+                                      const uint8_t* __restrict__ buckets, int64_t batch, int64_t moves,
+                                      int64_t* __restrict__ sparse, int64_t* __restrict__ tactical,
+                                      float* __restrict__ mask) {
+  const int64_t n = batch * moves;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const Item it = decode(items[i]);
+    if (mask) mask[i] = it.policy ? 0.f : -1.0e9f;
+    int64_t sp[7], ta[2];
+    const bool live = it.policy && it.move && in_range(it) && it.from / 90 < 7;
+    if (live) {
+      const uint32_t b = buckets[i / moves];
+      const int us = b & 15, them = b >> 4, pair = us * 9 + them;
+      const int piece = it.from / 90, from = it.from % 90, to = it.to % 90;
+      const int64_t mv = it.mv;
+      // policy_king_distance_buckets (src/az.rs:841-859)
+      const int king = 89 - ((7 + them / 3) * 9 + 3 + them % 3);
+      const int before = abs(from / 9 - king / 9) + abs(from % 9 - king % 9);
+      const int after = abs(to / 9 - king / 9) + abs(to % 9 - king % 9);
+      const int approach = min(max(before - after, -2), 2) + 2, distance = min(after, 5);
+      const int64_t move_piece = 2086LL * 14, move_king = 2086LL * 81, dist_off = move_piece + move_king + 14 * 81;
+      sp[0] = ((mv * 14 + piece) * 9 + us) * 9 + them;
+      sp[1] = kSparseMain + mv * 15 + (it.capture ? it.cap / 90 : 14);
+      sp[2] = kSparseTable + mv * 14 + piece;
+      sp[3] = kSparseTable + move_piece + mv * 81 + pair;
+      sp[4] = kSparseTable + move_piece + move_king + piece * 81 + pair;
+      sp[5] = kSparseTable + dist_off + piece * 6 + distance;
+      sp[6] = kSparseTable + dist_off + 14 * 6 + piece * 5 + approach;
+      const int64_t sig = signature[i] & 63;
+      ta[0] = (mv * 7 + piece) * 64 + sig;
+      ta[1] = kTacticalExact + piece * 64 + sig;
+    } else {
+#pragma unroll
+      for (int k = 0; k < 7; ++k) sp[k] = kSparseTable - 1;
+      ta[0] = ta[1] = kTacticalSize;
+    }
+#pragma unroll
+    for (int k = 0; k < 7; ++k) sparse[i * 7 + k] = sp[k];
+    tactical[i * 2] = ta[0];
+    tactical[i * 2 + 1] = ta[1];
+  }
+}
+
 inline unsigned grid_for(int64_t n) { return (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16)); }
 
 }  // namespace
@@ -377,6 +424,18 @@ int cnnue_policy_table_bwd(const int64_t* d_indices, const float* d_grad_out, in
     if (int st = check_launch_error("index_keys_kernel")) return st;
   }
   return scat::launch_scatter_add(keys, d_grad_out, (uint32_t)terms, n, table_len, d_grad_table, scratch, s);
+}
+
+int cnnue_az_expand_policy_indices(const int64_t* d_items, const uint8_t* d_signature, const uint8_t* d_king_buckets,
+                                   int64_t batch, int64_t moves, int64_t* d_sparse, int64_t* d_tactical,
+                                   float* d_mask, void* stream) {
+  if (batch < 0 || moves < 0 ||
+      (batch * moves > 0 && (!d_items || !d_signature || !d_king_buckets || !d_sparse || !d_tactical)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
+  if (batch * moves == 0) return CNNUE_OK;
+  expand_indices_kernel<<<grid_for(batch * moves), 256, 0, (cudaStream_t)stream>>>(
+      d_items, d_signature, d_king_buckets, batch, moves, d_sparse, d_tactical, d_mask);
+  return check_launch_error("expand_indices_kernel");
 }
 
 }  // extern "C"

@@ -467,6 +467,12 @@ typedef struct cnnue_az_packed {
   float* policy_weights;
   float* value_weights;
   float* value_phase_masks;
+  /* compact form (policy_sparse_indices, policy_tactical_indices and
+   * policy_mask all NULL): per move the 6-bit tactical signature (0 for moves
+   * without an own piece on the source), per row us_bucket | them_bucket << 4;
+   * cnnue_az_expand_policy_indices rebuilds the index arrays on the device */
+  uint8_t* policy_signature;       /* [B][M] */
+  uint8_t* king_buckets;           /* [B] */
 } cnnue_az_packed;
 /* Packs the samples rows[0..batch) (rows NULL = 0..batch) on n_threads host
  * threads (<= 0: up to 16).  The output arrays must hold the capacities
@@ -480,7 +486,19 @@ int cnnue_az_pack_batch(const cnnue_az_samples* samples, const int64_t* rows, in
                         int64_t cap_features, int64_t cap_moves, int64_t cap_threats, int fixed_strides,
                         cnnue_az_packed* out, int n_threads);
 
-/* Per-move records for the policy logits/* Per-move records for the policy logits (the per-move inputs of
+/* Device half of the compact packed batch: the sparse [B][M][7] and
+ * tactical [B][M][2] index arrays of the policy lookups rebuilt from the
+ * policy items (move, source and destination squares, pieces, flags), the
+ * per-move signatures and the per-row king buckets - equal to what
+ * cnnue_az_pack_batch writes in full form (policy_sparse_main_index /
+ * _capture_index / _factor_indices, policy_tactical_indices,
+ * src/az.rs:763-859).  d_mask (optional) gets 0 for policy-valid items and
+ * -1e9 elsewhere (the packer's policy_mask). */
+int cnnue_az_expand_policy_indices(const int64_t* d_items, const uint8_t* d_signature,
+                                   const uint8_t* d_king_buckets, int64_t batch, int64_t moves,
+                                   int64_t* d_sparse, int64_t* d_tactical, float* d_mask, void* stream);
+
+/* Per-move records for the policy logits (the per-move inputs of
  * evaluate_prepared_hidden_with_context, src/az.rs:1766-1887), side to move
  * `side`.  moves[2i], moves[2i+1] = from, to squares (absolute).  info[2i] =
  * dense move index of the canonical move (12 bits, 0xfff when not in the

@@ -46,3 +46,19 @@ def test_capacity_growth_and_empty():
     assert b.policy_items.shape[1] >= 1 and b.feature_items.shape[1] >= 1
     e = az_train.pack_batch(s, rows=np.zeros(0, np.int64))
     assert e.batch_size == 0
+
+
+def test_compact_pack_shares_everything_but_the_lookups(samples):
+    full = az_train.pack_batch(samples, caps=(40, 96, 96), fixed=True)
+    comp = az_train.pack_batch(samples, caps=(40, 96, 96), fixed=True, compact=True)
+    assert comp.compact and not full.compact
+    for name in ("feature_items", "value_threat_indices", "policy_items", "policy_targets", "value_wdl", "values",
+                 "rule_context", "policy_weights", "value_weights", "value_phase_masks"):
+        np.testing.assert_array_equal(getattr(comp, name), getattr(full, name), err_msg=name)
+    live = ((full.policy_items >> 45) & 1) == 1
+    # the signature is the tactical index's low 6 bits on live moves, 0 elsewhere
+    np.testing.assert_array_equal(comp.policy_signature[live], full.policy_tactical_indices[..., 1][live] & 63)
+    assert (comp.policy_signature[~live] == 0).all()
+    us = comp.king_buckets & 15
+    them = comp.king_buckets >> 4
+    assert (us <= 8).all() and (them <= 8).all()

@@ -132,3 +132,30 @@ def test_graph_steps_equal_eager_steps():
     graph.step(batches[0])
     for a, c in zip(eager.tensors(), graph.tensors()):
         np.testing.assert_array_equal(a, c)
+
+
+def test_gpu_index_expansion_matches_host_packer():
+    s = az_train.random_samples(200, 21)
+    full = az_train.pack_batch(s, caps=(40, 96, 96), fixed=True)
+    comp = az_train.pack_batch(s, caps=(40, 96, 96), fixed=True, compact=True)
+    w, _ = make(32, 4, 22)
+    tr = az_train.AzTrainer(w)
+    ex = tr.expand(tr.to_device(comp))
+    np.testing.assert_array_equal(ex["policy_sparse_indices"].cpu().numpy(), full.policy_sparse_indices)
+    np.testing.assert_array_equal(ex["policy_tactical_indices"].cpu().numpy(), full.policy_tactical_indices)
+    np.testing.assert_array_equal(ex["policy_mask"].cpu().numpy(), full.policy_mask)
+
+
+def test_compact_batches_train_identically():
+    s = az_train.random_samples(128, 23)
+    rows = [np.arange(k * 64, (k + 1) * 64) for k in range(2)]
+    full = [az_train.pack_batch(s, r, caps=(40, 96, 96), fixed=True) for r in rows]
+    comp = [az_train.pack_batch(s, r, caps=(40, 96, 96), fixed=True, compact=True) for r in rows]
+    w, _ = make(32, 4, 24)
+    a = az_train.AzTrainer(w, lr=2e-3)
+    b = az_train.AzTrainer(w, lr=2e-3, graph=True)
+    for k in range(4):
+        sa, sb = a.step(full[k % 2]), b.step(comp[k % 2])
+        assert sa.loss == sb.loss
+    for x, y in zip(a.tensors(), b.tensors()):
+        np.testing.assert_array_equal(x, y)

@@ -25,9 +25,11 @@
 // deterministic run to run; a row with at most kSeg contributions is summed in
 // exactly the reference CPU order.
 //
-// Tables of more than kSegMaxRows rows (the 57,702-row threat table) whose
-// per-chunk histograms would not fit in shared memory take the radix-sorted
-// row scatter of scatter.cuh instead: same order, same exactness.
+// The AZ feature pool's backward, and plain tables of more than kSegMaxRows
+// rows (the 57,702-row threat table, whose per-chunk histograms would not fit
+// in shared memory), take the radix-sorted row scatter of scatter.cuh
+// instead: same order, same exactness, and parallel over rows rather than
+// over chunks of items (the segmented form keeps the C4 training step).
 #include <algorithm>
 
 #include "common.cuh"
@@ -178,6 +180,22 @@ inline size_t sorted_bwd_bytes(int64_t n_items, int64_t hidden) {
          scat::workspace_bytes(n_items, hidden);
 }
 
+// Feature-pool items as scatter keys: contribution e = 6 * item + slot, the
+// item's six rows in the reference order; padding and bad items map to the
+// drop key (bad ones are flagged).
+__global__ void az_keys_kernel(const uint32_t* __restrict__ items, int64_t n_items, uint32_t* __restrict__ keys,
+                               uint32_t* status) {
+  const AzDecoder dec{kRows};
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_items;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    uint32_t rows[6];
+    const int nr = dec.decode_item(items[i], rows);
+    if (nr < 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+#pragma unroll
+    for (int r = 0; r < 6; ++r) keys[i * 6 + r] = nr == 6 ? rows[r] : (uint32_t)kRows;
+  }
+}
+
 int check_shape(int64_t batch, int64_t item_count, int64_t hidden) {
   if (batch < 0 || item_count < 0 || hidden <= 0)
     return set_error(CNNUE_ERR_INVALID_ARG, "bad shape batch=%lld items=%lld hidden=%lld",
@@ -209,7 +227,7 @@ int cnnue_feature_pool_fwd(const float* d_tables, const uint32_t* d_items, int64
 
 size_t cnnue_feature_pool_bwd_workspace_bytes(int64_t batch, int64_t item_count, int64_t hidden) {
   if (batch < 0 || item_count < 0 || hidden <= 0) return 0;
-  return seg::bwd_bytes(batch * item_count, 6, kRows, hidden);
+  return sorted_bwd_bytes(batch * item_count * 6, hidden);
 }
 
 int cnnue_feature_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int64_t batch,
@@ -219,11 +237,21 @@ int cnnue_feature_pool_bwd(const uint32_t* d_items, const float* d_grad_out, int
   if (st) return st;
   if (!d_grad_tables || !d_workspace || (batch && !d_grad_out) || (batch * item_count && !d_items))
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer");
-  if (workspace_bytes < seg::bwd_bytes(batch * item_count, 6, kRows, hidden))
+  if (workspace_bytes < cnnue_feature_pool_bwd_workspace_bytes(batch, item_count, hidden))
     return set_error(CNNUE_ERR_WORKSPACE, "workspace too small");
-  AzDecoder dec{kRows, d_items, item_count};
-  return seg::launch_bwd(batch * item_count, d_grad_out, hidden, dec, d_grad_tables, d_workspace,
-                         (cudaStream_t)stream);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int64_t n_items = batch * item_count;
+  CNNUE_CUDA_TRY(cudaMemsetAsync(d_workspace, 0, sizeof(WorkspaceHeader), s));
+  uint32_t* status = &((WorkspaceHeader*)d_workspace)->status;
+  uint32_t* keys = (uint32_t*)((char*)d_workspace + sizeof(WorkspaceHeader));
+  void* scratch = (char*)keys + align_up((size_t)std::max<int64_t>(6 * n_items, 1) * 4, 256);
+  if (n_items > 0) {
+    const unsigned g = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n_items + 255) / 256, 148 * 16));
+    az_keys_kernel<<<g, 256, 0, s>>>(d_items, n_items, keys, status);
+    if (int e = check_launch_error("az_keys_kernel")) return e;
+  }
+  return scat::launch_scatter_add_rows(keys, d_grad_out, (uint32_t)(6 * item_count), hidden, 6 * n_items, kRows,
+                                       d_grad_tables, scratch, s);
 }
 
 int cnnue_sparse_pool_fwd(const float* d_table, int64_t rows, const uint32_t* d_items,

@@ -256,13 +256,17 @@ __global__ void table_fwd_kernel(const float* __restrict__ table, int64_t table_
   }
 }
 
-__global__ void index_keys_kernel(const int64_t* __restrict__ idx, int64_t n, int64_t table_len,
-                                  uint32_t* __restrict__ keys, uint32_t* status) {
+// Contribution (o, k) adds grad_out[o] to entry idx[o * terms + k].  Out of
+// range indices are flagged and dropped; so are contributions whose value is
+// exactly zero (masked move slots), which change no sum: partial sums here
+// start at +0 and never hold -0, and x + (+-0) == x for every other x.
+__global__ void index_keys_kernel(const int64_t* __restrict__ idx, const float* __restrict__ grad_out, int terms,
+                                  int64_t n, int64_t table_len, uint32_t* __restrict__ keys, uint32_t* status) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t j = idx[i];
     const bool ok = j >= 0 && j < table_len;
     if (!ok) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
-    keys[i] = ok ? (uint32_t)j : (uint32_t)table_len;  // out of range: dropped by the scatter
+    keys[i] = ok && grad_out[i / terms] != 0.f ? (uint32_t)j : (uint32_t)table_len;  // else dropped
   }
 }
 
@@ -420,7 +424,7 @@ int cnnue_policy_table_bwd(const int64_t* d_indices, const float* d_grad_out, in
   uint32_t* keys = (uint32_t*)((char*)ws + sizeof(WorkspaceHeader));
   void* scratch = (char*)keys + align_up((size_t)n * 4, 256);
   if (n > 0) {
-    index_keys_kernel<<<grid_for(n), 256, 0, s>>>(d_indices, n, table_len, keys, status);
+    index_keys_kernel<<<grid_for(n), 256, 0, s>>>(d_indices, d_grad_out, terms, n, table_len, keys, status);
     if (int st = check_launch_error("index_keys_kernel")) return st;
   }
   return scat::launch_scatter_add(keys, d_grad_out, (uint32_t)terms, n, table_len, d_grad_table, scratch, s);

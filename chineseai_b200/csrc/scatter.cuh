@@ -207,8 +207,9 @@ __global__ void run_units_kernel(const uint32_t* __restrict__ run_start, const u
 }
 
 // One thread per unit: the unit's <= 256 contributions in order, loads
-// issued eight at a time.
-__global__ void unit_sum_kernel(const uint32_t* __restrict__ idx, const float* __restrict__ values, uint32_t div,
+// issued eight at a time.  Units of the drop key are skipped.
+__global__ void unit_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx,
+                                const float* __restrict__ values, uint32_t div, int64_t n_keys,
                                 const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ unit_off,
                                 const uint32_t* __restrict__ n_runs_d, const uint32_t* __restrict__ n_units_d,
                                 int64_t n, float* __restrict__ partial) {
@@ -223,6 +224,7 @@ __global__ void unit_sum_kernel(const uint32_t* __restrict__ idx, const float* _
     }
     const uint32_t r = lo;
     const uint32_t rbeg = run_start[r], rend = r + 1 < n_runs ? run_start[r + 1] : (uint32_t)n;
+    if ((int64_t)keys[rbeg] >= n_keys) continue;
     const uint32_t beg = rbeg + ((uint32_t)u - unit_off[r]) * kUnit;
     const uint32_t end = min(rend, beg + kUnit);
     float s = 0.f;
@@ -247,15 +249,16 @@ __global__ void run_sum_kernel(const uint32_t* __restrict__ keys, const uint32_t
   const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < n_runs; r += (int64_t)gridDim.x * blockDim.x) {
     const uint32_t k = keys[run_start[r]];
+    if ((int64_t)k >= n_keys) continue;  // key n_keys: dropped contributions
     const uint32_t u0 = unit_off[r], u1 = r + 1 < n_runs ? unit_off[r + 1] : n_units;
     float s = partial[u0];
     for (uint32_t u = u0 + 1; u < u1; ++u) s += partial[u];
-    if ((int64_t)k < n_keys) out[k] = s;  // key n_keys: a dropped contribution
+    out[k] = s;
   }
 }
 
-// Row form: one warp per unit; lanes walk the columns 32 at a time.  A
-// unit that is its run's only one writes the table row directly.  Val(e, h)
+// Row form: one warp per (unit, 32-column block); lanes own one column each.
+// A unit that is its run's only one writes the table row directly.  Val(e, h)
 // gives column h of contribution e; Out(key, h) the output element.
 template <class Val, class Out>
 __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const uint32_t* __restrict__ idx, Val val,
@@ -266,7 +269,10 @@ __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const ui
   const uint32_t n_runs = *n_runs_d, n_units = *n_units_d;
   const int lane = threadIdx.x & 31;
   const int64_t warps = ((int64_t)gridDim.x * blockDim.x) >> 5;
-  for (int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; u < n_units; u += warps) {
+  const int64_t col_blocks = (hidden + 31) >> 5;
+  for (int64_t q = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; q < (int64_t)n_units * col_blocks;
+       q += warps) {
+    const int64_t u = q / col_blocks, h = (q - u * col_blocks) * 32 + lane;
     uint32_t lo = 0, hi = n_runs - 1;
     while (lo < hi) {
       const uint32_t mid = (lo + hi + 1) >> 1;
@@ -280,21 +286,19 @@ __global__ void unit_sum_rows_kernel(const uint32_t* __restrict__ keys, const ui
     const uint32_t end = min(rend, beg + kUnit);
     const uint32_t key = keys[rbeg];
     const bool single = u1 - unit_off[r] == 1;
-    if ((int64_t)key >= n_keys) continue;  // dropped contributions: never evaluated
-    for (int64_t h = lane; h < hidden; h += 32) {
-      float s = 0.f;
-      uint32_t j = beg;
-      for (; j + 8 <= end; j += 8) {
-        float v[8];
+    if ((int64_t)key >= n_keys || h >= hidden) continue;  // dropped contributions: never evaluated
+    float s = 0.f;
+    uint32_t j = beg;
+    for (; j + 8 <= end; j += 8) {
+      float v[8];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) v[k] = val(__ldg(idx + j + k), h);
+      for (int k = 0; k < 8; ++k) v[k] = val(__ldg(idx + j + k), h);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s += v[k];
-      }
-      for (; j < end; ++j) s += val(__ldg(idx + j), h);
-      if (single) out(key, h) = s;
-      else partial[u * hidden + h] = s;
+      for (int k = 0; k < 8; ++k) s += v[k];
     }
+    for (; j < end; ++j) s += val(__ldg(idx + j), h);
+    if (single) out(key, h) = s;
+    else partial[u * hidden + h] = s;
   }
 }
 
@@ -431,8 +435,8 @@ int launch_scatter_add(const uint32_t* keys, const float* values, uint32_t div, 
   if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
   // grids for the upper bounds (units, runs <= n); the kernels stop at the counts
   const unsigned gb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 16));
-  unit_sum_kernel<<<gb, 256, 0, s>>>(r.idx, values, div, r.run_start, r.unit_off, r.n_runs, r.n_units, n,
-                                     r.partial);
+  unit_sum_kernel<<<gb, 256, 0, s>>>(r.keys, r.idx, values, div, n_keys, r.run_start, r.unit_off, r.n_runs,
+                                     r.n_units, n, r.partial);
   if (int st = check_launch_error("scatter unit sums")) return st;
   run_sum_kernel<<<gb, 256, 0, s>>>(r.keys, r.run_start, r.unit_off, r.n_runs, r.n_units, r.partial, n_keys, out);
   return check_launch_error("scatter run sums");
@@ -450,7 +454,8 @@ int launch_scatter_rows(const uint32_t* keys, Val val, Out out, int64_t hidden, 
   Runs r;
   if (int st = sort_runs(keys, n, n_keys, ws, s, &r)) return st;
   // grids for the upper bounds (units, runs <= n); the kernels stop at the counts
-  const unsigned ub = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n * 32 + 255) / 256, 148 * 16));
+  const unsigned ub =
+      (unsigned)std::max<int64_t>(1, std::min<int64_t>((n * ((hidden + 31) / 32) * 32 + 255) / 256, 148 * 16));
   unit_sum_rows_kernel<<<ub, 256, 0, s>>>(r.keys, r.idx, val, hidden, r.run_start, r.unit_off, r.n_runs, r.n_units,
                                           n, n_keys, r.partial, out);
   if (int st = check_launch_error("scatter unit row sums")) return st;

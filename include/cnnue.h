@@ -228,12 +228,12 @@ int cnnue_feature_pool_fwd(const float* d_tables, const uint32_t* d_items, int64
                            void* stream);
 
 /* grad_tables[r][h] = sum of grad_out[b][h] over every (b, item, slot) whose
- * slot row is r, without atomics: a stable counting sort of the contributions
- * by row, then a segmented reduction in that order (rows with at most 256
- * contributions are summed in exactly the reference CPU order; longer rows in
- * 256-contribution segments combined in order).  Deterministic run to run.
- * Every row of grad_tables is written.  The workspace's first word is the
- * status word (read it with cnnue_read_status).
+ * slot row is r, without atomics: a stable radix sort of the contributions by
+ * row, then per-row sums in that order (rows with at most 256 contributions
+ * are summed in exactly the reference CPU order; longer rows in
+ * 256-contribution units combined in order).  Deterministic run to run, no
+ * host synchronisation.  Every row of grad_tables is written.  The
+ * workspace's first word is the status word (read it with cnnue_read_status).
  * Replaces FeaturePoolGrad / kernel feature_pool_grad
  * (src/az/fused_feature_pool.rs:51-76, :214-223, CPU twin :231-260). */
 size_t cnnue_feature_pool_bwd_workspace_bytes(int64_t batch, int64_t item_count, int64_t hidden);

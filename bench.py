@@ -687,6 +687,17 @@ AZ_TRAIN_BATCH = 1024  # the reference's default batch (src/az_loop_config.rs:11
 AZ_TRAIN_CAPS = (40, 96, 96)  # fixed per-row widths: features, policy moves, threats
 
 
+def adam_traffic(n_params: int):
+    """DRAM bytes per AdamW launch from the committed ncu capture
+    (profiles/adamw_vec4_kernel.json), scaled to n_params."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "adamw_vec4_kernel.json")) as f:
+            d = json.load(f)
+        return int(d["dram_bytes_per_launch"] * n_params / d["params"])
+    except Exception:
+        return None
+
+
 def run_az_train(args):
     import torch
 
@@ -766,7 +777,7 @@ def run_az_train(args):
                        "parallelism": f"replicas{world}", "host_pack_ms_per_batch": pack_ms,
                        "l2": "not flushed: the step's inputs and parameters (~33 MB) are L2-sized"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": adam_traffic(tr.n_params),
                          "scope": f"adamw_vec4_kernel alone: 28 B x {tr.n_params} parameters per launch, "
                                   f"{a_ms * 1e3:.1f} us"},
             "e2e": {"value": world * B / (e2e_total / args.steps / 1e3), "unit": "samples/s",

@@ -100,6 +100,13 @@ SIGNATURES = {
     "cnnue_az_policy_moves": (c_int, [P, c_int, P, c_int, P]),
     "cnnue_az_pack_batch": (c_int, [c_void_p, P, c_i64, c_i64, c_i64, c_i64, c_int, c_void_p, c_int]),
     "cnnue_az_expand_policy_indices": (c_int, [P, P, P, c_i64, c_i64, P, P, P, P]),
+    "cnnue_az_legal_moves": (c_int, [P, c_int, P, c_int, C.POINTER(c_int)]),
+    "cnnue_mcts_default_limits": (None, [c_void_p]),
+    "cnnue_mcts_create": (c_int, [c_void_p, c_void_p, c_int, C.POINTER(c_void_p)]),
+    "cnnue_mcts_destroy": (c_int, [c_void_p]),
+    "cnnue_mcts_search": (c_int, [c_void_p, P, P, P, c_i64, c_void_p, P, C.POINTER(c_u64)]),
+    "cnnue_mcts_result": (c_int, [c_void_p, c_i64, P, P, P, P, c_int, C.POINTER(c_int), C.POINTER(c_int),
+                                  C.POINTER(C.c_float), C.POINTER(c_u32)]),
     "cnnue_az_evaluate_workspace_bytes": (c_size, [c_void_p, c_i64]),
     "cnnue_az_evaluate": (c_int, [c_void_p, P, P, P, P, c_u32, P, P, P, c_u32, P, c_i64, P, P, P, P, c_size, P]),
     "cnnue_rn_model_create": (c_int, [C.c_void_p, c_int, C.POINTER(c_void_p)]),

@@ -756,6 +756,54 @@ int cnnue_synth_q_update(uint64_t seed, int64_t n_positions, int16_t* h_parent, 
                          uint16_t* h_add, uint32_t* h_add_offsets, uint32_t* n_add,
                          uint8_t* h_count0);
 
+/* ---- wide-batch AlphaZero search ------------------------------------------
+ * Legal moves of `side` (pseudo-legal moves of every piece, less those that
+ * leave the mover's general attacked or facing the other general on an open
+ * file), as from/to square pairs in moves[2i], moves[2i+1]; *count gets the
+ * number (CNNUE_ERR_WORKSPACE when it exceeds capacity).  Board as above. */
+int cnnue_az_legal_moves(const int8_t* board, int side, uint8_t* moves, int capacity, int* count);
+
+/* AzSearchLimits (src/az/alphazero.rs:22-66) less the seed and root
+ * Dirichlet noise: the PUCT constants, max_depth (0 = simulations), first
+ * play urgency, policy softmax temperature, draw score and value scale. */
+typedef struct cnnue_mcts_limits {
+  int64_t simulations;
+  float cpuct, cpuct_at_root, cpuct_base, cpuct_factor, cpuct_base_at_root, cpuct_factor_at_root;
+  int64_t max_depth;
+  float fpu_value, fpu_value_at_root, policy_softmax_temp, draw_score, value_scale;
+} cnnue_mcts_limits;
+/* AzSearchLimits::default (simulations 10000, cpuct 1.5, base 19652, factor
+ * 2, fpu 0.30 / 0.20 at the root, temperature 1, draw score 0, scale 1). */
+void cnnue_mcts_default_limits(cnnue_mcts_limits* limits);
+
+/* A search over many roots in lockstep: each round every tree descends to one
+ * leaf and all leaves go to the GPU evaluator as one batch (trunk refresh of
+ * the side to move, policy accumulator refresh, threat logits when active,
+ * value head and the policy logits of the leaf's legal moves).  Replaces the
+ * batch-of-four scheduler alphazero_search_batch4_reusing
+ * (src/az/alphazero.rs:388-521) with AzTree's selection, expansion and
+ * backup (:959-1817).  The rules engine's repetition adjudication and rule
+ * history are not restated: every leaf of a tree takes its root's rule
+ * context (NULL = zeros).  Host-side leaf work runs on n_threads threads
+ * (<= 0: up to 16).  The model and weights must outlive the search. */
+typedef struct cnnue_mcts cnnue_mcts;
+int cnnue_mcts_create(const cnnue_az_model* model, const cnnue_az_weights* weights, int n_threads,
+                      cnnue_mcts** out);
+int cnnue_mcts_destroy(cnnue_mcts* search);
+/* boards [n_roots][90], sides [n_roots], rule_context [n_roots][7] or NULL.
+ * Runs limits->simulations simulations per root; *n_evaluations (optional)
+ * gets the number of network evaluations (leaves) spent. */
+int cnnue_mcts_search(cnnue_mcts* search, const int8_t* boards, const uint8_t* sides,
+                      const float* rule_context, int64_t n_roots, const cnnue_mcts_limits* limits,
+                      void* stream, uint64_t* n_evaluations);
+/* Root statistics of the last search: per root move (from/to pairs) its
+ * visits, prior and Q (root player's view), the index of the best move
+ * (visits, then Q, then prior: best_root_child, src/az/alphazero.rs:
+ * 1693-1716), the root's Q and visit count.  Output arrays may be NULL. */
+int cnnue_mcts_result(const cnnue_mcts* search, int64_t root, uint8_t* moves, uint32_t* visits,
+                      float* priors, float* q, int capacity, int* n_moves, int* best, float* root_q,
+                      uint32_t* root_visits);
+
 #ifdef __cplusplus
 }
 #endif

@@ -812,6 +812,124 @@ def run_az_train(args):
     return 0
 
 
+# ---------------------------------------------------------------------------
+# Wide-batch AlphaZero search (--workload mcts; not the headline line)
+# ---------------------------------------------------------------------------
+MCTS_ROOTS = 4096
+MCTS_SIMS = 64
+START_FEN = "rnbakabnr/9/1c5c1/p1p1p1p1p/9/9/P1P1P1P1P/1C5C1/9/RNBAKABNR w - - 0 1"
+
+
+def playout_roots(n: int, seed: int):
+    """The start position and positions after 1-40 random legal moves from it."""
+    from chineseai_b200 import az, mcts
+    rng = np.random.default_rng(seed)
+    b0, s0 = az.board_from_fen(START_FEN)
+    boards, sides = [b0], [s0]
+    while len(boards) < n:
+        b, side = b0.copy(), s0
+        for _ in range(int(rng.integers(1, 41))):
+            moves = mcts.legal_moves(b, side)
+            if len(moves) == 0 or not (b == -1).any() or not (b == 1).any():
+                break
+            frm, to = moves[rng.integers(len(moves))]
+            b[to], b[frm] = b[frm], 0
+            side = 1 - side
+        if (b == -1).any() and (b == 1).any() and len(mcts.legal_moves(b, side)):
+            boards.append(b)
+            sides.append(side)
+    return np.array(boards, np.int8), np.array(sides, np.uint8)
+
+
+def run_mcts(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+    from chineseai_b200 import az, mcts
+
+    w = az.AzWeights.random(128, 20260807)
+    model = az.AzModel(w, device=local)
+    boards, sides = playout_roots(MCTS_ROOTS, seed=1 + rank)
+    search = mcts.Search(model, w)
+    lim = mcts.default_limits(MCTS_SIMS)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(1, args.warmup // 3)):
+        search.run(boards[:256], sides[:256], lim, stream=stream.cuda_stream)
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    evals = []
+    box = {}
+
+    def one():
+        box["e"] = search.run(boards, sides, lim, stream=stream.cuda_stream)
+
+    steps = max(1, min(args.steps, 3))
+    total = 0.0
+    for _ in range(steps):
+        total += _device_loop(one, 1, dev, stream)
+        evals.append(box["e"])
+    clocks = sampler.stop()
+    st = search.stats()
+    stats = torch.tensor([total], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total = stats.item()
+    if rank == 0:
+        ms = total / steps
+        ev = float(np.mean(evals))
+        line = {
+            "metric": "AZ wide-batch search: network leaf evaluations/sec (4096 roots x 64 simulations, H=128)",
+            "value": world * ev / (ms / 1e3), "unit": "evals/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "AzNnue::random(128, 20260807); 4096 roots (start position + random legal "
+                                   "playouts of 1-40 plies), 64 simulations each, AzSearchLimits defaults; "
+                                   "one GPU batch of leaves per round", "roots_per_gpu": MCTS_ROOTS,
+                       "simulations": MCTS_SIMS, "parallelism": f"replicas{world}",
+                       "phase_seconds_last_search": st, "evaluations_per_search": ev,
+                       "simulations_per_sec": world * MCTS_ROOTS * MCTS_SIMS / (ms / 1e3)},
+            "roofline": None,
+            "e2e": {"value": world * ev / (ms / 1e3), "unit": "evals/s",
+                    "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                    "note": "the search is host-driven: value is already end to end"},
+            "clocks": clocks, "gpu_launches": 4 * st["rounds"] * steps,
+        }
+        if not args.no_cpu_baseline:
+            from oracle import mcts_ref
+            th, ta = w.quant_flags()
+            evr = mcts_ref.Evaluator(w.tensors(), 128, th, ta)
+            t0 = time.time()
+            n_ev = 0
+            k = 0
+            while time.time() - t0 < min(args.cpu_seconds, 15.0) or k == 0:
+                srch = mcts_ref.Search(evr, boards[k % len(boards)], int(sides[k % len(sides)]), MCTS_SIMS).run()
+                n_ev += sum(1 for n in srch.nodes if n["expanded"] and n["children"])
+                k += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": n_ev / el, "unit": "evals/s", "cores": 1, "kind": "port",
+                                    "sample": f"{k} single-tree searches of {MCTS_SIMS} simulations: the "
+                                              "oracle's search restatement with its C evaluator, one thread"}
+        print(json.dumps(line), flush=True)
+    search.close()
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -820,10 +938,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az", "az-train"], default="eval",
+    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az", "az-train", "mcts"], default="eval",
                     help="eval: the headline quantised forward; train: the data-parallel training step; "
                          "resnet: AlphaZero ResNet leaf batch; az: reference-native AZ-NNUE evaluation; "
-                         "az-train: the AZ-NNUE training step")
+                         "az-train: the AZ-NNUE training step; mcts: the wide-batch AlphaZero search")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -837,6 +955,8 @@ def main():
         return run_az(args)
     if args.workload == "az-train":
         return run_az_train(args)
+    if args.workload == "mcts":
+        return run_mcts(args)
     return run_ours(args)
 
 

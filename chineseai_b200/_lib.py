@@ -105,6 +105,7 @@ SIGNATURES = {
     "cnnue_mcts_create": (c_int, [c_void_p, c_void_p, c_int, C.POINTER(c_void_p)]),
     "cnnue_mcts_destroy": (c_int, [c_void_p]),
     "cnnue_mcts_search": (c_int, [c_void_p, P, P, P, c_i64, c_void_p, P, C.POINTER(c_u64)]),
+    "cnnue_mcts_stats": (c_int, [c_void_p, P, C.POINTER(c_u64)]),
     "cnnue_mcts_result": (c_int, [c_void_p, c_i64, P, P, P, P, c_int, C.POINTER(c_int), C.POINTER(c_int),
                                   C.POINTER(C.c_float), C.POINTER(c_u32)]),
     "cnnue_az_evaluate_workspace_bytes": (c_size, [c_void_p, c_i64]),

@@ -26,6 +26,7 @@
 // the moves that leave the mover's general attacked (or facing the other
 // general on an open file) removed.
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <condition_variable>
 #include <cstring>
@@ -681,6 +682,10 @@ struct cnnue_mcts {
     size_t bytes = 0;
   };
   Buf items, offsets, acc, pacc, threats, t_off, minfo, m_off, rule, wdl, q, logits, ws, ws_eval;
+  // seconds spent in the last search: selection + leaf preparation on the
+  // host, leaf inputs + GPU evaluation + copies, finalisation + backup
+  double t_select = 0, t_inputs = 0, t_gpu = 0, t_finalize = 0;
+  uint64_t rounds = 0;
   ~cnnue_mcts() {
     for (Buf* b : {&items, &offsets, &acc, &pacc, &threats, &t_off, &minfo, &m_off, &rule, &wdl, &q, &logits, &ws,
                    &ws_eval})
@@ -714,9 +719,14 @@ int grow(cnnue_mcts::Buf& b, size_t bytes) {
   } while (0)
 
 // Evaluates the pending leaves of trees[ids] in one GPU batch and finalises them.
+inline double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
 int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t stream) {
   const int64_t n = (int64_t)ids.size();
   if (n == 0) return CNNUE_OK;
+  const double t0 = now_s();
   // host inputs, in parallel per leaf
   s->pool->run(n, [&](int64_t k) {
     Tree& t = s->trees[ids[k]];
@@ -752,13 +762,17 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
   std::vector<uint32_t> items(std::max<uint32_t>(off[n], 1)), threats(std::max<uint32_t>(toff[n], 1)),
       minfo(2 * std::max<uint32_t>(moff[n], 1));
   std::vector<float> rule((size_t)n * CNNUE_AZ_RULE_CONTEXT);
-  for (int64_t k = 0; k < n; ++k) {
-    const Tree& t = s->trees[ids[k]];
-    std::copy(t.items.begin(), t.items.end(), items.begin() + off[k]);
-    std::copy(t.threats.begin(), t.threats.end(), threats.begin() + toff[k]);
-    std::copy(t.move_info.begin(), t.move_info.begin() + 2 * t.pending.moves.size(), minfo.begin() + 2 * moff[k]);
-    std::copy(t.rule, t.rule + CNNUE_AZ_RULE_CONTEXT, rule.begin() + k * CNNUE_AZ_RULE_CONTEXT);
-  }
+  const int64_t chunk = 256;
+  s->pool->run((n + chunk - 1) / chunk, [&](int64_t c) {
+    for (int64_t k = c * chunk; k < std::min(n, (c + 1) * chunk); ++k) {
+      const Tree& t = s->trees[ids[k]];
+      std::copy(t.items.begin(), t.items.end(), items.begin() + off[k]);
+      std::copy(t.threats.begin(), t.threats.end(), threats.begin() + toff[k]);
+      std::copy(t.move_info.begin(), t.move_info.begin() + 2 * t.pending.moves.size(), minfo.begin() + 2 * moff[k]);
+      std::copy(t.rule, t.rule + CNNUE_AZ_RULE_CONTEXT, rule.begin() + k * CNNUE_AZ_RULE_CONTEXT);
+    }
+  });
+  const double t1 = now_s();
   const size_t ev_ws = cnnue_az_evaluate_workspace_bytes(s->model, n);
   MCTS_TRY(grow(s->items, items.size() * 4));
   MCTS_TRY(grow(s->offsets, off.size() * 4));
@@ -800,11 +814,17 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
   if (status != CNNUE_OK) return set_error(status, "leaf evaluation reported bad input");
   MCTS_TRY(cnnue_read_status(s->ws_eval.d, stream, &status));
   if (status != CNNUE_OK) return set_error(status, "leaf evaluation reported bad input");
+  const double t2 = now_s();
   s->pool->run(n, [&](int64_t k) {
     Tree& t = s->trees[ids[k]];
     Eval e{{wdl[k * 3], wdl[k * 3 + 1], wdl[k * 3 + 2]}, q[k]};
     t.finalize(e, logits.data() + moff[k]);
   });
+  const double t3 = now_s();
+  s->t_inputs += t1 - t0;
+  s->t_gpu += t2 - t1;
+  s->t_finalize += t3 - t2;
+  s->rounds += 1;
   return CNNUE_OK;
 }
 
@@ -887,6 +907,8 @@ int cnnue_mcts_search(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides,
       t.rule[k] = rule_context ? rule_context[i * CNNUE_AZ_RULE_CONTEXT + k] : 0.f;
   }
   uint64_t evals = 0;
+  s->t_select = s->t_inputs = s->t_gpu = s->t_finalize = 0;
+  s->rounds = 0;
   // every root is expanded first, in one batch (tree.expand(root), :440-445)
   {
     std::vector<uint32_t> ids;
@@ -899,6 +921,7 @@ int cnnue_mcts_search(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides,
     MCTS_TRY(evaluate_round(s, ids, st));
   }
   for (;;) {
+    const double ts = now_s();
     s->pool->run(n_roots, [&](int64_t i) {
       Tree& t = s->trees[i];
       while (!t.has_pending && t.completed < (uint64_t)t.lim.simulations) {
@@ -913,11 +936,22 @@ int cnnue_mcts_search(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides,
     std::vector<uint32_t> ids;
     for (int64_t i = 0; i < n_roots; ++i)
       if (s->trees[i].has_pending) ids.push_back((uint32_t)i);
+    s->t_select += now_s() - ts;
     if (ids.empty()) break;
     evals += ids.size();
     MCTS_TRY(evaluate_round(s, ids, st));
   }
   if (n_evaluations) *n_evaluations = evals;
+  return CNNUE_OK;
+}
+
+int cnnue_mcts_stats(const cnnue_mcts* s, double* seconds, uint64_t* rounds) {
+  if (!s || !seconds) return set_error(CNNUE_ERR_INVALID_ARG, "null search or seconds");
+  seconds[0] = s->t_select;
+  seconds[1] = s->t_inputs;
+  seconds[2] = s->t_gpu;
+  seconds[3] = s->t_finalize;
+  if (rounds) *rounds = s->rounds;
   return CNNUE_OK;
 }
 

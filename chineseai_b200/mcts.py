@@ -82,6 +82,14 @@ class Search:
         self.n_roots = len(b)
         return evals.value
 
+    def stats(self) -> dict:
+        """Seconds of the last search by phase and its number of GPU rounds."""
+        sec = np.zeros(4, np.float64)
+        rounds = C.c_uint64()
+        check(lib().cnnue_mcts_stats(self._h, sec.ctypes.data, C.byref(rounds)), "cnnue_mcts_stats")
+        return {"select_s": sec[0], "inputs_s": sec[1], "gpu_s": sec[2], "finalize_s": sec[3],
+                "rounds": rounds.value}
+
     def result(self, root: int) -> dict:
         cap = 128
         moves = np.zeros((cap, 2), np.uint8)

@@ -311,23 +311,33 @@ __global__ void __launch_bounds__(kPThreads, 1) rn_pconv_kernel(const __grid_con
         tc::fence_after_sync();
         const uint32_t d0 = tmem + (uint32_t)(buf * 256), d1 = d0 + 128;
         bool ok = true;
-        for (int kb = 0; kb < kKb; ++kb, ++g) {
-          const uint32_t s = g % kPStages, u = g / kPStages;
-          if (!pipe::mbar_wait(&sm.ready[s], u & 1, &sm.abort, status)) {
-            ok = false;
-            break;
+        // K blocks two at a time: both stages' waits, one fence, 16 MMAs,
+        // then both stages released (one fence per 1024 cycles of MMA work)
+        for (int kb = 0; kb < kKb; kb += 2) {
+          const int nk = kb + 1 < kKb ? 2 : 1;
+          for (int j = 0; j < nk; ++j) {
+            const uint32_t s = (g + j) % kPStages, u = (g + j) / kPStages;
+            if (!pipe::mbar_wait(&sm.ready[s], u & 1, &sm.abort, status)) {
+              ok = false;
+              break;
+            }
           }
+          if (!ok) break;
           tc::fence_after_sync();
-          const uint32_t a0 = pipe::smem_addr(sm.a[s][0]), a1 = pipe::smem_addr(sm.a[s][1]);
-          const uint32_t b0 = pipe::smem_addr(sm.b[s]);
+          for (int j = 0; j < nk; ++j) {
+            const uint32_t s = (g + j) % kPStages;
+            const uint32_t a0 = pipe::smem_addr(sm.a[s][0]), a1 = pipe::smem_addr(sm.a[s][1]);
+            const uint32_t b0 = pipe::smem_addr(sm.b[s]);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = tc::smem_desc(b0 + kk * 32, 0, 1024, tc::kSwizzle128B);
-            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-            tc::mma_bf16(d0, tc::smem_desc(a0 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
-            tc::mma_bf16(d1, tc::smem_desc(a1 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bd = tc::smem_desc(b0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+              const uint32_t acc = ((kb + j) | kk) != 0 ? 1u : 0u;
+              tc::mma_bf16(d0, tc::smem_desc(a0 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
+              tc::mma_bf16(d1, tc::smem_desc(a1 + kk * 32, 0, 1024, tc::kSwizzle128B), bd, idesc, acc);
+            }
+            tc::commit(pipe::smem_addr(&sm.empty[s]));
           }
-          tc::commit(pipe::smem_addr(&sm.empty[s]));
+          g += nk;
         }
         tc::commit(pipe::smem_addr(&sm.acc_full[buf]));
         if (!ok) break;

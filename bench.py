@@ -720,12 +720,12 @@ def run_az_train(args):
     batches = [az_train.pack_batch(samples, np.arange(k * B, (k + 1) * B), caps=AZ_TRAIN_CAPS, fixed=True,
                                    compact=True) for k in range(4)]
     pack_ms = (time.time() - t0) / 4 * 1e3
-    tr = az_train.AzTrainer(w, lr=1e-3, device=local, graph=True)
+    tr = az_train.AzTrainer(w, lr=1e-3, device=local, graph=True, group=pg.group.WORLD if pg else None)
     for i in range(max(args.warmup, 3)):
         tr.step(batches[i % 4])
     # kernels of one step: a profiled eager step of a twin trainer (outside the timed region)
     from torch.profiler import ProfilerActivity, profile
-    twin = az_train.AzTrainer(w, lr=1e-3, device=local)
+    twin = az_train.AzTrainer(w, lr=1e-3, device=local)  # single-rank twin: counts kernels, no collective
     twin.step(batches[0])
     with profile(activities=[ProfilerActivity.CUDA]) as prof:
         twin.step(batches[1])
@@ -743,7 +743,12 @@ def run_az_train(args):
         pg.barrier()
     sampler.start()
     time.sleep(0.3)
-    total = _device_loop(tr._graph.replay, args.steps, dev, stream)
+    def device_step():
+        tr._graph.replay()
+        if tr.world > 1:
+            tr._exchange_and_update()
+
+    total = _device_loop(device_step, args.steps, dev, stream)
     clocks = sampler.stop()
     # end to end: AzTrainer.step on host batches (pinned staging + H2D, metrics back)
     e2e_total = _device_loop(lambda: tr.step(batches[np.random.randint(4)]), args.steps, dev, stream)
@@ -774,7 +779,7 @@ def run_az_train(args):
                                    "(random boards, pseudo moves, gamma visit targets), fixed widths "
                                    f"{AZ_TRAIN_CAPS}, compact batches (lookup indices rebuilt on the GPU); "
                                    "one CUDA-graph step", "batch_per_gpu": B,
-                       "parallelism": f"replicas{world}", "host_pack_ms_per_batch": pack_ms,
+                       "parallelism": f"dp{world}" if world > 1 else "dp1", "host_pack_ms_per_batch": pack_ms,
                        "l2": "not flushed: the step's inputs and parameters (~33 MB) are L2-sized"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": adam_traffic(tr.n_params),

@@ -221,6 +221,17 @@ def pack_batch(samples: Samples, rows: Optional[np.ndarray] = None, n_threads: i
 
 
 # ---- the training step --------------------------------------------------------
+def mean_allreduce_(grad, group=None) -> int:
+    """grad <- the mean of grad over the ranks of `group` (sum all-reduce, then
+    1 / world); returns the world size.  With equal shares of the batch per
+    rank this is the gradient of the whole batch's mean loss."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    dist.all_reduce(grad, op=dist.ReduceOp.SUM, group=group)
+    grad.mul_(1.0 / world)
+    return world
+
+
 def _raise_status(word: int, where: str) -> None:
     """The kernels' status bits as cnnue_read_status maps them."""
     if word == 0:
@@ -280,13 +291,25 @@ class AzTrainer:
     CUDA graph once a batch shape repeats (batches packed with fixed=True all
     share one shape), and replays it; the first step of each new shape runs
     eagerly.  The AdamW step counter and learning rate live in device memory
-    (cnnue_adamw_device), so replays advance them."""
+    (cnnue_adamw_device), so replays advance them.
+
+    group: a torch.distributed process group (NCCL) for data parallelism:
+    every rank steps on its own equal share of the batch, the flat gradient is
+    sum-all-reduced once and scaled by 1 / world (the gradient of the whole
+    batch's mean loss), and every rank applies the same AdamW update.  The
+    captured graph then holds forward and backward only; the all-reduce and
+    AdamW run after it, outside the graph."""
 
     def __init__(self, weights: "az.AzWeights", lr: float = 1e-3, device: int = 0, weight_decay: float = 1e-4,
-                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False):
+                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False, group=None):
         import torch
         self.torch = torch
         self.use_graph = graph
+        self.group = group
+        self.world = 1
+        if group is not None:
+            import torch.distributed as dist
+            self.world = dist.get_world_size(group)
         self._graph = None
         self._graph_key = None
         self._last_key = None
@@ -453,11 +476,21 @@ class AzTrainer:
         self.status.zero_()
         loss, metrics = self.loss(self.expand(bt), value_weight, policy_weight)
         loss.backward()
+        if self.world == 1:
+            self._adamw()
+        return self.torch.cat([metrics, self.status.float()])
+
+    def _adamw(self) -> None:
         check(lib().cnnue_adamw_device(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
                                        self.grad.data_ptr(), self.n_params, self.adam_state.data_ptr(),
                                        self.torch.cuda.current_stream(self.device).cuda_stream),
               "cnnue_adamw_device")
-        return self.torch.cat([metrics, self.status.float()])
+
+    def _exchange_and_update(self) -> None:
+        """Data parallel: the gradient averaged over the ranks, then the same
+        AdamW step everywhere (one NCCL all-reduce per step)."""
+        mean_allreduce_(self.grad[: self.n_params], self.group)
+        self._adamw()
 
     def step(self, batch: PackedBatch, value_weight: float = 1.0, policy_weight: float = 1.0) -> TrainStats:
         """One train_batch_single (src/az/train_gpu_candle.rs:145-160):
@@ -486,6 +519,8 @@ class AzTrainer:
         else:
             out = self._step_body(bt, value_weight, policy_weight)
         self._last_key = key
+        if self.world > 1:
+            self._exchange_and_update()
         m = out.cpu().numpy()
         _raise_status(int(m[-1]), "AzTrainer.step")
         return TrainStats(*[float(x) for x in m[:9]], samples=batch.batch_size, phase=m[9:30].reshape(3, 7))

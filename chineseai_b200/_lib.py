@@ -83,6 +83,7 @@ SIGNATURES = {
     "cnnue_az_weights_tensor": (c_int, [c_void_p, c_int, C.POINTER(C.POINTER(C.c_float)), C.POINTER(c_i64)]),
     "cnnue_az_model_create": (c_int, [c_void_p, c_int, C.POINTER(c_void_p)]),
     "cnnue_az_model_destroy": (c_int, [c_void_p]),
+    "cnnue_az_model_device": (c_int, [c_void_p]),
     "cnnue_az_workspace_bytes": (c_size, []),
     "cnnue_az_refresh": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_az_transition": (c_int, [c_void_p, P, P, P, P, c_u32, P, c_i64, P, P, c_size, P]),

@@ -881,6 +881,8 @@ int cnnue_az_model_create(const cnnue_az_weights* w, int device, cnnue_az_model*
   return CNNUE_OK;
 }
 
+int cnnue_az_model_device(const cnnue_az_model* m) { return m ? m->device : -1; }
+
 int cnnue_az_model_destroy(cnnue_az_model* m) {
   if (!m) return CNNUE_OK;
   DeviceGuard guard(m->device);

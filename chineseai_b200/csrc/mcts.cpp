@@ -883,11 +883,31 @@ int cnnue_mcts_destroy(cnnue_mcts* s) {
   return CNNUE_OK;
 }
 
+namespace {
+int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, const float* rule_context,
+                     int64_t n_roots, const cnnue_mcts_limits* limits, void* stream, uint64_t* n_evaluations);
+}
+
 int cnnue_mcts_search(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, const float* rule_context,
                       int64_t n_roots, const cnnue_mcts_limits* limits, void* stream, uint64_t* n_evaluations) {
   if (!s || !limits || n_roots < 0 || (n_roots > 0 && (!boards || !sides)))
     return set_error(CNNUE_ERR_INVALID_ARG, "null search, limits, boards or sides");
   if (limits->simulations < 0) return set_error(CNNUE_ERR_INVALID_ARG, "negative simulations");
+  // the staging buffers and every launch go to the model's device
+  int prev = -1;
+  MCTS_CUDA(cudaGetDevice(&prev));
+  const int dev = cnnue_az_model_device(s->model);
+  if (dev != prev) MCTS_CUDA(cudaSetDevice(dev));
+  const int st = search_on_device(s, boards, sides, rule_context, n_roots, limits, stream, n_evaluations);
+  if (dev != prev) cudaSetDevice(prev);
+  return st;
+}
+
+}  // extern "C"
+
+namespace {
+int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, const float* rule_context,
+                     int64_t n_roots, const cnnue_mcts_limits* limits, void* stream, uint64_t* n_evaluations) {
   cudaStream_t st = (cudaStream_t)stream;
   s->trees.clear();
   s->trees.resize(n_roots);
@@ -944,6 +964,9 @@ int cnnue_mcts_search(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides,
   if (n_evaluations) *n_evaluations = evals;
   return CNNUE_OK;
 }
+}  // namespace
+
+extern "C" {
 
 int cnnue_mcts_stats(const cnnue_mcts* s, double* seconds, uint64_t* rounds) {
   if (!s || !seconds) return set_error(CNNUE_ERR_INVALID_ARG, "null search or seconds");

@@ -571,6 +571,8 @@ int cnnue_az_dense_moves(uint16_t* dense_to_sparse, uint16_t* sparse_to_dense);
 typedef struct cnnue_az_model cnnue_az_model;
 int cnnue_az_model_create(const cnnue_az_weights* weights, int device, cnnue_az_model** out);
 int cnnue_az_model_destroy(cnnue_az_model* model);
+/* The CUDA device ordinal the model lives on (-1 for a null model). */
+int cnnue_az_model_device(const cnnue_az_model* model);
 /* Workspace of the AZ entry points (the status word). */
 size_t cnnue_az_workspace_bytes(void);
 

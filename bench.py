@@ -681,6 +681,232 @@ def run_az(args):
 
 
 # ---------------------------------------------------------------------------
+# fp32 HalfKA forward (--workload fp32) and incremental update (--workload update)
+# ---------------------------------------------------------------------------
+F32_BATCH = 4096
+F32_STACK_BYTES = 8 * (16 * 512 + 16 + 32 * 16 + 32 + 32 + 1) * 4 + 256 * 4
+
+
+def _dist_init(local):
+    import torch
+    if dist_env()[1] == 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return dist
+
+
+def _timed_steps(step, steps, dev, stream, flush):
+    """Per step: L2 flush (not timed), then the step between CUDA events."""
+    import torch
+    total = 0.0
+    for _ in range(steps):
+        flush.fill_(1)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        step()
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        total += a.elapsed_time(b)
+    return total
+
+
+def run_fp32(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = _dist_init(local)
+    from chineseai_b200 import synth
+    from chineseai_b200.fp32 import FloatNnue
+    from chineseai_b200.quantized import as_device
+
+    w = synth.float_weights(2)
+    model = FloatNnue(w, device=local)
+    pos = synth.positions(F32_BATCH, 1 + rank)
+    n_idx = len(pos.indices)
+    idx, off = as_device(pos.indices, dev), as_device(pos.offsets, dev)
+    out = torch.empty(F32_BATCH, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    h_idx = torch.from_numpy(pos.indices.view(np.int16)).pin_memory()
+    h_off = torch.from_numpy(pos.offsets.view(np.int32)).pin_memory()
+    h_out = torch.empty(F32_BATCH, dtype=torch.float32).pin_memory()
+
+    def step():
+        model.forward(idx, off, F32_BATCH, out=out, check_status=False)
+
+    def step_e2e():
+        idx.copy_(h_idx, non_blocking=True)
+        off.copy_(h_off, non_blocking=True)
+        step()
+        h_out.copy_(out, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        step_e2e()
+    model.forward(idx, off, F32_BATCH, out=out)  # checks the kernel status once
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    total = _timed_steps(step, args.steps, dev, stream, flush)
+    clocks = sampler.stop()
+    e2e_total = _timed_steps(step_e2e, args.steps, dev, stream, flush)
+    stats = torch.tensor([total, e2e_total], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, e2e_total = stats.tolist()
+    if rank == 0:
+        ms = total / args.steps
+        alg = n_idx * 256 * 4 + n_idx * 2 + pos.offsets.nbytes + F32_BATCH * 4 + F32_STACK_BYTES
+        peak, peak_kind = measured_hbm_peak()
+        achieved = alg / (ms / 1e3) / 1e9
+        line = {
+            "metric": "fp32 HalfKA NNUE evals/sec (batch 4096)", "value": world * F32_BATCH / (ms / 1e3),
+            "unit": "evals/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "fp32 HalfKA forward: FT 11340x256 N(0,0.01) per perspective, 2-32 unique "
+                                   "sorted indices, CReLU, bucket=(n0-1)/4 of 8 stacks 512->16->32->1",
+                       "batch_per_gpu": F32_BATCH, "parallelism": f"replicas{world}",
+                       "l2": "flushed (256 MiB write) before each timed step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "scope": "whole forward (one kernel): gathered fp32 rows, indices, offsets, outputs, "
+                                  "stack weights once; the 11.6 MB table is L2-resident after the first rows"},
+            "e2e": {"value": world * F32_BATCH / (e2e_total / args.steps / 1e3), "unit": "evals/s",
+                    "h2d_bytes_per_step": int(pos.indices.nbytes + pos.offsets.nbytes),
+                    "d2h_bytes_per_step": F32_BATCH * 4},
+            "clocks": clocks, "gpu_launches": args.steps,
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            t0 = time.time()
+            reps = 0
+            while time.time() - t0 < min(args.cpu_seconds, 10.0) or reps == 0:
+                oracle.f_forward(w, pos)
+                reps += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": reps * F32_BATCH / el, "unit": "evals/s", "cores": 1, "kind": "port",
+                                    "sample": f"{reps} x the 4096-position batch, one thread"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def run_update(args):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = _dist_init(local)
+    from chineseai_b200 import synth
+    from chineseai_b200._lib import check, lib
+    from chineseai_b200.quantized import QuantizedNnue, as_device
+
+    L = lib()
+    w = synth.quantized_weights(2)
+    model = QuantizedNnue(w, device=local)
+    ub = synth.update_batch(BATCH, 1 + rank)
+    n = ub.n
+    parent = as_device(ub.parent, dev)
+    flags, c0 = as_device(ub.flags, dev), as_device(ub.count0, dev)
+    rem, add = as_device(ub.rem, dev), as_device(ub.add, dev)
+    ro, ao = as_device(ub.rem_offsets, dev), as_device(ub.add_offsets, dev)
+    child = torch.empty((n, 2, 1024), dtype=torch.int16, device=dev)
+    scores = torch.empty(n, dtype=torch.int32, device=dev)
+    ws = model.workspace(n)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    pinned = {k: torch.from_numpy(np.ascontiguousarray(getattr(ub, k)).view(
+        {1: np.int8, 2: np.int16, 4: np.int32}[getattr(ub, k).dtype.itemsize])).pin_memory()
+        for k in ("flags", "rem", "rem_offsets", "add", "add_offsets", "count0")}
+    dst = {"flags": flags, "rem": rem, "rem_offsets": ro, "add": add, "add_offsets": ao, "count0": c0}
+    h_scores = torch.empty(n, dtype=torch.int32).pin_memory()
+
+    def step():
+        check(L.cnnue_q_update(model.handle, parent.data_ptr(), flags.data_ptr(), rem.data_ptr(), len(ub.rem),
+                               ro.data_ptr(), add.data_ptr(), len(ub.add), ao.data_ptr(), c0.data_ptr(), n,
+                               child.data_ptr(), scores.data_ptr(), ws.data_ptr(), ws.numel(), sp), "update")
+
+    def step_e2e():
+        for k, t in pinned.items():
+            dst[k].view(t.dtype).copy_(t, non_blocking=True)
+        step()
+        h_scores.copy_(scores, non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        step_e2e()
+    torch.cuda.synchronize(dev)
+    check(model.read_status(ws), "update kernel status")
+    sampler = ClockSampler(local)
+    if pg:
+        pg.barrier()
+    sampler.start()
+    time.sleep(0.3)
+    total = _timed_steps(step, args.steps, dev, stream, flush)
+    clocks = sampler.stop()
+    e2e_total = _timed_steps(step_e2e, args.steps, dev, stream, flush)
+    stats = torch.tensor([total, e2e_total], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(stats, op=pg.ReduceOp.MAX)
+    total, e2e_total = stats.tolist()
+    if rank == 0:
+        ms = total / args.steps
+        rows = len(ub.rem) + len(ub.add)
+        list_bytes = sum(np.asarray(getattr(ub, k)).nbytes for k in dst)
+        alg = n * 4096 * 2 + rows * 2048 + list_bytes + n * 4 + STACK_BYTES
+        peak, peak_kind = measured_hbm_peak()
+        achieved = alg / (ms / 1e3) / 1e9
+        line = {
+            "metric": "quantised incremental update + stack evals/sec (batch 64K)",
+            "value": world * n / (ms / 1e3), "unit": "evals/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int16/int8", "data": "synthetic",
+            "config": {"workload": "65,536 int16 parent accumulators [2][1024] U[-2000,2000]; per perspective 1-2 "
+                                   "removed and 1-3 added rows, 5% full refreshes of 2-32 rows; then the pairwise "
+                                   "pack and the 16 int8 bucket stacks", "batch_per_gpu": n,
+                       "parallelism": f"replicas{world}", "l2": "flushed (256 MiB write) before each timed step"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "scope": "cnnue_q_update (one kernel): parent read + child write (8 KB per position), "
+                                  "2 KB per added/removed row, the lists, scores, stack weights once"},
+            "e2e": {"value": world * n / (e2e_total / args.steps / 1e3), "unit": "evals/s",
+                    "h2d_bytes_per_step": int(list_bytes), "d2h_bytes_per_step": n * 4,
+                    "note": "parents and children stay on the device (the search's node arena); the step's "
+                            "delta lists go up and its scores come back"},
+            "clocks": clocks, "gpu_launches": args.steps,
+        }
+        if not args.no_cpu_baseline:
+            import oracle
+            sample = synth.update_batch(8192, 1 + rank)
+            t0 = time.time()
+            reps = 0
+            while time.time() - t0 < min(args.cpu_seconds, 10.0) or reps == 0:
+                oracle.q_update(w, sample, n_threads=cpu_threads())
+                reps += 1
+            el = time.time() - t0
+            line["cpu_baseline"] = {"value": reps * sample.n / el, "unit": "evals/s", "cores": cpu_threads(),
+                                    "kind": "port", "sample": f"{reps} x 8192 updates (same generator), "
+                                                              "all host threads"}
+        print(json.dumps(line), flush=True)
+    model.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+# ---------------------------------------------------------------------------
 # AZ-NNUE training step (--workload az-train; not the headline line)
 # ---------------------------------------------------------------------------
 AZ_TRAIN_BATCH = 1024  # the reference's default batch (src/az_loop_config.rs:115)
@@ -943,8 +1169,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["eval", "train", "resnet", "az", "az-train", "mcts"], default="eval",
-                    help="eval: the headline quantised forward; train: the data-parallel training step; "
+    ap.add_argument("--workload", choices=["eval", "fp32", "update", "train", "resnet", "az", "az-train", "mcts"],
+                    default="eval",
+                    help="eval: the headline quantised forward; fp32: the fp32 forward (batch 4096); "
+                         "update: the incremental update + stack; train: the data-parallel training step; "
                          "resnet: AlphaZero ResNet leaf batch; az: reference-native AZ-NNUE evaluation; "
                          "az-train: the AZ-NNUE training step; mcts: the wide-batch AlphaZero search")
     args = ap.parse_args()
@@ -962,6 +1190,10 @@ def main():
         return run_az_train(args)
     if args.workload == "mcts":
         return run_mcts(args)
+    if args.workload == "fp32":
+        return run_fp32(args)
+    if args.workload == "update":
+        return run_update(args)
     return run_ours(args)
 
 

@@ -166,11 +166,13 @@ __device__ __forceinline__ uint32_t desc_rows(const PosDesc& d) {
   return d.init[0] + d.rem[0].cnt + d.add[0].cnt + d.init[1] + d.rem[1].cnt + d.add[1].cnt;
 }
 
-// Stage layout.  Each position contributes, per perspective, up to three row
-// lists in this order: the parent row (update only, 1 row), the removed rows
-// (update only, subtracted) and the added/active rows.  Every list starts on
-// a fresh stage of at most kStageRows rows, so a stage never mixes lists and
-// both sides walk stages, not rows.  Stage st lives in ring slots
+// Stage layout.  Each position contributes one row sequence per perspective,
+// starting on a fresh stage of at most kStageRows rows: in the forward the
+// active rows; in the update the parent row (unless the perspective is
+// refreshed), then the removed rows (subtracted), then the added rows - one
+// sequence, so a typical update perspective (1 + 2 + 3 rows) fills a single
+// stage.  int16 wraparound sums are order-free, so grouping does not change
+// results.  Both sides walk stages, not rows.  Stage st lives in ring slots
 // (st % kStages) * kStageRows ...; lane 0 of its producer warp performs the
 // stage's barrier operations
 // and bulk copies.  Stages are dealt round-robin to the producer warps (stage
@@ -235,7 +237,77 @@ struct Producer {
       }
     }
   }
+
+  // Update mode: the stages of one perspective's sequence [parent row if
+  // init][removed rows][added rows].  `head_rem` / `head_add` hold the first
+  // 32 entries of the two lists (prefetched); row r of the sequence resolves
+  // lane-parallel (lane j -> row first + j).
+  __device__ __forceinline__ void update_seq(const char* ft, const char* parent_row, uint32_t init,
+                                             const uint16_t* rem_list, Seg rem, uint32_t head_rem,
+                                             const uint16_t* add_list, Seg add, uint32_t head_add, uint32_t st0) {
+    const uint32_t total = init + rem.cnt + add.cnt;
+    const uint32_t ns = n_stages(total);
+    uint32_t k = (uint32_t)((w - (int)(st0 % kProducers) + kProducers) % kProducers);
+    for (; k < ns; k += kProducers) {
+      const uint32_t st = st0 + k;
+      const uint32_t first = k * kStageRows;
+      const uint32_t rows = min((uint32_t)kStageRows, total - first);
+      const uint32_t r = first + (uint32_t)lane;
+      const uint32_t ir = r - init;            // index into the removed list (when in range)
+      const uint32_t ia = r - init - rem.cnt;  // index into the added list (when in range)
+      const uint32_t hr = __shfl_sync(kFull, head_rem, (int)(ir & 31u));
+      const uint32_t ha = __shfl_sync(kFull, head_add, (int)(ia & 31u));
+      uint32_t f = 0, par = 0;
+      if ((uint32_t)lane < rows) {
+        if (r < init) {
+          par = 1;
+        } else if (ir < rem.cnt) {
+          f = ir < 32 ? hr : rem_list[rem.beg + ir];
+        } else {
+          f = ia < 32 ? ha : add_list[add.beg + ia];
+        }
+        if (!par && f >= (uint32_t)kF) {  // bad index -> the zero row
+          atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+          f = kF;
+        }
+      }
+      bool go = false;
+      if (lane == 0) go = begin_stage(st, rows);
+      for (uint32_t j = 0; j < rows; ++j) {
+        const uint32_t fj = __shfl_sync(kFull, f, (int)j);
+        const uint32_t pj = __shfl_sync(kFull, par, (int)j);
+        if (lane == 0 && go) copy(st, j, pj ? parent_row : ft + (size_t)fj * kRowBytes);
+      }
+    }
+  }
 };
+
+// Consumer of an update perspective's sequence: rows [0, init) set from the
+// parent (acc starts at zero then), [init, init + n_rem) subtracted, the rest
+// added.  Returns the next stage number.
+__device__ __forceinline__ uint32_t consume_update(BulkSmem& sm, uint32_t st, uint32_t init, uint32_t n_rem,
+                                                   uint32_t n_add, int t, int lane, uint32_t* status,
+                                                   uint4& acc) {
+  const uint32_t total = init + n_rem + n_add;
+  for (uint32_t first = 0; first < total; first += kStageRows, ++st) {
+    const uint32_t sidx = st % kStages;
+    const uint32_t rows = min((uint32_t)kStageRows, total - first);
+    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status);
+    const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
+    uint4 v[kStageRows];
+#pragma unroll
+    for (int j = 0; j < kStageRows; ++j)
+      v[j] = (uint32_t)j < rows ? *reinterpret_cast<const uint4*>(slot + j * kRowBytes) : make_uint4(0, 0, 0, 0);
+    __syncwarp();
+    if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
+#pragma unroll
+    for (int j = 0; j < kStageRows; ++j) {
+      const uint32_t r = first + (uint32_t)j;
+      acc = (r >= init && r < init + n_rem) ? vsub(acc, v[j]) : vadd(acc, v[j]);
+    }
+  }
+  return st;
+}
 
 // Consumer: accumulates the rows of one list into acc (kOp 0 = set from the
 // single parent row, 1 = add, 2 = subtract).  Returns the next stage number.
@@ -265,8 +337,7 @@ __device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint
 }
 
 __device__ __forceinline__ uint32_t desc_stages(const PosDesc& d) {
-  return d.init[0] + n_stages(d.rem[0].cnt) + n_stages(d.add[0].cnt) + d.init[1] +
-         n_stages(d.rem[1].cnt) + n_stages(d.add[1].cnt);
+  return n_stages(d.init[0] + d.rem[0].cnt + d.add[0].cnt) + n_stages(d.init[1] + d.rem[1].cnt + d.add[1].cnt);
 }
 
 // Lane-parallel descriptor of position i (valid lanes only).
@@ -370,16 +441,13 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
 #pragma unroll
         for (int p = 0; p < 2; ++p) {
           if (kUpdate) {
-            if (cur.init[p]) {
-              if ((int)(st % kProducers) == pr.w && lane == 0 && pr.begin_stage(st, 1))
-                pr.copy(st, 0, par_lo + (2 * (int64_t)cur.pos + p) * kRowBytes);
-              st += 1;
-            }
-            pr.list(ft, a.rem, cur.rem[p], head.rem[p], st);
-            st += n_stages(cur.rem[p].cnt);
+            pr.update_seq(ft, par_lo + (2 * (int64_t)cur.pos + p) * kRowBytes, cur.init[p], a.rem, cur.rem[p],
+                          head.rem[p], a.idx, cur.add[p], head.add[p], st);
+            st += n_stages(cur.init[p] + cur.rem[p].cnt + cur.add[p].cnt);
+          } else {
+            pr.list(ft, a.idx, cur.add[p], head.add[p], st);
+            st += n_stages(cur.add[p].cnt);
           }
-          pr.list(ft, a.idx, cur.add[p], head.add[p], st);
-          st += n_stages(cur.add[p].cnt);
         }
       }
       st_base += batch_stages;
@@ -432,10 +500,11 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
     for (int p = 0; p < 2; ++p) {
       uint4 v = bias;
       if (kUpdate) {
-        st = consume_list<0>(sm, st, d.init[p], t, lane, a.status, v);
-        st = consume_list<2>(sm, st, d.rem[p].cnt, t, lane, a.status, v);
+        if (d.init[p]) v = make_uint4(0, 0, 0, 0);  // the parent row replaces the bias
+        st = consume_update(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, t, lane, a.status, v);
+      } else {
+        st = consume_list<1>(sm, st, d.add[p].cnt, t, lane, a.status, v);
       }
-      st = consume_list<1>(sm, st, d.add[p].cnt, t, lane, a.status, v);
       acc[p] = v;
     }
     if (kWriteAcc) {

@@ -49,6 +49,7 @@ SIGNATURES = {
                                c_size, P]),
     "cnnue_f_model_create": (c_int, [C.POINTER(FWeights), c_int, C.POINTER(c_void_p)]),
     "cnnue_f_model_destroy": (c_int, [c_void_p]),
+    "cnnue_f_workspace_bytes": (c_size, [c_i64]),
     "cnnue_f_forward": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, P]),
     "cnnue_feature_pool_fwd": (c_int, [P, P, c_i64, c_i64, c_i64, P, P, P]),
     "cnnue_feature_pool_bwd_workspace_bytes": (c_size, [c_i64, c_i64, c_i64]),

@@ -1,13 +1,22 @@
 // f_forward.cu - fp32 HalfKA NNUE evaluation on sm_100a.
 //
-// Same shape as the quantised evaluator: one group of 128 threads per
-// position, warps 0-1 on perspective 0 and 2-3 on perspective 1; thread c of a
-// perspective owns FT columns [4c, 4c+4) (one 16-byte load per 1 KB row).
-// Each column is summed bias-first in index order with plain fp32 adds, which
-// is the order of the scalar evaluator, so the FT output is bit-identical to
-// it; the stack's dot products use a fixed warp-tree order instead.
-// Positions are walked in bucket order so the bucket's 16x512 L1 weights stay
-// in registers (16 float4 per thread).
+// Three launches per batch:
+//   1. the offsets check (monotone, within the index array);
+//   2. f_gather_kernel: one warp per (position, perspective) list, lane l
+//      owning FT columns [8l, 8l + 8) (two 16-byte loads per 1 KB row, rows
+//      eight at a time in flight).  Each column is summed bias-first in
+//      index order with plain fp32 adds - the order of the scalar evaluator -
+//      so the FT output is bit-identical to it; the clipped values go to the
+//      workspace as x [n][512] (perspective 0, then 1);
+//   3. f_stack_kernel: CTA (bucket b, part j) keeps bucket b's 16x512 L1
+//      weights in shared memory and evaluates the positions of bucket b
+//      (bucket = min((max(n0, 1) - 1) >> 2, 7) from the perspective-0 count)
+//      in its contiguous share (offsets read 32 positions at a time, the
+//      bucket's positions picked by ballot), one warp per position: L1 by lanes over the 512
+//      inputs and a 16-way warp reduce-scatter, L2 by lanes over its 32
+//      outputs, L3 by a warp sum (a fixed order, within 1e-4 of the scalar
+//      one).  No bucket sort: every part of every bucket scans the batch's
+//      offsets (4 bytes x 2 per position).
 #include <algorithm>
 
 #include "common.cuh"
@@ -20,11 +29,10 @@ constexpr int kCols = CNNUE_F_COLS;
 constexpr int kRowBytes = kCols * 4;
 constexpr int kNB = CNNUE_F_BUCKETS;
 constexpr int kIn = 2 * kCols;
-constexpr int kGroup = 128;
-constexpr int kGroupsPerCta = 2;
-constexpr int kCta = kGroup * kGroupsPerCta;
 constexpr int kUnroll = 8;
+constexpr int kWarps = 8;  // warps per CTA in both kernels
 constexpr unsigned kFull = 0xffffffffu;
+static_assert(kCols == 256 && kIn == 512, "lane mapping assumes 256 columns per perspective");
 
 struct DevWeights {
   const float* ft;
@@ -42,10 +50,9 @@ struct Args {
   const uint16_t* idx;
   uint32_t n_idx;
   const uint32_t* offsets;
+  float* x;  // [n][512] clipped FT outputs (workspace)
   float* out;
   int64_t n;
-  const uint32_t* perm;
-  const uint8_t* sorted_bucket;
   uint32_t* status;
 };
 
@@ -57,79 +64,96 @@ __device__ __forceinline__ void add4(float4& a, const float4& b) {
 }
 
 __device__ __forceinline__ float clamp01(float v) { return fminf(fmaxf(v, 0.f), 1.f); }
+__device__ __forceinline__ float4 clamp01(float4 v) {
+  return make_float4(clamp01(v.x), clamp01(v.y), clamp01(v.z), clamp01(v.w));
+}
 
-__global__ void __launch_bounds__(kCta, 2) f_eval_kernel(const Args a) {
-  __shared__ float red[kGroupsPerCta][2][4][16];
-  __shared__ __align__(16) float h1s[kGroupsPerCta][16];
-
-  const int g = threadIdx.x / kGroup;
-  const int t = threadIdx.x % kGroup;
-  const int warp = t >> 5, lane = t & 31;
-  const int persp = t >> 6;
-  const int c = t & 63;
-
-  const int64_t n_groups = (int64_t)gridDim.x * kGroupsPerCta;
-  const int64_t gid = (int64_t)blockIdx.x * kGroupsPerCta + g;
-  const int64_t begin = a.n * gid / n_groups;
-  const int64_t end = a.n * (gid + 1) / n_groups;
-
-  const char* ftc = (const char*)a.w.ft + c * 16;
-  const float4 bias = __ldg((const float4*)(a.w.bias + 4 * c));
-
-  int cur_bucket = -1;
-  float4 w1[16];
-  float4 w2[4];
-  float b1v = 0.f, b2v = 0.f, w3v = 0.f, b3v = 0.f;
-  int parity = 0;
-
-  for (int64_t i = begin; i < end; ++i) {
-    const uint32_t pos = a.perm[i];
-    const int bucket = a.sorted_bucket[i];
-    if (bucket != cur_bucket) {
-      cur_bucket = bucket;
-      const float* w1p = a.w.l1w + (size_t)bucket * 16 * kIn + persp * kCols + 4 * c;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) w1[k] = __ldg((const float4*)(w1p + (size_t)k * kIn));
-      const float* w2p = a.w.l2w + ((size_t)bucket * 32 + lane) * 16;
-#pragma unroll
-      for (int q = 0; q < 4; ++q) w2[q] = __ldg((const float4*)(w2p + 4 * q));
-      b2v = __ldg(a.w.l2b + bucket * 32 + lane);
-      w3v = __ldg(a.w.l3w + bucket * 32 + lane);
-      b1v = lane < 16 ? __ldg(a.w.l1b + bucket * 16 + lane) : 0.f;
-      b3v = __ldg(a.w.l3b + bucket);
-    }
-
-    const int64_t ps = 2 * (int64_t)pos + persp;
-    float4 acc = bias;
-    const uint32_t ob = min(a.offsets[ps], a.n_idx);
-    const uint32_t oe = min(max(a.offsets[ps + 1], ob), a.n_idx);
+__global__ void __launch_bounds__(kWarps * 32) f_gather_kernel(const Args a) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * kWarps;
+  const char* ft = (const char*)a.w.ft + lane * 32;
+  const float4 bias0 = __ldg((const float4*)(a.w.bias + 8 * lane));
+  const float4 bias1 = __ldg((const float4*)(a.w.bias + 8 * lane + 4));
+  for (int64_t l = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); l < 2 * a.n; l += warps) {
+    const uint32_t ob = min(a.offsets[l], a.n_idx);
+    const uint32_t oe = min(max(a.offsets[l + 1], ob), a.n_idx);
+    float4 acc0 = bias0, acc1 = bias1;
     for (uint32_t base = ob; base < oe; base += 32) {
       const int cnt = (int)min(32u, oe - base);
       uint32_t my = lane < cnt ? (uint32_t)a.idx[base + lane] : 0u;
       const bool bad = lane < cnt && my >= (uint32_t)kF;
-      if (__any_sync(kFull, bad)) {
-        if (bad) atomicOr(a.status, CNNUE_STATUS_BAD_INDEX);
+      if (bad) {
+        atomicOr(a.status, CNNUE_STATUS_BAD_INDEX);
+        my = 0xffffffffu;
       }
-      if (bad) my = 0xffffffffu;
       for (int r0 = 0; r0 < cnt; r0 += kUnroll) {
-        float4 v[kUnroll];
+        float4 v0[kUnroll], v1[kUnroll];
         bool ok[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const uint32_t f = __shfl_sync(kFull, my, r0 + u);
+          const uint32_t f = __shfl_sync(kFull, my, (r0 + u) & 31);
           ok[u] = r0 + u < cnt && f != 0xffffffffu;
-          if (ok[u]) v[u] = ldg_stream16f(ftc + (size_t)f * kRowBytes);
+          if (ok[u]) {
+            v0[u] = ldg_stream16f(ft + (size_t)f * kRowBytes);
+            v1[u] = ldg_stream16f(ft + (size_t)f * kRowBytes + 16);
+          }
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u)
-          if (ok[u]) add4(acc, v[u]);
+          if (ok[u]) {
+            add4(acc0, v0[u]);
+            add4(acc1, v1[u]);
+          }
       }
     }
+    float* xo = a.x + (l >> 1) * kIn + (l & 1) * kCols + 8 * lane;
+    *(float4*)xo = clamp01(acc0);
+    *(float4*)(xo + 4) = clamp01(acc1);
+  }
+}
 
-    const float x0 = clamp01(acc.x), x1 = clamp01(acc.y), x2 = clamp01(acc.z), x3 = clamp01(acc.w);
+__global__ void __launch_bounds__(kWarps * 32) f_stack_kernel(const Args a) {
+  __shared__ __align__(16) float w1s[16 * kIn];  // this CTA's bucket: 32 KB
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x % kNB;
+  const int part = blockIdx.x / kNB, parts = gridDim.x / kNB;
+  const float4* w1g = (const float4*)(a.w.l1w + (size_t)b * 16 * kIn);
+  for (int i = threadIdx.x; i < 16 * kIn / 4; i += kWarps * 32) ((float4*)w1s)[i] = __ldg(w1g + i);
+  const float b1v = __ldg(a.w.l1b + b * 16 + (lane >> 1));
+  float4 w2[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) w2[q] = __ldg((const float4*)(a.w.l2w + ((size_t)b * 32 + lane) * 16) + q);
+  const float b2v = __ldg(a.w.l2b + b * 32 + lane), w3v = __ldg(a.w.l3w + b * 32 + lane), b3v = __ldg(a.w.l3b + b);
+  __syncthreads();
+  // this warp's contiguous share of the batch, scanned 32 positions at a time
+  const int64_t wid = (int64_t)part * kWarps + warp, nw = (int64_t)parts * kWarps;
+  const int64_t p_begin = a.n * wid / nw, p_end = a.n * (wid + 1) / nw;
+  for (int64_t c0 = p_begin; c0 < p_end; c0 += 32) {
+    const int64_t q = c0 + lane;
+    bool mine = false;
+    if (q < p_end) {
+      const uint32_t ob = min(a.offsets[2 * q], a.n_idx);
+      const uint32_t oe = min(max(a.offsets[2 * q + 1], ob), a.n_idx);
+      mine = (int)min((max(oe - ob, 1u) - 1u) >> 2, (uint32_t)(kNB - 1)) == b;
+    }
+    uint32_t todo = __ballot_sync(kFull, mine);
+    while (todo) {
+      const int src = __ffs(todo) - 1;
+      todo &= todo - 1;
+      const int64_t p = c0 + src;
+    const float* xp = a.x + p * kIn;
+    float xv[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) xv[i] = xp[lane + 32 * i];
     float v[16];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) v[k] = w1[k].x * x0 + w1[k].y * x1 + w1[k].z * x2 + w1[k].w * x3;
+    for (int o = 0; o < 16; ++o) {
+      float sacc = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) sacc += w1s[o * kIn + lane + 32 * i] * xv[i];
+      v[o] = sacc;
+    }
+    // 16 outputs reduced over the 32 lanes: output o ends on lanes 2o, 2o+1
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const bool up = lane & 16;
@@ -158,29 +182,18 @@ __global__ void __launch_bounds__(kCta, 2) f_eval_kernel(const Args a) {
       v[0] = keep + __shfl_xor_sync(kFull, send, 2);
     }
     v[0] += __shfl_xor_sync(kFull, v[0], 1);
-    if ((lane & 1) == 0) red[g][parity][warp][lane >> 1] = v[0];
-    named_bar_sync(1 + g, kGroup);
-
-    if (warp == 0) {
-      if (lane < 16) {
-        const float s = b1v + red[g][parity][0][lane] + red[g][parity][1][lane] +
-                        red[g][parity][2][lane] + red[g][parity][3][lane];
-        h1s[g][lane] = clamp01(s);
-      }
-      __syncwarp();
-      float s2 = b2v;
+    const float y1 = clamp01(b1v + v[0]);  // output lane >> 1 (both lanes of the pair)
+    float s2 = b2v;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 h = *(const float4*)&h1s[g][4 * q];
-        s2 += w2[q].x * h.x + w2[q].y * h.y + w2[q].z * h.z + w2[q].w * h.w;
-      }
-      float s3 = w3v * clamp01(s2);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) s3 += __shfl_xor_sync(kFull, s3, o);
-      if (lane == 0) a.out[pos] = b3v + s3;
-      __syncwarp();
+    for (int q = 0; q < 4; ++q) {
+      s2 += w2[q].x * __shfl_sync(kFull, y1, 8 * q) + w2[q].y * __shfl_sync(kFull, y1, 8 * q + 2) +
+            w2[q].z * __shfl_sync(kFull, y1, 8 * q + 4) + w2[q].w * __shfl_sync(kFull, y1, 8 * q + 6);
     }
-    parity ^= 1;
+    float s3 = w3v * clamp01(s2);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s3 += __shfl_xor_sync(kFull, s3, o);
+    if (lane == 0) a.out[p] = b3v + s3;
+    }
   }
 }
 
@@ -194,7 +207,7 @@ struct cnnue_f_model {
   int device = 0;
   DevWeights w{};
   void* blob = nullptr;
-  int grid = 0;
+  int sms = 148;
 };
 
 extern "C" {
@@ -239,10 +252,7 @@ int cnnue_f_model_create(const cnnue_f_weights* w, int device, cnnue_f_model** o
   const float** dst[8] = {&m->w.ft, &m->w.bias, &m->w.l1w, &m->w.l1b,
                           &m->w.l2w, &m->w.l2b, &m->w.l3w, &m->w.l3b};
   for (int i = 0; i < 8; ++i) *dst[i] = (const float*)((char*)m->blob + offs[i]);
-  int sms = 0, occ = 0;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, f_eval_kernel, kCta, 0);
-  m->grid = sms * std::max(occ, 1);
+  cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, device);
   *out = m;
   return CNNUE_OK;
 }
@@ -255,6 +265,10 @@ int cnnue_f_model_destroy(cnnue_f_model* m) {
   return CNNUE_OK;
 }
 
+size_t cnnue_f_workspace_bytes(int64_t n_positions) {
+  return sizeof(WorkspaceHeader) + align_up((size_t)std::max<int64_t>(n_positions, 1) * kIn * 4, 256);
+}
+
 int cnnue_f_forward(const cnnue_f_model* m, const uint16_t* d_idx, uint32_t n_idx,
                     const uint32_t* d_offsets, int64_t n, float* d_out, void* ws, size_t ws_bytes,
                     void* stream) {
@@ -263,27 +277,33 @@ int cnnue_f_forward(const cnnue_f_model* m, const uint16_t* d_idx, uint32_t n_id
   if (n == 0) return CNNUE_OK;
   if (!d_offsets || !d_out || (n_idx && !d_idx) || !ws)
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer");
-  if (ws_bytes < bucket_workspace_bytes(n))
-    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu < %zu", ws_bytes, bucket_workspace_bytes(n));
+  if (ws_bytes < cnnue_f_workspace_bytes(n))
+    return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu < %zu", ws_bytes, cnnue_f_workspace_bytes(n));
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
-  int st = launch_bucket_sort(d_offsets, n_idx, nullptr, n, 2, kNB, ws, s);
+  CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
+  int st = launch_offsets_check(d_offsets, n_idx, 2 * n, ws, s);
   if (st) return st;
-  WorkspaceView v = carve_workspace(ws, n);
   Args a{};
   a.w = m->w;
   a.idx = d_idx;
   a.n_idx = n_idx;
   a.offsets = d_offsets;
+  a.x = (float*)((char*)ws + sizeof(WorkspaceHeader));
   a.out = d_out;
   a.n = n;
-  a.perm = v.perm;
-  a.sorted_bucket = v.sorted_bucket;
-  a.status = &v.hdr->status;
-  const int grid = (int)std::min<int64_t>(m->grid, (n + kGroupsPerCta - 1) / kGroupsPerCta);
-  f_eval_kernel<<<grid, kCta, 0, s>>>(a);
-  return check_launch_error("f_eval_kernel");
+  a.status = &((WorkspaceHeader*)ws)->status;
+  const int64_t lists = 2 * n;
+  const unsigned g1 = (unsigned)std::max<int64_t>(1, std::min<int64_t>((lists + kWarps - 1) / kWarps,
+                                                                        (int64_t)m->sms * 16));
+  f_gather_kernel<<<g1, kWarps * 32, 0, s>>>(a);
+  if (int e = check_launch_error("f_gather_kernel")) return e;
+  // parts per bucket: about 4 positions per warp, at most 4 CTAs per SM overall
+  const int64_t parts = std::max<int64_t>(1, std::min<int64_t>((n + kNB * kWarps * 4 - 1) / (kNB * kWarps * 4),
+                                                              (int64_t)m->sms * 4 / kNB));
+  f_stack_kernel<<<(unsigned)(kNB * parts), kWarps * 32, 0, s>>>(a);
+  return check_launch_error("f_stack_kernel");
 }
 
 }  // extern "C"

@@ -43,7 +43,7 @@ class FloatNnue:
                 out: Optional[torch.Tensor] = None, stream=None, check_status: bool = True) -> torch.Tensor:
         if out is None:
             out = torch.empty(n_positions, dtype=torch.float32, device=self.device)
-        need = int(lib().cnnue_q_workspace_bytes(n_positions))
+        need = int(lib().cnnue_f_workspace_bytes(n_positions))
         if self._ws is None or self._ws.numel() < need:
             self._ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         ws = self._ws

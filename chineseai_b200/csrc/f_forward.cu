@@ -1,14 +1,15 @@
 // f_forward.cu - fp32 HalfKA NNUE evaluation on sm_100a.
 //
-// Three launches per batch:
-//   1. the offsets check (monotone, within the index array);
-//   2. f_gather_kernel: one warp per (position, perspective) list, lane l
-//      owning FT columns [8l, 8l + 8) (two 16-byte loads per 1 KB row, rows
-//      eight at a time in flight).  Each column is summed bias-first in
+// Two launches per batch (after the status word is cleared):
+//   1. f_gather_kernel (which also checks every list's offsets: monotone,
+//      within the index array): one warp per (position, perspective) list, lane l
+//      owning FT columns [4l, 4l + 4) and [128 + 4l, 128 + 4l + 4) (two
+//      16-byte loads per 1 KB row, each load instruction covering 512
+//      contiguous bytes, rows eight at a time in flight).  Each column is summed bias-first in
 //      index order with plain fp32 adds - the order of the scalar evaluator -
 //      so the FT output is bit-identical to it; the clipped values go to the
 //      workspace as x [n][512] (perspective 0, then 1);
-//   3. f_stack_kernel: CTA (bucket b, part j) keeps bucket b's 16x512 L1
+//   2. f_stack_kernel: CTA (bucket b, part j) keeps bucket b's 16x512 L1
 //      weights in shared memory and evaluates the positions of bucket b
 //      (bucket = min((max(n0, 1) - 1) >> 2, 7) from the perspective-0 count)
 //      in its contiguous share (offsets read 32 positions at a time, the
@@ -71,12 +72,14 @@ __device__ __forceinline__ float4 clamp01(float4 v) {
 __global__ void __launch_bounds__(kWarps * 32) f_gather_kernel(const Args a) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * kWarps;
-  const char* ft = (const char*)a.w.ft + lane * 32;
-  const float4 bias0 = __ldg((const float4*)(a.w.bias + 8 * lane));
-  const float4 bias1 = __ldg((const float4*)(a.w.bias + 8 * lane + 4));
+  const char* ft = (const char*)a.w.ft + lane * 16;
+  const float4 bias0 = __ldg((const float4*)(a.w.bias + 4 * lane));
+  const float4 bias1 = __ldg((const float4*)(a.w.bias + 128 + 4 * lane));
   for (int64_t l = (int64_t)blockIdx.x * kWarps + (threadIdx.x >> 5); l < 2 * a.n; l += warps) {
-    const uint32_t ob = min(a.offsets[l], a.n_idx);
-    const uint32_t oe = min(max(a.offsets[l + 1], ob), a.n_idx);
+    const uint32_t o0 = a.offsets[l], o1 = a.offsets[l + 1];
+    if (lane == 0 && !(o0 <= o1 && o1 <= a.n_idx)) atomicOr(a.status, CNNUE_STATUS_BAD_OFFSETS);
+    const uint32_t ob = min(o0, a.n_idx);
+    const uint32_t oe = min(max(o1, ob), a.n_idx);
     float4 acc0 = bias0, acc1 = bias1;
     for (uint32_t base = ob; base < oe; base += 32) {
       const int cnt = (int)min(32u, oe - base);
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(kWarps * 32) f_gather_kernel(const Args a) {
           ok[u] = r0 + u < cnt && f != 0xffffffffu;
           if (ok[u]) {
             v0[u] = ldg_stream16f(ft + (size_t)f * kRowBytes);
-            v1[u] = ldg_stream16f(ft + (size_t)f * kRowBytes + 16);
+            v1[u] = ldg_stream16f(ft + (size_t)f * kRowBytes + 512);
           }
         }
 #pragma unroll
@@ -106,9 +109,9 @@ __global__ void __launch_bounds__(kWarps * 32) f_gather_kernel(const Args a) {
           }
       }
     }
-    float* xo = a.x + (l >> 1) * kIn + (l & 1) * kCols + 8 * lane;
+    float* xo = a.x + (l >> 1) * kIn + (l & 1) * kCols + 4 * lane;
     *(float4*)xo = clamp01(acc0);
-    *(float4*)(xo + 4) = clamp01(acc1);
+    *(float4*)(xo + 128) = clamp01(acc1);
   }
 }
 
@@ -283,8 +286,6 @@ int cnnue_f_forward(const cnnue_f_model* m, const uint16_t* d_idx, uint32_t n_id
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
   CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
-  int st = launch_offsets_check(d_offsets, n_idx, 2 * n, ws, s);
-  if (st) return st;
   Args a{};
   a.w = m->w;
   a.idx = d_idx;

@@ -48,3 +48,12 @@ def test_all_buckets(fmodel, fweights):
     out = fmodel.forward_positions(pos)
     st, ref, _ = oracle.f_forward(fweights, pos)
     np.testing.assert_allclose(out, ref, rtol=RTOL, atol=ATOL)
+
+
+def test_bad_offsets_and_indices_are_reported(fmodel):
+    from chineseai_b200._lib import CnnueError
+    idx = np.array([5, 7, 11339, 3], np.uint16)
+    with pytest.raises(CnnueError):  # a list that ends before it starts
+        fmodel.forward_positions(synth.Positions(idx, np.array([0, 3, 2, 4], np.uint32)[:3].copy()))
+    with pytest.raises(CnnueError):  # a feature past 11340
+        fmodel.forward_positions(synth.Positions(np.array([5, 11340], np.uint16), np.array([0, 1, 2], np.uint32)))

@@ -73,6 +73,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Teardown form of mbar_wait: ignores the abort word (it is used after an
+// abort, to let copies or MMAs already in flight land before the CTA ends),
+// still gives up after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, uint32_t* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(status, CNNUE_STATUS_TIMEOUT);
+      return false;
+    }
+  }
+  return true;
+}
+
 // Orders this thread's earlier shared-memory accesses (and what it observed)
 // before its later async-proxy operations on shared memory (bulk copies).
 __device__ __forceinline__ void fence_proxy_async_smem() {

@@ -3,9 +3,12 @@
 //
 // Trunk: 21 3x3 convolutions (stem 15->128, 10 residual blocks of two
 // 128->128), each an implicit GEMM on the 5th-generation tensor cores:
-// rows = board squares of the batch (M = 90 B), columns = 128 output
-// channels, K = 9 taps x input channels.  Activations are bf16, square-major
-// ([B*90][C], channels contiguous); the stem input is packed to 64 channels.
+// rows = board squares of the batch, columns = 128 output channels, K = 9
+// taps x input channels.  Activations are bf16 with channels contiguous; the
+// stem input is packed to 64 channels.  Three conv kernels compute the same
+// convolution (cnnue_rn_set_conv_kernel): the default rn_hconv_kernel on a
+// padded, 8-board-interleaved row layout (described at its definition), and
+// two on the square-major layout ([B*90][C]) described here.
 //
 // rn_conv_kernel, one CTA per 128 x 128 output tile, 6 warps:
 //   warp 4     allocates the 128 TMEM columns of the fp32 accumulator and
@@ -119,7 +122,7 @@ __global__ void __launch_bounds__(kConvThreads) rn_conv_kernel(const __grid_cons
     for (int kb = 0; kb < kKb; ++kb) {
       const int s = kb % kStages, u = kb / kStages;
       if (!pipe::mbar_wait(&sm.loaded[s], u & 1, &sm.abort, status)) break;
-      const int tap = kb / kKbPerTap;
+      const int tap = kb % 9;
       const int r2 = r + tap / 3 - 1, f2 = f + tap % 3 - 1;
       if (m < M && (r2 < 0 || r2 > 9 || f2 < 0 || f2 > 8)) {
         uint8_t* line = sm.a[s] + row * 128;
@@ -182,7 +185,7 @@ __global__ void __launch_bounds__(kConvThreads) rn_conv_kernel(const __grid_cons
       for (int kb = 0; kb < kKb; ++kb) {
         const int s = kb % kStages, u = kb / kStages;
         if (u > 0 && !pipe::mbar_wait(&sm.empty[s], (u - 1) & 1, &sm.abort, status)) break;
-        const int tap = kb / kKbPerTap, c0 = (kb % kKbPerTap) * 64;
+        const int tap = kb % 9, c0 = (kb / 9) * 64;
         const int shift = (tap / 3 - 1) * 9 + (tap % 3 - 1);
         pipe::mbar_arrive_expect_tx(&sm.loaded[s], 2 * kTileBytes);
         tc::tma_load_2d(pipe::smem_addr(sm.a[s]), &tmap_in, c0, m0 + shift, pipe::smem_addr(&sm.loaded[s]));
@@ -287,7 +290,7 @@ __global__ void __launch_bounds__(kPThreads, 1) rn_pconv_kernel(const __grid_con
         for (int kb = 0; kb < kKb; ++kb, ++g) {
           const uint32_t s = g % kPStages, u = g / kPStages;
           if (u > 0 && !pipe::mbar_wait(&sm.empty[s], (u - 1) & 1, &sm.abort, status)) goto done_load;
-          const int tap = kb / kKbPerTap, c0 = (kb % kKbPerTap) * 64;
+          const int tap = kb % 9, c0 = (kb / 9) * 64;
           const int shift = (tap / 3 - 1) * 9 + (tap % 3 - 1);
           pipe::mbar_arrive_expect_tx(&sm.loaded[s], 3 * kTileBytes);
           tc::tma_load_2d(pipe::smem_addr(sm.a[s][0]), &tmap_in, c0, m0 + shift, pipe::smem_addr(&sm.loaded[s]));
@@ -366,7 +369,7 @@ __global__ void __launch_bounds__(kPThreads, 1) rn_pconv_kernel(const __grid_con
           ok = false;
           break;
         }
-        const int tap = kb / kKbPerTap;
+        const int tap = kb % 9;
         const int dr = tap / 3 - 1, df = tap % 3 - 1;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -437,6 +440,344 @@ __global__ void __launch_bounds__(kPThreads, 1) rn_pconv_kernel(const __grid_con
   if (warp == 1) tc::tmem_dealloc(tmem, 512);
 }
 
+// ---- halo variant: padded, 8-board-interleaved activations ----------------
+// Layout: boards are taken in groups of 8; a group holds 11 padded ranks
+// (rank 0 all zeros, ranks 1..10 the board's ranks 0..9) of 10 padded files
+// (files 0..8, file 9 all zeros), and each (rank, file) cell holds the 8
+// boards' rows:  row = ((group * 11 + rank + 1) * 10 + file) * 8 + board % 8.
+// A 3x3 tap (dr, df) is then the constant row shift (10 dr + df) * 8 for
+// every square of every board, and every neighbour off the board lands on a
+// zero row (the zero file or zero rank of this group, or of the neighbouring
+// group, or outside the buffer, which TMA fills with zeros).  The shifts are
+// multiples of 8 rows, i.e. of the 1024-byte 128B-swizzle atom, so one halo
+// tile of rows m0 - 88 .. m0 + 343 (432 rows, 64 channels, 54 KB) serves all
+// nine taps of a 256-row pair as descriptor offsets: no per-tap A loads and
+// no edge fix-up.  The cost is 880 rows per 8 boards instead of 720 (22 %
+// more MMA rows); the epilogue writes zeros to the padding rows, so each
+// conv's output is again a valid padded input.
+//
+// The MMA is the transposed product D[channel][row] = W[channel][k] .
+// X[row][k]: A = a 128-channel weight tile, B = the pair's 256 activation
+// rows, one M128 N256 K16 instruction per K step (128 tensor cycles; half
+// the instructions, and a third less shared-memory operand traffic, than two
+// M128 N128 ones with the activations as A).
+//
+// rn_hconv_kernel, one CTA per SM, loops over 256-row pairs.  K blocks run
+// channel-half major (9 taps of channels 0-63, then of 64-127): a halo tile
+// per channel half, double-buffered, so the next pair's first half loads
+// while this pair's second half runs.  Weights stream through a 6-stage ring
+// of 16 KB tiles.  Warps: 0 loader; 1 MMA issuer and TMEM owner (512
+// columns: two pairs' accumulators of 256 rows); 2-9 epilogue (TMEM lane
+// quadrant w % 4 is the channel block, warps 2-5 take rows 0-127 of the pair
+// and 6-9 rows 128-255).  The issuing thread is the critical path -- an
+// mbarrier wait costs it 100-250 cycles while the tensor core streams
+// operands, against 512 tensor cycles per weight tile -- so its tap loop is
+// unrolled into constant descriptor offsets with no per-block division.
+// The epilogue turns each 32 x 32 (channel x row) accumulator block into
+// row-major bf16 with a register transpose (butterfly shuffles), so its
+// global loads and stores are 16-byte accesses covering 8 rows x 64 bytes
+// per warp instruction.  Consecutive convs are programmatic dependent
+// launches.  Bounded waits throughout; after an abort the loader waits for
+// its copies in flight and the issuer for its MMAs before the CTA ends.
+constexpr int kPitchF = 10;                           // padded files per rank
+constexpr int kPitchR = 11;                           // padded ranks per group
+constexpr int kGroupBoards = 8;                       // boards interleaved per group
+constexpr int kGroupRows = kPitchF * kPitchR * kGroupBoards;  // 880
+constexpr int kHalo = (kPitchF + 1) * kGroupBoards;   // 88: the largest tap shift
+constexpr int kPairRows = 2 * kTileM;                 // 256: the MMA's N
+constexpr int kHaloRows = kPairRows + 2 * kHalo;      // 432
+constexpr int kHaloBox = kHaloRows / 2;               // 216 rows per TMA box (<= 256)
+constexpr int kHaloBytes = kHaloRows * 128;           // 55,296 (54 x 1024)
+constexpr int kWStages = 6;                           // weight stages of one K block (16 KB)
+constexpr int kEpiWarps = 8;                          // epilogue warps (4 or 8: a multiple of the 4 lane quadrants)
+constexpr int kEpiChunks = kPairRows / 32 / (kEpiWarps / 4);  // 32-row chunks per epilogue warp and pair
+constexpr int kHThreads = 64 + 32 * kEpiWarps;
+static_assert(kHaloBox % 8 == 0 && kHaloBytes % 1024 == 0, "halo boxes keep the swizzle atom");
+
+__host__ __device__ inline int64_t padded_row(int64_t board, int square) {
+  return (((board >> 3) * kPitchR + square / 9 + 1) * kPitchF + square % 9) * kGroupBoards + (board & 7);
+}
+inline int64_t padded_rows(int64_t batch) { return (batch + kGroupBoards - 1) / kGroupBoards * kGroupRows; }
+
+struct HConvSmem {
+  alignas(1024) uint8_t halo[2][kHaloBytes];
+  alignas(1024) uint8_t w[kWStages][kTileBytes];
+  uint64_t w_full[kWStages];
+  uint64_t w_empty[kWStages];
+  uint64_t halo_full[2];
+  uint64_t halo_empty[2];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// One butterfly stage of a 32 x 32 register transpose across a warp: lanes
+// l and l ^ K swap the halves of their register pairs (i, i + K) that the
+// other side needs.  After the stages K = 16, 8, 4, 2, 1, lane l holds in
+// v[i] what lane i held in v[l].
+template <int K>
+__device__ __forceinline__ void transpose32(float (&v)[32], int lane) {
+  const bool upper = (lane & K) != 0;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    if (i & K) continue;
+    const float recv = __shfl_xor_sync(0xffffffffu, upper ? v[i] : v[i + K], K);
+    v[i] = upper ? recv : v[i];
+    v[i + K] = upper ? v[i + K] : recv;
+  }
+}
+
+template <int CIN>
+__global__ void __launch_bounds__(kHThreads, 1) rn_hconv_kernel(const __grid_constant__ CUtensorMap tmap_in,
+                                                               const uint8_t* __restrict__ wtiles,
+                                                               const float* __restrict__ bias,
+                                                               const __nv_bfloat16* __restrict__ resid,
+                                                               __nv_bfloat16* __restrict__ out, int M,
+                                                               uint32_t* status) {
+  constexpr int kKh = CIN / 64;  // channel halves
+  extern __shared__ uint8_t smem_raw[];
+  HConvSmem& sm = *reinterpret_cast<HConvSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_pairs = (M + kPairRows - 1) / kPairRows;
+
+  if (warp == 1) {
+    tc::tmem_alloc(pipe::smem_addr(&sm.tmem_base), 512);
+    tc::tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int s = 0; s < kWStages; ++s) {
+      pipe::mbar_init(&sm.w_full[s], 1);
+      pipe::mbar_init(&sm.w_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      pipe::mbar_init(&sm.halo_full[b], 1);
+      pipe::mbar_init(&sm.halo_empty[b], 1);
+      pipe::mbar_init(&sm.acc_full[b], 1);
+      pipe::mbar_init(&sm.acc_empty[b], 32 * kEpiWarps);
+    }
+    pipe::mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    pipe::mbar_init_fence();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  // Programmatic dependent launch: the next conv may be scheduled now (its
+  // CTAs take SMs as this grid's CTAs exit, and set up there); every thread
+  // waits here until the previous grid has completed and its writes are
+  // visible, before any activation is read or written.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+
+  if (warp == 0) {
+    // ---- loader: per pair and channel half, the halo (two TMA boxes), then
+    // the half's nine weight tiles.
+    if (lane == 0) {
+      uint32_t nw = 0, nh = 0;  // weight tiles / halos issued
+      uint32_t ws = 0, wphase = 0;
+      for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x) {
+        const int y0 = pair * kPairRows - kHalo;
+        for (int kh = 0; kh < kKh; ++kh) {
+          const uint32_t hb = nh & 1, hu = nh >> 1;
+          if (hu > 0 && !pipe::mbar_wait(&sm.halo_empty[hb], (hu - 1) & 1, &sm.abort, status)) goto done_load;
+          pipe::mbar_arrive_expect_tx(&sm.halo_full[hb], kHaloBytes);
+          tc::tma_load_2d(pipe::smem_addr(sm.halo[hb]), &tmap_in, kh * 64, y0, pipe::smem_addr(&sm.halo_full[hb]));
+          tc::tma_load_2d(pipe::smem_addr(sm.halo[hb]) + kHaloBox * 128, &tmap_in, kh * 64, y0 + kHaloBox,
+                          pipe::smem_addr(&sm.halo_full[hb]));
+          ++nh;
+          const uint8_t* src = wtiles + (size_t)kh * 9 * kTileBytes;
+          for (int tap = 0; tap < 9; ++tap, src += kTileBytes) {
+            if (nw >= kWStages && !pipe::mbar_wait(&sm.w_empty[ws], wphase ^ 1, &sm.abort, status)) goto done_load;
+            pipe::mbar_arrive_expect_tx(&sm.w_full[ws], kTileBytes);
+            pipe::bulk_copy_g2s(sm.w[ws], src, kTileBytes, &sm.w_full[ws]);
+            ++nw;
+            if (++ws == kWStages) {
+              ws = 0;
+              wphase ^= 1;
+            }
+          }
+        }
+      }
+    done_load:
+      if (sm.abort) {
+        // land every copy still in flight: the last use of each buffer
+        for (uint32_t i = nw > kWStages ? nw - kWStages : 0; i < nw; ++i)
+          pipe::mbar_wait_drain(&sm.w_full[i % kWStages], (i / kWStages) & 1, status);
+        for (uint32_t i = nh > 2 ? nh - 2 : 0; i < nh; ++i)
+          pipe::mbar_wait_drain(&sm.halo_full[i & 1], (i >> 1) & 1, status);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---- MMA issuer: per K step one M128 (channels) x N256 (rows) x K16.
+    // The issuing thread is the critical path (each barrier wait costs it a
+    // few hundred cycles while the tensor core streams operands), so the
+    // tap loop is unrolled: tap shifts are constant descriptor offsets and
+    // the stage index and phase advance without division.
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_bf16_f32(128, kPairRows);
+      const uint64_t wdesc0 = tc::smem_desc(pipe::smem_addr(sm.w[0]), 0, 1024, tc::kSwizzle128B);
+      uint32_t nh = 0, ws = 0, wphase = 0;
+      int it = 0;
+      bool ok = true;
+      for (int pair = blockIdx.x; pair < n_pairs && ok; pair += gridDim.x, ++it) {
+        const int buf = it & 1, use = it >> 1;
+        if (use > 0 && !pipe::mbar_wait(&sm.acc_empty[buf], (use - 1) & 1, &sm.abort, status)) break;
+        const uint32_t d = tmem + (uint32_t)(buf * kPairRows);
+        for (int kh = 0; kh < kKh && ok; ++kh) {
+          const uint32_t hb = nh & 1;
+          if (!pipe::mbar_wait(&sm.halo_full[hb], (nh >> 1) & 1, &sm.abort, status)) {
+            ok = false;
+            break;
+          }
+          ++nh;
+          // descriptor of the halo row m0 (tap shift 0); a shift of r rows is + 8 r
+          const uint64_t xdesc0 =
+              tc::smem_desc(pipe::smem_addr(sm.halo[hb]) + kHalo * 128, 0, 1024, tc::kSwizzle128B);
+#pragma unroll
+          for (int tap = 0; tap < 9; ++tap) {
+            if (!pipe::mbar_wait(&sm.w_full[ws], wphase, &sm.abort, status)) {
+              ok = false;
+              break;
+            }
+            tc::fence_after_sync();
+            const int shift = ((tap / 3 - 1) * kPitchF + (tap % 3 - 1)) * kGroupBoards;
+            const uint64_t ad = wdesc0 + (uint64_t)ws * (kTileBytes >> 4);
+            const uint64_t bd = xdesc0 + (uint64_t)(int64_t)(shift * 8);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)  // +32 bytes per K step: +2 in the descriptor's address field
+              tc::mma_bf16(d, ad + 2 * kk, bd + 2 * kk, idesc, (kh | tap | kk) != 0 ? 1u : 0u);
+            tc::commit(pipe::smem_addr(&sm.w_empty[ws]));
+            if (++ws == kWStages) {
+              ws = 0;
+              wphase ^= 1;
+            }
+          }
+          if (!ok) break;
+          tc::commit(pipe::smem_addr(&sm.halo_empty[hb]));
+        }
+        tc::commit(pipe::smem_addr(&sm.acc_full[buf]));
+      }
+      // every MMA issued has completed before TMEM is released
+      tc::commit(pipe::smem_addr(&sm.drain));
+      pipe::mbar_wait_drain(&sm.drain, 0, status);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: TMEM lane quadrant w % 4 is channels 32 (w % 4) .. + 31;
+    // warp w covers rows part * 32 kEpiChunks .. of the pair (part =
+    // (w - 2) / 4) in chunks of 32.  Per chunk a lane loads its channel's 32
+    // rows (+ bias); three butterfly stages and a lane rotation then leave
+    // lane l with rows 8t + l / 4 (t = 0..3), channels 8 (l % 4) .. + 7, so
+    // each warp-wide 16-byte access covers 8 rows x 64 contiguous bytes.  The
+    // 8 rows of one (rank, file) cell share real/padding: ReLU(acc + bias (+
+    // residual)) in bf16, or zeros.
+    const int q = warp & 3, part = (warp - 2) >> 2;
+    const float bc = __ldg(bias + 32 * q + lane);
+    const uint32_t lane_addr = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(part * 32 * kEpiChunks);
+    const int rsub = lane >> 2, csub = 32 * q + 8 * (lane & 3);
+    const int rot_src = ((lane & 3) << 3) | (lane >> 2);
+    int it = 0;
+    for (int pair = blockIdx.x; pair < n_pairs; pair += gridDim.x, ++it) {
+      const int buf = it & 1, use = it >> 1;
+      const int m0 = pair * kPairRows + part * 32 * kEpiChunks;
+      bool ok = true;
+#pragma unroll 1
+      for (int cg = 0; cg < kEpiChunks; cg += 4) {
+        // real cells and residual rows of four chunks first: the loads
+        // overlap the accumulator wait (and the previous chunks' work)
+        uint32_t real_bits = 0;
+        uint4 rv[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int cm = m0 + 32 * (cg + j) + 8 * t, cell = cm >> 3;  // the cell of rows cm .. cm + 7
+            const bool real = cm < M && (cell / kPitchF) % kPitchR >= 1 && cell % kPitchF < 9;
+            real_bits |= (uint32_t)real << (4 * j + t);
+            rv[j][t] = (resid != nullptr && real)
+                           ? __ldg(reinterpret_cast<const uint4*>(resid + (size_t)(cm + rsub) * kC + csub))
+                           : make_uint4(0u, 0u, 0u, 0u);
+          }
+        if (cg == 0) {
+          // warp-uniform, so that no lane skips the shuffles below
+          ok = __all_sync(0xffffffffu, pipe::mbar_wait(&sm.acc_full[buf], use & 1, &sm.abort, status));
+          tc::fence_after_sync();
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t v[32];
+          __syncwarp();
+          tc::tmem_ld32(lane_addr + (uint32_t)(buf * kPairRows + 32 * (cg + j)), v);
+          tc::wait_ld();
+          if (!ok) continue;
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) + bc;
+          transpose32<4>(f, lane);
+          transpose32<2>(f, lane);
+          transpose32<1>(f, lane);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = __shfl_sync(0xffffffffu, f[i], rot_src);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int cm = m0 + 32 * (cg + j) + 8 * t;
+            if (cm >= M) break;  // M is a multiple of 8: whole cells only
+            uint32_t packed[4] = {0u, 0u, 0u, 0u};
+            if ((real_bits >> (4 * j + t)) & 1u) {
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t rw = (&rv[j][t].x)[e];
+                const float2 r2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw));
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaxf(f[8 * t + 2 * e] + r2.x, 0.f),
+                                                                fmaxf(f[8 * t + 2 * e + 1] + r2.y, 0.f));
+                packed[e] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+            }
+            *reinterpret_cast<uint4*>(out + (size_t)(cm + rsub) * kC + csub) =
+                make_uint4(packed[0], packed[1], packed[2], packed[3]);
+          }
+        }
+      }
+      tc::fence_before_sync();
+      pipe::mbar_arrive(&sm.acc_empty[buf]);
+      if (!ok) break;
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 1) tc::tmem_dealloc(tmem, 512);
+}
+
+// [B][15][90] bf16 planes -> the padded layout above, [rows][64] bf16,
+// channels 15..63 zero, padding rows (and the boards past B in the last
+// group) all zero.  One thread per padded row.
+__global__ void rn_pack_padded_kernel(const __nv_bfloat16* __restrict__ planes, int64_t B, int64_t rows,
+                                      __nv_bfloat16* __restrict__ out) {
+  const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (m >= rows) return;
+  const int64_t cell = m >> 3;
+  const int file = (int)(cell % kPitchF), rank = (int)((cell / kPitchF) % kPitchR);
+  const int64_t b = (cell / (kPitchF * kPitchR)) * kGroupBoards + (m & 7);
+  uint32_t w[32];
+#pragma unroll
+  for (int k = 0; k < 32; ++k) w[k] = 0u;
+  if (rank >= 1 && file < 9 && b < B) {
+    const int p = (rank - 1) * 9 + file;
+#pragma unroll
+    for (int c = 0; c < CNNUE_RN_PLANES; ++c) {
+      const uint16_t v = reinterpret_cast<const uint16_t*>(planes)[(b * CNNUE_RN_PLANES + c) * kSq + p];
+      w[c >> 1] |= (uint32_t)v << (16 * (c & 1));
+    }
+  }
+  uint4* o = reinterpret_cast<uint4*>(out + m * 64);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+}
+
 // [B][15][90] bf16 planes -> [B*90][64] bf16, channels 15..63 zero.
 __global__ void rn_pack_kernel(const __nv_bfloat16* __restrict__ planes, int64_t B, __nv_bfloat16* __restrict__ out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -469,6 +810,7 @@ struct HeadArgs {
   const float* v2w;            // [256]
   const float* v2b;            // [1]
   int64_t B;
+  int padded;     // trunk in the padded 8-board layout (else [B*90][128])
   float* logits;  // [B][2086] or null
   float* probs;   // [B][2086]
   float* value;   // [B]
@@ -488,7 +830,8 @@ __global__ void __launch_bounds__(kHeadThreads) rn_head_prep_kernel(HeadArgs a, 
     const int64_t b = b0 + bl;
     float s0 = 0.f, s1 = 0.f, s2 = 0.f;
     if (b < a.B) {
-      const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(a.trunk + (size_t)(b * kSq + p) * kC);
+      const int64_t r = a.padded ? padded_row(b, p) : b * kSq + p;
+      const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(a.trunk + (size_t)r * kC);
 #pragma unroll 8
       for (int c2 = 0; c2 < kC / 2; ++c2) {
         const float2 x = __bfloat1622float2(row[c2]);
@@ -608,11 +951,12 @@ inline uint16_t to_bf16(float f) {
 }
 
 // One conv's weights (OIHW [128][cin][3][3]) as K-block tiles of the UMMA
-// layout: K index = tap * cin_pad + channel; channels >= cin are zero.
+// layout, channel-half major: K block kb covers tap kb % 9 and channels
+// 64 * (kb / 9) .. + 63; channels >= cin are zero.
 void tile_conv(const float* w, int cin, int cin_pad, uint8_t* dst) {
   const int kb_per_tap = cin_pad / 64;
   for (int kb = 0; kb < 9 * kb_per_tap; ++kb) {
-    const int tap = kb / kb_per_tap, c0 = (kb % kb_per_tap) * 64;
+    const int tap = kb % 9, c0 = (kb / 9) * 64;
     const int kh = tap / 3, kw = tap % 3;
     uint8_t* tile = dst + (size_t)kb * kTileBytes;
     for (int n = 0; n < kC; ++n)
@@ -627,6 +971,7 @@ void tile_conv(const float* w, int cin, int cin_pad, uint8_t* dst) {
 
 size_t conv_smem_bytes() { return sizeof(ConvSmem) + 1024; }
 size_t pconv_smem_bytes() { return sizeof(PConvSmem) + 1024; }
+size_t hconv_smem_bytes() { return sizeof(HConvSmem) + 1024; }
 
 // cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -642,14 +987,15 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map of an activation buffer [M][cin] bf16 read in boxes of 128 rows
-// x 64 channels with the 128-byte swizzle; rows outside [0, M) read zeros.
-int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M) {
+// Tensor map of an activation buffer [M][cin] bf16 read in boxes of
+// `box_rows` rows x 64 channels with the 128-byte swizzle; rows outside
+// [0, M) read zeros.
+int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M, int box_rows) {
   PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
   if (!fn) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)cin, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)cin * 2};
-  const cuuint32_t box[2] = {64, 128};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -665,7 +1011,7 @@ int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M) {
 struct cnnue_rn_model {
   int device = 0;
   int sms = 148;
-  int persistent = 1;  // 1: rn_pconv_kernel, 0: the one-tile-per-CTA rn_conv_kernel
+  int conv_kind = 2;  // 2: rn_hconv_kernel, 1: rn_pconv_kernel, 0: the one-tile-per-CTA rn_conv_kernel
   void* blob = nullptr;
   uint8_t* tiles = nullptr;  // [kTotalKb][16 KB]
   float* conv_bias = nullptr;  // [21][128]
@@ -679,7 +1025,8 @@ using namespace cnnue::rn;
 extern "C" {
 
 size_t cnnue_rn_workspace_bytes(int64_t batch) {
-  const size_t m = batch > 0 ? (size_t)batch * kSq : 0;
+  // rows of the padded layout (>= 90 per board, so either layout fits)
+  const size_t m = batch > 0 ? (size_t)padded_rows(batch) : 0;
   const size_t b = batch > 0 ? (size_t)batch : 0;
   return sizeof(WorkspaceHeader) + align_up(m * 64 * 2, 256) + 3 * align_up(m * kC * 2, 256) +
          align_up(b * 2 * kSq * 4, 256) + align_up(b * kMoves * 4, 256);
@@ -748,7 +1095,11 @@ int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model*
         (e = cudaFuncSetAttribute(rn_pconv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   (int)pconv_smem_bytes())) != cudaSuccess ||
         (e = cudaFuncSetAttribute(rn_pconv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  (int)pconv_smem_bytes())) != cudaSuccess)
+                                  (int)pconv_smem_bytes())) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(rn_hconv_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)hconv_smem_bytes())) != cudaSuccess ||
+        (e = cudaFuncSetAttribute(rn_hconv_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  (int)hconv_smem_bytes())) != cudaSuccess)
       st = cuda_error(e, "cudaFuncSetAttribute(rn_conv_kernel)");
     int sms = 0;
     if (!st && (e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess)
@@ -797,39 +1148,64 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   cudaStream_t s = (cudaStream_t)stream;
   CNNUE_CUDA_TRY(cudaMemsetAsync(ws, 0, sizeof(WorkspaceHeader), s));
   if (batch == 0) return CNNUE_OK;
-  const int M = (int)(batch * kSq);
+  const bool padded = m->conv_kind == 2;
+  const int M = (int)(padded ? padded_rows(batch) : batch * kSq);
   char* p = (char*)ws + sizeof(WorkspaceHeader);
+  const size_t rows_cap = (size_t)padded_rows(batch);
   auto* in64 = (__nv_bfloat16*)p;
-  p += align_up((size_t)M * 64 * 2, 256);
+  p += align_up(rows_cap * 64 * 2, 256);
   __nv_bfloat16* act[3];
   for (int i = 0; i < 3; ++i) {
     act[i] = (__nv_bfloat16*)p;
-    p += align_up((size_t)M * kC * 2, 256);
+    p += align_up(rows_cap * kC * 2, 256);
   }
   float* pc = (float*)p;
   p += align_up((size_t)batch * 2 * kSq * 4, 256);
   float* logits = d_logits ? d_logits : (float*)p;
   uint32_t* status = &((WorkspaceHeader*)ws)->status;
-  rn_pack_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, in64);
+  if (padded)
+    rn_pack_padded_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, M,
+                                                                      in64);
+  else
+    rn_pack_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, in64);
   if (int st = check_launch_error("rn_pack_kernel")) return st;
-  const unsigned tiles = (unsigned)((M + kTileM - 1) / kTileM);
-  const size_t smem = conv_smem_bytes();
+  const int box_rows = padded ? kHaloBox : kTileM;
   CUtensorMap map_in, map_act[3];
-  if (int st = make_act_map(&map_in, in64, 64, M)) return st;
+  if (int st = make_act_map(&map_in, in64, 64, M, box_rows)) return st;
   for (int i = 0; i < 3; ++i)
-    if (int st = make_act_map(&map_act[i], act[i], kC, M)) return st;
+    if (int st = make_act_map(&map_act[i], act[i], kC, M, box_rows)) return st;
+  const unsigned tiles = (unsigned)((M + kTileM - 1) / kTileM);
   const int pairs = (M + 2 * kTileM - 1) / (2 * kTileM);
   const unsigned pgrid = (unsigned)(pairs < m->sms ? pairs : m->sms);
-  const size_t psmem = pconv_smem_bytes();
   auto conv = [&](bool stem, const CUtensorMap& map, int c, const __nv_bfloat16* resid, __nv_bfloat16* dst) {
     const uint8_t* wt = m->tiles + conv_tile_offset(c) * kTileBytes;
     const float* b = m->conv_bias + c * kC;
-    if (m->persistent) {
-      if (stem) rn_pconv_kernel<64><<<pgrid, kPThreads, psmem, s>>>(map, wt, b, resid, dst, M, status);
-      else rn_pconv_kernel<128><<<pgrid, kPThreads, psmem, s>>>(map, wt, b, resid, dst, M, status);
-    } else {
-      if (stem) rn_conv_kernel<64><<<tiles, kConvThreads, smem, s>>>(map, wt, b, resid, dst, M, status);
-      else rn_conv_kernel<128><<<tiles, kConvThreads, smem, s>>>(map, wt, b, resid, dst, M, status);
+    switch (m->conv_kind) {
+      case 2: {
+        // launched as a programmatic dependent of the previous kernel in the
+        // stream: launch and set-up overlap that kernel's tail
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(pgrid);
+        cfg.blockDim = dim3(kHThreads);
+        cfg.dynamicSmemBytes = hconv_smem_bytes();
+        cfg.stream = s;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        cudaError_t e = stem ? cudaLaunchKernelEx(&cfg, rn_hconv_kernel<64>, map, wt, b, resid, dst, M, status)
+                             : cudaLaunchKernelEx(&cfg, rn_hconv_kernel<128>, map, wt, b, resid, dst, M, status);
+        if (e != cudaSuccess) return cuda_error(e, "cudaLaunchKernelEx(rn_hconv_kernel)");
+        break;
+      }
+      case 1:
+        if (stem) rn_pconv_kernel<64><<<pgrid, kPThreads, pconv_smem_bytes(), s>>>(map, wt, b, resid, dst, M, status);
+        else rn_pconv_kernel<128><<<pgrid, kPThreads, pconv_smem_bytes(), s>>>(map, wt, b, resid, dst, M, status);
+        break;
+      default:
+        if (stem) rn_conv_kernel<64><<<tiles, kConvThreads, conv_smem_bytes(), s>>>(map, wt, b, resid, dst, M, status);
+        else rn_conv_kernel<128><<<tiles, kConvThreads, conv_smem_bytes(), s>>>(map, wt, b, resid, dst, M, status);
     }
     return check_launch_error("rn conv");
   };
@@ -845,6 +1221,7 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   HeadArgs h = m->h;
   h.trunk = act[x];
   h.B = batch;
+  h.padded = padded ? 1 : 0;
   h.logits = logits;
   h.probs = d_probs;
   h.value = d_value;
@@ -857,9 +1234,9 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   return check_launch_error("rn_softmax_kernel");
 }
 
-int cnnue_rn_set_conv_kernel(cnnue_rn_model* m, int persistent) {
-  if (!m || (persistent != 0 && persistent != 1)) return set_error(CNNUE_ERR_INVALID_ARG, "model or kernel choice");
-  m->persistent = persistent;
+int cnnue_rn_set_conv_kernel(cnnue_rn_model* m, int kind) {
+  if (!m || kind < 0 || kind > 2) return set_error(CNNUE_ERR_INVALID_ARG, "model or conv kernel kind (0, 1 or 2)");
+  m->conv_kind = kind;
   return CNNUE_OK;
 }
 

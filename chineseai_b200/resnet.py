@@ -98,9 +98,15 @@ class ResNetModel:
     def handle(self):
         return self._h
 
-    def set_conv_kernel(self, persistent: bool) -> None:
-        """Chooses the persistent conv kernel (default) or the one-tile-per-CTA one."""
-        check(lib().cnnue_rn_set_conv_kernel(self._h, 1 if persistent else 0), "cnnue_rn_set_conv_kernel")
+    CONV_KERNELS = {"tile": 0, "persistent": 1, "halo": 2}
+
+    def set_conv_kernel(self, kind: str) -> None:
+        """Chooses the trunk conv kernel: "halo" (default; padded 8-board
+        layout, one halo tile per channel half), "persistent" or "tile"
+        (square-major layout, one TMA box per tap).  All compute the same
+        convolution; only the summation order inside the tensor cores may
+        differ."""
+        check(lib().cnnue_rn_set_conv_kernel(self._h, self.CONV_KERNELS[kind]), "cnnue_rn_set_conv_kernel")
 
     def workspace(self, batch: int):
         need = int(lib().cnnue_rn_workspace_bytes(batch))

@@ -710,10 +710,13 @@ size_t cnnue_rn_workspace_bytes(int64_t batch);
 int cnnue_rn_forward(const cnnue_rn_model* model, const uint16_t* d_planes, int64_t batch, float* d_probs,
                      float* d_logits, float* d_value, void* d_workspace, size_t workspace_bytes,
                      void* stream);
-/* Conv kernel choice: 1 (default) the persistent kernel (one CTA per SM, two
- * 128-row tiles per K block sharing each weight tile, double-buffered TMEM),
- * 0 the one-tile-per-CTA kernel.  Both compute the same results. */
-int cnnue_rn_set_conv_kernel(cnnue_rn_model* model, int persistent);
+/* Conv kernel choice: 2 (default) the halo kernel (activations in a padded,
+ * 8-board-interleaved layout where every 3x3 tap is a whole-atom row shift of
+ * one shared-memory halo tile), 1 the persistent square-major kernel (one CTA
+ * per SM, two 128-row tiles per K block sharing each weight tile,
+ * double-buffered TMEM), 0 the one-tile-per-CTA kernel.  All compute the same
+ * convolution. */
+int cnnue_rn_set_conv_kernel(cnnue_rn_model* model, int kind);
 
 /* ---- deterministic synthetic workloads (host) --------------------------- */
 /* SplitMix64 as the reference defines it (src/az.rs:3146-3176): the state is

@@ -53,3 +53,47 @@ def test_resnet_is_deterministic_and_batch_independent():
     # a board's result does not depend on its neighbours in the batch
     p3, l3, v3 = model.forward(dev[5:6].contiguous(), with_logits=True)
     assert torch.equal(l3[0], l1[5]) and torch.equal(v3[0], v1[5])
+
+
+def _check_against_oracle(w, planes, probs, logits, value):
+    lg, pr, _, v, _ = oracle.rn_forward(w, planes)
+    scale = max(1.0, float(np.abs(lg).max()))
+    assert np.abs(logits - lg).max() <= 1e-2 * scale
+    np.testing.assert_allclose(probs, pr, atol=1e-3, rtol=0)
+    np.testing.assert_allclose(value, v, atol=5e-3, rtol=0)
+
+
+@pytest.mark.parametrize("kind", ["tile", "persistent"])
+def test_square_major_conv_kernels_match_oracle(kind):
+    """The two square-major conv kernels (one TMA box per tap, edge rows
+    zeroed in shared memory) against the oracle."""
+    w, model = _model()
+    planes = resnet.synthetic_planes(37, 13)
+    dev = torch.from_numpy(planes.view(np.int16)).cuda()
+    model.set_conv_kernel(kind)
+    try:
+        probs, logits, value = model.forward(dev, with_logits=True)
+        assert model.read_status() == 0
+    finally:
+        model.set_conv_kernel("halo")
+    _check_against_oracle(w, planes, probs.cpu().numpy(), logits.cpu().numpy(), value.cpu().numpy())
+
+
+def test_halo_kernel_many_pairs_per_cta():
+    """700 boards: 88 groups of 8 (the last one partial), 77,440 padded rows,
+    303 row pairs, so every CTA of the persistent halo kernel runs two or
+    three pairs and both halo buffers and TMEM accumulators turn over.  A
+    sample of boards is checked against the oracle (boards are independent),
+    and each board equals its result in a batch of one."""
+    w, model = _model()
+    planes = resnet.synthetic_planes(700, 14)
+    planes[699] = 0
+    dev = torch.from_numpy(planes.view(np.int16)).cuda()
+    probs, logits, value = model.forward(dev, with_logits=True)
+    assert model.read_status() == 0
+    sample = np.array([0, 1, 7, 8, 255, 256, 351, 352, 517, 694, 695, 696, 699])
+    _check_against_oracle(w, planes[sample], probs.cpu().numpy()[sample], logits.cpu().numpy()[sample],
+                          value.cpu().numpy()[sample])
+    for b in (0, 352, 699):
+        p1, l1, v1 = model.forward(dev[b:b + 1].contiguous(), with_logits=True)
+        assert torch.equal(l1[0], logits[b]) and torch.equal(v1[0], value[b])

@@ -26,10 +26,11 @@
 // (loaded, ready, empty); every wait is bounded (1 s) and reports
 // CNNUE_STATUS_TIMEOUT.  No load uses cluster multicast.
 //
-// Heads, fp32 on CUDA cores: rn_head_prep_kernel (1x1 convs to 2 policy and
-// 1 value planes, value FC 90 -> 256 -> 1 with tanh, 8 boards per CTA),
-// rn_policy_fc_kernel (FC 180 -> 2086 as a tiled GEMM, 32 boards x 128 moves
-// per CTA), rn_softmax_kernel (one warp per board).
+// Heads, fp32 on CUDA cores: rn_head_conv_kernel (1x1 convs to 2 policy and
+// 1 value planes, a warp per trunk row), rn_value_kernel (value FC 90 -> 256
+// -> 1 with tanh, 32 boards per CTA), rn_policy_fc_kernel (FC 180 -> 2086 as
+// a tiled GEMM, 128 boards x 128 moves per CTA), rn_softmax_kernel (one warp
+// per board).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -58,7 +59,6 @@ constexpr int kStages = 3;
 constexpr int kConvThreads = 192;
 constexpr int kStemKb = 9;   // 9 taps x 64 (packed) channels / 64
 constexpr int kBlockKb = 18; // 9 taps x 128 channels / 64
-constexpr int kHeadBoards = 8;
 
 inline size_t conv_tile_offset(int conv) { return conv == 0 ? 0 : (size_t)kStemKb + (size_t)(conv - 1) * kBlockKb; }
 constexpr size_t kTotalKb = kStemKb + (size_t)(kConvs - 1) * kBlockKb;
@@ -816,106 +816,171 @@ struct HeadArgs {
   float* value;   // [B]
 };
 
-constexpr int kHeadThreads = 256;
 
-// 1x1 convs of 8 boards (policy planes to pc [B][180], value plane) and the
-// value MLP 90 -> 256 -> 1 with tanh.
-__global__ void __launch_bounds__(kHeadThreads) rn_head_prep_kernel(HeadArgs a, float* __restrict__ pc_out) {
-  __shared__ float vc[kHeadBoards][kSq];
-  __shared__ float red[kHeadBoards][kHeadThreads / 32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t b0 = (int64_t)blockIdx.x * kHeadBoards;
-  for (int i = tid; i < kHeadBoards * kSq; i += kHeadThreads) {
-    const int bl = i / kSq, p = i - bl * kSq;
-    const int64_t b = b0 + bl;
-    float s0 = 0.f, s1 = 0.f, s2 = 0.f;
-    if (b < a.B) {
-      const int64_t r = a.padded ? padded_row(b, p) : b * kSq + p;
-      const __nv_bfloat162* row = reinterpret_cast<const __nv_bfloat162*>(a.trunk + (size_t)r * kC);
-#pragma unroll 8
-      for (int c2 = 0; c2 < kC / 2; ++c2) {
-        const float2 x = __bfloat1622float2(row[c2]);
-        s0 = fmaf(x.x, __ldg(a.pcw + 2 * c2), s0);
-        s0 = fmaf(x.y, __ldg(a.pcw + 2 * c2 + 1), s0);
-        s1 = fmaf(x.x, __ldg(a.pcw + kC + 2 * c2), s1);
-        s1 = fmaf(x.y, __ldg(a.pcw + kC + 2 * c2 + 1), s1);
-        s2 = fmaf(x.x, __ldg(a.vcw + 2 * c2), s2);
-        s2 = fmaf(x.y, __ldg(a.vcw + 2 * c2 + 1), s2);
-      }
-      pc_out[b * 2 * kSq + p] = fmaxf(s0 + a.pcb[0], 0.f);
-      pc_out[b * 2 * kSq + kSq + p] = fmaxf(s1 + a.pcb[1], 0.f);
+// 1x1 convs of the trunk: policy planes to pc_t [180][B] and the value plane
+// to vc_t [90][B] (both after bias and ReLU), one warp per trunk row: lane l
+// reads channels 4l .. 4l+3 (the warp's load is the row's 256 contiguous
+// bytes) and the three dot products are reduced across the warp.  A warp
+// takes kConvRows rows at a time so that many loads are in flight.
+constexpr int kConvRows = 8;
+__global__ void __launch_bounds__(256) rn_head_conv_kernel(HeadArgs a, float* __restrict__ pc_t,
+                                                           float* __restrict__ vc_t) {
+  const int lane = threadIdx.x & 31;
+  const int64_t n_rows = a.B * kSq;
+  const int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kConvRows;
+  if (r0 >= n_rows) return;
+  const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.pcw) + lane);
+  const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.pcw + kC) + lane);
+  const float4 wv = __ldg(reinterpret_cast<const float4*>(a.vcw) + lane);
+  const float pcb0 = __ldg(a.pcb), pcb1 = __ldg(a.pcb + 1), vcb = __ldg(a.vcb);
+  float s[kConvRows][3];
+#pragma unroll
+  for (int u = 0; u < kConvRows; ++u) {
+    const int64_t i = r0 + u, b = i / kSq;
+    const int p = (int)(i - b * kSq);
+    s[u][0] = s[u][1] = s[u][2] = 0.f;
+    if (i < n_rows) {
+      const int64_t r = a.padded ? padded_row(b, p) : i;
+      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(a.trunk + (size_t)r * kC) + lane);
+      const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+      const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+      s[u][0] = fmaf(xb.y, w0.w, fmaf(xb.x, w0.z, fmaf(xa.y, w0.y, xa.x * w0.x)));
+      s[u][1] = fmaf(xb.y, w1.w, fmaf(xb.x, w1.z, fmaf(xa.y, w1.y, xa.x * w1.x)));
+      s[u][2] = fmaf(xb.y, wv.w, fmaf(xb.x, wv.z, fmaf(xa.y, wv.y, xa.x * wv.x)));
     }
-    vc[bl][p] = fmaxf(s2 + a.vcb[0], 0.f);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int u = 0; u < kConvRows; ++u)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) s[u][c] += __shfl_xor_sync(0xffffffffu, s[u][c], o);
+  // lanes 0 .. kConvRows-1 each write one row's three outputs
+#pragma unroll
+  for (int u = 0; u < kConvRows; ++u) {
+    const int64_t i = r0 + u, b = i / kSq;
+    const int p = (int)(i - b * kSq);
+    if (lane == u && i < n_rows) {
+      pc_t[(size_t)p * a.B + b] = fmaxf(s[u][0] + pcb0, 0.f);
+      pc_t[(size_t)(kSq + p) * a.B + b] = fmaxf(s[u][1] + pcb1, 0.f);
+      vc_t[(size_t)p * a.B + b] = fmaxf(s[u][2] + vcb, 0.f);
+    }
+  }
+}
+
+// Value MLP 90 -> 256 (ReLU) -> 1 (tanh) for 32 boards per CTA: thread j is
+// hidden unit j for all 32 boards (the value plane of the 32 boards staged in
+// shared memory, read as broadcasts); the 256 -> 1 layer is a block reduction.
+constexpr int kValueBoards = 32;
+__global__ void __launch_bounds__(256) rn_value_kernel(HeadArgs a, const float* __restrict__ vc_t) {
+  __shared__ __align__(16) float vc[kSq][kValueBoards];
+  __shared__ float red[kValueBoards][8];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t b0 = (int64_t)blockIdx.x * kValueBoards;
+  for (int i = tid; i < kSq * kValueBoards; i += 256) {
+    const int p = i / kValueBoards, bl = i % kValueBoards;
+    vc[p][bl] = b0 + bl < a.B ? vc_t[(size_t)p * a.B + b0 + bl] : 0.f;
   }
   __syncthreads();
-  float hsum[kHeadBoards];
+  float h[kValueBoards];
 #pragma unroll
-  for (int bl = 0; bl < kHeadBoards; ++bl) hsum[bl] = 0.f;
+  for (int bl = 0; bl < kValueBoards; ++bl) h[bl] = 0.f;
+#pragma unroll 6
   for (int p = 0; p < kSq; ++p) {
     const float w = __ldg(a.v1w_t + (size_t)p * 256 + tid);
 #pragma unroll
-    for (int bl = 0; bl < kHeadBoards; ++bl) hsum[bl] = fmaf(vc[bl][p], w, hsum[bl]);
+    for (int q = 0; q < kValueBoards / 4; ++q) {
+      const float4 x = *reinterpret_cast<const float4*>(&vc[p][4 * q]);
+      h[4 * q] = fmaf(x.x, w, h[4 * q]);
+      h[4 * q + 1] = fmaf(x.y, w, h[4 * q + 1]);
+      h[4 * q + 2] = fmaf(x.z, w, h[4 * q + 2]);
+      h[4 * q + 3] = fmaf(x.w, w, h[4 * q + 3]);
+    }
   }
   const float w2 = __ldg(a.v2w + tid), b1 = __ldg(a.v1b + tid);
 #pragma unroll
-  for (int bl = 0; bl < kHeadBoards; ++bl) {
-    float v = fmaxf(hsum[bl] + b1, 0.f) * w2;
+  for (int bl = 0; bl < kValueBoards; ++bl) {
+    float v = fmaxf(h[bl] + b1, 0.f) * w2;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     if (lane == 0) red[bl][warp] = v;
   }
   __syncthreads();
-  if (tid < kHeadBoards && b0 + tid < a.B) {
+  if (tid < kValueBoards && b0 + tid < a.B) {
     float v = 0.f;
-    for (int w = 0; w < kHeadThreads / 32; ++w) v += red[tid][w];
-    a.value[b0 + tid] = tanhf(v + a.v2b[0]);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += red[tid][w];
+    a.value[b0 + tid] = tanhf(v + __ldg(a.v2b));
   }
 }
 
-// Policy FC logits[B][2086] = pc[B][180] . W^T + b: CTA tile 32 boards x 128
-// moves, K staged in smem in chunks of 36; thread = 4 boards x 4 moves.
-constexpr int kFcBoards = 32, kFcMoves = 128, kFcK = 36;
-__global__ void __launch_bounds__(256) rn_policy_fc_kernel(const float* __restrict__ pc,
+// Policy FC logits[B][2086] = pc[B][180] . W^T + b, from pc_t [180][B]: CTA
+// tile 128 boards x 128 moves, thread tile 8 x 8 (four 16-byte shared loads
+// per 64 FMAs), K in chunks of 20 double-buffered through registers: the
+// next chunk's global loads are in flight while this one is multiplied.
+constexpr int kFcBoards = 128, kFcMoves = 128, kFcK = 20;
+__global__ void __launch_bounds__(256) rn_policy_fc_kernel(const float* __restrict__ pc_t,
                                                            const float* __restrict__ pfw_t,
                                                            const float* __restrict__ pfb, int64_t B,
                                                            float* __restrict__ logits) {
-  __shared__ float xs[kFcK][kFcBoards + 1];
-  __shared__ float ws[kFcK][kFcMoves];
+  __shared__ __align__(16) float xs[2][kFcK][kFcBoards];
+  __shared__ __align__(16) float ws[2][kFcK][kFcMoves];
+  constexpr int kPer = kFcK * kFcBoards / 256;  // elements of each operand a thread stages per chunk
+  static_assert(kFcK * kFcBoards % 256 == 0 && kFcBoards == kFcMoves && (2 * kSq) % kFcK == 0, "tiles");
   const int tid = threadIdx.x;
   const int64_t b0 = (int64_t)blockIdx.x * kFcBoards;
   const int j0 = blockIdx.y * kFcMoves;
-  const int tb = (tid >> 5) * 4, tj = (tid & 31) * 4;  // 8 x 4 boards, 32 x 4 moves
-  float acc[4][4] = {};
+  const int tb = (tid >> 4) * 8, tj = (tid & 15) * 8;
+  float rx[kPer], rw[kPer];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int i = tid + 256 * r, k = i / kFcBoards, c = i % kFcBoards;
+      rx[r] = b0 + c < B ? __ldg(pc_t + (size_t)(k0 + k) * B + b0 + c) : 0.f;
+      rw[r] = j0 + c < kMoves ? __ldg(pfw_t + (size_t)(k0 + k) * kMoves + j0 + c) : 0.f;
+    }
+  };
+  auto stage = [&](int buf) {
+#pragma unroll
+    for (int r = 0; r < kPer; ++r) {
+      const int i = tid + 256 * r, k = i / kFcBoards, c = i % kFcBoards;
+      xs[buf][k][c] = rx[r];
+      ws[buf][k][c] = rw[r];
+    }
+  };
+  float acc[8][8] = {};
+  fetch(0);
+  stage(0);
+  __syncthreads();
+  int buf = 0;
   for (int k0 = 0; k0 < 2 * kSq; k0 += kFcK) {
-    for (int i = tid; i < kFcK * kFcBoards; i += 256) {
-      const int bl = i / kFcK, k = i - bl * kFcK;
-      xs[k][bl] = b0 + bl < B ? pc[(b0 + bl) * 2 * kSq + k0 + k] : 0.f;
-    }
-    for (int i = tid; i < kFcK * kFcMoves; i += 256) {
-      const int k = i / kFcMoves, jj = i - k * kFcMoves;
-      ws[k][jj] = j0 + jj < kMoves ? __ldg(pfw_t + (size_t)(k0 + k) * kMoves + j0 + jj) : 0.f;
-    }
-    __syncthreads();
-#pragma unroll 6
+    const bool more = k0 + kFcK < 2 * kSq;
+    if (more) fetch(k0 + kFcK);
+#pragma unroll 4
     for (int k = 0; k < kFcK; ++k) {
-      float x[4], w[4];
+      const float4 xa = *reinterpret_cast<const float4*>(&xs[buf][k][tb]);
+      const float4 xb = *reinterpret_cast<const float4*>(&xs[buf][k][tb + 4]);
+      const float4 wa = *reinterpret_cast<const float4*>(&ws[buf][k][tj]);
+      const float4 wb = *reinterpret_cast<const float4*>(&ws[buf][k][tj + 4]);
+      const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+      const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) x[i] = xs[k][tb + i];
+      for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) w[i] = ws[k][tj + i];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[i][q] = fmaf(x[i], w[q], acc[i][q]);
+        for (int q = 0; q < 8; ++q) acc[i][q] = fmaf(x[i], w[q], acc[i][q]);
     }
-    __syncthreads();
+    if (more) {
+      stage(buf ^ 1);
+      __syncthreads();
+      buf ^= 1;
+    }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const int64_t b = b0 + tb + i;
     if (b >= B) continue;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 8; ++q) {
       const int j = j0 + tj + q;
       if (j < kMoves) logits[b * kMoves + j] = acc[i][q] + __ldg(pfb + j);
     }
@@ -1029,7 +1094,7 @@ size_t cnnue_rn_workspace_bytes(int64_t batch) {
   const size_t m = batch > 0 ? (size_t)padded_rows(batch) : 0;
   const size_t b = batch > 0 ? (size_t)batch : 0;
   return sizeof(WorkspaceHeader) + align_up(m * 64 * 2, 256) + 3 * align_up(m * kC * 2, 256) +
-         align_up(b * 2 * kSq * 4, 256) + align_up(b * kMoves * 4, 256);
+         align_up(b * 2 * kSq * 4, 256) + align_up(b * kSq * 4, 256) + align_up(b * kMoves * 4, 256);
 }
 
 int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model** out) {
@@ -1068,6 +1133,9 @@ int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model*
   float* v2w = hp; std::memcpy(v2w, w->value_fc2_w, sizeof(float) * 256); hp += 256;
   float* v2b = hp; v2b[0] = w->value_fc2_b[0];
 
+  // rn_head_conv_kernel reads pcw and vcw as float4
+  if ((pcw - head.data()) % 4 != 0 || (vcw - head.data()) % 4 != 0)
+    return set_error(CNNUE_ERR_INVALID_ARG, "head weight block misaligned");
   auto* m = new (std::nothrow) cnnue_rn_model;
   if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
   m->device = device;
@@ -1159,8 +1227,10 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
     act[i] = (__nv_bfloat16*)p;
     p += align_up(rows_cap * kC * 2, 256);
   }
-  float* pc = (float*)p;
+  float* pc = (float*)p;  // pc_t [180][B]
   p += align_up((size_t)batch * 2 * kSq * 4, 256);
+  float* vc = (float*)p;  // vc_t [90][B]
+  p += align_up((size_t)batch * kSq * 4, 256);
   float* logits = d_logits ? d_logits : (float*)p;
   uint32_t* status = &((WorkspaceHeader*)ws)->status;
   if (padded)
@@ -1225,8 +1295,11 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   h.logits = logits;
   h.probs = d_probs;
   h.value = d_value;
-  rn_head_prep_kernel<<<(unsigned)((batch + kHeadBoards - 1) / kHeadBoards), kHeadThreads, 0, s>>>(h, pc);
-  if (int st = check_launch_error("rn_head_prep_kernel")) return st;
+  const int64_t conv_warps = (batch * kSq + kConvRows - 1) / kConvRows;
+  rn_head_conv_kernel<<<(unsigned)((conv_warps + 7) / 8), 256, 0, s>>>(h, pc, vc);
+  if (int st = check_launch_error("rn_head_conv_kernel")) return st;
+  rn_value_kernel<<<(unsigned)((batch + kValueBoards - 1) / kValueBoards), 256, 0, s>>>(h, vc);
+  if (int st = check_launch_error("rn_value_kernel")) return st;
   const dim3 fc_grid((unsigned)((batch + kFcBoards - 1) / kFcBoards), (kMoves + kFcMoves - 1) / kFcMoves);
   rn_policy_fc_kernel<<<fc_grid, 256, 0, s>>>(pc, h.pfw_t, h.pfb, batch, logits);
   if (int st = check_launch_error("rn_policy_fc_kernel")) return st;

@@ -811,8 +811,8 @@ void attacked_squares(const int8_t* b, int by, uint8_t* mask) {
 }
 
 // Position::gives_check_after_move_fast (src/xiangqi/mod.rs:763-1012).
-bool gives_check(const int8_t* b, int side, int from, int to) {
-  const int g = general_of(b, 1 - side);
+// g: the square of the general of 1 - side (general_of), -1 if none.
+bool gives_check(const int8_t* b, int side, int from, int to, int g) {
   if (g < 0 || b[from] == 0) return false;
   const int moving = b[from];
   auto occ = [&](int sq) -> int { return sq == from ? 0 : (sq == to ? moving : (int)b[sq]); };
@@ -987,6 +987,7 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
   uint8_t opp[kSq], own[kSq];
   attacked_squares(board, 1, opp);
   attacked_squares(board, 0, own);
+  const int enemy_general = general_of(board, 1);
   const auto& moves = dense_moves();
   const bool compact = o->policy_sparse_indices == nullptr;
   int64_t* items = o->policy_items + row * M;
@@ -1033,7 +1034,7 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
                            (uint64_t)move_valid << 45 | (uint64_t)capture << 46 | (uint64_t)1 << 47);
     if (move_valid && compact) {
       signature[off] = (uint8_t)(opp[from] | opp[to] << 1 | own[from] << 2 | own[to] << 3 | (int)capture << 4 |
-                                 (int)gives_check(board, 0, from, to) << 5);
+                                 (int)gives_check(board, 0, from, to, enemy_general) << 5);
     } else if (move_valid) {
       const int piece = mf / kSq;
       const int pair = us * 9 + them;
@@ -1053,7 +1054,7 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
       // policy_tactical_indices (src/az.rs:815-839)
       const int64_t sig = (int64_t)opp[from] | (int64_t)opp[to] << 1 | (int64_t)own[from] << 2 |
                           (int64_t)own[to] << 3 | (int64_t)capture << 4 |
-                          (int64_t)gives_check(board, 0, from, to) << 5;
+                          (int64_t)gives_check(board, 0, from, to, enemy_general) << 5;
       tactical[off * 2] = ((int64_t)mi * 7 + piece) * 64 + sig;
       tactical[off * 2 + 1] = kTacticalExact + piece * 64 + sig;
     }
@@ -1127,6 +1128,7 @@ int cnnue_az_policy_moves(const int8_t* board, int side, const uint8_t* moves, i
   attacked_squares(board, side, own);
   int us, them;
   buckets_of(board, side, &us, &them);
+  const int enemy_general = general_of(board, 1 - side);
   int status = CNNUE_OK;
   for (int i = 0; i < n_moves; ++i) {
     const int from = moves[2 * i], to = moves[2 * i + 1];
@@ -1141,7 +1143,7 @@ int cnnue_az_policy_moves(const int8_t* board, int side, const uint8_t* moves, i
     const int captured = board[to] != 0 ? (color_of(board[to]) == side ? 0 : 7) + kind_of(board[to]) : 15;
     const uint32_t sig = (uint32_t)opp[from] | (uint32_t)opp[to] << 1 | (uint32_t)own[from] << 2 |
                          (uint32_t)own[to] << 3 | (uint32_t)(board[to] != 0) << 4 |
-                         (uint32_t)gives_check(board, side, from, to) << 5;
+                         (uint32_t)gives_check(board, side, from, to, enemy_general) << 5;
     info[2 * i] = (dense == 0xffff ? 0xfffu : dense) | (uint32_t)moved << 12 | (uint32_t)captured << 16 | sig << 20;
     info[2 * i + 1] = (uint32_t)cf | (uint32_t)ct << 7 | (uint32_t)us << 14 | (uint32_t)them << 18;
   }

@@ -26,6 +26,7 @@
 // the moves that leave the mover's general attacked (or facing the other
 // general on an open file) removed.
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <condition_variable>
@@ -246,19 +247,42 @@ int count_checkers(const int8_t* b, int g, int by) {
 // Order of Position::legal_moves (src/xiangqi/mod.rs:576-579, :1113-1131,
 // :1259-1305): pieces in square order, each piece's steps in the reference's
 // step tables; in check by a single piece the general's moves come first.
+//
+// The attack test runs on the board with the move made in place (and then
+// unmade).  When the side is not in check, a move by another piece can only
+// expose its general if it leaves or enters the general's rank or file
+// (rook, cannon screen, facing generals) or leaves one of the general's four
+// diagonal neighbours (the leg of a horse aimed at it): soldiers need no open
+// path, and the enemy advisors and elephants never reach this palace.  Such
+// moves are legal without the test.
 void legal_moves(const int8_t* b, int side, std::vector<Move>& pseudo, std::vector<Move>& out) {
   pseudo_moves(b, side, pseudo);
   const int king = general_square(b, side);
-  if (king >= 0 && square_attacked(b, king, 1 - side) && count_checkers(b, king, 1 - side) == 1)
+  const bool check = king >= 0 && square_attacked(b, king, 1 - side);
+  if (check && count_checkers(b, king, 1 - side) == 1)
     std::stable_partition(pseudo.begin(), pseudo.end(), [&](const Move& m) { return m.from == king; });
   out.clear();
+  if (king < 0) {
+    out = pseudo;
+    return;
+  }
+  const int kf = king % 9, kr = king / 9;
+  auto on_lines = [&](int sq) { return sq % 9 == kf || sq / 9 == kr; };
+  auto leg = [&](int sq) { return std::abs(sq % 9 - kf) == 1 && std::abs(sq / 9 - kr) == 1; };
   int8_t c[kSq];
+  std::memcpy(c, b, kSq);
   for (const Move& m : pseudo) {
-    std::memcpy(c, b, kSq);
-    c[m.to] = c[m.from];
+    if (!check && m.from != king && !on_lines(m.from) && !on_lines(m.to) && !leg(m.from)) {
+      out.push_back(m);
+      continue;
+    }
+    const int8_t moving = c[m.from], captured = c[m.to];
+    c[m.to] = moving;
     c[m.from] = 0;
-    const int g = general_square(c, side);
-    if (g < 0 || !square_attacked(c, g, 1 - side)) out.push_back(m);
+    const int g = m.from == king ? m.to : king;
+    if (!square_attacked(c, g, 1 - side)) out.push_back(m);
+    c[m.from] = moving;
+    c[m.to] = captured;
   }
 }
 
@@ -306,17 +330,20 @@ class Pool {
     cv_.notify_all();
     for (auto& t : workers_) t.join();
   }
-  // fn(i) for i in [0, n), spread over the workers and the calling thread.
+  // fn(i) for i in [0, n), spread over the workers and the calling thread;
+  // items are claimed in chunks from an atomic counter.
   void run(int64_t n, const std::function<void(int64_t)>& fn) {
     if (workers_.empty() || n < 2) {
       for (int64_t i = 0; i < n; ++i) fn(i);
       return;
     }
+    const int64_t threads = (int64_t)workers_.size() + 1;
     {
       std::lock_guard<std::mutex> g(mu_);
       fn_ = &fn;
       n_ = n;
-      next_ = 0;
+      grain_ = std::max<int64_t>(1, std::min<int64_t>(64, n / (threads * 8)));
+      next_.store(0, std::memory_order_relaxed);
       busy_ = (int)workers_.size();
       ++gen_;
     }
@@ -329,14 +356,12 @@ class Pool {
 
  private:
   void work() {
+    const int64_t n = n_, grain = grain_;
     for (;;) {
-      int64_t i;
-      {
-        std::lock_guard<std::mutex> g(mu_);
-        if (next_ >= n_) return;
-        i = next_++;
-      }
-      (*fn_)(i);
+      const int64_t i0 = next_.fetch_add(grain, std::memory_order_relaxed);
+      if (i0 >= n) return;
+      const int64_t i1 = std::min(n, i0 + grain);
+      for (int64_t i = i0; i < i1; ++i) (*fn_)(i);
     }
   }
   void loop() {
@@ -360,7 +385,8 @@ class Pool {
   std::mutex mu_;
   std::condition_variable cv_, done_cv_;
   const std::function<void(int64_t)>* fn_ = nullptr;
-  int64_t n_ = 0, next_ = 0;
+  int64_t n_ = 0, grain_ = 1;
+  std::atomic<int64_t> next_{0};
   int busy_ = 0;
   uint64_t gen_ = 0;
   bool stop_ = false;
@@ -452,8 +478,57 @@ struct Tree {
   Sim active;
   Pending pending;
   std::vector<Move> scratch_pseudo, scratch_moves;
-  // leaf inputs of this round (filled by prepare, read by the batcher)
+  std::vector<uint8_t> scratch_mv;
+  std::vector<float> scratch_prior;
+  // leaf inputs of this round (filled when the leaf becomes pending)
   std::vector<uint32_t> items, threats, move_info;
+
+  // A fresh tree for `root`, keeping every vector's capacity from the last
+  // search (a search re-uses its trees).
+  void reset(const Node& root, const cnnue_mcts_limits& limits) {
+    nodes.clear();
+    children.clear();
+    nodes.push_back(root);
+    lim = limits;
+    completed = 0;
+    has_active = has_pending = false;
+    active.node = active.depth = 0;
+    active.path.clear();
+    clear_pending();
+  }
+
+  // The pending leaf's network inputs: trunk features, threat features and
+  // the policy descriptors of its moves (cnnue_az_features,
+  // cnnue_az_threat_features, cnnue_az_policy_moves).
+  void leaf_inputs(bool threat_active) {
+    const Node& leaf = nodes[pending.sim.node];
+    items.resize(CNNUE_AZ_SQUARES);
+    int cnt = 0;
+    cnnue_az_features(leaf.board, leaf.side, items.data(), &cnt);
+    items.resize(cnt);
+    threats.clear();
+    if (threat_active) {
+      threats.resize(CNNUE_AZ_THREAT_MAX);
+      int tc = 0;
+      cnnue_az_threat_features(leaf.board, leaf.side, threats.data(), &tc);
+      threats.resize(tc);
+    }
+    const size_t m = pending.moves.size();
+    scratch_mv.resize(2 * m);
+    for (size_t i = 0; i < m; ++i) {
+      scratch_mv[2 * i] = pending.moves[i].from;
+      scratch_mv[2 * i + 1] = pending.moves[i].to;
+    }
+    move_info.resize(2 * std::max<size_t>(m, 1));
+    cnnue_az_policy_moves(leaf.board, leaf.side, scratch_mv.data(), (int)m, move_info.data());
+  }
+
+  void clear_pending() {
+    pending.sim.node = pending.sim.depth = 0;
+    pending.sim.path.clear();
+    pending.moves.clear();
+    pending.in_check = pending.cutoff = pending.root_expand = false;
+  }
 
   uint32_t max_depth() const { return lim.max_depth > 0 ? (uint32_t)lim.max_depth : (uint32_t)lim.simulations; }
 
@@ -542,7 +617,7 @@ struct Tree {
 
   // prepare_batch_simulation (src/az/alphazero.rs:1384-1495): true = a leaf
   // is pending; false = the simulation completed without an evaluation.
-  bool prepare(Sim sim) {
+  bool prepare(Sim& sim) {
     for (;;) {
       const uint32_t ni = sim.node;
       Node& n = nodes[ni];
@@ -569,9 +644,9 @@ struct Tree {
           finish(sim, e);
           return false;
         }
-        pending = Pending();
-        pending.sim = std::move(sim);
-        pending.moves = scratch_moves;
+        clear_pending();
+        std::swap(pending.sim, sim);
+        pending.moves.assign(scratch_moves.begin(), scratch_moves.end());
         pending.in_check = !cutoff && in_check(n.board, n.side);
         pending.cutoff = cutoff;
         has_pending = true;
@@ -607,8 +682,8 @@ struct Tree {
       r.expanded = true;
       return;
     }
-    pending = Pending();
-    pending.moves = scratch_moves;
+    clear_pending();
+    pending.moves.assign(scratch_moves.begin(), scratch_moves.end());
     pending.root_expand = true;
     has_pending = true;
   }
@@ -637,7 +712,8 @@ struct Tree {
     float mx = -INFINITY;
     for (size_t i = 0; i < m; ++i) mx = std::max(mx, logits[i]);
     const float inv_t = 1.0f / std::max(lim.policy_softmax_temp, 1.0e-3f);
-    std::vector<float> pri(m);
+    std::vector<float>& pri = scratch_prior;
+    pri.resize(m);
     float sum = 0.f;
     for (size_t i = 0; i < m; ++i) {
       pri[i] = std::exp((logits[i] - mx) * inv_t);
@@ -655,7 +731,7 @@ struct Tree {
     nodes[ni].expanded = true;
     if (root_expand) return false;
     if (m > 0 && (p.in_check || m == 1)) {
-      active = std::move(p.sim);
+      std::swap(active, p.sim);
       const uint32_t child = ensure_child(ni, 0);
       active.path.push_back({ni, 0});
       active.node = child;
@@ -682,6 +758,12 @@ struct cnnue_mcts {
     size_t bytes = 0;
   };
   Buf items, offsets, acc, pacc, threats, t_off, minfo, m_off, rule, wdl, q, logits, ws, ws_eval;
+  // pinned host staging of a round's leaf inputs and results (grown on demand)
+  struct HostBuf {
+    void* h = nullptr;
+    size_t bytes = 0;
+  };
+  HostBuf h_items, h_off, h_threats, h_toff, h_minfo, h_moff, h_rule, h_wdl, h_q, h_logits;
   // seconds spent in the last search: selection + leaf preparation on the
   // host, leaf inputs + GPU evaluation + copies, finalisation + backup
   double t_select = 0, t_inputs = 0, t_gpu = 0, t_finalize = 0;
@@ -690,6 +772,8 @@ struct cnnue_mcts {
     for (Buf* b : {&items, &offsets, &acc, &pacc, &threats, &t_off, &minfo, &m_off, &rule, &wdl, &q, &logits, &ws,
                    &ws_eval})
       if (b->d) cudaFree(b->d);
+    for (HostBuf* b : {&h_items, &h_off, &h_threats, &h_toff, &h_minfo, &h_moff, &h_rule, &h_wdl, &h_q, &h_logits})
+      if (b->h) cudaFreeHost(b->h);
     delete pool;
   }
 };
@@ -705,6 +789,23 @@ int grow(cnnue_mcts::Buf& b, size_t bytes) {
   const size_t want = bytes + bytes / 2;
   if (cudaMalloc(&b.d, want) != cudaSuccess) return set_error(CNNUE_ERR_CUDA, "cudaMalloc of %zu bytes", want);
   b.bytes = want;
+  return CNNUE_OK;
+}
+
+// Pinned host memory, so that the round's copies run asynchronously.
+template <class T>
+int grow_host(cnnue_mcts::HostBuf& b, size_t count, T** out) {
+  const size_t bytes = std::max<size_t>(count * sizeof(T), 256);
+  if (b.bytes < bytes) {
+    if (b.h) cudaFreeHost(b.h);
+    b.h = nullptr;
+    b.bytes = 0;
+    const size_t want = bytes + bytes / 2;
+    if (cudaHostAlloc(&b.h, want, cudaHostAllocDefault) != cudaSuccess)
+      return set_error(CNNUE_ERR_CUDA, "cudaHostAlloc of %zu bytes", want);
+    b.bytes = want;
+  }
+  *out = static_cast<T*>(b.h);
   return CNNUE_OK;
 }
 
@@ -727,74 +828,61 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
   const int64_t n = (int64_t)ids.size();
   if (n == 0) return CNNUE_OK;
   const double t0 = now_s();
-  // host inputs, in parallel per leaf
-  s->pool->run(n, [&](int64_t k) {
-    Tree& t = s->trees[ids[k]];
-    const Node& leaf = t.nodes[t.pending.sim.node];
-    t.items.resize(CNNUE_AZ_SQUARES);
-    int cnt = 0;
-    cnnue_az_features(leaf.board, leaf.side, t.items.data(), &cnt);
-    t.items.resize(cnt);
-    t.threats.clear();
-    if (s->threat_active) {
-      t.threats.resize(CNNUE_AZ_THREAT_MAX);
-      int tc = 0;
-      cnnue_az_threat_features(leaf.board, leaf.side, t.threats.data(), &tc);
-      t.threats.resize(tc);
-    }
-    const size_t m = t.pending.moves.size();
-    std::vector<uint8_t> mv(2 * m);
-    for (size_t i = 0; i < m; ++i) {
-      mv[2 * i] = t.pending.moves[i].from;
-      mv[2 * i + 1] = t.pending.moves[i].to;
-    }
-    t.move_info.resize(2 * std::max<size_t>(m, 1));
-    cnnue_az_policy_moves(leaf.board, leaf.side, mv.data(), (int)m, t.move_info.data());
-  });
-  // CSR layout
-  std::vector<uint32_t> off(n + 1, 0), toff(n + 1, 0), moff(n + 1, 0);
+  // (each leaf's inputs were computed when it became pending)
+  // CSR layout, in pinned staging buffers
+  uint32_t *off, *toff, *moff;
+  MCTS_TRY(grow_host(s->h_off, n + 1, &off));
+  MCTS_TRY(grow_host(s->h_toff, n + 1, &toff));
+  MCTS_TRY(grow_host(s->h_moff, n + 1, &moff));
+  off[0] = toff[0] = moff[0] = 0;
   for (int64_t k = 0; k < n; ++k) {
     const Tree& t = s->trees[ids[k]];
     off[k + 1] = off[k] + (uint32_t)t.items.size();
     toff[k + 1] = toff[k] + (uint32_t)t.threats.size();
     moff[k + 1] = moff[k] + (uint32_t)t.pending.moves.size();
   }
-  std::vector<uint32_t> items(std::max<uint32_t>(off[n], 1)), threats(std::max<uint32_t>(toff[n], 1)),
-      minfo(2 * std::max<uint32_t>(moff[n], 1));
-  std::vector<float> rule((size_t)n * CNNUE_AZ_RULE_CONTEXT);
+  const size_t n_items = std::max<uint32_t>(off[n], 1), n_threats = std::max<uint32_t>(toff[n], 1);
+  const size_t n_minfo = 2 * (size_t)std::max<uint32_t>(moff[n], 1), n_rule = (size_t)n * CNNUE_AZ_RULE_CONTEXT;
+  uint32_t *items, *threats, *minfo;
+  float* rule;
+  MCTS_TRY(grow_host(s->h_items, n_items, &items));
+  MCTS_TRY(grow_host(s->h_threats, n_threats, &threats));
+  MCTS_TRY(grow_host(s->h_minfo, n_minfo, &minfo));
+  MCTS_TRY(grow_host(s->h_rule, n_rule, &rule));
   const int64_t chunk = 256;
   s->pool->run((n + chunk - 1) / chunk, [&](int64_t c) {
     for (int64_t k = c * chunk; k < std::min(n, (c + 1) * chunk); ++k) {
       const Tree& t = s->trees[ids[k]];
-      std::copy(t.items.begin(), t.items.end(), items.begin() + off[k]);
-      std::copy(t.threats.begin(), t.threats.end(), threats.begin() + toff[k]);
-      std::copy(t.move_info.begin(), t.move_info.begin() + 2 * t.pending.moves.size(), minfo.begin() + 2 * moff[k]);
-      std::copy(t.rule, t.rule + CNNUE_AZ_RULE_CONTEXT, rule.begin() + k * CNNUE_AZ_RULE_CONTEXT);
+      std::copy(t.items.begin(), t.items.end(), items + off[k]);
+      std::copy(t.threats.begin(), t.threats.end(), threats + toff[k]);
+      std::copy(t.move_info.begin(), t.move_info.begin() + 2 * t.pending.moves.size(), minfo + 2 * moff[k]);
+      std::copy(t.rule, t.rule + CNNUE_AZ_RULE_CONTEXT, rule + k * CNNUE_AZ_RULE_CONTEXT);
     }
   });
   const double t1 = now_s();
   const size_t ev_ws = cnnue_az_evaluate_workspace_bytes(s->model, n);
-  MCTS_TRY(grow(s->items, items.size() * 4));
-  MCTS_TRY(grow(s->offsets, off.size() * 4));
+  const size_t n_off = (size_t)n + 1;
+  MCTS_TRY(grow(s->items, n_items * 4));
+  MCTS_TRY(grow(s->offsets, n_off * 4));
   MCTS_TRY(grow(s->acc, (size_t)n * s->hidden * 4));
   MCTS_TRY(grow(s->pacc, (size_t)n * 32 * 2));
-  MCTS_TRY(grow(s->threats, threats.size() * 4));
-  MCTS_TRY(grow(s->t_off, toff.size() * 4));
-  MCTS_TRY(grow(s->minfo, minfo.size() * 4));
-  MCTS_TRY(grow(s->m_off, moff.size() * 4));
-  MCTS_TRY(grow(s->rule, rule.size() * 4));
+  MCTS_TRY(grow(s->threats, n_threats * 4));
+  MCTS_TRY(grow(s->t_off, n_off * 4));
+  MCTS_TRY(grow(s->minfo, n_minfo * 4));
+  MCTS_TRY(grow(s->m_off, n_off * 4));
+  MCTS_TRY(grow(s->rule, n_rule * 4));
   MCTS_TRY(grow(s->wdl, (size_t)n * 12));
   MCTS_TRY(grow(s->q, (size_t)n * 4));
   MCTS_TRY(grow(s->logits, (size_t)std::max<uint32_t>(moff[n], 1) * 4));
   MCTS_TRY(grow(s->ws, cnnue_az_workspace_bytes()));
   MCTS_TRY(grow(s->ws_eval, ev_ws));
-  MCTS_CUDA(cudaMemcpyAsync(s->items.d, items.data(), items.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->offsets.d, off.data(), off.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->threats.d, threats.data(), threats.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->t_off.d, toff.data(), toff.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->minfo.d, minfo.data(), minfo.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->m_off.d, moff.data(), moff.size() * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->rule.d, rule.data(), rule.size() * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->items.d, items, n_items * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->offsets.d, off, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->threats.d, threats, n_threats * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->t_off.d, toff, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->minfo.d, minfo, n_minfo * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->m_off.d, moff, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(s->rule.d, rule, n_rule * 4, cudaMemcpyHostToDevice, stream));
   MCTS_CUDA(cudaMemsetAsync(s->ws.d, 0, s->ws.bytes, stream));
   MCTS_TRY(cnnue_az_refresh(s->model, (const uint32_t*)s->items.d, off[n], (const uint32_t*)s->offsets.d, n,
                             (float*)s->acc.d, s->ws.d, s->ws.bytes, stream));
@@ -805,10 +893,14 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
                              s->threat_active ? (const uint32_t*)s->t_off.d : nullptr, (const int16_t*)s->pacc.d,
                              (const uint32_t*)s->minfo.d, moff[n], (const uint32_t*)s->m_off.d, n, (float*)s->wdl.d,
                              (float*)s->q.d, (float*)s->logits.d, s->ws_eval.d, s->ws_eval.bytes, stream));
-  std::vector<float> wdl((size_t)n * 3), q(n), logits(std::max<uint32_t>(moff[n], 1));
-  MCTS_CUDA(cudaMemcpyAsync(wdl.data(), s->wdl.d, wdl.size() * 4, cudaMemcpyDeviceToHost, stream));
-  MCTS_CUDA(cudaMemcpyAsync(q.data(), s->q.d, q.size() * 4, cudaMemcpyDeviceToHost, stream));
-  MCTS_CUDA(cudaMemcpyAsync(logits.data(), s->logits.d, logits.size() * 4, cudaMemcpyDeviceToHost, stream));
+  const size_t n_logits = std::max<uint32_t>(moff[n], 1);
+  float *wdl, *q, *logits;
+  MCTS_TRY(grow_host(s->h_wdl, (size_t)n * 3, &wdl));
+  MCTS_TRY(grow_host(s->h_q, (size_t)n, &q));
+  MCTS_TRY(grow_host(s->h_logits, n_logits, &logits));
+  MCTS_CUDA(cudaMemcpyAsync(wdl, s->wdl.d, (size_t)n * 3 * 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(q, s->q.d, (size_t)n * 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(logits, s->logits.d, n_logits * 4, cudaMemcpyDeviceToHost, stream));
   int status = CNNUE_OK;
   MCTS_TRY(cnnue_read_status(s->ws.d, stream, &status));
   if (status != CNNUE_OK) return set_error(status, "leaf evaluation reported bad input");
@@ -818,7 +910,7 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
   s->pool->run(n, [&](int64_t k) {
     Tree& t = s->trees[ids[k]];
     Eval e{{wdl[k * 3], wdl[k * 3 + 1], wdl[k * 3 + 2]}, q[k]};
-    t.finalize(e, logits.data() + moff[k]);
+    t.finalize(e, logits + moff[k]);
   });
   const double t3 = now_s();
   s->t_inputs += t1 - t0;
@@ -909,20 +1001,17 @@ namespace {
 int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, const float* rule_context,
                      int64_t n_roots, const cnnue_mcts_limits* limits, void* stream, uint64_t* n_evaluations) {
   cudaStream_t st = (cudaStream_t)stream;
-  s->trees.clear();
-  s->trees.resize(n_roots);
+  if ((int64_t)s->trees.size() != n_roots) s->trees.resize(n_roots);
   for (int64_t i = 0; i < n_roots; ++i) {
     Tree& t = s->trees[i];
     for (int sq = 0; sq < kSq; ++sq)
       if (boards[i * kSq + sq] < -7 || boards[i * kSq + sq] > 7)
         return set_error(CNNUE_ERR_INVALID_ARG, "root %lld: board[%d] = %d", (long long)i, sq, boards[i * kSq + sq]);
     if (sides[i] > 1) return set_error(CNNUE_ERR_INVALID_ARG, "root %lld: side %d", (long long)i, sides[i]);
-    t.lim = *limits;
     Node root;
     std::memcpy(root.board, boards + i * kSq, kSq);
     root.side = sides[i];
-    t.nodes.reserve(1024);
-    t.nodes.push_back(root);
+    t.reset(root, *limits);
     for (int k = 0; k < CNNUE_AZ_RULE_CONTEXT; ++k)
       t.rule[k] = rule_context ? rule_context[i * CNNUE_AZ_RULE_CONTEXT + k] : 0.f;
   }
@@ -931,12 +1020,15 @@ int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, 
   s->rounds = 0;
   // every root is expanded first, in one batch (tree.expand(root), :440-445)
   {
+    s->pool->run(n_roots, [&](int64_t i) {
+      Tree& t = s->trees[i];
+      if (t.lim.simulations <= 0) return;
+      t.start_root();
+      if (t.has_pending) t.leaf_inputs(s->threat_active);
+    });
     std::vector<uint32_t> ids;
-    for (int64_t i = 0; i < n_roots; ++i) {
-      if (s->trees[i].lim.simulations <= 0) continue;
-      s->trees[i].start_root();
+    for (int64_t i = 0; i < n_roots; ++i)
       if (s->trees[i].has_pending) ids.push_back((uint32_t)i);
-    }
     evals += ids.size();
     MCTS_TRY(evaluate_round(s, ids, st));
   }
@@ -945,12 +1037,15 @@ int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, 
     s->pool->run(n_roots, [&](int64_t i) {
       Tree& t = s->trees[i];
       while (!t.has_pending && t.completed < (uint64_t)t.lim.simulations) {
-        Sim sim;
-        if (t.has_active) {
-          sim = std::move(t.active);
-          t.has_active = false;
+        if (!t.has_active) {  // a new simulation from the root
+          t.active.node = t.active.depth = 0;
+          t.active.path.clear();
         }
-        if (t.prepare(std::move(sim))) break;
+        t.has_active = false;
+        if (t.prepare(t.active)) {
+          t.leaf_inputs(s->threat_active);
+          break;
+        }
       }
     });
     std::vector<uint32_t> ids;

@@ -805,9 +805,10 @@ int cnnue_mcts_search(cnnue_mcts* search, const int8_t* boards, const uint8_t* s
                       const float* rule_context, int64_t n_roots, const cnnue_mcts_limits* limits,
                       void* stream, uint64_t* n_evaluations);
 /* Wall-clock seconds of the last search by phase: seconds[0] selection and
- * leaf preparation, [1] leaf inputs (features, threats, move records),
- * [2] GPU evaluation with its copies, [3] finalisation and backup; *rounds
- * (optional) the number of GPU batches. */
+ * leaf preparation (legal moves, and each new leaf's network inputs:
+ * features, threats, move records), [1] assembly of the round's batch in
+ * pinned host buffers, [2] GPU evaluation with its copies, [3] finalisation
+ * and backup; *rounds (optional) the number of GPU batches. */
 int cnnue_mcts_stats(const cnnue_mcts* search, double* seconds, uint64_t* rounds);
 /* Root statistics of the last search: per root move (from/to pairs) its
  * visits, prior and Q (root player's view), the index of the best move

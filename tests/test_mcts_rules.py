@@ -46,3 +46,29 @@ def test_facing_generals_and_pins():
     assert rook and all(to % 9 == 4 for _, to in rook)
     # the Red general may not step onto the open file facing the Black general: nothing blocks after 49 leaves
     assert sorted(map(tuple, moves.tolist())) == sorted(mcts_ref.legal_moves(b, 0))
+
+
+def test_playout_positions_match_restatement():
+    """Positions from random legal playouts of 1-80 plies from the start (the
+    search's own inputs: checks, pins of every kind, cannon screens, horse
+    legs next to the general), both sides to move: the same legal moves in
+    the same order.  Guards the generator's shortcut that skips the attack
+    test for moves that cannot expose the general."""
+    rng = np.random.default_rng(11)
+    b0, s0 = az.board_from_fen(START)
+    n, checks = 0, 0
+    while n < 1000:
+        b, side = b0.copy(), s0
+        for _ in range(int(rng.integers(1, 81))):
+            moves = mcts.legal_moves(b, side)  # fast; the end positions are compared below
+            if not len(moves) or not (b == -1).any() or not (b == 1).any():
+                break
+            frm, to = moves[rng.integers(len(moves))]
+            b[to], b[frm] = b[frm], 0
+            side = 1 - side
+        for s in (0, 1):
+            got = list(map(tuple, mcts.legal_moves(b, s).tolist()))
+            assert got == mcts_ref.legal_moves(b, s), (n, s)
+            checks += mcts_ref.in_check(b, s)
+        n += 1
+    assert checks > 10

@@ -890,6 +890,9 @@ bool gives_check(const int8_t* b, int side, int from, int to, int g) {
     }
   }
   // a horse or elephant whose leg / eye was `from` (leaper_revealed_*, :845-918).
+  // Every leg or eye of a leap onto the general is one of its four diagonal
+  // neighbours, so no other `from` can reveal one.
+  if (std::abs(from % 9 - gf) != 1 || std::abs(from / 9 - gr) != 1) return false;
   static const int hs[8][4] = {{0, -1, -1, -2}, {0, -1, 1, -2}, {0, 1, -1, 2}, {0, 1, 1, 2},
                                {-1, 0, -2, -1}, {-1, 0, -2, 1}, {1, 0, 2, -1}, {1, 0, 2, 1}};
   for (auto& h : hs) {

@@ -752,28 +752,42 @@ struct cnnue_mcts {
   bool threat_active = false;
   Pool* pool = nullptr;
   std::vector<Tree> trees;
-  // device staging (grown on demand)
-  struct Buf {
+  struct Buf {  // device memory, grown on demand
     void* d = nullptr;
     size_t bytes = 0;
   };
-  Buf items, offsets, acc, pacc, threats, t_off, minfo, m_off, rule, wdl, q, logits, ws, ws_eval;
-  // pinned host staging of a round's leaf inputs and results (grown on demand)
-  struct HostBuf {
+  struct HostBuf {  // pinned host memory, grown on demand
     void* h = nullptr;
     size_t bytes = 0;
   };
-  HostBuf h_items, h_off, h_threats, h_toff, h_minfo, h_moff, h_rule, h_wdl, h_q, h_logits;
-  // seconds spent in the last search: selection + leaf preparation on the
-  // host, leaf inputs + GPU evaluation + copies, finalisation + backup
+  // One in-flight GPU batch: the trees are split in two halves whose rounds
+  // alternate, so one half's selection runs while the other's leaves are on
+  // the GPU.  Each slot has its own device buffers (one workspace per
+  // evaluation call, so that each call's status word is read), pinned
+  // staging and a completion event.
+  struct Slot {
+    Buf items, offsets, acc, pacc, threats, t_off, minfo, m_off, rule, wdl, q, logits, ws_trunk, ws_policy, ws_eval;
+    HostBuf h_items, h_off, h_threats, h_toff, h_minfo, h_moff, h_rule, h_wdl, h_q, h_logits, h_status;
+    cudaEvent_t done = nullptr;
+    std::vector<uint32_t> ids;  // the trees whose leaves are in this batch
+    bool in_flight = false;
+  };
+  Slot slot[2];
+  // seconds spent in the last search: selection and leaf inputs; batch
+  // assembly and launch; waiting for the GPU; finalisation and backup
   double t_select = 0, t_inputs = 0, t_gpu = 0, t_finalize = 0;
   uint64_t rounds = 0;
   ~cnnue_mcts() {
-    for (Buf* b : {&items, &offsets, &acc, &pacc, &threats, &t_off, &minfo, &m_off, &rule, &wdl, &q, &logits, &ws,
-                   &ws_eval})
-      if (b->d) cudaFree(b->d);
-    for (HostBuf* b : {&h_items, &h_off, &h_threats, &h_toff, &h_minfo, &h_moff, &h_rule, &h_wdl, &h_q, &h_logits})
-      if (b->h) cudaFreeHost(b->h);
+    for (Slot& sl : slot) {
+      if (sl.in_flight && sl.done) cudaEventSynchronize(sl.done);
+      for (Buf* b : {&sl.items, &sl.offsets, &sl.acc, &sl.pacc, &sl.threats, &sl.t_off, &sl.minfo, &sl.m_off, &sl.rule,
+                     &sl.wdl, &sl.q, &sl.logits, &sl.ws_trunk, &sl.ws_policy, &sl.ws_eval})
+        if (b->d) cudaFree(b->d);
+      for (HostBuf* b : {&sl.h_items, &sl.h_off, &sl.h_threats, &sl.h_toff, &sl.h_minfo, &sl.h_moff, &sl.h_rule,
+                         &sl.h_wdl, &sl.h_q, &sl.h_logits, &sl.h_status})
+        if (b->h) cudaFreeHost(b->h);
+      if (sl.done) cudaEventDestroy(sl.done);
+    }
     delete pool;
   }
 };
@@ -824,16 +838,27 @@ inline double now_s() {
   return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
 
-int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t stream) {
+// The kernel status word of a workspace (as cnnue_read_status decodes it).
+int decode_status(uint32_t word) {
+  if (word & CNNUE_STATUS_BAD_OFFSETS) return CNNUE_ERR_BAD_OFFSETS;
+  if (word & CNNUE_STATUS_BAD_INDEX) return CNNUE_ERR_BAD_INDEX;
+  if (word & CNNUE_STATUS_TIMEOUT) return CNNUE_ERR_TIMEOUT;
+  return word != 0 ? CNNUE_ERR_INTERNAL : CNNUE_OK;
+}
+
+// Assembles the pending leaves of trees sl.ids into one batch (CSR arrays in
+// the slot's pinned buffers) and queues its copies, the evaluation kernels,
+// the copies back and the status words on `stream`, then the slot's event.
+int launch_round(cnnue_mcts* s, cnnue_mcts::Slot& sl, cudaStream_t stream) {
+  const std::vector<uint32_t>& ids = sl.ids;
   const int64_t n = (int64_t)ids.size();
   if (n == 0) return CNNUE_OK;
   const double t0 = now_s();
   // (each leaf's inputs were computed when it became pending)
-  // CSR layout, in pinned staging buffers
   uint32_t *off, *toff, *moff;
-  MCTS_TRY(grow_host(s->h_off, n + 1, &off));
-  MCTS_TRY(grow_host(s->h_toff, n + 1, &toff));
-  MCTS_TRY(grow_host(s->h_moff, n + 1, &moff));
+  MCTS_TRY(grow_host(sl.h_off, n + 1, &off));
+  MCTS_TRY(grow_host(sl.h_toff, n + 1, &toff));
+  MCTS_TRY(grow_host(sl.h_moff, n + 1, &moff));
   off[0] = toff[0] = moff[0] = 0;
   for (int64_t k = 0; k < n; ++k) {
     const Tree& t = s->trees[ids[k]];
@@ -843,12 +868,17 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
   }
   const size_t n_items = std::max<uint32_t>(off[n], 1), n_threats = std::max<uint32_t>(toff[n], 1);
   const size_t n_minfo = 2 * (size_t)std::max<uint32_t>(moff[n], 1), n_rule = (size_t)n * CNNUE_AZ_RULE_CONTEXT;
-  uint32_t *items, *threats, *minfo;
-  float* rule;
-  MCTS_TRY(grow_host(s->h_items, n_items, &items));
-  MCTS_TRY(grow_host(s->h_threats, n_threats, &threats));
-  MCTS_TRY(grow_host(s->h_minfo, n_minfo, &minfo));
-  MCTS_TRY(grow_host(s->h_rule, n_rule, &rule));
+  const size_t n_logits = std::max<uint32_t>(moff[n], 1), n_off = (size_t)n + 1;
+  uint32_t *items, *threats, *minfo, *status;
+  float *rule, *wdl, *q, *logits;
+  MCTS_TRY(grow_host(sl.h_items, n_items, &items));
+  MCTS_TRY(grow_host(sl.h_threats, n_threats, &threats));
+  MCTS_TRY(grow_host(sl.h_minfo, n_minfo, &minfo));
+  MCTS_TRY(grow_host(sl.h_rule, n_rule, &rule));
+  MCTS_TRY(grow_host(sl.h_wdl, (size_t)n * 3, &wdl));
+  MCTS_TRY(grow_host(sl.h_q, (size_t)n, &q));
+  MCTS_TRY(grow_host(sl.h_logits, n_logits, &logits));
+  MCTS_TRY(grow_host(sl.h_status, 3, &status));
   const int64_t chunk = 256;
   s->pool->run((n + chunk - 1) / chunk, [&](int64_t c) {
     for (int64_t k = c * chunk; k < std::min(n, (c + 1) * chunk); ++k) {
@@ -859,64 +889,77 @@ int evaluate_round(cnnue_mcts* s, const std::vector<uint32_t>& ids, cudaStream_t
       std::copy(t.rule, t.rule + CNNUE_AZ_RULE_CONTEXT, rule + k * CNNUE_AZ_RULE_CONTEXT);
     }
   });
-  const double t1 = now_s();
   const size_t ev_ws = cnnue_az_evaluate_workspace_bytes(s->model, n);
-  const size_t n_off = (size_t)n + 1;
-  MCTS_TRY(grow(s->items, n_items * 4));
-  MCTS_TRY(grow(s->offsets, n_off * 4));
-  MCTS_TRY(grow(s->acc, (size_t)n * s->hidden * 4));
-  MCTS_TRY(grow(s->pacc, (size_t)n * 32 * 2));
-  MCTS_TRY(grow(s->threats, n_threats * 4));
-  MCTS_TRY(grow(s->t_off, n_off * 4));
-  MCTS_TRY(grow(s->minfo, n_minfo * 4));
-  MCTS_TRY(grow(s->m_off, n_off * 4));
-  MCTS_TRY(grow(s->rule, n_rule * 4));
-  MCTS_TRY(grow(s->wdl, (size_t)n * 12));
-  MCTS_TRY(grow(s->q, (size_t)n * 4));
-  MCTS_TRY(grow(s->logits, (size_t)std::max<uint32_t>(moff[n], 1) * 4));
-  MCTS_TRY(grow(s->ws, cnnue_az_workspace_bytes()));
-  MCTS_TRY(grow(s->ws_eval, ev_ws));
-  MCTS_CUDA(cudaMemcpyAsync(s->items.d, items, n_items * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->offsets.d, off, n_off * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->threats.d, threats, n_threats * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->t_off.d, toff, n_off * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->minfo.d, minfo, n_minfo * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->m_off.d, moff, n_off * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemcpyAsync(s->rule.d, rule, n_rule * 4, cudaMemcpyHostToDevice, stream));
-  MCTS_CUDA(cudaMemsetAsync(s->ws.d, 0, s->ws.bytes, stream));
-  MCTS_TRY(cnnue_az_refresh(s->model, (const uint32_t*)s->items.d, off[n], (const uint32_t*)s->offsets.d, n,
-                            (float*)s->acc.d, s->ws.d, s->ws.bytes, stream));
-  MCTS_TRY(cnnue_az_policy_refresh(s->model, (const uint32_t*)s->items.d, off[n], (const uint32_t*)s->offsets.d, n,
-                                   (int16_t*)s->pacc.d, s->ws.d, s->ws.bytes, stream));
-  MCTS_TRY(cnnue_az_evaluate(s->model, (const float*)s->acc.d, nullptr, (const float*)s->rule.d,
-                             s->threat_active ? (const uint32_t*)s->threats.d : nullptr, toff[n],
-                             s->threat_active ? (const uint32_t*)s->t_off.d : nullptr, (const int16_t*)s->pacc.d,
-                             (const uint32_t*)s->minfo.d, moff[n], (const uint32_t*)s->m_off.d, n, (float*)s->wdl.d,
-                             (float*)s->q.d, (float*)s->logits.d, s->ws_eval.d, s->ws_eval.bytes, stream));
-  const size_t n_logits = std::max<uint32_t>(moff[n], 1);
-  float *wdl, *q, *logits;
-  MCTS_TRY(grow_host(s->h_wdl, (size_t)n * 3, &wdl));
-  MCTS_TRY(grow_host(s->h_q, (size_t)n, &q));
-  MCTS_TRY(grow_host(s->h_logits, n_logits, &logits));
-  MCTS_CUDA(cudaMemcpyAsync(wdl, s->wdl.d, (size_t)n * 3 * 4, cudaMemcpyDeviceToHost, stream));
-  MCTS_CUDA(cudaMemcpyAsync(q, s->q.d, (size_t)n * 4, cudaMemcpyDeviceToHost, stream));
-  MCTS_CUDA(cudaMemcpyAsync(logits, s->logits.d, n_logits * 4, cudaMemcpyDeviceToHost, stream));
-  int status = CNNUE_OK;
-  MCTS_TRY(cnnue_read_status(s->ws.d, stream, &status));
-  if (status != CNNUE_OK) return set_error(status, "leaf evaluation reported bad input");
-  MCTS_TRY(cnnue_read_status(s->ws_eval.d, stream, &status));
-  if (status != CNNUE_OK) return set_error(status, "leaf evaluation reported bad input");
-  const double t2 = now_s();
+  MCTS_TRY(grow(sl.items, n_items * 4));
+  MCTS_TRY(grow(sl.offsets, n_off * 4));
+  MCTS_TRY(grow(sl.acc, (size_t)n * s->hidden * 4));
+  MCTS_TRY(grow(sl.pacc, (size_t)n * 32 * 2));
+  MCTS_TRY(grow(sl.threats, n_threats * 4));
+  MCTS_TRY(grow(sl.t_off, n_off * 4));
+  MCTS_TRY(grow(sl.minfo, n_minfo * 4));
+  MCTS_TRY(grow(sl.m_off, n_off * 4));
+  MCTS_TRY(grow(sl.rule, n_rule * 4));
+  MCTS_TRY(grow(sl.wdl, (size_t)n * 12));
+  MCTS_TRY(grow(sl.q, (size_t)n * 4));
+  MCTS_TRY(grow(sl.logits, n_logits * 4));
+  MCTS_TRY(grow(sl.ws_trunk, cnnue_az_workspace_bytes()));
+  MCTS_TRY(grow(sl.ws_policy, cnnue_az_workspace_bytes()));
+  MCTS_TRY(grow(sl.ws_eval, ev_ws));
+  if (!sl.done) MCTS_CUDA(cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming));
+  MCTS_CUDA(cudaMemcpyAsync(sl.items.d, items, n_items * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.offsets.d, off, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.threats.d, threats, n_threats * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.t_off.d, toff, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.minfo.d, minfo, n_minfo * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.m_off.d, moff, n_off * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemcpyAsync(sl.rule.d, rule, n_rule * 4, cudaMemcpyHostToDevice, stream));
+  MCTS_CUDA(cudaMemsetAsync(sl.ws_trunk.d, 0, sl.ws_trunk.bytes, stream));
+  MCTS_CUDA(cudaMemsetAsync(sl.ws_policy.d, 0, sl.ws_policy.bytes, stream));
+  MCTS_TRY(cnnue_az_refresh(s->model, (const uint32_t*)sl.items.d, off[n], (const uint32_t*)sl.offsets.d, n,
+                            (float*)sl.acc.d, sl.ws_trunk.d, sl.ws_trunk.bytes, stream));
+  MCTS_TRY(cnnue_az_policy_refresh(s->model, (const uint32_t*)sl.items.d, off[n], (const uint32_t*)sl.offsets.d, n,
+                                   (int16_t*)sl.pacc.d, sl.ws_policy.d, sl.ws_policy.bytes, stream));
+  MCTS_TRY(cnnue_az_evaluate(s->model, (const float*)sl.acc.d, nullptr, (const float*)sl.rule.d,
+                             s->threat_active ? (const uint32_t*)sl.threats.d : nullptr, toff[n],
+                             s->threat_active ? (const uint32_t*)sl.t_off.d : nullptr, (const int16_t*)sl.pacc.d,
+                             (const uint32_t*)sl.minfo.d, moff[n], (const uint32_t*)sl.m_off.d, n, (float*)sl.wdl.d,
+                             (float*)sl.q.d, (float*)sl.logits.d, sl.ws_eval.d, sl.ws_eval.bytes, stream));
+  MCTS_CUDA(cudaMemcpyAsync(wdl, sl.wdl.d, (size_t)n * 3 * 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(q, sl.q.d, (size_t)n * 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(logits, sl.logits.d, n_logits * 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(status, sl.ws_trunk.d, 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(status + 1, sl.ws_policy.d, 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaMemcpyAsync(status + 2, sl.ws_eval.d, 4, cudaMemcpyDeviceToHost, stream));
+  MCTS_CUDA(cudaEventRecord(sl.done, stream));
+  sl.in_flight = true;
+  s->t_inputs += now_s() - t0;
+  s->rounds += 1;
+  return CNNUE_OK;
+}
+
+// Waits for the slot's batch, checks its status words and finalises its
+// leaves (priors, backup, forced replies).
+int complete_round(cnnue_mcts* s, cnnue_mcts::Slot& sl) {
+  if (!sl.in_flight) return CNNUE_OK;
+  const double t0 = now_s();
+  sl.in_flight = false;
+  MCTS_CUDA(cudaEventSynchronize(sl.done));
+  const uint32_t* status = static_cast<const uint32_t*>(sl.h_status.h);
+  for (int k = 0; k < 3; ++k)
+    if (int st = decode_status(status[k])) return set_error(st, "leaf evaluation reported bad input");
+  const double t1 = now_s();
+  const int64_t n = (int64_t)sl.ids.size();
+  const float* wdl = static_cast<const float*>(sl.h_wdl.h);
+  const float* q = static_cast<const float*>(sl.h_q.h);
+  const float* logits = static_cast<const float*>(sl.h_logits.h);
+  const uint32_t* moff = static_cast<const uint32_t*>(sl.h_moff.h);
   s->pool->run(n, [&](int64_t k) {
-    Tree& t = s->trees[ids[k]];
+    Tree& t = s->trees[sl.ids[k]];
     Eval e{{wdl[k * 3], wdl[k * 3 + 1], wdl[k * 3 + 2]}, q[k]};
     t.finalize(e, logits + moff[k]);
   });
-  const double t3 = now_s();
-  s->t_inputs += t1 - t0;
-  s->t_gpu += t2 - t1;
-  s->t_finalize += t3 - t2;
-  s->rounds += 1;
+  s->t_gpu += t1 - t0;
+  s->t_finalize += now_s() - t1;
   return CNNUE_OK;
 }
 
@@ -1018,43 +1061,67 @@ int search_on_device(cnnue_mcts* s, const int8_t* boards, const uint8_t* sides, 
   uint64_t evals = 0;
   s->t_select = s->t_inputs = s->t_gpu = s->t_finalize = 0;
   s->rounds = 0;
+  for (cnnue_mcts::Slot& sl : s->slot) {  // a batch left by a failed search
+    if (sl.in_flight) cudaEventSynchronize(sl.done);
+    sl.in_flight = false;
+  }
   // every root is expanded first, in one batch (tree.expand(root), :440-445)
   {
+    const double ts = now_s();
     s->pool->run(n_roots, [&](int64_t i) {
       Tree& t = s->trees[i];
       if (t.lim.simulations <= 0) return;
       t.start_root();
       if (t.has_pending) t.leaf_inputs(s->threat_active);
     });
-    std::vector<uint32_t> ids;
+    cnnue_mcts::Slot& sl = s->slot[0];
+    sl.ids.clear();
     for (int64_t i = 0; i < n_roots; ++i)
-      if (s->trees[i].has_pending) ids.push_back((uint32_t)i);
-    evals += ids.size();
-    MCTS_TRY(evaluate_round(s, ids, st));
-  }
-  for (;;) {
-    const double ts = now_s();
-    s->pool->run(n_roots, [&](int64_t i) {
-      Tree& t = s->trees[i];
-      while (!t.has_pending && t.completed < (uint64_t)t.lim.simulations) {
-        if (!t.has_active) {  // a new simulation from the root
-          t.active.node = t.active.depth = 0;
-          t.active.path.clear();
-        }
-        t.has_active = false;
-        if (t.prepare(t.active)) {
-          t.leaf_inputs(s->threat_active);
-          break;
-        }
-      }
-    });
-    std::vector<uint32_t> ids;
-    for (int64_t i = 0; i < n_roots; ++i)
-      if (s->trees[i].has_pending) ids.push_back((uint32_t)i);
+      if (s->trees[i].has_pending) sl.ids.push_back((uint32_t)i);
     s->t_select += now_s() - ts;
-    if (ids.empty()) break;
-    evals += ids.size();
-    MCTS_TRY(evaluate_round(s, ids, st));
+    evals += sl.ids.size();
+    MCTS_TRY(launch_round(s, sl, st));
+    MCTS_TRY(complete_round(s, sl));
+  }
+  // Then rounds alternate between the two halves of the roots: finalise a
+  // half's last batch, run its selection (each tree to its next leaf) and
+  // launch its new batch, which the GPU runs while the other half does the
+  // same.  Trees are independent, so each tree's search is the same as in
+  // one batch of all roots.
+  const int64_t bounds[3] = {0, n_roots / 2, n_roots};
+  bool live[2] = {true, true};
+  while (live[0] || live[1]) {
+    for (int h = 0; h < 2; ++h) {
+      if (!live[h]) continue;
+      cnnue_mcts::Slot& sl = s->slot[h];
+      MCTS_TRY(complete_round(s, sl));
+      const double ts = now_s();
+      const int64_t lo = bounds[h], hi = bounds[h + 1];
+      s->pool->run(hi - lo, [&](int64_t k) {
+        Tree& t = s->trees[lo + k];
+        while (!t.has_pending && t.completed < (uint64_t)t.lim.simulations) {
+          if (!t.has_active) {  // a new simulation from the root
+            t.active.node = t.active.depth = 0;
+            t.active.path.clear();
+          }
+          t.has_active = false;
+          if (t.prepare(t.active)) {
+            t.leaf_inputs(s->threat_active);
+            break;
+          }
+        }
+      });
+      sl.ids.clear();
+      for (int64_t i = lo; i < hi; ++i)
+        if (s->trees[i].has_pending) sl.ids.push_back((uint32_t)i);
+      s->t_select += now_s() - ts;
+      if (sl.ids.empty()) {
+        live[h] = false;
+        continue;
+      }
+      evals += sl.ids.size();
+      MCTS_TRY(launch_round(s, sl, st));
+    }
   }
   if (n_evaluations) *n_evaluations = evals;
   return CNNUE_OK;

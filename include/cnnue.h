@@ -806,9 +806,11 @@ int cnnue_mcts_search(cnnue_mcts* search, const int8_t* boards, const uint8_t* s
                       void* stream, uint64_t* n_evaluations);
 /* Wall-clock seconds of the last search by phase: seconds[0] selection and
  * leaf preparation (legal moves, and each new leaf's network inputs:
- * features, threats, move records), [1] assembly of the round's batch in
- * pinned host buffers, [2] GPU evaluation with its copies, [3] finalisation
- * and backup; *rounds (optional) the number of GPU batches. */
+ * features, threats, move records), [1] assembly and launch of the batches
+ * (pinned host buffers, copies, kernels), [2] waiting for a batch's GPU
+ * evaluation (the roots are split in two halves whose batches alternate, so
+ * the GPU mostly runs while the other half is being selected), [3]
+ * finalisation and backup; *rounds (optional) the number of GPU batches. */
 int cnnue_mcts_stats(const cnnue_mcts* search, double* seconds, uint64_t* rounds);
 /* Root statistics of the last search: per root move (from/to pairs) its
  * visits, prior and Q (root player's view), the index of the best move

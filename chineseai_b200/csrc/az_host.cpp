@@ -118,19 +118,21 @@ inline uint32_t feature_of(int v, int sq, int perspective) {
   return (uint32_t)(piece_index * kSq + canonical_square(perspective, sq));
 }
 
+// The last square in scan order holding the general of `color` (piece code
+// +1 Red, -1 Black), -1 if none: a branch-free scan.
+inline int last_general(const int8_t* board, int color) {
+  const int8_t code = color == 0 ? 1 : -1;
+  int g = -1;
+  for (int sq = 0; sq < kSq; ++sq) g = board[sq] == code ? sq : g;
+  return g;
+}
+
 // (us, them) buckets of a board for a perspective: the last general of each
 // side in scan order, 4 when absent (canonical_general_buckets_from_features).
 void buckets_of(const int8_t* board, int perspective, int* us, int* them) {
-  *us = 4;
-  *them = 4;
-  for (int sq = 0; sq < kSq; ++sq) {
-    const int v = board[sq];
-    if (v == 0 || (v > 0 ? v : -v) != 1) continue;
-    const uint32_t f = feature_of(v, sq, perspective);
-    const int piece_index = (int)f / kSq, csq = (int)f % kSq;
-    if (piece_index == 0) *us = general_bucket(0, csq);
-    if (piece_index == 7) *them = general_bucket(7, csq);
-  }
+  const int own = last_general(board, perspective), enemy = last_general(board, 1 - perspective);
+  *us = own < 0 ? 4 : general_bucket(0, canonical_square(perspective, own));
+  *them = enemy < 0 ? 4 : general_bucket(7, canonical_square(perspective, enemy));
 }
 
 inline uint32_t pack(uint32_t feature, int us, int them) {
@@ -725,21 +727,16 @@ inline int kind_of(int v) { return (v > 0 ? v : -v) - 1; }
 inline bool on_board(int f, int r) { return f >= 0 && f < 9 && r >= 0 && r < 10; }
 inline bool palace(int color, int f, int r) { return f >= 3 && f <= 5 && (color == 0 ? r >= 7 : r <= 2); }
 
-int general_of(const int8_t* b, int color) {
-  int g = -1;
-  for (int sq = 0; sq < kSq; ++sq)
-    if (b[sq] != 0 && kind_of(b[sq]) == 0 && color_of(b[sq]) == color) g = sq;  // last in scan order
-  return g;
-}
+int general_of(const int8_t* b, int color) { return last_general(b, color); }  // last in scan order
 
 // Position::attacked_squares_mask (src/xiangqi/mod.rs:391-484) as a 90-entry
 // flag array: squares attacked by `by`, empty or not.
-void attacked_squares(const int8_t* b, int by, uint8_t* mask) {
+// enemy_general: general_of(b, 1 - by).
+void attacked_squares(const int8_t* b, int by, uint8_t* mask, int enemy_general) {
   std::memset(mask, 0, kSq);
   auto mark = [&](int f, int r) {
     if (on_board(f, r)) mask[r * 9 + f] = 1;
   };
-  const int enemy_general = general_of(b, 1 - by);
   for (int sq = 0; sq < kSq; ++sq) {
     const int v = b[sq];
     if (v == 0 || color_of(v) != by) continue;
@@ -988,9 +985,9 @@ void pack_row(const cnnue_az_samples* s, int64_t sample, int64_t row, const RowD
   int bf[kSq];
   sample_board(f, nf, board, bf);
   uint8_t opp[kSq], own[kSq];
-  attacked_squares(board, 1, opp);
-  attacked_squares(board, 0, own);
   const int enemy_general = general_of(board, 1);
+  attacked_squares(board, 1, opp, general_of(board, 0));
+  attacked_squares(board, 0, own, enemy_general);
   const auto& moves = dense_moves();
   const bool compact = o->policy_sparse_indices == nullptr;
   int64_t* items = o->policy_items + row * M;
@@ -1127,11 +1124,11 @@ int cnnue_az_policy_moves(const int8_t* board, int side, const uint8_t* moves, i
     return v;
   }();
   uint8_t opp[kSq], own[kSq];
-  attacked_squares(board, 1 - side, opp);
-  attacked_squares(board, side, own);
+  const int enemy_general = general_of(board, 1 - side);
+  attacked_squares(board, 1 - side, opp, general_of(board, side));
+  attacked_squares(board, side, own, enemy_general);
   int us, them;
   buckets_of(board, side, &us, &them);
-  const int enemy_general = general_of(board, 1 - side);
   int status = CNNUE_OK;
   for (int i = 0; i < n_moves; ++i) {
     const int from = moves[2 * i], to = moves[2 * i + 1];

@@ -64,10 +64,13 @@ inline bool is(const int8_t* b, int f, int r, int color, int kind) {
   return v != 0 && color_of(v) == color && kind_of(v) == kind;
 }
 
+// The first square in scan order holding the general of `color` (piece code
+// +1 Red, -1 Black), -1 if none: a branch-free scan from the end.
 int general_square(const int8_t* b, int color) {
-  for (int sq = 0; sq < kSq; ++sq)
-    if (b[sq] != 0 && color_of(b[sq]) == color && kind_of(b[sq]) == 0) return sq;
-  return -1;
+  const int8_t code = color == 0 ? 1 : -1;
+  int g = -1;
+  for (int sq = kSq - 1; sq >= 0; --sq) g = b[sq] == code ? sq : g;
+  return g;
 }
 
 // Is `sq` attacked by `by` (the general attacks along an open file: the

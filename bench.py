@@ -781,7 +781,7 @@ def run_fp32(args):
             "e2e": {"value": world * F32_BATCH / (e2e_total / args.steps / 1e3), "unit": "evals/s",
                     "h2d_bytes_per_step": int(pos.indices.nbytes + pos.offsets.nbytes),
                     "d2h_bytes_per_step": F32_BATCH * 4},
-            "clocks": clocks, "gpu_launches": args.steps,
+            "clocks": clocks, "gpu_launches": 2 * args.steps,  # f_gather_kernel + f_stack_kernel
         }
         if not args.no_cpu_baseline:
             import oracle

@@ -1093,8 +1093,8 @@ def run_mcts(args):
     search = mcts.Search(model, w)
     lim = mcts.default_limits(MCTS_SIMS)
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(1, args.warmup // 3)):
-        search.run(boards[:256], sides[:256], lim, stream=stream.cuda_stream)
+    for _ in range(max(1, args.warmup // 3)):  # the timed shape: trees and buffers reach their size here
+        search.run(boards, sides, lim, stream=stream.cuda_stream)
     sampler = ClockSampler(local)
     if pg:
         pg.barrier()

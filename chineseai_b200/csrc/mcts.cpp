@@ -253,11 +253,59 @@ int count_checkers(const int8_t* b, int g, int by) {
 //
 // The attack test runs on the board with the move made in place (and then
 // unmade).  When the side is not in check, a move by another piece can only
-// expose its general if it leaves or enters the general's rank or file
-// (rook, cannon screen, facing generals) or leaves one of the general's four
-// diagonal neighbours (the leg of a horse aimed at it): soldiers need no open
-// path, and the enemy advisors and elephants never reach this palace.  Such
-// moves are legal without the test.
+// create an attack on its general (1) along a rank or file through the
+// general that the move leaves or enters (rook, facing general, cannon
+// screen) or (2) by leaving one of the general's four diagonal neighbours
+// (the leg of a horse or the eye of an elephant aimed at it): soldiers and
+// advisors need no open path, and the move removes no blocker elsewhere.
+// Moves of neither kind are legal without a test; moves of kind (1) only
+// rescan the one or two rays they touch (ray_attacked, the same rule as
+// square_attacked's orthogonal part), kind (2) and the general's own moves
+// take the full test.
+
+// Is the general on `g` attacked along direction d by `by`, on the board with
+// `moving` moved from `from` to `to`?
+bool ray_attacked(const int8_t* b, int g, int df, int dr, int from, int to, int moving, int by) {
+  const int f = g % 9, r = g / 9;
+  int tf = f + df, tr = r + dr, seen = 0;
+  while (on_board(tf, tr)) {
+    const int sq = tr * 9 + tf;
+    const int v = sq == from ? 0 : (sq == to ? moving : (int)b[sq]);
+    if (v != 0) {
+      const bool mine = color_of(v) == by;
+      if (seen == 0) {
+        if (mine && kind_of(v) == 4) return true;                   // rook
+        if (mine && kind_of(v) == 0 && df == 0) return true;        // facing general
+        if (mine && kind_of(v) == 0 && (std::abs(tf - f) + std::abs(tr - r)) == 1 && in_palace(by, f, r))
+          return true;                                              // general step
+      } else {
+        return mine && kind_of(v) == 5;                             // cannon over one screen
+      }
+      ++seen;
+    }
+    tf += df;
+    tr += dr;
+  }
+  return false;
+}
+
+// The direction from the general on `g` to `sq` when `sq` lies on its rank
+// or file (0 none).
+inline int ray_of(int g, int sq, int* df, int* dr) {
+  const int gf = g % 9, gr = g / 9, f = sq % 9, r = sq / 9;
+  if (f == gf && r != gr) {
+    *df = 0;
+    *dr = r > gr ? 1 : -1;
+    return 1;
+  }
+  if (r == gr && f != gf) {
+    *df = f > gf ? 1 : -1;
+    *dr = 0;
+    return 1;
+  }
+  return 0;
+}
+
 void legal_moves(const int8_t* b, int side, std::vector<Move>& pseudo, std::vector<Move>& out) {
   pseudo_moves(b, side, pseudo);
   const int king = general_square(b, side);
@@ -270,13 +318,18 @@ void legal_moves(const int8_t* b, int side, std::vector<Move>& pseudo, std::vect
     return;
   }
   const int kf = king % 9, kr = king / 9;
-  auto on_lines = [&](int sq) { return sq % 9 == kf || sq / 9 == kr; };
   auto leg = [&](int sq) { return std::abs(sq % 9 - kf) == 1 && std::abs(sq / 9 - kr) == 1; };
   int8_t c[kSq];
   std::memcpy(c, b, kSq);
   for (const Move& m : pseudo) {
-    if (!check && m.from != king && !on_lines(m.from) && !on_lines(m.to) && !leg(m.from)) {
-      out.push_back(m);
+    if (!check && m.from != king && !leg(m.from)) {
+      int df0, dr0, df1, dr1;
+      const int on0 = ray_of(king, m.from, &df0, &dr0), on1 = ray_of(king, m.to, &df1, &dr1);
+      const int moving = b[m.from];
+      const bool hit = (on0 && ray_attacked(b, king, df0, dr0, m.from, m.to, moving, 1 - side)) ||
+                       (on1 && (!on0 || df1 != df0 || dr1 != dr0) &&
+                        ray_attacked(b, king, df1, dr1, m.from, m.to, moving, 1 - side));
+      if (!hit) out.push_back(m);
       continue;
     }
     const int8_t moving = c[m.from], captured = c[m.to];

@@ -1,6 +1,7 @@
 // f_forward.cu - fp32 HalfKA NNUE evaluation on sm_100a.
 //
-// Two launches per batch (after the status word is cleared):
+// Two launches per batch (after the status word is cleared; the second is a
+// programmatic dependent launch that stages its weights during the first's tail):
 //   1. f_gather_kernel (which also checks every list's offsets: monotone,
 //      within the index array): one warp per (position, perspective) list, lane l
 //      owning FT columns [4l, 4l + 4) and [128 + 4l, 128 + 4l + 4) (two
@@ -70,6 +71,9 @@ __device__ __forceinline__ float4 clamp01(float4 v) {
 }
 
 __global__ void __launch_bounds__(kWarps * 32) f_gather_kernel(const Args a) {
+  // the stack kernel may be scheduled now: it stages its weights, then waits
+  // for this grid to complete before reading x
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * kWarps;
   const char* ft = (const char*)a.w.ft + lane * 16;
@@ -128,6 +132,9 @@ __global__ void __launch_bounds__(kWarps * 32) f_stack_kernel(const Args a) {
   for (int q = 0; q < 4; ++q) w2[q] = __ldg((const float4*)(a.w.l2w + ((size_t)b * 32 + lane) * 16) + q);
   const float b2v = __ldg(a.w.l2b + b * 32 + lane), w3v = __ldg(a.w.l3w + b * 32 + lane), b3v = __ldg(a.w.l3b + b);
   __syncthreads();
+  // launched as a programmatic dependent of f_gather_kernel: x is complete
+  // (and visible) only after this wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   // this warp's contiguous share of the batch, scanned 32 positions at a time
   const int64_t wid = (int64_t)part * kWarps + warp, nw = (int64_t)parts * kWarps;
   const int64_t p_begin = a.n * wid / nw, p_end = a.n * (wid + 1) / nw;
@@ -303,7 +310,17 @@ int cnnue_f_forward(const cnnue_f_model* m, const uint16_t* d_idx, uint32_t n_id
   // parts per bucket: about 4 positions per warp, at most 4 CTAs per SM overall
   const int64_t parts = std::max<int64_t>(1, std::min<int64_t>((n + kNB * kWarps * 4 - 1) / (kNB * kWarps * 4),
                                                               (int64_t)m->sms * 4 / kNB));
-  f_stack_kernel<<<(unsigned)(kNB * parts), kWarps * 32, 0, s>>>(a);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(kNB * parts));
+  cfg.blockDim = dim3(kWarps * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, f_stack_kernel, a);
+  if (e != cudaSuccess) return cuda_error(e, "cudaLaunchKernelEx(f_stack_kernel)");
   return check_launch_error("f_stack_kernel");
 }
 

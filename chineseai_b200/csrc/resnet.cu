@@ -28,7 +28,7 @@
 //
 // Heads, fp32 on CUDA cores: rn_head_conv_kernel (1x1 convs to 2 policy and
 // 1 value planes, a warp per trunk row), rn_value_kernel (value FC 90 -> 256
-// -> 1 with tanh, 32 boards per CTA), rn_policy_fc_kernel (FC 180 -> 2086 as
+// -> 1 with tanh, 8 boards per CTA), rn_policy_fc_kernel (FC 180 -> 2086 as
 // a tiled GEMM, 128 boards x 128 moves per CTA), rn_softmax_kernel (one warp
 // per board).
 #include <cuda.h>
@@ -868,10 +868,10 @@ __global__ void __launch_bounds__(256) rn_head_conv_kernel(HeadArgs a, float* __
   }
 }
 
-// Value MLP 90 -> 256 (ReLU) -> 1 (tanh) for 32 boards per CTA: thread j is
-// hidden unit j for all 32 boards (the value plane of the 32 boards staged in
+// Value MLP 90 -> 256 (ReLU) -> 1 (tanh) for 8 boards per CTA: thread j is
+// hidden unit j for all 8 boards (the value plane of the 8 boards staged in
 // shared memory, read as broadcasts); the 256 -> 1 layer is a block reduction.
-constexpr int kValueBoards = 32;
+constexpr int kValueBoards = 8;
 __global__ void __launch_bounds__(256) rn_value_kernel(HeadArgs a, const float* __restrict__ vc_t) {
   __shared__ __align__(16) float vc[kSq][kValueBoards];
   __shared__ float red[kValueBoards][8];

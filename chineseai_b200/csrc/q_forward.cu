@@ -95,7 +95,7 @@ struct ForwardArgs {
 
 // ===========================================================================
 // Fused evaluation kernel.  One CTA: 4 consumer warps evaluating one
-// position at a time and kProducers producer warps that copy every FT row
+// position at a time and 4 (forward) or 2 (update) producer warps that copy every FT row
 // (2 KB) by cp.async.bulk into a ring of kSlots shared-memory slots, so up to
 // kSlots rows per CTA are in flight without holding registers.  Every
 // consumer thread t owns the 16-byte column chunk t of every row (both
@@ -107,11 +107,18 @@ struct ForwardArgs {
 constexpr int kStageRows = 8;                    // rows per pipeline stage
 constexpr int kStages = 6;                       // stages in the ring
 constexpr int kSlots = kStages * kStageRows;     // 48 row slots, 96 KB
-constexpr int kProducers = 4;                    // producer warps (one issuing lane each)
+// Producer warps (one issuing lane each): four in the forward, whose active
+// rows fill stages fast; two in the update, where every producer walking
+// every position's bookkeeping costs the consumers issue slots (measured:
+// 0.488 -> 0.439 ms per 65,536 updates, forward unchanged).
+constexpr int kProducersEval = 4;
+constexpr int kProducersUpdate = 2;
+constexpr int producers_of(bool update) { return update ? kProducersUpdate : kProducersEval; }
 constexpr int kPrefetch = 4;                     // positions of index lists loaded ahead
-static_assert(kProducers <= kStages, "parity waits on the empty barriers need kProducers <= kStages");
+static_assert(kProducersEval <= kStages && kProducersUpdate <= kStages,
+              "parity waits on the empty barriers need producers <= kStages");
 constexpr int kBulkConsumers = 128;
-constexpr int kBulkThreads = kBulkConsumers + 32 * kProducers;
+constexpr int bulk_threads(bool update) { return kBulkConsumers + 32 * producers_of(update); }
 constexpr int kBulkMinBlocks = 2;
 
 struct BulkSmem {
@@ -162,6 +169,58 @@ __device__ __forceinline__ PosDesc load_desc(const ForwardArgs& a, int64_t i) {
   return d;
 }
 
+// The consumers' descriptor of the next position, in two halves so that its
+// global loads overlap a position's work: load_raw issues every load (the
+// removed-list offsets unconditionally: they exist for every list), and
+// finish_desc clamps as load_desc does, once the values have arrived.
+struct RawDesc {
+  uint32_t pos;
+  int bucket;
+  uint32_t o[2][2], ro[2][2];
+  uint8_t fl[2];
+};
+
+template <bool kUpdate>
+__device__ __forceinline__ RawDesc load_raw(const ForwardArgs& a, uint32_t pos, int bucket) {
+  RawDesc r;
+  r.pos = pos;
+  r.bucket = bucket;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int64_t ps = 2 * (int64_t)pos + p;
+    r.o[p][0] = a.offsets[ps];
+    r.o[p][1] = a.offsets[ps + 1];
+    if (kUpdate) {
+      r.fl[p] = a.flags[ps];
+      r.ro[p][0] = a.rem_offsets[ps];
+      r.ro[p][1] = a.rem_offsets[ps + 1];
+    }
+  }
+  return r;
+}
+
+template <bool kUpdate>
+__device__ __forceinline__ PosDesc finish_desc(const ForwardArgs& a, const RawDesc& r) {
+  PosDesc d;
+  d.pos = r.pos;
+  d.bucket = r.bucket;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const uint32_t b = min(r.o[p][0], a.n_idx);
+    d.add[p] = Seg{b, min(max(r.o[p][1], b), a.n_idx) - b};
+    if (kUpdate) {
+      const bool refresh = (r.fl[p] & 1) != 0;
+      d.init[p] = refresh ? 0u : 1u;
+      const uint32_t rb = min(r.ro[p][0], a.n_rem);
+      d.rem[p] = refresh ? Seg{0, 0} : Seg{rb, min(max(r.ro[p][1], rb), a.n_rem) - rb};
+    } else {
+      d.init[p] = 0;
+      d.rem[p] = Seg{0, 0};
+    }
+  }
+  return d;
+}
+
 __device__ __forceinline__ uint32_t desc_rows(const PosDesc& d) {
   return d.init[0] + d.rem[0].cnt + d.add[0].cnt + d.init[1] + d.rem[1].cnt + d.add[1].cnt;
 }
@@ -184,6 +243,7 @@ __device__ __forceinline__ uint32_t n_stages(uint32_t rows) {
   return (rows + kStageRows - 1) / kStageRows;
 }
 
+template <int kProducers>
 struct Producer {
   BulkSmem* sm;
   uint32_t* status;
@@ -387,7 +447,7 @@ __device__ __forceinline__ ListHead load_heads(const ForwardArgs& a, const PosDe
 }
 
 template <bool kUpdate, bool kWriteAcc>
-__global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(const ForwardArgs a) {
+__global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_kernel(const ForwardArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   BulkSmem& sm = *reinterpret_cast<BulkSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -408,7 +468,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
 
   if (warp >= kBulkConsumers / 32) {
     // ------------------------------ producers -----------------------------
-    Producer pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true};
+    Producer<producers_of(kUpdate)> pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true};
     const char* par_lo = (const char*)a.parent;
     uint32_t st_base = 0;  // stage number of the batch's first position
     for (int64_t b0 = begin; b0 < end; b0 += 32) {
@@ -458,7 +518,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
       const uint32_t first = st_base > (uint32_t)kStages ? st_base - kStages : 0u;
       const unsigned long long t0 = pipe::globaltimer();
       for (uint32_t k = first; k < st_base; ++k) {
-        if ((int)(k % kProducers) != pr.w) continue;
+        if ((int)(k % producers_of(kUpdate)) != pr.w) continue;
         while (!pipe::mbar_try_wait(&sm.full[k % kStages], (k / kStages) & 1u)) {
           if (sm.abort || pipe::globaltimer() - t0 > pipe::kWaitLimitNs) break;
         }
@@ -479,10 +539,20 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
   uint32_t st = 0;  // next stage number
   PosDesc nxt;
   if (begin < end) nxt = load_desc<kUpdate>(a, begin);
+  // position and bucket of the position after the next (loaded an iteration
+  // before its descriptor loads need them)
+  uint32_t pos_n = begin + 1 < end ? a.perm[begin + 1] : 0u;
+  int bucket_n = begin + 1 < end ? (int)a.sorted_bucket[begin + 1] : 0;
 
   for (int64_t i = begin; i < end; ++i) {
     const PosDesc d = nxt;
-    if (i + 1 < end) nxt = load_desc<kUpdate>(a, i + 1);
+    const bool has_next = i + 1 < end;
+    RawDesc raw;
+    if (has_next) raw = load_raw<kUpdate>(a, pos_n, bucket_n);
+    if (i + 2 < end) {
+      pos_n = a.perm[i + 2];
+      bucket_n = (int)a.sorted_bucket[i + 2];
+    }
     if (d.bucket != cur_bucket) {
       cur_bucket = d.bucket;
       const int8_t* w1p = a.w.l1w + (size_t)d.bucket * kL1 * kCols + 8 * t;
@@ -577,6 +647,7 @@ __global__ void __launch_bounds__(kBulkThreads, kBulkMinBlocks) q_bulk_kernel(co
       __syncwarp();
     }
     parity ^= 1;
+    if (has_next) nxt = finish_desc<kUpdate>(a, raw);
   }
 }
 
@@ -640,9 +711,9 @@ int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
   const int grid = (int)std::min<int64_t>(m->grid_eval, n);
   const size_t smem = sizeof(BulkSmem);
   if (d_acc)
-    q_bulk_kernel<false, true><<<grid, kBulkThreads, smem, s>>>(a);
+    q_bulk_kernel<false, true><<<grid, bulk_threads(false), smem, s>>>(a);
   else
-    q_bulk_kernel<false, false><<<grid, kBulkThreads, smem, s>>>(a);
+    q_bulk_kernel<false, false><<<grid, bulk_threads(false), smem, s>>>(a);
   return check_launch("q_bulk_kernel");
 }
 
@@ -719,8 +790,8 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   cudaFuncSetAttribute(q_bulk_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   cudaFuncSetAttribute(q_bulk_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   int occ_eval = 0, occ_upd = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_bulk_kernel<false, false>, kBulkThreads, smem);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_upd, q_bulk_kernel<true, true>, kBulkThreads, smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_bulk_kernel<false, false>, bulk_threads(false), smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_upd, q_bulk_kernel<true, true>, bulk_threads(true), smem);
   m->grid_eval = m->sm_count * std::max(occ_eval, 1);
   m->grid_update = m->sm_count * std::max(occ_upd, 1);
   e = cudaGetLastError();
@@ -875,7 +946,7 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
   const int grid = (int)std::min<int64_t>(m->grid_update, n);
-  q_bulk_kernel<true, true><<<grid, kBulkThreads, sizeof(BulkSmem), s>>>(a);
+  q_bulk_kernel<true, true><<<grid, bulk_threads(true), sizeof(BulkSmem), s>>>(a);
   return check_launch("q_bulk_kernel<update>");
 }
 

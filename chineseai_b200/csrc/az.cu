@@ -120,13 +120,38 @@ __device__ __forceinline__ void store_cols(float* __restrict__ row, int chunks, 
   }
 }
 
-// a += w (kSign > 0) or a -= w, one rounding per element.
+// Two independent IEEE round-to-nearest fp32 additions (subtractions) in one
+// packed instruction: (a0, a1) +-= (b0, b1), the same results as two
+// __fadd_rn (__fsub_rn).
+template <int kSign>
+__device__ __forceinline__ void add_pair_rn(float& a0, float& a1, float b0, float b1) {
+  if constexpr (kSign > 0)
+    asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+  else
+    asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+
+// a += w (kSign > 0) or a -= w, one rounding per element (packed in pairs
+// of columns for 4-wide chunks: half the add instructions).
 template <int kSign, int VW, int K>
 __device__ __forceinline__ void accumulate(Cols<VW, K>& a, const Cols<VW, K>& w) {
 #pragma unroll
-  for (int k = 0; k < K; ++k)
+  for (int k = 0; k < K; ++k) {
+    if constexpr (VW == 4) {
+      add_pair_rn<kSign>(a.v[k][0], a.v[k][1], w.v[k][0], w.v[k][1]);
+      add_pair_rn<kSign>(a.v[k][2], a.v[k][3], w.v[k][2], w.v[k][3]);
+    } else {
 #pragma unroll
-    for (int e = 0; e < VW; ++e) a.v[k][e] = kSign > 0 ? __fadd_rn(a.v[k][e], w.v[k][e]) : __fsub_rn(a.v[k][e], w.v[k][e]);
+      for (int e = 0; e < VW; ++e)
+        a.v[k][e] = kSign > 0 ? __fadd_rn(a.v[k][e], w.v[k][e]) : __fsub_rn(a.v[k][e], w.v[k][e]);
+    }
+  }
 }
 
 // acc += the rows of the items [beg, end) in the reference's refresh order:

@@ -120,21 +120,12 @@ __device__ __forceinline__ void store_cols(float* __restrict__ row, int chunks, 
   }
 }
 
-// Two independent IEEE round-to-nearest fp32 additions (subtractions) in one
-// packed instruction: (a0, a1) +-= (b0, b1), the same results as two
-// __fadd_rn (__fsub_rn).
 template <int kSign>
 __device__ __forceinline__ void add_pair_rn(float& a0, float& a1, float b0, float b1) {
   if constexpr (kSign > 0)
-    asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(b0), "f"(b1));
+    fadd2_rn(a0, a1, b0, b1);
   else
-    asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
-        "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(b0), "f"(b1));
+    fsub2_rn(a0, a1, b0, b1);
 }
 
 // a += w (kSign > 0) or a -= w, one rounding per element (packed in pairs

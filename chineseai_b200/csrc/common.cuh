@@ -27,6 +27,22 @@ int use_device(int device);
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
+// Two independent IEEE round-to-nearest fp32 additions (subtractions) in one
+// packed sm_100 instruction: (a0, a1) += (b0, b1), the same results as two
+// __fadd_rn (__fsub_rn).
+__device__ __forceinline__ void fadd2_rn(float& a0, float& a1, float b0, float b1) {
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void fsub2_rn(float& a0, float& a1, float b0, float b1) {
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%0, %1};\n\tmov.b64 rb, {%2, %3};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "+f"(a0), "+f"(a1)
+      : "f"(b0), "f"(b1));
+}
+
 // Workspace header shared by every entry point that takes a workspace.
 // The status word is the first 4 bytes; kernels OR CNNUE_STATUS_* bits in.
 struct WorkspaceHeader {

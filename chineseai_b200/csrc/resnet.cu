@@ -716,7 +716,11 @@ __global__ void __launch_bounds__(kHThreads, 1) rn_hconv_kernel(const __grid_con
           if (!ok) continue;
           float f[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]) + bc;
+          for (int i = 0; i < 32; i += 2) {  // + bias, packed in pairs
+            f[i] = __uint_as_float(v[i]);
+            f[i + 1] = __uint_as_float(v[i + 1]);
+            fadd2_rn(f[i], f[i + 1], bc, bc);
+          }
           transpose32<4>(f, lane);
           transpose32<2>(f, lane);
           transpose32<1>(f, lane);
@@ -732,8 +736,9 @@ __global__ void __launch_bounds__(kHThreads, 1) rn_hconv_kernel(const __grid_con
               for (int e = 0; e < 4; ++e) {
                 const uint32_t rw = (&rv[j][t].x)[e];
                 const float2 r2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw));
-                const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaxf(f[8 * t + 2 * e] + r2.x, 0.f),
-                                                                fmaxf(f[8 * t + 2 * e + 1] + r2.y, 0.f));
+                float x0 = f[8 * t + 2 * e], x1 = f[8 * t + 2 * e + 1];
+                fadd2_rn(x0, x1, r2.x, r2.y);
+                const __nv_bfloat162 h2 = __floats2bfloat162_rn(fmaxf(x0, 0.f), fmaxf(x1, 0.f));
                 packed[e] = *reinterpret_cast<const uint32_t*>(&h2);
               }
             }

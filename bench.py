@@ -1127,7 +1127,7 @@ def run_mcts(args):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "AzNnue::random(128, 20260807); 4096 roots (start position + random legal "
                                    "playouts of 1-40 plies), 64 simulations each, AzSearchLimits defaults; "
-                                   "one GPU batch of leaves per round", "roots_per_gpu": MCTS_ROOTS,
+                                   "roots in two halves whose GPU leaf batches alternate (one half is selected while the other is evaluated)", "roots_per_gpu": MCTS_ROOTS,
                        "simulations": MCTS_SIMS, "parallelism": f"replicas{world}",
                        "phase_seconds_last_search": st, "evaluations_per_search": ev,
                        "simulations_per_sec": world * MCTS_ROOTS * MCTS_SIMS / (ms / 1e3)},

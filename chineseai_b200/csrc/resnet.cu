@@ -27,10 +27,10 @@
 // CNNUE_STATUS_TIMEOUT.  No load uses cluster multicast.
 //
 // Heads, fp32 on CUDA cores: rn_head_conv_kernel (1x1 convs to 2 policy and
-// 1 value planes, a warp per trunk row), rn_value_kernel (value FC 90 -> 256
-// -> 1 with tanh, 8 boards per CTA), rn_policy_fc_kernel (FC 180 -> 2086 as
-// a tiled GEMM, 128 boards x 128 moves per CTA), rn_softmax_kernel (one warp
-// per board).
+// 1 value planes, a warp per trunk row), rn_heads_kernel (its blocks are
+// either policy FC 180 -> 2086 tiles of a tiled GEMM, 128 boards x 128 moves,
+// or value FC 90 -> 256 -> 1 with tanh, 8 boards), rn_softmax_kernel (one
+// warp per board).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -877,11 +877,13 @@ __global__ void __launch_bounds__(256) rn_head_conv_kernel(HeadArgs a, float* __
 // hidden unit j for all 8 boards (the value plane of the 8 boards staged in
 // shared memory, read as broadcasts); the 256 -> 1 layer is a block reduction.
 constexpr int kValueBoards = 8;
-__global__ void __launch_bounds__(256) rn_value_kernel(HeadArgs a, const float* __restrict__ vc_t) {
-  __shared__ __align__(16) float vc[kSq][kValueBoards];
-  __shared__ float red[kValueBoards][8];
+constexpr int kValueSmemFloats = kSq * kValueBoards + kValueBoards * 8;
+__device__ __forceinline__ void value_block(const HeadArgs& a, const float* __restrict__ vc_t, int64_t blk,
+                                            float* smem) {
+  float (*vc)[kValueBoards] = reinterpret_cast<float (*)[kValueBoards]>(smem);
+  float (*red)[8] = reinterpret_cast<float (*)[8]>(smem + kSq * kValueBoards);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int64_t b0 = (int64_t)blockIdx.x * kValueBoards;
+  const int64_t b0 = blk * kValueBoards;
   for (int i = tid; i < kSq * kValueBoards; i += 256) {
     const int p = i / kValueBoards, bl = i % kValueBoards;
     vc[p][bl] = b0 + bl < a.B ? vc_t[(size_t)p * a.B + b0 + bl] : 0.f;
@@ -924,17 +926,17 @@ __global__ void __launch_bounds__(256) rn_value_kernel(HeadArgs a, const float* 
 // per 64 FMAs), K in chunks of 20 double-buffered through registers: the
 // next chunk's global loads are in flight while this one is multiplied.
 constexpr int kFcBoards = 128, kFcMoves = 128, kFcK = 20;
-__global__ void __launch_bounds__(256) rn_policy_fc_kernel(const float* __restrict__ pc_t,
-                                                           const float* __restrict__ pfw_t,
-                                                           const float* __restrict__ pfb, int64_t B,
-                                                           float* __restrict__ logits) {
-  __shared__ __align__(16) float xs[2][kFcK][kFcBoards];
-  __shared__ __align__(16) float ws[2][kFcK][kFcMoves];
+constexpr int kFcSmemFloats = 2 * kFcK * kFcBoards + 2 * kFcK * kFcMoves;
+__device__ __forceinline__ void policy_fc_block(const float* __restrict__ pc_t, const float* __restrict__ pfw_t,
+                                                const float* __restrict__ pfb, int64_t B,
+                                                float* __restrict__ logits, int64_t bx, int by, float* smem) {
+  float (*xs)[kFcK][kFcBoards] = reinterpret_cast<float (*)[kFcK][kFcBoards]>(smem);
+  float (*ws)[kFcK][kFcMoves] = reinterpret_cast<float (*)[kFcK][kFcMoves]>(smem + 2 * kFcK * kFcBoards);
   constexpr int kPer = kFcK * kFcBoards / 256;  // elements of each operand a thread stages per chunk
   static_assert(kFcK * kFcBoards % 256 == 0 && kFcBoards == kFcMoves && (2 * kSq) % kFcK == 0, "tiles");
   const int tid = threadIdx.x;
-  const int64_t b0 = (int64_t)blockIdx.x * kFcBoards;
-  const int j0 = blockIdx.y * kFcMoves;
+  const int64_t b0 = bx * kFcBoards;
+  const int j0 = by * kFcMoves;
   const int tb = (tid >> 4) * 8, tj = (tid & 15) * 8;
   float rx[kPer], rw[kPer];
   auto fetch = [&](int k0) {
@@ -990,6 +992,21 @@ __global__ void __launch_bounds__(256) rn_policy_fc_kernel(const float* __restri
       if (j < kMoves) logits[b * kMoves + j] = acc[i][q] + __ldg(pfb + j);
     }
   }
+}
+
+// The value MLP and the policy FC both read only rn_head_conv_kernel's
+// outputs, so one launch runs them side by side: blocks [0, n_fc) are policy
+// FC tiles (fc_x tiles of boards per row of moves), the rest value blocks.
+// Each block computes exactly what the separate kernel would.
+static_assert(kFcSmemFloats >= kValueSmemFloats, "head smem");
+__global__ void __launch_bounds__(256, 2) rn_heads_kernel(HeadArgs a, const float* __restrict__ pc_t,
+                                                       const float* __restrict__ vc_t, unsigned fc_x,
+                                                       unsigned n_fc) {
+  __shared__ __align__(16) float smem[kFcSmemFloats];
+  if (blockIdx.x < n_fc)
+    policy_fc_block(pc_t, a.pfw_t, a.pfb, a.B, a.logits, blockIdx.x % fc_x, (int)(blockIdx.x / fc_x), smem);
+  else
+    value_block(a, vc_t, blockIdx.x - n_fc, smem);
 }
 
 // Softmax over the 2086 logits of a board, one warp per board.
@@ -1303,11 +1320,11 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   const int64_t conv_warps = (batch * kSq + kConvRows - 1) / kConvRows;
   rn_head_conv_kernel<<<(unsigned)((conv_warps + 7) / 8), 256, 0, s>>>(h, pc, vc);
   if (int st = check_launch_error("rn_head_conv_kernel")) return st;
-  rn_value_kernel<<<(unsigned)((batch + kValueBoards - 1) / kValueBoards), 256, 0, s>>>(h, vc);
-  if (int st = check_launch_error("rn_value_kernel")) return st;
-  const dim3 fc_grid((unsigned)((batch + kFcBoards - 1) / kFcBoards), (kMoves + kFcMoves - 1) / kFcMoves);
-  rn_policy_fc_kernel<<<fc_grid, 256, 0, s>>>(pc, h.pfw_t, h.pfb, batch, logits);
-  if (int st = check_launch_error("rn_policy_fc_kernel")) return st;
+  const unsigned fc_x = (unsigned)((batch + kFcBoards - 1) / kFcBoards);
+  const unsigned n_fc = fc_x * ((kMoves + kFcMoves - 1) / kFcMoves);
+  const unsigned n_value = (unsigned)((batch + kValueBoards - 1) / kValueBoards);
+  rn_heads_kernel<<<n_fc + n_value, 256, 0, s>>>(h, pc, vc, fc_x, n_fc);
+  if (int st = check_launch_error("rn_heads_kernel")) return st;
   rn_softmax_kernel<<<(unsigned)((batch + 7) / 8), 256, 0, s>>>(logits, batch, d_probs);
   return check_launch_error("rn_softmax_kernel");
 }

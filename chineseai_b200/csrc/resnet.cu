@@ -27,7 +27,7 @@
 // CNNUE_STATUS_TIMEOUT.  No load uses cluster multicast.
 //
 // Heads, fp32 on CUDA cores: rn_head_conv_kernel (1x1 convs to 2 policy and
-// 1 value planes, a warp per trunk row), rn_heads_kernel (its blocks are
+// 1 value planes, a lane per trunk row), rn_heads_kernel (its blocks are
 // either policy FC 180 -> 2086 tiles of a tiled GEMM, 128 boards x 128 moves,
 // or value FC 90 -> 256 -> 1 with tanh, 8 boards), rn_softmax_kernel (one
 // warp per board).
@@ -823,54 +823,52 @@ struct HeadArgs {
 
 
 // 1x1 convs of the trunk: policy planes to pc_t [180][B] and the value plane
-// to vc_t [90][B] (both after bias and ReLU), one warp per trunk row: lane l
-// reads channels 4l .. 4l+3 (the warp's load is the row's 256 contiguous
-// bytes) and the three dot products are reduced across the warp.  A warp
-// takes kConvRows rows at a time so that many loads are in flight.
-constexpr int kConvRows = 8;
+// to vc_t [90][B] (both after bias and ReLU).  A warp takes one square of 32
+// consecutive boards, lane l board 32k + l: it reads that board's whole
+// 128-channel row (sixteen 16-byte loads, all in flight together; in the
+// padded layout a warp's rows are four runs of 8 adjacent rows) and forms the
+// three dot products alone, with the weights as shared-memory broadcasts, so
+// no shuffles are needed and the warp's stores to pc_t / vc_t are 128
+// contiguous bytes each.
+constexpr int kConvBoards = 32;
 __global__ void __launch_bounds__(256) rn_head_conv_kernel(HeadArgs a, float* __restrict__ pc_t,
                                                            float* __restrict__ vc_t) {
+  __shared__ __align__(16) float w[3][kC];  // policy plane 0, policy plane 1, value plane
+  for (int i = threadIdx.x; i < 3 * kC; i += blockDim.x)
+    (&w[0][0])[i] = i < 2 * kC ? __ldg(a.pcw + i) : __ldg(a.vcw + (i - 2 * kC));
+  __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int64_t n_rows = a.B * kSq;
-  const int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * kConvRows;
-  if (r0 >= n_rows) return;
-  const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.pcw) + lane);
-  const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.pcw + kC) + lane);
-  const float4 wv = __ldg(reinterpret_cast<const float4*>(a.vcw) + lane);
-  const float pcb0 = __ldg(a.pcb), pcb1 = __ldg(a.pcb + 1), vcb = __ldg(a.vcb);
-  float s[kConvRows][3];
+  const int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t chunks = (a.B + kConvBoards - 1) / kConvBoards;
+  if (item >= chunks * kSq) return;
+  const int64_t chunk = item / kSq;
+  const int p = (int)(item - chunk * kSq);
+  const int64_t b = chunk * kConvBoards + lane;
+  if (b >= a.B) return;
+  const int64_t r = a.padded ? padded_row(b, p) : b * kSq + p;
+  const uint4* row = reinterpret_cast<const uint4*>(a.trunk + (size_t)r * kC);
+  uint4 x[kC / 8];
 #pragma unroll
-  for (int u = 0; u < kConvRows; ++u) {
-    const int64_t i = r0 + u, b = i / kSq;
-    const int p = (int)(i - b * kSq);
-    s[u][0] = s[u][1] = s[u][2] = 0.f;
-    if (i < n_rows) {
-      const int64_t r = a.padded ? padded_row(b, p) : i;
-      const uint2 raw = __ldg(reinterpret_cast<const uint2*>(a.trunk + (size_t)r * kC) + lane);
-      const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
-      const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
-      s[u][0] = fmaf(xb.y, w0.w, fmaf(xb.x, w0.z, fmaf(xa.y, w0.y, xa.x * w0.x)));
-      s[u][1] = fmaf(xb.y, w1.w, fmaf(xb.x, w1.z, fmaf(xa.y, w1.y, xa.x * w1.x)));
-      s[u][2] = fmaf(xb.y, wv.w, fmaf(xb.x, wv.z, fmaf(xa.y, wv.y, xa.x * wv.x)));
+  for (int q = 0; q < kC / 8; ++q) x[q] = __ldg(row + q);
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+#pragma unroll
+  for (int q = 0; q < kC / 8; ++q) {
+    const uint32_t u[4] = {x[q].x, x[q].y, x[q].z, x[q].w};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const float4 w0 = *reinterpret_cast<const float4*>(&w[0][8 * q + 4 * h]);
+      const float4 w1 = *reinterpret_cast<const float4*>(&w[1][8 * q + 4 * h]);
+      const float4 wv = *reinterpret_cast<const float4*>(&w[2][8 * q + 4 * h]);
+      const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h]));
+      const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h + 1]));
+      s0 = fmaf(xb.y, w0.w, fmaf(xb.x, w0.z, fmaf(xa.y, w0.y, fmaf(xa.x, w0.x, s0))));
+      s1 = fmaf(xb.y, w1.w, fmaf(xb.x, w1.z, fmaf(xa.y, w1.y, fmaf(xa.x, w1.x, s1))));
+      s2 = fmaf(xb.y, wv.w, fmaf(xb.x, wv.z, fmaf(xa.y, wv.y, fmaf(xa.x, wv.x, s2))));
     }
   }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int u = 0; u < kConvRows; ++u)
-#pragma unroll
-      for (int c = 0; c < 3; ++c) s[u][c] += __shfl_xor_sync(0xffffffffu, s[u][c], o);
-  // lanes 0 .. kConvRows-1 each write one row's three outputs
-#pragma unroll
-  for (int u = 0; u < kConvRows; ++u) {
-    const int64_t i = r0 + u, b = i / kSq;
-    const int p = (int)(i - b * kSq);
-    if (lane == u && i < n_rows) {
-      pc_t[(size_t)p * a.B + b] = fmaxf(s[u][0] + pcb0, 0.f);
-      pc_t[(size_t)(kSq + p) * a.B + b] = fmaxf(s[u][1] + pcb1, 0.f);
-      vc_t[(size_t)p * a.B + b] = fmaxf(s[u][2] + vcb, 0.f);
-    }
-  }
+  pc_t[(size_t)p * a.B + b] = fmaxf(s0 + __ldg(a.pcb), 0.f);
+  pc_t[(size_t)(kSq + p) * a.B + b] = fmaxf(s1 + __ldg(a.pcb + 1), 0.f);
+  vc_t[(size_t)p * a.B + b] = fmaxf(s2 + __ldg(a.vcb), 0.f);
 }
 
 // Value MLP 90 -> 256 (ReLU) -> 1 (tanh) for 8 boards per CTA: thread j is
@@ -1155,9 +1153,6 @@ int cnnue_rn_model_create(const cnnue_rn_weights* w, int device, cnnue_rn_model*
   float* v2w = hp; std::memcpy(v2w, w->value_fc2_w, sizeof(float) * 256); hp += 256;
   float* v2b = hp; v2b[0] = w->value_fc2_b[0];
 
-  // rn_head_conv_kernel reads pcw and vcw as float4
-  if ((pcw - head.data()) % 4 != 0 || (vcw - head.data()) % 4 != 0)
-    return set_error(CNNUE_ERR_INVALID_ARG, "head weight block misaligned");
   auto* m = new (std::nothrow) cnnue_rn_model;
   if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "out of host memory");
   m->device = device;
@@ -1317,7 +1312,7 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   h.logits = logits;
   h.probs = d_probs;
   h.value = d_value;
-  const int64_t conv_warps = (batch * kSq + kConvRows - 1) / kConvRows;
+  const int64_t conv_warps = (batch + kConvBoards - 1) / kConvBoards * kSq;
   rn_head_conv_kernel<<<(unsigned)((conv_warps + 7) / 8), 256, 0, s>>>(h, pc, vc);
   if (int st = check_launch_error("rn_head_conv_kernel")) return st;
   const unsigned fc_x = (unsigned)((batch + kFcBoards - 1) / kFcBoards);

@@ -30,7 +30,7 @@
 // 1 value planes, a lane per trunk row), rn_heads_kernel (its blocks are
 // either policy FC 180 -> 2086 tiles of a tiled GEMM, 128 boards x 128 moves,
 // or value FC 90 -> 256 -> 1 with tanh, 8 boards), rn_softmax_kernel (one
-// warp per board).
+// warp per board, the row held in registers).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cudaTypedefs.h>
@@ -825,7 +825,7 @@ struct HeadArgs {
 // 1x1 convs of the trunk: policy planes to pc_t [180][B] and the value plane
 // to vc_t [90][B] (both after bias and ReLU).  A warp takes one square of 32
 // consecutive boards, lane l board 32k + l: it reads that board's whole
-// 128-channel row (sixteen 16-byte loads, all in flight together; in the
+// 128-channel row (sixteen 16-byte loads; in the
 // padded layout a warp's rows are four runs of 8 adjacent rows) and forms the
 // three dot products alone, with the weights as shared-memory broadcasts, so
 // no shuffles are needed and the warp's stores to pc_t / vc_t are 128
@@ -1007,23 +1007,45 @@ __global__ void __launch_bounds__(256, 2) rn_heads_kernel(HeadArgs a, const floa
     value_block(a, vc_t, blockIdx.x - n_fc, smem);
 }
 
-// Softmax over the 2086 logits of a board, one warp per board.
-__global__ void __launch_bounds__(256) rn_softmax_kernel(const float* __restrict__ logits, int64_t B,
-                                                         float* __restrict__ probs) {
-  const int64_t b = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+// Softmax over the 2086 logits of a board, one warp per board, 4 boards per
+// CTA.  Lane l keeps logits l, l + 32, ... of its board in registers, so the
+// row is read once and each exponential computed once (the sum runs in the
+// same order as a strided loop over the row would).
+constexpr int kSoftmaxBoards = 4;
+constexpr int kSoftmaxPer = (kMoves + 31) / 32;
+__global__ void __launch_bounds__(32 * kSoftmaxBoards) rn_softmax_kernel(const float* __restrict__ logits,
+                                                                        int64_t B, float* __restrict__ probs) {
+  const int64_t b = (int64_t)blockIdx.x * kSoftmaxBoards + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (b >= B) return;
   const float* row = logits + b * kMoves;
+  float e[kSoftmaxPer];
   float m = -INFINITY;
-  for (int j = lane; j < kMoves; j += 32) m = fmaxf(m, row[j]);
+#pragma unroll
+  for (int i = 0; i < kSoftmaxPer; ++i) {
+    const int j = lane + 32 * i;
+    e[i] = j < kMoves ? __ldg(row + j) : -INFINITY;
+    m = fmaxf(m, e[i]);
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float s = 0.f;
-  for (int j = lane; j < kMoves; j += 32) s += expf(row[j] - m);
+#pragma unroll
+  for (int i = 0; i < kSoftmaxPer; ++i) {
+    if (lane + 32 * i < kMoves) {
+      e[i] = expf(e[i] - m);
+      s += e[i];
+    }
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float inv = 1.f / s;
-  for (int j = lane; j < kMoves; j += 32) probs[b * kMoves + j] = expf(row[j] - m) * inv;
+  float* out = probs + b * kMoves;
+#pragma unroll
+  for (int i = 0; i < kSoftmaxPer; ++i) {
+    const int j = lane + 32 * i;
+    if (j < kMoves) out[j] = e[i] * inv;
+  }
 }
 
 // Host: fp32 -> bf16 bits, round to nearest even.
@@ -1320,7 +1342,8 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   const unsigned n_value = (unsigned)((batch + kValueBoards - 1) / kValueBoards);
   rn_heads_kernel<<<n_fc + n_value, 256, 0, s>>>(h, pc, vc, fc_x, n_fc);
   if (int st = check_launch_error("rn_heads_kernel")) return st;
-  rn_softmax_kernel<<<(unsigned)((batch + 7) / 8), 256, 0, s>>>(logits, batch, d_probs);
+  rn_softmax_kernel<<<(unsigned)((batch + kSoftmaxBoards - 1) / kSoftmaxBoards), 32 * kSoftmaxBoards, 0, s>>>(
+      logits, batch, d_probs);
   return check_launch_error("rn_softmax_kernel");
 }
 

@@ -935,7 +935,9 @@ __device__ __forceinline__ void policy_fc_block(const float* __restrict__ pc_t, 
   const int tid = threadIdx.x;
   const int64_t b0 = bx * kFcBoards;
   const int j0 = by * kFcMoves;
-  const int tb = (tid >> 4) * 8, tj = (tid & 15) * 8;
+  // thread tile: boards tb .. tb+7, moves tj .. tj+3 and tj+64 .. tj+67 (a
+  // warp's two 16-byte weight reads are then 256 contiguous bytes each)
+  const int tb = (tid >> 4) * 8, tj = (tid & 15) * 4;
   float rx[kPer], rw[kPer];
   auto fetch = [&](int k0) {
 #pragma unroll
@@ -966,7 +968,7 @@ __device__ __forceinline__ void policy_fc_block(const float* __restrict__ pc_t, 
       const float4 xa = *reinterpret_cast<const float4*>(&xs[buf][k][tb]);
       const float4 xb = *reinterpret_cast<const float4*>(&xs[buf][k][tb + 4]);
       const float4 wa = *reinterpret_cast<const float4*>(&ws[buf][k][tj]);
-      const float4 wb = *reinterpret_cast<const float4*>(&ws[buf][k][tj + 4]);
+      const float4 wb = *reinterpret_cast<const float4*>(&ws[buf][k][tj + kFcMoves / 2]);
       const float x[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
       const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
@@ -986,7 +988,7 @@ __device__ __forceinline__ void policy_fc_block(const float* __restrict__ pc_t, 
     if (b >= B) continue;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      const int j = j0 + tj + q;
+      const int j = j0 + tj + (q < 4 ? q : kFcMoves / 2 + q - 4);
       if (j < kMoves) logits[b * kMoves + j] = acc[i][q] + __ldg(pfb + j);
     }
   }

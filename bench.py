@@ -538,7 +538,7 @@ def run_resnet(args):
             "e2e": {"value": world * RN_BATCH / (e2e_total / args.steps / 1e3), "unit": "boards/s",
                     "h2d_bytes_per_step": planes.nbytes,
                     "d2h_bytes_per_step": RN_BATCH * resnet.MOVES * 4 + RN_BATCH * 4},
-            "clocks": clocks, "gpu_launches": 26 * args.steps,
+            "clocks": clocks, "gpu_launches": 25 * args.steps,  # pack + 21 convs + 1x1 convs + FC/value + softmax
         }
         if not args.no_cpu_baseline:
             import oracle

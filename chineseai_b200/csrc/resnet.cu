@@ -759,28 +759,30 @@ __global__ void __launch_bounds__(kHThreads, 1) rn_hconv_kernel(const __grid_con
 
 // [B][15][90] bf16 planes -> the padded layout above, [rows][64] bf16,
 // channels 15..63 zero, padding rows (and the boards past B in the last
-// group) all zero.  One thread per padded row.
+// group) all zero.  One thread per 16-byte chunk of a padded row (8 channels),
+// so a warp's stores are 512 contiguous bytes.
 __global__ void rn_pack_padded_kernel(const __nv_bfloat16* __restrict__ planes, int64_t B, int64_t rows,
                                       __nv_bfloat16* __restrict__ out) {
-  const int64_t m = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (m >= rows) return;
+  const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= rows * 8) return;
+  const int64_t m = t >> 3;
+  const int q = (int)(t & 7);
   const int64_t cell = m >> 3;
   const int file = (int)(cell % kPitchF), rank = (int)((cell / kPitchF) % kPitchR);
   const int64_t b = (cell / (kPitchF * kPitchR)) * kGroupBoards + (m & 7);
-  uint32_t w[32];
-#pragma unroll
-  for (int k = 0; k < 32; ++k) w[k] = 0u;
-  if (rank >= 1 && file < 9 && b < B) {
+  uint32_t w[4] = {0u, 0u, 0u, 0u};
+  if (q * 8 < CNNUE_RN_PLANES && rank >= 1 && file < 9 && b < B) {
     const int p = (rank - 1) * 9 + file;
 #pragma unroll
-    for (int c = 0; c < CNNUE_RN_PLANES; ++c) {
-      const uint16_t v = reinterpret_cast<const uint16_t*>(planes)[(b * CNNUE_RN_PLANES + c) * kSq + p];
-      w[c >> 1] |= (uint32_t)v << (16 * (c & 1));
+    for (int k = 0; k < 8; ++k) {
+      const int c = q * 8 + k;
+      if (c < CNNUE_RN_PLANES) {
+        const uint16_t v = reinterpret_cast<const uint16_t*>(planes)[(b * CNNUE_RN_PLANES + c) * kSq + p];
+        w[k >> 1] |= (uint32_t)v << (16 * (k & 1));
+      }
     }
   }
-  uint4* o = reinterpret_cast<uint4*>(out + m * 64);
-#pragma unroll
-  for (int q = 0; q < 8; ++q) o[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  reinterpret_cast<uint4*>(out + m * 64)[q] = make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 // [B][15][90] bf16 planes -> [B*90][64] bf16, channels 15..63 zero.
@@ -1275,8 +1277,8 @@ int cnnue_rn_forward(const cnnue_rn_model* m, const uint16_t* d_planes, int64_t 
   float* logits = d_logits ? d_logits : (float*)p;
   uint32_t* status = &((WorkspaceHeader*)ws)->status;
   if (padded)
-    rn_pack_padded_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, M,
-                                                                      in64);
+    rn_pack_padded_kernel<<<(unsigned)((M * 8 + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch,
+                                                                          M, in64);
   else
     rn_pack_kernel<<<(unsigned)((M + 255) / 256), 256, 0, s>>>((const __nv_bfloat16*)d_planes, batch, in64);
   if (int st = check_launch_error("rn_pack_kernel")) return st;

@@ -55,6 +55,26 @@ def test_resnet_is_deterministic_and_batch_independent():
     assert torch.equal(l3[0], l1[5]) and torch.equal(v3[0], v1[5])
 
 
+def test_resnet_back_to_back_forwards_identical():
+    # forwards of two alternating batches queued with no host synchronisation:
+    # every kernel of a forward (the head kernels are programmatic dependents)
+    # must read its predecessor's finished output, so each result equals the
+    # synchronised first result of its batch bit for bit
+    w, model = _model()
+    a = torch.from_numpy(resnet.synthetic_planes(1024, 21).view(np.int16)).cuda()
+    b = torch.from_numpy(resnet.synthetic_planes(1024, 22).view(np.int16)).cuda()
+    ref = []
+    for x in (a, b):
+        out = model.forward(x, with_logits=True)
+        torch.cuda.synchronize()
+        ref.append([t.clone() for t in out])
+    outs = [model.forward(a if i % 2 == 0 else b, with_logits=True) for i in range(16)]
+    torch.cuda.synchronize()
+    for i, out in enumerate(outs):
+        for got, want in zip(out, ref[i % 2]):
+            assert torch.equal(got, want), i
+
+
 def _check_against_oracle(w, planes, probs, logits, value):
     lg, pr, _, v, _ = oracle.rn_forward(w, planes)
     scale = max(1.0, float(np.abs(lg).max()))

@@ -27,7 +27,7 @@
 // CNNUE_STATUS_TIMEOUT.  No load uses cluster multicast.
 //
 // Heads, fp32 on CUDA cores: rn_head_conv_kernel (1x1 convs to 2 policy and
-// 1 value planes, a lane per trunk row), rn_heads_kernel (its blocks are
+// 1 value planes, two lanes per trunk row), rn_heads_kernel (its blocks are
 // either policy FC 180 -> 2086 tiles of a tiled GEMM, 128 boards x 128 moves,
 // or value FC 90 -> 256 -> 1 with tanh, 8 boards), rn_softmax_kernel (one
 // warp per board, the row held in registers).
@@ -825,52 +825,59 @@ struct HeadArgs {
 
 
 // 1x1 convs of the trunk: policy planes to pc_t [180][B] and the value plane
-// to vc_t [90][B] (both after bias and ReLU).  A warp takes one square of 32
-// consecutive boards, lane l board 32k + l: it reads that board's whole
-// 128-channel row (sixteen 16-byte loads; in the
-// padded layout a warp's rows are four runs of 8 adjacent rows) and forms the
-// three dot products alone, with the weights as shared-memory broadcasts, so
-// no shuffles are needed and the warp's stores to pc_t / vc_t are 128
-// contiguous bytes each.
-constexpr int kConvBoards = 32;
+// to vc_t [90][B] (both after bias and ReLU).  A warp takes one square of 16
+// consecutive boards, two lanes per board: lanes l and l + 16 read the
+// even and the odd 16-byte chunks of board 16k + l's 128-channel row (eight
+// loads each; in the padded layout a warp's rows are two runs of 8 adjacent
+// rows), form partial dot products with the weights as shared-memory
+// broadcasts, and add them with one shuffle; the warp's stores to pc_t / vc_t
+// are 64 contiguous bytes each.
+constexpr int kConvBoards = 16;
 __global__ void __launch_bounds__(256) rn_head_conv_kernel(HeadArgs a, float* __restrict__ pc_t,
                                                            float* __restrict__ vc_t) {
   __shared__ __align__(16) float w[3][kC];  // policy plane 0, policy plane 1, value plane
   for (int i = threadIdx.x; i < 3 * kC; i += blockDim.x)
     (&w[0][0])[i] = i < 2 * kC ? __ldg(a.pcw + i) : __ldg(a.vcw + (i - 2 * kC));
   __syncthreads();
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, half = lane >> 4;
   const int64_t item = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int64_t chunks = (a.B + kConvBoards - 1) / kConvBoards;
-  if (item >= chunks * kSq) return;
+  if (item >= chunks * kSq) return;  // whole warp
   const int64_t chunk = item / kSq;
   const int p = (int)(item - chunk * kSq);
-  const int64_t b = chunk * kConvBoards + lane;
-  if (b >= a.B) return;
-  const int64_t r = a.padded ? padded_row(b, p) : b * kSq + p;
-  const uint4* row = reinterpret_cast<const uint4*>(a.trunk + (size_t)r * kC);
-  uint4 x[kC / 8];
-#pragma unroll
-  for (int q = 0; q < kC / 8; ++q) x[q] = __ldg(row + q);
+  const int64_t b = chunk * kConvBoards + (lane & 15);
   float s0 = 0.f, s1 = 0.f, s2 = 0.f;
+  if (b < a.B) {
+    const int64_t r = a.padded ? padded_row(b, p) : b * kSq + p;
+    const uint4* row = reinterpret_cast<const uint4*>(a.trunk + (size_t)r * kC);
+    uint4 x[kC / 16];
 #pragma unroll
-  for (int q = 0; q < kC / 8; ++q) {
-    const uint32_t u[4] = {x[q].x, x[q].y, x[q].z, x[q].w};
+    for (int q = 0; q < kC / 16; ++q) x[q] = __ldg(row + 2 * q + half);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const float4 w0 = *reinterpret_cast<const float4*>(&w[0][8 * q + 4 * h]);
-      const float4 w1 = *reinterpret_cast<const float4*>(&w[1][8 * q + 4 * h]);
-      const float4 wv = *reinterpret_cast<const float4*>(&w[2][8 * q + 4 * h]);
-      const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h]));
-      const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h + 1]));
-      s0 = fmaf(xb.y, w0.w, fmaf(xb.x, w0.z, fmaf(xa.y, w0.y, fmaf(xa.x, w0.x, s0))));
-      s1 = fmaf(xb.y, w1.w, fmaf(xb.x, w1.z, fmaf(xa.y, w1.y, fmaf(xa.x, w1.x, s1))));
-      s2 = fmaf(xb.y, wv.w, fmaf(xb.x, wv.z, fmaf(xa.y, wv.y, fmaf(xa.x, wv.x, s2))));
+    for (int q = 0; q < kC / 16; ++q) {
+      const uint32_t u[4] = {x[q].x, x[q].y, x[q].z, x[q].w};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = 16 * q + 8 * half + 4 * h;
+        const float4 w0 = *reinterpret_cast<const float4*>(&w[0][c]);
+        const float4 w1 = *reinterpret_cast<const float4*>(&w[1][c]);
+        const float4 wv = *reinterpret_cast<const float4*>(&w[2][c]);
+        const float2 xa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h]));
+        const float2 xb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u[2 * h + 1]));
+        s0 = fmaf(xb.y, w0.w, fmaf(xb.x, w0.z, fmaf(xa.y, w0.y, fmaf(xa.x, w0.x, s0))));
+        s1 = fmaf(xb.y, w1.w, fmaf(xb.x, w1.z, fmaf(xa.y, w1.y, fmaf(xa.x, w1.x, s1))));
+        s2 = fmaf(xb.y, wv.w, fmaf(xb.x, wv.z, fmaf(xa.y, wv.y, fmaf(xa.x, wv.x, s2))));
+      }
     }
   }
-  pc_t[(size_t)p * a.B + b] = fmaxf(s0 + __ldg(a.pcb), 0.f);
-  pc_t[(size_t)(kSq + p) * a.B + b] = fmaxf(s1 + __ldg(a.pcb + 1), 0.f);
-  vc_t[(size_t)p * a.B + b] = fmaxf(s2 + __ldg(a.vcb), 0.f);
+  s0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+  s1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+  s2 += __shfl_xor_sync(0xffffffffu, s2, 16);
+  if (half == 0 && b < a.B) {
+    pc_t[(size_t)p * a.B + b] = fmaxf(s0 + __ldg(a.pcb), 0.f);
+    pc_t[(size_t)(kSq + p) * a.B + b] = fmaxf(s1 + __ldg(a.pcb + 1), 0.f);
+    vc_t[(size_t)p * a.B + b] = fmaxf(s2 + __ldg(a.vcb), 0.f);
+  }
 }
 
 // Value MLP 90 -> 256 (ReLU) -> 1 (tanh) for 8 boards per CTA: thread j is

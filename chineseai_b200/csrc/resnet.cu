@@ -930,9 +930,9 @@ __device__ __forceinline__ void value_block(const HeadArgs& a, const float* __re
 
 // Policy FC logits[B][2086] = pc[B][180] . W^T + b, from pc_t [180][B]: CTA
 // tile 128 boards x 128 moves, thread tile 8 x 8 (four 16-byte shared loads
-// per 64 FMAs), K in chunks of 20 double-buffered through registers: the
+// per 64 FMAs), K in chunks of 10 double-buffered through registers: the
 // next chunk's global loads are in flight while this one is multiplied.
-constexpr int kFcBoards = 128, kFcMoves = 128, kFcK = 20;
+constexpr int kFcBoards = 128, kFcMoves = 128, kFcK = 10;
 constexpr int kFcSmemFloats = 2 * kFcK * kFcBoards + 2 * kFcK * kFcMoves;
 __device__ __forceinline__ void policy_fc_block(const float* __restrict__ pc_t, const float* __restrict__ pfw_t,
                                                 const float* __restrict__ pfb, int64_t B,

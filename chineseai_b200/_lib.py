@@ -45,6 +45,7 @@ SIGNATURES = {
     "cnnue_q_forward_host": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P]),
     "cnnue_q_forward_acc": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, P, c_size, P]),
     "cnnue_q_forward_noalloc": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P]),
+    "cnnue_q_forward_stall_test": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, c_u32, c_u32, c_u64, P]),
     "cnnue_q_update": (c_int, [c_void_p, P, P, P, c_u32, P, P, c_u32, P, P, c_i64, P, P, P,
                                c_size, P]),
     "cnnue_f_model_create": (c_int, [C.POINTER(FWeights), c_int, C.POINTER(c_void_p)]),

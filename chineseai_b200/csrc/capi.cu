@@ -2,8 +2,10 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
+#include "tma.cuh"
 
 namespace cnnue {
 
@@ -20,6 +22,19 @@ int set_error(int status, const char* fmt, ...) {
 int cuda_error(cudaError_t err, const char* what) {
   return set_error(CNNUE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(err),
                    cudaGetErrorName(err));
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
 }
 
 int use_device(int device) {

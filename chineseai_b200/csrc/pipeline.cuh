@@ -59,13 +59,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of `bar` with the given parity to complete.  Returns
 // false (after flagging) on timeout or when *abort is set.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          uint32_t* status) {
+                                          uint32_t* status, unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
     if (*abort) return false;
     if (mbar_try_wait(bar, parity)) return true;
-    if (globaltimer() - t0 > kWaitLimitNs) {
+    if (globaltimer() - t0 > limit_ns) {
       *abort = 1;
       atomicOr(status, CNNUE_STATUS_TIMEOUT);
       return false;

@@ -18,10 +18,12 @@
 //     round-robin to the producer warps and one lane per warp issues;
 //   * consumer thread t owns the 16-byte column chunk t of every row of both
 //     perspectives: per stage one wait, up to 8 shared loads, int16
-//     wraparound adds as __vadd2/__vsub2, one release;
+//     wraparound adds as native 16x2 adds (add.s16x2, one instruction per
+//     word; a list's last partial stage adds only its rows), one release;
 //   * the pairwise pack pairs chunk t with chunk t^64 (exchanged through
-//     shared memory); L1 = 32 dp4a per thread, a 16-way warp reduce-scatter
-//     and a 4-warp sum; warp 0 then runs L2/L3;
+//     shared memory; clamps by min.relu.s16x2, products by dp2a); L1 = 32
+//     dp4a per thread, a 16-way warp reduce-scatter and a 4-warp sum; warp 0
+//     then runs L2/L3;
 //   * positions are first grouped by bucket (a two-kernel counting sort) and
 //     each CTA walks a contiguous slice of that order, so the current bucket's
 //     16 KB of L1 weights stay in registers (16 x 8 bytes per thread).
@@ -58,21 +60,40 @@ struct DevWeights {
 // ---------------------------------------------------------------------------
 // Stage 3: fused gather + pack + bucket stack.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 vadd(uint4 a, uint4 b) {
-  return make_uint4(__vadd2(a.x, b.x), __vadd2(a.y, b.y), __vadd2(a.z, b.z), __vadd2(a.w, b.w));
+// int16 pair arithmetic with the sm_90+ 16x2 integer instructions: add wraps
+// per halfword (the FT's int16 wraparound), min.relu clamps to [0, b].
+__device__ __forceinline__ uint32_t add16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
 }
+__device__ __forceinline__ uint32_t clamp16x2_0_127(uint32_t a) {
+  uint32_t d;
+  asm("min.relu.s16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(0x007f007fu));
+  return d;
+}
+__device__ __forceinline__ uint4 vadd(uint4 a, uint4 b) {
+  return make_uint4(add16x2(a.x, b.x), add16x2(a.y, b.y), add16x2(a.z, b.z), add16x2(a.w, b.w));
+}
+// a - b per halfword, as a + (~b + 1).
 __device__ __forceinline__ uint4 vsub(uint4 a, uint4 b) {
-  return make_uint4(__vsub2(a.x, b.x), __vsub2(a.y, b.y), __vsub2(a.z, b.z), __vsub2(a.w, b.w));
+  return make_uint4(add16x2(a.x, add16x2(~b.x, 0x00010001u)), add16x2(a.y, add16x2(~b.y, 0x00010001u)),
+                    add16x2(a.z, add16x2(~b.z, 0x00010001u)), add16x2(a.w, add16x2(~b.w, 0x00010001u)));
 }
 
-// Two packed outputs from one int16 pair of the low half and the matching
-// pair of the high half: (clamp(a,0,127) * clamp(b,0,127)) >> 7 per lane.
-__device__ __forceinline__ uint32_t pack_pair(uint32_t lo, uint32_t hi) {
-  const uint32_t a = __vmaxs2(__vmins2(lo, 0x007f007fu), 0u);
-  const uint32_t b = __vmaxs2(__vmins2(hi, 0x007f007fu), 0u);
-  const uint32_t p0 = ((a & 0xffffu) * (b & 0xffffu)) >> 7;
-  const uint32_t p1 = ((a >> 16) * (b >> 16)) >> 7;
-  return p0 | (p1 << 8);
+// Four packed outputs from two words of the low half (columns j, j+1 and
+// j+2, j+3) and the matching words of the high half (columns j+512 ...):
+// (clamp(a,0,127) * clamp(b,0,127)) >> 7 per column, as bytes j..j+3.  Each
+// product is below 2^14, so the two products of a word sit in its two
+// halfwords and one 32-bit shift by 7 leaves both results in bytes 0 and 2.
+__device__ __forceinline__ uint32_t pack_quad(uint32_t lo0, uint32_t hi0, uint32_t lo1, uint32_t hi1) {
+  const uint32_t a0 = clamp16x2_0_127(lo0), b0 = clamp16x2_0_127(hi0);
+  const uint32_t a1 = clamp16x2_0_127(lo1), b1 = clamp16x2_0_127(hi1);
+  // dp2a with the clamped partner word as bytes: b = (b_lo, 0, b_hi, 0), so
+  // the low dot is a_lo * b_lo and the low dot of b >> 8 is a_hi * b_hi.
+  const uint32_t p0 = __dp2a_lo(a0, b0, 0u) | (__dp2a_lo(a0, b0 >> 8, 0u) << 16);
+  const uint32_t p1 = __dp2a_lo(a1, b1, 0u) | (__dp2a_lo(a1, b1 >> 8, 0u) << 16);
+  return __byte_perm(p0 >> 7, p1 >> 7, 0x6420);
 }
 
 struct ForwardArgs {
@@ -91,6 +112,11 @@ struct ForwardArgs {
   const uint32_t* perm;
   const uint8_t* sorted_bucket;
   uint32_t* status;
+  unsigned long long wait_ns;  // limit of every bounded wait
+  // Test hook of the bounded waits: CTA stall_block never issues its stage
+  // stall_stage (no transaction count, no copies), so the consumers' wait on
+  // it runs out.  0xffffffff = off.
+  uint32_t stall_block, stall_stage;
 };
 
 // ===========================================================================
@@ -125,6 +151,7 @@ struct BulkSmem {
   uint8_t ring[kSlots][kRowBytes];
   uint64_t full[kStages];   // completes when a stage's rows have landed
   uint64_t empty[kStages];  // completes when all consumer warps released a stage
+  uint32_t issued[kStages]; // latest stage announced on full[s] (0xffffffff: none)
   uint4 xbuf[kBulkConsumers];
   int32_t red[2][4][16];
   uint8_t y1s[16];
@@ -249,7 +276,9 @@ struct Producer {
   uint32_t* status;
   int w;      // producer index
   int lane;
-  bool ok;    // false once a wait gave up (stop issuing)
+  bool ok;    // false once a wait gave up or the CTA aborted (stop issuing)
+  unsigned long long wait_ns;
+  uint32_t stall_stage;  // this CTA's stage to leave unissued (test hook), or 0xffffffff
 
   // Lane 0: wait until stage st's slots are free (all consumer warps released
   // stage st - kStages), then announce `rows` rows on the stage's barrier.
@@ -257,14 +286,23 @@ struct Producer {
   // kProducers, whose own wait already saw stage st - kProducers - kStages
   // released, and kProducers <= kStages, so the empty barrier is at most one
   // phase behind the phase waited for.
+  // After an abort nothing more is announced, so every full barrier has at
+  // most its latest announced phase outstanding (recorded in sm->issued for
+  // the teardown drain).
   __device__ __forceinline__ bool begin_stage(uint32_t st, uint32_t rows) {
     const uint32_t sidx = st % kStages, use = st / kStages;
     if (!ok) return false;
-    if (use > 0 && !pipe::mbar_wait(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status)) {
+    if (use > 0 && !pipe::mbar_wait(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status, wait_ns)) {
       ok = false;
       return false;
     }
+    if (*(volatile int*)&sm->abort) {
+      ok = false;
+      return false;
+    }
+    if (st == stall_stage) return false;  // test hook: the stage stays unannounced
     pipe::mbar_arrive_expect_tx(&sm->full[sidx], rows * kRowBytes);
+    sm->issued[sidx] = st;
     return true;
   }
   __device__ __forceinline__ void copy(uint32_t st, uint32_t j, const char* src) {
@@ -347,12 +385,13 @@ struct Producer {
 // added.  Returns the next stage number.
 __device__ __forceinline__ uint32_t consume_update(BulkSmem& sm, uint32_t st, uint32_t init, uint32_t n_rem,
                                                    uint32_t n_add, int t, int lane, uint32_t* status,
-                                                   uint4& acc) {
+                                                   unsigned long long wait_ns, uint4& acc) {
   const uint32_t total = init + n_rem + n_add;
+  uint4 rem = make_uint4(0, 0, 0, 0);  // sum of the removed rows, subtracted once at the end
   for (uint32_t first = 0; first < total; first += kStageRows, ++st) {
     const uint32_t sidx = st % kStages;
     const uint32_t rows = min((uint32_t)kStageRows, total - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status);
+    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status, wait_ns);
     const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
     uint4 v[kStageRows];
 #pragma unroll
@@ -363,34 +402,46 @@ __device__ __forceinline__ uint32_t consume_update(BulkSmem& sm, uint32_t st, ui
 #pragma unroll
     for (int j = 0; j < kStageRows; ++j) {
       const uint32_t r = first + (uint32_t)j;
-      acc = (r >= init && r < init + n_rem) ? vsub(acc, v[j]) : vadd(acc, v[j]);
+      if (r >= init && r < init + n_rem)
+        rem = vadd(rem, v[j]);
+      else
+        acc = vadd(acc, v[j]);
     }
   }
+  acc = vsub(acc, rem);
   return st;
 }
 
-// Consumer: accumulates the rows of one list into acc (kOp 0 = set from the
-// single parent row, 1 = add, 2 = subtract).  Returns the next stage number.
-template <int kOp>
-__device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint32_t cnt, int t,
-                                                 int lane, uint32_t* status, uint4& acc) {
+// Consumer: adds the rows of one list into acc.  Full stages take an unrolled
+// tree of adds; the list's last, partial stage adds only its rows.  Returns
+// the next stage number.
+__device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint32_t cnt, int t, int lane,
+                                                 uint32_t* status, unsigned long long wait_ns, uint4& acc) {
   for (uint32_t first = 0; first < cnt; first += kStageRows, ++st) {
     const uint32_t sidx = st % kStages;
     const uint32_t rows = min((uint32_t)kStageRows, cnt - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status);
+    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status, wait_ns);
     const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
-    uint4 v[kStageRows];
+    if (rows == (uint32_t)kStageRows) {
+      uint4 v[kStageRows];
 #pragma unroll
-    for (int j = 0; j < kStageRows; ++j)
-      v[j] = (uint32_t)j < rows ? *reinterpret_cast<const uint4*>(slot + j * kRowBytes) : make_uint4(0, 0, 0, 0);
-    __syncwarp();
-    if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
-    if (kOp == 0) {
-      acc = v[0];
-    } else {
+      for (int j = 0; j < kStageRows; ++j) v[j] = *reinterpret_cast<const uint4*>(slot + j * kRowBytes);
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
       const uint4 s01 = vadd(vadd(v[0], v[1]), vadd(v[2], v[3]));
       const uint4 s23 = vadd(vadd(v[4], v[5]), vadd(v[6], v[7]));
-      acc = kOp == 1 ? vadd(acc, vadd(s01, s23)) : vsub(acc, vadd(s01, s23));
+      acc = vadd(acc, vadd(s01, s23));
+    } else {
+      // rows in [1, 7]: pairs, then a single row
+      uint4 s = make_uint4(0, 0, 0, 0);
+      uint32_t j = 0;
+      for (; j + 2 <= rows; j += 2)
+        s = vadd(s, vadd(*reinterpret_cast<const uint4*>(slot + j * kRowBytes),
+                         *reinterpret_cast<const uint4*>(slot + (j + 1) * kRowBytes)));
+      if (j < rows) s = vadd(s, *reinterpret_cast<const uint4*>(slot + j * kRowBytes));
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
+      acc = vadd(acc, s);
     }
   }
   return st;
@@ -456,6 +507,7 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
     for (int s = 0; s < kStages; ++s) {
       pipe::mbar_init(&sm.full[s], 1);
       pipe::mbar_init(&sm.empty[s], kBulkConsumers / 32);
+      sm.issued[s] = 0xffffffffu;
     }
     sm.abort = 0;
     pipe::mbar_init_fence();
@@ -468,7 +520,8 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 
   if (warp >= kBulkConsumers / 32) {
     // ------------------------------ producers -----------------------------
-    Producer<producers_of(kUpdate)> pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true};
+    Producer<producers_of(kUpdate)> pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true, a.wait_ns,
+                                       blockIdx.x == a.stall_block ? a.stall_stage : 0xffffffffu};
     const char* par_lo = (const char*)a.parent;
     uint32_t st_base = 0;  // stage number of the batch's first position
     for (int64_t b0 = begin; b0 < end; b0 += 32) {
@@ -512,16 +565,17 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
       }
       st_base += batch_stages;
     }
-    // Stay resident until the copies of this warp's last stages have landed
-    // (bounded by the wait limit).
-    if (lane == 0 && st_base > 0) {
-      const uint32_t first = st_base > (uint32_t)kStages ? st_base - kStages : 0u;
-      const unsigned long long t0 = pipe::globaltimer();
-      for (uint32_t k = first; k < st_base; ++k) {
-        if ((int)(k % producers_of(kUpdate)) != pr.w) continue;
-        while (!pipe::mbar_try_wait(&sm.full[k % kStages], (k / kStages) & 1u)) {
-          if (sm.abort || pipe::globaltimer() - t0 > pipe::kWaitLimitNs) break;
-        }
+    // Teardown: once every producer has stopped announcing stages, stay
+    // resident until the latest announced stage of every ring slot has
+    // landed (after an abort too; bounded), so no copy is in flight into
+    // this CTA's shared memory when it ends.  Only the latest announced phase
+    // of a slot can be outstanding (a slot is re-announced only after its
+    // previous stage was consumed), so the parity waits are exact.
+    named_bar_sync(2, 32 * producers_of(kUpdate));
+    if (lane == 0) {
+      for (int s = pr.w; s < kStages; s += producers_of(kUpdate)) {
+        const uint32_t last = sm.issued[s];
+        if (last != 0xffffffffu) pipe::mbar_wait_drain(&sm.full[s], (last / kStages) & 1u, a.status);
       }
     }
     __syncwarp();
@@ -571,9 +625,9 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
       uint4 v = bias;
       if (kUpdate) {
         if (d.init[p]) v = make_uint4(0, 0, 0, 0);  // the parent row replaces the bias
-        st = consume_update(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, t, lane, a.status, v);
+        st = consume_update(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, t, lane, a.status, a.wait_ns, v);
       } else {
-        st = consume_list<1>(sm, st, d.add[p].cnt, t, lane, a.status, v);
+        st = consume_list(sm, st, d.add[p].cnt, t, lane, a.status, a.wait_ns, v);
       }
       acc[p] = v;
     }
@@ -589,8 +643,8 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
     const uint4 other = sm.xbuf[t ^ 64];
     const uint4 plo = lo ? acc[0] : other;  // columns j   of the packed perspective
     const uint4 phi = lo ? other : acc[1];  // columns j+512
-    const uint32_t x0 = pack_pair(plo.x, phi.x) | (pack_pair(plo.y, phi.y) << 16);
-    const uint32_t x1 = pack_pair(plo.z, phi.z) | (pack_pair(plo.w, phi.w) << 16);
+    const uint32_t x0 = pack_quad(plo.x, phi.x, plo.y, phi.y);
+    const uint32_t x1 = pack_quad(plo.z, phi.z, plo.w, phi.w);
 
     int32_t v[kL1];
 #pragma unroll
@@ -693,11 +747,20 @@ int launch_sort(const cnnue_q_model* m, const uint32_t* d_offsets, uint32_t n_in
   return launch_bucket_sort(d_offsets, n_indices, d_count0, n, 1, kNB, ws, s);
 }
 
+// Arguments with the default wait limit and the stall hook off.
+ForwardArgs base_args() {
+  ForwardArgs a{};
+  a.wait_ns = pipe::kWaitLimitNs;
+  a.stall_block = 0xffffffffu;
+  a.stall_stage = 0xffffffffu;
+  return a;
+}
+
 int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
                 const uint32_t* d_offsets, int64_t n, int32_t* d_scores, int16_t* d_acc, void* ws,
-                cudaStream_t s) {
+                cudaStream_t s, const ForwardArgs& hooks = base_args()) {
   WorkspaceView v = carve_workspace(ws, n);
-  ForwardArgs a{};
+  ForwardArgs a = hooks;
   a.w = m->w;
   a.idx = d_idx;
   a.n_idx = n_idx;
@@ -906,6 +969,29 @@ int cnnue_q_forward_host(cnnue_q_model* m, const uint16_t* h_idx, uint32_t n_idx
   return status;
 }
 
+int cnnue_q_forward_stall_test(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
+                               const uint32_t* d_offsets, int64_t n, int32_t* d_scores, void* ws,
+                               size_t ws_bytes, uint32_t stall_block, uint32_t stall_stage,
+                               uint64_t wait_limit_ns, void* stream) {
+  int st = validate_common(m, n, ws, ws_bytes);
+  if (st) return st;
+  st = check_indices_args(d_idx, n_idx, d_offsets, d_scores, n);
+  if (st) return st;
+  if (n == 0) return CNNUE_OK;
+  if (wait_limit_ns == 0 || wait_limit_ns > pipe::kWaitLimitNs)
+    return set_error(CNNUE_ERR_INVALID_ARG, "wait limit must be in (0, %llu] ns", pipe::kWaitLimitNs);
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  cudaStream_t s = (cudaStream_t)stream;
+  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s);
+  if (st) return st;
+  ForwardArgs hooks = base_args();
+  hooks.wait_ns = wait_limit_ns;
+  hooks.stall_block = stall_block;
+  hooks.stall_stage = stall_stage;
+  return launch_eval(m, d_idx, n_idx, d_offsets, n, d_scores, nullptr, ws, s, hooks);
+}
+
 int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_t* d_flags,
                    const uint16_t* d_rem, uint32_t n_rem, const uint32_t* d_rem_offsets,
                    const uint16_t* d_add, uint32_t n_add, const uint32_t* d_add_offsets,
@@ -929,7 +1015,7 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   st = launch_offsets_check(d_add_offsets, n_add, 2 * n, ws, s);
   if (st) return st;
   WorkspaceView v = carve_workspace(ws, n);
-  ForwardArgs a{};
+  ForwardArgs a = base_args();
   a.w = m->w;
   a.idx = d_add;
   a.n_idx = n_add;

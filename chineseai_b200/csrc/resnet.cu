@@ -44,6 +44,7 @@
 #include "common.cuh"
 #include "pipeline.cuh"
 #include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace cnnue {
 namespace rn {
@@ -1091,25 +1092,11 @@ size_t conv_smem_bytes() { return sizeof(ConvSmem) + 1024; }
 size_t pconv_smem_bytes() { return sizeof(PConvSmem) + 1024; }
 size_t hconv_smem_bytes() { return sizeof(HConvSmem) + 1024; }
 
-// cuTensorMapEncodeTiled from the driver (no link-time libcuda dependency).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
 // Tensor map of an activation buffer [M][cin] bf16 read in boxes of
 // `box_rows` rows x 64 channels with the 128-byte swizzle; rows outside
 // [0, M) read zeros.
 int make_act_map(CUtensorMap* map, const void* base, int cin, int64_t M, int box_rows) {
-  PFN_cuTensorMapEncodeTiled_v12000 fn = encode_fn();
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tma_encode_fn();
   if (!fn) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
   const cuuint64_t dims[2] = {(cuuint64_t)cin, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)cin * 2};

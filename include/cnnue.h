@@ -121,6 +121,23 @@ int cnnue_q_forward_sorted(const cnnue_q_model* model, const uint16_t* d_indices
                            int32_t* d_scores, void* d_workspace, size_t workspace_bytes,
                            void* stream);
 
+/* Test hook of the bounded device-side waits (no counterpart in the
+ * reference, whose only failure handling is the search's stop flag,
+ * src/main.rs:2106-2114).  Runs cnnue_q_forward with every wait of the
+ * evaluation kernel limited to wait_limit_ns (0 < limit <= 1 s) and with CTA
+ * `stall_block` never announcing or copying its pipeline stage
+ * `stall_stage`, so the consumers' wait on that stage runs out: the kernel
+ * sets CNNUE_STATUS_TIMEOUT, stops issuing, lets the copies already in flight
+ * land and ends.  The scores are then undefined; cnnue_read_status reports
+ * CNNUE_ERR_TIMEOUT and clears the word, and the model stays usable.  A
+ * stall_block past the grid or a stall_stage past the CTA's stages runs the
+ * plain forward. */
+int cnnue_q_forward_stall_test(const cnnue_q_model* model, const uint16_t* d_indices,
+                               uint32_t n_indices, const uint32_t* d_offsets, int64_t n_positions,
+                               int32_t* d_scores, void* d_workspace, size_t workspace_bytes,
+                               uint32_t stall_block, uint32_t stall_stage, uint64_t wait_limit_ns,
+                               void* stream);
+
 /* Same as cnnue_q_forward with HOST buffers: copies the inputs to the device,
  * runs the forward and copies the scores back, then synchronises `stream`
  * and returns the kernels' status.  The model keeps device staging buffers

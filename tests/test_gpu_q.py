@@ -158,3 +158,36 @@ def test_second_model_on_same_device(qweights):
     scores, _ = m2.forward_positions(pos)
     np.testing.assert_array_equal(scores, oracle.q_forward(qweights, pos)[1])
     m2.close()
+
+
+@pytest.mark.parametrize("n,block,stage", [(64, 0, 0), (64, 5, 1), (3000, 7, 9)])
+def test_bounded_wait_runs_out_and_model_recovers(qmodel, qweights, n, block, stage):
+    """One CTA leaves one pipeline stage unannounced (nothing copies into it),
+    so the consumers' bounded wait on it runs out after 2 ms: the call
+    reports CNNUE_ERR_TIMEOUT through the status word, and the next call on
+    the same model and workspace is bit-exact again."""
+    import ctypes as C
+
+    from chineseai_b200._lib import lib
+    pos = synth.positions(n, 40 + block)
+    dev = qmodel.device
+    idx, off = as_device(pos.indices, dev), as_device(pos.offsets, dev)
+    out = torch.empty(pos.n, dtype=torch.int32, device=dev)
+    ws = qmodel.workspace(pos.n)
+    s = torch.cuda.current_stream().cuda_stream
+    rc = lib().cnnue_q_forward_stall_test(qmodel.handle, idx.data_ptr(), len(pos.indices), off.data_ptr(), pos.n,
+                                          out.data_ptr(), ws.data_ptr(), ws.numel(), block, stage, 2_000_000, s)
+    assert rc == 0
+    st = C.c_int(-1)
+    assert lib().cnnue_read_status(ws.data_ptr(), s, C.byref(st)) == 0
+    assert st.value == 9  # CNNUE_ERR_TIMEOUT
+    # the same call without a stall, then the plain forward: both bit-exact
+    rc = lib().cnnue_q_forward_stall_test(qmodel.handle, idx.data_ptr(), len(pos.indices), off.data_ptr(), pos.n,
+                                          out.data_ptr(), ws.data_ptr(), ws.numel(), 0xFFFFFFFF, 0xFFFFFFFF,
+                                          2_000_000, s)
+    assert rc == 0
+    assert lib().cnnue_read_status(ws.data_ptr(), s, C.byref(st)) == 0 and st.value == 0
+    ref = oracle.q_forward(qweights, pos)[1]
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+    scores, _ = qmodel.forward_positions(pos)
+    np.testing.assert_array_equal(scores, ref)

@@ -111,7 +111,7 @@ __global__ void bucket_scan_kernel(uint32_t nblk, int n_buckets, WorkspaceHeader
 __global__ void __launch_bounds__(kSortThreads) bucket_scatter_kernel(
     int64_t n, const uint8_t* __restrict__ bucket_of, const WorkspaceHeader* __restrict__ hdr,
     const uint32_t* __restrict__ block_hist, uint32_t* __restrict__ perm,
-    uint8_t* __restrict__ sorted_bucket) {
+    uint8_t* __restrict__ sorted_bucket, uint32_t* __restrict__ inv) {
   constexpr int kWarps = kSortThreads / 32;
   __shared__ uint32_t wcount[kWarps][32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,6 +130,7 @@ __global__ void __launch_bounds__(kSortThreads) bucket_scatter_kernel(
     const uint32_t slot = hdr->cursors[b] + block_hist[(size_t)blockIdx.x * 32 + b] + before + rank;
     perm[slot] = (uint32_t)p;
     sorted_bucket[slot] = (uint8_t)b;
+    if (inv) inv[p] = slot;
   }
 }
 
@@ -151,7 +152,7 @@ __global__ void offsets_check_kernel(const uint32_t* __restrict__ offsets, uint3
 }  // namespace
 
 int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
-                       int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s) {
+                       int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s, uint32_t* inv) {
   WorkspaceView v = carve_workspace(ws, n);
   CNNUE_CUDA_TRY(cudaMemsetAsync(v.hdr, 0, sizeof(WorkspaceHeader), s));
   if (n <= 0) return CNNUE_OK;
@@ -164,7 +165,7 @@ int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint
   st = check_launch("bucket_scan_kernel");
   if (st) return st;
   bucket_scatter_kernel<<<blocks, kSortThreads, 0, s>>>(n, v.bucket_of, v.hdr, v.block_hist, v.perm,
-                                                        v.sorted_bucket);
+                                                        v.sorted_bucket, inv);
   return check_launch("bucket_scatter_kernel");
 }
 

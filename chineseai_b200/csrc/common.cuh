@@ -71,8 +71,11 @@ WorkspaceView carve_workspace(void* ws, int64_t n);
 // them into bucket order, stably (ascending positions within a bucket), so
 // everything computed in that order is deterministic.  Offsets are validated
 // into the status word.
+// When `inv` is not null it receives the inverse order: inv[p] = the sorted
+// slot of position p.
 int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
-                       int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s);
+                       int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s,
+                       uint32_t* inv = nullptr);
 // ORs CNNUE_STATUS_BAD_OFFSETS into the workspace status when a CSR offsets
 // array of n_lists lists is not monotone or runs past n_values.
 int launch_offsets_check(const uint32_t* d_offsets, uint32_t n_values, int64_t n_lists, void* ws,

@@ -108,6 +108,9 @@ struct ForwardArgs {
   const uint8_t* flags;       // update only, [2n]
   int16_t* acc_out;           // [n][2][1024] or null
   int32_t* scores;
+  uint8_t* packed;            // split path: [n][1024] packed activations in sorted order
+  const uint32_t* inv;        // split path: sorted slot of every position
+  int natural;                // 1: walk positions in batch order (split path), 0: in sorted order
   int64_t n;
   const uint32_t* perm;
   const uint8_t* sorted_bucket;
@@ -178,7 +181,7 @@ __device__ __forceinline__ Seg clamp_seg(const uint32_t* off, int64_t i, uint32_
 template <bool kUpdate>
 __device__ __forceinline__ PosDesc load_desc(const ForwardArgs& a, int64_t i) {
   PosDesc d;
-  d.pos = a.perm[i];
+  d.pos = a.natural ? (uint32_t)i : a.perm[i];
   d.bucket = a.sorted_bucket[i];
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
@@ -266,13 +269,17 @@ __device__ __forceinline__ uint32_t desc_rows(const PosDesc& d) {
 // parallel; one bulk copy occupies the issuing warp for ~100 cycles.  Every
 // producer warp walks all positions of the CTA's slice; the index lists are
 // prefetched kPrefetch positions ahead.
+template <int kSR = kStageRows>
 __device__ __forceinline__ uint32_t n_stages(uint32_t rows) {
-  return (rows + kStageRows - 1) / kStageRows;
+  return (rows + kSR - 1) / kSR;
 }
 
-template <int kProducers>
+// Ring geometry: kSR rows per stage, kNS stages; Smem has ring[kSR * kNS],
+// full/empty/issued[kNS] and abort.
+template <int kProducers, int kSR = kStageRows, int kNS = kStages, class Smem = BulkSmem>
 struct Producer {
-  BulkSmem* sm;
+  static_assert(kProducers <= kNS, "parity waits on the empty barriers need producers <= stages");
+  Smem* sm;
   uint32_t* status;
   int w;      // producer index
   int lane;
@@ -281,16 +288,16 @@ struct Producer {
   uint32_t stall_stage;  // this CTA's stage to leave unissued (test hook), or 0xffffffff
 
   // Lane 0: wait until stage st's slots are free (all consumer warps released
-  // stage st - kStages), then announce `rows` rows on the stage's barrier.
+  // stage st - kNS), then announce `rows` rows on the stage's barrier.
   // Parity waits cannot alias here: this warp's previous stage was st -
-  // kProducers, whose own wait already saw stage st - kProducers - kStages
-  // released, and kProducers <= kStages, so the empty barrier is at most one
+  // kProducers, whose own wait already saw stage st - kProducers - kNS
+  // released, and kProducers <= kNS, so the empty barrier is at most one
   // phase behind the phase waited for.
   // After an abort nothing more is announced, so every full barrier has at
   // most its latest announced phase outstanding (recorded in sm->issued for
   // the teardown drain).
   __device__ __forceinline__ bool begin_stage(uint32_t st, uint32_t rows) {
-    const uint32_t sidx = st % kStages, use = st / kStages;
+    const uint32_t sidx = st % kNS, use = st / kNS;
     if (!ok) return false;
     if (use > 0 && !pipe::mbar_wait(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status, wait_ns)) {
       ok = false;
@@ -306,20 +313,20 @@ struct Producer {
     return true;
   }
   __device__ __forceinline__ void copy(uint32_t st, uint32_t j, const char* src) {
-    const uint32_t sidx = st % kStages;
-    pipe::bulk_copy_g2s(sm->ring[sidx * kStageRows + j], src, kRowBytes, &sm->full[sidx]);
+    const uint32_t sidx = st % kNS;
+    pipe::bulk_copy_g2s(sm->ring[sidx * kSR + j], src, kRowBytes, &sm->full[sidx]);
   }
 
   // Issues this warp's stages among st0, st0+1, ... (the stages of list[seg]).
   // `head` holds lst[seg.beg + lane] for the first 32 entries (prefetched).
   __device__ __forceinline__ void list(const char* ft, const uint16_t* lst, Seg seg, uint32_t head,
                                        uint32_t st0) {
-    const uint32_t ns = n_stages(seg.cnt);
+    const uint32_t ns = n_stages<kSR>(seg.cnt);
     uint32_t k = (uint32_t)((w - (int)(st0 % kProducers) + kProducers) % kProducers);
     for (; k < ns; k += kProducers) {
       const uint32_t st = st0 + k;
-      const uint32_t first = k * kStageRows;
-      const uint32_t rows = min((uint32_t)kStageRows, seg.cnt - first);
+      const uint32_t first = k * kSR;
+      const uint32_t rows = min((uint32_t)kSR, seg.cnt - first);
       uint32_t f = head;
       if (first >= 32) f = (uint32_t)lane < rows ? lst[seg.beg + first + lane] : 0u;
       const int src_lane0 = first >= 32 ? 0 : (int)first;
@@ -344,12 +351,12 @@ struct Producer {
                                              const uint16_t* rem_list, Seg rem, uint32_t head_rem,
                                              const uint16_t* add_list, Seg add, uint32_t head_add, uint32_t st0) {
     const uint32_t total = init + rem.cnt + add.cnt;
-    const uint32_t ns = n_stages(total);
+    const uint32_t ns = n_stages<kSR>(total);
     uint32_t k = (uint32_t)((w - (int)(st0 % kProducers) + kProducers) % kProducers);
     for (; k < ns; k += kProducers) {
       const uint32_t st = st0 + k;
-      const uint32_t first = k * kStageRows;
-      const uint32_t rows = min((uint32_t)kStageRows, total - first);
+      const uint32_t first = k * kSR;
+      const uint32_t rows = min((uint32_t)kSR, total - first);
       const uint32_t r = first + (uint32_t)lane;
       const uint32_t ir = r - init;            // index into the removed list (when in range)
       const uint32_t ia = r - init - rem.cnt;  // index into the added list (when in range)
@@ -382,25 +389,27 @@ struct Producer {
 
 // Consumer of an update perspective's sequence: rows [0, init) set from the
 // parent (acc starts at zero then), [init, init + n_rem) subtracted, the rest
-// added.  Returns the next stage number.
-__device__ __forceinline__ uint32_t consume_update(BulkSmem& sm, uint32_t st, uint32_t init, uint32_t n_rem,
-                                                   uint32_t n_add, int t, int lane, uint32_t* status,
+// added.  The thread's 16 bytes of every row start at col_byte.  Returns the
+// next stage number.
+template <int kSR = kStageRows, int kNS = kStages, class Smem = BulkSmem>
+__device__ __forceinline__ uint32_t consume_update(Smem& sm, uint32_t st, uint32_t init, uint32_t n_rem,
+                                                   uint32_t n_add, int col_byte, int lane, uint32_t* status,
                                                    unsigned long long wait_ns, uint4& acc) {
   const uint32_t total = init + n_rem + n_add;
   uint4 rem = make_uint4(0, 0, 0, 0);  // sum of the removed rows, subtracted once at the end
-  for (uint32_t first = 0; first < total; first += kStageRows, ++st) {
-    const uint32_t sidx = st % kStages;
-    const uint32_t rows = min((uint32_t)kStageRows, total - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status, wait_ns);
-    const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
-    uint4 v[kStageRows];
+  for (uint32_t first = 0; first < total; first += kSR, ++st) {
+    const uint32_t sidx = st % kNS;
+    const uint32_t rows = min((uint32_t)kSR, total - first);
+    pipe::mbar_wait(&sm.full[sidx], (st / kNS) & 1u, &sm.abort, status, wait_ns);
+    const uint8_t* slot = &sm.ring[sidx * kSR][col_byte];
+    uint4 v[kSR];
 #pragma unroll
-    for (int j = 0; j < kStageRows; ++j)
+    for (int j = 0; j < kSR; ++j)
       v[j] = (uint32_t)j < rows ? *reinterpret_cast<const uint4*>(slot + j * kRowBytes) : make_uint4(0, 0, 0, 0);
     __syncwarp();
     if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
 #pragma unroll
-    for (int j = 0; j < kStageRows; ++j) {
+    for (int j = 0; j < kSR; ++j) {
       const uint32_t r = first + (uint32_t)j;
       if (r >= init && r < init + n_rem)
         rem = vadd(rem, v[j]);
@@ -412,27 +421,31 @@ __device__ __forceinline__ uint32_t consume_update(BulkSmem& sm, uint32_t st, ui
   return st;
 }
 
-// Consumer: adds the rows of one list into acc.  Full stages take an unrolled
-// tree of adds; the list's last, partial stage adds only its rows.  Returns
-// the next stage number.
-__device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint32_t cnt, int t, int lane,
+// Consumer: adds the rows of one list into acc (the thread's 16 bytes of
+// every row start at col_byte).  Full stages take an unrolled tree of adds;
+// the list's last, partial stage adds only its rows.  Returns the next stage
+// number.
+template <int kSR = kStageRows, int kNS = kStages, class Smem = BulkSmem>
+__device__ __forceinline__ uint32_t consume_list(Smem& sm, uint32_t st, uint32_t cnt, int col_byte, int lane,
                                                  uint32_t* status, unsigned long long wait_ns, uint4& acc) {
-  for (uint32_t first = 0; first < cnt; first += kStageRows, ++st) {
-    const uint32_t sidx = st % kStages;
-    const uint32_t rows = min((uint32_t)kStageRows, cnt - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kStages) & 1u, &sm.abort, status, wait_ns);
-    const uint8_t* slot = &sm.ring[sidx * kStageRows][t * 16];
-    if (rows == (uint32_t)kStageRows) {
-      uint4 v[kStageRows];
+  for (uint32_t first = 0; first < cnt; first += kSR, ++st) {
+    const uint32_t sidx = st % kNS;
+    const uint32_t rows = min((uint32_t)kSR, cnt - first);
+    pipe::mbar_wait(&sm.full[sidx], (st / kNS) & 1u, &sm.abort, status, wait_ns);
+    const uint8_t* slot = &sm.ring[sidx * kSR][col_byte];
+    if (rows == (uint32_t)kSR) {
+      uint4 v[kSR];
 #pragma unroll
-      for (int j = 0; j < kStageRows; ++j) v[j] = *reinterpret_cast<const uint4*>(slot + j * kRowBytes);
+      for (int j = 0; j < kSR; ++j) v[j] = *reinterpret_cast<const uint4*>(slot + j * kRowBytes);
       __syncwarp();
       if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
-      const uint4 s01 = vadd(vadd(v[0], v[1]), vadd(v[2], v[3]));
-      const uint4 s23 = vadd(vadd(v[4], v[5]), vadd(v[6], v[7]));
-      acc = vadd(acc, vadd(s01, s23));
+#pragma unroll
+      for (int h = kSR / 2; h >= 1; h /= 2)
+#pragma unroll
+        for (int j = 0; j < h; ++j) v[j] = vadd(v[j], v[j + h]);
+      acc = vadd(acc, v[0]);
     } else {
-      // rows in [1, 7]: pairs, then a single row
+      // rows in [1, kSR): pairs, then a single row
       uint4 s = make_uint4(0, 0, 0, 0);
       uint32_t j = 0;
       for (; j + 2 <= rows; j += 2)
@@ -447,8 +460,10 @@ __device__ __forceinline__ uint32_t consume_list(BulkSmem& sm, uint32_t st, uint
   return st;
 }
 
+template <int kSR = kStageRows>
 __device__ __forceinline__ uint32_t desc_stages(const PosDesc& d) {
-  return n_stages(d.init[0] + d.rem[0].cnt + d.add[0].cnt) + n_stages(d.init[1] + d.rem[1].cnt + d.add[1].cnt);
+  return n_stages<kSR>(d.init[0] + d.rem[0].cnt + d.add[0].cnt) +
+         n_stages<kSR>(d.init[1] + d.rem[1].cnt + d.add[1].cnt);
 }
 
 // Lane-parallel descriptor of position i (valid lanes only).
@@ -497,6 +512,143 @@ __device__ __forceinline__ ListHead load_heads(const ForwardArgs& a, const PosDe
   return h;
 }
 
+// Producer warps of a CTA's slice [begin, end) of the sorted positions:
+// warp w of kP walks every position, issues the stages dealt to it (stage st
+// belongs to warp st % kP) and finally drains the ring.
+template <bool kUpdate, int kP, int kSR, int kNS, class Smem>
+__device__ __forceinline__ void produce(Smem& sm, const ForwardArgs& a, int64_t begin, int64_t end, int w,
+                                        int lane) {
+  Producer<kP, kSR, kNS, Smem> pr{&sm, a.status, w, lane, true, a.wait_ns,
+                                 blockIdx.x == a.stall_block ? a.stall_stage : 0xffffffffu};
+  const char* ft = (const char*)a.w.ft;
+  const char* par_lo = (const char*)a.parent;
+  uint32_t st_base = 0;  // stage number of the batch's first position
+  for (int64_t b0 = begin; b0 < end; b0 += 32) {
+    const int nb = (int)min((int64_t)32, end - b0);
+    PosDesc mine;
+    lane_desc<kUpdate>(a, b0 + lane, lane < nb, mine);
+    const uint32_t my_ns = lane < nb ? desc_stages<kSR>(mine) : 0u;
+    uint32_t incl = my_ns;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += x;
+    }
+    const uint32_t excl = incl - my_ns;
+    const uint32_t batch_stages = __shfl_sync(kFull, incl, 31);
+    // index-list heads of positions q .. q+3 (a rotating window)
+    ListHead h0{}, h1{}, h2{}, h3{};
+    if (0 < nb) h0 = load_heads<kUpdate>(a, shfl_desc(mine, 0), lane);
+    if (1 < nb) h1 = load_heads<kUpdate>(a, shfl_desc(mine, 1), lane);
+    if (2 < nb) h2 = load_heads<kUpdate>(a, shfl_desc(mine, 2), lane);
+    if (3 < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, 3), lane);
+    for (int q = 0; q < nb; ++q) {
+      const PosDesc cur = shfl_desc(mine, q);
+      const ListHead head = h0;
+      h0 = h1;
+      h1 = h2;
+      h2 = h3;
+      if (q + kPrefetch < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, q + kPrefetch), lane);
+      uint32_t st = st_base + __shfl_sync(kFull, excl, q);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (kUpdate) {
+          pr.update_seq(ft, par_lo + (2 * (int64_t)cur.pos + p) * kRowBytes, cur.init[p], a.rem, cur.rem[p],
+                        head.rem[p], a.idx, cur.add[p], head.add[p], st);
+          st += n_stages<kSR>(cur.init[p] + cur.rem[p].cnt + cur.add[p].cnt);
+        } else {
+          pr.list(ft, a.idx, cur.add[p], head.add[p], st);
+          st += n_stages<kSR>(cur.add[p].cnt);
+        }
+      }
+    }
+    st_base += batch_stages;
+  }
+  // Teardown: once every producer has stopped announcing stages, stay
+  // resident until the latest announced stage of every ring slot has
+  // landed (after an abort too; bounded), so no copy is in flight into
+  // this CTA's shared memory when it ends.  Only the latest announced phase
+  // of a slot can be outstanding (a slot is re-announced only after its
+  // previous stage was consumed), so the parity waits are exact.
+  named_bar_sync(2, 32 * kP);
+  if (lane == 0) {
+    for (int s = pr.w; s < kNS; s += kP) {
+      const uint32_t last = sm.issued[s];
+      if (last != 0xffffffffu) pipe::mbar_wait_drain(&sm.full[s], (last / kNS) & 1u, a.status);
+    }
+  }
+  __syncwarp();
+}
+
+// Lean forward producers for the split path, which walks positions in batch
+// order: per chunk of 32 positions each lane loads one position's offsets (a
+// lane per position), the stage counts
+// are scanned across the warp, and per position only the two lists' begin
+// and length are shuffled out; a stage's row indices are read from global
+// memory (lane j: row j of the stage) when the warp reaches it.  Stage st
+// belongs to warp st % kP; the ring protocol and teardown are Producer's.
+template <int kP, int kSR, int kNS, class Smem>
+__device__ __forceinline__ void produce_forward(Smem& sm, const ForwardArgs& a, int64_t begin, int64_t end, int w,
+                                                int lane) {
+  Producer<kP, kSR, kNS, Smem> pr{&sm, a.status, w, lane, true, a.wait_ns,
+                                 blockIdx.x == a.stall_block ? a.stall_stage : 0xffffffffu};
+  const char* ft = (const char*)a.w.ft;
+  uint32_t st_base = 0;  // stage number of the chunk's first position
+  for (int64_t b0 = begin; b0 < end; b0 += 32) {
+    const int nb = (int)min((int64_t)32, end - b0);
+    Seg s0{0, 0}, s1{0, 0};
+    if (lane < nb) {
+      const int64_t ps = 2 * (b0 + lane);
+      s0 = clamp_seg(a.offsets, ps, a.n_idx);
+      s1 = clamp_seg(a.offsets, ps + 1, a.n_idx);
+    }
+    const uint32_t my_ns = n_stages<kSR>(s0.cnt) + n_stages<kSR>(s1.cnt);
+    uint32_t incl = my_ns;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += x;
+    }
+    const uint32_t excl = incl - my_ns;
+    const uint32_t chunk_stages = __shfl_sync(kFull, incl, 31);
+    for (int q = 0; q < nb; ++q) {
+      uint32_t st = st_base + __shfl_sync(kFull, excl, q);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint32_t beg = __shfl_sync(kFull, p ? s1.beg : s0.beg, q);
+        const uint32_t cnt = __shfl_sync(kFull, p ? s1.cnt : s0.cnt, q);
+        const uint32_t ns = n_stages<kSR>(cnt);
+        for (uint32_t k = (uint32_t)((w - (int)(st % kP) + kP) % kP); k < ns; k += kP) {
+          const uint32_t sn = st + k, first = k * kSR;
+          const uint32_t rows = min((uint32_t)kSR, cnt - first);
+          uint32_t f = (uint32_t)lane < rows ? (uint32_t)a.idx[beg + first + lane] : 0u;
+          if ((uint32_t)lane < rows && f >= (uint32_t)kF) {  // bad index -> the zero row
+            atomicOr(a.status, CNNUE_STATUS_BAD_INDEX);
+            f = kF;
+          }
+          bool go = false;
+          if (lane == 0) go = pr.begin_stage(sn, rows);
+          for (uint32_t j = 0; j < rows; ++j) {
+            const uint32_t fj = __shfl_sync(kFull, f, (int)j);
+            if (lane == 0 && go) pr.copy(sn, j, ft + (size_t)fj * kRowBytes);
+          }
+        }
+        st += ns;
+      }
+    }
+    st_base += chunk_stages;
+  }
+  // Teardown as in produce().
+  named_bar_sync(2, 32 * kP);
+  if (lane == 0) {
+    for (int s = w; s < kNS; s += kP) {
+      const uint32_t last = sm.issued[s];
+      if (last != 0xffffffffu) pipe::mbar_wait_drain(&sm.full[s], (last / kNS) & 1u, a.status);
+    }
+  }
+  __syncwarp();
+}
+
 template <bool kUpdate, bool kWriteAcc>
 __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_kernel(const ForwardArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -516,69 +668,10 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 
   const int64_t begin = a.n * blockIdx.x / gridDim.x;
   const int64_t end = a.n * (blockIdx.x + 1) / gridDim.x;
-  const char* ft = (const char*)a.w.ft;
 
   if (warp >= kBulkConsumers / 32) {
-    // ------------------------------ producers -----------------------------
-    Producer<producers_of(kUpdate)> pr{&sm, a.status, warp - kBulkConsumers / 32, lane, true, a.wait_ns,
-                                       blockIdx.x == a.stall_block ? a.stall_stage : 0xffffffffu};
-    const char* par_lo = (const char*)a.parent;
-    uint32_t st_base = 0;  // stage number of the batch's first position
-    for (int64_t b0 = begin; b0 < end; b0 += 32) {
-      const int nb = (int)min((int64_t)32, end - b0);
-      PosDesc mine;
-      lane_desc<kUpdate>(a, b0 + lane, lane < nb, mine);
-      const uint32_t my_ns = lane < nb ? desc_stages(mine) : 0u;
-      uint32_t incl = my_ns;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const uint32_t x = __shfl_up_sync(kFull, incl, o);
-        if (lane >= o) incl += x;
-      }
-      const uint32_t excl = incl - my_ns;
-      const uint32_t batch_stages = __shfl_sync(kFull, incl, 31);
-      // index-list heads of positions q .. q+3 (a rotating window)
-      ListHead h0{}, h1{}, h2{}, h3{};
-      if (0 < nb) h0 = load_heads<kUpdate>(a, shfl_desc(mine, 0), lane);
-      if (1 < nb) h1 = load_heads<kUpdate>(a, shfl_desc(mine, 1), lane);
-      if (2 < nb) h2 = load_heads<kUpdate>(a, shfl_desc(mine, 2), lane);
-      if (3 < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, 3), lane);
-      for (int q = 0; q < nb; ++q) {
-        const PosDesc cur = shfl_desc(mine, q);
-        const ListHead head = h0;
-        h0 = h1;
-        h1 = h2;
-        h2 = h3;
-        if (q + kPrefetch < nb) h3 = load_heads<kUpdate>(a, shfl_desc(mine, q + kPrefetch), lane);
-        uint32_t st = st_base + __shfl_sync(kFull, excl, q);
-#pragma unroll
-        for (int p = 0; p < 2; ++p) {
-          if (kUpdate) {
-            pr.update_seq(ft, par_lo + (2 * (int64_t)cur.pos + p) * kRowBytes, cur.init[p], a.rem, cur.rem[p],
-                          head.rem[p], a.idx, cur.add[p], head.add[p], st);
-            st += n_stages(cur.init[p] + cur.rem[p].cnt + cur.add[p].cnt);
-          } else {
-            pr.list(ft, a.idx, cur.add[p], head.add[p], st);
-            st += n_stages(cur.add[p].cnt);
-          }
-        }
-      }
-      st_base += batch_stages;
-    }
-    // Teardown: once every producer has stopped announcing stages, stay
-    // resident until the latest announced stage of every ring slot has
-    // landed (after an abort too; bounded), so no copy is in flight into
-    // this CTA's shared memory when it ends.  Only the latest announced phase
-    // of a slot can be outstanding (a slot is re-announced only after its
-    // previous stage was consumed), so the parity waits are exact.
-    named_bar_sync(2, 32 * producers_of(kUpdate));
-    if (lane == 0) {
-      for (int s = pr.w; s < kStages; s += producers_of(kUpdate)) {
-        const uint32_t last = sm.issued[s];
-        if (last != 0xffffffffu) pipe::mbar_wait_drain(&sm.full[s], (last / kStages) & 1u, a.status);
-      }
-    }
-    __syncwarp();
+    produce<kUpdate, producers_of(kUpdate), kStageRows, kStages>(sm, a, begin, end, warp - kBulkConsumers / 32,
+                                                                 lane);
     return;
   }
 
@@ -625,9 +718,9 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
       uint4 v = bias;
       if (kUpdate) {
         if (d.init[p]) v = make_uint4(0, 0, 0, 0);  // the parent row replaces the bias
-        st = consume_update(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, t, lane, a.status, a.wait_ns, v);
+        st = consume_update(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, t * 16, lane, a.status, a.wait_ns, v);
       } else {
-        st = consume_list(sm, st, d.add[p].cnt, t, lane, a.status, a.wait_ns, v);
+        st = consume_list(sm, st, d.add[p].cnt, t * 16, lane, a.status, a.wait_ns, v);
       }
       acc[p] = v;
     }
@@ -705,6 +798,234 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
   }
 }
 
+
+// ===========================================================================
+// Split evaluation, kernel 1 of 2: gather + pack.  Same producers as the
+// fused kernel on a ring of 12 stages x 4 rows (finer stages keep more of a
+// list's rows in flight and waste fewer slots on a list's last stage than
+// 6 x 8).  The four consumer warps own the 16-byte column chunks so that a
+// chunk's pack partner (columns j and j + 512) sits in the same warp: lane
+// l < 16 of warp w owns chunk 16w + l, lane l + 16 owns chunk 64 + 16w + l.
+// After a position's two perspectives are summed, partner lanes swap one
+// perspective's chunk with a single 16-byte shuffle exchange, lane l < 16
+// packs perspective 0 and lane l + 16 perspective 1, and each lane stores its
+// 8 packed bytes: 1024 uint8 per position, written at the position's sorted
+// slot.  The CTAs walk positions in batch order (a CTA's index lists are
+// contiguous, which the producers' per-stage index loads find in L1; the
+// sorted order scatters them and measured ~110 us slower per 65,536).  No
+// barrier joins the consumer warps; the bucket stacks run in kernel 2 over
+// the packed rows.
+// ===========================================================================
+constexpr int kGRows = 4;
+constexpr int kGStages = 12;
+constexpr int kGProducersEval = 4;
+constexpr int kGProducersUpdate = 2;
+constexpr int gproducers_of(bool update) { return update ? kGProducersUpdate : kGProducersEval; }
+constexpr int gather_threads(bool update) { return kBulkConsumers + 32 * gproducers_of(update); }
+
+struct GatherSmem {
+  uint8_t ring[kGRows * kGStages][kRowBytes];
+  uint64_t full[kGStages];
+  uint64_t empty[kGStages];
+  uint32_t issued[kGStages];
+  int abort;
+};
+
+template <bool kUpdate, bool kWriteAcc>
+__global__ void __launch_bounds__(gather_threads(kUpdate), 2) q_gather_kernel(const ForwardArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  GatherSmem& sm = *reinterpret_cast<GatherSmem*>(smem_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGStages; ++s) {
+      pipe::mbar_init(&sm.full[s], 1);
+      pipe::mbar_init(&sm.empty[s], kBulkConsumers / 32);
+      sm.issued[s] = 0xffffffffu;
+    }
+    sm.abort = 0;
+    pipe::mbar_init_fence();
+  }
+  __syncthreads();
+
+  const int64_t begin = a.n * blockIdx.x / gridDim.x;
+  const int64_t end = a.n * (blockIdx.x + 1) / gridDim.x;
+
+  if (warp >= kBulkConsumers / 32) {
+    if (kUpdate)
+      produce<true, gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32, lane);
+    else
+      produce_forward<gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32,
+                                                                lane);
+    return;
+  }
+
+  // -------------------------------- consumers ------------------------------
+  const bool lo = lane < 16;
+  const int sub = lane & 15;
+  const int chunk = lo ? 16 * warp + sub : 64 + 16 * warp + sub;  // columns [8 chunk, 8 chunk + 8)
+  const int col_byte = chunk * 16;
+  const uint4 bias = __ldg((const uint4*)((const char*)a.w.bias + col_byte));
+  uint32_t st = 0;  // next stage number
+  PosDesc nxt;
+  if (begin < end) nxt = finish_desc<kUpdate>(a, load_raw<kUpdate>(a, (uint32_t)begin, 0));
+  uint32_t slot_n = begin < end ? a.inv[begin] : 0u;  // sorted slot of the next position
+
+  for (int64_t i = begin; i < end; ++i) {
+    const PosDesc d = nxt;
+    const uint32_t slot = slot_n;
+    const bool has_next = i + 1 < end;
+    RawDesc raw;
+    if (has_next) {
+      raw = load_raw<kUpdate>(a, (uint32_t)(i + 1), 0);
+      slot_n = a.inv[i + 1];
+    }
+
+    uint4 acc[2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint4 v = bias;
+      if (kUpdate) {
+        if (d.init[p]) v = make_uint4(0, 0, 0, 0);  // the parent row replaces the bias
+        st = consume_update<kGRows, kGStages>(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, col_byte, lane,
+                                              a.status, a.wait_ns, v);
+      } else {
+        st = consume_list<kGRows, kGStages>(sm, st, d.add[p].cnt, col_byte, lane, a.status, a.wait_ns, v);
+      }
+      acc[p] = v;
+    }
+    if (kWriteAcc) {
+      *(uint4*)((char*)(a.acc_out + (2 * (int64_t)d.pos) * kCols) + col_byte) = acc[0];
+      *(uint4*)((char*)(a.acc_out + (2 * (int64_t)d.pos + 1) * kCols) + col_byte) = acc[1];
+    }
+    // lane l < 16 keeps perspective 0's low chunk and takes its high partner;
+    // lane l + 16 keeps perspective 1's high chunk and takes its low partner
+    const uint4 give = lo ? acc[1] : acc[0];
+    uint4 take;
+    take.x = __shfl_xor_sync(kFull, give.x, 16);
+    take.y = __shfl_xor_sync(kFull, give.y, 16);
+    take.z = __shfl_xor_sync(kFull, give.z, 16);
+    take.w = __shfl_xor_sync(kFull, give.w, 16);
+    const uint4 plo = lo ? acc[0] : take;  // columns j of the packed perspective
+    const uint4 phi = lo ? take : acc[1];  // columns j + 512
+    uint2 out;
+    out.x = pack_quad(plo.x, phi.x, plo.y, phi.y);
+    out.y = pack_quad(plo.z, phi.z, plo.w, phi.w);
+    *(uint2*)(a.packed + (size_t)slot * CNNUE_Q_PACKED + (lo ? 0 : CNNUE_Q_HALF) + 8 * (16 * warp + sub)) = out;
+    if (has_next) nxt = finish_desc<kUpdate>(a, raw);
+  }
+}
+
+// ===========================================================================
+// Split evaluation, kernel 2 of 2: the bucket stacks over the packed rows.
+// The sorted order keeps each bucket's rows contiguous; one CTA takes one
+// tile of up to 128 rows of one bucket (tile g of the buckets' tiles in
+// bucket order), one thread per row.  The bucket's L1 weights (16 KB) and
+// the tile's rows, 128 bytes of K at a time, are staged in shared memory
+// (row stride 144 bytes: conflict-free 16-byte reads); each thread forms its
+// 16 L1 sums with dp4a against broadcast weight reads, then L2 and L3 in
+// registers, and writes its score at the position's original index.
+// ===========================================================================
+constexpr int kStackTile = 128;
+constexpr int kStackKChunk = 128;
+constexpr int kStackStride = kStackKChunk + 16;
+
+struct StackSmem {
+  uint8_t w1[kL1][CNNUE_Q_PACKED];
+  uint8_t x[kStackTile][kStackStride];
+  int8_t w2[kL2][kL1];
+  int32_t b2[kL2];
+  int8_t w3[kL2];
+  int32_t b1[kL1];
+  int bucket, start, count;
+};
+
+__global__ void __launch_bounds__(kStackTile) q_stack_kernel(const ForwardArgs a, const WorkspaceHeader* hdr) {
+  __shared__ __align__(16) StackSmem sm;
+  const int t = threadIdx.x;
+  if (t == 0) {
+    // tile blockIdx.x among the buckets' tiles, in bucket order
+    uint32_t g = blockIdx.x;
+    int b = 0;
+    sm.bucket = -1;
+    for (; b < kNB; ++b) {
+      const uint32_t c = hdr->counts[b];
+      const uint32_t tiles = (c + kStackTile - 1) / kStackTile;
+      if (g < tiles) {
+        sm.bucket = b;
+        sm.start = (int)(hdr->cursors[b] + g * kStackTile);
+        sm.count = (int)min((uint32_t)kStackTile, c - g * kStackTile);
+        break;
+      }
+      g -= tiles;
+    }
+  }
+  __syncthreads();
+  const int b = sm.bucket;
+  if (b < 0) return;  // past the last tile (uniform across the CTA)
+  const int start = sm.start, count = sm.count;
+  {
+    const uint4* src = (const uint4*)(a.w.l1w + (size_t)b * kL1 * CNNUE_Q_PACKED);
+    uint4* dst = (uint4*)&sm.w1[0][0];
+    for (int k = t; k < kL1 * CNNUE_Q_PACKED / 16; k += kStackTile) dst[k] = __ldg(src + k);
+    if (t < kL2 * kL1 / 16) ((uint4*)&sm.w2[0][0])[t] = __ldg((const uint4*)(a.w.l2w + (size_t)b * kL2 * kL1) + t);
+    if (t < kL2) {
+      sm.b2[t] = __ldg(a.w.l2b + b * kL2 + t);
+      sm.w3[t] = __ldg(a.w.l3w + b * kL2 + t);
+    }
+    if (t < kL1) sm.b1[t] = __ldg(a.w.l1b + b * kL1 + t);
+  }
+  int32_t s1[kL1];
+#pragma unroll
+  for (int o = 0; o < kL1; ++o) s1[o] = 0;
+  const int64_t last_row = a.n - 1;
+  for (int kc = 0; kc < CNNUE_Q_PACKED; kc += kStackKChunk) {
+    __syncthreads();  // the previous chunk's reads (and the weight stores) are done
+    // coalesced copy of the tile's K chunk: 8 threads per 128-byte row piece
+#pragma unroll
+    for (int j = 0; j < kStackTile * kStackKChunk / 16 / kStackTile; ++j) {
+      const int id = t + kStackTile * j;
+      const int r = id >> 3, part = id & 7;
+      const int64_t row = min((int64_t)start + r, last_row);
+      *(uint4*)&sm.x[r][part * 16] = *(const uint4*)(a.packed + (size_t)row * CNNUE_Q_PACKED + kc + part * 16);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < kStackKChunk / 16; ++q) {
+      const uint4 xv = *(const uint4*)&sm.x[t][q * 16];
+#pragma unroll
+      for (int o = 0; o < kL1; ++o) {
+        const uint4 wv = *(const uint4*)&sm.w1[o][kc + q * 16];  // broadcast
+        int32_t acc = s1[o];
+        acc = __dp4a((int)xv.x, (int)wv.x, acc);
+        acc = __dp4a((int)xv.y, (int)wv.y, acc);
+        acc = __dp4a((int)xv.z, (int)wv.z, acc);
+        acc = __dp4a((int)xv.w, (int)wv.w, acc);
+        s1[o] = acc;
+      }
+    }
+  }
+  if (t >= count) return;
+  uint32_t y1[4] = {0, 0, 0, 0};
+#pragma unroll
+  for (int o = 0; o < kL1; ++o) {
+    const uint32_t y = (uint32_t)min(max((s1[o] + sm.b1[o]) >> 6, 0), 127);
+    y1[o >> 2] |= y << (8 * (o & 3));
+  }
+  int32_t s3 = 0;
+#pragma unroll 8
+  for (int j = 0; j < kL2; ++j) {
+    const uint4 wv = *(const uint4*)&sm.w2[j][0];
+    int32_t s2 = sm.b2[j];
+    s2 = __dp4a((int)y1[0], (int)wv.x, s2);
+    s2 = __dp4a((int)y1[1], (int)wv.y, s2);
+    s2 = __dp4a((int)y1[2], (int)wv.z, s2);
+    s2 = __dp4a((int)y1[3], (int)wv.w, s2);
+    s3 += (int32_t)sm.w3[j] * min(max(s2 >> 6, 0), 127);
+  }
+  a.scores[a.perm[start + t]] = __ldg(a.w.l3b + b) + s3;
+}
+
 }  // namespace q
 }  // namespace cnnue
 
@@ -719,8 +1040,9 @@ struct cnnue_q_model {
   DevWeights w{};
   void* blob = nullptr;
   int sm_count = 0;
-  int grid_eval = 0;
-  int grid_update = 0;
+  int grid_eval = 0;     // fused kernel (the no-allocation entry point)
+  int grid_gather = 0;   // split path, forward
+  int grid_gather_update = 0;
   // Staging for cnnue_q_forward_host.
   void* stage = nullptr;
   size_t stage_bytes = 0;
@@ -730,21 +1052,30 @@ namespace {
 
 int check_launch(const char* what) { return check_launch_error(what); }
 
+// Workspace of the split path: the bucket-sort workspace, then the packed
+// activations [n][1024] uint8 in sorted order, then the sorted slot of every
+// position [n] uint32.
+size_t packed_offset(int64_t n) { return align_up(bucket_workspace_bytes(n), 256); }
+size_t inv_offset(int64_t n) { return packed_offset(n) + align_up((size_t)(n > 0 ? n : 0) * CNNUE_Q_PACKED, 256); }
+size_t q_workspace_bytes(int64_t n) { return inv_offset(n) + align_up((size_t)(n > 0 ? n : 0) * 4, 256); }
+uint32_t* ws_inv(void* ws, int64_t n) { return (uint32_t*)((char*)ws + inv_offset(n)); }
+
 int validate_common(const cnnue_q_model* m, int64_t n, void* ws, size_t ws_bytes) {
   if (!m) return set_error(CNNUE_ERR_INVALID_ARG, "model is null");
   if (n < 0 || n > (int64_t)INT32_MAX)
     return set_error(CNNUE_ERR_INVALID_ARG, "n_positions %lld out of range", (long long)n);
   if (n > 0 && !ws) return set_error(CNNUE_ERR_INVALID_ARG, "workspace is null");
-  if (n > 0 && ws_bytes < bucket_workspace_bytes(n))
+  if (((uintptr_t)ws & 255u) != 0) return set_error(CNNUE_ERR_INVALID_ARG, "workspace must be 256-byte aligned");
+  if (n > 0 && ws_bytes < q_workspace_bytes(n))
     return set_error(CNNUE_ERR_WORKSPACE, "workspace %zu bytes < %zu required", ws_bytes,
-                     bucket_workspace_bytes(n));
+                     q_workspace_bytes(n));
   return CNNUE_OK;
 }
 
 int launch_sort(const cnnue_q_model* m, const uint32_t* d_offsets, uint32_t n_indices,
-                const uint8_t* d_count0, int64_t n, void* ws, cudaStream_t s) {
+                const uint8_t* d_count0, int64_t n, void* ws, cudaStream_t s, uint32_t* inv) {
   (void)m;
-  return launch_bucket_sort(d_offsets, n_indices, d_count0, n, 1, kNB, ws, s);
+  return launch_bucket_sort(d_offsets, n_indices, d_count0, n, 1, kNB, ws, s, inv);
 }
 
 // Arguments with the default wait limit and the stall hook off.
@@ -756,6 +1087,14 @@ ForwardArgs base_args() {
   return a;
 }
 
+// The bucket stacks of the split path over the packed rows.
+int launch_stack(const ForwardArgs& a, const WorkspaceView& v, cudaStream_t s) {
+  const int64_t tiles = (a.n + kStackTile - 1) / kStackTile + kNB;  // bound on the buckets' tiles
+  q_stack_kernel<<<(unsigned)tiles, kStackTile, 0, s>>>(a, v.hdr);
+  return check_launch("q_stack_kernel");
+}
+
+// Forward over the sorted order (split path): gather + pack, then the stacks.
 int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
                 const uint32_t* d_offsets, int64_t n, int32_t* d_scores, int16_t* d_acc, void* ws,
                 cudaStream_t s, const ForwardArgs& hooks = base_args()) {
@@ -767,16 +1106,41 @@ int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
   a.offsets = d_offsets;
   a.acc_out = d_acc;
   a.scores = d_scores;
+  a.packed = (uint8_t*)ws + packed_offset(n);
+  a.inv = ws_inv(ws, n);
+  a.natural = 1;
+  a.n = n;
+  a.perm = v.perm;
+  a.sorted_bucket = v.sorted_bucket;
+  a.status = &v.hdr->status;
+  const int grid = (int)std::min<int64_t>(m->grid_gather, n);
+  const size_t smem = sizeof(GatherSmem);
+  if (d_acc)
+    q_gather_kernel<false, true><<<grid, gather_threads(false), smem, s>>>(a);
+  else
+    q_gather_kernel<false, false><<<grid, gather_threads(false), smem, s>>>(a);
+  const int st = check_launch("q_gather_kernel");
+  if (st) return st;
+  return launch_stack(a, v, s);
+}
+
+// Fused single-kernel forward (gather, pack and stacks in one kernel; needs
+// only the bucket-sort workspace): the no-allocation entry point's path.
+int launch_fused(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
+                 const uint32_t* d_offsets, int64_t n, int32_t* d_scores, void* ws, cudaStream_t s) {
+  WorkspaceView v = carve_workspace(ws, n);
+  ForwardArgs a = base_args();
+  a.w = m->w;
+  a.idx = d_idx;
+  a.n_idx = n_idx;
+  a.offsets = d_offsets;
+  a.scores = d_scores;
   a.n = n;
   a.perm = v.perm;
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
   const int grid = (int)std::min<int64_t>(m->grid_eval, n);
-  const size_t smem = sizeof(BulkSmem);
-  if (d_acc)
-    q_bulk_kernel<false, true><<<grid, bulk_threads(false), smem, s>>>(a);
-  else
-    q_bulk_kernel<false, false><<<grid, bulk_threads(false), smem, s>>>(a);
+  q_bulk_kernel<false, false><<<grid, bulk_threads(false), sizeof(BulkSmem), s>>>(a);
   return check_launch("q_bulk_kernel");
 }
 
@@ -850,13 +1214,17 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device);
   const int smem = (int)sizeof(BulkSmem);
   cudaFuncSetAttribute(q_bulk_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  cudaFuncSetAttribute(q_bulk_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  cudaFuncSetAttribute(q_bulk_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  int occ_eval = 0, occ_upd = 0;
+  const int gsmem = (int)sizeof(GatherSmem);
+  cudaFuncSetAttribute(q_gather_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+  cudaFuncSetAttribute(q_gather_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+  cudaFuncSetAttribute(q_gather_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+  int occ_eval = 0, occ_g = 0, occ_gu = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_bulk_kernel<false, false>, bulk_threads(false), smem);
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_upd, q_bulk_kernel<true, true>, bulk_threads(true), smem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_g, q_gather_kernel<false, false>, gather_threads(false), gsmem);
+  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_gu, q_gather_kernel<true, true>, gather_threads(true), gsmem);
   m->grid_eval = m->sm_count * std::max(occ_eval, 1);
-  m->grid_update = m->sm_count * std::max(occ_upd, 1);
+  m->grid_gather = m->sm_count * std::max(occ_g, 1);
+  m->grid_gather_update = m->sm_count * std::max(occ_gu, 1);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     cudaFree(m->blob);
@@ -876,7 +1244,7 @@ int cnnue_q_model_destroy(cnnue_q_model* m) {
   return CNNUE_OK;
 }
 
-size_t cnnue_q_workspace_bytes(int64_t n_positions) { return bucket_workspace_bytes(n_positions); }
+size_t cnnue_q_workspace_bytes(int64_t n_positions) { return q_workspace_bytes(n_positions); }
 
 int cnnue_q_bucket_sort(const cnnue_q_model* m, const uint32_t* d_offsets, uint32_t n_indices,
                         int64_t n, void* ws, size_t ws_bytes, void* stream) {
@@ -886,7 +1254,7 @@ int cnnue_q_bucket_sort(const cnnue_q_model* m, const uint32_t* d_offsets, uint3
   if (!d_offsets) return set_error(CNNUE_ERR_INVALID_ARG, "null offsets");
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
-  return launch_sort(m, d_offsets, n_indices, nullptr, n, ws, (cudaStream_t)stream);
+  return launch_sort(m, d_offsets, n_indices, nullptr, n, ws, (cudaStream_t)stream, ws_inv(ws, n));
 }
 
 int cnnue_q_forward_sorted(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
@@ -914,7 +1282,7 @@ int cnnue_q_forward_acc(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t 
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
-  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s);
+  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s, ws_inv(ws, n));
   if (st) return st;
   return launch_eval(m, d_idx, n_idx, d_offsets, n, d_scores, d_acc, ws, s);
 }
@@ -939,7 +1307,7 @@ int cnnue_q_forward_host(cnnue_q_model* m, const uint16_t* h_idx, uint32_t n_idx
   const size_t b_idx = align_up((size_t)n_idx * 2, 256);
   const size_t b_off = align_up((size_t)(2 * n + 1) * 4, 256);
   const size_t b_sc = align_up((size_t)n * 4, 256);
-  const size_t b_ws = align_up(bucket_workspace_bytes(n), 256);
+  const size_t b_ws = align_up(q_workspace_bytes(n), 256);
   const size_t need = b_idx + b_off + b_sc + b_ws;
   if (need > m->stage_bytes) {
     if (m->stage) {
@@ -958,7 +1326,7 @@ int cnnue_q_forward_host(cnnue_q_model* m, const uint16_t* h_idx, uint32_t n_idx
   void* ws = p + b_idx + b_off + b_sc;
   if (n_idx) CNNUE_CUDA_TRY(cudaMemcpyAsync(d_idx, h_idx, (size_t)n_idx * 2, cudaMemcpyHostToDevice, s));
   CNNUE_CUDA_TRY(cudaMemcpyAsync(d_off, h_offsets, (size_t)(2 * n + 1) * 4, cudaMemcpyHostToDevice, s));
-  int st = launch_sort(m, d_off, n_idx, nullptr, n, ws, s);
+  int st = launch_sort(m, d_off, n_idx, nullptr, n, ws, s, ws_inv(ws, n));
   if (st) return st;
   st = launch_eval(m, d_idx, n_idx, d_off, n, d_sc, nullptr, ws, s);
   if (st) return st;
@@ -983,7 +1351,7 @@ int cnnue_q_forward_stall_test(const cnnue_q_model* m, const uint16_t* d_idx, ui
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
-  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s);
+  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s, ws_inv(ws, n));
   if (st) return st;
   ForwardArgs hooks = base_args();
   hooks.wait_ns = wait_limit_ns;
@@ -1008,7 +1376,7 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
-  st = launch_sort(m, nullptr, 0, d_count0, n, ws, s);
+  st = launch_sort(m, nullptr, 0, d_count0, n, ws, s, ws_inv(ws, n));
   if (st) return st;
   st = launch_offsets_check(d_rem_offsets, n_rem, 2 * n, ws, s);
   if (st) return st;
@@ -1016,6 +1384,9 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   if (st) return st;
   WorkspaceView v = carve_workspace(ws, n);
   ForwardArgs a = base_args();
+  a.packed = (uint8_t*)ws + packed_offset(n);
+  a.inv = ws_inv(ws, n);
+  a.natural = 1;
   a.w = m->w;
   a.idx = d_add;
   a.n_idx = n_add;
@@ -1031,9 +1402,11 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   a.perm = v.perm;
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
-  const int grid = (int)std::min<int64_t>(m->grid_update, n);
-  q_bulk_kernel<true, true><<<grid, bulk_threads(true), sizeof(BulkSmem), s>>>(a);
-  return check_launch("q_bulk_kernel<update>");
+  const int grid = (int)std::min<int64_t>(m->grid_gather_update, n);
+  q_gather_kernel<true, true><<<grid, gather_threads(true), sizeof(GatherSmem), s>>>(a);
+  st = check_launch("q_gather_kernel<update>");
+  if (st) return st;
+  return launch_stack(a, v, s);
 }
 
 }  // extern "C"
@@ -1093,9 +1466,9 @@ extern "C" int cnnue_q_forward_noalloc(const cnnue_q_model* m, const uint16_t* d
   cudaStream_t s = (cudaStream_t)stream;
   // launch_sort zeroes the scratch header (status word, bucket counts and
   // cursors); the rest of the scratch is fully rewritten by every call.
-  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s);
+  st = launch_sort(m, d_offsets, n_idx, nullptr, n, ws, s, nullptr);
   if (st) return st;
-  st = launch_eval(m, d_idx, n_idx, d_offsets, n, d_scores, nullptr, ws, s);
+  st = launch_fused(m, d_idx, n_idx, d_offsets, n, d_scores, ws, s);
   if (st) return st;
   int status = CNNUE_OK;
   st = cnnue_read_status(ws, stream, &status);

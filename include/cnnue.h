@@ -89,7 +89,9 @@ int cnnue_q_model_create(const cnnue_q_weights* weights, int device, cnnue_q_mod
 int cnnue_q_model_destroy(cnnue_q_model* model);
 
 /* Bytes of device workspace cnnue_q_forward / cnnue_q_update need for
- * `n_positions` positions (bucket sort + status word). */
+ * `n_positions` positions: the status word, the bucket sort and the packed
+ * activations (1 KB per position).  Workspaces are 256-byte aligned
+ * (cudaMalloc'd memory is). */
 size_t cnnue_q_workspace_bytes(int64_t n_positions);
 
 /* Reads and clears the status word of a workspace after the work queued on
@@ -108,8 +110,9 @@ int cnnue_read_status(void* d_workspace, void* stream, int* status_out);
  *              d_indices[d_offsets[2p+s] .. d_offsets[2p+s+1])
  *   d_scores   [n_positions] int32 output
  * Two stages, also callable separately: cnnue_q_bucket_sort (groups positions
- * by bucket into the workspace) and cnnue_q_forward_sorted (the fused
- * gather/pack/stack kernel over the sorted order). */
+ * by bucket into the workspace) and cnnue_q_forward_sorted (over the sorted
+ * order: the gather + pack kernel, which writes every position's 1024 packed
+ * bytes into the workspace, then the bucket-stack kernel). */
 int cnnue_q_forward(const cnnue_q_model* model, const uint16_t* d_indices, uint32_t n_indices,
                     const uint32_t* d_offsets, int64_t n_positions, int32_t* d_scores,
                     void* d_workspace, size_t workspace_bytes, void* stream);

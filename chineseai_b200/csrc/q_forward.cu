@@ -800,10 +800,11 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 
 
 // ===========================================================================
-// Split evaluation, kernel 1 of 2: gather + pack.  Same producers as the
-// fused kernel on a ring of 12 stages x 4 rows (finer stages keep more of a
-// list's rows in flight and waste fewer slots on a list's last stage than
-// 6 x 8).  The four consumer warps own the 16-byte column chunks so that a
+// Split evaluation, kernel 1 of 2: gather + pack.  Same ring protocol as the
+// fused kernel, on 6 stages x 4 rows per CTA and 4 CTAs per SM (measured per
+// 65,536 positions, gather + stacks: 0.486 ms with 12 x 4 rows and 2 CTAs per
+// SM, 0.404 with 8 x 4 and 3, 0.381 with 6 x 4 and 4, 0.406 with 4 x 4 and 5;
+// 4 producer warps per CTA beat 2, 3, 5, 6 and 8).  The four consumer warps own the 16-byte column chunks so that a
 // chunk's pack partner (columns j and j + 512) sits in the same warp: lane
 // l < 16 of warp w owns chunk 16w + l, lane l + 16 owns chunk 64 + 16w + l.
 // After a position's two perspectives are summed, partner lanes swap one
@@ -817,7 +818,8 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 // the packed rows.
 // ===========================================================================
 constexpr int kGRows = 4;
-constexpr int kGStages = 12;
+constexpr int kGStages = 6;
+constexpr int kGMinBlocks = 4;  // CTAs per SM (ring 48 KB each)
 constexpr int kGProducersEval = 4;
 constexpr int kGProducersUpdate = 2;
 constexpr int gproducers_of(bool update) { return update ? kGProducersUpdate : kGProducersEval; }
@@ -832,7 +834,7 @@ struct GatherSmem {
 };
 
 template <bool kUpdate, bool kWriteAcc>
-__global__ void __launch_bounds__(gather_threads(kUpdate), 2) q_gather_kernel(const ForwardArgs a) {
+__global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather_kernel(const ForwardArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GatherSmem& sm = *reinterpret_cast<GatherSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

@@ -31,9 +31,12 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "pipeline.cuh"
+#include "tcgen05.cuh"
+#include "tma.cuh"
 
 namespace cnnue {
 namespace q {
@@ -918,39 +921,60 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
   }
 }
 
-// ===========================================================================
-// Split evaluation, kernel 2 of 2: the bucket stacks over the packed rows.
-// The sorted order keeps each bucket's rows contiguous; one CTA takes one
-// tile of up to 128 rows of one bucket (tile g of the buckets' tiles in
-// bucket order), one thread per row.  The bucket's L1 weights (16 KB) and
-// the tile's rows, 128 bytes of K at a time, are staged in shared memory
-// (row stride 144 bytes: conflict-free 16-byte reads); each thread forms its
-// 16 L1 sums with dp4a against broadcast weight reads, then L2 and L3 in
-// registers, and writes its score at the position's original index.
-// ===========================================================================
-constexpr int kStackTile = 128;
-constexpr int kStackKChunk = 128;
-constexpr int kStackStride = kStackKChunk + 16;
+constexpr int kStackTile = 128;  // rows of one bucket per stack tile
 
-struct StackSmem {
-  uint8_t w1[kL1][CNNUE_Q_PACKED];
-  uint8_t x[kStackTile][kStackStride];
-  int8_t w2[kL2][kL1];
+// ===========================================================================
+// Split evaluation, kernel 2 of 2 (tensor cores): the bucket stacks over the
+// packed rows.  L1 of a tile of 128 rows of one bucket is the bucket GEMM
+// D[128 x 16] = X[128 x 1024] (uint8) . W1[16 x 1024]^T (int8) on tcgen05
+// (kind::i8, int32 accumulator in TMEM): X arrives by 2-D TMA in 128-byte K
+// chunks (128B swizzle) through a 4-stage ring, W1 by one bulk copy of the
+// bucket's pre-tiled weights.  Warps 0-3 then read their rows' 16 sums from
+// TMEM (lane = row) and run the L1 activation, L2 and L3 in registers.
+// Warp 4 loads (and owns TMEM), warp 5 issues the MMAs.
+// ===========================================================================
+constexpr int kTcStages = 4;
+constexpr int kTcChunk = 128;                          // K bytes per stage
+constexpr int kTcChunks = CNNUE_Q_PACKED / kTcChunk;   // 8
+constexpr int kTcThreads = 192;
+constexpr int kTcTileBytes = kStackTile * kTcChunk;    // 16 KB
+constexpr int kTcWTileBytes = kL1 * kTcChunk;          // 2 KB
+
+struct StackTcSmem {
+  alignas(1024) uint8_t a[kTcStages][kTcTileBytes];
+  alignas(1024) uint8_t b[kTcChunks][kTcWTileBytes];
+  uint64_t loaded[kTcStages];
+  uint64_t empty[kTcStages];
+  uint64_t wload;
+  uint64_t accum;
+  uint64_t drain;
+  alignas(16) int8_t w2[kL2][kL1];  // read and written as 16-byte rows
   int32_t b2[kL2];
-  int8_t w3[kL2];
   int32_t b1[kL1];
+  int8_t w3[kL2];
+  uint32_t tmem_base;
   int bucket, start, count;
+  int abort;
 };
 
-__global__ void __launch_bounds__(kStackTile) q_stack_kernel(const ForwardArgs a, const WorkspaceHeader* hdr) {
-  __shared__ __align__(16) StackSmem sm;
-  const int t = threadIdx.x;
-  if (t == 0) {
+// Byte offset of (row, k) of a K-chunk tile (rows of 128 bytes, 128B swizzle:
+// the 16-byte chunk c of row r sits at chunk position c ^ (r % 8)).
+__host__ __device__ constexpr uint32_t sw128_offset(int row, int k) {
+  return (uint32_t)(row * 128 + ((((k >> 4) ^ row) & 7) << 4) + (k & 15));
+}
+
+__global__ void __launch_bounds__(kTcThreads) q_stack_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                                                                const ForwardArgs a, const uint8_t* w1tiles,
+                                                                const WorkspaceHeader* hdr) {
+  extern __shared__ uint8_t smem_raw[];
+  StackTcSmem& sm =
+      *reinterpret_cast<StackTcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
     // tile blockIdx.x among the buckets' tiles, in bucket order
     uint32_t g = blockIdx.x;
-    int b = 0;
     sm.bucket = -1;
-    for (; b < kNB; ++b) {
+    for (int b = 0; b < kNB; ++b) {
       const uint32_t c = hdr->counts[b];
       const uint32_t tiles = (c + kStackTile - 1) / kStackTile;
       if (g < tiles) {
@@ -961,71 +985,114 @@ __global__ void __launch_bounds__(kStackTile) q_stack_kernel(const ForwardArgs a
       }
       g -= tiles;
     }
+    for (int s = 0; s < kTcStages; ++s) {
+      pipe::mbar_init(&sm.loaded[s], 1);
+      pipe::mbar_init(&sm.empty[s], 1);
+    }
+    pipe::mbar_init(&sm.wload, 1);
+    pipe::mbar_init(&sm.accum, 1);
+    pipe::mbar_init(&sm.drain, 1);
+    sm.abort = 0;
+    pipe::mbar_init_fence();
   }
   __syncthreads();
   const int b = sm.bucket;
-  if (b < 0) return;  // past the last tile (uniform across the CTA)
-  const int start = sm.start, count = sm.count;
-  {
-    const uint4* src = (const uint4*)(a.w.l1w + (size_t)b * kL1 * CNNUE_Q_PACKED);
-    uint4* dst = (uint4*)&sm.w1[0][0];
-    for (int k = t; k < kL1 * CNNUE_Q_PACKED / 16; k += kStackTile) dst[k] = __ldg(src + k);
-    if (t < kL2 * kL1 / 16) ((uint4*)&sm.w2[0][0])[t] = __ldg((const uint4*)(a.w.l2w + (size_t)b * kL2 * kL1) + t);
-    if (t < kL2) {
-      sm.b2[t] = __ldg(a.w.l2b + b * kL2 + t);
-      sm.w3[t] = __ldg(a.w.l3w + b * kL2 + t);
-    }
-    if (t < kL1) sm.b1[t] = __ldg(a.w.l1b + b * kL1 + t);
+  if (b < 0) return;  // past the last tile (uniform across the CTA; no TMEM held yet)
+  if (warp == 4) {
+    tc::tmem_alloc(pipe::smem_addr(&sm.tmem_base), 32);
+    tc::tmem_relinquish();
   }
-  int32_t s1[kL1];
-#pragma unroll
-  for (int o = 0; o < kL1; ++o) s1[o] = 0;
-  const int64_t last_row = a.n - 1;
-  for (int kc = 0; kc < CNNUE_Q_PACKED; kc += kStackKChunk) {
-    __syncthreads();  // the previous chunk's reads (and the weight stores) are done
-    // coalesced copy of the tile's K chunk: 8 threads per 128-byte row piece
-#pragma unroll
-    for (int j = 0; j < kStackTile * kStackKChunk / 16 / kStackTile; ++j) {
-      const int id = t + kStackTile * j;
-      const int r = id >> 3, part = id & 7;
-      const int64_t row = min((int64_t)start + r, last_row);
-      *(uint4*)&sm.x[r][part * 16] = *(const uint4*)(a.packed + (size_t)row * CNNUE_Q_PACKED + kc + part * 16);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < kStackKChunk / 16; ++q) {
-      const uint4 xv = *(const uint4*)&sm.x[t][q * 16];
+  if (tid < kL2 * kL1 / 16) ((uint4*)&sm.w2[0][0])[tid] = __ldg((const uint4*)(a.w.l2w + (size_t)b * kL2 * kL1) + tid);
+  if (tid < kL2) {
+    sm.b2[tid] = __ldg(a.w.l2b + b * kL2 + tid);
+    sm.w3[tid] = __ldg(a.w.l3w + b * kL2 + tid);
+  }
+  if (tid < kL1) sm.b1[tid] = __ldg(a.w.l1b + b * kL1 + tid);
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = sm.tmem_base;
+  const int start = sm.start, count = sm.count;
+
+  if (warp < 4) {
+    // ---- epilogue: TMEM lane = row of the tile.
+    const bool ok = pipe::mbar_wait(&sm.accum, 0, &sm.abort, a.status, a.wait_ns);
+    tc::fence_after_sync();
+    uint32_t v[16];
+    __syncwarp();
+    tc::tmem_ld16(tmem + ((uint32_t)(32 * warp) << 16), v);
+    tc::wait_ld();
+    const int t = tid;
+    if (ok && t < count) {
+      uint32_t y1[4] = {0, 0, 0, 0};
 #pragma unroll
       for (int o = 0; o < kL1; ++o) {
-        const uint4 wv = *(const uint4*)&sm.w1[o][kc + q * 16];  // broadcast
-        int32_t acc = s1[o];
-        acc = __dp4a((int)xv.x, (int)wv.x, acc);
-        acc = __dp4a((int)xv.y, (int)wv.y, acc);
-        acc = __dp4a((int)xv.z, (int)wv.z, acc);
-        acc = __dp4a((int)xv.w, (int)wv.w, acc);
-        s1[o] = acc;
+        const uint32_t y = (uint32_t)min(max(((int32_t)v[o] + sm.b1[o]) >> 6, 0), 127);
+        y1[o >> 2] |= y << (8 * (o & 3));
+      }
+      int32_t s3 = 0;
+#pragma unroll 8
+      for (int j = 0; j < kL2; ++j) {
+        const uint4 wv = *(const uint4*)&sm.w2[j][0];
+        int32_t s2 = sm.b2[j];
+        s2 = __dp4a((int)y1[0], (int)wv.x, s2);
+        s2 = __dp4a((int)y1[1], (int)wv.y, s2);
+        s2 = __dp4a((int)y1[2], (int)wv.z, s2);
+        s2 = __dp4a((int)y1[3], (int)wv.w, s2);
+        s3 += (int32_t)sm.w3[j] * min(max(s2 >> 6, 0), 127);
+      }
+      a.scores[a.perm[start + t]] = __ldg(a.w.l3b + b) + s3;
+    }
+  } else if (warp == 4) {
+    // ---- loads: the bucket's W1 tiles once, then X chunk by chunk.
+    if (lane == 0) {
+      pipe::mbar_arrive_expect_tx(&sm.wload, kTcChunks * kTcWTileBytes);
+      pipe::bulk_copy_g2s(&sm.b[0][0], w1tiles + (size_t)b * kTcChunks * kTcWTileBytes, kTcChunks * kTcWTileBytes,
+                          &sm.wload);
+      int issued = 0;
+      for (int kc = 0; kc < kTcChunks; ++kc) {
+        const int s = kc % kTcStages, u = kc / kTcStages;
+        if (u > 0 && !pipe::mbar_wait(&sm.empty[s], (u - 1) & 1, &sm.abort, a.status, a.wait_ns)) break;
+        pipe::mbar_arrive_expect_tx(&sm.loaded[s], kTcTileBytes);
+        tc::tma_load_2d(pipe::smem_addr(sm.a[s]), &tmap_x, kc * kTcChunk, start, pipe::smem_addr(&sm.loaded[s]));
+        ++issued;
+      }
+      // after an abort: let the copies in flight land before the CTA ends
+      if (sm.abort) {
+        pipe::mbar_wait_drain(&sm.wload, 0, a.status);
+        for (int kc = max(0, issued - kTcStages); kc < issued; ++kc)
+          pipe::mbar_wait_drain(&sm.loaded[kc % kTcStages], (kc / kTcStages) & 1, a.status);
       }
     }
-  }
-  if (t >= count) return;
-  uint32_t y1[4] = {0, 0, 0, 0};
+    __syncwarp();
+  } else {
+    // ---- MMA issuer.
+    if (lane == 0) {
+      constexpr uint32_t idesc = tc::idesc_u8s8_s32(kStackTile, kL1);
+      bool ok = pipe::mbar_wait(&sm.wload, 0, &sm.abort, a.status, a.wait_ns);
+      for (int kc = 0; ok && kc < kTcChunks; ++kc) {
+        const int s = kc % kTcStages, u = kc / kTcStages;
+        if (!pipe::mbar_wait(&sm.loaded[s], u & 1, &sm.abort, a.status, a.wait_ns)) break;
+        tc::fence_after_sync();
+        const uint32_t a0 = pipe::smem_addr(sm.a[s]), b0 = pipe::smem_addr(sm.b[kc]);
 #pragma unroll
-  for (int o = 0; o < kL1; ++o) {
-    const uint32_t y = (uint32_t)min(max((s1[o] + sm.b1[o]) >> 6, 0), 127);
-    y1[o >> 2] |= y << (8 * (o & 3));
+        for (int kk = 0; kk < kTcChunk / 32; ++kk) {
+          const uint64_t ad = tc::smem_desc(a0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+          const uint64_t bd = tc::smem_desc(b0 + kk * 32, 0, 1024, tc::kSwizzle128B);
+          tc::mma_i8(tmem, ad, bd, idesc, (kc | kk) != 0 ? 1u : 0u);
+        }
+        tc::commit(pipe::smem_addr(&sm.empty[s]));
+      }
+      tc::commit(pipe::smem_addr(&sm.accum));
+      // every MMA issued has completed before TMEM is freed
+      tc::commit(pipe::smem_addr(&sm.drain));
+      pipe::mbar_wait_drain(&sm.drain, 0, a.status);
+    }
+    __syncwarp();
   }
-  int32_t s3 = 0;
-#pragma unroll 8
-  for (int j = 0; j < kL2; ++j) {
-    const uint4 wv = *(const uint4*)&sm.w2[j][0];
-    int32_t s2 = sm.b2[j];
-    s2 = __dp4a((int)y1[0], (int)wv.x, s2);
-    s2 = __dp4a((int)y1[1], (int)wv.y, s2);
-    s2 = __dp4a((int)y1[2], (int)wv.z, s2);
-    s2 = __dp4a((int)y1[3], (int)wv.w, s2);
-    s3 += (int32_t)sm.w3[j] * min(max(s2 >> 6, 0), 127);
-  }
-  a.scores[a.perm[start + t]] = __ldg(a.w.l3b + b) + s3;
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 4) tc::tmem_dealloc(tmem, 32);
 }
 
 }  // namespace q
@@ -1042,6 +1109,7 @@ struct cnnue_q_model {
   DevWeights w{};
   void* blob = nullptr;
   int sm_count = 0;
+  uint8_t* w1tiles = nullptr;  // [16 buckets][8 K chunks][16 rows x 128 B], 128B-swizzled (tensor-core B)
   int grid_eval = 0;     // fused kernel (the no-allocation entry point)
   int grid_gather = 0;   // split path, forward
   int grid_gather_update = 0;
@@ -1089,11 +1157,24 @@ ForwardArgs base_args() {
   return a;
 }
 
-// The bucket stacks of the split path over the packed rows.
-int launch_stack(const ForwardArgs& a, const WorkspaceView& v, cudaStream_t s) {
+size_t stack_tc_smem_bytes() { return sizeof(StackTcSmem) + 1024; }
+
+// The bucket stacks of the split path over the packed rows (tensor cores).
+int launch_stack(const cnnue_q_model* m, const ForwardArgs& a, const WorkspaceView& v, cudaStream_t s) {
+  PFN_cuTensorMapEncodeTiled_v12000 fn = tma_encode_fn();
+  if (!fn) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  CUtensorMap map;
+  const cuuint64_t dims[2] = {(cuuint64_t)CNNUE_Q_PACKED, (cuuint64_t)a.n};
+  const cuuint64_t strides[1] = {(cuuint64_t)CNNUE_Q_PACKED};
+  const cuuint32_t box[2] = {(cuuint32_t)kTcChunk, (cuuint32_t)kStackTile};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, a.packed, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled(packed rows) failed (%d)", (int)r);
   const int64_t tiles = (a.n + kStackTile - 1) / kStackTile + kNB;  // bound on the buckets' tiles
-  q_stack_kernel<<<(unsigned)tiles, kStackTile, 0, s>>>(a, v.hdr);
-  return check_launch("q_stack_kernel");
+  q_stack_tc_kernel<<<(unsigned)tiles, kTcThreads, stack_tc_smem_bytes(), s>>>(map, a, m->w1tiles, v.hdr);
+  return check_launch("q_stack_tc_kernel");
 }
 
 // Forward over the sorted order (split path): gather + pack, then the stacks.
@@ -1123,7 +1204,7 @@ int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
     q_gather_kernel<false, false><<<grid, gather_threads(false), smem, s>>>(a);
   const int st = check_launch("q_gather_kernel");
   if (st) return st;
-  return launch_stack(a, v, s);
+  return launch_stack(m, a, v, s);
 }
 
 // Fused single-kernel forward (gather, pack and stacks in one kernel; needs
@@ -1213,6 +1294,26 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   m->w.l3w = (const int8_t*)(b + offs[6]);
   m->w.l3b = (const int32_t*)(b + offs[7]);
 
+  {
+    // W1 as the stack kernel's tensor-core B operand: per bucket and 128-byte
+    // K chunk a 16-row tile in the 128B-swizzled K-major layout.
+    const size_t tile_bytes = (size_t)kNB * kTcChunks * kTcWTileBytes;
+    std::vector<uint8_t> tiles(tile_bytes);
+    for (int b = 0; b < kNB; ++b)
+      for (int kc = 0; kc < kTcChunks; ++kc)
+        for (int o = 0; o < kL1; ++o)
+          for (int k = 0; k < kTcChunk; ++k)
+            tiles[((size_t)b * kTcChunks + kc) * kTcWTileBytes + sw128_offset(o, k)] =
+                (uint8_t)w->l1_weight[((size_t)b * kL1 + o) * kCols + kc * kTcChunk + k];
+    e = cudaMalloc(&m->w1tiles, tile_bytes);
+    if (e == cudaSuccess) e = cudaMemcpy(m->w1tiles, tiles.data(), tile_bytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      if (m->w1tiles) cudaFree(m->w1tiles);
+      cudaFree(m->blob);
+      delete m;
+      return cuda_error(e, "W1 tiles");
+    }
+  }
   cudaDeviceGetAttribute(&m->sm_count, cudaDevAttrMultiProcessorCount, device);
   const int smem = (int)sizeof(BulkSmem);
   cudaFuncSetAttribute(q_bulk_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1220,6 +1321,7 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   cudaFuncSetAttribute(q_gather_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
   cudaFuncSetAttribute(q_gather_kernel<false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
   cudaFuncSetAttribute(q_gather_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, gsmem);
+  cudaFuncSetAttribute(q_stack_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)stack_tc_smem_bytes());
   int occ_eval = 0, occ_g = 0, occ_gu = 0;
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_eval, q_bulk_kernel<false, false>, bulk_threads(false), smem);
   cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_g, q_gather_kernel<false, false>, gather_threads(false), gsmem);
@@ -1230,6 +1332,7 @@ int cnnue_q_model_create(const cnnue_q_weights* w, int device, cnnue_q_model** o
   e = cudaGetLastError();
   if (e != cudaSuccess) {
     cudaFree(m->blob);
+    cudaFree(m->w1tiles);
     delete m;
     return cuda_error(e, "kernel attributes");
   }
@@ -1241,6 +1344,7 @@ int cnnue_q_model_destroy(cnnue_q_model* m) {
   if (!m) return CNNUE_OK;
   DeviceGuard guard(m->device);
   if (m->blob) cudaFree(m->blob);
+  if (m->w1tiles) cudaFree(m->w1tiles);
   if (m->stage) cudaFree(m->stage);
   delete m;
   return CNNUE_OK;
@@ -1408,7 +1512,7 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   q_gather_kernel<true, true><<<grid, gather_threads(true), sizeof(GatherSmem), s>>>(a);
   st = check_launch("q_gather_kernel<update>");
   if (st) return st;
-  return launch_stack(a, v, s);
+  return launch_stack(m, a, v, s);
 }
 
 }  // extern "C"

@@ -45,6 +45,11 @@ SIGNATURES = {
     "cnnue_q_forward_host": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P]),
     "cnnue_q_forward_acc": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, P, c_size, P]),
     "cnnue_q_forward_noalloc": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P]),
+    "cnnue_q_ctx_create": (c_int, [c_void_p, c_i64, c_u32, C.POINTER(c_void_p)]),
+    "cnnue_q_ctx_destroy": (c_int, [c_void_p]),
+    "cnnue_q_ctx_next_stream": (c_int, [c_void_p, C.POINTER(c_void_p)]),
+    "cnnue_q_forward_host_async": (c_int, [c_void_p, P, c_u32, P, c_i64, P, C.POINTER(c_u64)]),
+    "cnnue_q_ctx_wait": (c_int, [c_void_p, c_u64, C.POINTER(c_int)]),
     "cnnue_q_forward_stall_test": (c_int, [c_void_p, P, c_u32, P, c_i64, P, P, c_size, c_u32, c_u32, c_u64, P]),
     "cnnue_q_update": (c_int, [c_void_p, P, P, P, c_u32, P, P, c_u32, P, P, c_i64, P, P, P,
                                c_size, P]),

@@ -37,6 +37,20 @@ PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
   return fn;
 }
 
+int status_from_word(uint32_t word) {
+  int st = CNNUE_OK;
+  if (word & CNNUE_STATUS_BAD_OFFSETS)
+    st = CNNUE_ERR_BAD_OFFSETS;
+  else if (word & CNNUE_STATUS_BAD_INDEX)
+    st = CNNUE_ERR_BAD_INDEX;
+  else if (word & CNNUE_STATUS_TIMEOUT)
+    st = CNNUE_ERR_TIMEOUT;
+  else if (word != 0)
+    st = CNNUE_ERR_INTERNAL;
+  if (st != CNNUE_OK) set_error(st, "kernel status word 0x%x", word);
+  return st;
+}
+
 int use_device(int device) {
   int cur = -1;
   cudaError_t e = cudaGetDevice(&cur);
@@ -81,18 +95,7 @@ int cnnue_read_status(void* d_workspace, void* stream, int* status_out) {
   CNNUE_CUDA_TRY(cudaMemcpyAsync(&word, d_workspace, 4, cudaMemcpyDeviceToHost, s));
   CNNUE_CUDA_TRY(cudaStreamSynchronize(s));
   CNNUE_CUDA_TRY(cudaMemsetAsync(d_workspace, 0, 4, s));
-  if (word & CNNUE_STATUS_BAD_OFFSETS)
-    *status_out = CNNUE_ERR_BAD_OFFSETS;
-  else if (word & CNNUE_STATUS_BAD_INDEX)
-    *status_out = CNNUE_ERR_BAD_INDEX;
-  else if (word & CNNUE_STATUS_TIMEOUT)
-    *status_out = CNNUE_ERR_TIMEOUT;
-  else if (word != 0)
-    *status_out = CNNUE_ERR_INTERNAL;
-  else
-    *status_out = CNNUE_OK;
-  if (*status_out != CNNUE_OK)
-    cnnue::set_error(*status_out, "kernel status word 0x%x", word);
+  *status_out = cnnue::status_from_word(word);
   return CNNUE_OK;
 }
 

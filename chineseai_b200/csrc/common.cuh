@@ -22,6 +22,10 @@ int cuda_error(cudaError_t err, const char* what);
     if (err__ != cudaSuccess) return ::cnnue::cuda_error(err__, #expr); \
   } while (0)
 
+// Maps a kernel status word (CNNUE_STATUS_* bits) to a CNNUE_ERR_* code and
+// records the detail as the thread's last error.
+int status_from_word(uint32_t word);
+
 // Checks that `device` is the current device, switching to it if needed.
 int use_device(int device);
 

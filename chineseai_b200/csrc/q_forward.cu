@@ -1517,6 +1517,160 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
 
 }  // extern "C"
 
+
+// ---------------------------------------------------------------------------
+// Pipelined host-buffer evaluation: a caller-owned context with two slots,
+// each with its own stream, device staging (indices, offsets, scores,
+// workspace) and pinned status word, so one batch's host-to-device copies run
+// while the previous batch's kernels do.  Created once (it allocates); the
+// calls allocate nothing.
+// ---------------------------------------------------------------------------
+struct cnnue_q_stream_ctx {
+  static constexpr int kSlots = 2;
+  const cnnue_q_model* model = nullptr;
+  int64_t max_n = 0;
+  uint32_t max_idx = 0;
+  struct Slot {
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done = nullptr;
+    char* dev = nullptr;
+    uint32_t* h_status = nullptr;  // pinned
+    bool busy = false;
+    uint64_t ticket = 0;
+    int launch_status = CNNUE_OK;
+  } slot[kSlots];
+  uint64_t next_ticket = 0;
+};
+
+namespace {
+
+struct SlotLayout {
+  size_t idx, off, sc, ws, total;
+};
+
+SlotLayout slot_layout(int64_t n, uint32_t n_idx) {
+  SlotLayout l;
+  l.idx = 0;
+  l.off = align_up((size_t)n_idx * 2 + 2, 256);
+  l.sc = l.off + align_up((size_t)(2 * n + 1) * 4, 256);
+  l.ws = l.sc + align_up((size_t)n * 4, 256);
+  l.total = l.ws + align_up(q_workspace_bytes(n), 256);
+  return l;
+}
+
+void ctx_free(cnnue_q_stream_ctx* c) {
+  for (auto& sl : c->slot) {
+    if (sl.stream) cudaStreamSynchronize(sl.stream);
+    if (sl.dev) cudaFree(sl.dev);
+    if (sl.h_status) cudaFreeHost(sl.h_status);
+    if (sl.done) cudaEventDestroy(sl.done);
+    if (sl.stream) cudaStreamDestroy(sl.stream);
+  }
+  delete c;
+}
+
+}  // namespace
+
+extern "C" {
+
+int cnnue_q_ctx_create(const cnnue_q_model* m, int64_t max_positions, uint32_t max_indices,
+                       cnnue_q_stream_ctx** out) {
+  if (!m || !out) return set_error(CNNUE_ERR_INVALID_ARG, "null model or out");
+  if (max_positions <= 0 || max_positions > (int64_t)INT32_MAX)
+    return set_error(CNNUE_ERR_INVALID_ARG, "max_positions %lld out of range", (long long)max_positions);
+  *out = nullptr;
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  auto* c = new cnnue_q_stream_ctx();
+  c->model = m;
+  c->max_n = max_positions;
+  c->max_idx = max_indices;
+  const SlotLayout l = slot_layout(max_positions, max_indices);
+  for (auto& sl : c->slot) {
+    cudaError_t e = cudaStreamCreateWithFlags(&sl.stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sl.done, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaMalloc(&sl.dev, l.total);
+    if (e == cudaSuccess) e = cudaMallocHost(&sl.h_status, 64);
+    if (e != cudaSuccess) {
+      ctx_free(c);
+      return cuda_error(e, "cnnue_q_ctx_create");
+    }
+  }
+  *out = c;
+  return CNNUE_OK;
+}
+
+int cnnue_q_ctx_destroy(cnnue_q_stream_ctx* c) {
+  if (!c) return CNNUE_OK;
+  DeviceGuard guard(c->model->device);
+  ctx_free(c);
+  return CNNUE_OK;
+}
+
+int cnnue_q_ctx_next_stream(const cnnue_q_stream_ctx* c, void** stream) {
+  if (!c || !stream) return set_error(CNNUE_ERR_INVALID_ARG, "null context or stream");
+  *stream = (void*)c->slot[c->next_ticket % cnnue_q_stream_ctx::kSlots].stream;
+  return CNNUE_OK;
+}
+
+int cnnue_q_forward_host_async(cnnue_q_stream_ctx* c, const uint16_t* h_idx, uint32_t n_idx,
+                               const uint32_t* h_offsets, int64_t n, int32_t* h_scores, uint64_t* ticket) {
+  if (!c || !ticket) return set_error(CNNUE_ERR_INVALID_ARG, "null context or ticket");
+  if (n < 0 || n > c->max_n)
+    return set_error(CNNUE_ERR_INVALID_ARG, "n_positions %lld outside [0, %lld] of the context", (long long)n,
+                     (long long)c->max_n);
+  if (n_idx > c->max_idx)
+    return set_error(CNNUE_ERR_INVALID_ARG, "n_indices %u above the context's %u", n_idx, c->max_idx);
+  if (n > 0 && (!h_offsets || !h_scores || (n_idx > 0 && !h_idx)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null host buffer");
+  auto& sl = c->slot[c->next_ticket % cnnue_q_stream_ctx::kSlots];
+  if (sl.busy)
+    return set_error(CNNUE_ERR_INVALID_ARG, "two calls of this context are in flight: wait for ticket %llu first",
+                     (unsigned long long)sl.ticket);
+  const cnnue_q_model* m = c->model;
+  DeviceGuard guard(m->device);
+  if (guard.status) return guard.status;
+  const SlotLayout l = slot_layout(c->max_n, c->max_idx);
+  uint16_t* d_idx = (uint16_t*)(sl.dev + l.idx);
+  uint32_t* d_off = (uint32_t*)(sl.dev + l.off);
+  int32_t* d_sc = (int32_t*)(sl.dev + l.sc);
+  void* ws = sl.dev + l.ws;
+  cudaStream_t s = sl.stream;
+  int st = CNNUE_OK;
+  *sl.h_status = 0;
+  if (n > 0) {
+    if (n_idx) CNNUE_CUDA_TRY(cudaMemcpyAsync(d_idx, h_idx, (size_t)n_idx * 2, cudaMemcpyHostToDevice, s));
+    CNNUE_CUDA_TRY(cudaMemcpyAsync(d_off, h_offsets, (size_t)(2 * n + 1) * 4, cudaMemcpyHostToDevice, s));
+    st = launch_sort(m, d_off, n_idx, nullptr, n, ws, s, ws_inv(ws, n));
+    if (!st) st = launch_eval(m, d_idx, n_idx, d_off, n, d_sc, nullptr, ws, s);
+    if (!st) {
+      CNNUE_CUDA_TRY(cudaMemcpyAsync(h_scores, d_sc, (size_t)n * 4, cudaMemcpyDeviceToHost, s));
+      CNNUE_CUDA_TRY(cudaMemcpyAsync(sl.h_status, ws, 4, cudaMemcpyDeviceToHost, s));
+    }
+  }
+  CNNUE_CUDA_TRY(cudaEventRecord(sl.done, s));
+  sl.busy = true;
+  sl.ticket = c->next_ticket++;
+  sl.launch_status = st;
+  *ticket = sl.ticket;
+  return CNNUE_OK;
+}
+
+int cnnue_q_ctx_wait(cnnue_q_stream_ctx* c, uint64_t ticket, int* status) {
+  if (!c || !status) return set_error(CNNUE_ERR_INVALID_ARG, "null context or status");
+  auto& sl = c->slot[ticket % cnnue_q_stream_ctx::kSlots];
+  if (!sl.busy || sl.ticket != ticket)
+    return set_error(CNNUE_ERR_INVALID_ARG, "ticket %llu is not in flight", (unsigned long long)ticket);
+  DeviceGuard guard(c->model->device);
+  if (guard.status) return guard.status;
+  CNNUE_CUDA_TRY(cudaEventSynchronize(sl.done));
+  sl.busy = false;
+  *status = sl.launch_status ? sl.launch_status : status_from_word(*sl.h_status);
+  return CNNUE_OK;
+}
+
+}  // extern "C"
+
 // ---------------------------------------------------------------------------
 // No-allocation entry point: the bucket-sort scratch of cnnue_q_forward lives
 // in this file-scope device array instead of a caller workspace.  Host code

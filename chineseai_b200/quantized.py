@@ -128,6 +128,10 @@ class QuantizedNnue:
               "cnnue_q_forward_host")
         return out
 
+    def pipeline(self, max_positions: int, max_indices: int) -> "HostPipeline":
+        """A pipelined host-buffer evaluator (one per thread) over this model."""
+        return HostPipeline(self, max_positions, max_indices)
+
     def update(self, batch: UpdateBatch, stream=None):
         """Incremental update + stack: returns (child acc np.int16[n,2,1024], scores np.int32[n])."""
         d = self.device
@@ -150,3 +154,50 @@ class QuantizedNnue:
             check(self.read_status(ws, stream), "cnnue_q_update (kernel status)")
         torch.cuda.synchronize(d)
         return child.cpu().numpy(), scores.cpu().numpy()
+
+
+class HostPipeline:
+    """Two-slot pipelined evaluation of host batches (cnnue_q_ctx_*): `submit`
+    enqueues a batch and returns a ticket at once, `wait` returns its status
+    once the scores are in the caller's output array.  Up to two batches are
+    in flight, so one batch's host-to-device copies overlap the previous
+    batch's kernels.  Use pinned numpy arrays (e.g. from
+    torch.empty(..., pin_memory=True).numpy()) for asynchronous copies; the
+    arrays of a batch must stay untouched until its wait returns."""
+
+    def __init__(self, model: QuantizedNnue, max_positions: int, max_indices: int):
+        self.model = model
+        h = C.c_void_p()
+        check(lib().cnnue_q_ctx_create(model.handle, max_positions, max_indices, C.byref(h)), "cnnue_q_ctx_create")
+        self._h = h
+        self._keep = {}
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().cnnue_q_ctx_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def next_stream(self) -> int:
+        s = C.c_void_p()
+        check(lib().cnnue_q_ctx_next_stream(self._h, C.byref(s)), "cnnue_q_ctx_next_stream")
+        return s.value or 0
+
+    def submit(self, indices: np.ndarray, offsets: np.ndarray, out: np.ndarray) -> int:
+        n = (len(offsets) - 1) // 2
+        t = C.c_uint64(0)
+        check(lib().cnnue_q_forward_host_async(self._h, indices.ctypes.data, len(indices), offsets.ctypes.data, n,
+                                               out.ctypes.data, C.byref(t)), "cnnue_q_forward_host_async")
+        self._keep[t.value] = (indices, offsets, out)
+        return t.value
+
+    def wait(self, ticket: int) -> int:
+        st = C.c_int(0)
+        check(lib().cnnue_q_ctx_wait(self._h, ticket, C.byref(st)), "cnnue_q_ctx_wait")
+        self._keep.pop(ticket, None)
+        return st.value

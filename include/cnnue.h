@@ -149,6 +149,36 @@ int cnnue_q_forward_host(cnnue_q_model* model, const uint16_t* h_indices, uint32
                          const uint32_t* h_offsets, int64_t n_positions, int32_t* h_scores,
                          void* stream);
 
+/* Pipelined host-buffer evaluation.  Replaces, for batched callers, the
+ * per-thread evaluation loop over AzNnue::evaluate_with_scratch_output
+ * (src/az.rs:1562-1604) with its per-thread AzEvalScratch (src/az.rs:309-367):
+ * the context is the per-thread scratch, the model stays shared read-only.
+ *
+ * A context holds two slots, each with its own CUDA stream and device staging
+ * for batches of up to max_positions positions and max_indices indices;
+ * cnnue_q_ctx_create allocates them, the calls allocate nothing.  Call k runs
+ * on slot k % 2: it enqueues the host-to-device copies of its indices and
+ * offsets, the bucket sort, the forward and the device-to-host copy of the
+ * scores, and returns at once with a ticket, so batch k + 1's copies overlap
+ * batch k's kernels.  cnnue_q_ctx_wait(ticket) blocks until that batch's
+ * scores are in h_scores and returns its kernels' status in *status.  At most
+ * two calls may be in flight: a third call before the oldest is waited for
+ * returns CNNUE_ERR_INVALID_ARG.  The host buffers of a call must stay
+ * untouched until its wait returns; page-locked (pinned) buffers make the
+ * copies asynchronous, pageable ones still work but serialise the copies.
+ * One context per thread; several contexts may share a model.
+ * cnnue_q_ctx_next_stream gives the stream the next call will use (to order
+ * other work, e.g. a cache flush, before it). */
+typedef struct cnnue_q_stream_ctx cnnue_q_stream_ctx;
+int cnnue_q_ctx_create(const cnnue_q_model* model, int64_t max_positions, uint32_t max_indices,
+                       cnnue_q_stream_ctx** out);
+int cnnue_q_ctx_destroy(cnnue_q_stream_ctx* ctx);
+int cnnue_q_ctx_next_stream(const cnnue_q_stream_ctx* ctx, void** stream);
+int cnnue_q_forward_host_async(cnnue_q_stream_ctx* ctx, const uint16_t* h_indices, uint32_t n_indices,
+                               const uint32_t* h_offsets, int64_t n_positions, int32_t* h_scores,
+                               uint64_t* ticket);
+int cnnue_q_ctx_wait(cnnue_q_stream_ctx* ctx, uint64_t ticket, int* status);
+
 /* No-allocation variant of cnnue_q_forward (no counterpart in the reference).
  *
  * For callers that cannot allocate device memory at evaluation time: a search

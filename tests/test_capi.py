@@ -46,6 +46,10 @@ def test_invalid_arguments_are_rejected_without_a_gpu():
     assert lib.cnnue_f_model_create(None, 0, C.byref(h)) == 1
     assert lib.cnnue_q_forward(None, None, 0, None, 10, None, None, 0, None) == 1
     assert lib.cnnue_q_forward_host(None, None, 0, None, 1, None, None) == 1
+    assert lib.cnnue_q_ctx_create(None, 10, 10, C.byref(h)) == 1
+    assert lib.cnnue_q_forward_host_async(None, None, 0, None, 1, None, None) == 1
+    st = C.c_int(0)
+    assert lib.cnnue_q_ctx_wait(None, 0, C.byref(st)) == 1
     assert lib.cnnue_feature_pool_fwd(None, None, -1, 1, 1, None, None, None) == 1
     assert lib.cnnue_read_status(None, None, None) == 1
     assert lib.cnnue_sparse_pool_bwd(None, None, 20000, 1, 1, 1, None, None, 0, None) == 1

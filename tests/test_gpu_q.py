@@ -191,3 +191,62 @@ def test_bounded_wait_runs_out_and_model_recovers(qmodel, qweights, n, block, st
     np.testing.assert_array_equal(out.cpu().numpy(), ref)
     scores, _ = qmodel.forward_positions(pos)
     np.testing.assert_array_equal(scores, ref)
+
+
+def test_pipelined_host_contexts(qmodel, qweights):
+    """cnnue_q_ctx_*: batches submitted two at a time through one context match
+    the device-resident forward bit for bit; a batch with a bad index reports
+    it through its own ticket only; a third call in flight is refused; two
+    threads with their own contexts share the model."""
+    import threading
+
+    from chineseai_b200._lib import CnnueError
+    batches = [synth.positions(n, 60 + k) for k, n in enumerate([4096, 1, 3000, 4096, 777])]
+    refs = [qmodel.forward_positions(b)[0] for b in batches]
+    pinned = lambda a: torch.from_numpy(a).pin_memory().numpy()  # noqa: E731
+    pipe = qmodel.pipeline(4096, 4096 * 64)
+    outs = [pinned(np.full(b.n, -7, np.int32)) for b in batches]
+    tickets = []
+    for k, b in enumerate(batches):
+        if len(tickets) == 2:
+            assert pipe.wait(tickets.pop(0)) == 0
+        tickets.append(pipe.submit(pinned(b.indices), pinned(b.offsets), outs[k]))
+    for t in tickets:
+        assert pipe.wait(t) == 0
+    for o, r in zip(outs, refs):
+        np.testing.assert_array_equal(o, r)
+    # a bad index in one batch: only its ticket reports it
+    bad = synth.positions(100, 70)
+    bad_idx = bad.indices.copy()
+    bad_idx[5] = 11340
+    good = batches[2]
+    o1, o2 = np.zeros(100, np.int32), np.zeros(good.n, np.int32)
+    t1 = pipe.submit(bad_idx, bad.offsets, o1)
+    t2 = pipe.submit(good.indices, good.offsets, o2)
+    with pytest.raises(CnnueError):
+        pipe.submit(good.indices, good.offsets, np.zeros(good.n, np.int32))
+    assert pipe.wait(t1) == 2  # CNNUE_ERR_BAD_INDEX
+    assert pipe.wait(t2) == 0
+    np.testing.assert_array_equal(o2, refs[2])
+    pipe.close()
+
+    errors = []
+
+    def worker(seed):
+        try:
+            p = qmodel.pipeline(2048, 2048 * 64)
+            for j in range(3):
+                b = synth.positions(2048, seed + j)
+                o = np.zeros(b.n, np.int32)
+                assert p.wait(p.submit(b.indices, b.offsets, o)) == 0
+                np.testing.assert_array_equal(o, oracle.q_forward(qweights, b)[1])
+            p.close()
+        except Exception as e:  # noqa: BLE001
+            errors.append(e)
+
+    threads = [threading.Thread(target=worker, args=(100 * i,)) for i in range(2)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert not errors, errors

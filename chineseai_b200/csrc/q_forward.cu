@@ -302,7 +302,7 @@ struct Producer {
   __device__ __forceinline__ bool begin_stage(uint32_t st, uint32_t rows) {
     const uint32_t sidx = st % kNS, use = st / kNS;
     if (!ok) return false;
-    if (use > 0 && !pipe::mbar_wait(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status, wait_ns)) {
+    if (use > 0 && !pipe::mbar_wait_sleep(&sm->empty[sidx], (use - 1) & 1u, &sm->abort, status, wait_ns)) {
       ok = false;
       return false;
     }
@@ -400,10 +400,10 @@ __device__ __forceinline__ uint32_t consume_update(Smem& sm, uint32_t st, uint32
                                                    unsigned long long wait_ns, uint4& acc) {
   const uint32_t total = init + n_rem + n_add;
   uint4 rem = make_uint4(0, 0, 0, 0);  // sum of the removed rows, subtracted once at the end
+  uint32_t sidx = st % kNS, phase = (st / kNS) & 1u;
   for (uint32_t first = 0; first < total; first += kSR, ++st) {
-    const uint32_t sidx = st % kNS;
     const uint32_t rows = min((uint32_t)kSR, total - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kNS) & 1u, &sm.abort, status, wait_ns);
+    pipe::mbar_wait_sleep(&sm.full[sidx], phase, &sm.abort, status, wait_ns);
     const uint8_t* slot = &sm.ring[sidx * kSR][col_byte];
     uint4 v[kSR];
 #pragma unroll
@@ -419,6 +419,10 @@ __device__ __forceinline__ uint32_t consume_update(Smem& sm, uint32_t st, uint32
       else
         acc = vadd(acc, v[j]);
     }
+    if (++sidx == (uint32_t)kNS) {
+      sidx = 0;
+      phase ^= 1u;
+    }
   }
   acc = vsub(acc, rem);
   return st;
@@ -431,10 +435,10 @@ __device__ __forceinline__ uint32_t consume_update(Smem& sm, uint32_t st, uint32
 template <int kSR = kStageRows, int kNS = kStages, class Smem = BulkSmem>
 __device__ __forceinline__ uint32_t consume_list(Smem& sm, uint32_t st, uint32_t cnt, int col_byte, int lane,
                                                  uint32_t* status, unsigned long long wait_ns, uint4& acc) {
+  uint32_t sidx = st % kNS, phase = (st / kNS) & 1u;
   for (uint32_t first = 0; first < cnt; first += kSR, ++st) {
-    const uint32_t sidx = st % kNS;
     const uint32_t rows = min((uint32_t)kSR, cnt - first);
-    pipe::mbar_wait(&sm.full[sidx], (st / kNS) & 1u, &sm.abort, status, wait_ns);
+    pipe::mbar_wait_sleep(&sm.full[sidx], phase, &sm.abort, status, wait_ns);
     const uint8_t* slot = &sm.ring[sidx * kSR][col_byte];
     if (rows == (uint32_t)kSR) {
       uint4 v[kSR];
@@ -458,6 +462,10 @@ __device__ __forceinline__ uint32_t consume_list(Smem& sm, uint32_t st, uint32_t
       __syncwarp();
       if (lane == 0) pipe::mbar_arrive(&sm.empty[sidx]);
       acc = vadd(acc, s);
+    }
+    if (++sidx == (uint32_t)kNS) {
+      sidx = 0;
+      phase ^= 1u;
     }
   }
   return st;
@@ -650,6 +658,148 @@ __device__ __forceinline__ void produce_forward(Smem& sm, const ForwardArgs& a, 
     }
   }
   __syncwarp();
+}
+
+// Forward producers and consumers of the gather kernel with their ring
+// positions held in registers: a producer warp w issues exactly the stages
+// w, w + kP, w + 2 kP, ... (stage st belongs to warp st % kP), so its slot
+// and use count advance by kP per stage without a division; consumers walk
+// every stage and bump their barrier and slot addresses.
+template <int kP, int kSR, int kNS, class Smem>
+__device__ __forceinline__ void produce_forward_fast(Smem& sm, const ForwardArgs& a, int64_t begin, int64_t end,
+                                                     int w, int lane) {
+  static_assert(kP <= kNS, "a producer's slot advances by kP < kNS per stage");
+  const uint32_t full0 = pipe::smem_addr(&sm.full[0]), empty0 = pipe::smem_addr(&sm.empty[0]);
+  const uint32_t ring0 = pipe::smem_addr(&sm.ring[0][0]);
+  const char* ft = (const char*)a.w.ft;
+  const uint32_t stall = blockIdx.x == a.stall_block ? a.stall_stage : 0xffffffffu;
+  uint32_t s_next = (uint32_t)w;  // this warp's next stage
+  uint32_t sidx = (uint32_t)w, use = 0;
+  bool ok = true;
+  uint32_t st_base = 0;  // stage number of the chunk's first position
+  for (int64_t b0 = begin; b0 < end && ok; b0 += 32) {
+    const int nb = (int)min((int64_t)32, end - b0);
+    Seg s0{0, 0}, s1{0, 0};
+    if (lane < nb) {
+      const int64_t ps = 2 * (b0 + lane);
+      s0 = clamp_seg(a.offsets, ps, a.n_idx);
+      s1 = clamp_seg(a.offsets, ps + 1, a.n_idx);
+    }
+    const uint32_t my_ns = n_stages<kSR>(s0.cnt) + n_stages<kSR>(s1.cnt);
+    uint32_t incl = my_ns;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t x = __shfl_up_sync(kFull, incl, o);
+      if (lane >= o) incl += x;
+    }
+    const uint32_t excl = incl - my_ns;
+    const uint32_t chunk_stages = __shfl_sync(kFull, incl, 31);
+    for (int q = 0; q < nb && ok; ++q) {
+      uint32_t st = st_base + __shfl_sync(kFull, excl, q);
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const uint32_t beg = __shfl_sync(kFull, p ? s1.beg : s0.beg, q);
+        const uint32_t cnt = __shfl_sync(kFull, p ? s1.cnt : s0.cnt, q);
+        const uint32_t st_end = st + n_stages<kSR>(cnt);
+        while (ok && s_next < st_end) {
+          const uint32_t first = (s_next - st) * kSR;
+          const uint32_t rows = min((uint32_t)kSR, cnt - first);
+          uint32_t f = (uint32_t)lane < rows ? (uint32_t)a.idx[beg + first + lane] : 0u;
+          if ((uint32_t)lane < rows && f >= (uint32_t)kF) {  // bad index -> the zero row
+            atomicOr(a.status, CNNUE_STATUS_BAD_INDEX);
+            f = kF;
+          }
+          uint32_t fj[kSR];
+#pragma unroll
+          for (int j = 0; j < kSR; ++j) fj[j] = __shfl_sync(kFull, f, j);
+          if (lane == 0) {
+            bool go = use == 0 || pipe::mbar_wait_addr(empty0 + 8 * sidx, (use - 1) & 1u, &sm.abort, a.status,
+                                                       a.wait_ns);
+            if (go && *(volatile int*)&sm.abort) go = false;
+            if (!go) {
+              ok = false;
+            } else if (s_next != stall) {  // the stall test hook leaves its stage unannounced
+              const uint32_t bar = full0 + 8 * sidx;
+              pipe::mbar_expect_tx_addr(bar, rows * kRowBytes);
+              sm.issued[sidx] = s_next;
+              const uint32_t dst = ring0 + sidx * (kSR * kRowBytes);
+#pragma unroll
+              for (int j = 0; j < kSR; ++j)
+                if ((uint32_t)j < rows)
+                  pipe::bulk_copy_g2s_addr(dst + j * kRowBytes, ft + ((size_t)fj[j] << 11), kRowBytes, bar);
+            }
+          }
+          ok = __shfl_sync(kFull, ok, 0);
+          s_next += kP;
+          sidx += kP;
+          if (sidx >= (uint32_t)kNS) {
+            sidx -= kNS;
+            ++use;
+          }
+        }
+        st = st_end;
+      }
+    }
+    st_base += chunk_stages;
+  }
+  // Teardown as in produce().
+  named_bar_sync(2, 32 * kP);
+  if (lane == 0) {
+    for (int s = w; s < kNS; s += kP) {
+      const uint32_t last = sm.issued[s];
+      if (last != 0xffffffffu) pipe::mbar_wait_drain(&sm.full[s], (last / kNS) & 1u, a.status);
+    }
+  }
+  __syncwarp();
+}
+
+// A consumer thread's position in the ring (addresses of the current stage).
+struct ConsumerRing {
+  uint32_t full, empty, slot;  // slot: this thread's 16 bytes of the stage's first row
+  uint32_t sidx, phase;
+};
+
+template <int kSR, int kNS>
+__device__ __forceinline__ void ring_advance(ConsumerRing& r) {
+  r.full += 8;
+  r.empty += 8;
+  r.slot += kSR * kRowBytes;
+  if (++r.sidx == (uint32_t)kNS) {
+    r.sidx = 0;
+    r.full -= 8 * kNS;
+    r.empty -= 8 * kNS;
+    r.slot -= kNS * kSR * kRowBytes;
+    r.phase ^= 1u;
+  }
+}
+
+// Adds the rows of one forward list into acc.
+template <int kSR, int kNS>
+__device__ __forceinline__ void consume_list_fast(ConsumerRing& r, volatile int* abort, uint32_t cnt, int lane,
+                                                  uint32_t* status, unsigned long long wait_ns, uint4& acc) {
+  for (uint32_t first = 0; first < cnt; first += kSR) {
+    const uint32_t rows = min((uint32_t)kSR, cnt - first);
+    pipe::mbar_wait_addr(r.full, r.phase, abort, status, wait_ns);
+    if (rows == (uint32_t)kSR) {
+      uint4 v[kSR];
+#pragma unroll
+      for (int j = 0; j < kSR; ++j) v[j] = pipe::lds128(r.slot + j * kRowBytes);
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive_addr(r.empty);
+#pragma unroll
+      for (int h = kSR / 2; h >= 1; h /= 2)
+#pragma unroll
+        for (int j = 0; j < h; ++j) v[j] = vadd(v[j], v[j + h]);
+      acc = vadd(acc, v[0]);
+    } else {
+      uint4 s = pipe::lds128(r.slot);
+      for (uint32_t j = 1; j < rows; ++j) s = vadd(s, pipe::lds128(r.slot + j * kRowBytes));
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive_addr(r.empty);
+      acc = vadd(acc, s);
+    }
+    ring_advance<kSR, kNS>(r);
+  }
 }
 
 template <bool kUpdate, bool kWriteAcc>
@@ -860,8 +1010,8 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
     if (kUpdate)
       produce<true, gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32, lane);
     else
-      produce_forward<gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32,
-                                                                lane);
+      produce_forward_fast<gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32,
+                                                                     lane);
     return;
   }
 
@@ -871,7 +1021,9 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
   const int chunk = lo ? 16 * warp + sub : 64 + 16 * warp + sub;  // columns [8 chunk, 8 chunk + 8)
   const int col_byte = chunk * 16;
   const uint4 bias = __ldg((const uint4*)((const char*)a.w.bias + col_byte));
-  uint32_t st = 0;  // next stage number
+  uint32_t st = 0;  // next stage number (update path)
+  ConsumerRing ring{pipe::smem_addr(&sm.full[0]), pipe::smem_addr(&sm.empty[0]),
+                    pipe::smem_addr(&sm.ring[0][0]) + (uint32_t)col_byte, 0u, 0u};
   PosDesc nxt;
   if (begin < end) nxt = finish_desc<kUpdate>(a, load_raw<kUpdate>(a, (uint32_t)begin, 0));
   uint32_t slot_n = begin < end ? a.inv[begin] : 0u;  // sorted slot of the next position
@@ -895,7 +1047,7 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
         st = consume_update<kGRows, kGStages>(sm, st, d.init[p], d.rem[p].cnt, d.add[p].cnt, col_byte, lane,
                                               a.status, a.wait_ns, v);
       } else {
-        st = consume_list<kGRows, kGStages>(sm, st, d.add[p].cnt, col_byte, lane, a.status, a.wait_ns, v);
+        consume_list_fast<kGRows, kGStages>(ring, &sm.abort, d.add[p].cnt, lane, a.status, a.wait_ns, v);
       }
       acc[p] = v;
     }

@@ -987,7 +987,8 @@ def run_az_train(args):
     def device_step():
         tr._graph.replay()
         if tr.world > 1:
-            tr._exchange_and_update()
+            tr._exchange(tr._graph_out, read=False)
+            tr._adamw()
 
     total = _device_loop(device_step, args.steps, dev, stream)
     clocks = sampler.stop()

@@ -232,6 +232,40 @@ def mean_allreduce_(grad, group=None) -> int:
     return world
 
 
+# Tail of the gradient buffer: 30 metrics, then 4 status-bit indicators.
+_TAIL = 64
+_N_METRICS = 30
+
+
+def exchange_with_status_(buf, n_grad: int, tail_at: int, metrics, word, group=None, read: bool = True,
+                          guard=None, step: int = 0):
+    """The data-parallel exchange of one training step, in one sum
+    all-reduce over `group`: buf[:n_grad] holds this rank's gradient and
+    becomes the ranks' mean; buf[tail_at:] receives this rank's metrics
+    (summed over the ranks: the whole batch's sums) and its kernel status
+    word as four 0/1 bit indicators (a sum above zero means some rank set the
+    bit, so every rank reads the same OR).  Returns (metrics sums, status
+    word) as host values when `read`, else None (no host synchronisation).
+    With a dist_guard.StepGuard the peers' heartbeats for `step` are checked
+    before the collective and the collective is bounded (RankFailure)."""
+    import torch
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    tail = buf[tail_at: tail_at + _N_METRICS + 4]
+    tail[:_N_METRICS].copy_(metrics[:_N_METRICS])
+    w = torch.as_tensor(word).to(device=buf.device, dtype=torch.int32).reshape(())
+    tail[_N_METRICS:].copy_(torch.stack([((w >> b) & 1).float() for b in range(4)]))
+    if guard is not None:
+        guard.all_reduce(buf, step)
+    else:
+        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    buf[:n_grad].mul_(1.0 / world)
+    if not read:
+        return None
+    m = tail.cpu().numpy()
+    return m[:_N_METRICS].copy(), sum(1 << b for b in range(4) if m[_N_METRICS + b] > 0)
+
+
 def _raise_status(word: int, where: str) -> None:
     """The kernels' status bits as cnnue_read_status maps them."""
     if word == 0:
@@ -298,14 +332,19 @@ class AzTrainer:
     sum-all-reduced once and scaled by 1 / world (the gradient of the whole
     batch's mean loss), and every rank applies the same AdamW update.  The
     captured graph then holds forward and backward only; the all-reduce and
-    AdamW run after it, outside the graph."""
+    AdamW run after it, outside the graph.  With a process group the step's
+    statistics (TrainStats) are the whole batch's (sums over every rank's
+    share, samples = the global batch), and a kernel status raised on any
+    rank skips AdamW and raises on every rank."""
 
     def __init__(self, weights: "az.AzWeights", lr: float = 1e-3, device: int = 0, weight_decay: float = 1e-4,
-                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False, group=None):
+                 beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False, group=None,
+                 guard=None):
         import torch
         self.torch = torch
         self.use_graph = graph
         self.group = group
+        self.guard = guard  # optional dist_guard.StepGuard for the exchange
         self.world = 1
         if group is not None:
             import torch.distributed as dist
@@ -330,7 +369,10 @@ class AzTrainer:
             host[off:off + int(starts[last + 1] - starts[first])] = np.concatenate(
                 [weights.tensor(i).reshape(-1) for i in range(first, last + 1)])
         self.flat = torch.from_numpy(host).to(self.device)
-        self.grad = torch.zeros_like(self.flat)
+        # the gradient, then (data parallel) a tail that carries the step's
+        # metrics and status bits through the same all-reduce
+        self._tail_at = (pos + _ALIGN - 1) // _ALIGN * _ALIGN
+        self.grad = torch.zeros(self._tail_at + _TAIL, dtype=torch.float32, device=self.device)
         self.m = torch.zeros(self.n_params, dtype=torch.float32, device=self.device)
         self.v = torch.zeros_like(self.m)
         self._layout = layout
@@ -486,11 +528,15 @@ class AzTrainer:
                                        self.torch.cuda.current_stream(self.device).cuda_stream),
               "cnnue_adamw_device")
 
-    def _exchange_and_update(self) -> None:
-        """Data parallel: the gradient averaged over the ranks, then the same
-        AdamW step everywhere (one NCCL all-reduce per step)."""
-        mean_allreduce_(self.grad[: self.n_params], self.group)
-        self._adamw()
+    def _exchange(self, out, read: bool = True):
+        """Data parallel: one NCCL sum all-reduce carries the gradient and
+        every rank's metrics and status bits (exchange_with_status_); all
+        ranks then take the same decision on AdamW."""
+        r = exchange_with_status_(self.grad, self.n_params, self._tail_at, out, out[_N_METRICS], self.group, read,
+                                  self.guard, self.step_count)
+        if r is None:
+            return None
+        return np.concatenate([r[0], [float(r[1])]])
 
     def step(self, batch: PackedBatch, value_weight: float = 1.0, policy_weight: float = 1.0) -> TrainStats:
         """One train_batch_single (src/az/train_gpu_candle.rs:145-160):
@@ -519,11 +565,16 @@ class AzTrainer:
         else:
             out = self._step_body(bt, value_weight, policy_weight)
         self._last_key = key
+        samples = batch.batch_size
         if self.world > 1:
-            self._exchange_and_update()
-        m = out.cpu().numpy()
+            m = self._exchange(out)
+            samples *= self.world
+            if int(m[-1]) == 0:  # every rank applies the step, or none does
+                self._adamw()
+        else:
+            m = out.cpu().numpy()
         _raise_status(int(m[-1]), "AzTrainer.step")
-        return TrainStats(*[float(x) for x in m[:9]], samples=batch.batch_size, phase=m[9:30].reshape(3, 7))
+        return TrainStats(*[float(x) for x in m[:9]], samples=samples, phase=m[9:30].reshape(3, 7))
 
     # -- weights ------------------------------------------------------------------
     def tensors(self) -> list:

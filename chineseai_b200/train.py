@@ -83,21 +83,28 @@ class AdamConfig:
     eps: float = 1e-8
 
 
-def allreduce_sum_(grads: torch.Tensor, group=None) -> int:
+def allreduce_sum_(grads: torch.Tensor, group=None, guard=None, step: int = 0) -> int:
     """Sums `grads` in place over the default (or given) process group and
-    returns the world size (1 without torch.distributed)."""
+    returns the world size (1 without torch.distributed).  With a
+    dist_guard.StepGuard the peers' heartbeats for `step` are checked first
+    and the collective is bounded (RankFailure instead of a hang)."""
     import torch.distributed as dist
     if not (dist.is_available() and dist.is_initialized()):
         return 1
-    dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=group)
+    if guard is not None:
+        guard.all_reduce(grads, step)
+    else:
+        dist.all_reduce(grads, op=dist.ReduceOp.SUM, group=group)
     return dist.get_world_size(group)
 
 
 class Trainer:
-    def __init__(self, params: np.ndarray, device: int = 0, adam: AdamConfig = AdamConfig(), group=None):
+    def __init__(self, params: np.ndarray, device: int = 0, adam: AdamConfig = AdamConfig(), group=None,
+                 guard=None):
         self.device = torch.device("cuda", device)
         self.adam = adam
         self.group = group
+        self.guard = guard  # optional dist_guard.StepGuard for the exchange
         n = param_count()
         if params.shape != (n,):
             raise ValueError(f"expected {n} parameters, got {params.shape}")
@@ -141,7 +148,7 @@ class Trainer:
     def step(self, idx: torch.Tensor, n_idx: int, off: torch.Tensor, n: int, target: torch.Tensor) -> None:
         """One data-parallel step (asynchronous on the current stream)."""
         self.forward_backward(idx, n_idx, off, n, target)
-        world = allreduce_sum_(self.grads, self.group)
+        world = allreduce_sum_(self.grads, self.group, self.guard, self.step_count)
         self.apply_adam(1.0 / world)
 
     def step_positions(self, pos: Positions, target: np.ndarray) -> float:

@@ -73,3 +73,53 @@ def test_two_rank_data_parallel_equals_full_batch():
         assert d.max() <= 4 * lr * 1.01
         loose = d > 1e-6 + 1e-4 * np.abs(r)
         assert loose.mean() <= 1e-4, loose.sum()
+
+
+def _rank_bad(rank, world, port, out):
+    import datetime
+
+    import torch.distributed as dist
+    from chineseai_b200 import az_train
+    from chineseai_b200._lib import CnnueError
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    w, s = _setup()
+    tr = az_train.AzTrainer(w, lr=2e-3, device=rank, graph=False, group=dist.group.WORLD)
+    before = [t.copy() for t in tr.tensors()]
+    b = az_train.pack_batch(s, np.arange(rank * 64, (rank + 1) * 64), caps=(40, 96, 96), fixed=True, compact=True)
+    if rank == 1:
+        b.policy_items[0, 0] = (3000 | 1 << 47)  # a move index past the 2086-move space
+    raised = False
+    try:
+        tr.step(b)
+    except CnnueError:
+        raised = True
+    unchanged = all(np.array_equal(a, c) for a, c in zip(before, tr.tensors()))
+    # the group is still usable: a clean step on both ranks goes through
+    tr.step(az_train.pack_batch(s, np.arange(128 + rank * 64, 128 + (rank + 1) * 64), caps=(40, 96, 96),
+                                fixed=True, compact=True))
+    out[rank] = (raised, unchanged)
+    torch.cuda.synchronize()
+    del tr
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_bad_batch_on_one_rank_stops_every_rank():
+    """Rank 1's batch holds a bad move index: both ranks raise after the
+    step, neither applies AdamW (parameters unchanged), and the next clean
+    step runs on both."""
+    ctx = mp.get_context("spawn")
+    out = ctx.Manager().dict()
+    port = 29700 + os.getpid() % 1000
+    procs = [ctx.Process(target=_rank_bad, args=(r, 2, port, out)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(240)
+        assert p.exitcode == 0
+    assert out[0] == (True, True) and out[1] == (True, True)

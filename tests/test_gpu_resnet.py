@@ -117,3 +117,23 @@ def test_halo_kernel_many_pairs_per_cta():
     for b in (0, 352, 699):
         p1, l1, v1 = model.forward(dev[b:b + 1].contiguous(), with_logits=True)
         assert torch.equal(l1[0], logits[b]) and torch.equal(v1[0], value[b])
+
+
+def test_resnet_full_config_batch_1024_every_board():
+    """The configured leaf batch, 1024 boards (128 whole 8-board groups),
+    compared board by board with the oracle at the tolerances above; the
+    batch includes an empty board at both ends of the buffer."""
+    w, model = _model()
+    planes = resnet.synthetic_planes(1024, 21)
+    planes[0] = 0
+    planes[-1] = 0
+    dev = torch.from_numpy(planes.view(np.int16)).cuda()
+    probs, logits, value = model.forward(dev, with_logits=True)
+    assert model.read_status() == 0
+    lg, pr, _, v, _ = oracle.rn_forward(w, planes)
+    g_logits, g_probs, g_value = logits.cpu().numpy(), probs.cpu().numpy(), value.cpu().numpy()
+    scale = np.maximum(1.0, np.abs(lg).max(axis=1))
+    per_board = np.abs(g_logits - lg).max(axis=1) / scale
+    assert per_board.max() <= 1e-2, (int(per_board.argmax()), float(per_board.max()))
+    np.testing.assert_allclose(g_probs, pr, atol=1e-3, rtol=0)
+    np.testing.assert_allclose(g_value, v, atol=5e-3, rtol=0)

@@ -77,7 +77,10 @@ SIGNATURES = {
     "cnnue_t_make_shadow": (c_int, [P, P, P]),
     "cnnue_t_forward_backward": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, P, c_size, P]),
     "cnnue_t_adam": (c_int, [P, P, P, P, P, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
-                             c_int, P]),
+                             c_int, P, P]),
+    "cnnue_t_forward_backward_begin": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, c_size, P]),
+    "cnnue_t_ft_grad_rows": (c_int, [c_i64, c_u32, P, P, c_size, c_i64, c_i64, P]),
+    "cnnue_t_finish": (c_int, [c_i64, c_u32, P, P, c_size, P, P]),
     "cnnue_az_board_from_fen": (c_int, [C.c_char_p, P, C.POINTER(c_int)]),
     "cnnue_az_features": (c_int, [P, c_int, P, C.POINTER(c_int)]),
     "cnnue_az_move_items": (c_int, [P, c_int, c_int, c_int, P, P, P, C.POINTER(c_int)]),

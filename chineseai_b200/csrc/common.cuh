@@ -85,6 +85,28 @@ int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint
 int launch_offsets_check(const uint32_t* d_offsets, uint32_t n_values, int64_t n_lists, void* ws,
                          cudaStream_t s);
 
+// Tile g of the buckets' tiles in bucket order (each bucket's rows of the
+// sorted order cut into tiles of `rows`): its bucket, first sorted slot and
+// row count.  False past the last tile.
+__device__ __forceinline__ bool bucket_tile(const WorkspaceHeader* hdr, int n_buckets, uint32_t rows, uint32_t g,
+                                            int* bucket, int* start, int* count, uint32_t* first_tile) {
+  uint32_t tiles_before = 0;
+  for (int b = 0; b < n_buckets; ++b) {
+    const uint32_t c = hdr->counts[b];
+    const uint32_t tiles = (c + rows - 1) / rows;
+    if (g < tiles) {
+      *bucket = b;
+      *start = (int)(hdr->cursors[b] + g * rows);
+      *count = (int)min(rows, c - g * rows);
+      *first_tile = tiles_before;
+      return true;
+    }
+    g -= tiles;
+    tiles_before += tiles;
+  }
+  return false;
+}
+
 // RAII switch to a device, restoring the caller's current device.
 struct DeviceGuard {
   int prev = -1;

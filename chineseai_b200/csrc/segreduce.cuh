@@ -247,12 +247,15 @@ __device__ __forceinline__ int64_t unit_row(const uint32_t* unit_start, int64_t 
   return lo;
 }
 
+// Units of rows [row_begin, row_end) (all rows by default).
 template <bool kVec4>
 __global__ void bwd_reduce_kernel(const float* __restrict__ grad_out, int64_t hidden,
-                                  int64_t n_rows, BwdView v, float* __restrict__ grad_table) {
+                                  int64_t n_rows, BwdView v, float* __restrict__ grad_table,
+                                  int64_t row_begin = 0, int64_t row_end = -1) {
   const int lane = threadIdx.x & 31;
-  const int64_t u = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const uint32_t n_units = v.unit_start[n_rows];
+  if (row_end < 0) row_end = n_rows;
+  const int64_t u = v.unit_start[row_begin] + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const uint32_t n_units = v.unit_start[row_end];
   if (u >= n_units) return;
   const int64_t r = unit_row(v.unit_start, n_rows, (uint32_t)u);
   const uint32_t k = (uint32_t)u - v.unit_start[r];
@@ -296,14 +299,17 @@ __global__ void bwd_reduce_kernel(const float* __restrict__ grad_out, int64_t hi
   }
 }
 
-// One CTA per row: rows with several units sum their unit partials in unit
-// order (threads over columns); rows without contributions get zeros.
+// One warp per row: rows with several units sum their unit partials in unit
+// order (lanes over columns); rows without contributions get zeros; rows
+// with one unit were written by the reduction itself.
 __global__ void bwd_finalize_kernel(int64_t hidden, int64_t n_rows, BwdView v,
-                                    float* __restrict__ grad_table) {
-  const int64_t r = blockIdx.x;
+                                    float* __restrict__ grad_table, int64_t row_begin = 0, int64_t row_end = -1) {
+  if (row_end < 0) row_end = n_rows;
+  const int64_t r = row_begin + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  if (r >= row_end) return;
   const uint32_t u0 = v.unit_start[r], u1 = v.unit_start[r + 1];
   if (u1 - u0 == 1) return;
-  for (int64_t h = threadIdx.x; h < hidden; h += blockDim.x) {
+  for (int64_t h = threadIdx.x & 31; h < hidden; h += 32) {
     float acc = 0.f;
     uint32_t u = u0;
     for (; u + 4 <= u1; u += 4) {
@@ -316,6 +322,62 @@ __global__ void bwd_finalize_kernel(int64_t hidden, int64_t n_rows, BwdView v,
     for (; u < u1; ++u) acc += v.partial[(int64_t)u * hidden + h];
     grad_table[r * hidden + h] = acc;
   }
+}
+
+// The reduction of rows [row_begin, row_end) after launch_bwd_prepare (any
+// split of the rows into ranges, in any order, gives the same results).
+inline int launch_bwd_rows(int64_t n_items, int slots, const float* grad_out, int64_t hidden, int64_t n_rows,
+                           float* grad_table, void* ws, int64_t row_begin, int64_t row_end, cudaStream_t s) {
+  BwdView v = carve_bwd(ws, n_items, slots, n_rows);
+  if (row_begin >= row_end) return CNNUE_OK;
+  const int64_t max_units = max_units_of(n_items * slots, n_rows);
+  const bool vec4 = hidden % 4 == 0 && ((uintptr_t)grad_out % 16 == 0) &&
+                    ((uintptr_t)grad_table % 16 == 0);
+  const unsigned rblocks = (unsigned)((max_units * 32 + 255) / 256);
+  if (vec4)
+    bwd_reduce_kernel<true><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table, row_begin, row_end);
+  else
+    bwd_reduce_kernel<false><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table, row_begin, row_end);
+  int st = check_launch_error("bwd_reduce_kernel");
+  if (st) return st;
+  bwd_finalize_kernel<<<(unsigned)(((row_end - row_begin) * 32 + 255) / 256), 256, 0, s>>>(hidden, n_rows, v,
+                                                                                          grad_table, row_begin,
+                                                                                          row_end);
+  return check_launch_error("bwd_finalize_kernel");
+}
+
+// Steps 1-4 (histograms, prefixes, scans, stable scatter) of launch_bwd.
+template <class Dec>
+int launch_bwd_prepare(int64_t n_items, Dec dec, void* ws, cudaStream_t s) {
+  const int64_t n_rows = dec.n_rows;
+  const int64_t nc = n_chunks_of(n_items);
+  BwdView v = carve_bwd(ws, n_items, Dec::kSlots, n_rows);
+  CNNUE_CUDA_TRY(cudaMemsetAsync(v.status, 0, 4, s));
+  const size_t hist_smem = (size_t)n_rows * 4;
+  if (hist_smem > 200 * 1024) return set_error(CNNUE_ERR_INVALID_ARG, "table has too many rows");
+  if (hist_smem > 48 * 1024) {
+    CNNUE_CUDA_TRY(cudaFuncSetAttribute(bwd_hist_kernel<Dec>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)hist_smem));
+    CNNUE_CUDA_TRY(cudaFuncSetAttribute(bwd_scatter_kernel<Dec>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)hist_smem));
+  }
+  if (nc > 0) {
+    bwd_hist_kernel<Dec><<<(unsigned)nc, 256, hist_smem, s>>>(n_items, dec, v);
+    int st = check_launch_error("bwd_hist_kernel");
+    if (st) return st;
+  }
+  bwd_chunk_prefix_kernel<<<(unsigned)((n_rows + 255) / 256), 256, 0, s>>>(nc, n_rows, v);
+  int st = check_launch_error("bwd_chunk_prefix_kernel");
+  if (st) return st;
+  bwd_row_scan_kernel<<<1, 1024, 0, s>>>(n_rows, v);
+  st = check_launch_error("bwd_row_scan_kernel");
+  if (st) return st;
+  if (nc > 0) {
+    bwd_scatter_kernel<Dec><<<(unsigned)nc, 32, hist_smem, s>>>(n_items, dec, v);
+    st = check_launch_error("bwd_scatter_kernel");
+    if (st) return st;
+  }
+  return CNNUE_OK;
 }
 
 template <class Dec>
@@ -359,7 +421,8 @@ int launch_bwd(int64_t n_items, const float* grad_out, int64_t hidden, Dec dec, 
     bwd_reduce_kernel<false><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table);
   st = check_launch_error("bwd_reduce_kernel");
   if (st) return st;
-  bwd_finalize_kernel<<<(unsigned)n_rows, 256, 0, s>>>(hidden, n_rows, v, grad_table);
+  bwd_finalize_kernel<<<(unsigned)((n_rows * 32 + 255) / 256), 256, 0, s>>>(hidden, n_rows, v, grad_table, 0,
+                                                                            n_rows);
   return check_launch_error("bwd_finalize_kernel");
 }
 

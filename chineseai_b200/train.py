@@ -98,20 +98,37 @@ def allreduce_sum_(grads: torch.Tensor, group=None, guard=None, step: int = 0) -
     return dist.get_world_size(group)
 
 
+OFF_W1 = N_FEATURES * COLS + COLS  # first stack parameter (the FT weights and bias come first)
+
+
 class Trainer:
+    """One rank of the HalfKA training step.
+
+    With a process group of more than one rank the step overlaps the
+    gradient exchange with the FT backward: the stack gradients (and a status
+    flag) are all-reduced on a side stream while the FT gradient is reduced,
+    then the FT gradient in `ft_chunks` row ranges, each all-reduced as soon
+    as its rows are final; Adam waits for every exchange and is skipped on
+    every rank when any rank's batch had bad input."""
+
     def __init__(self, params: np.ndarray, device: int = 0, adam: AdamConfig = AdamConfig(), group=None,
-                 guard=None):
+                 guard=None, ft_chunks: int = 4):
         self.device = torch.device("cuda", device)
         self.adam = adam
         self.group = group
         self.guard = guard  # optional dist_guard.StepGuard for the exchange
+        self.ft_chunks = ft_chunks
         n = param_count()
         if params.shape != (n,):
             raise ValueError(f"expected {n} parameters, got {params.shape}")
         self.params = torch.from_numpy(np.ascontiguousarray(params, np.float32)).to(self.device)
         self.m = torch.zeros(n, dtype=torch.float32, device=self.device)
         self.v = torch.zeros(n, dtype=torch.float32, device=self.device)
-        self.grads = torch.empty(n, dtype=torch.float32, device=self.device)
+        # the gradient, then the status flag (reduced with the stack gradients)
+        self._gbuf = torch.zeros(n + 64, dtype=torch.float32, device=self.device)
+        self.grads = self._gbuf[:n]
+        self.flag = self._gbuf[n:n + 1]
+        self._side = None
         self.shadow = torch.empty(SHADOW, dtype=torch.int16, device=self.device)
         self.loss = torch.zeros(1, dtype=torch.float32, device=self.device)
         self.step_count = 0
@@ -138,18 +155,74 @@ class Trainer:
         check(lib().cnnue_read_status(self._ws.data_ptr(), _stream_ptr(stream), C.byref(st)), "cnnue_read_status")
         return st.value
 
-    def apply_adam(self, grad_scale: float, stream=None) -> None:
+    def apply_adam(self, grad_scale: float, stream=None, skip: Optional[torch.Tensor] = None) -> None:
         self.step_count += 1
         a = self.adam
         check(lib().cnnue_t_adam(self.params.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
                                  self.grads.data_ptr(), self.shadow.data_ptr(), grad_scale, a.lr, a.beta1,
-                                 a.beta2, a.eps, self.step_count, _stream_ptr(stream)), "cnnue_t_adam")
+                                 a.beta2, a.eps, self.step_count, skip.data_ptr() if skip is not None else None,
+                                 _stream_ptr(stream)), "cnnue_t_adam")
+
+    def world(self) -> int:
+        import torch.distributed as dist
+        if not (dist.is_available() and dist.is_initialized()):
+            return 1
+        return dist.get_world_size(self.group)
 
     def step(self, idx: torch.Tensor, n_idx: int, off: torch.Tensor, n: int, target: torch.Tensor) -> None:
         """One data-parallel step (asynchronous on the current stream)."""
-        self.forward_backward(idx, n_idx, off, n, target)
-        world = allreduce_sum_(self.grads, self.group, self.guard, self.step_count)
-        self.apply_adam(1.0 / world)
+        if self.world() == 1:
+            self.forward_backward(idx, n_idx, off, n, target)
+            self.apply_adam(1.0)
+            return
+        self._step_overlapped(idx, n_idx, off, n, target)
+
+    def _all_reduce(self, t: torch.Tensor, tag: int):
+        """Sum all-reduce issued on the side stream (after its event waits);
+        returns the work to wait on, or None when the guard ran it to
+        completion."""
+        import torch.distributed as dist
+        if self.guard is not None:
+            self.guard.all_reduce(t, 8 * self.step_count + tag)
+            return None
+        return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+
+    def _step_overlapped(self, idx, n_idx, off, n, target) -> None:
+        ws = self.workspace(n, n_idx)
+        s = torch.cuda.current_stream(self.device)
+        sp = s.cuda_stream
+        if self._side is None:
+            self._side = torch.cuda.Stream(self.device)
+        L = lib()
+        check(L.cnnue_t_forward_backward_begin(self.params.data_ptr(), self.shadow.data_ptr(), idx.data_ptr(), n_idx,
+                                               off.data_ptr(), n, target.data_ptr(), self.grads.data_ptr(),
+                                               ws.data_ptr(), ws.numel(), sp), "cnnue_t_forward_backward_begin")
+        check(L.cnnue_t_finish(n, n_idx, self.loss.data_ptr(), ws.data_ptr(), ws.numel(), self.flag.data_ptr(), sp),
+              "cnnue_t_finish")
+        works = []
+
+        def exchange(t, tag):
+            ev = torch.cuda.Event()
+            ev.record(s)
+            with torch.cuda.stream(self._side):
+                self._side.wait_event(ev)
+                works.append(self._all_reduce(t, tag))
+
+        exchange(self._gbuf[OFF_W1:param_count() + 1], 0)  # stack gradients + the status flag
+        rows = N_FEATURES + 1
+        bounds = [rows * k // self.ft_chunks for k in range(self.ft_chunks + 1)]
+        for k in range(self.ft_chunks):
+            rb, re = bounds[k], bounds[k + 1]
+            check(L.cnnue_t_ft_grad_rows(n, n_idx, self.grads.data_ptr(), ws.data_ptr(), ws.numel(), rb, re, sp),
+                  "cnnue_t_ft_grad_rows")
+            exchange(self.grads[rb * COLS: re * COLS], 1 + k)
+        for w in works:
+            if w is not None:
+                w.wait()  # the current stream waits for the collective
+        ev = torch.cuda.Event()
+        ev.record(self._side)
+        s.wait_event(ev)
+        self.apply_adam(1.0 / self.world(), skip=self.flag)
 
     def step_positions(self, pos: Positions, target: np.ndarray) -> float:
         """Convenience: host batch -> one step; returns this rank's loss."""
@@ -158,4 +231,7 @@ class Trainer:
         t = torch.from_numpy(np.ascontiguousarray(target, np.float32)).to(self.device)
         self.step(idx, len(pos.indices), off, pos.n, t)
         check(self.status(), "training step (kernel status)")
+        if self.world() > 1 and float(self.flag.item()) != 0.0:
+            from ._lib import CnnueError
+            raise CnnueError(2, "training step", "a rank's batch had bad input; no rank applied Adam")
         return float(self.loss.item())

@@ -394,11 +394,35 @@ int cnnue_t_forward_backward(const float* d_params, const uint16_t* d_shadow,
                              const uint32_t* d_offsets, int64_t n_positions, const float* d_target,
                              float* d_grads, float* d_loss, void* d_workspace,
                              size_t workspace_bytes, void* stream);
+/* cnnue_t_forward_backward in three phases, so that a data-parallel caller
+ * can exchange gradients while the FT gradient is still being reduced (the
+ * backward of GpuTrainer::compute_batch_grads, src/az/train_gpu_candle.rs:
+ * 166-219, split at its gradient boundaries):
+ *   _begin: everything but the FT gradient - gather, head, loss terms, the
+ *     stack gradients (W1..b3 of d_grads are final when it completes) and the
+ *     preparation of the FT segmented reduction;
+ *   _ft_grad_rows: the FT gradient rows [row_begin, row_end) of the table
+ *     [11340 + 1][1024] (row 11340 is the FT bias); ranges may be issued in
+ *     any order and split any way, results are the same;
+ *   _finish: the mean loss into d_loss[0] and, when d_flag is not null, the
+ *     kernels' status as a float flag (0 clean, 1 bad input) to reduce with
+ *     the gradient. */
+int cnnue_t_forward_backward_begin(const float* d_params, const uint16_t* d_shadow, const uint16_t* d_indices,
+                                   uint32_t n_indices, const uint32_t* d_offsets, int64_t n_positions,
+                                   const float* d_target, float* d_grads, void* d_workspace,
+                                   size_t workspace_bytes, void* stream);
+int cnnue_t_ft_grad_rows(int64_t n_positions, uint32_t n_indices, float* d_grads, void* d_workspace,
+                         size_t workspace_bytes, int64_t row_begin, int64_t row_end, void* stream);
+int cnnue_t_finish(int64_t n_positions, uint32_t n_indices, float* d_loss, void* d_workspace,
+                   size_t workspace_bytes, float* d_flag, void* stream);
+
 /* Adam step over all parameters with gradient grad * grad_scale (e.g. 1/world
- * after a sum all-reduce); refreshes the bf16 shadow.  step counts from 1. */
+ * after a sum all-reduce); refreshes the bf16 shadow.  step counts from 1.
+ * When d_skip is not null and *d_skip != 0 (a status flag summed over the
+ * ranks) nothing is updated. */
 int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, uint16_t* d_shadow,
                  float grad_scale, float lr, float beta1, float beta2, float eps, int step,
-                 void* stream);
+                 const float* d_skip, void* stream);
 
 /* AdamW step over n fp32 parameters (flat buffer) with moments m, v, as
  * candle-nn's AdamW::step (the AZ trainer's optimizer, lr / betas / eps /

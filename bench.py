@@ -143,13 +143,26 @@ def cpu_threads() -> int:
 
 
 def cpu_cpu_model() -> str:
+    """Host CPU: model name, sockets x cores per socket, logical CPUs, and
+    whether the timed CPU path runs its AVX2 kernels."""
+    model, cores, sockets = "unknown", None, set()
     try:
         for line in open("/proc/cpuinfo"):
-            if line.startswith("model name"):
-                return line.split(":", 1)[1].strip()
+            if line.startswith("model name") and model == "unknown":
+                model = line.split(":", 1)[1].strip()
+            elif line.startswith("cpu cores") and cores is None:
+                cores = int(line.split(":", 1)[1])
+            elif line.startswith("physical id"):
+                sockets.add(line.split(":", 1)[1].strip())
     except Exception:
         pass
-    return "unknown"
+    try:
+        import oracle
+        avx2 = bool(oracle.lib().oracle_q_has_avx2())
+    except Exception:
+        avx2 = False
+    return (f"{model}, {max(len(sockets), 1)} socket(s) x {cores} cores, {os.cpu_count()} logical CPUs, "
+            f"{'AVX2 kernels' if avx2 else 'scalar kernels'}")
 
 
 def cpu_time_batches(w, pos, threads: int, min_seconds: float, min_reps: int):

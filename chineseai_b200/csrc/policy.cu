@@ -3,7 +3,8 @@
 // table lookups (src/az/fused_sparse_policy.rs), forward and backward.
 //
 // Forward kernels keep the CPU twins' operation order (one product and one
-// add per term, no fused multiply-add), so outputs are bit-identical to them.
+// add per term, no fused multiply-add), so outputs are bit-identical to them;
+// fused_policy runs a warp per board with lanes over its moves.
 // Backward passes are atomic-free and deterministic (scatter.cuh):
 //   - fused_policy: the table gradient splits by section.  Feature rows (the
 //     consequence rows and the accumulator feature rows, 1260 x 32 each) take
@@ -16,6 +17,8 @@
 //     its moves in order by one thread per (board, context column);
 //   - sparse / tactical: scalar (entry, output) pairs through the scalar
 //     scatter.
+#include <algorithm>
+
 #include "common.cuh"
 #include "scatter.cuh"
 
@@ -57,37 +60,93 @@ __device__ __forceinline__ bool in_range(const Item& it) {
                        (!it.capture || it.cap < (uint32_t)CNNUE_AZ_INPUT)));
 }
 
-__global__ void fused_fwd_kernel(const float* __restrict__ t, const float* __restrict__ ctx,
-                                 const int64_t* __restrict__ items, int64_t batch, int64_t moves,
-                                 float* __restrict__ out, uint32_t* status) {
-  const int64_t n = batch * moves;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    const Item it = decode(items[i]);
-    if (!it.policy) {
-      out[i] = 0.f;
-      continue;
-    }
-    if (!in_range(it)) {
-      atomicOr(status, CNNUE_STATUS_BAD_INDEX);
-      out[i] = 0.f;
-      continue;
-    }
-    float v = t[kBias + it.mv];
-    if (it.move) {
-      const float* c = ctx + (i / moves) * kCtx;
-      for (int h = 0; h < 32; ++h) {
-        float delta = __fsub_rn(t[it.to * 32 + h], t[it.from * 32 + h]);
-        if (it.capture) delta = __fsub_rn(delta, t[it.cap * 32 + h]);
-        v = __fadd_rn(v, __fmul_rn(delta, t[kConsequence + h]));
+// One warp per board, lane l taking the board's moves l, l + 32, ...: the
+// board's 48 context values and the 32 consequence weights sit in shared
+// memory, and a move's table rows are read as vectors (float4 for the
+// 32-float rows of the consequence section, which start on 16-byte
+// boundaries; float2 for the move-context, accumulator-feature and
+// accumulator-move sections, whose offsets are 2 mod 4 floats).  Each move's
+// 80 terms are added in the CPU twin's order (one product and one add per
+// term, no contraction), so outputs stay bit-identical to it.
+constexpr int kFwdWarps = 8;
+
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float2 ld2(const float* p) { return __ldg(reinterpret_cast<const float2*>(p)); }
+
+__global__ void __launch_bounds__(32 * kFwdWarps) fused_fwd_kernel(const float* __restrict__ t,
+                                                                   const float* __restrict__ ctx,
+                                                                   const int64_t* __restrict__ items, int64_t batch,
+                                                                   int64_t moves, float* __restrict__ out,
+                                                                   uint32_t* status) {
+  __shared__ float cons[32];
+  __shared__ float cs[kFwdWarps][kCtx];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x < 32) cons[threadIdx.x] = t[kConsequence + threadIdx.x];
+  __syncthreads();
+  const int64_t n_warps = (int64_t)gridDim.x * kFwdWarps;
+  for (int64_t b = (int64_t)blockIdx.x * kFwdWarps + warp; b < batch; b += n_warps) {
+    __syncwarp();
+    cs[warp][lane] = ctx[b * kCtx + lane];
+    if (lane < kCtx - 32) cs[warp][32 + lane] = ctx[b * kCtx + 32 + lane];
+    __syncwarp();
+    const float* c = cs[warp];
+    for (int64_t m = lane; m < moves; m += 32) {
+      const int64_t i = b * moves + m;
+      const Item it = decode(items[i]);
+      if (!it.policy) {
+        out[i] = 0.f;
+        continue;
       }
-      for (int h = 0; h < 16; ++h) v = __fadd_rn(v, __fmul_rn(c[h], t[kContext + it.mv * 16 + h]));
-      for (int h = 0; h < 32; ++h) {
-        float after = __fsub_rn(__fadd_rn(c[16 + h], t[kAccFeature + it.to * 32 + h]), t[kAccFeature + it.from * 32 + h]);
-        if (it.capture) after = __fsub_rn(after, t[kAccFeature + it.cap * 32 + h]);
-        v = __fadd_rn(v, __fmul_rn(after, t[kAccMove + it.mv * 32 + h]));
+      if (!in_range(it)) {
+        atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+        out[i] = 0.f;
+        continue;
       }
+      float v = __ldg(t + kBias + it.mv);
+      if (it.move) {
+        const float* rt = t + it.to * 32;
+        const float* rf = t + it.from * 32;
+        const float* rc = t + it.cap * 32;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 a = ld4(rt + 4 * q), f = ld4(rf + 4 * q);
+          float4 d = make_float4(__fsub_rn(a.x, f.x), __fsub_rn(a.y, f.y), __fsub_rn(a.z, f.z), __fsub_rn(a.w, f.w));
+          if (it.capture) {
+            const float4 e = ld4(rc + 4 * q);
+            d = make_float4(__fsub_rn(d.x, e.x), __fsub_rn(d.y, e.y), __fsub_rn(d.z, e.z), __fsub_rn(d.w, e.w));
+          }
+          v = __fadd_rn(v, __fmul_rn(d.x, cons[4 * q]));
+          v = __fadd_rn(v, __fmul_rn(d.y, cons[4 * q + 1]));
+          v = __fadd_rn(v, __fmul_rn(d.z, cons[4 * q + 2]));
+          v = __fadd_rn(v, __fmul_rn(d.w, cons[4 * q + 3]));
+        }
+        const float* mc = t + kContext + it.mv * 16;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float2 w = ld2(mc + 2 * q);
+          v = __fadd_rn(v, __fmul_rn(c[2 * q], w.x));
+          v = __fadd_rn(v, __fmul_rn(c[2 * q + 1], w.y));
+        }
+        const float* at = t + kAccFeature + it.to * 32;
+        const float* af = t + kAccFeature + it.from * 32;
+        const float* ac = t + kAccFeature + it.cap * 32;
+        const float* am = t + kAccMove + it.mv * 32;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) {
+          const float2 x = ld2(at + 2 * q), y = ld2(af + 2 * q), w = ld2(am + 2 * q);
+          float a0 = __fsub_rn(__fadd_rn(c[16 + 2 * q], x.x), y.x);
+          float a1 = __fsub_rn(__fadd_rn(c[17 + 2 * q], x.y), y.y);
+          if (it.capture) {
+            const float2 z = ld2(ac + 2 * q);
+            a0 = __fsub_rn(a0, z.x);
+            a1 = __fsub_rn(a1, z.y);
+          }
+          v = __fadd_rn(v, __fmul_rn(a0, w.x));
+          v = __fadd_rn(v, __fmul_rn(a1, w.y));
+        }
+      }
+      out[i] = v;
     }
-    out[i] = v;
   }
 }
 
@@ -333,8 +392,10 @@ int cnnue_policy_fused_fwd(const float* d_tables, const float* d_context, const 
   if (batch < 0 || moves < 0 || (batch * moves > 0 && (!d_tables || !d_context || !d_items || !d_out || !d_status)))
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
   if (batch * moves == 0) return CNNUE_OK;
-  fused_fwd_kernel<<<grid_for(batch * moves), 256, 0, (cudaStream_t)stream>>>(d_tables, d_context, d_items, batch,
-                                                                              moves, d_out, d_status);
+  if ((uintptr_t)d_tables & 15u) return set_error(CNNUE_ERR_INVALID_ARG, "d_tables must be 16-byte aligned");
+  const int64_t blocks = std::min<int64_t>((batch + kFwdWarps - 1) / kFwdWarps, 148 * 16);
+  fused_fwd_kernel<<<(unsigned)blocks, 32 * kFwdWarps, 0, (cudaStream_t)stream>>>(d_tables, d_context, d_items,
+                                                                                 batch, moves, d_out, d_status);
   return check_launch_error("fused_fwd_kernel");
 }
 

@@ -51,6 +51,9 @@
 #include <string.h>
 #ifdef _OPENMP
 #include <omp.h>
+#ifdef __AVX2__
+#include <immintrin.h>
+#endif
 #endif
 
 #define Q_F 11340
@@ -170,7 +173,119 @@ int oracle_q_forward(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
                          scores, acc_out);
 }
 
-/* Multi-threaded variant (OpenMP, static split) used as the timed CPU baseline. */
+#ifdef __AVX2__
+/* The timed CPU baseline's hand-written AVX2 path (the reference's own
+ * evaluator adds int8/int16 rows with 256-bit integer adds, src/az.rs:
+ * 2616-2654); every result is bit-identical to the scalar forward above.
+ *   - accumulation in 4 column tiles of 256 int16: a tile lives in 16 ymm
+ *     registers while every row of the list is added (_mm256_add_epi16:
+ *     int16 wraparound);
+ *   - pack: clamp by max/min, 16-bit products (at most 127 * 127), >> 7,
+ *     unsigned saturating narrow (no saturation: results are at most 126);
+ *   - L1: _mm256_maddubs_epi16 of the packed uint8 (<= 126) with the int8
+ *     weights (pair sums within +-2 * 126 * 128, inside int16, so exact),
+ *     _mm256_madd_epi16 with ones to int32. */
+static int q_accumulate_avx2(const int16_t* ft, const int16_t* bias, const uint16_t* idx, uint32_t n,
+                             int16_t* acc) {
+  int status = 0;
+  for (int t = 0; t < Q_COLS; t += 256) {
+    __m256i r[16];
+    for (int k = 0; k < 16; ++k) r[k] = _mm256_loadu_si256((const __m256i*)(bias + t + 16 * k));
+    for (uint32_t i = 0; i < n; ++i) {
+      const uint32_t f = idx[i];
+      if (f >= Q_F) {
+        status = 2;
+        continue;
+      }
+      const int16_t* row = ft + (size_t)f * Q_COLS + t;
+      for (int k = 0; k < 16; ++k) r[k] = _mm256_add_epi16(r[k], _mm256_loadu_si256((const __m256i*)(row + 16 * k)));
+    }
+    for (int k = 0; k < 16; ++k) _mm256_storeu_si256((__m256i*)(acc + t + 16 * k), r[k]);
+  }
+  return status;
+}
+
+static void q_pack_avx2(const int16_t* acc, uint8_t* out512) {
+  const __m256i zero = _mm256_setzero_si256(), top = _mm256_set1_epi16(127);
+  for (int j = 0; j < Q_HALF; j += 32) {
+    __m256i a0 = _mm256_loadu_si256((const __m256i*)(acc + j));
+    __m256i a1 = _mm256_loadu_si256((const __m256i*)(acc + j + 16));
+    __m256i b0 = _mm256_loadu_si256((const __m256i*)(acc + j + Q_HALF));
+    __m256i b1 = _mm256_loadu_si256((const __m256i*)(acc + j + Q_HALF + 16));
+    a0 = _mm256_min_epi16(_mm256_max_epi16(a0, zero), top);
+    a1 = _mm256_min_epi16(_mm256_max_epi16(a1, zero), top);
+    b0 = _mm256_min_epi16(_mm256_max_epi16(b0, zero), top);
+    b1 = _mm256_min_epi16(_mm256_max_epi16(b1, zero), top);
+    const __m256i p0 = _mm256_srli_epi16(_mm256_mullo_epi16(a0, b0), 7);
+    const __m256i p1 = _mm256_srli_epi16(_mm256_mullo_epi16(a1, b1), 7);
+    /* packus interleaves the 128-bit lanes: restore the column order */
+    const __m256i u8 = _mm256_permute4x64_epi64(_mm256_packus_epi16(p0, p1), 0xd8);
+    _mm256_storeu_si256((__m256i*)(out512 + j), u8);
+  }
+}
+
+static int32_t q_stack_avx2(const uint8_t* x, int bucket, const int8_t* l1w, const int32_t* l1b,
+                            const int8_t* l2w, const int32_t* l2b, const int8_t* l3w, const int32_t* l3b) {
+  int32_t y1[Q_L1], y2[Q_L2];
+  const int8_t* w1 = l1w + (size_t)bucket * Q_L1 * Q_COLS;
+  const __m256i ones = _mm256_set1_epi16(1);
+  for (int k = 0; k < Q_L1; ++k) {
+    __m256i s = _mm256_setzero_si256();
+    for (int i = 0; i < Q_COLS; i += 32) {
+      const __m256i xv = _mm256_loadu_si256((const __m256i*)(x + i));
+      const __m256i wv = _mm256_loadu_si256((const __m256i*)(w1 + k * Q_COLS + i));
+      s = _mm256_add_epi32(s, _mm256_madd_epi16(_mm256_maddubs_epi16(xv, wv), ones));
+    }
+    __m128i h = _mm_add_epi32(_mm256_castsi256_si128(s), _mm256_extracti128_si256(s, 1));
+    h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0x4e));
+    h = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0xb1));
+    y1[k] = clampi((l1b[bucket * Q_L1 + k] + _mm_cvtsi128_si32(h)) >> 6, 0, 127);
+  }
+  const int8_t* w2 = l2w + (size_t)bucket * Q_L2 * Q_L1;
+  for (int m = 0; m < Q_L2; ++m) {
+    int32_t s = l2b[bucket * Q_L2 + m];
+    for (int k = 0; k < Q_L1; ++k) s += (int32_t)w2[m * Q_L1 + k] * y1[k];
+    y2[m] = clampi(s >> 6, 0, 127);
+  }
+  int32_t s = l3b[bucket];
+  for (int m = 0; m < Q_L2; ++m) s += (int32_t)l3w[bucket * Q_L2 + m] * y2[m];
+  return s;
+}
+
+static int q_forward_range_avx2(const int16_t* ft, const int16_t* bias, const int8_t* l1w, const int32_t* l1b,
+                                const int8_t* l2w, const int32_t* l2b, const int8_t* l3w, const int32_t* l3b,
+                                const uint16_t* idx, const uint32_t* offsets, int64_t begin, int64_t end,
+                                int32_t* scores) {
+  int status = 0;
+  int16_t acc[2][Q_COLS];
+  uint8_t x[Q_COLS];
+  for (int64_t p = begin; p < end; ++p) {
+    for (int s = 0; s < 2; ++s) {
+      uint32_t b = offsets[2 * p + s], e = offsets[2 * p + s + 1];
+      int st = q_accumulate_avx2(ft, bias, idx + b, e - b, acc[s]);
+      if (st) status = st;
+      q_pack_avx2(acc[s], x + s * Q_HALF);
+    }
+    uint32_t n0 = offsets[2 * p + 1] - offsets[2 * p];
+    scores[p] = q_stack_avx2(x, oracle_q_bucket(n0), l1w, l1b, l2w, l2b, l3w, l3b);
+  }
+  return status;
+}
+#define Q_FORWARD_RANGE_FAST(...) q_forward_range_avx2(__VA_ARGS__)
+#else
+#define Q_FORWARD_RANGE_FAST(...) q_forward_range(__VA_ARGS__, NULL)
+#endif
+
+int oracle_q_has_avx2(void) {
+#ifdef __AVX2__
+  return 1;
+#else
+  return 0;
+#endif
+}
+
+/* Multi-threaded variant (OpenMP, static split) used as the timed CPU
+ * baseline: the AVX2 path when the library is built for it. */
 int oracle_q_forward_mt(const int16_t* ft, const int16_t* bias, const int8_t* l1w,
                         const int32_t* l1b, const int8_t* l2w, const int32_t* l2b,
                         const int8_t* l3w, const int32_t* l3b, const uint16_t* idx,
@@ -187,13 +302,11 @@ int oracle_q_forward_mt(const int16_t* ft, const int16_t* bias, const int8_t* l1
     int64_t chunk = (n_positions + nt - 1) / nt;
     int64_t b = t * chunk, e = b + chunk < n_positions ? b + chunk : n_positions;
     if (b < e)
-      status |= q_forward_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, b, e,
-                                scores, NULL);
+      status |= Q_FORWARD_RANGE_FAST(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, b, e, scores);
   }
 #else
   (void)n_threads;
-  status = q_forward_range(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, 0, n_positions,
-                           scores, NULL);
+  status = Q_FORWARD_RANGE_FAST(ft, bias, l1w, l1b, l2w, l2b, l3w, l3b, idx, offsets, 0, n_positions, scores);
 #endif
   return status;
 }

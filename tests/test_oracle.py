@@ -206,3 +206,20 @@ def test_feature_pool_oracle_flags_rows_past_table():
     tables = np.zeros((1545, 4), np.float32)
     items = np.array([[0 | (15 << 15)]], np.uint32)  # them bucket 15 -> row past 1545
     assert oracle.feature_pool_fwd(tables, items, 4)[0] == 2
+
+
+def test_cpu_baseline_avx2_path_matches_scalar_oracle():
+    """The timed CPU baseline (oracle_q_forward_mt: hand-written AVX2 row adds,
+    pack and L1 when built for AVX2) is bit-identical to the scalar oracle,
+    including int16 wraparound and empty lists."""
+    import oracle
+    from chineseai_b200 import synth
+    w = synth.quantized_weights(2)
+    cases = [synth.positions(n, seed) for n, seed in [(1, 3), (513, 4), (3000, 5)]]
+    idx = np.concatenate([np.full(300, 5, np.uint16), np.full(257, 11339, np.uint16)])
+    cases.append(synth.Positions(idx, np.array([0, 300, 557, 557, 557], np.uint32)))
+    for pos in cases:
+        st, ref = oracle.q_forward(w, pos)[:2]
+        st2, fast = oracle.q_forward_mt(w, pos, 3)
+        assert st == st2 == 0
+        np.testing.assert_array_equal(fast, ref)

@@ -395,7 +395,8 @@ def run_train(args):
     from chineseai_b200 import synth, train
     from chineseai_b200.quantized import as_device
 
-    tr = train.Trainer(train.init_params(3), device=local, group=pg.group.WORLD if pg else None)
+    tr = train.Trainer(train.init_params(3), device=local, group=pg.group.WORLD if pg else None,
+                       ft_chunks=args.ft_chunks)
     pos = synth.positions(TRAIN_BATCH, 1 + rank)
     t = torch.from_numpy(train.targets(TRAIN_BATCH, 100 + rank)).to(dev)
     idx, off = as_device(pos.indices, dev), as_device(pos.offsets, dev)
@@ -457,7 +458,7 @@ def run_train(args):
                                    "tcgen05), MSE(sigmoid(s/400), t), atomic-free FT backward, NCCL all-reduce "
                                    "overlapped with the FT backward (stack gradients + 4 FT row chunks), Adam",
                        "batch_per_gpu": TRAIN_BATCH, "global_batch": world * TRAIN_BATCH,
-                       "parallelism": f"dp{world}", "grad_bytes": grad_bytes},
+                       "parallelism": f"dp{world}", "grad_bytes": grad_bytes, "ft_chunks": args.ft_chunks},
             "phases_ms": {"forward_backward_alone": fb, "allreduce_alone": ar, "adam_alone": ad,
                           "exposed_exchange": ms - fb - ad},
             "allreduce_busbw_gbs": (2 * (world - 1) / world * grad_bytes / (ar / 1e3) / 1e9) if world > 1 else None,
@@ -1205,6 +1206,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ft-chunks", type=int, default=4, help="train: FT-gradient row chunks exchanged as they finish")
     ap.add_argument("--workload", choices=["eval", "fp32", "update", "train", "resnet", "az", "az-train", "mcts"],
                     default="eval",
                     help="eval: the headline quantised forward; fp32: the fp32 forward (batch 4096); "

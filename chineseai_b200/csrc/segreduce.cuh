@@ -299,29 +299,34 @@ __global__ void bwd_reduce_kernel(const float* __restrict__ grad_out, int64_t hi
   }
 }
 
-// One warp per row: rows with several units sum their unit partials in unit
-// order (lanes over columns); rows without contributions get zeros; rows
-// with one unit were written by the reduction itself.
+// Rows with several units sum their unit partials in unit order; rows
+// without contributions get zeros; rows with one unit were written by the
+// reduction itself.  Grid: (row groups of 8, column chunks of 256); warp w of
+// a CTA takes row 8 blockIdx.x + w and its lanes 8 columns each of the
+// chunk, so the few rows with many units (the FT bias row: every list) are
+// summed by many lanes with independent loads.
+constexpr int kFinRows = 8;
+constexpr int kFinCols = 256;
 __global__ void bwd_finalize_kernel(int64_t hidden, int64_t n_rows, BwdView v,
                                     float* __restrict__ grad_table, int64_t row_begin = 0, int64_t row_end = -1) {
   if (row_end < 0) row_end = n_rows;
-  const int64_t r = row_begin + (((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int64_t r = row_begin + (int64_t)blockIdx.x * kFinRows + (threadIdx.x >> 5);
   if (r >= row_end) return;
   const uint32_t u0 = v.unit_start[r], u1 = v.unit_start[r + 1];
   if (u1 - u0 == 1) return;
-  for (int64_t h = threadIdx.x & 31; h < hidden; h += 32) {
-    float acc = 0.f;
-    uint32_t u = u0;
-    for (; u + 4 <= u1; u += 4) {
-      float p[4];
+  const int64_t h0 = (int64_t)blockIdx.y * kFinCols + (threadIdx.x & 31) * 8;
+  if (h0 >= hidden) return;
+  const int nh = (int)min((int64_t)8, hidden - h0);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (uint32_t u = u0; u < u1; ++u) {  // unit order; the 8 columns are independent loads
+    const float* pr = v.partial + (int64_t)u * hidden + h0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) p[q] = v.partial[(int64_t)(u + q) * hidden + h];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) acc += p[q];
-    }
-    for (; u < u1; ++u) acc += v.partial[(int64_t)u * hidden + h];
-    grad_table[r * hidden + h] = acc;
+    for (int q = 0; q < 8; ++q)
+      if (q < nh) acc[q] += pr[q];
   }
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    if (q < nh) grad_table[r * hidden + h0 + q] = acc[q];
 }
 
 // The reduction of rows [row_begin, row_end) after launch_bwd_prepare (any
@@ -340,9 +345,9 @@ inline int launch_bwd_rows(int64_t n_items, int slots, const float* grad_out, in
     bwd_reduce_kernel<false><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table, row_begin, row_end);
   int st = check_launch_error("bwd_reduce_kernel");
   if (st) return st;
-  bwd_finalize_kernel<<<(unsigned)(((row_end - row_begin) * 32 + 255) / 256), 256, 0, s>>>(hidden, n_rows, v,
-                                                                                          grad_table, row_begin,
-                                                                                          row_end);
+  const dim3 fgrid((unsigned)((row_end - row_begin + kFinRows - 1) / kFinRows),
+                   (unsigned)((hidden + kFinCols - 1) / kFinCols));
+  bwd_finalize_kernel<<<fgrid, 32 * kFinRows, 0, s>>>(hidden, n_rows, v, grad_table, row_begin, row_end);
   return check_launch_error("bwd_finalize_kernel");
 }
 
@@ -421,8 +426,8 @@ int launch_bwd(int64_t n_items, const float* grad_out, int64_t hidden, Dec dec, 
     bwd_reduce_kernel<false><<<rblocks, 256, 0, s>>>(grad_out, hidden, n_rows, v, grad_table);
   st = check_launch_error("bwd_reduce_kernel");
   if (st) return st;
-  bwd_finalize_kernel<<<(unsigned)((n_rows * 32 + 255) / 256), 256, 0, s>>>(hidden, n_rows, v, grad_table, 0,
-                                                                            n_rows);
+  const dim3 fgrid((unsigned)((n_rows + kFinRows - 1) / kFinRows), (unsigned)((hidden + kFinCols - 1) / kFinCols));
+  bwd_finalize_kernel<<<fgrid, 32 * kFinRows, 0, s>>>(hidden, n_rows, v, grad_table, 0, n_rows);
   return check_launch_error("bwd_finalize_kernel");
 }
 

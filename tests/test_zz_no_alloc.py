@@ -73,3 +73,37 @@ def test_no_alloc_refuses_batches_above_its_limit(qweights):
         assert str(MAX_POSITIONS) in last_error()
     finally:
         model.close()
+
+
+def test_no_alloc_allocates_nothing_and_clears_its_status(qweights):
+    """The property the entry point exists for: once the library and the
+    model are set up (a first call has looked up the scratch address), a call
+    takes no device memory - the device's free memory is the same after it.
+    A call on bad offsets reports CNNUE_ERR_BAD_OFFSETS through the shared
+    scratch's status word, and the next good call is clean and exact."""
+    model = QuantizedNnue(qweights, device=0)
+    try:
+        pos = synth.positions(4096, 43)
+        idx = as_device(pos.indices, model.device)
+        off = as_device(pos.offsets, model.device)
+        expected = _with_workspace(model, idx, off, pos.n)
+        out = torch.empty(pos.n, dtype=torch.int32, device=model.device)
+        stream = torch.cuda.current_stream().cuda_stream
+        call = lambda i, o, n: lib().cnnue_q_forward_noalloc(  # noqa: E731
+            model.handle, i.data_ptr(), i.numel(), o.data_ptr(), n, out.data_ptr(), stream)
+        assert call(idx, off, pos.n) == 0  # warm-up: the scratch address is looked up here
+        torch.cuda.synchronize()
+        free_before, _ = torch.cuda.mem_get_info(model.device)
+        for _ in range(3):
+            assert call(idx, off, pos.n) == 0
+        torch.cuda.synchronize()
+        free_after, _ = torch.cuda.mem_get_info(model.device)
+        assert free_after == free_before
+        np.testing.assert_array_equal(out.cpu().numpy(), expected)
+        bad_idx = as_device(np.array([3, 4, 5], np.uint16), model.device)
+        bad_off = as_device(np.array([0, 3, 2], np.uint32), model.device)
+        assert call(bad_idx, bad_off, 1) == 3  # CNNUE_ERR_BAD_OFFSETS
+        assert call(idx, off, pos.n) == 0
+        np.testing.assert_array_equal(out.cpu().numpy(), expected)
+    finally:
+        model.close()

@@ -111,6 +111,10 @@ SIGNATURES = {
     "cnnue_az_policy_moves": (c_int, [P, c_int, P, c_int, P]),
     "cnnue_az_pack_batch": (c_int, [c_void_p, P, c_i64, c_i64, c_i64, c_i64, c_int, c_void_p, c_int]),
     "cnnue_az_expand_policy_indices": (c_int, [P, P, P, c_i64, c_i64, P, P, P, P]),
+    "cnnue_azt_create": (c_int, [c_int, C.POINTER(c_void_p)]),
+    "cnnue_azt_destroy": (c_int, [c_void_p]),
+    "cnnue_azt_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64]),
+    "cnnue_azt_step": (c_int, [c_void_p, P, P, c_i64, P, c_i64, P, C.c_float, C.c_float, P, P, P, c_size, P]),
     "cnnue_az_legal_moves": (c_int, [P, c_int, P, c_int, C.POINTER(c_int)]),
     "cnnue_mcts_default_limits": (None, [c_void_p]),
     "cnnue_mcts_create": (c_int, [c_void_p, c_void_p, c_int, C.POINTER(c_void_p)]),

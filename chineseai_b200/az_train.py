@@ -143,6 +143,18 @@ class PackedBatch:
 _PACKED_FIELDS = [f.name for f in fields(PackedBatch)]
 
 
+class _CAztBatch(C.Structure):
+    """cnnue_azt_batch: the packed batch's device arrays (full form)."""
+    _fields_ = [(n, C.c_int64) for n in ("batch", "features", "moves", "threats")] + \
+        [(n, C.c_void_p) for n in (
+            "feature_items", "value_threat_indices", "policy_items", "policy_sparse_indices",
+            "policy_tactical_indices", "policy_targets", "policy_mask", "value_wdl", "values", "rule_context",
+            "policy_weights", "value_weights", "value_phase_masks")]
+
+
+NATIVE_HIDDEN = (32, 64, 128, 256, 512)  # hidden sizes of the native step (cnnue_azt_step)
+
+
 class _CPacked(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("batch", "max_features", "max_policy_moves", "max_value_threats")] + \
         [(name, C.c_void_p) for name in _PACKED_FIELDS]
@@ -339,9 +351,15 @@ class AzTrainer:
 
     def __init__(self, weights: "az.AzWeights", lr: float = 1e-3, device: int = 0, weight_decay: float = 1e-4,
                  beta1: float = 0.9, beta2: float = 0.999, eps: float = 1e-8, graph: bool = False, group=None,
-                 guard=None):
+                 guard=None, native: Optional[bool] = None):
         import torch
         self.torch = torch
+        if native is None:
+            native = weights.hidden in NATIVE_HIDDEN
+        if native and weights.hidden not in NATIVE_HIDDEN:
+            raise ValueError(f"the native step supports hidden sizes {NATIVE_HIDDEN}, got {weights.hidden}")
+        self.native = native
+        self._engine = None
         self.use_graph = graph
         self.group = group
         self.guard = guard  # optional dist_guard.StepGuard for the exchange
@@ -389,6 +407,26 @@ class AzTrainer:
         state = np.zeros(12, np.float64)
         state[:5] = [lr, beta1, beta2, eps, weight_decay]
         self.adam_state = torch.from_numpy(state.view(np.uint8).copy()).to(self.device)
+        # native step: leaf offsets of the flat buffers, metrics, workspaces by batch shape
+        self._leaf_offsets = np.array([off for _, _, _, _, off, _ in layout], np.int64)
+        self._metrics = torch.zeros(_N_METRICS + 1, dtype=torch.float32, device=self.device)
+        self._ws = {}
+        if self.native:
+            e = C.c_void_p()
+            check(lib().cnnue_azt_create(device, C.byref(e)), "cnnue_azt_create")
+            self._engine = e
+
+    def close(self) -> None:
+        """Releases the native step's engine (its stream and events)."""
+        if self._engine is not None:
+            lib().cnnue_azt_destroy(self._engine)
+            self._engine = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
     def set_learning_rate(self, lr: float) -> None:
         """GpuTrainer::set_learning_rate (src/az/train_gpu_candle.rs:134-136)."""
@@ -513,7 +551,42 @@ class AzTrainer:
                                  phase.reshape(-1)])
         return loss, metrics
 
+    def native_loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0):
+        """The native step's forward, loss and backward (cnnue_azt_step) on a
+        device batch: the 22 gradients land in self.grad (zeroed first);
+        returns the metrics tensor [31] (the 30 statistics of compute_batch_loss,
+        then the kernels' status word as a float).  No optimizer step."""
+        torch = self.torch
+        bt = self.expand(bt)
+        B, F = bt["feature_items"].shape
+        M = bt["policy_items"].shape[1]
+        T = bt["value_threat_indices"].shape[1]
+        key = (B, F, M, T)
+        ws = self._ws.get(key)
+        if ws is None:
+            nbytes = int(lib().cnnue_azt_workspace_bytes(self.hidden, B, F, M, T))
+            if nbytes == 0:
+                raise ValueError(f"native step: unsupported batch dims {key} at hidden {self.hidden}")
+            ws = self._ws[key] = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        names = [f[0] for f in _CAztBatch._fields_[4:]]
+        arrays = {n: bt["values" if n == "values" else n] for n in names}
+        for n, a in arrays.items():
+            if not a.is_contiguous():
+                raise ValueError(f"native step: batch array {n} is not contiguous")
+        batch = _CAztBatch(B, F, M, T, *[arrays[n].data_ptr() for n in names])
+        check(lib().cnnue_azt_step(self._engine, self.flat.data_ptr(), self.grad.data_ptr(), self._tail_at,
+                                   self._leaf_offsets.ctypes.data, self.hidden, C.byref(batch),
+                                   float(value_weight), float(policy_weight), self._metrics.data_ptr(),
+                                   self.status.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   torch.cuda.current_stream(self.device).cuda_stream), "cnnue_azt_step")
+        return self._metrics
+
     def _step_body(self, bt: dict, value_weight: float, policy_weight: float):
+        if self.native:
+            out = self.native_loss(bt, value_weight, policy_weight)
+            if self.world == 1:
+                self._adamw()
+            return out
         self.grad.zero_()
         self.status.zero_()
         loss, metrics = self.loss(self.expand(bt), value_weight, policy_weight)

@@ -1,0 +1,1439 @@
+// az_step.cu - the AZ-NNUE training step as native kernels: forward of
+// AzCandleModel (src/az/candle_model.rs:46-147), the loss of
+// compute_batch_loss (src/az/train_gpu_candle.rs:221-305), and the backward
+// of every one of the 22 weight tensors, in a fixed number of launches
+// whatever the batch (no autograd graph, no library GEMM).
+//
+// Stream layout of one step (cnnue_azt_step):
+//   main:  zero the gradient | forward (trunk per board + accumulator
+//          features) | policy logits + both losses + the logit gradients
+//          (per board) | trunk backward (per board) | wait for the side
+//          stream | table row sums | multi-unit row sums | weight-gradient
+//          tiles + feature-row gradient + metrics
+//   side:  one key per table contribution of the batch | one joint LSD radix
+//          sort of all of them with their runs and units (scatter.cuh)
+// The batch alone decides which table rows a step touches, so the sort runs
+// beside the forward and the per-board backward.
+//
+// Every table gradient (feature pool rows, threat rows, policy move rows,
+// policy feature rows, sparse and tactical scalars) is one sort problem in
+// a joint key space; a run of equal keys is summed in units of at most
+// kUnit contributions, in sorted (= contribution) order, one warp per row
+// unit (lanes over the row's columns) and one lane per scalar unit; runs of
+// several units add their unit partials in order.  Dense weight gradients
+// are reductions over the batch's boards, computed as tiles with a fixed
+// split of the boards and a fixed order of the split partials.  No atomics
+// touch a value, so a step is deterministic run to run.
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "scatter.cuh"
+
+namespace cnnue {
+namespace azt {
+namespace {
+
+constexpr unsigned kFull = 0xffffffffu;
+constexpr uint32_t kPad = 0xffffffffu;
+constexpr int kTrunkRows = CNNUE_AZ_TRUNK_ROWS;  // 1545
+constexpr int kInput = CNNUE_AZ_INPUT;           // 1260
+constexpr int kVH = CNNUE_AZ_VALUE_HEAD;         // 96
+constexpr int kRule = CNNUE_AZ_RULE_CONTEXT;     // 7
+constexpr int kVocab = CNNUE_AZ_THREAT_VOCAB;    // 57702
+constexpr int kTR = CNNUE_AZ_THREAT_RANK;        // 64
+constexpr int kPair = 2 * kTR;                   // 128: [act, act^2]
+constexpr int kMoves = CNNUE_AZ_DENSE_MOVES;     // 2086
+constexpr int kCtx = CNNUE_POLICY_CONTEXT;       // 48 = 16 move context + 32 accumulator
+constexpr int kAcc = 32;                         // accumulator rank
+constexpr int kPsp = 32;                         // consequence columns of the feature rows
+constexpr int64_t kSparseLen = 2596273;          // sparse table + sparse factors
+constexpr int64_t kTactLen = 934977;             // tactical table + its constant zero
+constexpr float kMaskDrop = -1.0e8f;             // masked (the packer writes -1e9)
+
+// Joint key space of the table gradients.
+constexpr uint32_t kKeyPool = 0;
+constexpr uint32_t kKeyThreat = kKeyPool + kTrunkRows;
+constexpr uint32_t kKeyMove = kKeyThreat + kVocab;
+constexpr uint32_t kKeyFeat = kKeyMove + kMoves;
+constexpr uint32_t kKeyRowsEnd = kKeyFeat + kInput;  // keys below: row problems
+constexpr uint32_t kKeySparse = kKeyRowsEnd;
+constexpr uint32_t kKeyTact = kKeySparse + (uint32_t)kSparseLen;
+constexpr uint32_t kKeyDrop = kKeyTact + (uint32_t)kTactLen;
+constexpr uint32_t kUnit = 64;  // contributions per unit
+constexpr int kMoveW = 1 + 16 + kAcc;  // move row: bias, move context, accumulator move
+constexpr int kFeatW = kPsp + kAcc;    // feature row: consequence rows, accumulator features
+
+// The 17 parameter leaves of the flat buffer (tensors 0-4 form the trunk
+// table, 19-20 the sparse table).
+enum Leaf {
+  L_FT, L_RULE, L_HB, L_VHH, L_VHB, L_VHO, L_TE, L_VTO, L_PTC, L_MB, L_CONS, L_PCH, L_MC, L_PAH, L_AM, L_SPARSE,
+  L_TACT, kLeaves
+};
+static_assert(kLeaves == CNNUE_AZT_LEAVES, "leaf count");
+
+struct Params {
+  const float* p[kLeaves];
+};
+struct Grads {
+  float* g[kLeaves];
+};
+
+struct Batch {
+  int64_t B, F, M, T;
+  const uint32_t* fi;   // [B][F]
+  const uint32_t* ti;   // [B][T]
+  const int64_t* pi;    // [B][M]
+  const int64_t* sp;    // [B][M][7]
+  const int64_t* tc;    // [B][M][2]
+  const float* tgt;     // [B][M]
+  const float* mask;    // [B][M]
+  const float* wdl;     // [B][3]
+  const float* values;  // [B]
+  const float* rule;    // [B][7]
+  const float* pw;      // [B]
+  const float* vw;      // [B]
+  const float* phase;   // [B][3]
+};
+
+// Contribution index bases of the joint sort.
+struct Bases {
+  uint32_t pool, threat, move, feat, sparse, tact, n;
+};
+__host__ __device__ inline Bases bases(int64_t B, int64_t F, int64_t M, int64_t T) {
+  Bases b;
+  b.pool = 0;
+  b.threat = (uint32_t)(B * F * 6);
+  b.move = b.threat + (uint32_t)(B * T);
+  b.feat = b.move + (uint32_t)(B * M);
+  b.sparse = b.feat + (uint32_t)(B * M * 3);
+  b.tact = b.sparse + (uint32_t)(B * M * 7);
+  b.n = b.tact + (uint32_t)(B * M * 2);
+  return b;
+}
+
+// Per-board and per-step buffers of the workspace.
+struct Act {
+  float *bp, *hid, *rms, *vh, *ta, *ctx, *vl, *af;      // forward
+  float *dl, *dvl, *dctx, *cons, *rec;                  // loss
+  float *dbp, *dpre, *dta, *dvh;                        // backward
+  float *pspaf;                                         // [1260][64] feature-row gradients
+  float *row_part, *tile_part;                          // unit partial rows, weight-tile partials
+  uint32_t *keys, *counters, *tile_cnt;                 // counters[0]: row contributions
+  uint32_t row_units_max;
+  int row_w;                                            // partial row width max(H, 64)
+};
+
+// ---- policy items (src/az/fused_policy.rs:10-35) -----------------------------
+struct Item {
+  bool policy, move, capture;
+  uint32_t mv, from, to, cap;
+};
+__device__ __forceinline__ Item decode(int64_t packed_s) {
+  const uint64_t p = (uint64_t)packed_s;
+  Item it;
+  it.policy = (p >> 47) & 1u;
+  it.move = (p >> 45) & 1u;
+  it.capture = (p >> 46) & 1u;
+  it.mv = (uint32_t)(p & 0xfffu);
+  it.from = (uint32_t)((p >> 12) & 0x7ffu);
+  it.to = (uint32_t)((p >> 23) & 0x7ffu);
+  it.cap = (uint32_t)((p >> 34) & 0x7ffu);
+  return it;
+}
+__device__ __forceinline__ bool in_range(const Item& it) {
+  return it.mv < (uint32_t)kMoves &&
+         (!it.move || (it.from < (uint32_t)kInput && it.to < (uint32_t)kInput &&
+                       (!it.capture || it.cap < (uint32_t)kInput)));
+}
+
+// Trunk feature item -> its six rows (fused_feature_pool.rs:389-403); 0 for
+// padding, -1 when a row falls outside the table.
+__device__ __forceinline__ int pool_rows(uint32_t packed, uint32_t rows[6]) {
+  if (packed == kPad) return 0;
+  const uint32_t feature = packed & 0x7ffu, us = (packed >> 11) & 0xfu, them = (packed >> 15) & 0xfu;
+  const uint32_t piece = feature / 90u, square = feature - piece * 90u;
+  rows[0] = feature;
+  rows[1] = 1260u + piece;
+  rows[2] = 1274u + square / 9u;
+  rows[3] = 1284u + square % 9u;
+  rows[4] = 1293u + us * 14u + piece;
+  rows[5] = 1293u + (9u + them) * 14u + piece;
+  bool ok = true;
+#pragma unroll
+  for (int r = 0; r < 6; ++r) ok &= rows[r] < (uint32_t)kTrunkRows;
+  return ok ? 6 : -1;
+}
+
+// ---- warp helpers ----------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(kFull, v, o));
+  return v;
+}
+// v[o] holds each lane's partial of output o (o < 32); afterwards v[0] of
+// lane l is the sum over lanes of output l (31 shuffles for 32 outputs).
+__device__ __forceinline__ void reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool up = lane & off;
+#pragma unroll
+    for (int i = 0; i < off; ++i) {
+      const float send = up ? v[i] : v[i + off];
+      const float keep = up ? v[i + off] : v[i];
+      v[i] = keep + __shfl_xor_sync(kFull, send, off);
+    }
+  }
+}
+
+// A lane's columns of an H = 32 * NC row: chunks of V consecutive columns,
+// chunk q at V * lane + 32 * V * q (16-byte loads when NC % 4 == 0).
+template <int NC>
+struct Lay {
+  static constexpr int V = NC % 4 == 0 ? 4 : (NC % 2 == 0 ? 2 : 1);
+  static constexpr int Q = NC / V;
+  static __device__ __forceinline__ int col(int lane, int q) { return V * lane + 32 * V * q; }
+};
+template <int NC>
+__device__ __forceinline__ void ld_row(const float* __restrict__ row, int lane, float (&x)[NC]) {
+  using L = Lay<NC>;
+#pragma unroll
+  for (int q = 0; q < L::Q; ++q) {
+    const float* p = row + L::col(lane, q);
+    if constexpr (L::V == 4) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(p));
+      x[4 * q] = t.x, x[4 * q + 1] = t.y, x[4 * q + 2] = t.z, x[4 * q + 3] = t.w;
+    } else if constexpr (L::V == 2) {
+      const float2 t = __ldg(reinterpret_cast<const float2*>(p));
+      x[2 * q] = t.x, x[2 * q + 1] = t.y;
+    } else {
+      x[q] = __ldg(p);
+    }
+  }
+}
+// The same for rows written earlier in this kernel's grid or by this step
+// (plain loads, no read-only path).
+template <int NC>
+__device__ __forceinline__ void ld_row_rw(const float* row, int lane, float (&x)[NC]) {
+  using L = Lay<NC>;
+#pragma unroll
+  for (int q = 0; q < L::Q; ++q) {
+    const float* p = row + L::col(lane, q);
+    if constexpr (L::V == 4) {
+      const float4 t = *reinterpret_cast<const float4*>(p);
+      x[4 * q] = t.x, x[4 * q + 1] = t.y, x[4 * q + 2] = t.z, x[4 * q + 3] = t.w;
+    } else if constexpr (L::V == 2) {
+      const float2 t = *reinterpret_cast<const float2*>(p);
+      x[2 * q] = t.x, x[2 * q + 1] = t.y;
+    } else {
+      x[q] = *p;
+    }
+  }
+}
+template <int NC>
+__device__ __forceinline__ void st_row(float* row, int lane, const float (&x)[NC]) {
+  using L = Lay<NC>;
+#pragma unroll
+  for (int q = 0; q < L::Q; ++q) {
+    float* p = row + L::col(lane, q);
+    if constexpr (L::V == 4) {
+      *reinterpret_cast<float4*>(p) = make_float4(x[4 * q], x[4 * q + 1], x[4 * q + 2], x[4 * q + 3]);
+    } else if constexpr (L::V == 2) {
+      *reinterpret_cast<float2*>(p) = make_float2(x[2 * q], x[2 * q + 1]);
+    } else {
+      *p = x[q];
+    }
+  }
+}
+// This lane's partial of dot(W row, x).
+template <int NC>
+__device__ __forceinline__ float dot_row(const float* __restrict__ wrow, int lane, const float (&x)[NC]) {
+  float w[NC];
+  ld_row<NC>(wrow, lane, w);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) s = fmaf(w[i], x[i], s);
+  return s;
+}
+// x += a * W row.
+template <int NC>
+__device__ __forceinline__ void axpy_row(const float* __restrict__ wrow, int lane, float a, float (&x)[NC]) {
+  float w[NC];
+  ld_row<NC>(wrow, lane, w);
+#pragma unroll
+  for (int i = 0; i < NC; ++i) x[i] = fmaf(a, w[i], x[i]);
+}
+// Outputs o < n_out (<= 32) of W[n_out][H] . x; lane l gets output l (0 for
+// l >= n_out).
+template <int NC>
+__device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, int n_out, const float (&x)[NC],
+                                          int lane) {
+  float v[32];
+#pragma unroll
+  for (int o = 0; o < 32; ++o) v[o] = o < n_out ? dot_row<NC>(W + (size_t)o * H, lane, x) : 0.f;
+  reduce_scatter32(v, lane);
+  return v[0];
+}
+
+// ---- keys of every table contribution (side stream) -----------------------------
+// One thread per feature item, threat index or policy move.  A contribution
+// that cannot change a table gradient gets kKeyDrop: padding items and
+// threats, moves without the policy bit (torch.where passes them no
+// gradient), feature rows of moves without the move bit or of an absent
+// capture, and the sparse / tactical lookups of padded moves (no policy bit,
+// masked, zero target: their softmax probability underflows to exactly 0,
+// so their logit gradient is exactly 0).  Indices outside their tables set
+// CNNUE_STATUS_BAD_INDEX and are dropped.  counters[0] gets the number of
+// row-problem contributions kept (the sorted position where scalar keys
+// begin).
+__global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_t* __restrict__ keys,
+                                                     uint32_t* __restrict__ counters, uint32_t* __restrict__ status) {
+  const int64_t nf = bt.B * bt.F, nt = bt.B * bt.T, nm = bt.B * bt.M;
+  const int64_t total = nf + nt + nm;
+  uint32_t rows_kept = 0, bad = 0;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    if (t < nf) {
+      uint32_t rows[6];
+      const int r = pool_rows(bt.fi[t], rows);
+      bad |= r < 0;
+      uint32_t* k = keys + cb.pool + t * 6;
+#pragma unroll
+      for (int s = 0; s < 6; ++s) k[s] = r > 0 ? kKeyPool + rows[s] : kKeyDrop;
+      rows_kept += r > 0 ? 6 : 0;
+    } else if (t < nf + nt) {
+      const int64_t u = t - nf;
+      const uint32_t idx = bt.ti[u];
+      const bool ok = idx < (uint32_t)kVocab;
+      bad |= !ok && idx != kPad;
+      keys[cb.threat + u] = ok ? kKeyThreat + idx : kKeyDrop;
+      rows_kept += ok;
+    } else {
+      const int64_t u = t - nf - nt;
+      const Item it = decode(bt.pi[u]);
+      const bool ok = in_range(it);
+      bad |= it.policy && !ok;
+      const bool live = it.policy && ok;
+      keys[cb.move + u] = live ? kKeyMove + it.mv : kKeyDrop;
+      const bool feat = live && it.move;
+      uint32_t* fk = keys + cb.feat + u * 3;
+      fk[0] = feat ? kKeyFeat + it.to : kKeyDrop;
+      fk[1] = feat ? kKeyFeat + it.from : kKeyDrop;
+      fk[2] = feat && it.capture ? kKeyFeat + it.cap : kKeyDrop;
+      rows_kept += live + (feat ? 2 + it.capture : 0);
+      const bool drop = !it.policy && bt.mask[u] <= kMaskDrop && bt.tgt[u] == 0.f;
+#pragma unroll
+      for (int j = 0; j < 7; ++j) {
+        const int64_t s = bt.sp[u * 7 + j];
+        const bool sok = s >= 0 && s < kSparseLen;
+        bad |= !sok;
+        keys[cb.sparse + u * 7 + j] = sok && !drop ? kKeySparse + (uint32_t)s : kKeyDrop;
+      }
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int64_t s = bt.tc[u * 2 + j];
+        const bool sok = s >= 0 && s < kTactLen;
+        bad |= !sok;
+        keys[cb.tact + u * 2 + j] = sok && !drop ? kKeyTact + (uint32_t)s : kKeyDrop;
+      }
+    }
+  }
+  // block total of the kept row contributions (a count: order-free)
+  __shared__ uint32_t part[8];
+  uint32_t v = rows_kept;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
+  if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t s = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += part[w];
+    if (s) atomicAdd(counters, s);
+  }
+}
+
+// ---- forward -------------------------------------------------------------------------
+// Blocks [0, trunk_blocks): one warp per board -
+//   board_pre = feature pool (six rows per item) + hidden bias,
+//   sparse_hidden = relu(board_pre + rule_context . R), hidden = RMS-normed,
+//   accumulator context = W_acc . board_pre, value head = relu(W_v . hidden +
+//   b_v), threat accumulator (64) over the board's threat rows, pair = [act,
+//   act^2] with act = clamp(threat, 0, 1), value logits = W_o . value head +
+//   W_to . pair, move context = W_pc . hidden + W_ptc . pair;
+// blocks after them: one warp per input row r < 1260 - the accumulator
+// features af[r] = W_acc . trunk_table[r] (32 values).
+constexpr int kWarps = 8;  // warps per block of every per-board kernel
+
+template <int NC>
+__global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Act A, int trunk_blocks,
+                                                          uint32_t* __restrict__ status) {
+  constexpr int H = 32 * NC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if ((int)blockIdx.x >= trunk_blocks) {
+    const int r = ((int)blockIdx.x - trunk_blocks) * kWarps + warp;
+    if (r >= kInput) return;
+    float x[NC];
+    ld_row<NC>(P.p[L_FT] + (size_t)r * H, lane, x);
+    A.af[(size_t)r * kAcc + lane] = matvec32<NC>(P.p[L_PAH], H, kAcc, x, lane);
+    return;
+  }
+  const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
+  if (b >= bt.B) return;
+  // feature pool: items fetched 32 at a time, one per lane, then broadcast
+  float acc[NC];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) acc[i] = 0.f;
+  bool bad = false;
+  for (int64_t i0 = 0; i0 < bt.F; i0 += 32) {
+    const uint32_t mine = i0 + lane < bt.F ? bt.fi[b * bt.F + i0 + lane] : kPad;
+    const int cnt = (int)(bt.F - i0 < 32 ? bt.F - i0 : 32);
+    for (int j = 0; j < cnt; ++j) {
+      const uint32_t item = __shfl_sync(kFull, mine, j);
+      uint32_t rows[6];
+      const int r = pool_rows(item, rows);
+      if (r <= 0) {
+        bad |= r < 0;
+        continue;
+      }
+      float x[6][NC];
+#pragma unroll
+      for (int s = 0; s < 6; ++s) ld_row<NC>(P.p[L_FT] + (size_t)rows[s] * H, lane, x[s]);
+#pragma unroll
+      for (int s = 0; s < 6; ++s)
+#pragma unroll
+        for (int c = 0; c < NC; ++c) acc[c] += x[s][c];
+    }
+  }
+  float bias[NC], bp[NC], h[NC];
+  ld_row<NC>(P.p[L_HB], lane, bias);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) bp[c] = acc[c] + bias[c];
+  // rule context, relu, RMS norm
+  float pre[NC];
+#pragma unroll
+  for (int c = 0; c < NC; ++c) pre[c] = 0.f;
+#pragma unroll
+  for (int k = 0; k < kRule; ++k) axpy_row<NC>(P.p[L_RULE] + (size_t)k * H, lane, __ldg(bt.rule + b * kRule + k), pre);
+  float ss = 0.f;
+#pragma unroll
+  for (int c = 0; c < NC; ++c) {
+    h[c] = fmaxf(bp[c] + pre[c], 0.f);
+    ss = fmaf(h[c], h[c], ss);
+  }
+  const float rms = sqrtf(warp_sum(ss) / (float)H + 1.0e-6f);
+#pragma unroll
+  for (int c = 0; c < NC; ++c) h[c] = h[c] / rms;
+  // accumulator context and value head
+  const float acc_ctx = matvec32<NC>(P.p[L_PAH], H, kAcc, bp, lane);
+  float vh[3];
+#pragma unroll
+  for (int g = 0; g < 3; ++g)
+    vh[g] = fmaxf(matvec32<NC>(P.p[L_VHH] + (size_t)32 * g * H, H, 32, h, lane) + __ldg(P.p[L_VHB] + 32 * g + lane),
+                  0.f);
+  // threat accumulator: lane owns columns 2 lane, 2 lane + 1
+  float t0 = 0.f, t1 = 0.f;
+  for (int64_t i0 = 0; i0 < bt.T; i0 += 32) {
+    const uint32_t mine = i0 + lane < bt.T ? bt.ti[b * bt.T + i0 + lane] : kPad;
+    const int cnt = (int)(bt.T - i0 < 32 ? bt.T - i0 : 32);
+    for (int j = 0; j < cnt; ++j) {
+      const uint32_t idx = __shfl_sync(kFull, mine, j);
+      if (idx >= (uint32_t)kVocab) {
+        bad |= idx != kPad;
+        continue;
+      }
+      const float2 v = __ldg(reinterpret_cast<const float2*>(P.p[L_TE] + (size_t)idx * kTR) + lane);
+      t0 += v.x;
+      t1 += v.y;
+    }
+  }
+  const float a0 = fminf(fmaxf(t0, 0.f), 1.f), a1 = fminf(fmaxf(t1, 0.f), 1.f);
+  const float pr[4] = {a0, a1, a0 * a0, a1 * a1};  // pair columns 2l, 2l+1, 64+2l, 65+2l
+  const int pc[4] = {2 * lane, 2 * lane + 1, kTR + 2 * lane, kTR + 2 * lane + 1};
+  // value logits
+  float vl[3];
+#pragma unroll
+  for (int k = 0; k < 3; ++k) {
+    float s = 0.f;
+#pragma unroll
+    for (int g = 0; g < 3; ++g) s = fmaf(vh[g], __ldg(P.p[L_VHO] + k * kVH + 32 * g + lane), s);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) s = fmaf(pr[q], __ldg(P.p[L_VTO] + k * kPair + pc[q]), s);
+    vl[k] = warp_sum(s);
+  }
+  // move context (16): hidden and pair terms in one reduce-scatter
+  float v[32];
+#pragma unroll
+  for (int o = 0; o < 32; ++o) {
+    float s = 0.f;
+    if (o < 16) {
+      s = dot_row<NC>(P.p[L_PCH] + (size_t)o * H, lane, h);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) s = fmaf(pr[q], __ldg(P.p[L_PTC] + o * kPair + pc[q]), s);
+    }
+    v[o] = s;
+  }
+  reduce_scatter32(v, lane);
+  // saved for the loss and the backward
+  st_row<NC>(A.bp + b * H, lane, bp);
+  st_row<NC>(A.hid + b * H, lane, h);
+  if (lane == 0) A.rms[b] = rms;
+#pragma unroll
+  for (int g = 0; g < 3; ++g) A.vh[b * kVH + 32 * g + lane] = vh[g];
+  reinterpret_cast<float2*>(A.ta + b * kTR)[lane] = make_float2(t0, t1);
+  if (lane < 16) A.ctx[b * kCtx + lane] = v[0];
+  A.ctx[b * kCtx + 16 + lane] = acc_ctx;
+  if (lane < 3) A.vl[b * 4 + lane] = lane == 0 ? vl[0] : (lane == 1 ? vl[1] : vl[2]);
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+}
+
+// ---- policy logits, losses, logit gradients ------------------------------------------
+// One warp per board, lane l taking moves l, l + 32, ...  A move's logit is
+// (policy bit set) bias[mv] + move_bit * (consequence . (psp[to] - psp[from]
+// - capture * psp[cap]) + ctx16 . move_context[mv] + (ctx32 + af[to] -
+// af[from] - capture * af[cap]) . accumulator_move[mv]), else 0, plus its 7
+// sparse and 2 tactical lookups (fused_policy.rs:178-241,
+// fused_sparse_policy.rs:8-34); psp = trunk_table[:, :32].  Then, per board
+// (compute_batch_loss): log-softmax of logits + mask, policy CE = -sum t *
+// log p, dlogit = pw_scale * w_b / B * (p * sum t - t); value log-softmax,
+// CE against the WDL target, value = p_win - p_loss, dvalue_logit likewise.
+// The board's move-context gradient (48) and its share of the consequence
+// weights' gradient (32) are summed over its moves here.
+__device__ __forceinline__ float4 ld4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+__device__ __forceinline__ float4 sub4(float4 a, float4 b) {
+  return make_float4(a.x - b.x, a.y - b.y, a.z - b.z, a.w - b.w);
+}
+
+struct LossScale {
+  float value, policy;  // max(weight, 0) / B
+};
+
+__global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt, Act A, int H, LossScale ls,
+                                                             uint32_t* __restrict__ status) {
+  extern __shared__ float smem[];
+  __shared__ float cons[kPsp];
+  __shared__ float sctx[kWarps][kCtx];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* z = smem + (size_t)warp * bt.M;  // logits, then probabilities
+  if (threadIdx.x < kPsp) cons[threadIdx.x] = __ldg(P.p[L_CONS] + threadIdx.x);
+  __syncthreads();
+  const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
+  if (b >= bt.B) return;
+  sctx[warp][lane] = A.ctx[b * kCtx + lane];
+  if (lane < kCtx - 32) sctx[warp][32 + lane] = A.ctx[b * kCtx + 32 + lane];
+  __syncwarp();
+  const float* c = sctx[warp];
+  const float* ft = P.p[L_FT];
+  bool bad = false;
+  float zmax = -INFINITY;
+  for (int64_t m = lane; m < bt.M; m += 32) {
+    const int64_t u = b * bt.M + m;
+    const Item it = decode(bt.pi[u]);
+    float v = 0.f;
+    if (it.policy) {
+      if (!in_range(it)) {
+        bad = true;
+      } else {
+        v = __ldg(P.p[L_MB] + it.mv);
+        if (it.move) {
+          const float* rt = ft + (size_t)it.to * H;
+          const float* rf = ft + (size_t)it.from * H;
+          const float* rc = ft + (size_t)it.cap * H;
+          float s = 0.f;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 d = sub4(ld4(rt + 4 * q), ld4(rf + 4 * q));
+            if (it.capture) d = sub4(d, ld4(rc + 4 * q));
+            s = fmaf(d.x, cons[4 * q], s);
+            s = fmaf(d.y, cons[4 * q + 1], s);
+            s = fmaf(d.z, cons[4 * q + 2], s);
+            s = fmaf(d.w, cons[4 * q + 3], s);
+          }
+          const float* mc = P.p[L_MC] + (size_t)it.mv * 16;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float4 w = ld4(mc + 4 * q);
+            s = fmaf(c[4 * q], w.x, s);
+            s = fmaf(c[4 * q + 1], w.y, s);
+            s = fmaf(c[4 * q + 2], w.z, s);
+            s = fmaf(c[4 * q + 3], w.w, s);
+          }
+          const float* at = A.af + (size_t)it.to * kAcc;
+          const float* af = A.af + (size_t)it.from * kAcc;
+          const float* ac = A.af + (size_t)it.cap * kAcc;
+          const float* am = P.p[L_AM] + (size_t)it.mv * kAcc;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            float4 x = sub4(*reinterpret_cast<const float4*>(at + 4 * q), *reinterpret_cast<const float4*>(af + 4 * q));
+            if (it.capture) x = sub4(x, *reinterpret_cast<const float4*>(ac + 4 * q));
+            const float4 w = ld4(am + 4 * q);
+            s = fmaf(c[16 + 4 * q] + x.x, w.x, s);
+            s = fmaf(c[17 + 4 * q] + x.y, w.y, s);
+            s = fmaf(c[18 + 4 * q] + x.z, w.z, s);
+            s = fmaf(c[19 + 4 * q] + x.w, w.w, s);
+          }
+          v += s;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 7; ++j) {
+      const int64_t s = bt.sp[u * 7 + j];
+      if (s >= 0 && s < kSparseLen) v += __ldg(P.p[L_SPARSE] + s);
+      else bad = true;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int64_t s = bt.tc[u * 2 + j];
+      if (s >= 0 && s < kTactLen) v += __ldg(P.p[L_TACT] + s);
+      else bad = true;
+    }
+    const float zz = v + bt.mask[u];
+    z[m] = zz;
+    zmax = fmaxf(zmax, zz);
+  }
+  zmax = warp_max(zmax);
+  float se = 0.f;
+  for (int64_t m = lane; m < bt.M; m += 32) se += expf(z[m] - zmax);
+  const float lse = zmax + logf(warp_sum(se));
+  float ce = 0.f, tsum = 0.f;
+  for (int64_t m = lane; m < bt.M; m += 32) {
+    const float lp = z[m] - lse, t = bt.tgt[b * bt.M + m];
+    ce -= t * lp;
+    tsum += t;
+    z[m] = expf(lp);
+  }
+  ce = warp_sum(ce);
+  tsum = warp_sum(tsum);
+  const float scale_p = ls.policy * __ldg(bt.pw + b);
+  // logit gradients and the board's move-context / consequence sums
+  float g16[32], g32[32], gc[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) g16[j] = g32[j] = gc[j] = 0.f;
+  for (int64_t m = lane; m < bt.M; m += 32) {
+    const int64_t u = b * bt.M + m;
+    const float dl = scale_p * (z[m] * tsum - bt.tgt[u]);
+    A.dl[u] = dl;
+    const Item it = decode(bt.pi[u]);
+    if (!it.policy || !it.move || !in_range(it) || dl == 0.f) continue;
+    const float* mc = P.p[L_MC] + (size_t)it.mv * 16;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 w = ld4(mc + 4 * q);
+      g16[4 * q] = fmaf(dl, w.x, g16[4 * q]);
+      g16[4 * q + 1] = fmaf(dl, w.y, g16[4 * q + 1]);
+      g16[4 * q + 2] = fmaf(dl, w.z, g16[4 * q + 2]);
+      g16[4 * q + 3] = fmaf(dl, w.w, g16[4 * q + 3]);
+    }
+    const float* am = P.p[L_AM] + (size_t)it.mv * kAcc;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 w = ld4(am + 4 * q);
+      g32[4 * q] = fmaf(dl, w.x, g32[4 * q]);
+      g32[4 * q + 1] = fmaf(dl, w.y, g32[4 * q + 1]);
+      g32[4 * q + 2] = fmaf(dl, w.z, g32[4 * q + 2]);
+      g32[4 * q + 3] = fmaf(dl, w.w, g32[4 * q + 3]);
+    }
+    const float* rt = ft + (size_t)it.to * H;
+    const float* rf = ft + (size_t)it.from * H;
+    const float* rc = ft + (size_t)it.cap * H;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 d = sub4(ld4(rt + 4 * q), ld4(rf + 4 * q));
+      if (it.capture) d = sub4(d, ld4(rc + 4 * q));
+      gc[4 * q] = fmaf(dl, d.x, gc[4 * q]);
+      gc[4 * q + 1] = fmaf(dl, d.y, gc[4 * q + 1]);
+      gc[4 * q + 2] = fmaf(dl, d.z, gc[4 * q + 2]);
+      gc[4 * q + 3] = fmaf(dl, d.w, gc[4 * q + 3]);
+    }
+  }
+  reduce_scatter32(g16, lane);
+  reduce_scatter32(g32, lane);
+  reduce_scatter32(gc, lane);
+  if (lane < 16) A.dctx[b * kCtx + lane] = g16[0];
+  A.dctx[b * kCtx + 16 + lane] = g32[0];
+  A.cons[b * kPsp + lane] = gc[0];
+  // value head loss (lane 0)
+  if (lane == 0) {
+    const float l0 = A.vl[b * 4], l1 = A.vl[b * 4 + 1], l2 = A.vl[b * 4 + 2];
+    const float mx = fmaxf(l0, fmaxf(l1, l2));
+    const float lse3 = mx + logf(expf(l0 - mx) + expf(l1 - mx) + expf(l2 - mx));
+    const float lp[3] = {l0 - lse3, l1 - lse3, l2 - lse3};
+    const float w0 = bt.wdl[b * 3], w1 = bt.wdl[b * 3 + 1], w2 = bt.wdl[b * 3 + 2];
+    const float vce = -(w0 * lp[0] + w1 * lp[1] + w2 * lp[2]);
+    const float p0 = expf(lp[0]), p1 = expf(lp[1]), p2 = expf(lp[2]);
+    const float wsum = w0 + w1 + w2;
+    const float sv = ls.value * __ldg(bt.vw + b);
+    A.dvl[b * 4] = sv * (p0 * wsum - w0);
+    A.dvl[b * 4 + 1] = sv * (p1 * wsum - w1);
+    A.dvl[b * 4 + 2] = sv * (p2 * wsum - w2);
+    A.dvl[b * 4 + 3] = 0.f;
+    float* r = A.rec + b * 8;
+    r[0] = vce * __ldg(bt.vw + b);
+    r[1] = ce * __ldg(bt.pw + b);
+    r[2] = vce;
+    r[3] = ce;
+    r[4] = p0 - p2;  // value = p . (1, 0, -1)
+  }
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+}
+
+// ---- trunk backward (one warp per board) -------------------------------------------
+// From dvalue_logits (3) and the move-context gradient (48):
+//   dvh = W_o^T dvl (where value head > 0), dpair = W_to^T dvl + W_ptc^T dctx16,
+//   dthreat = (dpair[:64] + 2 act dpair[64:]) where 0 <= threat <= 1,
+//   dhidden = W_v^T dvh + W_pc^T dctx16,
+//   dsparse = (dhidden - hidden * mean(dhidden * hidden)) / rms where > 0,
+//   dboard = dsparse + W_acc^T dctx32.
+template <int NC>
+__global__ void __launch_bounds__(32 * kWarps) bwd_kernel(Params P, Batch bt, Act A) {
+  constexpr int H = 32 * NC;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
+  if (b >= bt.B) return;
+  const float dv0 = A.dvl[b * 4], dv1 = A.dvl[b * 4 + 1], dv2 = A.dvl[b * 4 + 2];
+  const float c16 = lane < 16 ? A.dctx[b * kCtx + lane] : 0.f;
+  const float c32 = A.dctx[b * kCtx + 16 + lane];
+  // value head pre-activation gradient: lane owns outputs lane, 32 + lane, 64 + lane
+  float dvh[3];
+#pragma unroll
+  for (int g = 0; g < 3; ++g) {
+    const int o = 32 * g + lane;
+    const float t = dv0 * __ldg(P.p[L_VHO] + o) + dv1 * __ldg(P.p[L_VHO] + kVH + o) +
+                    dv2 * __ldg(P.p[L_VHO] + 2 * kVH + o);
+    dvh[g] = A.vh[b * kVH + o] > 0.f ? t : 0.f;
+    A.dvh[b * kVH + o] = dvh[g];
+  }
+  // threat: lane owns columns 2 lane, 2 lane + 1 of act (pair 2l, 2l+1, 64+2l, 65+2l)
+  const float2 ta = reinterpret_cast<const float2*>(A.ta + b * kTR)[lane];
+  const int pc[4] = {2 * lane, 2 * lane + 1, kTR + 2 * lane, kTR + 2 * lane + 1};
+  float dp[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    dp[q] = dv0 * __ldg(P.p[L_VTO] + pc[q]) + dv1 * __ldg(P.p[L_VTO] + kPair + pc[q]) +
+            dv2 * __ldg(P.p[L_VTO] + 2 * kPair + pc[q]);
+#pragma unroll
+  for (int o = 0; o < 16; ++o) {
+    const float co = __shfl_sync(kFull, c16, o);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) dp[q] = fmaf(co, __ldg(P.p[L_PTC] + o * kPair + pc[q]), dp[q]);
+  }
+  const float a0 = fminf(fmaxf(ta.x, 0.f), 1.f), a1 = fminf(fmaxf(ta.y, 0.f), 1.f);
+  const float d0 = dp[0] + 2.f * a0 * dp[2], d1 = dp[1] + 2.f * a1 * dp[3];
+  reinterpret_cast<float2*>(A.dta + b * kTR)[lane] =
+      make_float2(ta.x >= 0.f && ta.x <= 1.f ? d0 : 0.f, ta.y >= 0.f && ta.y <= 1.f ? d1 : 0.f);
+  // hidden
+  float dh[NC];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) dh[i] = 0.f;
+#pragma unroll
+  for (int g = 0; g < 3; ++g)
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j)
+      axpy_row<NC>(P.p[L_VHH] + (size_t)(32 * g + j) * H, lane, __shfl_sync(kFull, dvh[g], j), dh);
+#pragma unroll
+  for (int o = 0; o < 16; ++o) axpy_row<NC>(P.p[L_PCH] + (size_t)o * H, lane, __shfl_sync(kFull, c16, o), dh);
+  float h[NC];
+  ld_row_rw<NC>(A.hid + b * H, lane, h);
+  float dot = 0.f;
+#pragma unroll
+  for (int i = 0; i < NC; ++i) dot = fmaf(dh[i], h[i], dot);
+  const float mean = warp_sum(dot) / (float)H;
+  const float rms = A.rms[b];
+  float dpre[NC], dbp[NC];
+#pragma unroll
+  for (int i = 0; i < NC; ++i) {
+    dpre[i] = h[i] > 0.f ? (dh[i] - h[i] * mean) / rms : 0.f;
+    dbp[i] = dpre[i];
+  }
+#pragma unroll 8
+  for (int j = 0; j < kAcc; ++j) axpy_row<NC>(P.p[L_PAH] + (size_t)j * H, lane, __shfl_sync(kFull, c32, j), dbp);
+  st_row<NC>(A.dpre + b * H, lane, dpre);
+  st_row<NC>(A.dbp + b * H, lane, dbp);
+}
+
+// ---- table gradients: unit and run sums over the joint sort ---------------------------
+struct Sorted {
+  const uint32_t* keys;       // [n] sorted keys
+  const uint32_t* idx;        // [n] contribution of each sorted slot
+  const uint32_t* run_start;  // [n_runs]
+  const uint32_t* unit_off;   // [n_runs] first unit of each run
+  const uint32_t* n_runs_d;
+  const uint32_t* n_units_d;
+  const uint32_t* run_of;     // run index at each run's first slot
+  float* spart;               // scalar unit partials, by unit
+  uint32_t n;
+};
+
+// Last run r with unit_off[r] <= u (unit_off strictly increasing, unit_off[0]
+// = 0): a 32-way search, 32 probes per round, at most 7 rounds for 2^31 runs.
+__device__ __forceinline__ uint32_t warp_find_run(const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t u,
+                                                  int lane) {
+  uint32_t lo = 0, hi = n_runs - 1;
+  for (int round = 0; round < 8 && lo < hi; ++round) {
+    const uint32_t step = (hi - lo + 32) / 32;
+    const uint32_t r = lo + (uint32_t)lane * step;
+    const bool pred = r <= hi && unit_off[r] <= u;
+    const int k = __popc(__ballot_sync(kFull, pred)) - 1;  // >= 0: lane 0 probes lo
+    lo += (uint32_t)k * step;
+    hi = min(hi, lo + step - 1);
+  }
+  return lo;
+}
+
+__device__ __forceinline__ uint32_t run_units(const Sorted& s, uint32_t r, uint32_t n_runs, uint32_t n_units) {
+  return (r + 1 < n_runs ? s.unit_off[r + 1] : n_units) - s.unit_off[r];
+}
+
+// Row problems: width and destination of a key's row.
+enum Problem { PR_POOL, PR_THREAT, PR_MOVE, PR_FEAT };
+__device__ __forceinline__ Problem problem_of(uint32_t key) {
+  return key < kKeyThreat ? PR_POOL : key < kKeyMove ? PR_THREAT : key < kKeyFeat ? PR_MOVE : PR_FEAT;
+}
+__device__ __forceinline__ int row_width(Problem p, int H) {
+  return p == PR_POOL ? H : p == PR_MOVE ? kMoveW : kTR;  // threat and feature rows: 64
+}
+__device__ __forceinline__ float* row_dest(const Grads& G, const Act& A, Problem p, uint32_t key, int c, int H) {
+  switch (p) {
+    case PR_POOL:
+      return G.g[L_FT] + (size_t)(key - kKeyPool) * H + c;
+    case PR_THREAT:
+      return G.g[L_TE] + (size_t)(key - kKeyThreat) * kTR + c;
+    case PR_MOVE: {
+      const uint32_t mv = key - kKeyMove;
+      return c == 0 ? G.g[L_MB] + mv : c <= 16 ? G.g[L_MC] + (size_t)mv * 16 + (c - 1)
+                                                : G.g[L_AM] + (size_t)mv * kAcc + (c - 17);
+    }
+    default:
+      return A.pspaf + (size_t)(key - kKeyFeat) * kFeatW + c;
+  }
+}
+
+// Column c of the row that contribution e (of problem p) adds.
+__device__ __forceinline__ float row_value(const Params& P, const Act& A, const Batch& bt, const Bases& cb, Problem p,
+                                           uint32_t e, int c, int H) {
+  switch (p) {
+    case PR_POOL:
+      return A.dbp[(size_t)(e / (uint32_t)(6 * bt.F)) * H + c];
+    case PR_THREAT:
+      return A.dta[(size_t)((e - cb.threat) / (uint32_t)bt.T) * kTR + c];
+    case PR_MOVE: {
+      const uint32_t u = e - cb.move;
+      const float dl = A.dl[u];
+      if (c == 0) return dl;
+      const Item it = decode(bt.pi[u]);
+      if (!it.move) return 0.f;
+      const size_t b = u / (uint32_t)bt.M;
+      if (c <= 16) return dl * A.ctx[b * kCtx + (c - 1)];
+      const int j = c - 17;
+      float x = A.ctx[b * kCtx + 16 + j] + A.af[(size_t)it.to * kAcc + j] - A.af[(size_t)it.from * kAcc + j];
+      if (it.capture) x -= A.af[(size_t)it.cap * kAcc + j];
+      return dl * x;
+    }
+    default: {
+      const uint32_t v = e - cb.feat, u = v / 3u, role = v - 3u * u;
+      const float dl = role == 0 ? A.dl[u] : -A.dl[u];
+      if (c < kPsp) return dl * __ldg(P.p[L_CONS] + c);
+      const Item it = decode(bt.pi[u]);
+      return dl * __ldg(P.p[L_AM] + (size_t)it.mv * kAcc + (c - kPsp));
+    }
+  }
+}
+
+// One warp per row unit (lanes over columns c = lane + 32 k), then one lane
+// per scalar unit (32 consecutive units per warp).  A unit that is its run's
+// only one writes the gradient row directly; the others leave partials.
+template <int NC>
+__global__ void __launch_bounds__(256) unit_kernel(Params P, Grads G, Act A, Batch bt, Bases cb, Sorted s, int H,
+                                                   uint32_t* __restrict__ status) {
+  constexpr int KW = NC > 2 ? NC : 2;  // column chunks: max(H, 64) / 32
+  const int lane = threadIdx.x & 31;
+  const uint32_t n_runs = *s.n_runs_d, n_units = *s.n_units_d, P0 = A.counters[0];
+  if (n_runs == 0) return;
+  const uint32_t u_rows = P0 < s.n ? s.unit_off[s.run_of[P0]] : n_units;
+  const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
+  for (uint32_t u = gw; u < u_rows; u += n_warps) {
+    if (u >= A.row_units_max) {
+      if (lane == 0) atomicOr(status, CNNUE_STATUS_INTERNAL);
+      break;
+    }
+    const uint32_t r = warp_find_run(s.unit_off, n_runs, u, lane);
+    const uint32_t rbeg = s.run_start[r], rend = r + 1 < n_runs ? s.run_start[r + 1] : s.n;
+    const uint32_t beg = rbeg + (u - s.unit_off[r]) * kUnit, end = min(rend, beg + kUnit);
+    const uint32_t key = s.keys[rbeg];
+    const bool single = run_units(s, r, n_runs, n_units) == 1;
+    const Problem p = problem_of(key);
+    const int W = row_width(p, H);
+    const int len = (int)(end - beg);
+    const uint32_t e_lo = lane < len ? s.idx[beg + lane] : 0u;
+    const uint32_t e_hi = 32 + lane < len ? s.idx[beg + 32 + lane] : 0u;
+    float acc[KW];
+#pragma unroll
+    for (int k = 0; k < KW; ++k) acc[k] = 0.f;
+    if (p == PR_POOL) {
+      // the bulk: dboard rows, four contributions' loads in flight
+      for (int j = 0; j < len; j += 4) {
+        float x[4][NC];
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int jj = j + t;
+          const uint32_t e = __shfl_sync(kFull, jj < 32 ? e_lo : e_hi, jj & 31);
+#pragma unroll
+          for (int k = 0; k < NC; ++k)
+            x[t][k] = jj < len ? A.dbp[(size_t)(e / (uint32_t)(6 * bt.F)) * H + lane + 32 * k] : 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int k = 0; k < NC; ++k) acc[k] += x[t][k];
+      }
+    } else {
+      for (int j = 0; j < len; ++j) {
+        const uint32_t e = __shfl_sync(kFull, j < 32 ? e_lo : e_hi, j & 31);
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+          const int c = lane + 32 * k;
+          if (c < W) acc[k] += row_value(P, A, bt, cb, p, e, c, H);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      const int c = lane + 32 * k;
+      if (c >= W) continue;
+      if (single) *row_dest(G, A, p, key, c, H) = acc[k];
+      else A.row_part[(size_t)u * A.row_w + c] = acc[k];
+    }
+  }
+  for (uint32_t u0 = u_rows + gw * 32; u0 < n_units; u0 += n_warps * 32) {
+    const uint32_t r0 = warp_find_run(s.unit_off, n_runs, u0, lane);
+    const uint32_t x = r0 + 1 + lane < n_runs ? s.unit_off[r0 + 1 + lane] : 0xffffffffu;
+    const uint32_t u = u0 + lane;
+    uint32_t d = 0;
+#pragma unroll 8
+    for (int j = 0; j < 32; ++j) d += __shfl_sync(kFull, x, j) <= u;
+    if (u >= n_units) continue;
+    const uint32_t r = r0 + d;
+    const uint32_t rbeg = s.run_start[r], rend = r + 1 < n_runs ? s.run_start[r + 1] : s.n;
+    const uint32_t key = s.keys[rbeg];
+    if (key >= kKeyDrop) continue;
+    const uint32_t beg = rbeg + (u - s.unit_off[r]) * kUnit, end = min(rend, beg + kUnit);
+    const bool tact = key >= kKeyTact;
+    const uint32_t base = tact ? cb.tact : cb.sparse, div = tact ? 2u : 7u;
+    float sum = 0.f;
+    uint32_t j = beg;
+    for (; j + 4 <= end; j += 4) {
+      float v[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) v[t] = A.dl[(s.idx[j + t] - base) / div];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) sum += v[t];
+    }
+    for (; j < end; ++j) sum += A.dl[(s.idx[j] - base) / div];
+    if (run_units(s, r, n_runs, n_units) == 1) {
+      if (tact) G.g[L_TACT][key - kKeyTact] = sum;
+      else G.g[L_SPARSE][key - kKeySparse] = sum;
+    } else {
+      s.spart[u] = sum;
+    }
+  }
+}
+
+// Runs of several units add their unit partials in unit order: row runs one
+// warp each (lanes over columns), scalar runs one warp each (lanes over
+// units, then a fixed butterfly).  32 runs are screened per warp step.
+template <int NC>
+__global__ void __launch_bounds__(256) run_kernel(Grads G, Act A, Sorted s, int H) {
+  constexpr int KW = NC > 2 ? NC : 2;
+  const int lane = threadIdx.x & 31;
+  const uint32_t n_runs = *s.n_runs_d, n_units = *s.n_units_d, P0 = A.counters[0];
+  if (n_runs == 0) return;
+  const uint32_t r_rows = P0 < s.n ? s.run_of[P0] : n_runs;
+  const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
+  for (uint32_t r0 = gw * 32; r0 < r_rows; r0 += n_warps * 32) {
+    const uint32_t r = r0 + lane;
+    uint32_t pending = __ballot_sync(kFull, r < r_rows && run_units(s, r, n_runs, n_units) > 1);
+    while (pending) {
+      const uint32_t rr = r0 + (uint32_t)(__ffs(pending) - 1);
+      pending &= pending - 1;
+      const uint32_t u0 = s.unit_off[rr], u1 = rr + 1 < n_runs ? s.unit_off[rr + 1] : n_units;
+      const uint32_t key = s.keys[s.run_start[rr]];
+      const Problem p = problem_of(key);
+      const int W = row_width(p, H);
+      if (u1 > A.row_units_max) continue;  // flagged by unit_kernel
+#pragma unroll
+      for (int k = 0; k < KW; ++k) {
+        const int c = lane + 32 * k;
+        if (c >= W) continue;
+        float sum = A.row_part[(size_t)u0 * A.row_w + c];
+        for (uint32_t u = u0 + 1; u < u1; ++u) sum += A.row_part[(size_t)u * A.row_w + c];
+        *row_dest(G, A, p, key, c, H) = sum;
+      }
+    }
+  }
+  for (uint32_t r0 = r_rows + gw * 32; r0 < n_runs; r0 += n_warps * 32) {
+    const uint32_t r = r0 + lane;
+    bool multi = r < n_runs && run_units(s, r, n_runs, n_units) > 1;
+    if (multi) multi = s.keys[s.run_start[r]] < kKeyDrop;
+    uint32_t pending = __ballot_sync(kFull, multi);
+    while (pending) {
+      const uint32_t rr = r0 + (uint32_t)(__ffs(pending) - 1);
+      pending &= pending - 1;
+      const uint32_t u0 = s.unit_off[rr], u1 = rr + 1 < n_runs ? s.unit_off[rr + 1] : n_units;
+      const uint32_t key = s.keys[s.run_start[rr]];
+      float sum = 0.f;
+      for (uint32_t u = u0 + lane; u < u1; u += 32) sum += s.spart[u];
+      sum = warp_sum(sum);
+      if (lane == 0) {
+        if (key >= kKeyTact) G.g[L_TACT][key - kKeyTact] = sum;
+        else G.g[L_SPARSE][key - kKeySparse] = sum;
+      }
+    }
+  }
+}
+
+// ---- dense weight gradients, feature-row gradient, metrics ----------------------------
+// A reduction problem: out[o][c] = sum over k of A(k, o) X(k, c), k over the
+// boards, then (optionally) over K2 further rows of a second pair.  Tiles of
+// 16 x 64 outputs, the k range split kSplits ways; the split partials are
+// added in split order by whichever block of the tile finishes last.
+constexpr int kTO = 16, kTC = 64, kTK = 32, kSplits = 8, kMaxProb = 12;
+
+struct RedProb {
+  const float* a;  // A(k, o) = a[k * lda + o]; nullptr: A = 1
+  int lda, O;
+  const float* x;  // X(k, c) = x[k * ldx + c]; xpair: x is the threat accumulator, X = pair columns
+  int ldx, C, xpair;
+  const float* a2;  // rows k >= K of the second pair
+  int lda2;
+  const float* x2;
+  int ldx2, K2;
+  float* out;
+  int tiles_c, tile0;
+};
+struct RedTable {
+  RedProb p[kMaxProb];
+  int n_prob, n_tiles, K;
+};
+
+__device__ __forceinline__ float pair_of(const float* ta, int c) {
+  const float a = fminf(fmaxf(ta[c & (kTR - 1)], 0.f), 1.f);
+  return c < kTR ? a : a * a;
+}
+
+__device__ void tile_block(const RedTable& T, Act& A, int tile, int split) {
+  __shared__ float As[kTK][kTO];
+  __shared__ float Xs[kTK][kTC];
+  __shared__ bool last;
+  int pi = 0;
+  while (pi + 1 < T.n_prob && T.p[pi + 1].tile0 <= tile) ++pi;
+  const RedProb& q = T.p[pi];
+  const int t = tile - q.tile0, o0 = (t / q.tiles_c) * kTO, c0 = (t % q.tiles_c) * kTC;
+  const int K = T.K + q.K2;
+  const int chunk = (K + kSplits * kTK - 1) / (kSplits * kTK) * kTK;
+  const int k_beg = split * chunk, k_end = min(K, k_beg + chunk);
+  const int tid = threadIdx.x, to = tid / 16, tc = (tid % 16) * 4;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = k_beg; k0 < k_end; k0 += kTK) {
+    for (int i = tid; i < kTK * kTO; i += 256) {
+      const int kk = i / kTO, oo = i % kTO, k = k0 + kk, o = o0 + oo;
+      float v = 0.f;
+      if (k < k_end && o < q.O) {
+        if (k < T.K) v = q.a ? q.a[(size_t)k * q.lda + o] : 1.f;
+        else v = q.a2[(size_t)(k - T.K) * q.lda2 + o];
+      }
+      As[kk][oo] = v;
+    }
+    for (int i = tid; i < kTK * kTC; i += 256) {
+      const int kk = i / kTC, cc = i % kTC, k = k0 + kk, c = c0 + cc;
+      float v = 0.f;
+      if (k < k_end && c < q.C) {
+        if (k < T.K) v = q.xpair ? pair_of(q.x + (size_t)k * kTR, c) : q.x[(size_t)k * q.ldx + c];
+        else v = q.x2[(size_t)(k - T.K) * q.ldx2 + c];
+      }
+      Xs[kk][cc] = v;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kTK; ++kk) {
+      const float a = As[kk][to];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) acc[v] = fmaf(a, Xs[kk][tc + v], acc[v]);
+    }
+    __syncthreads();
+  }
+  float* part = A.tile_part + ((size_t)tile * kSplits + split) * (kTO * kTC) + tid * 4;
+  *reinterpret_cast<float4*>(part) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(A.tile_cnt + tile, 1u) == kSplits - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int sp = 0; sp < kSplits; ++sp) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(A.tile_part + ((size_t)tile * kSplits + sp) * (kTO * kTC) +
+                                                           tid * 4));
+    sum[0] += v.x, sum[1] += v.y, sum[2] += v.z, sum[3] += v.w;
+  }
+  const int o = o0 + to;
+#pragma unroll
+  for (int v = 0; v < 4; ++v) {
+    const int c = c0 + tc + v;
+    if (o < q.O && c < q.C) q.out[(size_t)o * q.C + c] = sum[v];
+  }
+  if (tid == 0) A.tile_cnt[tile] = 0;  // ready for the next step
+}
+
+// The 30 metrics of compute_batch_loss (train_gpu_candle.rs:271-300) and the
+// status word, summed over the boards in a fixed order.
+__device__ void metrics_block(const Batch& bt, const Act& A, LossScale raw, const uint32_t* status, float* out) {
+  constexpr int kN = 2 + 2 + 6 + 21;  // weighted CEs, CEs, per-sample sums, phase
+  __shared__ float red[256][kN + 1];
+  float s[kN];
+#pragma unroll
+  for (int i = 0; i < kN; ++i) s[i] = 0.f;
+  for (int64_t b = threadIdx.x; b < bt.B; b += 256) {
+    const float* r = A.rec + b * 8;
+    const float v = r[4], t = bt.values[b], err = v - t;
+    const float per[6] = {v, v * v, t, t * t, v * t, err * err};
+    s[0] += r[0], s[1] += r[1], s[2] += r[2], s[3] += r[3];
+#pragma unroll
+    for (int k = 0; k < 6; ++k) s[4 + k] += per[k];
+#pragma unroll
+    for (int ph = 0; ph < 3; ++ph) {
+      const float m = bt.phase[b * 3 + ph];
+      s[10 + ph * 7] += m;
+#pragma unroll
+      for (int k = 0; k < 6; ++k) s[10 + ph * 7 + 1 + k] += m * per[k];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kN; ++i) red[threadIdx.x][i] = s[i];
+  __syncthreads();
+  for (int w = 128; w >= 1; w >>= 1) {
+    if ((int)threadIdx.x < w)
+      for (int i = 0; i < kN; ++i) red[threadIdx.x][i] += red[threadIdx.x + w][i];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    const float* t = red[0];
+    out[0] = t[0] * raw.value + t[1] * raw.policy;  // loss sum (not divided by the batch)
+    out[1] = t[2];
+    out[2] = t[3];
+    for (int k = 0; k < 6; ++k) out[3 + k] = t[4 + k];
+    for (int k = 0; k < 21; ++k) out[9 + k] = t[10 + k];
+    out[30] = (float)*(volatile const uint32_t*)status;
+  }
+}
+
+// Blocks [0, n_tiles * kSplits): weight-gradient tiles; then the feature-row
+// gradient grad_trunk[r][c] += dpsp[r][c] (c < 32) + sum_j daf[r][j] W_acc[j][c]
+// for r < 1260 (one thread per element); the last block: metrics.
+__global__ void __launch_bounds__(256) final_kernel(RedTable T, Params P, Grads G, Act A, Batch bt, int H,
+                                                    LossScale raw, const uint32_t* status, float* metrics) {
+  const int tile_blocks = T.n_tiles * kSplits;
+  const int64_t feat_elems = (int64_t)kInput * H;
+  const int feat_blocks = (int)((feat_elems + 255) / 256);
+  if ((int)blockIdx.x < tile_blocks) {
+    tile_block(T, A, blockIdx.x / kSplits, blockIdx.x % kSplits);
+    return;
+  }
+  const int fb = (int)blockIdx.x - tile_blocks;
+  if (fb < feat_blocks) {
+    const int64_t i = (int64_t)fb * 256 + threadIdx.x;
+    if (i >= feat_elems) return;
+    const int r = (int)(i / H), c = (int)(i % H);
+    const float* d = A.pspaf + (size_t)r * kFeatW;
+    float v = c < kPsp ? d[c] : 0.f;
+#pragma unroll 8
+    for (int j = 0; j < kAcc; ++j) v = fmaf(d[kPsp + j], __ldg(P.p[L_PAH] + (size_t)j * H + c), v);
+    G.g[L_FT][i] += v;
+    return;
+  }
+  metrics_block(bt, A, raw, status, metrics);
+}
+
+// ---- host -----------------------------------------------------------------------------
+constexpr size_t kSmallCounters = 64;   // u32: counters[0] = kept row contributions
+constexpr size_t kTileCounters = 256;   // u32: one per weight tile (<= 97 at H = 512)
+
+int64_t leaf_size(int leaf, int64_t H) {
+  switch (leaf) {
+    case L_FT: return (int64_t)kTrunkRows * H;
+    case L_RULE: return (int64_t)kRule * H;
+    case L_HB: return H;
+    case L_VHH: return (int64_t)kVH * H;
+    case L_VHB: return kVH;
+    case L_VHO: return 3 * kVH;
+    case L_TE: return (int64_t)kVocab * kTR;
+    case L_VTO: return 3 * kPair;
+    case L_PTC: return 16 * kPair;
+    case L_MB: return kMoves;
+    case L_CONS: return kPsp;
+    case L_PCH: return 16 * H;
+    case L_MC: return (int64_t)kMoves * 16;
+    case L_PAH: return (int64_t)kAcc * H;
+    case L_AM: return (int64_t)kMoves * kAcc;
+    case L_SPARSE: return kSparseLen;
+    default: return kTactLen;
+  }
+}
+
+struct Plan {
+  size_t small, keys, sort, row_part, tile_part;
+  size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
+  size_t small_bytes, total;
+  uint32_t row_units_max;
+  int row_w, max_tiles;
+};
+
+int tiles_for(int64_t O, int64_t C) { return (int)(((O + kTO - 1) / kTO) * ((C + kTC - 1) / kTC)); }
+int max_tiles(int64_t H) {
+  return tiles_for(kRule, H) + tiles_for(1, H) + tiles_for(kVH, H) + tiles_for(1, kVH) + tiles_for(3, kVH) +
+         tiles_for(3, kPair) + tiles_for(16, kPair) + tiles_for(16, H) + tiles_for(kAcc, H) + tiles_for(1, kPsp);
+}
+
+Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
+  Plan p{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align_up(bytes, 256);
+    return o;
+  };
+  const Bases cb = bases(B, F, M, T);
+  const int64_t n = cb.n;
+  const int64_t n_rows = B * (6 * F + T + 4 * M);
+  p.row_units_max = (uint32_t)(kKeyRowsEnd + (n_rows + kUnit - 1) / kUnit + 1);
+  p.row_w = (int)std::max<int64_t>(H, kTR);
+  p.max_tiles = max_tiles(H);
+  p.small_bytes = (kSmallCounters + kTileCounters) * 4 + (size_t)kInput * kFeatW * 4;
+  p.small = take(p.small_bytes);
+  p.keys = take((size_t)n * 4);
+  p.sort = take(scat::workspace_bytes(n, 1));
+  p.row_part = take((size_t)p.row_units_max * p.row_w * 4);
+  p.tile_part = take((size_t)p.max_tiles * kSplits * kTO * kTC * 4);
+  p.bp = take((size_t)B * H * 4);
+  p.hid = take((size_t)B * H * 4);
+  p.rms = take((size_t)B * 4);
+  p.vh = take((size_t)B * kVH * 4);
+  p.ta = take((size_t)B * kTR * 4);
+  p.ctx = take((size_t)B * kCtx * 4);
+  p.vl = take((size_t)B * 4 * 4);
+  p.af = take((size_t)kInput * kAcc * 4);
+  p.dl = take((size_t)B * M * 4);
+  p.dvl = take((size_t)B * 4 * 4);
+  p.dctx = take((size_t)B * kCtx * 4);
+  p.cons = take((size_t)B * kPsp * 4);
+  p.rec = take((size_t)B * 8 * 4);
+  p.dbp = take((size_t)B * H * 4);
+  p.dpre = take((size_t)B * H * 4);
+  p.dta = take((size_t)B * kTR * 4);
+  p.dvh = take((size_t)B * kVH * 4);
+  p.total = off;
+  return p;
+}
+
+bool dims_ok(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
+  if (!(H == 32 || H == 64 || H == 128 || H == 256 || H == 512)) return false;
+  if (B < 1 || F < 1 || M < 1 || T < 1 || M > 1024) return false;
+  const double n = (double)B * (6.0 * F + T + 13.0 * M);
+  return n < 2147483647.0;
+}
+
+void add_prob(RedTable& T, const float* a, int lda, int O, const float* x, int ldx, int C, int xpair, float* out,
+              const float* a2 = nullptr, int lda2 = 0, const float* x2 = nullptr, int ldx2 = 0, int K2 = 0) {
+  RedProb& q = T.p[T.n_prob++];
+  q.a = a, q.lda = lda, q.O = O;
+  q.x = x, q.ldx = ldx, q.C = C, q.xpair = xpair;
+  q.a2 = a2, q.lda2 = lda2, q.x2 = x2, q.ldx2 = ldx2, q.K2 = K2;
+  q.out = out;
+  q.tiles_c = (C + kTC - 1) / kTC;
+  q.tile0 = T.n_tiles;
+  T.n_tiles += tiles_for(O, C);
+}
+
+template <int NC>
+int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const Bases& cb, const Sorted& srt,
+                LossScale ls, LossScale raw, uint32_t* status, float* metrics, cudaStream_t s, cudaStream_t side,
+                cudaEvent_t join) {
+  constexpr int H = 32 * NC;
+  const int board_blocks = (int)((bt.B + kWarps - 1) / kWarps);
+  const int af_blocks = (kInput + kWarps - 1) / kWarps;
+  fwd_kernel<NC><<<board_blocks + af_blocks, 32 * kWarps, 0, s>>>(P, bt, A, board_blocks, status);
+  if (int st = check_launch_error("azt forward")) return st;
+  policy_kernel<<<board_blocks, 32 * kWarps, (size_t)kWarps * bt.M * 4, s>>>(P, bt, A, H, ls, status);
+  if (int st = check_launch_error("azt policy")) return st;
+  bwd_kernel<NC><<<board_blocks, 32 * kWarps, 0, s>>>(P, bt, A);
+  if (int st = check_launch_error("azt backward")) return st;
+  if (side != s) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, join, 0));
+  const int unit_blocks = (int)std::min<int64_t>((A.row_units_max + 7) / 8, 148 * 16);
+  unit_kernel<NC><<<unit_blocks, 256, 0, s>>>(P, G, A, bt, cb, srt, H, status);
+  if (int st = check_launch_error("azt unit sums")) return st;
+  run_kernel<NC><<<148 * 4, 256, 0, s>>>(G, A, srt, H);
+  if (int st = check_launch_error("azt run sums")) return st;
+  RedTable T{};
+  T.K = (int)bt.B;
+  add_prob(T, bt.rule, kRule, kRule, A.dpre, H, H, 0, G.g[L_RULE]);
+  add_prob(T, nullptr, 0, 1, A.dbp, H, H, 0, G.g[L_HB]);
+  add_prob(T, A.dvh, kVH, kVH, A.hid, H, H, 0, G.g[L_VHH]);
+  add_prob(T, nullptr, 0, 1, A.dvh, kVH, kVH, 0, G.g[L_VHB]);
+  add_prob(T, A.dvl, 4, 3, A.vh, kVH, kVH, 0, G.g[L_VHO]);
+  add_prob(T, A.dvl, 4, 3, A.ta, kTR, kPair, 1, G.g[L_VTO]);
+  add_prob(T, A.dctx, kCtx, 16, A.ta, kTR, kPair, 1, G.g[L_PTC]);
+  add_prob(T, A.dctx, kCtx, 16, A.hid, H, H, 0, G.g[L_PCH]);
+  add_prob(T, A.dctx + 16, kCtx, kAcc, A.bp, H, H, 0, G.g[L_PAH], A.pspaf + kPsp, kFeatW, P.p[L_FT], H, kInput);
+  add_prob(T, nullptr, 0, 1, A.cons, kPsp, kPsp, 0, G.g[L_CONS]);
+  const int feat_blocks = (int)(((int64_t)kInput * H + 255) / 256);
+  final_kernel<<<T.n_tiles * kSplits + feat_blocks + 1, 256, 0, s>>>(T, P, G, A, bt, H, raw, status, metrics);
+  return check_launch_error("azt final");
+}
+
+}  // namespace
+}  // namespace azt
+}  // namespace cnnue
+
+struct cnnue_azt {
+  int device;
+  cudaStream_t side;
+  cudaEvent_t fork, join;
+};
+
+using namespace cnnue;
+using namespace cnnue::azt;
+
+extern "C" {
+
+int cnnue_azt_create(int device, cnnue_azt** out) {
+  if (!out) return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_create: out is NULL");
+  *out = nullptr;
+  if (int st = use_device(device)) return st;
+  cnnue_azt* e = new cnnue_azt{device, nullptr, nullptr, nullptr};
+  cudaError_t err = cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking);
+  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->fork, cudaEventDisableTiming);
+  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->join, cudaEventDisableTiming);
+  if (err != cudaSuccess) {
+    if (e->join) cudaEventDestroy(e->join);
+    if (e->fork) cudaEventDestroy(e->fork);
+    if (e->side) cudaStreamDestroy(e->side);
+    delete e;
+    return cuda_error(err, "cnnue_azt_create");
+  }
+  *out = e;
+  return CNNUE_OK;
+}
+
+int cnnue_azt_destroy(cnnue_azt* e) {
+  if (!e) return CNNUE_OK;
+  use_device(e->device);
+  cudaStreamSynchronize(e->side);
+  cudaEventDestroy(e->join);
+  cudaEventDestroy(e->fork);
+  cudaStreamDestroy(e->side);
+  delete e;
+  return CNNUE_OK;
+}
+
+size_t cnnue_azt_workspace_bytes(int64_t hidden, int64_t batch, int64_t features, int64_t moves, int64_t threats) {
+  if (!dims_ok(hidden, batch, features, moves, threats)) return 0;
+  return make_plan(hidden, batch, features, moves, threats).total;
+}
+
+int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t n_grads, const int64_t* leaf_offsets,
+                   int64_t hidden, const cnnue_azt_batch* batch, float value_weight, float policy_weight,
+                   float* d_metrics, uint32_t* d_status, void* d_ws, size_t ws_bytes, void* stream) {
+  if (!d_params || !d_grads || !leaf_offsets || !batch || !d_metrics || !d_status || !d_ws)
+    return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: NULL argument");
+  const cnnue_azt_batch& b = *batch;
+  if (!dims_ok(hidden, b.batch, b.features, b.moves, b.threats))
+    return set_error(CNNUE_ERR_INVALID_ARG,
+                     "cnnue_azt_step: hidden must be 32, 64, 128, 256 or 512, dims >= 1, moves <= 1024 "
+                     "(hidden %lld, batch %lld, features %lld, moves %lld, threats %lld)",
+                     (long long)hidden, (long long)b.batch, (long long)b.features, (long long)b.moves,
+                     (long long)b.threats);
+  if (!b.feature_items || !b.value_threat_indices || !b.policy_items || !b.policy_sparse_indices ||
+      !b.policy_tactical_indices || !b.policy_targets || !b.policy_mask || !b.value_wdl || !b.values ||
+      !b.rule_context || !b.policy_weights || !b.value_weights || !b.value_phase_masks)
+    return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: every batch array is needed (expand compact batches)");
+  if (((uintptr_t)d_params | (uintptr_t)d_grads) & 15)
+    return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: parameters and gradients must be 16-byte aligned");
+  for (int l = 0; l < kLeaves; ++l) {
+    if (leaf_offsets[l] < 0 || (leaf_offsets[l] & 3) || leaf_offsets[l] + leaf_size(l, hidden) > n_grads)
+      return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: leaf %d offset %lld (size %lld) outside the %lld "
+                       "gradients or not a multiple of 4", l, (long long)leaf_offsets[l],
+                       (long long)leaf_size(l, hidden), (long long)n_grads);
+  }
+  const Plan pl = make_plan(hidden, b.batch, b.features, b.moves, b.threats);
+  if ((uintptr_t)d_ws & 255) return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: workspace not 256-byte aligned");
+  if (ws_bytes < pl.total)
+    return set_error(CNNUE_ERR_WORKSPACE, "cnnue_azt_step: workspace %zu bytes, need %zu", ws_bytes, pl.total);
+  if (e) {
+    if (int st = use_device(e->device)) return st;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaStream_t side = e ? e->side : s;
+
+  Params P;
+  Grads G;
+  for (int l = 0; l < kLeaves; ++l) {
+    P.p[l] = d_params + leaf_offsets[l];
+    G.g[l] = d_grads + leaf_offsets[l];
+  }
+  Batch bt{b.batch, b.features, b.moves, b.threats, b.feature_items, b.value_threat_indices, b.policy_items,
+           b.policy_sparse_indices, b.policy_tactical_indices, b.policy_targets, b.policy_mask, b.value_wdl,
+           b.values, b.rule_context, b.policy_weights, b.value_weights, b.value_phase_masks};
+  char* w = (char*)d_ws;
+  Act A{};
+  A.counters = (uint32_t*)(w + pl.small);
+  A.tile_cnt = A.counters + kSmallCounters;
+  A.pspaf = (float*)(A.tile_cnt + kTileCounters);
+  A.keys = (uint32_t*)(w + pl.keys);
+  A.row_part = (float*)(w + pl.row_part);
+  A.tile_part = (float*)(w + pl.tile_part);
+  A.bp = (float*)(w + pl.bp), A.hid = (float*)(w + pl.hid), A.rms = (float*)(w + pl.rms);
+  A.vh = (float*)(w + pl.vh), A.ta = (float*)(w + pl.ta), A.ctx = (float*)(w + pl.ctx);
+  A.vl = (float*)(w + pl.vl), A.af = (float*)(w + pl.af), A.dl = (float*)(w + pl.dl);
+  A.dvl = (float*)(w + pl.dvl), A.dctx = (float*)(w + pl.dctx), A.cons = (float*)(w + pl.cons);
+  A.rec = (float*)(w + pl.rec), A.dbp = (float*)(w + pl.dbp), A.dpre = (float*)(w + pl.dpre);
+  A.dta = (float*)(w + pl.dta), A.dvh = (float*)(w + pl.dvh);
+  A.row_units_max = pl.row_units_max;
+  A.row_w = pl.row_w;
+  const Bases cb = bases(b.batch, b.features, b.moves, b.threats);
+  const LossScale raw{std::max(value_weight, 0.f), std::max(policy_weight, 0.f)};
+  const LossScale ls{raw.value / (float)b.batch, raw.policy / (float)b.batch};
+
+  CNNUE_CUDA_TRY(cudaMemsetAsync(d_grads, 0, (size_t)n_grads * 4, s));
+  CNNUE_CUDA_TRY(cudaMemsetAsync(w + pl.small, 0, pl.small_bytes, s));
+  CNNUE_CUDA_TRY(cudaMemsetAsync(d_status, 0, 4, s));
+  if (side != s) {
+    CNNUE_CUDA_TRY(cudaEventRecord(e->fork, s));
+    CNNUE_CUDA_TRY(cudaStreamWaitEvent(side, e->fork, 0));
+  }
+  // side: keys of every table contribution, one joint sort with runs and units
+  const int64_t items = b.batch * (b.features + b.threats + b.moves);
+  const unsigned kb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148 * 8));
+  keygen_kernel<<<kb, 256, 0, side>>>(bt, cb, A.keys, A.counters, d_status);
+  if (int st = check_launch_error("azt keys")) return st;
+  scat::Runs runs;
+  if (int st = scat::sort_runs(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &runs, kUnit)) return st;
+  if (side != s) CNNUE_CUDA_TRY(cudaEventRecord(e->join, side));
+  Sorted srt{runs.keys, runs.idx, runs.run_start, runs.unit_off, runs.n_runs, runs.n_units, runs.run_of,
+             runs.partial, cb.n};
+  switch (hidden) {
+    case 32: return launch_main<1>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+    case 64: return launch_main<2>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+    case 128: return launch_main<4>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+    case 256: return launch_main<8>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+    default: return launch_main<16>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+  }
+}
+
+}  // extern "C"

@@ -194,12 +194,12 @@ __global__ void run_start_kernel(const uint32_t* __restrict__ keys, int64_t n, c
 // units[r] = the unit count of run r (0 past the last run, up to entry n;
 // the scan's entry n is then the unit count).
 __global__ void run_units_kernel(const uint32_t* __restrict__ run_start, const uint32_t* __restrict__ n_runs_d,
-                                 int64_t n, uint32_t* __restrict__ units) {
+                                 int64_t n, uint32_t unit, uint32_t* __restrict__ units) {
   const uint32_t n_runs = *n_runs_d;
   for (int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r <= n; r += (int64_t)gridDim.x * blockDim.x) {
     if (r < n_runs) {
       const uint32_t beg = run_start[r], end = r + 1 < n_runs ? run_start[r + 1] : (uint32_t)n;
-      units[r] = (end - beg + kUnit - 1) / kUnit;
+      units[r] = (end - beg + unit - 1) / unit;
     } else {
       units[r] = 0;
     }
@@ -362,11 +362,14 @@ struct Runs {
   float* partial;         // unit partials
   const uint32_t* n_runs;   // device word: number of runs
   const uint32_t* n_units;  // device word: number of units
+  const uint32_t* run_of;   // [n + 1]: at a run's first slot, the run's index
 };
 
-// Sorts (key, contribution) pairs stably by key and finds runs and units
-// (counts left in device memory).  Requires 0 < n < 2^32 - 1.
-int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s, Runs* out) {
+// Sorts (key, contribution) pairs stably by key and finds runs and units of
+// at most `unit` contributions (counts left in device memory).  Requires
+// 0 < n < 2^32 - 1.
+int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s, Runs* out,
+              uint32_t unit = kUnit) {
   const size_t nn = (size_t)n;
   const int64_t nb = n_blocks(n);
   char* p = (char*)ws;
@@ -408,7 +411,7 @@ int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStr
   if (int st = launch_scan(flag, n + 1, aux, s)) return st;  // run ids; flag[n] = run count
   run_start_kernel<<<gb, 256, 0, s>>>(kin, n, flag, rstart);
   if (int st = check_launch_error("scatter run starts")) return st;
-  run_units_kernel<<<gb, 256, 0, s>>>(rstart, flag + n, n, uoff);
+  run_units_kernel<<<gb, 256, 0, s>>>(rstart, flag + n, n, unit, uoff);
   if (int st = check_launch_error("scatter run units")) return st;
   if (int st = launch_scan(uoff, n + 1, aux, s)) return st;  // unit offsets; uoff[n] = unit count
   out->keys = kin;
@@ -417,6 +420,7 @@ int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStr
   out->unit_off = uoff;
   out->n_runs = flag + n;
   out->n_units = uoff + n;
+  out->run_of = flag;
   return CNNUE_OK;
 }
 

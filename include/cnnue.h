@@ -577,6 +577,60 @@ int cnnue_az_expand_policy_indices(const int64_t* d_items, const uint8_t* d_sign
                                    const uint8_t* d_king_buckets, int64_t batch, int64_t moves,
                                    int64_t* d_sparse, int64_t* d_tactical, float* d_mask, void* stream);
 
+/* ---- native AZ-NNUE training step --------------------------------------
+ * One train_batch_single (src/az/train_gpu_candle.rs:145-160) without its
+ * optimizer step: AzCandleModel::forward (src/az/candle_model.rs:46-147),
+ * compute_batch_loss (train_gpu_candle.rs:221-305) and the gradients of all
+ * 22 weight tensors, as a fixed set of kernels (no autograd graph).  The
+ * parameters and their gradients live in flat fp32 buffers of 17 leaves in
+ * this order: trunk table [1545][H] (tensors 0-4), rule_context_hidden
+ * [7][H], hidden_bias [H], value_head_hidden [96][H], value_head_bias [96],
+ * value_head_output [3][96], value_threat_embedding [57702][64],
+ * value_threat_output [3][128], policy_threat_context [16][128],
+ * policy_move_bias [2086], policy_consequence_output [32],
+ * policy_context_hidden [16][H], policy_move_context [2086][16],
+ * policy_accumulator_hidden [32][H], policy_accumulator_move [2086][32],
+ * sparse table [2596273] (tensors 19-20), tactical table [934976] followed
+ * by its constant zero; leaf_offsets[17] are element offsets, multiples of
+ * 4.  The gradients are summed into nothing: d_grads[0..n_grads) is zeroed
+ * first.  The batch is the packed batch in full form (device pointers;
+ * expand a compact one with cnnue_az_expand_policy_indices first).
+ * d_metrics[31] gets the 30 statistics of AzTrainStats (loss sum, value CE
+ * sum, policy CE sum, the six value sums, the 3 x 7 phase table) and the
+ * status word as a float; d_status is cleared, then collects
+ * CNNUE_STATUS_BAD_INDEX for indices outside their tables (those lookups
+ * read 0 and pass no gradient).  hidden: 32, 64, 128, 256 or 512; moves <=
+ * 1024.  Deterministic: the same inputs give the same bits, run to run.
+ * The engine holds a second stream on which the batch's table indices are
+ * sorted while the forward runs; a step may be captured in a CUDA graph
+ * (the engine's stream joins the capture).  One engine per thread. */
+#define CNNUE_AZT_LEAVES 17
+typedef struct cnnue_azt_batch {
+  int64_t batch, features, moves, threats; /* B, F, M, T */
+  const uint32_t* feature_items;           /* [B][F] */
+  const uint32_t* value_threat_indices;    /* [B][T] */
+  const int64_t* policy_items;             /* [B][M] */
+  const int64_t* policy_sparse_indices;    /* [B][M][7] */
+  const int64_t* policy_tactical_indices;  /* [B][M][2] */
+  const float* policy_targets;             /* [B][M] */
+  const float* policy_mask;                /* [B][M] */
+  const float* value_wdl;                  /* [B][3] */
+  const float* values;                     /* [B] */
+  const float* rule_context;               /* [B][7] */
+  const float* policy_weights;             /* [B] */
+  const float* value_weights;              /* [B] */
+  const float* value_phase_masks;          /* [B][3] */
+} cnnue_azt_batch;
+typedef struct cnnue_azt cnnue_azt;
+int cnnue_azt_create(int device, cnnue_azt** out);
+int cnnue_azt_destroy(cnnue_azt* engine);
+/* Workspace of one step (0 for unsupported dims); 256-byte aligned. */
+size_t cnnue_azt_workspace_bytes(int64_t hidden, int64_t batch, int64_t features, int64_t moves, int64_t threats);
+int cnnue_azt_step(cnnue_azt* engine, const float* d_params, float* d_grads, int64_t n_grads,
+                   const int64_t* leaf_offsets, int64_t hidden, const cnnue_azt_batch* batch, float value_weight,
+                   float policy_weight, float* d_metrics, uint32_t* d_status, void* d_ws, size_t ws_bytes,
+                   void* stream);
+
 /* Per-move records for the policy logits (the per-move inputs of
  * evaluate_prepared_hidden_with_context, src/az.rs:1766-1887), side to move
  * `side`.  moves[2i], moves[2i+1] = from, to squares (absolute).  info[2i] =

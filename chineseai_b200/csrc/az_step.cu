@@ -8,22 +8,22 @@
 //   main:  zero the gradient | forward (trunk per board + accumulator
 //          features) | policy logits + both losses + the logit gradients
 //          (per board) | trunk backward (per board) | wait for the side
-//          stream | table row sums | multi-unit row sums | weight-gradient
-//          tiles + feature-row gradient + metrics
+//          stream | table gradient block sums | cross-block run sums |
+//          weight-gradient tiles + feature-row gradient + metrics
 //   side:  one key per table contribution of the batch | one joint LSD radix
-//          sort of all of them with their runs and units (scatter.cuh)
+//          sort of all of them (scatter.cuh)
 // The batch alone decides which table rows a step touches, so the sort runs
 // beside the forward and the per-board backward.
 //
 // Every table gradient (feature pool rows, threat rows, policy move rows,
 // policy feature rows, sparse and tactical scalars) is one sort problem in
-// a joint key space; a run of equal keys is summed in units of at most
-// kUnit contributions, in sorted (= contribution) order, one warp per row
-// unit (lanes over the row's columns) and one lane per scalar unit; runs of
-// several units add their unit partials in order.  Dense weight gradients
-// are reductions over the batch's boards, computed as tiles with a fixed
-// split of the boards and a fixed order of the split partials.  No atomics
-// touch a value, so a step is deterministic run to run.
+// a joint key space.  The sorted contributions are summed in aligned blocks
+// of 64 positions, one warp per block, each stretch of equal keys in sorted
+// (= contribution) order; runs that cross a block boundary add their block
+// partials in block order afterwards.  Dense weight gradients are
+// reductions over the batch's boards, computed as tiles with a fixed split
+// of the boards and a fixed order of the split partials.  No atomics touch
+// a value, so a step is deterministic run to run.
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -61,9 +61,11 @@ constexpr uint32_t kKeyRowsEnd = kKeyFeat + kInput;  // keys below: row problems
 constexpr uint32_t kKeySparse = kKeyRowsEnd;
 constexpr uint32_t kKeyTact = kKeySparse + (uint32_t)kSparseLen;
 constexpr uint32_t kKeyDrop = kKeyTact + (uint32_t)kTactLen;
-constexpr uint32_t kUnit = 64;  // contributions per unit
-constexpr int kMoveW = 1 + 16 + kAcc;  // move row: bias, move context, accumulator move
+constexpr int kMoveW = 16 + kAcc + 1;  // move row: move context, accumulator move, bias
+constexpr int kRowStride = 64;         // floats per stored move / feature gradient row
 constexpr int kFeatW = kPsp + kAcc;    // feature row: consequence rows, accumulator features
+
+constexpr int kWarps = 8;  // warps per block of every per-board kernel
 
 // The 17 parameter leaves of the flat buffer (tensors 0-4 form the trunk
 // table, 19-20 the sparse table).
@@ -117,13 +119,27 @@ __host__ __device__ inline Bases bases(int64_t B, int64_t F, int64_t M, int64_t 
 struct Act {
   float *bp, *hid, *rms, *vh, *ta, *ctx, *vl, *af;      // forward
   float *dl, *dvl, *dctx, *cons, *rec;                  // loss
+  float *mrow, *frow;                                   // per move: its move-row and feature-row gradients
+  float *pcnt;                                          // multiplicities of the derived trunk rows [B][5F]
   float *dbp, *dpre, *dta, *dvh;                        // backward
   float *pspaf;                                         // [1260][64] feature-row gradients
-  float *row_part, *tile_part;                          // unit partial rows, weight-tile partials
-  uint32_t *keys, *counters, *tile_cnt;                 // counters[0]: row contributions
-  uint32_t row_units_max;
+  float *part, *tile_part;                              // segment partials (head, tail per block), tile partials
+  uint32_t *keys, *counters, *tile_cnt;
   int row_w;                                            // partial row width max(H, 64)
+  uint32_t part_slots;                                  // 2 x blocks of the largest sort
+  uint32_t* status;
 };
+
+// A failed self-check: counters[2] gets the first check's code, counters[3..4]
+// its operands; the status word gets CNNUE_STATUS_INTERNAL; the access is
+// skipped by the caller.
+__device__ __noinline__ void check_failed(const Act& A, uint32_t code, uint32_t a, uint32_t b) {
+  if (atomicCAS(A.counters + 2, 0u, code) == 0u) {
+    A.counters[3] = a;
+    A.counters[4] = b;
+  }
+  atomicOr(A.status, CNNUE_STATUS_INTERNAL);
+}
 
 // ---- policy items (src/az/fused_policy.rs:10-35) -----------------------------
 struct Item {
@@ -282,79 +298,135 @@ __device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, in
 }
 
 // ---- keys of every table contribution (side stream) -----------------------------
-// One thread per feature item, threat index or policy move.  A contribution
-// that cannot change a table gradient gets kKeyDrop: padding items and
-// threats, moves without the policy bit (torch.where passes them no
-// gradient), feature rows of moves without the move bit or of an absent
-// capture, and the sparse / tactical lookups of padded moves (no policy bit,
-// masked, zero target: their softmax probability underflows to exactly 0,
-// so their logit gradient is exactly 0).  Indices outside their tables set
-// CNNUE_STATUS_BAD_INDEX and are dropped.  counters[0] gets the number of
-// row-problem contributions kept (the sorted position where scalar keys
-// begin).
+// Trunk-table contributions, per board (one warp): one per feature item (its
+// feature row) and one per distinct derived row (piece, rank, file and king
+// rows, 285 in all) with the number of the board's items that hit it as a
+// multiplicity - the board gradient times that count.  The trunk section
+// holds B x F feature slots, then 5F derived slots per board (a board hits
+// at most 5F derived rows).  Then one thread per threat index or policy
+// move.  A contribution that cannot change a table gradient gets kKeyDrop:
+// padding items and threats, moves without the policy bit (torch.where
+// passes them no gradient), feature rows of moves without the move bit or
+// of an absent capture, and the sparse / tactical lookups of padded moves
+// (no policy bit, masked, zero target: their softmax probability underflows
+// to exactly 0, so their logit gradient is exactly 0).  Indices outside
+// their tables set CNNUE_STATUS_BAD_INDEX and are dropped.  counters[0]
+// gets the number of row-problem contributions kept, counters[1] the number
+// of all kept (the sort drops the others in its first pass).
+constexpr int kDerived = kTrunkRows - kInput;  // 285
+// Shared words per warp of the forward's row list: the derived-row histogram
+// (kDerived + 1, even) and up to F + kDerived (row, multiplicity) pairs.
+__host__ __device__ inline int64_t fwd_smem_words(int64_t F) { return kDerived + 1 + 2 * (F + kDerived); }
+
 __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_t* __restrict__ keys,
-                                                     uint32_t* __restrict__ counters, uint32_t* __restrict__ status) {
-  const int64_t nf = bt.B * bt.F, nt = bt.B * bt.T, nm = bt.B * bt.M;
-  const int64_t total = nf + nt + nm;
-  uint32_t rows_kept = 0, bad = 0;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
-    if (t < nf) {
-      uint32_t rows[6];
-      const int r = pool_rows(bt.fi[t], rows);
-      bad |= r < 0;
-      uint32_t* k = keys + cb.pool + t * 6;
+                                                     float* __restrict__ pcnt, uint32_t* __restrict__ counters,
+                                                     uint32_t* __restrict__ status, int pool_blocks) {
+  __shared__ uint32_t hist[kWarps][kDerived];
+  __shared__ uint32_t part[2][kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint32_t rows_kept = 0, live = 0;
+  bool bad = false;
+  if ((int)blockIdx.x < pool_blocks) {
+    const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
+    if (b < bt.B) {
+      uint32_t* h = hist[warp];
+      for (int i = lane; i < kDerived; i += 32) h[i] = 0;
+      __syncwarp();
+      for (int64_t i = lane; i < bt.F; i += 32) {
+        uint32_t rows[6];
+        const int r = pool_rows(bt.fi[b * bt.F + i], rows);
+        bad |= r < 0;
+        keys[cb.pool + b * bt.F + i] = r > 0 ? kKeyPool + rows[0] : kKeyDrop;
+        if (r > 0) {
+          ++live;
 #pragma unroll
-      for (int s = 0; s < 6; ++s) k[s] = r > 0 ? kKeyPool + rows[s] : kKeyDrop;
-      rows_kept += r > 0 ? 6 : 0;
-    } else if (t < nf + nt) {
-      const int64_t u = t - nf;
-      const uint32_t idx = bt.ti[u];
-      const bool ok = idx < (uint32_t)kVocab;
-      bad |= !ok && idx != kPad;
-      keys[cb.threat + u] = ok ? kKeyThreat + idx : kKeyDrop;
-      rows_kept += ok;
-    } else {
-      const int64_t u = t - nf - nt;
-      const Item it = decode(bt.pi[u]);
-      const bool ok = in_range(it);
-      bad |= it.policy && !ok;
-      const bool live = it.policy && ok;
-      keys[cb.move + u] = live ? kKeyMove + it.mv : kKeyDrop;
-      const bool feat = live && it.move;
-      uint32_t* fk = keys + cb.feat + u * 3;
-      fk[0] = feat ? kKeyFeat + it.to : kKeyDrop;
-      fk[1] = feat ? kKeyFeat + it.from : kKeyDrop;
-      fk[2] = feat && it.capture ? kKeyFeat + it.cap : kKeyDrop;
-      rows_kept += live + (feat ? 2 + it.capture : 0);
-      const bool drop = !it.policy && bt.mask[u] <= kMaskDrop && bt.tgt[u] == 0.f;
-#pragma unroll
-      for (int j = 0; j < 7; ++j) {
-        const int64_t s = bt.sp[u * 7 + j];
-        const bool sok = s >= 0 && s < kSparseLen;
-        bad |= !sok;
-        keys[cb.sparse + u * 7 + j] = sok && !drop ? kKeySparse + (uint32_t)s : kKeyDrop;
+          for (int q = 1; q < 6; ++q) atomicAdd(&h[rows[q] - kInput], 1u);  // counts: order-free
+        }
       }
+      __syncwarp();
+      const int64_t slots = 5 * bt.F;
+      const int64_t dkey = cb.pool + bt.B * bt.F + b * slots;
+      uint32_t used = 0;
+      for (int bin0 = 0; bin0 < kDerived; bin0 += 32) {
+        const int bin = bin0 + lane;
+        const uint32_t c = bin < kDerived ? h[bin] : 0u;
+        const uint32_t m = __ballot_sync(kFull, c > 0);
+        if (c > 0) {
+          const uint32_t pos = used + __popc(m & ((1u << lane) - 1u));
+          if (pos < slots) {
+            keys[dkey + pos] = kKeyPool + kInput + bin;
+            pcnt[b * slots + pos] = (float)c;
+          } else {
+            atomicOr(status, CNNUE_STATUS_INTERNAL);
+          }
+        }
+        used += __popc(m);
+      }
+      for (int64_t k = used + lane; k < slots; k += 32) keys[dkey + k] = kKeyDrop;
+      if (lane == 0) live += used;
+    }
+    rows_kept = live;
+  } else {
+    const int64_t nt = bt.B * bt.T, nm = bt.B * bt.M;
+    const int64_t stride = (int64_t)(gridDim.x - pool_blocks) * blockDim.x;
+    for (int64_t t = (int64_t)(blockIdx.x - pool_blocks) * blockDim.x + threadIdx.x; t < nt + nm; t += stride) {
+      if (t < nt) {
+        const uint32_t idx = bt.ti[t];
+        const bool ok = idx < (uint32_t)kVocab;
+        bad |= !ok && idx != kPad;
+        keys[cb.threat + t] = ok ? kKeyThreat + idx : kKeyDrop;
+        rows_kept += ok;
+        live += ok;
+      } else {
+        const int64_t u = t - nt;
+        const Item it = decode(bt.pi[u]);
+        const bool ok = in_range(it);
+        bad |= it.policy && !ok;
+        const bool on = it.policy && ok;
+        keys[cb.move + u] = on ? kKeyMove + it.mv : kKeyDrop;
+        const bool feat = on && it.move;
+        uint32_t* fk = keys + cb.feat + u * 3;
+        fk[0] = feat ? kKeyFeat + it.to : kKeyDrop;
+        fk[1] = feat ? kKeyFeat + it.from : kKeyDrop;
+        fk[2] = feat && it.capture ? kKeyFeat + it.cap : kKeyDrop;
+        const uint32_t rk = on + (feat ? 2 + it.capture : 0);
+        rows_kept += rk;
+        live += rk;
+        const bool drop = !it.policy && bt.mask[u] <= kMaskDrop && bt.tgt[u] == 0.f;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int64_t s = bt.tc[u * 2 + j];
-        const bool sok = s >= 0 && s < kTactLen;
-        bad |= !sok;
-        keys[cb.tact + u * 2 + j] = sok && !drop ? kKeyTact + (uint32_t)s : kKeyDrop;
+        for (int j = 0; j < 7; ++j) {
+          const int64_t sx = bt.sp[u * 7 + j];
+          const bool sok = sx >= 0 && sx < kSparseLen;
+          bad |= !sok;
+          keys[cb.sparse + u * 7 + j] = sok && !drop ? kKeySparse + (uint32_t)sx : kKeyDrop;
+          live += sok && !drop;
+        }
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int64_t sx = bt.tc[u * 2 + j];
+          const bool sok = sx >= 0 && sx < kTactLen;
+          bad |= !sok;
+          keys[cb.tact + u * 2 + j] = sok && !drop ? kKeyTact + (uint32_t)sx : kKeyDrop;
+          live += sok && !drop;
+        }
       }
     }
   }
-  // block total of the kept row contributions (a count: order-free)
-  __shared__ uint32_t part[8];
-  uint32_t v = rows_kept;
+  // block totals (counts: order-free)
+  uint32_t v0 = rows_kept, v1 = live;
 #pragma unroll
-  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = v;
-  if (__any_sync(kFull, bad) && (threadIdx.x & 31) == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+  for (int o = 16; o; o >>= 1) {
+    v0 += __shfl_xor_sync(kFull, v0, o);
+    v1 += __shfl_xor_sync(kFull, v1, o);
+  }
+  if (lane == 0) part[0][warp] = v0, part[1][warp] = v1;
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
   __syncthreads();
   if (threadIdx.x == 0) {
-    uint32_t s = 0;
-    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += part[w];
-    if (s) atomicAdd(counters, s);
+    uint32_t s0 = 0, s1 = 0;
+    for (int w = 0; w < kWarps; ++w) s0 += part[0][w], s1 += part[1][w];
+    if (s0) atomicAdd(counters, s0);
+    if (s1) atomicAdd(counters + 1, s1);
   }
 }
 
@@ -368,7 +440,6 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
 //   W_to . pair, move context = W_pc . hidden + W_ptc . pair;
 // blocks after them: one warp per input row r < 1260 - the accumulator
 // features af[r] = W_acc . trunk_table[r] (32 values).
-constexpr int kWarps = 8;  // warps per block of every per-board kernel
 
 template <int NC>
 __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Act A, int trunk_blocks,
@@ -385,30 +456,58 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
   }
   const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
   if (b >= bt.B) return;
-  // feature pool: items fetched 32 at a time, one per lane, then broadcast
+  // feature pool: the board's feature rows and its distinct derived rows
+  // with multiplicities (a per-warp histogram), listed in shared memory,
+  // then summed eight rows at a time
+  extern __shared__ uint32_t fsm[];
+  uint32_t* hist = fsm + (size_t)warp * fwd_smem_words(bt.F);
+  uint2* list = reinterpret_cast<uint2*>(hist + kDerived + 1);  // 8-byte aligned: every stride is even
+  for (int i = lane; i < kDerived; i += 32) hist[i] = 0;
+  __syncwarp();
+  bool bad = false, bad_list = false;
+  uint32_t n_list = 0;
+  for (int64_t i0 = 0; i0 < bt.F; i0 += 32) {
+    uint32_t rows[6];
+    const int r = i0 + lane < bt.F ? pool_rows(bt.fi[b * bt.F + i0 + lane], rows) : 0;
+    bad |= r < 0;
+    const uint32_t m = __ballot_sync(kFull, r > 0);
+    if (r > 0) {
+      list[n_list + __popc(m & ((1u << lane) - 1u))] = make_uint2(rows[0], __float_as_uint(1.f));
+#pragma unroll
+      for (int q = 1; q < 6; ++q) atomicAdd(&hist[rows[q] - kInput], 1u);
+    }
+    n_list += __popc(m);
+  }
+  __syncwarp();
+  for (int bin0 = 0; bin0 < kDerived; bin0 += 32) {
+    const int bin = bin0 + lane;
+    const uint32_t c = bin < kDerived ? hist[bin] : 0u;
+    const uint32_t m = __ballot_sync(kFull, c > 0);
+    const uint32_t pos = n_list + __popc(m & ((1u << lane) - 1u));
+    if (c > 0 && pos < (uint32_t)(bt.F + kDerived)) list[pos] = make_uint2(kInput + bin, __float_as_uint((float)c));
+    bad_list |= c > 0 && pos >= (uint32_t)(bt.F + kDerived);
+    n_list += __popc(m);
+  }
+  __syncwarp();
+  if (n_list > (uint32_t)(bt.F + kDerived)) n_list = (uint32_t)(bt.F + kDerived);
+  constexpr int kB = NC > 4 ? 4 : 8;
   float acc[NC];
 #pragma unroll
   for (int i = 0; i < NC; ++i) acc[i] = 0.f;
-  bool bad = false;
-  for (int64_t i0 = 0; i0 < bt.F; i0 += 32) {
-    const uint32_t mine = i0 + lane < bt.F ? bt.fi[b * bt.F + i0 + lane] : kPad;
-    const int cnt = (int)(bt.F - i0 < 32 ? bt.F - i0 : 32);
-    for (int j = 0; j < cnt; ++j) {
-      const uint32_t item = __shfl_sync(kFull, mine, j);
-      uint32_t rows[6];
-      const int r = pool_rows(item, rows);
-      if (r <= 0) {
-        bad |= r < 0;
-        continue;
-      }
-      float x[6][NC];
+  for (uint32_t j0 = 0; j0 < n_list; j0 += kB) {
+    float x[kB][NC], mult[kB];
 #pragma unroll
-      for (int s = 0; s < 6; ++s) ld_row<NC>(P.p[L_FT] + (size_t)rows[s] * H, lane, x[s]);
-#pragma unroll
-      for (int s = 0; s < 6; ++s)
-#pragma unroll
-        for (int c = 0; c < NC; ++c) acc[c] += x[s][c];
+    for (int t = 0; t < kB; ++t) {
+      const bool ok = j0 + t < n_list;
+      const uint2 e = ok ? list[j0 + t] : make_uint2(0u, 0u);
+      mult[t] = __uint_as_float(e.y);
+      ld_row<NC>(P.p[L_FT] + (size_t)e.x * H, lane, x[t]);
     }
+#pragma unroll
+    for (int t = 0; t < kB; ++t)
+      if (j0 + t < n_list)
+#pragma unroll
+        for (int c = 0; c < NC; ++c) acc[c] = fmaf(mult[t], x[t][c], acc[c]);
   }
   float bias[NC], bp[NC], h[NC];
   ld_row<NC>(P.p[L_HB], lane, bias);
@@ -490,6 +589,7 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
   A.ctx[b * kCtx + 16 + lane] = acc_ctx;
   if (lane < 3) A.vl[b * 4 + lane] = lane == 0 ? vl[0] : (lane == 1 ? vl[1] : vl[2]);
   if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+  if (__any_sync(kFull, bad_list) && lane == 0) atomicOr(status, CNNUE_STATUS_INTERNAL);
 }
 
 // ---- policy logits, losses, logit gradients ------------------------------------------
@@ -620,7 +720,34 @@ __global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt,
     const float dl = scale_p * (z[m] * tsum - bt.tgt[u]);
     A.dl[u] = dl;
     const Item it = decode(bt.pi[u]);
-    if (!it.policy || !it.move || !in_range(it) || dl == 0.f) continue;
+    if (!it.policy || !in_range(it)) continue;
+    // the move's gradient rows, read by the table sums: move row [dl ctx16,
+    // dl (ctx32 + af delta), dl], feature row [dl consequence, dl acc move]
+    float* mrow = A.mrow + (size_t)u * kRowStride;
+    mrow[kMoveW - 1] = dl;
+    if (!it.move) {
+#pragma unroll
+      for (int q = 0; q < 12; ++q) reinterpret_cast<float4*>(mrow)[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      continue;
+    }
+    float* frow = A.frow + (size_t)u * kRowStride;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      reinterpret_cast<float4*>(mrow)[q] =
+          make_float4(dl * c[4 * q], dl * c[4 * q + 1], dl * c[4 * q + 2], dl * c[4 * q + 3]);
+    const float* at = A.af + (size_t)it.to * kAcc;
+    const float* af = A.af + (size_t)it.from * kAcc;
+    const float* ac = A.af + (size_t)it.cap * kAcc;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float4 x = sub4(*reinterpret_cast<const float4*>(at + 4 * q), *reinterpret_cast<const float4*>(af + 4 * q));
+      if (it.capture) x = sub4(x, *reinterpret_cast<const float4*>(ac + 4 * q));
+      reinterpret_cast<float4*>(mrow + 16)[q] =
+          make_float4(dl * (c[16 + 4 * q] + x.x), dl * (c[17 + 4 * q] + x.y), dl * (c[18 + 4 * q] + x.z),
+                      dl * (c[19 + 4 * q] + x.w));
+      reinterpret_cast<float4*>(frow)[q] =
+          make_float4(dl * cons[4 * q], dl * cons[4 * q + 1], dl * cons[4 * q + 2], dl * cons[4 * q + 3]);
+    }
     const float* mc = P.p[L_MC] + (size_t)it.mv * 16;
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -638,6 +765,7 @@ __global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt,
       g32[4 * q + 1] = fmaf(dl, w.y, g32[4 * q + 1]);
       g32[4 * q + 2] = fmaf(dl, w.z, g32[4 * q + 2]);
       g32[4 * q + 3] = fmaf(dl, w.w, g32[4 * q + 3]);
+      reinterpret_cast<float4*>(frow + kPsp)[q] = make_float4(dl * w.x, dl * w.y, dl * w.z, dl * w.w);
     }
     const float* rt = ft + (size_t)it.to * H;
     const float* rf = ft + (size_t)it.from * H;
@@ -757,243 +885,274 @@ __global__ void __launch_bounds__(32 * kWarps) bwd_kernel(Params P, Batch bt, Ac
   st_row<NC>(A.dbp + b * H, lane, dbp);
 }
 
-// ---- table gradients: unit and run sums over the joint sort ---------------------------
+// ---- table gradients: segment sums over the joint sort ---------------------------------
+// The sorted contributions are cut into aligned blocks of kSeg positions; a
+// segment is a maximal stretch of equal keys inside one block.  One warp per
+// block sums its segments in position (= contribution) order: a segment that
+// is its key's whole run writes the gradient row (or scalar) directly; a
+// segment continuing from the previous block leaves its partial in the
+// block's head slot, one that only continues into the next block in the tail
+// slot.  The combine kernel then gives every run crossing a block boundary to
+// one warp, which adds the run's tail partial and the head partials of the
+// following blocks in block order.  Every contribution's value is a row (or
+// scalar) already in memory: the board gradient of the feature pool, the
+// threat gradient, the move's move row / signed feature row, or dlogit.
+constexpr int kSeg = 64;
+
 struct Sorted {
-  const uint32_t* keys;       // [n] sorted keys
-  const uint32_t* idx;        // [n] contribution of each sorted slot
-  const uint32_t* run_start;  // [n_runs]
-  const uint32_t* unit_off;   // [n_runs] first unit of each run
-  const uint32_t* n_runs_d;
-  const uint32_t* n_units_d;
-  const uint32_t* run_of;     // run index at each run's first slot
-  float* spart;               // scalar unit partials, by unit
-  uint32_t n;
+  const uint32_t* keys;    // [n_live] sorted keys
+  const uint32_t* idx;     // [n_live] contribution of each sorted slot
+  const uint32_t* n_live;  // device word: contributions kept
+  uint32_t n_max;          // all contribution slots (bounds n_live)
 };
 
-// Last run r with unit_off[r] <= u (unit_off strictly increasing, unit_off[0]
-// = 0): a 32-way search, 32 probes per round, at most 7 rounds for 2^31 runs.
-__device__ __forceinline__ uint32_t warp_find_run(const uint32_t* __restrict__ unit_off, uint32_t n_runs, uint32_t u,
-                                                  int lane) {
-  uint32_t lo = 0, hi = n_runs - 1;
-  for (int round = 0; round < 8 && lo < hi; ++round) {
-    const uint32_t step = (hi - lo + 32) / 32;
-    const uint32_t r = lo + (uint32_t)lane * step;
-    const bool pred = r <= hi && unit_off[r] <= u;
-    const int k = __popc(__ballot_sync(kFull, pred)) - 1;  // >= 0: lane 0 probes lo
-    lo += (uint32_t)k * step;
-    hi = min(hi, lo + step - 1);
-  }
-  return lo;
-}
-
-__device__ __forceinline__ uint32_t run_units(const Sorted& s, uint32_t r, uint32_t n_runs, uint32_t n_units) {
-  return (r + 1 < n_runs ? s.unit_off[r + 1] : n_units) - s.unit_off[r];
-}
-
-// Row problems: width and destination of a key's row.
-enum Problem { PR_POOL, PR_THREAT, PR_MOVE, PR_FEAT };
-__device__ __forceinline__ Problem problem_of(uint32_t key) {
-  return key < kKeyThreat ? PR_POOL : key < kKeyMove ? PR_THREAT : key < kKeyFeat ? PR_MOVE : PR_FEAT;
-}
-__device__ __forceinline__ int row_width(Problem p, int H) {
-  return p == PR_POOL ? H : p == PR_MOVE ? kMoveW : kTR;  // threat and feature rows: 64
-}
-__device__ __forceinline__ float* row_dest(const Grads& G, const Act& A, Problem p, uint32_t key, int c, int H) {
-  switch (p) {
-    case PR_POOL:
-      return G.g[L_FT] + (size_t)(key - kKeyPool) * H + c;
-    case PR_THREAT:
-      return G.g[L_TE] + (size_t)(key - kKeyThreat) * kTR + c;
-    case PR_MOVE: {
-      const uint32_t mv = key - kKeyMove;
-      return c == 0 ? G.g[L_MB] + mv : c <= 16 ? G.g[L_MC] + (size_t)mv * 16 + (c - 1)
-                                                : G.g[L_AM] + (size_t)mv * kAcc + (c - 17);
+// Where contribution e (of key `key`) reads its row: src[c] * sign, c < W.
+struct Src {
+  const float* src;
+  float sign;
+  int W;
+};
+__device__ __forceinline__ Src source(const Act& A, const Batch& bt, const Bases& cb, uint32_t key, uint32_t e,
+                                      int H) {
+  const uint32_t nbm = (uint32_t)(bt.B * bt.M);
+  if (key < kKeyThreat) {
+    const uint32_t nf = (uint32_t)(bt.B * bt.F);
+    if (e < nf) return {A.dbp + (size_t)(e / (uint32_t)bt.F) * H, 1.f, H};
+    const uint32_t d = e - nf;  // a derived row: board d / 5F, multiplicity pcnt[d]
+    if (d >= (uint32_t)(bt.B * 5 * bt.F)) {
+      check_failed(A, 6, key, e);
+      return {A.dl, 0.f, 0};
     }
-    default:
-      return A.pspaf + (size_t)(key - kKeyFeat) * kFeatW + c;
+    return {A.dbp + (size_t)(d / (uint32_t)(5 * bt.F)) * H, A.pcnt[d], H};
   }
+  if (key < kKeyMove) {
+    if (e < cb.threat || e >= cb.move) {
+      check_failed(A, 7, key, e);
+      return {A.dl, 0.f, 0};
+    }
+    return {A.dta + (size_t)((e - cb.threat) / (uint32_t)bt.T) * kTR, 1.f, kTR};
+  }
+  if (key < kKeyFeat) {
+    if (e < cb.move || e >= cb.feat) {
+      check_failed(A, 8, key, e);
+      return {A.dl, 0.f, 0};
+    }
+    return {A.mrow + (size_t)(e - cb.move) * kRowStride, 1.f, kMoveW};
+  }
+  if (key < kKeyRowsEnd) {
+    if (e < cb.feat || e >= cb.sparse) {
+      check_failed(A, 9, key, e);
+      return {A.dl, 0.f, 0};
+    }
+    const uint32_t v = e - cb.feat, u = v / 3u;
+    return {A.frow + (size_t)u * kRowStride, v - 3u * u == 0 ? 1.f : -1.f, kFeatW};
+  }
+  const bool tact = key >= kKeyTact;
+  const uint32_t lo = tact ? cb.tact : cb.sparse, hi = tact ? cb.n : cb.tact;
+  if (e < lo || e >= hi || key >= kKeyDrop) {
+    check_failed(A, 10, key, e);
+    return {A.dl, 0.f, 0};
+  }
+  const uint32_t u = (e - lo) / (tact ? 2u : 7u);
+  (void)nbm;
+  return {A.dl + u, 1.f, 1};
+}
+__device__ __forceinline__ int key_width(uint32_t key, int H) {
+  return key < kKeyThreat ? H : key < kKeyMove ? kTR : key < kKeyFeat ? kMoveW : key < kKeyRowsEnd ? kFeatW : 1;
+}
+__device__ __forceinline__ float* key_dest(const Grads& G, const Act& A, uint32_t key, int c, int H) {
+  if (key < kKeyThreat) return G.g[L_FT] + (size_t)(key - kKeyPool) * H + c;
+  if (key < kKeyMove) return G.g[L_TE] + (size_t)(key - kKeyThreat) * kTR + c;
+  if (key < kKeyFeat) {
+    const uint32_t mv = key - kKeyMove;
+    return c < 16 ? G.g[L_MC] + (size_t)mv * 16 + c
+                  : c < 16 + kAcc ? G.g[L_AM] + (size_t)mv * kAcc + (c - 16) : G.g[L_MB] + mv;
+  }
+  if (key < kKeyRowsEnd) return A.pspaf + (size_t)(key - kKeyFeat) * kFeatW + c;
+  return key < kKeyTact ? G.g[L_SPARSE] + (key - kKeySparse) : G.g[L_TACT] + (key - kKeyTact);
 }
 
-// Column c of the row that contribution e (of problem p) adds.
-__device__ __forceinline__ float row_value(const Params& P, const Act& A, const Batch& bt, const Bases& cb, Problem p,
-                                           uint32_t e, int c, int H) {
-  switch (p) {
-    case PR_POOL:
-      return A.dbp[(size_t)(e / (uint32_t)(6 * bt.F)) * H + c];
-    case PR_THREAT:
-      return A.dta[(size_t)((e - cb.threat) / (uint32_t)bt.T) * kTR + c];
-    case PR_MOVE: {
-      const uint32_t u = e - cb.move;
-      const float dl = A.dl[u];
-      if (c == 0) return dl;
-      const Item it = decode(bt.pi[u]);
-      if (!it.move) return 0.f;
-      const size_t b = u / (uint32_t)bt.M;
-      if (c <= 16) return dl * A.ctx[b * kCtx + (c - 1)];
-      const int j = c - 17;
-      float x = A.ctx[b * kCtx + 16 + j] + A.af[(size_t)it.to * kAcc + j] - A.af[(size_t)it.from * kAcc + j];
-      if (it.capture) x -= A.af[(size_t)it.cap * kAcc + j];
-      return dl * x;
-    }
-    default: {
-      const uint32_t v = e - cb.feat, u = v / 3u, role = v - 3u * u;
-      const float dl = role == 0 ? A.dl[u] : -A.dl[u];
-      if (c < kPsp) return dl * __ldg(P.p[L_CONS] + c);
-      const Item it = decode(bt.pi[u]);
-      return dl * __ldg(P.p[L_AM] + (size_t)it.mv * kAcc + (c - kPsp));
-    }
-  }
-}
-
-// One warp per row unit (lanes over columns c = lane + 32 k), then one lane
-// per scalar unit (32 consecutive units per warp).  A unit that is its run's
-// only one writes the gradient row directly; the others leave partials.
 template <int NC>
-__global__ void __launch_bounds__(256) unit_kernel(Params P, Grads G, Act A, Batch bt, Bases cb, Sorted s, int H,
-                                                   uint32_t* __restrict__ status) {
-  constexpr int KW = NC > 2 ? NC : 2;  // column chunks: max(H, 64) / 32
+__global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Bases cb, Sorted s, int H) {
+  constexpr int KW = NC > 2 ? NC : 2;   // column chunks of the widest row: max(H, 64) / 32
+  constexpr int BT = NC > 4 ? 4 : 8;    // positions whose loads are in flight together
   const int lane = threadIdx.x & 31;
-  const uint32_t n_runs = *s.n_runs_d, n_units = *s.n_units_d, P0 = A.counters[0];
-  if (n_runs == 0) return;
-  const uint32_t u_rows = P0 < s.n ? s.unit_off[s.run_of[P0]] : n_units;
+  const uint32_t n = min(*s.n_live, s.n_max);
+  const uint32_t n_blocks = (n + kSeg - 1) / kSeg;
   const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
-  for (uint32_t u = gw; u < u_rows; u += n_warps) {
-    if (u >= A.row_units_max) {
-      if (lane == 0) atomicOr(status, CNNUE_STATUS_INTERNAL);
-      break;
+  for (uint32_t blk = gw; blk < n_blocks; blk += n_warps) {
+    const uint32_t base = blk * kSeg;
+    const int cnt = n - base < (uint32_t)kSeg ? (int)(n - base) : kSeg;
+    const uint32_t k_lo = lane < cnt ? s.keys[base + lane] : kKeyDrop;
+    const uint32_t k_hi = 32 + lane < cnt ? s.keys[base + 32 + lane] : kKeyDrop;
+    const uint32_t e_lo = lane < cnt ? s.idx[base + lane] : 0u;
+    const uint32_t e_hi = 32 + lane < cnt ? s.idx[base + 32 + lane] : 0u;
+    const uint32_t first = __shfl_sync(kFull, k_lo, 0);
+    if (first >= kKeyDrop) continue;  // keys ascend: the block is all dropped
+    const uint32_t prev = base > 0 ? s.keys[base - 1] : 0xffffffffu;
+    const uint32_t next = base + cnt < n ? s.keys[base + cnt] : 0xffffffffu;
+    if (first >= kKeyRowsEnd) {
+      // scalar block: each lane loads its two positions, then one pass in order
+      float v_lo = 0.f, v_hi = 0.f;
+      if (k_lo < kKeyDrop) {
+        const Src q = source(A, bt, cb, k_lo, e_lo, H);
+        if (q.W) v_lo = *q.src;
+      }
+      if (k_hi < kKeyDrop) {
+        const Src q = source(A, bt, cb, k_hi, e_hi, H);
+        if (q.W) v_hi = *q.src;
+      }
+      float acc = 0.f;
+      int seg_start = 0;
+      for (int j = 0; j < cnt; ++j) {
+        const uint32_t key = __shfl_sync(kFull, j < 32 ? k_lo : k_hi, j & 31);
+        const uint32_t kn = j + 1 < cnt ? __shfl_sync(kFull, j + 1 < 32 ? k_lo : k_hi, (j + 1) & 31) : next;
+        const float v = __shfl_sync(kFull, j < 32 ? v_lo : v_hi, j & 31);
+        if (key >= kKeyDrop) break;
+        acc += v;
+        if (j + 1 < cnt && kn == key) continue;
+        if (lane == 0) {
+          if (2 * blk + 1 >= A.part_slots) check_failed(A, 11, blk, A.part_slots);
+          else if (seg_start == 0 && prev == key) A.part[(size_t)(2 * blk) * A.row_w] = acc;
+          else if (j == cnt - 1 && next == key) A.part[(size_t)(2 * blk + 1) * A.row_w] = acc;
+          else *key_dest(G, A, key, 0, H) = acc;
+        }
+        acc = 0.f;
+        seg_start = j + 1;
+      }
+      continue;
     }
-    const uint32_t r = warp_find_run(s.unit_off, n_runs, u, lane);
-    const uint32_t rbeg = s.run_start[r], rend = r + 1 < n_runs ? s.run_start[r + 1] : s.n;
-    const uint32_t beg = rbeg + (u - s.unit_off[r]) * kUnit, end = min(rend, beg + kUnit);
-    const uint32_t key = s.keys[rbeg];
-    const bool single = run_units(s, r, n_runs, n_units) == 1;
-    const Problem p = problem_of(key);
-    const int W = row_width(p, H);
-    const int len = (int)(end - beg);
-    const uint32_t e_lo = lane < len ? s.idx[beg + lane] : 0u;
-    const uint32_t e_hi = 32 + lane < len ? s.idx[beg + 32 + lane] : 0u;
     float acc[KW];
 #pragma unroll
     for (int k = 0; k < KW; ++k) acc[k] = 0.f;
-    if (p == PR_POOL) {
-      // the bulk: dboard rows, four contributions' loads in flight
-      for (int j = 0; j < len; j += 4) {
-        float x[4][NC];
+    int seg_start = 0;
+    bool done = false;
+    for (int j0 = 0; j0 < cnt && !done; j0 += BT) {
+      uint32_t kk[BT + 1];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int jj = j + t;
-          const uint32_t e = __shfl_sync(kFull, jj < 32 ? e_lo : e_hi, jj & 31);
-#pragma unroll
-          for (int k = 0; k < NC; ++k)
-            x[t][k] = jj < len ? A.dbp[(size_t)(e / (uint32_t)(6 * bt.F)) * H + lane + 32 * k] : 0.f;
-        }
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int k = 0; k < NC; ++k) acc[k] += x[t][k];
+      for (int t = 0; t <= BT; ++t) {
+        const int j = j0 + t;
+        const uint32_t k = __shfl_sync(kFull, (j & 32) ? k_hi : k_lo, j & 31);
+        kk[t] = j < cnt ? k : next;
       }
-    } else {
-      for (int j = 0; j < len; ++j) {
-        const uint32_t e = __shfl_sync(kFull, j < 32 ? e_lo : e_hi, j & 31);
+      Src src[BT];
+#pragma unroll
+      for (int t = 0; t < BT; ++t) {
+        const int j = j0 + t;
+        const uint32_t e = __shfl_sync(kFull, (j & 32) ? e_hi : e_lo, j & 31);
+        src[t] = j < cnt && kk[t] < kKeyDrop ? source(A, bt, cb, kk[t], e, H) : Src{A.dl, 0.f, 0};
+      }
+      float v[BT][KW];
+#pragma unroll
+      for (int t = 0; t < BT; ++t)
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
           const int c = lane + 32 * k;
-          if (c < W) acc[k] += row_value(P, A, bt, cb, p, e, c, H);
+          v[t][k] = c < src[t].W ? src[t].sign * src[t].src[c] : 0.f;
         }
+#pragma unroll
+      for (int t = 0; t < BT; ++t) {
+        const int j = j0 + t;
+        const uint32_t key = kk[t];
+        if (j >= cnt || key >= kKeyDrop) {
+          done = true;
+          break;
+        }
+#pragma unroll
+        for (int k = 0; k < KW; ++k) acc[k] += v[t][k];
+        if (j + 1 < cnt && kk[t + 1] == key) continue;
+        // the segment [seg_start, j] ends here
+        const bool head = seg_start == 0 && prev == key;
+        const bool tail = j == cnt - 1 && next == key;
+        const int W = 2 * blk + 1 < A.part_slots ? key_width(key, H) : 0;
+        if (W == 0 && lane == 0) check_failed(A, 11, blk, A.part_slots);
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+          const int c = lane + 32 * k;
+          if (c < W) {
+            if (head) A.part[(size_t)(2 * blk) * A.row_w + c] = acc[k];
+            else if (tail) A.part[(size_t)(2 * blk + 1) * A.row_w + c] = acc[k];
+            else *key_dest(G, A, key, c, H) = acc[k];
+          }
+          acc[k] = 0.f;
+        }
+        seg_start = j + 1;
       }
-    }
-#pragma unroll
-    for (int k = 0; k < KW; ++k) {
-      const int c = lane + 32 * k;
-      if (c >= W) continue;
-      if (single) *row_dest(G, A, p, key, c, H) = acc[k];
-      else A.row_part[(size_t)u * A.row_w + c] = acc[k];
-    }
-  }
-  for (uint32_t u0 = u_rows + gw * 32; u0 < n_units; u0 += n_warps * 32) {
-    const uint32_t r0 = warp_find_run(s.unit_off, n_runs, u0, lane);
-    const uint32_t x = r0 + 1 + lane < n_runs ? s.unit_off[r0 + 1 + lane] : 0xffffffffu;
-    const uint32_t u = u0 + lane;
-    uint32_t d = 0;
-#pragma unroll 8
-    for (int j = 0; j < 32; ++j) d += __shfl_sync(kFull, x, j) <= u;
-    if (u >= n_units) continue;
-    const uint32_t r = r0 + d;
-    const uint32_t rbeg = s.run_start[r], rend = r + 1 < n_runs ? s.run_start[r + 1] : s.n;
-    const uint32_t key = s.keys[rbeg];
-    if (key >= kKeyDrop) continue;
-    const uint32_t beg = rbeg + (u - s.unit_off[r]) * kUnit, end = min(rend, beg + kUnit);
-    const bool tact = key >= kKeyTact;
-    const uint32_t base = tact ? cb.tact : cb.sparse, div = tact ? 2u : 7u;
-    float sum = 0.f;
-    uint32_t j = beg;
-    for (; j + 4 <= end; j += 4) {
-      float v[4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) v[t] = A.dl[(s.idx[j + t] - base) / div];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) sum += v[t];
-    }
-    for (; j < end; ++j) sum += A.dl[(s.idx[j] - base) / div];
-    if (run_units(s, r, n_runs, n_units) == 1) {
-      if (tact) G.g[L_TACT][key - kKeyTact] = sum;
-      else G.g[L_SPARSE][key - kKeySparse] = sum;
-    } else {
-      s.spart[u] = sum;
     }
   }
 }
 
-// Runs of several units add their unit partials in unit order: row runs one
-// warp each (lanes over columns), scalar runs one warp each (lanes over
-// units, then a fixed butterfly).  32 runs are screened per warp step.
+// Runs crossing block boundaries: the block holding a run's tail slot (the
+// run began in it) finds the run's last block (32 blocks probed per step)
+// and adds the tail partial and the following blocks' head partials in
+// block order.  32 blocks are screened per warp step.
 template <int NC>
-__global__ void __launch_bounds__(256) run_kernel(Grads G, Act A, Sorted s, int H) {
+__global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, int H) {
   constexpr int KW = NC > 2 ? NC : 2;
   const int lane = threadIdx.x & 31;
-  const uint32_t n_runs = *s.n_runs_d, n_units = *s.n_units_d, P0 = A.counters[0];
-  if (n_runs == 0) return;
-  const uint32_t r_rows = P0 < s.n ? s.run_of[P0] : n_runs;
+  const uint32_t n = min(*s.n_live, s.n_max);
+  const uint32_t n_blocks = (n + kSeg - 1) / kSeg;
   const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
-  for (uint32_t r0 = gw * 32; r0 < r_rows; r0 += n_warps * 32) {
-    const uint32_t r = r0 + lane;
-    uint32_t pending = __ballot_sync(kFull, r < r_rows && run_units(s, r, n_runs, n_units) > 1);
+  for (uint32_t b0 = gw * 32; b0 < n_blocks; b0 += n_warps * 32) {
+    const uint32_t blk = b0 + lane;
+    bool owner = false;
+    if (blk + 1 < n_blocks) {  // a full block with a successor
+      const uint32_t base = blk * kSeg;
+      const uint32_t kl = s.keys[base + kSeg - 1];
+      if (kl < kKeyDrop && s.keys[base + kSeg] == kl)
+        owner = !(s.keys[base] == kl && base > 0 && s.keys[base - 1] == kl);
+    }
+    uint32_t pending = __ballot_sync(kFull, owner);
     while (pending) {
-      const uint32_t rr = r0 + (uint32_t)(__ffs(pending) - 1);
+      const uint32_t ob = b0 + (uint32_t)(__ffs(pending) - 1);
       pending &= pending - 1;
-      const uint32_t u0 = s.unit_off[rr], u1 = rr + 1 < n_runs ? s.unit_off[rr + 1] : n_units;
-      const uint32_t key = s.keys[s.run_start[rr]];
-      const Problem p = problem_of(key);
-      const int W = row_width(p, H);
-      if (u1 > A.row_units_max) continue;  // flagged by unit_kernel
+      const uint32_t key = s.keys[ob * kSeg + kSeg - 1];
+      // last block q of the run: the run continues into block q + 1 while
+      // that block starts with the key
+      uint32_t q = ob + 1;
+      for (int round = 0; round < (1 << 20); ++round) {
+        const uint32_t probe = q + 1 + (uint32_t)lane;
+        const bool cont = probe < n_blocks && s.keys[probe * kSeg] == key;
+        const uint32_t bal = __ballot_sync(kFull, cont);
+        const int lead = bal == kFull ? 32 : __ffs(~bal) - 1;
+        q += (uint32_t)lead;
+        if (lead < 32) break;
+      }
+      const int W = 2 * q + 1 < A.part_slots ? key_width(key, H) : 0;
+      if (W == 0 && lane == 0) check_failed(A, 12, q, A.part_slots);
+      float sum[KW];
 #pragma unroll
       for (int k = 0; k < KW; ++k) {
         const int c = lane + 32 * k;
-        if (c >= W) continue;
-        float sum = A.row_part[(size_t)u0 * A.row_w + c];
-        for (uint32_t u = u0 + 1; u < u1; ++u) sum += A.row_part[(size_t)u * A.row_w + c];
-        *row_dest(G, A, p, key, c, H) = sum;
+        sum[k] = c < W ? A.part[(size_t)(2 * ob + 1) * A.row_w + c] : 0.f;
       }
-    }
-  }
-  for (uint32_t r0 = r_rows + gw * 32; r0 < n_runs; r0 += n_warps * 32) {
-    const uint32_t r = r0 + lane;
-    bool multi = r < n_runs && run_units(s, r, n_runs, n_units) > 1;
-    if (multi) multi = s.keys[s.run_start[r]] < kKeyDrop;
-    uint32_t pending = __ballot_sync(kFull, multi);
-    while (pending) {
-      const uint32_t rr = r0 + (uint32_t)(__ffs(pending) - 1);
-      pending &= pending - 1;
-      const uint32_t u0 = s.unit_off[rr], u1 = rr + 1 < n_runs ? s.unit_off[rr + 1] : n_units;
-      const uint32_t key = s.keys[s.run_start[rr]];
-      float sum = 0.f;
-      for (uint32_t u = u0 + lane; u < u1; u += 32) sum += s.spart[u];
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        if (key >= kKeyTact) G.g[L_TACT][key - kKeyTact] = sum;
-        else G.g[L_SPARSE][key - kKeySparse] = sum;
+      uint32_t b = ob + 1;
+      for (; b + 4 <= q + 1; b += 4) {
+        float x[4][KW];
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int k = 0; k < KW; ++k) {
+            const int c = lane + 32 * k;
+            x[t][k] = c < W ? A.part[(size_t)(2 * (b + t)) * A.row_w + c] : 0.f;
+          }
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+#pragma unroll
+          for (int k = 0; k < KW; ++k) sum[k] += x[t][k];
+      }
+      for (; b <= q; ++b)
+#pragma unroll
+        for (int k = 0; k < KW; ++k) {
+          const int c = lane + 32 * k;
+          if (c < W) sum[k] += A.part[(size_t)(2 * b) * A.row_w + c];
+        }
+#pragma unroll
+      for (int k = 0; k < KW; ++k) {
+        const int c = lane + 32 * k;
+        if (c < W) *key_dest(G, A, key, c, H) = sum[k];
       }
     }
   }
@@ -1188,10 +1347,9 @@ int64_t leaf_size(int leaf, int64_t H) {
 }
 
 struct Plan {
-  size_t small, keys, sort, row_part, tile_part;
-  size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
+  size_t small, keys, sort, part, tile_part;
+  size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, mrow, frow, pcnt, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
   size_t small_bytes, total;
-  uint32_t row_units_max;
   int row_w, max_tiles;
 };
 
@@ -1211,15 +1369,13 @@ Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   };
   const Bases cb = bases(B, F, M, T);
   const int64_t n = cb.n;
-  const int64_t n_rows = B * (6 * F + T + 4 * M);
-  p.row_units_max = (uint32_t)(kKeyRowsEnd + (n_rows + kUnit - 1) / kUnit + 1);
   p.row_w = (int)std::max<int64_t>(H, kTR);
   p.max_tiles = max_tiles(H);
   p.small_bytes = (kSmallCounters + kTileCounters) * 4 + (size_t)kInput * kFeatW * 4;
   p.small = take(p.small_bytes);
   p.keys = take((size_t)n * 4);
-  p.sort = take(scat::workspace_bytes(n, 1));
-  p.row_part = take((size_t)p.row_units_max * p.row_w * 4);
+  p.sort = take(scat::sort_bytes(n));
+  p.part = take((size_t)2 * ((n + kSeg - 1) / kSeg) * p.row_w * 4);
   p.tile_part = take((size_t)p.max_tiles * kSplits * kTO * kTC * 4);
   p.bp = take((size_t)B * H * 4);
   p.hid = take((size_t)B * H * 4);
@@ -1230,6 +1386,9 @@ Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   p.vl = take((size_t)B * 4 * 4);
   p.af = take((size_t)kInput * kAcc * 4);
   p.dl = take((size_t)B * M * 4);
+  p.mrow = take((size_t)B * M * kRowStride * 4);
+  p.frow = take((size_t)B * M * kRowStride * 4);
+  p.pcnt = take((size_t)B * 5 * F * 4);
   p.dvl = take((size_t)B * 4 * 4);
   p.dctx = take((size_t)B * kCtx * 4);
   p.cons = take((size_t)B * kPsp * 4);
@@ -1244,7 +1403,7 @@ Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
 
 bool dims_ok(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   if (!(H == 32 || H == 64 || H == 128 || H == 256 || H == 512)) return false;
-  if (B < 1 || F < 1 || M < 1 || T < 1 || M > 1024) return false;
+  if (B < 1 || F < 1 || M < 1 || T < 1 || M > 1024 || F > 256) return false;
   const double n = (double)B * (6.0 * F + T + 13.0 * M);
   return n < 2147483647.0;
 }
@@ -1268,18 +1427,20 @@ int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const 
   constexpr int H = 32 * NC;
   const int board_blocks = (int)((bt.B + kWarps - 1) / kWarps);
   const int af_blocks = (kInput + kWarps - 1) / kWarps;
-  fwd_kernel<NC><<<board_blocks + af_blocks, 32 * kWarps, 0, s>>>(P, bt, A, board_blocks, status);
+  fwd_kernel<NC><<<board_blocks + af_blocks, 32 * kWarps, (size_t)kWarps * fwd_smem_words(bt.F) * 4, s>>>(
+      P, bt, A, board_blocks, status);
   if (int st = check_launch_error("azt forward")) return st;
   policy_kernel<<<board_blocks, 32 * kWarps, (size_t)kWarps * bt.M * 4, s>>>(P, bt, A, H, ls, status);
   if (int st = check_launch_error("azt policy")) return st;
   bwd_kernel<NC><<<board_blocks, 32 * kWarps, 0, s>>>(P, bt, A);
   if (int st = check_launch_error("azt backward")) return st;
   if (side != s) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, join, 0));
-  const int unit_blocks = (int)std::min<int64_t>((A.row_units_max + 7) / 8, 148 * 16);
-  unit_kernel<NC><<<unit_blocks, 256, 0, s>>>(P, G, A, bt, cb, srt, H, status);
-  if (int st = check_launch_error("azt unit sums")) return st;
-  run_kernel<NC><<<148 * 4, 256, 0, s>>>(G, A, srt, H);
-  if (int st = check_launch_error("azt run sums")) return st;
+  const int64_t seg_blocks = (srt.n_max + kSeg - 1) / kSeg;
+  seg_kernel<NC><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((seg_blocks + 7) / 8, 148 * 32)), 256, 0, s>>>(
+      G, A, bt, cb, srt, H);
+  if (int st = check_launch_error("azt segment sums")) return st;
+  combine_kernel<NC><<<(unsigned)std::max<int64_t>(1, (seg_blocks + 255) / 256), 256, 0, s>>>(G, A, srt, H);
+  if (int st = check_launch_error("azt run combine")) return st;
   RedTable T{};
   T.K = (int)bt.B;
   add_prob(T, bt.rule, kRule, kRule, A.dpre, H, H, 0, G.g[L_RULE]);
@@ -1355,7 +1516,8 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   const cnnue_azt_batch& b = *batch;
   if (!dims_ok(hidden, b.batch, b.features, b.moves, b.threats))
     return set_error(CNNUE_ERR_INVALID_ARG,
-                     "cnnue_azt_step: hidden must be 32, 64, 128, 256 or 512, dims >= 1, moves <= 1024 "
+                     "cnnue_azt_step: hidden must be 32, 64, 128, 256 or 512, dims >= 1, moves <= 1024, "
+                     "features <= 256 "
                      "(hidden %lld, batch %lld, features %lld, moves %lld, threats %lld)",
                      (long long)hidden, (long long)b.batch, (long long)b.features, (long long)b.moves,
                      (long long)b.threats);
@@ -1396,17 +1558,19 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   A.tile_cnt = A.counters + kSmallCounters;
   A.pspaf = (float*)(A.tile_cnt + kTileCounters);
   A.keys = (uint32_t*)(w + pl.keys);
-  A.row_part = (float*)(w + pl.row_part);
+  A.part = (float*)(w + pl.part);
   A.tile_part = (float*)(w + pl.tile_part);
   A.bp = (float*)(w + pl.bp), A.hid = (float*)(w + pl.hid), A.rms = (float*)(w + pl.rms);
   A.vh = (float*)(w + pl.vh), A.ta = (float*)(w + pl.ta), A.ctx = (float*)(w + pl.ctx);
   A.vl = (float*)(w + pl.vl), A.af = (float*)(w + pl.af), A.dl = (float*)(w + pl.dl);
+  A.mrow = (float*)(w + pl.mrow), A.frow = (float*)(w + pl.frow), A.pcnt = (float*)(w + pl.pcnt);
   A.dvl = (float*)(w + pl.dvl), A.dctx = (float*)(w + pl.dctx), A.cons = (float*)(w + pl.cons);
   A.rec = (float*)(w + pl.rec), A.dbp = (float*)(w + pl.dbp), A.dpre = (float*)(w + pl.dpre);
   A.dta = (float*)(w + pl.dta), A.dvh = (float*)(w + pl.dvh);
-  A.row_units_max = pl.row_units_max;
   A.row_w = pl.row_w;
+  A.status = d_status;
   const Bases cb = bases(b.batch, b.features, b.moves, b.threats);
+  A.part_slots = (uint32_t)(2 * ((cb.n + kSeg - 1) / kSeg));
   const LossScale raw{std::max(value_weight, 0.f), std::max(policy_weight, 0.f)};
   const LossScale ls{raw.value / (float)b.batch, raw.policy / (float)b.batch};
 
@@ -1418,15 +1582,17 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
     CNNUE_CUDA_TRY(cudaStreamWaitEvent(side, e->fork, 0));
   }
   // side: keys of every table contribution, one joint sort with runs and units
-  const int64_t items = b.batch * (b.features + b.threats + b.moves);
-  const unsigned kb = (unsigned)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, 148 * 8));
-  keygen_kernel<<<kb, 256, 0, side>>>(bt, cb, A.keys, A.counters, d_status);
+  const int pool_blocks = (int)((b.batch + kWarps - 1) / kWarps);
+  const int64_t slots = b.batch * (b.threats + b.moves);
+  const int other_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((slots + 255) / 256, 148 * 8));
+  keygen_kernel<<<pool_blocks + other_blocks, 256, 0, side>>>(bt, cb, A.keys, A.pcnt, A.counters, d_status,
+                                                             pool_blocks);
   if (int st = check_launch_error("azt keys")) return st;
-  scat::Runs runs;
-  if (int st = scat::sort_runs(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &runs, kUnit)) return st;
+  Sorted srt{nullptr, nullptr, A.counters + 1, cb.n};
+  if (int st = scat::radix_sort(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &srt.keys, &srt.idx, A.counters + 1,
+                                kKeyDrop))
+    return st;
   if (side != s) CNNUE_CUDA_TRY(cudaEventRecord(e->join, side));
-  Sorted srt{runs.keys, runs.idx, runs.run_start, runs.unit_off, runs.n_runs, runs.n_units, runs.run_of,
-             runs.partial, cb.n};
   switch (hidden) {
     case 32: return launch_main<1>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
     case 64: return launch_main<2>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);

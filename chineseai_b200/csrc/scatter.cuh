@@ -114,16 +114,24 @@ int launch_scan(uint32_t* a, int64_t n, uint32_t* aux, cudaStream_t s) {
 }
 
 // ---- radix sort -------------------------------------------------------------
+// n_dev (optional): the live item count in device memory (<= n); keys >=
+// drop_key are skipped (as items past the end).
 __global__ void __launch_bounds__(kThreads) hist_kernel(const uint32_t* __restrict__ keys, int64_t n, int shift,
-                                                        int64_t nb, uint32_t* __restrict__ hist) {
+                                                        int64_t nb, uint32_t* __restrict__ hist,
+                                                        const uint32_t* __restrict__ n_dev = nullptr,
+                                                        uint32_t drop_key = 0xffffffffu) {
   __shared__ uint32_t h[kDigits];
   h[threadIdx.x] = 0;
+  if (n_dev && (int64_t)*n_dev < n) n = (int64_t)*n_dev;
   __syncthreads();
   const int64_t base = (int64_t)blockIdx.x * kBlockItems;
 #pragma unroll
   for (int r = 0; r < kItemsPerThread; ++r) {
     const int64_t i = base + r * kThreads + threadIdx.x;
-    if (i < n) atomicAdd(&h[(keys[i] >> shift) & 0xffu], 1u);  // counts are order-free
+    if (i < n) {
+      const uint32_t k = keys[i];
+      if (k < drop_key) atomicAdd(&h[(k >> shift) & 0xffu], 1u);  // counts are order-free
+    }
   }
   __syncthreads();
   hist[(size_t)threadIdx.x * nb + blockIdx.x] = h[threadIdx.x];  // digit-major
@@ -135,8 +143,11 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(const uint32_t* __res
                                                            const uint32_t* __restrict__ idx_in, int64_t n,
                                                            int shift, int64_t nb, const uint32_t* __restrict__ hist,
                                                            uint32_t* __restrict__ keys_out,
-                                                           uint32_t* __restrict__ idx_out) {
+                                                           uint32_t* __restrict__ idx_out,
+                                                           const uint32_t* __restrict__ n_dev = nullptr,
+                                                           uint32_t drop_key = 0xffffffffu) {
   constexpr int kWarps = kThreads / 32;
+  if (n_dev && (int64_t)*n_dev < n) n = (int64_t)*n_dev;
   __shared__ uint32_t base[kDigits];
   __shared__ uint32_t wcount[kWarps][kDigits];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -146,8 +157,8 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(const uint32_t* __res
     for (int i = threadIdx.x; i < kWarps * kDigits; i += kThreads) (&wcount[0][0])[i] = 0;
     __syncthreads();
     const int64_t i = b0 + r * kThreads + threadIdx.x;
-    const bool valid = i < n;
-    const uint32_t key = valid ? keys_in[i] : 0u;
+    const uint32_t key = i < n ? keys_in[i] : 0u;
+    const bool valid = i < n && key < drop_key;
     const uint32_t dig = valid ? (key >> shift) & 0xffu : 0x100u;  // 256 = no item
     const uint32_t peers = __match_any_sync(kFull, dig);
     const uint32_t rank = __popc(peers & ((1u << lane) - 1u));
@@ -157,8 +168,10 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(const uint32_t* __res
       uint32_t before = 0;
       for (int w = 0; w < warp; ++w) before += wcount[w][dig];
       const uint32_t slot = base[dig] + before + rank;
-      keys_out[slot] = key;
-      idx_out[slot] = idx_in ? idx_in[i] : (uint32_t)i;
+      if (slot < (uint64_t)n) {  // a self-check: the slots of n items are < n
+        keys_out[slot] = key;
+        idx_out[slot] = idx_in ? idx_in[i] : (uint32_t)i;
+      }
     }
     __syncthreads();
     uint32_t add = 0;
@@ -368,6 +381,59 @@ struct Runs {
 // Sorts (key, contribution) pairs stably by key and finds runs and units of
 // at most `unit` contributions (counts left in device memory).  Requires
 // 0 < n < 2^32 - 1.
+// Workspace of radix_sort for n pairs.
+inline size_t sort_bytes(int64_t n) {
+  const size_t nn = (size_t)(n > 0 ? n : 1);
+  const int64_t nb = n_blocks(n > 0 ? n : 1);
+  return 4 * align_up(nn * 4, 256) + align_up((size_t)nb * kDigits * 4, 256) + scan_bytes((int64_t)nb * kDigits);
+}
+
+// Stable LSD radix sort of (key, contribution index) pairs by key, as many
+// 8-bit passes as keys <= n_keys need; the sorted keys and indices are left
+// in ws (*keys_out, *idx_out).  Requires 0 < n < 2^32 - 1.  With d_live
+// (the number of keys below drop_key, in device memory) the first pass
+// drops the keys >= drop_key and the later passes sort the d_live others.
+int radix_sort(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s,
+               const uint32_t** keys_out, const uint32_t** idx_out, const uint32_t* d_live = nullptr,
+               uint32_t drop_key = 0xffffffffu) {
+  const size_t nn = (size_t)n;
+  const int64_t nb = n_blocks(n);
+  char* p = (char*)ws;
+  auto take = [&](size_t bytes) {
+    char* q = p;
+    p += align_up(bytes, 256);
+    return q;
+  };
+  uint32_t* k0 = (uint32_t*)take(nn * 4);
+  uint32_t* k1 = (uint32_t*)take(nn * 4);
+  uint32_t* i0 = (uint32_t*)take(nn * 4);
+  uint32_t* i1 = (uint32_t*)take(nn * 4);
+  uint32_t* hist = (uint32_t*)take((size_t)nb * kDigits * 4);
+  uint32_t* aux = (uint32_t*)p;
+  const int passes = key_passes(n_keys + 1);
+  const uint32_t* kin = keys;
+  const uint32_t* iin = nullptr;
+  uint32_t* kout = k0;
+  uint32_t* iout = i0;
+  for (int pass = 0; pass < passes; ++pass) {
+    const int shift = 8 * pass;
+    const uint32_t* nd = pass > 0 ? d_live : nullptr;
+    const uint32_t dk = pass == 0 && d_live ? drop_key : 0xffffffffu;
+    hist_kernel<<<(unsigned)nb, kThreads, 0, s>>>(kin, n, shift, nb, hist, nd, dk);
+    if (int st = check_launch_error("sort hist")) return st;
+    if (int st = launch_scan(hist, nb * kDigits, aux, s)) return st;
+    scatter_kernel<<<(unsigned)nb, kThreads, 0, s>>>(kin, iin, n, shift, nb, hist, kout, iout, nd, dk);
+    if (int st = check_launch_error("sort scatter")) return st;
+    kin = kout;
+    iin = iout;
+    kout = kout == k0 ? k1 : k0;
+    iout = iout == i0 ? i1 : i0;
+  }
+  *keys_out = kin;
+  *idx_out = iin;
+  return CNNUE_OK;
+}
+
 int sort_runs(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s, Runs* out,
               uint32_t unit = kUnit) {
   const size_t nn = (size_t)n;

@@ -63,6 +63,8 @@ constexpr uint32_t kKeyTact = kKeySparse + (uint32_t)kSparseLen;
 constexpr uint32_t kKeyDrop = kKeyTact + (uint32_t)kTactLen;
 constexpr int kMoveW = 16 + kAcc + 1;  // move row: move context, accumulator move, bias
 constexpr int kRowStride = 64;         // floats per stored move / feature gradient row
+constexpr int kMultBits = 11;          // trunk payload: board << 11 | multiplicity (<= 5 x 256)
+constexpr uint32_t kNegBit = 1u << 31; // feature payload: the row enters subtracted
 constexpr int kFeatW = kPsp + kAcc;    // feature row: consequence rows, accumulator features
 
 constexpr int kWarps = 8;  // warps per block of every per-board kernel
@@ -74,6 +76,7 @@ enum Leaf {
   L_TACT, kLeaves
 };
 static_assert(kLeaves == CNNUE_AZT_LEAVES, "leaf count");
+static_assert(kAcc == 32 && kVH == 96, "the forward's 32-output products");
 
 struct Params {
   const float* p[kLeaves];
@@ -120,7 +123,7 @@ struct Act {
   float *bp, *hid, *rms, *vh, *ta, *ctx, *vl, *af;      // forward
   float *dl, *dvl, *dctx, *cons, *rec;                  // loss
   float *mrow, *frow;                                   // per move: its move-row and feature-row gradients
-  float *pcnt;                                          // multiplicities of the derived trunk rows [B][5F]
+  uint32_t *pay;                                        // [n] payload of every contribution slot
   float *dbp, *dpre, *dta, *dvh;                        // backward
   float *pspaf;                                         // [1260][64] feature-row gradients
   float *part, *tile_part;                              // segment partials (head, tail per block), tile partials
@@ -285,14 +288,12 @@ __device__ __forceinline__ void axpy_row(const float* __restrict__ wrow, int lan
 #pragma unroll
   for (int i = 0; i < NC; ++i) x[i] = fmaf(a, w[i], x[i]);
 }
-// Outputs o < n_out (<= 32) of W[n_out][H] . x; lane l gets output l (0 for
-// l >= n_out).
+// The 32 outputs of W[32][H] . x; lane l gets output l.
 template <int NC>
-__device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, int n_out, const float (&x)[NC],
-                                          int lane) {
+__device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, const float (&x)[NC], int lane) {
   float v[32];
 #pragma unroll
-  for (int o = 0; o < 32; ++o) v[o] = o < n_out ? dot_row<NC>(W + (size_t)o * H, lane, x) : 0.f;
+  for (int o = 0; o < 32; ++o) v[o] = dot_row<NC>(W + (size_t)o * H, lane, x);
   reduce_scatter32(v, lane);
   return v[0];
 }
@@ -312,14 +313,17 @@ __device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, in
 // to exactly 0, so their logit gradient is exactly 0).  Indices outside
 // their tables set CNNUE_STATUS_BAD_INDEX and are dropped.  counters[0]
 // gets the number of row-problem contributions kept, counters[1] the number
-// of all kept (the sort drops the others in its first pass).
+// of all kept (the sort drops the others in its first pass).  Each slot also
+// gets its payload, carried through the sort: where its value row lives -
+// board << kMultBits | multiplicity (trunk), board (threat), move (move row,
+// scalar tables), move | kNegBit for a subtracted feature row.
 constexpr int kDerived = kTrunkRows - kInput;  // 285
 // Shared words per warp of the forward's row list: the derived-row histogram
 // (kDerived + 1, even) and up to F + kDerived (row, multiplicity) pairs.
 __host__ __device__ inline int64_t fwd_smem_words(int64_t F) { return kDerived + 1 + 2 * (F + kDerived); }
 
 __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_t* __restrict__ keys,
-                                                     float* __restrict__ pcnt, uint32_t* __restrict__ counters,
+                                                     uint32_t* __restrict__ pay, uint32_t* __restrict__ counters,
                                                      uint32_t* __restrict__ status, int pool_blocks) {
   __shared__ uint32_t hist[kWarps][kDerived];
   __shared__ uint32_t part[2][kWarps];
@@ -337,6 +341,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
         const int r = pool_rows(bt.fi[b * bt.F + i], rows);
         bad |= r < 0;
         keys[cb.pool + b * bt.F + i] = r > 0 ? kKeyPool + rows[0] : kKeyDrop;
+        pay[cb.pool + b * bt.F + i] = (uint32_t)b << kMultBits | 1u;
         if (r > 0) {
           ++live;
 #pragma unroll
@@ -355,7 +360,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
           const uint32_t pos = used + __popc(m & ((1u << lane) - 1u));
           if (pos < slots) {
             keys[dkey + pos] = kKeyPool + kInput + bin;
-            pcnt[b * slots + pos] = (float)c;
+            pay[dkey + pos] = (uint32_t)b << kMultBits | c;
           } else {
             atomicOr(status, CNNUE_STATUS_INTERNAL);
           }
@@ -375,6 +380,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
         const bool ok = idx < (uint32_t)kVocab;
         bad |= !ok && idx != kPad;
         keys[cb.threat + t] = ok ? kKeyThreat + idx : kKeyDrop;
+        pay[cb.threat + t] = (uint32_t)(t / bt.T);
         rows_kept += ok;
         live += ok;
       } else {
@@ -384,11 +390,15 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
         bad |= it.policy && !ok;
         const bool on = it.policy && ok;
         keys[cb.move + u] = on ? kKeyMove + it.mv : kKeyDrop;
+        pay[cb.move + u] = (uint32_t)u;
         const bool feat = on && it.move;
         uint32_t* fk = keys + cb.feat + u * 3;
         fk[0] = feat ? kKeyFeat + it.to : kKeyDrop;
         fk[1] = feat ? kKeyFeat + it.from : kKeyDrop;
         fk[2] = feat && it.capture ? kKeyFeat + it.cap : kKeyDrop;
+        pay[cb.feat + u * 3] = (uint32_t)u;
+        pay[cb.feat + u * 3 + 1] = (uint32_t)u | kNegBit;
+        pay[cb.feat + u * 3 + 2] = (uint32_t)u | kNegBit;
         const uint32_t rk = on + (feat ? 2 + it.capture : 0);
         rows_kept += rk;
         live += rk;
@@ -399,6 +409,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
           const bool sok = sx >= 0 && sx < kSparseLen;
           bad |= !sok;
           keys[cb.sparse + u * 7 + j] = sok && !drop ? kKeySparse + (uint32_t)sx : kKeyDrop;
+          pay[cb.sparse + u * 7 + j] = (uint32_t)u;
           live += sok && !drop;
         }
 #pragma unroll
@@ -407,6 +418,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
           const bool sok = sx >= 0 && sx < kTactLen;
           bad |= !sok;
           keys[cb.tact + u * 2 + j] = sok && !drop ? kKeyTact + (uint32_t)sx : kKeyDrop;
+          pay[cb.tact + u * 2 + j] = (uint32_t)u;
           live += sok && !drop;
         }
       }
@@ -451,7 +463,7 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
     if (r >= kInput) return;
     float x[NC];
     ld_row<NC>(P.p[L_FT] + (size_t)r * H, lane, x);
-    A.af[(size_t)r * kAcc + lane] = matvec32<NC>(P.p[L_PAH], H, kAcc, x, lane);
+    A.af[(size_t)r * kAcc + lane] = matvec32<NC>(P.p[L_PAH], H, x, lane);
     return;
   }
   const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
@@ -529,26 +541,33 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
 #pragma unroll
   for (int c = 0; c < NC; ++c) h[c] = h[c] / rms;
   // accumulator context and value head
-  const float acc_ctx = matvec32<NC>(P.p[L_PAH], H, kAcc, bp, lane);
+  const float acc_ctx = matvec32<NC>(P.p[L_PAH], H, bp, lane);
   float vh[3];
 #pragma unroll
   for (int g = 0; g < 3; ++g)
-    vh[g] = fmaxf(matvec32<NC>(P.p[L_VHH] + (size_t)32 * g * H, H, 32, h, lane) + __ldg(P.p[L_VHB] + 32 * g + lane),
+    vh[g] = fmaxf(matvec32<NC>(P.p[L_VHH] + (size_t)32 * g * H, H, h, lane) + __ldg(P.p[L_VHB] + 32 * g + lane),
                   0.f);
-  // threat accumulator: lane owns columns 2 lane, 2 lane + 1
+  // threat accumulator: lane owns columns 2 lane, 2 lane + 1; indices fetched
+  // 32 at a time (one per lane), rows loaded eight at a time
   float t0 = 0.f, t1 = 0.f;
   for (int64_t i0 = 0; i0 < bt.T; i0 += 32) {
     const uint32_t mine = i0 + lane < bt.T ? bt.ti[b * bt.T + i0 + lane] : kPad;
+    bad |= mine >= (uint32_t)kVocab && mine != kPad;
     const int cnt = (int)(bt.T - i0 < 32 ? bt.T - i0 : 32);
-    for (int j = 0; j < cnt; ++j) {
-      const uint32_t idx = __shfl_sync(kFull, mine, j);
-      if (idx >= (uint32_t)kVocab) {
-        bad |= idx != kPad;
-        continue;
+    for (int j0 = 0; j0 < cnt; j0 += 8) {
+      float2 v[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        const uint32_t idx = __shfl_sync(kFull, mine, (j0 + t) & 31);
+        v[t] = j0 + t < cnt && idx < (uint32_t)kVocab
+                   ? __ldg(reinterpret_cast<const float2*>(P.p[L_TE] + (size_t)idx * kTR) + lane)
+                   : make_float2(0.f, 0.f);
       }
-      const float2 v = __ldg(reinterpret_cast<const float2*>(P.p[L_TE] + (size_t)idx * kTR) + lane);
-      t0 += v.x;
-      t1 += v.y;
+#pragma unroll
+      for (int t = 0; t < 8; ++t) {
+        t0 += v[t].x;
+        t1 += v[t].y;
+      }
     }
   }
   const float a0 = fminf(fmaxf(t0, 0.f), 1.f), a1 = fminf(fmaxf(t1, 0.f), 1.f);
@@ -895,66 +914,43 @@ __global__ void __launch_bounds__(32 * kWarps) bwd_kernel(Params P, Batch bt, Ac
 // slot.  The combine kernel then gives every run crossing a block boundary to
 // one warp, which adds the run's tail partial and the head partials of the
 // following blocks in block order.  Every contribution's value is a row (or
-// scalar) already in memory: the board gradient of the feature pool, the
-// threat gradient, the move's move row / signed feature row, or dlogit.
+// scalar) already in memory, found from the payload it carries through the
+// sort: the board gradient times a multiplicity (trunk rows), the threat
+// gradient, the move's move row or signed feature row, or dlogit.
 constexpr int kSeg = 64;
 
 struct Sorted {
   const uint32_t* keys;    // [n_live] sorted keys
-  const uint32_t* idx;     // [n_live] contribution of each sorted slot
+  const uint32_t* pay;     // [n_live] payload of each sorted slot
   const uint32_t* n_live;  // device word: contributions kept
   uint32_t n_max;          // all contribution slots (bounds n_live)
 };
 
-// Where contribution e (of key `key`) reads its row: src[c] * sign, c < W.
+// The value row of a contribution: src[c] * mult for c < W (W = 0: none).
 struct Src {
   const float* src;
-  float sign;
+  float mult;
   int W;
 };
-__device__ __forceinline__ Src source(const Act& A, const Batch& bt, const Bases& cb, uint32_t key, uint32_t e,
-                                      int H) {
+__device__ __forceinline__ Src source(const Act& A, const Batch& bt, uint32_t key, uint32_t pay, int H) {
   const uint32_t nbm = (uint32_t)(bt.B * bt.M);
-  if (key < kKeyThreat) {
-    const uint32_t nf = (uint32_t)(bt.B * bt.F);
-    if (e < nf) return {A.dbp + (size_t)(e / (uint32_t)bt.F) * H, 1.f, H};
-    const uint32_t d = e - nf;  // a derived row: board d / 5F, multiplicity pcnt[d]
-    if (d >= (uint32_t)(bt.B * 5 * bt.F)) {
-      check_failed(A, 6, key, e);
-      return {A.dl, 0.f, 0};
-    }
-    return {A.dbp + (size_t)(d / (uint32_t)(5 * bt.F)) * H, A.pcnt[d], H};
-  }
   if (key < kKeyMove) {
-    if (e < cb.threat || e >= cb.move) {
-      check_failed(A, 7, key, e);
+    const bool trunk = key < kKeyThreat;
+    const uint32_t b = trunk ? pay >> kMultBits : pay;
+    if (b >= (uint32_t)bt.B) {
+      check_failed(A, trunk ? 6 : 7, key, pay);
       return {A.dl, 0.f, 0};
     }
-    return {A.dta + (size_t)((e - cb.threat) / (uint32_t)bt.T) * kTR, 1.f, kTR};
+    return trunk ? Src{A.dbp + (size_t)b * H, (float)(pay & ((1u << kMultBits) - 1u)), H}
+                 : Src{A.dta + (size_t)b * kTR, 1.f, kTR};
   }
-  if (key < kKeyFeat) {
-    if (e < cb.move || e >= cb.feat) {
-      check_failed(A, 8, key, e);
-      return {A.dl, 0.f, 0};
-    }
-    return {A.mrow + (size_t)(e - cb.move) * kRowStride, 1.f, kMoveW};
-  }
-  if (key < kKeyRowsEnd) {
-    if (e < cb.feat || e >= cb.sparse) {
-      check_failed(A, 9, key, e);
-      return {A.dl, 0.f, 0};
-    }
-    const uint32_t v = e - cb.feat, u = v / 3u;
-    return {A.frow + (size_t)u * kRowStride, v - 3u * u == 0 ? 1.f : -1.f, kFeatW};
-  }
-  const bool tact = key >= kKeyTact;
-  const uint32_t lo = tact ? cb.tact : cb.sparse, hi = tact ? cb.n : cb.tact;
-  if (e < lo || e >= hi || key >= kKeyDrop) {
-    check_failed(A, 10, key, e);
+  const uint32_t u = key < kKeyRowsEnd ? pay & ~kNegBit : pay;
+  if (u >= nbm || key >= kKeyDrop) {
+    check_failed(A, 8, key, pay);
     return {A.dl, 0.f, 0};
   }
-  const uint32_t u = (e - lo) / (tact ? 2u : 7u);
-  (void)nbm;
+  if (key < kKeyFeat) return {A.mrow + (size_t)u * kRowStride, 1.f, kMoveW};
+  if (key < kKeyRowsEnd) return {A.frow + (size_t)u * kRowStride, (pay & kNegBit) ? -1.f : 1.f, kFeatW};
   return {A.dl + u, 1.f, 1};
 }
 __device__ __forceinline__ int key_width(uint32_t key, int H) {
@@ -973,7 +969,7 @@ __device__ __forceinline__ float* key_dest(const Grads& G, const Act& A, uint32_
 }
 
 template <int NC>
-__global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Bases cb, Sorted s, int H) {
+__global__ void __launch_bounds__(256, 3) seg_kernel(Grads G, Act A, Batch bt, Sorted s, int H) {
   constexpr int KW = NC > 2 ? NC : 2;   // column chunks of the widest row: max(H, 64) / 32
   constexpr int BT = NC > 4 ? 4 : 8;    // positions whose loads are in flight together
   const int lane = threadIdx.x & 31;
@@ -986,40 +982,63 @@ __global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Base
     const int cnt = n - base < (uint32_t)kSeg ? (int)(n - base) : kSeg;
     const uint32_t k_lo = lane < cnt ? s.keys[base + lane] : kKeyDrop;
     const uint32_t k_hi = 32 + lane < cnt ? s.keys[base + 32 + lane] : kKeyDrop;
-    const uint32_t e_lo = lane < cnt ? s.idx[base + lane] : 0u;
-    const uint32_t e_hi = 32 + lane < cnt ? s.idx[base + 32 + lane] : 0u;
+    const uint32_t p_lo = lane < cnt ? s.pay[base + lane] : 0u;
+    const uint32_t p_hi = 32 + lane < cnt ? s.pay[base + 32 + lane] : 0u;
     const uint32_t first = __shfl_sync(kFull, k_lo, 0);
     if (first >= kKeyDrop) continue;  // keys ascend: the block is all dropped
     const uint32_t prev = base > 0 ? s.keys[base - 1] : 0xffffffffu;
     const uint32_t next = base + cnt < n ? s.keys[base + cnt] : 0xffffffffu;
+    if (2 * blk + 1 >= A.part_slots) {
+      if (lane == 0) check_failed(A, 11, blk, A.part_slots);
+      continue;
+    }
+    float* head_slot = A.part + (size_t)(2 * blk) * A.row_w;
+    float* tail_slot = head_slot + A.row_w;
     if (first >= kKeyRowsEnd) {
       // scalar block: each lane loads its two positions, then one pass in order
       float v_lo = 0.f, v_hi = 0.f;
       if (k_lo < kKeyDrop) {
-        const Src q = source(A, bt, cb, k_lo, e_lo, H);
+        const Src q = source(A, bt, k_lo, p_lo, H);
         if (q.W) v_lo = *q.src;
       }
       if (k_hi < kKeyDrop) {
-        const Src q = source(A, bt, cb, k_hi, e_hi, H);
+        const Src q = source(A, bt, k_hi, p_hi, H);
         if (q.W) v_hi = *q.src;
       }
-      float acc = 0.f;
-      int seg_start = 0;
-      for (int j = 0; j < cnt; ++j) {
-        const uint32_t key = __shfl_sync(kFull, j < 32 ? k_lo : k_hi, j & 31);
-        const uint32_t kn = j + 1 < cnt ? __shfl_sync(kFull, j + 1 < 32 ? k_lo : k_hi, (j + 1) & 31) : next;
-        const float v = __shfl_sync(kFull, j < 32 ? v_lo : v_hi, j & 31);
-        if (key >= kKeyDrop) break;
-        acc += v;
-        if (j + 1 < cnt && kn == key) continue;
-        if (lane == 0) {
-          if (2 * blk + 1 >= A.part_slots) check_failed(A, 11, blk, A.part_slots);
-          else if (seg_start == 0 && prev == key) A.part[(size_t)(2 * blk) * A.row_w] = acc;
-          else if (j == cnt - 1 && next == key) A.part[(size_t)(2 * blk + 1) * A.row_w] = acc;
-          else *key_dest(G, A, key, 0, H) = acc;
-        }
-        acc = 0.f;
-        seg_start = j + 1;
+      // segmented inclusive scans over the lanes (a fixed shuffle tree), one
+      // per half of the block; every shuffle runs on all lanes
+      const uint32_t lt = (1u << lane) - 1u, me = 1u << lane;
+      const uint32_t klo_up = __shfl_up_sync(kFull, k_lo, 1), khi_up = __shfl_up_sync(kFull, k_hi, 1);
+      const uint32_t klo_dn = __shfl_down_sync(kFull, k_lo, 1), khi_dn = __shfl_down_sync(kFull, k_hi, 1);
+      const uint32_t khi_0 = __shfl_sync(kFull, k_hi, 0), klo_31 = __shfl_sync(kFull, k_lo, 31);
+      const uint32_t bal_lo = __ballot_sync(kFull, lane == 0 || klo_up != k_lo);
+      const uint32_t bal_hi = __ballot_sync(kFull, lane == 0 || khi_up != k_hi);
+      const int seg_lo = 31 - __clz(bal_lo & (lt | me)), seg_hi = 31 - __clz(bal_hi & (lt | me));
+      float x_lo = v_lo, x_hi = v_hi;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y_lo = __shfl_up_sync(kFull, x_lo, o), y_hi = __shfl_up_sync(kFull, x_hi, o);
+        if (lane - o >= seg_lo) x_lo += y_lo;
+        if (lane - o >= seg_hi) x_hi += y_hi;
+      }
+      // the high half's first segment continues the low half's last one
+      const float carry = __shfl_sync(kFull, x_lo, 31);
+      const int first_hi_end = (bal_hi & ~1u) ? __ffs(bal_hi & ~1u) - 2 : 31;
+      if (cnt > 32 && khi_0 == klo_31 && lane <= first_hi_end) x_hi += carry;
+      const uint32_t kfirst = __shfl_sync(kFull, k_lo, 0);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int j = 32 * half + lane;
+        const uint32_t key = half ? k_hi : k_lo;
+        const uint32_t kn = half ? khi_dn : (lane < 31 ? klo_dn : khi_0);
+        const bool end = j < cnt && key < kKeyDrop && (j == cnt - 1 || kn != key);
+        if (!end) continue;
+        const float x = half ? x_hi : x_lo;
+        const bool head = key == kfirst && prev == key;  // keys ascend: such a segment starts the block
+        const bool tail = j == cnt - 1 && next == key;
+        if (head) *head_slot = x;
+        else if (tail) *tail_slot = x;
+        else *key_dest(G, A, key, 0, H) = x;
       }
       continue;
     }
@@ -1036,21 +1055,18 @@ __global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Base
         const uint32_t k = __shfl_sync(kFull, (j & 32) ? k_hi : k_lo, j & 31);
         kk[t] = j < cnt ? k : next;
       }
-      Src src[BT];
+      float v[BT][KW];
 #pragma unroll
       for (int t = 0; t < BT; ++t) {
         const int j = j0 + t;
-        const uint32_t e = __shfl_sync(kFull, (j & 32) ? e_hi : e_lo, j & 31);
-        src[t] = j < cnt && kk[t] < kKeyDrop ? source(A, bt, cb, kk[t], e, H) : Src{A.dl, 0.f, 0};
-      }
-      float v[BT][KW];
-#pragma unroll
-      for (int t = 0; t < BT; ++t)
+        const uint32_t py = __shfl_sync(kFull, (j & 32) ? p_hi : p_lo, j & 31);
+        const Src q = j < cnt && kk[t] < kKeyDrop ? source(A, bt, kk[t], py, H) : Src{A.dl, 0.f, 0};
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
           const int c = lane + 32 * k;
-          v[t][k] = c < src[t].W ? src[t].sign * src[t].src[c] : 0.f;
+          v[t][k] = c < q.W ? q.mult * q.src[c] : 0.f;
         }
+      }
 #pragma unroll
       for (int t = 0; t < BT; ++t) {
         const int j = j0 + t;
@@ -1065,14 +1081,13 @@ __global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Base
         // the segment [seg_start, j] ends here
         const bool head = seg_start == 0 && prev == key;
         const bool tail = j == cnt - 1 && next == key;
-        const int W = 2 * blk + 1 < A.part_slots ? key_width(key, H) : 0;
-        if (W == 0 && lane == 0) check_failed(A, 11, blk, A.part_slots);
+        const int W = key_width(key, H);
+        float* out = head ? head_slot : tail_slot;
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
           const int c = lane + 32 * k;
           if (c < W) {
-            if (head) A.part[(size_t)(2 * blk) * A.row_w + c] = acc[k];
-            else if (tail) A.part[(size_t)(2 * blk + 1) * A.row_w + c] = acc[k];
+            if (head || tail) out[c] = acc[k];
             else *key_dest(G, A, key, c, H) = acc[k];
           }
           acc[k] = 0.f;
@@ -1083,10 +1098,10 @@ __global__ void __launch_bounds__(256) seg_kernel(Grads G, Act A, Batch bt, Base
   }
 }
 
-// Runs crossing block boundaries: the block holding a run's tail slot (the
-// run began in it) finds the run's last block (32 blocks probed per step)
-// and adds the tail partial and the following blocks' head partials in
-// block order.  32 blocks are screened per warp step.
+// Runs crossing block boundaries, one warp per block: the block holding a
+// run's tail slot (the run began in it) finds the run's last block (32
+// blocks probed per step) and adds the tail partial and the following
+// blocks' head partials in block order.
 template <int NC>
 __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, int H) {
   constexpr int KW = NC > 2 ? NC : 2;
@@ -1095,65 +1110,56 @@ __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, 
   const uint32_t n_blocks = (n + kSeg - 1) / kSeg;
   const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
-  for (uint32_t b0 = gw * 32; b0 < n_blocks; b0 += n_warps * 32) {
-    const uint32_t blk = b0 + lane;
-    bool owner = false;
-    if (blk + 1 < n_blocks) {  // a full block with a successor
-      const uint32_t base = blk * kSeg;
-      const uint32_t kl = s.keys[base + kSeg - 1];
-      if (kl < kKeyDrop && s.keys[base + kSeg] == kl)
-        owner = !(s.keys[base] == kl && base > 0 && s.keys[base - 1] == kl);
+  for (uint32_t ob = gw; ob + 1 < n_blocks; ob += n_warps) {  // a full block with a successor
+    const uint32_t base = ob * kSeg;
+    const uint32_t key = s.keys[base + kSeg - 1], kn = s.keys[base + kSeg], k0 = s.keys[base];
+    const uint32_t kp = base > 0 ? s.keys[base - 1] : 0xffffffffu;
+    if (key >= kKeyDrop || kn != key) continue;
+    if (k0 == key && kp == key) continue;  // the run began in an earlier block
+    // last block q of the run: the run continues into block q + 1 while that
+    // block starts with the key
+    uint32_t q = ob + 1;
+    for (int round = 0; round < (1 << 20); ++round) {
+      const uint32_t probe = q + 1 + (uint32_t)lane;
+      const bool cont = probe < n_blocks && s.keys[probe * kSeg] == key;
+      const uint32_t bal = __ballot_sync(kFull, cont);
+      const int lead = bal == kFull ? 32 : __ffs(~bal) - 1;
+      q += (uint32_t)lead;
+      if (lead < 32) break;
     }
-    uint32_t pending = __ballot_sync(kFull, owner);
-    while (pending) {
-      const uint32_t ob = b0 + (uint32_t)(__ffs(pending) - 1);
-      pending &= pending - 1;
-      const uint32_t key = s.keys[ob * kSeg + kSeg - 1];
-      // last block q of the run: the run continues into block q + 1 while
-      // that block starts with the key
-      uint32_t q = ob + 1;
-      for (int round = 0; round < (1 << 20); ++round) {
-        const uint32_t probe = q + 1 + (uint32_t)lane;
-        const bool cont = probe < n_blocks && s.keys[probe * kSeg] == key;
-        const uint32_t bal = __ballot_sync(kFull, cont);
-        const int lead = bal == kFull ? 32 : __ffs(~bal) - 1;
-        q += (uint32_t)lead;
-        if (lead < 32) break;
-      }
-      const int W = 2 * q + 1 < A.part_slots ? key_width(key, H) : 0;
-      if (W == 0 && lane == 0) check_failed(A, 12, q, A.part_slots);
-      float sum[KW];
+    const int W = 2 * q + 1 < A.part_slots ? key_width(key, H) : 0;
+    if (W == 0 && lane == 0) check_failed(A, 12, q, A.part_slots);
+    float sum[KW];
 #pragma unroll
-      for (int k = 0; k < KW; ++k) {
-        const int c = lane + 32 * k;
-        sum[k] = c < W ? A.part[(size_t)(2 * ob + 1) * A.row_w + c] : 0.f;
-      }
-      uint32_t b = ob + 1;
-      for (; b + 4 <= q + 1; b += 4) {
-        float x[4][KW];
+    for (int k = 0; k < KW; ++k) {
+      const int c = lane + 32 * k;
+      sum[k] = c < W ? A.part[(size_t)(2 * ob + 1) * A.row_w + c] : 0.f;
+    }
+    uint32_t b = ob + 1;
+    for (; b + 4 <= q + 1; b += 4) {
+      float x[4][KW];
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int k = 0; k < KW; ++k) {
-            const int c = lane + 32 * k;
-            x[t][k] = c < W ? A.part[(size_t)(2 * (b + t)) * A.row_w + c] : 0.f;
-          }
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int k = 0; k < KW; ++k) sum[k] += x[t][k];
-      }
-      for (; b <= q; ++b)
+      for (int t = 0; t < 4; ++t)
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
           const int c = lane + 32 * k;
-          if (c < W) sum[k] += A.part[(size_t)(2 * b) * A.row_w + c];
+          x[t][k] = c < W ? A.part[(size_t)(2 * (b + t)) * A.row_w + c] : 0.f;
         }
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+#pragma unroll
+        for (int k = 0; k < KW; ++k) sum[k] += x[t][k];
+    }
+    for (; b <= q; ++b)
 #pragma unroll
       for (int k = 0; k < KW; ++k) {
         const int c = lane + 32 * k;
-        if (c < W) *key_dest(G, A, key, c, H) = sum[k];
+        if (c < W) sum[k] += A.part[(size_t)(2 * b) * A.row_w + c];
       }
+#pragma unroll
+    for (int k = 0; k < KW; ++k) {
+      const int c = lane + 32 * k;
+      if (c < W) *key_dest(G, A, key, c, H) = sum[k];
     }
   }
 }
@@ -1200,26 +1206,46 @@ __device__ void tile_block(const RedTable& T, Act& A, int tile, int split) {
   const int k_beg = split * chunk, k_end = min(K, k_beg + chunk);
   const int tid = threadIdx.x, to = tid / 16, tc = (tid % 16) * 4;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int k0 = k_beg; k0 < k_end; k0 += kTK) {
-    for (int i = tid; i < kTK * kTO; i += 256) {
-      const int kk = i / kTO, oo = i % kTO, k = k0 + kk, o = o0 + oo;
+  // one chunk of kTK rows of A (16 columns) and X (64 columns) per step; the
+  // next chunk's loads are issued into registers before this one's products
+  constexpr int kAL = kTK * kTO / 256, kXL = kTK * kTC / 256;  // loads per thread: 2, 8
+  float ra[kAL], rx[kXL];
+  auto fetch = [&](int k0) {
+#pragma unroll
+    for (int l = 0; l < kAL; ++l) {
+      const int i = tid + 256 * l, kk = i / kTO, oo = i % kTO, k = k0 + kk, o = o0 + oo;
       float v = 0.f;
       if (k < k_end && o < q.O) {
         if (k < T.K) v = q.a ? q.a[(size_t)k * q.lda + o] : 1.f;
         else v = q.a2[(size_t)(k - T.K) * q.lda2 + o];
       }
-      As[kk][oo] = v;
+      ra[l] = v;
     }
-    for (int i = tid; i < kTK * kTC; i += 256) {
-      const int kk = i / kTC, cc = i % kTC, k = k0 + kk, c = c0 + cc;
+#pragma unroll
+    for (int l = 0; l < kXL; ++l) {
+      const int i = tid + 256 * l, kk = i / kTC, cc = i % kTC, k = k0 + kk, c = c0 + cc;
       float v = 0.f;
       if (k < k_end && c < q.C) {
         if (k < T.K) v = q.xpair ? pair_of(q.x + (size_t)k * kTR, c) : q.x[(size_t)k * q.ldx + c];
         else v = q.x2[(size_t)(k - T.K) * q.ldx2 + c];
       }
-      Xs[kk][cc] = v;
+      rx[l] = v;
+    }
+  };
+  if (k_beg < k_end) fetch(k_beg);
+  for (int k0 = k_beg; k0 < k_end; k0 += kTK) {
+#pragma unroll
+    for (int l = 0; l < kAL; ++l) {
+      const int i = tid + 256 * l;
+      As[i / kTO][i % kTO] = ra[l];
+    }
+#pragma unroll
+    for (int l = 0; l < kXL; ++l) {
+      const int i = tid + 256 * l;
+      Xs[i / kTC][i % kTC] = rx[l];
     }
     __syncthreads();
+    if (k0 + kTK < k_end) fetch(k0 + kTK);
 #pragma unroll 8
     for (int kk = 0; kk < kTK; ++kk) {
       const float a = As[kk][to];
@@ -1348,7 +1374,7 @@ int64_t leaf_size(int leaf, int64_t H) {
 
 struct Plan {
   size_t small, keys, sort, part, tile_part;
-  size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, mrow, frow, pcnt, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
+  size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, mrow, frow, pay, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
   size_t small_bytes, total;
   int row_w, max_tiles;
 };
@@ -1388,7 +1414,7 @@ Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   p.dl = take((size_t)B * M * 4);
   p.mrow = take((size_t)B * M * kRowStride * 4);
   p.frow = take((size_t)B * M * kRowStride * 4);
-  p.pcnt = take((size_t)B * 5 * F * 4);
+  p.pay = take((size_t)n * 4);
   p.dvl = take((size_t)B * 4 * 4);
   p.dctx = take((size_t)B * kCtx * 4);
   p.cons = take((size_t)B * kPsp * 4);
@@ -1405,7 +1431,7 @@ bool dims_ok(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   if (!(H == 32 || H == 64 || H == 128 || H == 256 || H == 512)) return false;
   if (B < 1 || F < 1 || M < 1 || T < 1 || M > 1024 || F > 256) return false;
   const double n = (double)B * (6.0 * F + T + 13.0 * M);
-  return n < 2147483647.0;
+  return n < 2147483647.0 && B < (1 << (32 - kMultBits));
 }
 
 void add_prob(RedTable& T, const float* a, int lda, int O, const float* x, int ldx, int C, int xpair, float* out,
@@ -1436,10 +1462,10 @@ int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const 
   if (int st = check_launch_error("azt backward")) return st;
   if (side != s) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, join, 0));
   const int64_t seg_blocks = (srt.n_max + kSeg - 1) / kSeg;
-  seg_kernel<NC><<<(unsigned)std::max<int64_t>(1, std::min<int64_t>((seg_blocks + 7) / 8, 148 * 32)), 256, 0, s>>>(
-      G, A, bt, cb, srt, H);
+  const unsigned seg_grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((seg_blocks + 7) / 8, 148 * 32));
+  seg_kernel<NC><<<seg_grid, 256, 0, s>>>(G, A, bt, srt, H);
   if (int st = check_launch_error("azt segment sums")) return st;
-  combine_kernel<NC><<<(unsigned)std::max<int64_t>(1, (seg_blocks + 255) / 256), 256, 0, s>>>(G, A, srt, H);
+  combine_kernel<NC><<<seg_grid, 256, 0, s>>>(G, A, srt, H);
   if (int st = check_launch_error("azt run combine")) return st;
   RedTable T{};
   T.K = (int)bt.B;
@@ -1563,7 +1589,7 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   A.bp = (float*)(w + pl.bp), A.hid = (float*)(w + pl.hid), A.rms = (float*)(w + pl.rms);
   A.vh = (float*)(w + pl.vh), A.ta = (float*)(w + pl.ta), A.ctx = (float*)(w + pl.ctx);
   A.vl = (float*)(w + pl.vl), A.af = (float*)(w + pl.af), A.dl = (float*)(w + pl.dl);
-  A.mrow = (float*)(w + pl.mrow), A.frow = (float*)(w + pl.frow), A.pcnt = (float*)(w + pl.pcnt);
+  A.mrow = (float*)(w + pl.mrow), A.frow = (float*)(w + pl.frow), A.pay = (uint32_t*)(w + pl.pay);
   A.dvl = (float*)(w + pl.dvl), A.dctx = (float*)(w + pl.dctx), A.cons = (float*)(w + pl.cons);
   A.rec = (float*)(w + pl.rec), A.dbp = (float*)(w + pl.dbp), A.dpre = (float*)(w + pl.dpre);
   A.dta = (float*)(w + pl.dta), A.dvh = (float*)(w + pl.dvh);
@@ -1585,12 +1611,12 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   const int pool_blocks = (int)((b.batch + kWarps - 1) / kWarps);
   const int64_t slots = b.batch * (b.threats + b.moves);
   const int other_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((slots + 255) / 256, 148 * 8));
-  keygen_kernel<<<pool_blocks + other_blocks, 256, 0, side>>>(bt, cb, A.keys, A.pcnt, A.counters, d_status,
+  keygen_kernel<<<pool_blocks + other_blocks, 256, 0, side>>>(bt, cb, A.keys, A.pay, A.counters, d_status,
                                                              pool_blocks);
   if (int st = check_launch_error("azt keys")) return st;
   Sorted srt{nullptr, nullptr, A.counters + 1, cb.n};
-  if (int st = scat::radix_sort(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &srt.keys, &srt.idx, A.counters + 1,
-                                kKeyDrop))
+  if (int st = scat::radix_sort(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &srt.keys, &srt.pay, A.counters + 1,
+                                kKeyDrop, A.pay))
     return st;
   if (side != s) CNNUE_CUDA_TRY(cudaEventRecord(e->join, side));
   switch (hidden) {

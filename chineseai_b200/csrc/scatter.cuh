@@ -393,9 +393,11 @@ inline size_t sort_bytes(int64_t n) {
 // in ws (*keys_out, *idx_out).  Requires 0 < n < 2^32 - 1.  With d_live
 // (the number of keys below drop_key, in device memory) the first pass
 // drops the keys >= drop_key and the later passes sort the d_live others.
+// payload (optional): what the sorted slots carry instead of the items'
+// indices.
 int radix_sort(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaStream_t s,
                const uint32_t** keys_out, const uint32_t** idx_out, const uint32_t* d_live = nullptr,
-               uint32_t drop_key = 0xffffffffu) {
+               uint32_t drop_key = 0xffffffffu, const uint32_t* payload = nullptr) {
   const size_t nn = (size_t)n;
   const int64_t nb = n_blocks(n);
   char* p = (char*)ws;
@@ -412,7 +414,7 @@ int radix_sort(const uint32_t* keys, int64_t n, int64_t n_keys, void* ws, cudaSt
   uint32_t* aux = (uint32_t*)p;
   const int passes = key_passes(n_keys + 1);
   const uint32_t* kin = keys;
-  const uint32_t* iin = nullptr;
+  const uint32_t* iin = payload;
   uint32_t* kout = k0;
   uint32_t* iout = i0;
   for (int pass = 0; pass < passes; ++pass) {

@@ -396,7 +396,7 @@ def run_train(args):
     from chineseai_b200.quantized import as_device
 
     tr = train.Trainer(train.init_params(3), device=local, group=pg.group.WORLD if pg else None,
-                       ft_chunks=args.ft_chunks)
+                       ft_chunks=args.ft_chunks, shard=not args.no_shard)
     pos = synth.positions(TRAIN_BATCH, 1 + rank)
     t = torch.from_numpy(train.targets(TRAIN_BATCH, 100 + rank)).to(dev)
     idx, off = as_device(pos.indices, dev), as_device(pos.offsets, dev)
@@ -434,17 +434,28 @@ def run_train(args):
                                                        tr.grads.data_ptr(), tr.shadow.data_ptr(), 0.0, 1e-12, 0.9,
                                                        0.999, 1e-8, 1, None, stream.cuda_stream), args.steps, dev,
                       stream)
-    ar = 0.0
+    ar = rsag = 0.0
     if pg:
         scratch = torch.zeros_like(tr.grads)
         pg.barrier()
         ar = _device_loop(lambda: pg.all_reduce(scratch, op=pg.ReduceOp.SUM), args.steps, dev, stream)
-        del scratch
-    stats = torch.tensor([total, fb, ar, ad], dtype=torch.float64, device=dev)
+        # the sharded exchange's collectives alone: FT fp32 reduce-scatter + bf16 all-gather
+        ft = train.OFF_W1
+        part = ft // world
+        sh = torch.zeros(ft, dtype=torch.bfloat16, device=dev)
+
+        def rs_ag():
+            pg.reduce_scatter_tensor(scratch[:part], scratch[:ft], op=pg.ReduceOp.SUM)
+            pg.all_gather_into_tensor(sh, sh[:part])
+
+        pg.barrier()
+        rsag = _device_loop(rs_ag, args.steps, dev, stream)
+        del scratch, sh
+    stats = torch.tensor([total, fb, ar, ad, rsag], dtype=torch.float64, device=dev)
     if pg:
         pg.all_reduce(stats, op=pg.ReduceOp.MAX)
-    total, fb, ar, ad = stats.tolist()
-    fb, ar, ad = fb / args.steps, ar / args.steps, ad / args.steps
+    total, fb, ar, ad, rsag = stats.tolist()
+    fb, ar, ad, rsag = fb / args.steps, ar / args.steps, ad / args.steps, rsag / args.steps
     loss = float(tr.loss.item())
     if rank == 0:
         ms = total / args.steps
@@ -455,12 +466,16 @@ def run_train(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16/fp32",
             "data": "synthetic",
             "config": {"workload": "HalfKA training step: bf16 FT gather, pack, 16 bucket fp32 stacks (L1 on "
-                                   "tcgen05), MSE(sigmoid(s/400), t), atomic-free FT backward, NCCL all-reduce "
-                                   "overlapped with the FT backward (stack gradients + 4 FT row chunks), Adam",
+                                   "tcgen05), MSE(sigmoid(s/400), t), atomic-free FT backward, Adam; N > 1: "
+                                   "stack gradients all-reduced beside the FT backward, FT gradient "
+                                   + ("all-reduced" if args.no_shard else
+                                      "reduce-scattered, Adam on this rank's FT shard, bf16 FT shadow "
+                                      "all-gathered"),
                        "batch_per_gpu": TRAIN_BATCH, "global_batch": world * TRAIN_BATCH,
-                       "parallelism": f"dp{world}", "grad_bytes": grad_bytes, "ft_chunks": args.ft_chunks},
+                       "parallelism": f"dp{world}", "grad_bytes": grad_bytes, "ft_chunks": args.ft_chunks,
+                       "ft_exchange": "all-reduce" if args.no_shard else "sharded"},
             "phases_ms": {"forward_backward_alone": fb, "allreduce_alone": ar, "adam_alone": ad,
-                          "exposed_exchange": ms - fb - ad},
+                          "rs_ag_alone": rsag, "exposed_exchange_and_adam": ms - fb},
             "allreduce_busbw_gbs": (2 * (world - 1) / world * grad_bytes / (ar / 1e3) / 1e9) if world > 1 else None,
             "loss": loss, "clocks": clocks,
         }
@@ -1006,8 +1021,8 @@ def run_az_train(args):
     sampler.start()
     time.sleep(0.3)
     def device_step():
-        tr._graph.replay()
-        if tr.world > 1:
+        tr._graph.replay()  # with N > 1 the graph holds the NCCL exchange and AdamW too
+        if tr.world > 1 and not tr._in_graph_exchange():
             tr._exchange(tr._graph_out, read=False)
             tr._adamw()
 
@@ -1074,6 +1089,7 @@ def run_az_train(args):
                                     "sample": f"{n_rep} steps of {sample} samples: torch-CPU restatement "
                                               "(fp32 autograd) + the oracle's AdamW"}
         print(json.dumps(line), flush=True)
+    tr.close()  # releases the captured graph (it may hold NCCL calls)
     if pg:
         pg.barrier()
         pg.destroy_process_group()
@@ -1206,7 +1222,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--ft-chunks", type=int, default=4, help="train: FT-gradient row chunks exchanged as they finish")
+    ap.add_argument("--ft-chunks", type=int, default=1, help="train, --no-shard: FT-gradient row chunks "
+                    "all-reduced as they finish")
+    ap.add_argument("--no-shard", action="store_true", help="train: all-reduce the FT gradient and run Adam over "
+                    "everything on every rank, instead of the sharded exchange")
     ap.add_argument("--workload", choices=["eval", "fp32", "update", "train", "resnet", "az", "az-train", "mcts"],
                     default="eval",
                     help="eval: the headline quantised forward; fp32: the fp32 forward (batch 4096); "

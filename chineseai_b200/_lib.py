@@ -72,12 +72,15 @@ SIGNATURES = {
     "cnnue_adamw": (c_int, [P, P, P, P, c_i64, C.c_double, C.c_double, C.c_double, C.c_double, C.c_double,
                             c_i64, P]),
     "cnnue_adamw_device": (c_int, [P, P, P, P, c_i64, P, P]),
+    "cnnue_adamw_device_scaled": (c_int, [P, P, P, P, c_i64, P, C.c_float, P, c_int, P]),
     "cnnue_t_param_count": (c_size, []),
     "cnnue_t_workspace_bytes": (c_size, [c_i64, c_u32]),
     "cnnue_t_make_shadow": (c_int, [P, P, P]),
     "cnnue_t_forward_backward": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, P, c_size, P]),
     "cnnue_t_adam": (c_int, [P, P, P, P, P, C.c_float, C.c_float, C.c_float, C.c_float, C.c_float,
                              c_int, P, P]),
+    "cnnue_t_adam_range": (c_int, [P, P, P, P, P, c_i64, c_i64, C.c_float, C.c_float, C.c_float, C.c_float,
+                                   C.c_float, c_int, P, P]),
     "cnnue_t_forward_backward_begin": (c_int, [P, P, P, c_u32, P, c_i64, P, P, P, c_size, P]),
     "cnnue_t_ft_grad_rows": (c_int, [c_i64, c_u32, P, P, c_size, c_i64, c_i64, P]),
     "cnnue_t_finish": (c_int, [c_i64, c_u32, P, P, c_size, P, P]),

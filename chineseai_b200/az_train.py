@@ -247,6 +247,7 @@ def mean_allreduce_(grad, group=None) -> int:
 # Tail of the gradient buffer: 30 metrics, then 4 status-bit indicators.
 _TAIL = 64
 _N_METRICS = 30
+_NATIVE_OUT = _N_METRICS + 5  # the native step's metrics: 30 statistics, 4 status bits (0/1), the word
 
 
 def exchange_with_status_(buf, n_grad: int, tail_at: int, metrics, word, group=None, read: bool = True,
@@ -333,6 +334,10 @@ class TrainStats:
 class AzTrainer:
     """GpuTrainer (src/az/train_gpu_candle.rs:15-160) on one CUDA device.
 
+    native (default for hidden 32/64/128/256/512): the step is the native
+    kernel sequence cnnue_azt_step (forward, both losses, all gradients);
+    native=False: torch autograd around this package's CUDA ops.
+
     graph=True captures the whole step (forward, loss, backward, AdamW) in a
     CUDA graph once a batch shape repeats (batches packed with fixed=True all
     share one shape), and replays it; the first step of each new shape runs
@@ -343,8 +348,12 @@ class AzTrainer:
     every rank steps on its own equal share of the batch, the flat gradient is
     sum-all-reduced once and scaled by 1 / world (the gradient of the whole
     batch's mean loss), and every rank applies the same AdamW update.  The
-    captured graph then holds forward and backward only; the all-reduce and
-    AdamW run after it, outside the graph.  With a process group the step's
+    native step without a guard keeps that exchange on the device (metrics
+    and status bits written into the all-reduced gradient tail, AdamW
+    skipped on the device when any rank set a status bit), so a captured
+    graph holds the whole data-parallel step; call close() before
+    destroy_process_group.  With a guard (or native=False) the exchange and
+    AdamW run after the step, from the host.  Either way the step's
     statistics (TrainStats) are the whole batch's (sums over every rank's
     share, samples = the global batch), and a kernel status raised on any
     rank skips AdamW and raises on every rank."""
@@ -409,7 +418,7 @@ class AzTrainer:
         self.adam_state = torch.from_numpy(state.view(np.uint8).copy()).to(self.device)
         # native step: leaf offsets of the flat buffers, metrics, workspaces by batch shape
         self._leaf_offsets = np.array([off for _, _, _, _, off, _ in layout], np.int64)
-        self._metrics = torch.zeros(_N_METRICS + 1, dtype=torch.float32, device=self.device)
+        self._metrics = torch.zeros(_NATIVE_OUT, dtype=torch.float32, device=self.device)
         self._ws = {}
         if self.native:
             e = C.c_void_p()
@@ -417,7 +426,9 @@ class AzTrainer:
             self._engine = e
 
     def close(self) -> None:
-        """Releases the native step's engine (its stream and events)."""
+        """Releases the captured step (before destroy_process_group when it
+        holds the NCCL exchange) and the native step's engine."""
+        self._graph = None
         if self._engine is not None:
             lib().cnnue_azt_destroy(self._engine)
             self._engine = None
@@ -551,11 +562,12 @@ class AzTrainer:
                                  phase.reshape(-1)])
         return loss, metrics
 
-    def native_loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0):
+    def native_loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0, out=None):
         """The native step's forward, loss and backward (cnnue_azt_step) on a
         device batch: the 22 gradients land in self.grad (zeroed first);
-        returns the metrics tensor [31] (the 30 statistics of compute_batch_loss,
-        then the kernels' status word as a float).  No optimizer step."""
+        returns the metrics tensor [35] (`out`, default an own buffer): the
+        30 statistics of compute_batch_loss, the status word's 4 bits as 0/1,
+        the word as a float.  No optimizer step."""
         torch = self.torch
         bt = self.expand(bt)
         B, F = bt["feature_items"].shape
@@ -574,14 +586,33 @@ class AzTrainer:
             if not a.is_contiguous():
                 raise ValueError(f"native step: batch array {n} is not contiguous")
         batch = _CAztBatch(B, F, M, T, *[arrays[n].data_ptr() for n in names])
+        out = self._metrics if out is None else out
         check(lib().cnnue_azt_step(self._engine, self.flat.data_ptr(), self.grad.data_ptr(), self._tail_at,
                                    self._leaf_offsets.ctypes.data, self.hidden, C.byref(batch),
-                                   float(value_weight), float(policy_weight), self._metrics.data_ptr(),
+                                   float(value_weight), float(policy_weight), out.data_ptr(),
                                    self.status.data_ptr(), ws.data_ptr(), ws.numel(),
                                    torch.cuda.current_stream(self.device).cuda_stream), "cnnue_azt_step")
-        return self._metrics
+        return out
+
+    def _in_graph_exchange(self) -> bool:
+        """Native data-parallel steps without a guard keep the whole exchange
+        on the device: metrics and status bits in the gradient tail, one NCCL
+        sum all-reduce, AdamW scaled by 1/world and skipped on the device when
+        any rank set a status bit - so a captured step holds all of it."""
+        return self.native and self.world > 1 and self.guard is None
 
     def _step_body(self, bt: dict, value_weight: float, policy_weight: float):
+        if self._in_graph_exchange():
+            import torch.distributed as dist
+            out = self.grad[self._tail_at: self._tail_at + _NATIVE_OUT]
+            self.native_loss(bt, value_weight, policy_weight, out)
+            dist.all_reduce(self.grad, op=dist.ReduceOp.SUM, group=self.group)
+            check(lib().cnnue_adamw_device_scaled(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                                                  self.grad.data_ptr(), self.n_params, self.adam_state.data_ptr(),
+                                                  1.0 / self.world, out[_N_METRICS:].data_ptr(), 4,
+                                                  self.torch.cuda.current_stream(self.device).cuda_stream),
+                  "cnnue_adamw_device_scaled")
+            return out
         if self.native:
             out = self.native_loss(bt, value_weight, policy_weight)
             if self.world == 1:
@@ -605,7 +636,7 @@ class AzTrainer:
         """Data parallel: one NCCL sum all-reduce carries the gradient and
         every rank's metrics and status bits (exchange_with_status_); all
         ranks then take the same decision on AdamW."""
-        r = exchange_with_status_(self.grad, self.n_params, self._tail_at, out, out[_N_METRICS], self.group, read,
+        r = exchange_with_status_(self.grad, self.n_params, self._tail_at, out, out[-1], self.group, read,
                                   self.guard, self.step_count)
         if r is None:
             return None
@@ -639,7 +670,12 @@ class AzTrainer:
             out = self._step_body(bt, value_weight, policy_weight)
         self._last_key = key
         samples = batch.batch_size
-        if self.world > 1:
+        if self._in_graph_exchange():
+            t = out.cpu().numpy()  # summed over the ranks by the step's all-reduce
+            word = sum(1 << b for b in range(4) if t[_N_METRICS + b] > 0)
+            m = np.concatenate([t[:_N_METRICS], [float(word)]])
+            samples *= self.world
+        elif self.world > 1:
             m = self._exchange(out)
             samples *= self.world
             if int(m[-1]) == 0:  # every rank applies the step, or none does

@@ -1277,8 +1277,9 @@ __device__ void tile_block(const RedTable& T, Act& A, int tile, int split) {
   if (tid == 0) A.tile_cnt[tile] = 0;  // ready for the next step
 }
 
-// The 30 metrics of compute_batch_loss (train_gpu_candle.rs:271-300) and the
-// status word, summed over the boards in a fixed order.
+// The 30 metrics of compute_batch_loss (train_gpu_candle.rs:271-300), summed
+// over the boards in a fixed order, then the status word's four bits as 0/1
+// and the word itself: out[0..35).
 __device__ void metrics_block(const Batch& bt, const Act& A, LossScale raw, const uint32_t* status, float* out) {
   constexpr int kN = 2 + 2 + 6 + 21;  // weighted CEs, CEs, per-sample sums, phase
   __shared__ float red[256][kN + 1];
@@ -1315,7 +1316,9 @@ __device__ void metrics_block(const Batch& bt, const Act& A, LossScale raw, cons
     out[2] = t[3];
     for (int k = 0; k < 6; ++k) out[3 + k] = t[4 + k];
     for (int k = 0; k < 21; ++k) out[9 + k] = t[10 + k];
-    out[30] = (float)*(volatile const uint32_t*)status;
+    const uint32_t word = *(volatile const uint32_t*)status;
+    for (int k = 0; k < 4; ++k) out[30 + k] = (word >> k) & 1u ? 1.f : 0.f;
+    out[34] = (float)word;
   }
 }
 

@@ -45,13 +45,19 @@ __device__ __forceinline__ void adamw_one(float& p, float& m, float& v, float g,
 
 // The scalars come by value (host form) or from device memory (device form,
 // written by adamw_prepare_kernel); `kd` non-null selects the latter.
+// grad_scale multiplies every gradient first (one fp32 product: 1 is exact);
+// skip (device, optional): nonzero = leave everything as it is.
 __global__ void __launch_bounds__(256) adamw_vec4_kernel(float4* __restrict__ p, float4* __restrict__ m,
                                                          float4* __restrict__ v, const float4* __restrict__ g,
-                                                         int64_t n4, AdamWScalars k, const AdamWScalars* kd) {
+                                                         int64_t n4, AdamWScalars k, const AdamWScalars* kd,
+                                                         float grad_scale, const float* skip) {
+  if (skip && *skip != 0.f) return;
   if (kd) k = *kd;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     float4 pp = p[i], mm = m[i], vv = v[i];
-    const float4 gg = __ldg(g + i);
+    float4 gg = __ldg(g + i);
+    gg = make_float4(__fmul_rn(gg.x, grad_scale), __fmul_rn(gg.y, grad_scale), __fmul_rn(gg.z, grad_scale),
+                     __fmul_rn(gg.w, grad_scale));
     adamw_one(pp.x, mm.x, vv.x, gg.x, k);
     adamw_one(pp.y, mm.y, vv.y, gg.y, k);
     adamw_one(pp.z, mm.z, vv.z, gg.z, k);
@@ -64,11 +70,12 @@ __global__ void __launch_bounds__(256) adamw_vec4_kernel(float4* __restrict__ p,
 
 __global__ void adamw_scalar_kernel(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
                                     const float* __restrict__ g, int64_t begin, int64_t n, AdamWScalars k,
-                                    const AdamWScalars* kd) {
+                                    const AdamWScalars* kd, float grad_scale, const float* skip) {
+  if (skip && *skip != 0.f) return;
   if (kd) k = *kd;
   for (int64_t i = begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x)
-    adamw_one(p[i], m[i], v[i], g[i], k);
+    adamw_one(p[i], m[i], v[i], __fmul_rn(g[i], grad_scale), k);
 }
 
 // b^e for e >= 0 by repeated squaring (the powi runtime routine).
@@ -112,28 +119,34 @@ __host__ __device__ AdamWScalars make_scalars(double lr, double beta1, double be
   return k;
 }
 
-// Device form: advances the step counter and forms this step's scalars.
-__global__ void adamw_prepare_kernel(cnnue_adamw_state* st) {
+// Device form: advances the step counter and forms this step's scalars;
+// with skip flags (any nonzero) it marks the step skipped (pad[0] = 1) and
+// leaves the counter.
+__global__ void adamw_prepare_kernel(cnnue_adamw_state* st, const float* skip, int n_skip) {
+  bool sk = false;
+  for (int i = 0; i < n_skip; ++i) sk |= skip[i] != 0.f;
+  st->pad[0] = sk ? 1.f : 0.f;
+  if (sk) return;
   st->step += 1;
   const AdamWScalars k = make_scalars(st->lr, st->beta1, st->beta2, st->eps, st->weight_decay, st->step);
   memcpy(st->scalars, &k, sizeof(k));
 }
 
 int launch_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n, const AdamWScalars& k,
-                 const AdamWScalars* kd, cudaStream_t s) {
+                 const AdamWScalars* kd, cudaStream_t s, float grad_scale = 1.f, const float* skip = nullptr) {
   const bool aligned = ((uintptr_t)d_params | (uintptr_t)d_m | (uintptr_t)d_v | (uintptr_t)d_grads) % 16 == 0;
   int64_t done = 0;
   if (aligned && n >= 4) {
     const int64_t n4 = n / 4;
     const unsigned blocks = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
     adamw_vec4_kernel<<<blocks, 256, 0, s>>>((float4*)d_params, (float4*)d_m, (float4*)d_v, (const float4*)d_grads,
-                                            n4, k, kd);
+                                            n4, k, kd, grad_scale, skip);
     if (int st = check_launch_error("adamw_vec4_kernel")) return st;
     done = n4 * 4;
   }
   if (done < n) {
     const unsigned blocks = (unsigned)std::min<int64_t>((n - done + 255) / 256, 148 * 8);
-    adamw_scalar_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, done, n, k, kd);
+    adamw_scalar_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, done, n, k, kd, grad_scale, skip);
     if (int st = check_launch_error("adamw_scalar_kernel")) return st;
   }
   return CNNUE_OK;
@@ -163,10 +176,24 @@ int cnnue_adamw_device(float* d_params, float* d_m, float* d_v, const float* d_g
   if (n < 0 || !d_state || (n > 0 && (!d_params || !d_m || !d_v || !d_grads)))
     return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
   cudaStream_t s = (cudaStream_t)stream;
-  adamw_prepare_kernel<<<1, 1, 0, s>>>(d_state);
+  adamw_prepare_kernel<<<1, 1, 0, s>>>(d_state, nullptr, 0);
   if (int st = check_launch_error("adamw_prepare_kernel")) return st;
   if (n == 0) return CNNUE_OK;
   return launch_adamw(d_params, d_m, d_v, d_grads, n, AdamWScalars{}, (const AdamWScalars*)d_state->scalars, s);
+}
+
+int cnnue_adamw_device_scaled(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n,
+                              cnnue_adamw_state* d_state, float grad_scale, const float* d_skip, int n_skip,
+                              void* stream) {
+  if (n < 0 || !d_state || n_skip < 0 || (n_skip > 0 && !d_skip) ||
+      (n > 0 && (!d_params || !d_m || !d_v || !d_grads)))
+    return set_error(CNNUE_ERR_INVALID_ARG, "null buffer or negative size");
+  cudaStream_t s = (cudaStream_t)stream;
+  adamw_prepare_kernel<<<1, 1, 0, s>>>(d_state, d_skip, n_skip);
+  if (int st = check_launch_error("adamw_prepare_kernel")) return st;
+  if (n == 0) return CNNUE_OK;
+  return launch_adamw(d_params, d_m, d_v, d_grads, n, AdamWScalars{}, (const AdamWScalars*)d_state->scalars, s,
+                      grad_scale, d_state->pad);
 }
 
 }  // extern "C"

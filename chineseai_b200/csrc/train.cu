@@ -869,4 +869,24 @@ int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, 
   return check_launch_error("t_adam_kernel");
 }
 
+int cnnue_t_adam_range(float* d_params, float* d_m, float* d_v, const float* d_grads, uint16_t* d_shadow,
+                       int64_t begin, int64_t end, float grad_scale, float lr, float beta1, float beta2, float eps,
+                       int step, const float* d_skip, void* stream) {
+  if (!d_params || !d_m || !d_v || !d_grads || !d_shadow)
+    return set_error(CNNUE_ERR_INVALID_ARG, "null buffer");
+  if (step < 1) return set_error(CNNUE_ERR_INVALID_ARG, "step must be >= 1");
+  if (begin < 0 || end > kParams || begin > end)
+    return set_error(CNNUE_ERR_INVALID_ARG, "parameter range [%lld, %lld) outside [0, %lld)", (long long)begin,
+                     (long long)end, (long long)kParams);
+  if (begin == end) return CNNUE_OK;
+  const float c1 = 1.f - powf(beta1, (float)step);
+  const float c2 = 1.f - powf(beta2, (float)step);
+  const int64_t shadow_end = std::min<int64_t>(end, kOffW1);
+  t_adam_kernel<<<148 * 8, 256, 0, (cudaStream_t)stream>>>(
+      d_params + begin, d_m + begin, d_v + begin, d_grads + begin, end - begin,
+      (__nv_bfloat16*)d_shadow + begin, std::max<int64_t>(0, shadow_end - begin), grad_scale, lr, beta1, beta2, eps,
+      c1, c2, d_skip);
+  return check_launch_error("t_adam_kernel");
+}
+
 }  // extern "C"

@@ -104,20 +104,34 @@ OFF_W1 = N_FEATURES * COLS + COLS  # first stack parameter (the FT weights and b
 class Trainer:
     """One rank of the HalfKA training step.
 
-    With a process group of more than one rank the step overlaps the
-    gradient exchange with the FT backward: the stack gradients (and a status
-    flag) are all-reduced on a side stream while the FT gradient is reduced,
-    then the FT gradient in `ft_chunks` row ranges, each all-reduced as soon
-    as its rows are final; Adam waits for every exchange and is skipped on
-    every rank when any rank's batch had bad input."""
+    With a process group of more than one rank the stack gradients (and a
+    status flag) are all-reduced on a side stream while the FT gradient is
+    still being reduced.  The FT gradient is then exchanged one of two ways:
+
+    * shard=True (the default without a guard): one reduce-scatter leaves
+      each rank the summed gradient of its 1/world of the FT parameters,
+      Adam updates that shard (and the stack on every rank), and one
+      all-gather of the bf16 shadow the forward reads rebuilds the whole
+      table on every rank: 3/4 of an all-reduce's bytes and 1/world of the
+      FT Adam.  The fp32 FT parameters of other ranks' shards are then stale
+      on this rank; gather_state() all-gathers them (and the summed
+      gradient) when the full fp32 state is needed (tests, checkpoints);
+    * shard=False: `ft_chunks` row ranges, each all-reduced as soon as its
+      rows are final, then Adam over everything on every rank.
+
+    Adam waits for every exchange and is skipped on every rank when any
+    rank's batch had bad input."""
 
     def __init__(self, params: np.ndarray, device: int = 0, adam: AdamConfig = AdamConfig(), group=None,
-                 guard=None, ft_chunks: int = 4):
+                 guard=None, ft_chunks: int = 1, shard: Optional[bool] = None):
         self.device = torch.device("cuda", device)
         self.adam = adam
         self.group = group
         self.guard = guard  # optional dist_guard.StepGuard for the exchange
         self.ft_chunks = ft_chunks
+        self.shard = guard is None if shard is None else shard
+        if self.shard and guard is not None:
+            raise ValueError("the sharded exchange runs without a StepGuard; use shard=False with a guard")
         n = param_count()
         if params.shape != (n,):
             raise ValueError(f"expected {n} parameters, got {params.shape}")
@@ -187,6 +201,29 @@ class Trainer:
             return None
         return dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
 
+    def _shard_range(self):
+        """(begin, end) of this rank's FT shard in flat parameter indices, or
+        None when the FT does not split evenly (the all-reduce path runs)."""
+        import torch.distributed as dist
+        w = self.world()
+        if OFF_W1 % w:
+            return None
+        size = OFF_W1 // w
+        r = dist.get_rank(self.group)
+        return r * size, (r + 1) * size
+
+    def gather_state(self) -> None:
+        """Sharded exchange: all-gathers the fp32 FT parameters and the summed
+        FT gradient of every shard, so self.params and self.grads hold the
+        whole state (as after an all-reduce step) on every rank."""
+        import torch.distributed as dist
+        sr = self._shard_range() if self.shard and self.world() > 1 else None
+        if sr is None:
+            return
+        b, e = sr
+        dist.all_gather_into_tensor(self.params[:OFF_W1], self.params[b:e], group=self.group)
+        dist.all_gather_into_tensor(self.grads[:OFF_W1], self.grads[b:e], group=self.group)
+
     def _step_overlapped(self, idx, n_idx, off, n, target) -> None:
         ws = self.workspace(n, n_idx)
         s = torch.cuda.current_stream(self.device)
@@ -209,6 +246,10 @@ class Trainer:
                 works.append(self._all_reduce(t, tag))
 
         exchange(self._gbuf[OFF_W1:param_count() + 1], 0)  # stack gradients + the status flag
+        sr = self._shard_range() if self.shard else None
+        if sr is not None:
+            self._exchange_sharded(n, n_idx, ws, s, works, sr)
+            return
         rows = N_FEATURES + 1
         bounds = [rows * k // self.ft_chunks for k in range(self.ft_chunks + 1)]
         for k in range(self.ft_chunks):
@@ -223,6 +264,38 @@ class Trainer:
         ev.record(self._side)
         s.wait_event(ev)
         self.apply_adam(1.0 / self.world(), skip=self.flag)
+
+    def _exchange_sharded(self, n, n_idx, ws, s, works, sr) -> None:
+        """FT gradient: one in-place reduce-scatter on the side stream; Adam
+        on this rank's FT shard and on the stack; the shard's bf16 shadow
+        all-gathered in place."""
+        import torch.distributed as dist
+        L = lib()
+        sp = s.cuda_stream
+        check(L.cnnue_t_ft_grad_rows(n, n_idx, self.grads.data_ptr(), ws.data_ptr(), ws.numel(), 0, N_FEATURES + 1,
+                                     sp), "cnnue_t_ft_grad_rows")
+        b, e = sr
+        ev = torch.cuda.Event()
+        ev.record(s)
+        with torch.cuda.stream(self._side):
+            self._side.wait_event(ev)
+            works.append(dist.reduce_scatter_tensor(self.grads[b:e], self.grads[:OFF_W1], op=dist.ReduceOp.SUM,
+                                                    group=self.group, async_op=True))
+        for w in works:
+            w.wait()  # the current stream waits for the collectives
+        ev = torch.cuda.Event()
+        ev.record(self._side)
+        s.wait_event(ev)
+        self.step_count += 1
+        a = self.adam
+        scale = 1.0 / self.world()
+        for lo, hi in ((b, e), (OFF_W1, param_count())):
+            check(L.cnnue_t_adam_range(self.params.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                                       self.grads.data_ptr(), self.shadow.data_ptr(), lo, hi, scale, a.lr, a.beta1,
+                                       a.beta2, a.eps, self.step_count, self.flag.data_ptr(), sp),
+                  "cnnue_t_adam_range")
+        shadow = self.shadow.view(torch.bfloat16)
+        dist.all_gather_into_tensor(shadow[:OFF_W1], shadow[b:e], group=self.group)
 
     def step_positions(self, pos: Positions, target: np.ndarray) -> float:
         """Convenience: host batch -> one step; returns this rank's loss."""

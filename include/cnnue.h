@@ -425,6 +425,12 @@ int cnnue_t_finish(int64_t n_positions, uint32_t n_indices, float* d_loss, void*
 int cnnue_t_adam(float* d_params, float* d_m, float* d_v, const float* d_grads, uint16_t* d_shadow,
                  float grad_scale, float lr, float beta1, float beta2, float eps, int step,
                  const float* d_skip, void* stream);
+/* The same Adam step over the parameters [begin, end) only (flat
+ * indices; the shadow is refreshed for those below the FT end): a data-
+ * parallel rank's shard after a reduce-scatter of the gradient. */
+int cnnue_t_adam_range(float* d_params, float* d_m, float* d_v, const float* d_grads, uint16_t* d_shadow,
+                       int64_t begin, int64_t end, float grad_scale, float lr, float beta1, float beta2, float eps,
+                       int step, const float* d_skip, void* stream);
 
 /* AdamW step over n fp32 parameters (flat buffer) with moments m, v, as
  * candle-nn's AdamW::step (the AZ trainer's optimizer, lr / betas / eps /
@@ -443,10 +449,18 @@ typedef struct cnnue_adamw_state {
   double lr, beta1, beta2, eps, weight_decay;
   int64_t step;        /* steps taken; 0 before the first */
   float scalars[9];    /* written by the device: this step's fp32 factors */
-  float pad[3];
+  float pad[3];        /* pad[0]: 1 when the last device step was skipped */
 } cnnue_adamw_state;
 int cnnue_adamw_device(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n,
                        cnnue_adamw_state* d_state, void* stream);
+/* The device-state step for a data-parallel exchange: every gradient is
+ * multiplied by grad_scale first (1/world after a sum all-reduce), and when
+ * any of d_skip[0..n_skip) is nonzero (status bits summed over the ranks)
+ * the step is skipped on the device - nothing changes and the step counter
+ * stays; d_state->pad[0] then reads 1 (0 after a step taken). */
+int cnnue_adamw_device_scaled(float* d_params, float* d_m, float* d_v, const float* d_grads, int64_t n,
+                              cnnue_adamw_state* d_state, float grad_scale, const float* d_skip, int n_skip,
+                              void* stream);
 
 /* ---- reference-native AZ-NNUE evaluator (src/az.rs, src/nnue.rs) -------- */
 /* Squares are rank * 9 + file with rank 0 the first rank of a FEN (Black's
@@ -595,9 +609,11 @@ int cnnue_az_expand_policy_indices(const int64_t* d_items, const uint8_t* d_sign
  * 4.  The gradients are summed into nothing: d_grads[0..n_grads) is zeroed
  * first.  The batch is the packed batch in full form (device pointers;
  * expand a compact one with cnnue_az_expand_policy_indices first).
- * d_metrics[31] gets the 30 statistics of AzTrainStats (loss sum, value CE
- * sum, policy CE sum, the six value sums, the 3 x 7 phase table) and the
- * status word as a float; d_status is cleared, then collects
+ * d_metrics[35] gets the 30 statistics of AzTrainStats (loss sum, value CE
+ * sum, policy CE sum, the six value sums, the 3 x 7 phase table), the four
+ * status bits as 0/1 floats and the status word as a float (a layout that
+ * sums meaningfully over data-parallel ranks: d_metrics may point into the
+ * tail of the gradient buffer that is all-reduced); d_status is cleared, then collects
  * CNNUE_STATUS_BAD_INDEX for indices outside their tables (those lookups
  * read 0 and pass no gradient).  hidden: 32, 64, 128, 256 or 512; moves <=
  * 1024.  Deterministic: the same inputs give the same bits, run to run.

@@ -1,9 +1,10 @@
 """Data-parallel HalfKA training step on two GPUs (skipped with fewer): two
-NCCL ranks each stepping on half of a batch, with the exchange overlapped
-with the FT backward (stack gradients + FT row chunks on a side stream), end
-with bit-identical parameters, and their summed gradient divided by the
-world size equals one rank's gradient of the whole batch within the
-single-GPU parity tolerance."""
+NCCL ranks each stepping on half of a batch - the stack gradients all-reduced
+beside the FT backward, the FT gradient either reduce-scattered with a
+sharded Adam and an all-gather of the bf16 shadow, or all-reduced in row
+chunks - end with bit-identical parameters, and their summed gradient
+divided by the world size equals one rank's gradient of the whole batch
+within the single-GPU parity tolerance."""
 import os
 
 import numpy as np
@@ -35,7 +36,7 @@ def _half(pos, t, rank):
     return select(pos, keep), t[keep]
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, shard):
     import datetime
 
     import torch.distributed as dist
@@ -50,9 +51,10 @@ def _rank(rank, world, port, out):
                             device_id=dev)
     params, pos, t = _batch()
     mine, tm = _half(pos, t, rank)
-    tr = train.Trainer(params, rank, group=dist.group.WORLD)
+    tr = train.Trainer(params, rank, group=dist.group.WORLD, shard=shard, ft_chunks=1 if shard else 4)
     tr.step(as_device(mine.indices, dev), len(mine.indices), as_device(mine.offsets, dev), mine.n,
             torch.from_numpy(tm).to(dev))
+    tr.gather_state()
     torch.cuda.synchronize()
     out[rank] = (tr.grads.cpu().numpy() / world, tr.params.cpu().numpy(), float(tr.flag.item()))
     dist.barrier()
@@ -61,13 +63,14 @@ def _rank(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_two_rank_overlapped_step_equals_full_batch():
+@pytest.mark.parametrize("shard", [True, False])
+def test_two_rank_overlapped_step_equals_full_batch(shard):
     from chineseai_b200 import train
     from chineseai_b200.quantized import as_device
     ctx = mp.get_context("spawn")
     out = ctx.Manager().dict()
     port = 29800 + os.getpid() % 1000
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, out)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port + int(shard), out, shard)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

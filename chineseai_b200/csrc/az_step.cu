@@ -318,9 +318,6 @@ __device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, co
 // board << kMultBits | multiplicity (trunk), board (threat), move (move row,
 // scalar tables), move | kNegBit for a subtracted feature row.
 constexpr int kDerived = kTrunkRows - kInput;  // 285
-// Shared words per warp of the forward's row list: the derived-row histogram
-// (kDerived + 1, even) and up to F + kDerived (row, multiplicity) pairs.
-__host__ __device__ inline int64_t fwd_smem_words(int64_t F) { return kDerived + 1 + 2 * (F + kDerived); }
 
 __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_t* __restrict__ keys,
                                                      uint32_t* __restrict__ pay, uint32_t* __restrict__ counters,
@@ -443,70 +440,114 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
 }
 
 // ---- forward -------------------------------------------------------------------------
-// Blocks [0, trunk_blocks): one warp per board -
-//   board_pre = feature pool (six rows per item) + hidden bias,
-//   sparse_hidden = relu(board_pre + rule_context . R), hidden = RMS-normed,
-//   accumulator context = W_acc . board_pre, value head = relu(W_v . hidden +
-//   b_v), threat accumulator (64) over the board's threat rows, pair = [act,
-//   act^2] with act = clamp(threat, 0, 1), value logits = W_o . value head +
-//   W_to . pair, move context = W_pc . hidden + W_ptc . pair;
+// Blocks [0, B): one block of kBW warps per board -
+//   warp 0 lists the board's trunk rows (feature rows, and the distinct
+//   derived rows with multiplicities from a shared histogram) while warps
+//   1.. accumulate the threat rows; all warps then split the trunk rows;
+//   board_pre = pool + hidden bias, sparse_hidden = relu(board_pre + rule .
+//   R), hidden = RMS-normed (every warp), then one 32-output product per
+//   warp: warp 0 the accumulator context W_acc . board_pre and the move
+//   context W_pc . hidden + W_ptc . pair, warps 1-3 the value head groups;
+//   warp 0 finishes with the value logits W_o . value head + W_to . pair
+//   (pair = [act, act^2], act = clamp(threat, 0, 1));
 // blocks after them: one warp per input row r < 1260 - the accumulator
 // features af[r] = W_acc . trunk_table[r] (32 values).
+constexpr int kBW = 4;  // warps per board in the forward and policy kernels
+static_assert(kBW == 1 + kVH / 32, "one value-head group per warp after warp 0");
+
+// Shared floats of the forward's block: partial sums (kBW x H), threat partials
+// (kBW x 64), the value head (96), the derived-row histogram (kDerived + 1,
+// even) and up to F + kDerived (row, multiplicity) pairs.
+__host__ __device__ inline int64_t fwd_smem_words(int64_t F, int64_t H) {
+  return kBW * H + kBW * kTR + kVH + kDerived + 1 + 2 * (F + kDerived);
+}
 
 template <int NC>
-__global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Act A, int trunk_blocks,
-                                                          uint32_t* __restrict__ status) {
+__global__ void __launch_bounds__(32 * kBW) fwd_kernel(Params P, Batch bt, Act A, int trunk_blocks,
+                                                       uint32_t* __restrict__ status) {
   constexpr int H = 32 * NC;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if ((int)blockIdx.x >= trunk_blocks) {
-    const int r = ((int)blockIdx.x - trunk_blocks) * kWarps + warp;
+    const int r = ((int)blockIdx.x - trunk_blocks) * kBW + warp;
     if (r >= kInput) return;
     float x[NC];
     ld_row<NC>(P.p[L_FT] + (size_t)r * H, lane, x);
     A.af[(size_t)r * kAcc + lane] = matvec32<NC>(P.p[L_PAH], H, x, lane);
     return;
   }
-  const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
-  if (b >= bt.B) return;
-  // feature pool: the board's feature rows and its distinct derived rows
-  // with multiplicities (a per-warp histogram), listed in shared memory,
-  // then summed eight rows at a time
+  const int64_t b = blockIdx.x;
   extern __shared__ uint32_t fsm[];
-  uint32_t* hist = fsm + (size_t)warp * fwd_smem_words(bt.F);
-  uint2* list = reinterpret_cast<uint2*>(hist + kDerived + 1);  // 8-byte aligned: every stride is even
-  for (int i = lane; i < kDerived; i += 32) hist[i] = 0;
-  __syncwarp();
+  float* part = reinterpret_cast<float*>(fsm);  // [kBW][H]
+  float* tpart = part + kBW * H;                // [kBW][64]
+  float* vhs = tpart + kBW * kTR;               // [96]
+  uint32_t* hist = reinterpret_cast<uint32_t*>(vhs + kVH);
+  uint2* list = reinterpret_cast<uint2*>(hist + kDerived + 1);  // 8-byte aligned: every offset before is even
+  __shared__ uint32_t s_nlist;
+  __shared__ int s_flags;
+  if (threadIdx.x == 0) s_flags = 0;
   bool bad = false, bad_list = false;
-  uint32_t n_list = 0;
-  for (int64_t i0 = 0; i0 < bt.F; i0 += 32) {
-    uint32_t rows[6];
-    const int r = i0 + lane < bt.F ? pool_rows(bt.fi[b * bt.F + i0 + lane], rows) : 0;
-    bad |= r < 0;
-    const uint32_t m = __ballot_sync(kFull, r > 0);
-    if (r > 0) {
-      list[n_list + __popc(m & ((1u << lane) - 1u))] = make_uint2(rows[0], __float_as_uint(1.f));
+  if (warp == 0) {
+    for (int i = lane; i < kDerived; i += 32) hist[i] = 0;
+    __syncwarp();
+    uint32_t n_list = 0;
+    for (int64_t i0 = 0; i0 < bt.F; i0 += 32) {
+      uint32_t rows[6];
+      const int r = i0 + lane < bt.F ? pool_rows(bt.fi[b * bt.F + i0 + lane], rows) : 0;
+      bad |= r < 0;
+      const uint32_t m = __ballot_sync(kFull, r > 0);
+      if (r > 0) {
+        list[n_list + __popc(m & ((1u << lane) - 1u))] = make_uint2(rows[0], __float_as_uint(1.f));
 #pragma unroll
-      for (int q = 1; q < 6; ++q) atomicAdd(&hist[rows[q] - kInput], 1u);
+        for (int q = 1; q < 6; ++q) atomicAdd(&hist[rows[q] - kInput], 1u);
+      }
+      n_list += __popc(m);
     }
-    n_list += __popc(m);
+    __syncwarp();
+    for (int bin0 = 0; bin0 < kDerived; bin0 += 32) {
+      const int bin = bin0 + lane;
+      const uint32_t c = bin < kDerived ? hist[bin] : 0u;
+      const uint32_t m = __ballot_sync(kFull, c > 0);
+      const uint32_t pos = n_list + __popc(m & ((1u << lane) - 1u));
+      if (c > 0 && pos < (uint32_t)(bt.F + kDerived)) list[pos] = make_uint2(kInput + bin, __float_as_uint((float)c));
+      bad_list |= c > 0 && pos >= (uint32_t)(bt.F + kDerived);
+      n_list += __popc(m);
+    }
+    if (lane == 0) s_nlist = n_list < (uint32_t)(bt.F + kDerived) ? n_list : (uint32_t)(bt.F + kDerived);
+    reinterpret_cast<float2*>(tpart)[lane] = make_float2(0.f, 0.f);
+  } else {
+    // threat rows: chunks of 32 indices (one per lane) dealt round-robin to
+    // warps 1.., rows loaded eight at a time; lane owns columns 2 lane, 2 lane + 1
+    float t0 = 0.f, t1 = 0.f;
+    for (int64_t i0 = (int64_t)(warp - 1) * 32; i0 < bt.T; i0 += (int64_t)(kBW - 1) * 32) {
+      const uint32_t mine = i0 + lane < bt.T ? bt.ti[b * bt.T + i0 + lane] : kPad;
+      bad |= mine >= (uint32_t)kVocab && mine != kPad;
+      const int cnt = (int)(bt.T - i0 < 32 ? bt.T - i0 : 32);
+      for (int j0 = 0; j0 < cnt; j0 += 8) {
+        float2 v[8];
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          const uint32_t idx = __shfl_sync(kFull, mine, (j0 + t) & 31);
+          v[t] = j0 + t < cnt && idx < (uint32_t)kVocab
+                     ? __ldg(reinterpret_cast<const float2*>(P.p[L_TE] + (size_t)idx * kTR) + lane)
+                     : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int t = 0; t < 8; ++t) {
+          t0 += v[t].x;
+          t1 += v[t].y;
+        }
+      }
+    }
+    reinterpret_cast<float2*>(tpart + warp * kTR)[lane] = make_float2(t0, t1);
   }
-  __syncwarp();
-  for (int bin0 = 0; bin0 < kDerived; bin0 += 32) {
-    const int bin = bin0 + lane;
-    const uint32_t c = bin < kDerived ? hist[bin] : 0u;
-    const uint32_t m = __ballot_sync(kFull, c > 0);
-    const uint32_t pos = n_list + __popc(m & ((1u << lane) - 1u));
-    if (c > 0 && pos < (uint32_t)(bt.F + kDerived)) list[pos] = make_uint2(kInput + bin, __float_as_uint((float)c));
-    bad_list |= c > 0 && pos >= (uint32_t)(bt.F + kDerived);
-    n_list += __popc(m);
-  }
-  __syncwarp();
-  if (n_list > (uint32_t)(bt.F + kDerived)) n_list = (uint32_t)(bt.F + kDerived);
+  __syncthreads();
+  // trunk rows: batches of eight dealt round-robin to the warps
+  const uint32_t n_list = s_nlist;
   constexpr int kB = NC > 4 ? 4 : 8;
   float acc[NC];
 #pragma unroll
   for (int i = 0; i < NC; ++i) acc[i] = 0.f;
-  for (uint32_t j0 = 0; j0 < n_list; j0 += kB) {
+  for (uint32_t j0 = (uint32_t)warp * kB; j0 < n_list; j0 += kBW * kB) {
     float x[kB][NC], mult[kB];
 #pragma unroll
     for (int t = 0; t < kB; ++t) {
@@ -521,11 +562,22 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
 #pragma unroll
         for (int c = 0; c < NC; ++c) acc[c] = fmaf(mult[t], x[t][c], acc[c]);
   }
+  st_row<NC>(part + warp * H, lane, acc);
+  __syncthreads();
+  // every warp: board_pre (partials added in warp order), rule, relu, RMS
   float bias[NC], bp[NC], h[NC];
   ld_row<NC>(P.p[L_HB], lane, bias);
 #pragma unroll
-  for (int c = 0; c < NC; ++c) bp[c] = acc[c] + bias[c];
-  // rule context, relu, RMS norm
+  for (int c = 0; c < NC; ++c) bp[c] = 0.f;
+#pragma unroll
+  for (int w = 0; w < kBW; ++w) {
+    float x[NC];
+    ld_row_rw<NC>(part + w * H, lane, x);
+#pragma unroll
+    for (int c = 0; c < NC; ++c) bp[c] += x[c];
+  }
+#pragma unroll
+  for (int c = 0; c < NC; ++c) bp[c] += bias[c];
   float pre[NC];
 #pragma unroll
   for (int c = 0; c < NC; ++c) pre[c] = 0.f;
@@ -540,79 +592,68 @@ __global__ void __launch_bounds__(32 * kWarps) fwd_kernel(Params P, Batch bt, Ac
   const float rms = sqrtf(warp_sum(ss) / (float)H + 1.0e-6f);
 #pragma unroll
   for (int c = 0; c < NC; ++c) h[c] = h[c] / rms;
-  // accumulator context and value head
-  const float acc_ctx = matvec32<NC>(P.p[L_PAH], H, bp, lane);
-  float vh[3];
-#pragma unroll
-  for (int g = 0; g < 3; ++g)
-    vh[g] = fmaxf(matvec32<NC>(P.p[L_VHH] + (size_t)32 * g * H, H, h, lane) + __ldg(P.p[L_VHB] + 32 * g + lane),
-                  0.f);
-  // threat accumulator: lane owns columns 2 lane, 2 lane + 1; indices fetched
-  // 32 at a time (one per lane), rows loaded eight at a time
   float t0 = 0.f, t1 = 0.f;
-  for (int64_t i0 = 0; i0 < bt.T; i0 += 32) {
-    const uint32_t mine = i0 + lane < bt.T ? bt.ti[b * bt.T + i0 + lane] : kPad;
-    bad |= mine >= (uint32_t)kVocab && mine != kPad;
-    const int cnt = (int)(bt.T - i0 < 32 ? bt.T - i0 : 32);
-    for (int j0 = 0; j0 < cnt; j0 += 8) {
-      float2 v[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        const uint32_t idx = __shfl_sync(kFull, mine, (j0 + t) & 31);
-        v[t] = j0 + t < cnt && idx < (uint32_t)kVocab
-                   ? __ldg(reinterpret_cast<const float2*>(P.p[L_TE] + (size_t)idx * kTR) + lane)
-                   : make_float2(0.f, 0.f);
-      }
-#pragma unroll
-      for (int t = 0; t < 8; ++t) {
-        t0 += v[t].x;
-        t1 += v[t].y;
-      }
-    }
+  for (int w = 0; w < kBW; ++w) {
+    const float2 v = reinterpret_cast<const float2*>(tpart + w * kTR)[lane];
+    t0 += v.x;
+    t1 += v.y;
   }
   const float a0 = fminf(fmaxf(t0, 0.f), 1.f), a1 = fminf(fmaxf(t1, 0.f), 1.f);
   const float pr[4] = {a0, a1, a0 * a0, a1 * a1};  // pair columns 2l, 2l+1, 64+2l, 65+2l
   const int pc[4] = {2 * lane, 2 * lane + 1, kTR + 2 * lane, kTR + 2 * lane + 1};
-  // value logits
-  float vl[3];
+  if (warp > 0) {
+    const int g = warp - 1;
+    const float vh =
+        fmaxf(matvec32<NC>(P.p[L_VHH] + (size_t)32 * g * H, H, h, lane) + __ldg(P.p[L_VHB] + 32 * g + lane), 0.f);
+    vhs[32 * g + lane] = vh;
+    A.vh[b * kVH + 32 * g + lane] = vh;
+  } else {
+    const float acc_ctx = matvec32<NC>(P.p[L_PAH], H, bp, lane);
+    // move context (16): hidden and pair terms in one reduce-scatter
+    float v[32];
 #pragma unroll
-  for (int k = 0; k < 3; ++k) {
-    float s = 0.f;
+    for (int o = 0; o < 32; ++o) {
+      float sm = 0.f;
+      if (o < 16) {
+        sm = dot_row<NC>(P.p[L_PCH] + (size_t)o * H, lane, h);
 #pragma unroll
-    for (int g = 0; g < 3; ++g) s = fmaf(vh[g], __ldg(P.p[L_VHO] + k * kVH + 32 * g + lane), s);
-#pragma unroll
-    for (int q = 0; q < 4; ++q) s = fmaf(pr[q], __ldg(P.p[L_VTO] + k * kPair + pc[q]), s);
-    vl[k] = warp_sum(s);
-  }
-  // move context (16): hidden and pair terms in one reduce-scatter
-  float v[32];
-#pragma unroll
-  for (int o = 0; o < 32; ++o) {
-    float s = 0.f;
-    if (o < 16) {
-      s = dot_row<NC>(P.p[L_PCH] + (size_t)o * H, lane, h);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) s = fmaf(pr[q], __ldg(P.p[L_PTC] + o * kPair + pc[q]), s);
+        for (int q = 0; q < 4; ++q) sm = fmaf(pr[q], __ldg(P.p[L_PTC] + o * kPair + pc[q]), sm);
+      }
+      v[o] = sm;
     }
-    v[o] = s;
+    reduce_scatter32(v, lane);
+    if (lane < 16) A.ctx[b * kCtx + lane] = v[0];
+    A.ctx[b * kCtx + 16 + lane] = acc_ctx;
+    st_row<NC>(A.bp + b * H, lane, bp);
+    st_row<NC>(A.hid + b * H, lane, h);
+    if (lane == 0) A.rms[b] = rms;
+    reinterpret_cast<float2*>(A.ta + b * kTR)[lane] = make_float2(t0, t1);
   }
-  reduce_scatter32(v, lane);
-  // saved for the loss and the backward
-  st_row<NC>(A.bp + b * H, lane, bp);
-  st_row<NC>(A.hid + b * H, lane, h);
-  if (lane == 0) A.rms[b] = rms;
+  if (__any_sync(kFull, bad) && lane == 0) atomicOr(&s_flags, 1);
+  if (__any_sync(kFull, bad_list) && lane == 0) atomicOr(&s_flags, 2);
+  __syncthreads();
+  if (warp == 0) {
+    // value logits from the value head (shared) and the pair
+    float vl[3];
 #pragma unroll
-  for (int g = 0; g < 3; ++g) A.vh[b * kVH + 32 * g + lane] = vh[g];
-  reinterpret_cast<float2*>(A.ta + b * kTR)[lane] = make_float2(t0, t1);
-  if (lane < 16) A.ctx[b * kCtx + lane] = v[0];
-  A.ctx[b * kCtx + 16 + lane] = acc_ctx;
-  if (lane < 3) A.vl[b * 4 + lane] = lane == 0 ? vl[0] : (lane == 1 ? vl[1] : vl[2]);
-  if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
-  if (__any_sync(kFull, bad_list) && lane == 0) atomicOr(status, CNNUE_STATUS_INTERNAL);
+    for (int k = 0; k < 3; ++k) {
+      float sm = 0.f;
+#pragma unroll
+      for (int g = 0; g < 3; ++g) sm = fmaf(vhs[32 * g + lane], __ldg(P.p[L_VHO] + k * kVH + 32 * g + lane), sm);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sm = fmaf(pr[q], __ldg(P.p[L_VTO] + k * kPair + pc[q]), sm);
+      vl[k] = warp_sum(sm);
+    }
+    if (lane < 3) A.vl[b * 4 + lane] = lane == 0 ? vl[0] : (lane == 1 ? vl[1] : vl[2]);
+    if (lane == 0 && (s_flags & 1)) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+    if (lane == 0 && (s_flags & 2)) atomicOr(status, CNNUE_STATUS_INTERNAL);
+  }
 }
 
 // ---- policy logits, losses, logit gradients ------------------------------------------
-// One warp per board, lane l taking moves l, l + 32, ...  A move's logit is
+// One block of kBW warps per board, thread t taking moves t, t + 32 kBW, ...
+// (block reductions add the warps' results in warp order).  A move's logit is
 // (policy bit set) bias[mv] + move_bit * (consequence . (psp[to] - psp[from]
 // - capture * psp[cap]) + ctx16 . move_context[mv] + (ctx32 + af[to] -
 // af[from] - capture * af[cap]) . accumulator_move[mv]), else 0, plus its 7
@@ -632,25 +673,51 @@ struct LossScale {
   float value, policy;  // max(weight, 0) / B
 };
 
-__global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt, Act A, int H, LossScale ls,
-                                                             uint32_t* __restrict__ status) {
+// Block sum (or max) of one value per thread: warp butterflies, then the
+// warps' results in warp order; every thread gets the result.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int w = 1; w < kBW; ++w) t += red[w];
+  return t;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = red[0];
+#pragma unroll
+  for (int w = 1; w < kBW; ++w) t = fmaxf(t, red[w]);
+  return t;
+}
+
+__global__ void __launch_bounds__(32 * kBW, 4) policy_kernel(Params P, Batch bt, Act A, int H, LossScale ls,
+                                                          uint32_t* __restrict__ status) {
   extern __shared__ float smem[];
   __shared__ float cons[kPsp];
-  __shared__ float sctx[kWarps][kCtx];
+  __shared__ float sctx[kCtx];
+  __shared__ float red[kBW];
+  __shared__ float gred[kBW][96];
+  __shared__ int s_bad;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* z = smem + (size_t)warp * bt.M;  // logits, then probabilities
+  float* z = smem;  // the board's logits, then probabilities
+  const int64_t b = blockIdx.x;
   if (threadIdx.x < kPsp) cons[threadIdx.x] = __ldg(P.p[L_CONS] + threadIdx.x);
+  if (threadIdx.x < kCtx) sctx[threadIdx.x] = A.ctx[b * kCtx + threadIdx.x];
+  if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
-  const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
-  if (b >= bt.B) return;
-  sctx[warp][lane] = A.ctx[b * kCtx + lane];
-  if (lane < kCtx - 32) sctx[warp][32 + lane] = A.ctx[b * kCtx + 32 + lane];
-  __syncwarp();
-  const float* c = sctx[warp];
+  const float* c = sctx;
   const float* ft = P.p[L_FT];
   bool bad = false;
   float zmax = -INFINITY;
-  for (int64_t m = lane; m < bt.M; m += 32) {
+  for (int64_t m = threadIdx.x; m < bt.M; m += 32 * kBW) {
     const int64_t u = b * bt.M + m;
     const Item it = decode(bt.pi[u]);
     float v = 0.f;
@@ -716,25 +783,25 @@ __global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt,
     z[m] = zz;
     zmax = fmaxf(zmax, zz);
   }
-  zmax = warp_max(zmax);
+  zmax = block_max(zmax, red);
   float se = 0.f;
-  for (int64_t m = lane; m < bt.M; m += 32) se += expf(z[m] - zmax);
-  const float lse = zmax + logf(warp_sum(se));
+  for (int64_t m = threadIdx.x; m < bt.M; m += 32 * kBW) se += expf(z[m] - zmax);
+  const float lse = zmax + logf(block_sum(se, red));
   float ce = 0.f, tsum = 0.f;
-  for (int64_t m = lane; m < bt.M; m += 32) {
+  for (int64_t m = threadIdx.x; m < bt.M; m += 32 * kBW) {
     const float lp = z[m] - lse, t = bt.tgt[b * bt.M + m];
     ce -= t * lp;
     tsum += t;
     z[m] = expf(lp);
   }
-  ce = warp_sum(ce);
-  tsum = warp_sum(tsum);
+  ce = block_sum(ce, red);
+  tsum = block_sum(tsum, red);
   const float scale_p = ls.policy * __ldg(bt.pw + b);
   // logit gradients and the board's move-context / consequence sums
   float g16[32], g32[32], gc[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) g16[j] = g32[j] = gc[j] = 0.f;
-  for (int64_t m = lane; m < bt.M; m += 32) {
+  for (int64_t m = threadIdx.x; m < bt.M; m += 32 * kBW) {
     const int64_t u = b * bt.M + m;
     const float dl = scale_p * (z[m] * tsum - bt.tgt[u]);
     A.dl[u] = dl;
@@ -802,11 +869,26 @@ __global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt,
   reduce_scatter32(g16, lane);
   reduce_scatter32(g32, lane);
   reduce_scatter32(gc, lane);
-  if (lane < 16) A.dctx[b * kCtx + lane] = g16[0];
-  A.dctx[b * kCtx + 16 + lane] = g32[0];
-  A.cons[b * kPsp + lane] = gc[0];
-  // value head loss (lane 0)
-  if (lane == 0) {
+  gred[warp][lane] = g16[0];
+  gred[warp][32 + lane] = g32[0];
+  gred[warp][64 + lane] = gc[0];
+  if (__any_sync(kFull, bad) && lane == 0) s_bad = 1;
+  __syncthreads();
+  if (warp == 0) {
+    float x[3];
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+      x[q] = gred[0][32 * q + lane];
+#pragma unroll
+      for (int w = 1; w < kBW; ++w) x[q] += gred[w][32 * q + lane];
+    }
+    if (lane < 16) A.dctx[b * kCtx + lane] = x[0];
+    A.dctx[b * kCtx + 16 + lane] = x[1];
+    A.cons[b * kPsp + lane] = x[2];
+    if (lane == 0 && s_bad) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
+  }
+  // value head loss (thread 0)
+  if (threadIdx.x == 0) {
     const float l0 = A.vl[b * 4], l1 = A.vl[b * 4 + 1], l2 = A.vl[b * 4 + 2];
     const float mx = fmaxf(l0, fmaxf(l1, l2));
     const float lse3 = mx + logf(expf(l0 - mx) + expf(l1 - mx) + expf(l2 - mx));
@@ -827,7 +909,6 @@ __global__ void __launch_bounds__(32 * kWarps) policy_kernel(Params P, Batch bt,
     r[3] = ce;
     r[4] = p0 - p2;  // value = p . (1, 0, -1)
   }
-  if (__any_sync(kFull, bad) && lane == 0) atomicOr(status, CNNUE_STATUS_BAD_INDEX);
 }
 
 // ---- trunk backward (one warp per board) -------------------------------------------
@@ -1455,11 +1536,11 @@ int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const 
                 cudaEvent_t join) {
   constexpr int H = 32 * NC;
   const int board_blocks = (int)((bt.B + kWarps - 1) / kWarps);
-  const int af_blocks = (kInput + kWarps - 1) / kWarps;
-  fwd_kernel<NC><<<board_blocks + af_blocks, 32 * kWarps, (size_t)kWarps * fwd_smem_words(bt.F) * 4, s>>>(
-      P, bt, A, board_blocks, status);
+  const int af_blocks = (kInput + kBW - 1) / kBW;
+  fwd_kernel<NC><<<(unsigned)bt.B + af_blocks, 32 * kBW, (size_t)fwd_smem_words(bt.F, H) * 4, s>>>(
+      P, bt, A, (int)bt.B, status);
   if (int st = check_launch_error("azt forward")) return st;
-  policy_kernel<<<board_blocks, 32 * kWarps, (size_t)kWarps * bt.M * 4, s>>>(P, bt, A, H, ls, status);
+  policy_kernel<<<(unsigned)bt.B, 32 * kBW, (size_t)bt.M * 4, s>>>(P, bt, A, H, ls, status);
   if (int st = check_launch_error("azt policy")) return st;
   bwd_kernel<NC><<<board_blocks, 32 * kWarps, 0, s>>>(P, bt, A);
   if (int st = check_launch_error("azt backward")) return st;

@@ -70,20 +70,20 @@ struct WorkspaceView {
 };
 size_t bucket_workspace_bytes(int64_t n);
 WorkspaceView carve_workspace(void* ws, int64_t n);
-// Zeroes the header, then buckets the n positions (bucket = min((max(n0,1)-1)
+// Buckets the n positions (bucket = min((max(n0,1)-1)
 // >> shift, n_buckets-1), n0 from the offsets or from d_count0) and scatters
 // them into bucket order, stably (ascending positions within a bucket), so
 // everything computed in that order is deterministic.  Offsets are validated
-// into the status word.
+// into the status word, which the sort writes (clearing earlier bits): the
+// workspace needs no clearing before it.  n_buckets <= 31.
 // When `inv` is not null it receives the inverse order: inv[p] = the sorted
 // slot of position p.
+// d_extra0 / d_extra1 (optional): further [2n + 1] list offsets arrays whose
+// lists are checked with the sort (monotone, at most n_extra0 / n_extra1).
 int launch_bucket_sort(const uint32_t* d_offsets, uint32_t n_indices, const uint8_t* d_count0,
                        int64_t n, int shift, int n_buckets, void* ws, cudaStream_t s,
-                       uint32_t* inv = nullptr);
-// ORs CNNUE_STATUS_BAD_OFFSETS into the workspace status when a CSR offsets
-// array of n_lists lists is not monotone or runs past n_values.
-int launch_offsets_check(const uint32_t* d_offsets, uint32_t n_values, int64_t n_lists, void* ws,
-                         cudaStream_t s);
+                       uint32_t* inv = nullptr, const uint32_t* d_extra0 = nullptr, uint32_t n_extra0 = 0,
+                       const uint32_t* d_extra1 = nullptr, uint32_t n_extra1 = 0);
 
 // Tile g of the buckets' tiles in bucket order (each bucket's rows of the
 // sorted order cut into tiles of `rows`): its bucket, first sorted slot and

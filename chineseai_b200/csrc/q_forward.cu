@@ -28,6 +28,7 @@
 //     each CTA walks a contiguous slice of that order, so the current bucket's
 //     16 KB of L1 weights stay in registers (16 x 8 bytes per thread).
 #include <algorithm>
+#include <utility>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -991,6 +992,9 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
   extern __shared__ __align__(128) uint8_t smem_raw[];
   GatherSmem& sm = *reinterpret_cast<GatherSmem*>(smem_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // the stack kernel may be scheduled once every CTA of this grid is running:
+  // it sets up, then waits for this grid's packed rows
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
@@ -1026,6 +1030,10 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
                     pipe::smem_addr(&sm.ring[0][0]) + (uint32_t)col_byte, 0u, 0u};
   PosDesc nxt;
   if (begin < end) nxt = finish_desc<kUpdate>(a, load_raw<kUpdate>(a, (uint32_t)begin, 0));
+  // launched as a programmatic dependent of the bucket sort's scatter: the
+  // inverse order (written by it) is complete and visible only after this
+  // wait; the producers read only the batch's lists and never wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   uint32_t slot_n = begin < end ? a.inv[begin] : 0u;  // sorted slot of the next position
 
   for (int64_t i = begin; i < end; ++i) {
@@ -1163,6 +1171,10 @@ __global__ void __launch_bounds__(kTcThreads) q_stack_tc_kernel(const __grid_con
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
+  // launched as a programmatic dependent of the gather: its packed rows are
+  // complete and visible only after this wait (the set-up above reads only
+  // weights and the sort's bucket counts, done before the gather began)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t tmem = sm.tmem_base;
   const int start = sm.start, count = sm.count;
 
@@ -1295,9 +1307,12 @@ int validate_common(const cnnue_q_model* m, int64_t n, void* ws, size_t ws_bytes
 }
 
 int launch_sort(const cnnue_q_model* m, const uint32_t* d_offsets, uint32_t n_indices,
-                const uint8_t* d_count0, int64_t n, void* ws, cudaStream_t s, uint32_t* inv) {
+                const uint8_t* d_count0, int64_t n, void* ws, cudaStream_t s, uint32_t* inv,
+                const uint32_t* d_extra0 = nullptr, uint32_t n_extra0 = 0, const uint32_t* d_extra1 = nullptr,
+                uint32_t n_extra1 = 0) {
   (void)m;
-  return launch_bucket_sort(d_offsets, n_indices, d_count0, n, 1, kNB, ws, s, inv);
+  return launch_bucket_sort(d_offsets, n_indices, d_count0, n, 1, kNB, ws, s, inv, d_extra0, n_extra0, d_extra1,
+                            n_extra1);
 }
 
 // Arguments with the default wait limit and the stall hook off.
@@ -1310,6 +1325,27 @@ ForwardArgs base_args() {
 }
 
 size_t stack_tc_smem_bytes() { return sizeof(StackTcSmem) + 1024; }
+
+// Launches `kernel` as a programmatic dependent of the stream's previous
+// kernel: it may be scheduled while that one finishes, and waits for it with
+// griddepcontrol.wait before reading its results.
+template <typename... KArgs, typename... Args>
+int launch_dependent(const char* what, void (*kernel)(KArgs...), unsigned grid, unsigned block, size_t smem,
+                     cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) return cuda_error(e, what);
+  return check_launch(what);
+}
 
 // The bucket stacks of the split path over the packed rows (tensor cores).
 int launch_stack(const cnnue_q_model* m, const ForwardArgs& a, const WorkspaceView& v, cudaStream_t s) {
@@ -1325,8 +1361,8 @@ int launch_stack(const cnnue_q_model* m, const ForwardArgs& a, const WorkspaceVi
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(CNNUE_ERR_CUDA, "cuTensorMapEncodeTiled(packed rows) failed (%d)", (int)r);
   const int64_t tiles = (a.n + kStackTile - 1) / kStackTile + kNB;  // bound on the buckets' tiles
-  q_stack_tc_kernel<<<(unsigned)tiles, kTcThreads, stack_tc_smem_bytes(), s>>>(map, a, m->w1tiles, v.hdr);
-  return check_launch("q_stack_tc_kernel");
+  return launch_dependent("q_stack_tc_kernel", q_stack_tc_kernel, (unsigned)tiles, kTcThreads, stack_tc_smem_bytes(),
+                          s, map, a, (const uint8_t*)m->w1tiles, (const WorkspaceHeader*)v.hdr);
 }
 
 // Forward over the sorted order (split path): gather + pack, then the stacks.
@@ -1350,11 +1386,10 @@ int launch_eval(const cnnue_q_model* m, const uint16_t* d_idx, uint32_t n_idx,
   a.status = &v.hdr->status;
   const int grid = (int)std::min<int64_t>(m->grid_gather, n);
   const size_t smem = sizeof(GatherSmem);
-  if (d_acc)
-    q_gather_kernel<false, true><<<grid, gather_threads(false), smem, s>>>(a);
-  else
-    q_gather_kernel<false, false><<<grid, gather_threads(false), smem, s>>>(a);
-  const int st = check_launch("q_gather_kernel");
+  const int st = d_acc ? launch_dependent("q_gather_kernel", q_gather_kernel<false, true>, (unsigned)grid,
+                                          gather_threads(false), smem, s, a)
+                       : launch_dependent("q_gather_kernel", q_gather_kernel<false, false>, (unsigned)grid,
+                                          gather_threads(false), smem, s, a);
   if (st) return st;
   return launch_stack(m, a, v, s);
 }
@@ -1634,11 +1669,8 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   DeviceGuard guard(m->device);
   if (guard.status) return guard.status;
   cudaStream_t s = (cudaStream_t)stream;
-  st = launch_sort(m, nullptr, 0, d_count0, n, ws, s, ws_inv(ws, n));
-  if (st) return st;
-  st = launch_offsets_check(d_rem_offsets, n_rem, 2 * n, ws, s);
-  if (st) return st;
-  st = launch_offsets_check(d_add_offsets, n_add, 2 * n, ws, s);
+  // the sort also checks the removed and added lists' offsets
+  st = launch_sort(m, nullptr, 0, d_count0, n, ws, s, ws_inv(ws, n), d_rem_offsets, n_rem, d_add_offsets, n_add);
   if (st) return st;
   WorkspaceView v = carve_workspace(ws, n);
   ForwardArgs a = base_args();
@@ -1661,8 +1693,8 @@ int cnnue_q_update(const cnnue_q_model* m, const int16_t* d_parent, const uint8_
   a.sorted_bucket = v.sorted_bucket;
   a.status = &v.hdr->status;
   const int grid = (int)std::min<int64_t>(m->grid_gather_update, n);
-  q_gather_kernel<true, true><<<grid, gather_threads(true), sizeof(GatherSmem), s>>>(a);
-  st = check_launch("q_gather_kernel<update>");
+  st = launch_dependent("q_gather_kernel<update>", q_gather_kernel<true, true>, (unsigned)grid, gather_threads(true),
+                        sizeof(GatherSmem), s, a);
   if (st) return st;
   return launch_stack(m, a, v, s);
 }

@@ -304,8 +304,9 @@ __device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, co
 // rows, 285 in all) with the number of the board's items that hit it as a
 // multiplicity - the board gradient times that count.  The trunk section
 // holds B x F feature slots, then 5F derived slots per board (a board hits
-// at most 5F derived rows).  Then one thread per threat index or policy
-// move.  A contribution that cannot change a table gradient gets kKeyDrop:
+// at most 5F derived rows).  Then one thread per further contribution slot
+// (threat rows, and per policy move its move row, feature rows and lookups).
+// A contribution that cannot change a table gradient gets kKeyDrop:
 // padding items and threats, moves without the policy bit (torch.where
 // passes them no gradient), feature rows of moves without the move bit or
 // of an absent capture, and the sparse / tactical lookups of padded moves
@@ -369,56 +370,56 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
     }
     rows_kept = live;
   } else {
-    const int64_t nt = bt.B * bt.T, nm = bt.B * bt.M;
+    // one thread per contribution slot after the trunk section: threat
+    // slots, then per move its move row, 3 feature rows, 7 sparse and 2
+    // tactical lookups (each section contiguous: coalesced reads and writes)
+    const int64_t first = cb.threat, total = (int64_t)cb.n - first;
     const int64_t stride = (int64_t)(gridDim.x - pool_blocks) * blockDim.x;
-    for (int64_t t = (int64_t)(blockIdx.x - pool_blocks) * blockDim.x + threadIdx.x; t < nt + nm; t += stride) {
-      if (t < nt) {
+    for (int64_t t = (int64_t)(blockIdx.x - pool_blocks) * blockDim.x + threadIdx.x; t < total; t += stride) {
+      const uint32_t slot = (uint32_t)(first + t);
+      uint32_t key = kKeyDrop, py = 0;
+      bool row = false;
+      if (slot < cb.move) {
         const uint32_t idx = bt.ti[t];
         const bool ok = idx < (uint32_t)kVocab;
         bad |= !ok && idx != kPad;
-        keys[cb.threat + t] = ok ? kKeyThreat + idx : kKeyDrop;
-        pay[cb.threat + t] = (uint32_t)(t / bt.T);
-        rows_kept += ok;
-        live += ok;
-      } else {
-        const int64_t u = t - nt;
+        key = ok ? kKeyThreat + idx : kKeyDrop;
+        py = (uint32_t)(t / bt.T);
+        row = true;
+      } else if (slot < cb.sparse) {
+        const bool is_move = slot < cb.feat;
+        const uint32_t u = is_move ? slot - cb.move : (slot - cb.feat) / 3u;
+        const uint32_t role = is_move ? 0u : (slot - cb.feat) - 3u * u;
         const Item it = decode(bt.pi[u]);
         const bool ok = in_range(it);
-        bad |= it.policy && !ok;
+        bad |= is_move && it.policy && !ok;
         const bool on = it.policy && ok;
-        keys[cb.move + u] = on ? kKeyMove + it.mv : kKeyDrop;
-        pay[cb.move + u] = (uint32_t)u;
-        const bool feat = on && it.move;
-        uint32_t* fk = keys + cb.feat + u * 3;
-        fk[0] = feat ? kKeyFeat + it.to : kKeyDrop;
-        fk[1] = feat ? kKeyFeat + it.from : kKeyDrop;
-        fk[2] = feat && it.capture ? kKeyFeat + it.cap : kKeyDrop;
-        pay[cb.feat + u * 3] = (uint32_t)u;
-        pay[cb.feat + u * 3 + 1] = (uint32_t)u | kNegBit;
-        pay[cb.feat + u * 3 + 2] = (uint32_t)u | kNegBit;
-        const uint32_t rk = on + (feat ? 2 + it.capture : 0);
-        rows_kept += rk;
-        live += rk;
+        if (is_move) {
+          key = on ? kKeyMove + it.mv : kKeyDrop;
+          py = u;
+        } else {
+          const bool feat = on && it.move && (role < 2 || it.capture);
+          key = feat ? kKeyFeat + (role == 0 ? it.to : role == 1 ? it.from : it.cap) : kKeyDrop;
+          py = role == 0 ? u : u | kNegBit;
+        }
+        row = true;
+      } else {
+        const bool sparse = slot < cb.tact;
+        const uint32_t r = sparse ? slot - cb.sparse : slot - cb.tact;
+        const uint32_t u = sparse ? r / 7u : r >> 1;
+        const int64_t sx = sparse ? bt.sp[r] : bt.tc[r];
+        const bool sok = sx >= 0 && sx < (sparse ? kSparseLen : kTactLen);
+        bad |= !sok;
+        const Item it = decode(bt.pi[u]);
         const bool drop = !it.policy && bt.mask[u] <= kMaskDrop && bt.tgt[u] == 0.f;
-#pragma unroll
-        for (int j = 0; j < 7; ++j) {
-          const int64_t sx = bt.sp[u * 7 + j];
-          const bool sok = sx >= 0 && sx < kSparseLen;
-          bad |= !sok;
-          keys[cb.sparse + u * 7 + j] = sok && !drop ? kKeySparse + (uint32_t)sx : kKeyDrop;
-          pay[cb.sparse + u * 7 + j] = (uint32_t)u;
-          live += sok && !drop;
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int64_t sx = bt.tc[u * 2 + j];
-          const bool sok = sx >= 0 && sx < kTactLen;
-          bad |= !sok;
-          keys[cb.tact + u * 2 + j] = sok && !drop ? kKeyTact + (uint32_t)sx : kKeyDrop;
-          pay[cb.tact + u * 2 + j] = (uint32_t)u;
-          live += sok && !drop;
-        }
+        key = sok && !drop ? (sparse ? kKeySparse : kKeyTact) + (uint32_t)sx : kKeyDrop;
+        py = u;
       }
+      keys[slot] = key;
+      pay[slot] = py;
+      const bool kept = key < kKeyDrop;
+      rows_kept += row && kept;
+      live += kept;
     }
   }
   // block totals (counts: order-free)
@@ -1691,9 +1692,9 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
     CNNUE_CUDA_TRY(cudaEventRecord(e->fork, s));
     CNNUE_CUDA_TRY(cudaStreamWaitEvent(side, e->fork, 0));
   }
-  // side: keys of every table contribution, one joint sort with runs and units
+  // side: keys of every table contribution, one joint sort
   const int pool_blocks = (int)((b.batch + kWarps - 1) / kWarps);
-  const int64_t slots = b.batch * (b.threats + b.moves);
+  const int64_t slots = (int64_t)cb.n - cb.threat;  // threat and move slots: one thread each
   const int other_blocks = (int)std::max<int64_t>(1, std::min<int64_t>((slots + 255) / 256, 148 * 8));
   keygen_kernel<<<pool_blocks + other_blocks, 256, 0, side>>>(bt, cb, A.keys, A.pay, A.counters, d_status,
                                                              pool_blocks);

@@ -117,7 +117,7 @@ SIGNATURES = {
     "cnnue_azt_create": (c_int, [c_int, C.POINTER(c_void_p)]),
     "cnnue_azt_destroy": (c_int, [c_void_p]),
     "cnnue_azt_workspace_bytes": (c_size, [c_i64, c_i64, c_i64, c_i64, c_i64]),
-    "cnnue_azt_step": (c_int, [c_void_p, P, P, c_i64, P, c_i64, P, C.c_float, C.c_float, P, P, P, c_size, P]),
+    "cnnue_azt_step": (c_int, [c_void_p, P, P, c_i64, P, c_i64, P, C.c_float, C.c_float, P, P, P, c_size, P, P]),
     "cnnue_az_legal_moves": (c_int, [P, c_int, P, c_int, C.POINTER(c_int)]),
     "cnnue_mcts_default_limits": (None, [c_void_p]),
     "cnnue_mcts_create": (c_int, [c_void_p, c_void_p, c_int, C.POINTER(c_void_p)]),

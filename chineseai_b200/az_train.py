@@ -155,6 +155,11 @@ class _CAztBatch(C.Structure):
 NATIVE_HIDDEN = (32, 64, 128, 256, 512)  # hidden sizes of the native step (cnnue_azt_step)
 
 
+class _CAztOptim(C.Structure):
+    """cnnue_azt_optim: AdamW inside the native step."""
+    _fields_ = [(n, C.c_void_p) for n in ("params", "m", "v", "state")]
+
+
 class _CPacked(C.Structure):
     _fields_ = [(n, C.c_int64) for n in ("batch", "max_features", "max_policy_moves", "max_value_threats")] + \
         [(name, C.c_void_p) for name in _PACKED_FIELDS]
@@ -562,12 +567,14 @@ class AzTrainer:
                                  phase.reshape(-1)])
         return loss, metrics
 
-    def native_loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0, out=None):
+    def native_loss(self, bt: dict, value_weight: float = 1.0, policy_weight: float = 1.0, out=None,
+                    adamw: bool = False):
         """The native step's forward, loss and backward (cnnue_azt_step) on a
         device batch: the 22 gradients land in self.grad (zeroed first);
         returns the metrics tensor [35] (`out`, default an own buffer): the
         30 statistics of compute_batch_loss, the status word's 4 bits as 0/1,
-        the word as a float.  No optimizer step."""
+        the word as a float.  adamw=True also applies AdamW (single GPU): the
+        table leaves' update runs while the dense gradients finish."""
         torch = self.torch
         bt = self.expand(bt)
         B, F = bt["feature_items"].shape
@@ -587,10 +594,13 @@ class AzTrainer:
                 raise ValueError(f"native step: batch array {n} is not contiguous")
         batch = _CAztBatch(B, F, M, T, *[arrays[n].data_ptr() for n in names])
         out = self._metrics if out is None else out
+        optim = _CAztOptim(self.flat.data_ptr(), self.m.data_ptr(), self.v.data_ptr(),
+                           self.adam_state.data_ptr()) if adamw else None
         check(lib().cnnue_azt_step(self._engine, self.flat.data_ptr(), self.grad.data_ptr(), self._tail_at,
                                    self._leaf_offsets.ctypes.data, self.hidden, C.byref(batch),
                                    float(value_weight), float(policy_weight), out.data_ptr(),
                                    self.status.data_ptr(), ws.data_ptr(), ws.numel(),
+                                   C.byref(optim) if optim is not None else None,
                                    torch.cuda.current_stream(self.device).cuda_stream), "cnnue_azt_step")
         return out
 
@@ -614,10 +624,7 @@ class AzTrainer:
                   "cnnue_adamw_device_scaled")
             return out
         if self.native:
-            out = self.native_loss(bt, value_weight, policy_weight)
-            if self.world == 1:
-                self._adamw()
-            return out
+            return self.native_loss(bt, value_weight, policy_weight, adamw=self.world == 1)
         self.grad.zero_()
         self.status.zero_()
         loss, metrics = self.loss(self.expand(bt), value_weight, policy_weight)

@@ -314,7 +314,7 @@ __device__ __forceinline__ float matvec32(const float* __restrict__ W, int H, co
 // to exactly 0, so their logit gradient is exactly 0).  Indices outside
 // their tables set CNNUE_STATUS_BAD_INDEX and are dropped.  counters[0]
 // gets the number of row-problem contributions kept, counters[1] the number
-// of all kept (the sort drops the others in its first pass).  Each slot also
+// of scalar-table ones (each sort drops the others in its first pass).  Each slot also
 // gets its payload, carried through the sort: where its value row lives -
 // board << kMultBits | multiplicity (trunk), board (threat), move (move row,
 // scalar tables), move | kNegBit for a subtracted feature row.
@@ -326,7 +326,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
   __shared__ uint32_t hist[kWarps][kDerived];
   __shared__ uint32_t part[2][kWarps];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  uint32_t rows_kept = 0, live = 0;
+  uint32_t rows_kept = 0, scalars_kept = 0;
   bool bad = false;
   if ((int)blockIdx.x < pool_blocks) {
     const int64_t b = (int64_t)blockIdx.x * kWarps + warp;
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
         keys[cb.pool + b * bt.F + i] = r > 0 ? kKeyPool + rows[0] : kKeyDrop;
         pay[cb.pool + b * bt.F + i] = (uint32_t)b << kMultBits | 1u;
         if (r > 0) {
-          ++live;
+          ++rows_kept;
 #pragma unroll
           for (int q = 1; q < 6; ++q) atomicAdd(&h[rows[q] - kInput], 1u);  // counts: order-free
         }
@@ -366,9 +366,8 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
         used += __popc(m);
       }
       for (int64_t k = used + lane; k < slots; k += 32) keys[dkey + k] = kKeyDrop;
-      if (lane == 0) live += used;
+      if (lane == 0) rows_kept += used;
     }
-    rows_kept = live;
   } else {
     // one thread per contribution slot after the trunk section: threat
     // slots, then per move its move row, 3 feature rows, 7 sparse and 2
@@ -419,11 +418,11 @@ __global__ void __launch_bounds__(256) keygen_kernel(Batch bt, Bases cb, uint32_
       pay[slot] = py;
       const bool kept = key < kKeyDrop;
       rows_kept += row && kept;
-      live += kept;
+      scalars_kept += !row && kept;
     }
   }
   // block totals (counts: order-free)
-  uint32_t v0 = rows_kept, v1 = live;
+  uint32_t v0 = rows_kept, v1 = scalars_kept;
 #pragma unroll
   for (int o = 16; o; o >>= 1) {
     v0 += __shfl_xor_sync(kFull, v0, o);
@@ -1001,11 +1000,14 @@ __global__ void __launch_bounds__(32 * kWarps) bwd_kernel(Params P, Batch bt, Ac
 // gradient, the move's move row or signed feature row, or dlogit.
 constexpr int kSeg = 64;
 
+// Two sorted arrays (row keys, scalar-table keys: disjoint key ranges, so a
+// run never spans both); their blocks are enumerated one after the other.
 struct Sorted {
-  const uint32_t* keys;    // [n_live] sorted keys
-  const uint32_t* pay;     // [n_live] payload of each sorted slot
-  const uint32_t* n_live;  // device word: contributions kept
-  uint32_t n_max;          // all contribution slots (bounds n_live)
+  const uint32_t* keys[2];    // [n_live] sorted keys
+  const uint32_t* pay[2];     // [n_live] payload of each sorted slot
+  const uint32_t* n_live[2];  // device words: contributions kept
+  uint32_t n_max[2];          // contribution slots (bounds n_live)
+  uint32_t slot_base[2];      // first partial slot of each array's blocks
 };
 
 // The value row of a contribution: src[c] * mult for c < W (W = 0: none).
@@ -1055,26 +1057,31 @@ __global__ void __launch_bounds__(256, 3) seg_kernel(Grads G, Act A, Batch bt, S
   constexpr int KW = NC > 2 ? NC : 2;   // column chunks of the widest row: max(H, 64) / 32
   constexpr int BT = NC > 4 ? 4 : 8;    // positions whose loads are in flight together
   const int lane = threadIdx.x & 31;
-  const uint32_t n = min(*s.n_live, s.n_max);
-  const uint32_t n_blocks = (n + kSeg - 1) / kSeg;
+  const uint32_t n0 = min(*s.n_live[0], s.n_max[0]), n1 = min(*s.n_live[1], s.n_max[1]);
+  const uint32_t nb0 = (n0 + kSeg - 1) / kSeg, nb1 = (n1 + kSeg - 1) / kSeg;
   const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
-  for (uint32_t blk = gw; blk < n_blocks; blk += n_warps) {
+  for (uint32_t g = gw; g < nb0 + nb1; g += n_warps) {
+    const int sg = g < nb0 ? 0 : 1;
+    const uint32_t blk = sg ? g - nb0 : g, n = sg ? n1 : n0;
+    const uint32_t* keys = s.keys[sg];
+    const uint32_t* pays = s.pay[sg];
+    const uint32_t slot = s.slot_base[sg] + 2 * blk;
     const uint32_t base = blk * kSeg;
     const int cnt = n - base < (uint32_t)kSeg ? (int)(n - base) : kSeg;
-    const uint32_t k_lo = lane < cnt ? s.keys[base + lane] : kKeyDrop;
-    const uint32_t k_hi = 32 + lane < cnt ? s.keys[base + 32 + lane] : kKeyDrop;
-    const uint32_t p_lo = lane < cnt ? s.pay[base + lane] : 0u;
-    const uint32_t p_hi = 32 + lane < cnt ? s.pay[base + 32 + lane] : 0u;
+    const uint32_t k_lo = lane < cnt ? keys[base + lane] : kKeyDrop;
+    const uint32_t k_hi = 32 + lane < cnt ? keys[base + 32 + lane] : kKeyDrop;
+    const uint32_t p_lo = lane < cnt ? pays[base + lane] : 0u;
+    const uint32_t p_hi = 32 + lane < cnt ? pays[base + 32 + lane] : 0u;
     const uint32_t first = __shfl_sync(kFull, k_lo, 0);
     if (first >= kKeyDrop) continue;  // keys ascend: the block is all dropped
-    const uint32_t prev = base > 0 ? s.keys[base - 1] : 0xffffffffu;
-    const uint32_t next = base + cnt < n ? s.keys[base + cnt] : 0xffffffffu;
-    if (2 * blk + 1 >= A.part_slots) {
+    const uint32_t prev = base > 0 ? keys[base - 1] : 0xffffffffu;
+    const uint32_t next = base + cnt < n ? keys[base + cnt] : 0xffffffffu;
+    if (slot + 1 >= A.part_slots) {
       if (lane == 0) check_failed(A, 11, blk, A.part_slots);
       continue;
     }
-    float* head_slot = A.part + (size_t)(2 * blk) * A.row_w;
+    float* head_slot = A.part + (size_t)slot * A.row_w;
     float* tail_slot = head_slot + A.row_w;
     if (first >= kKeyRowsEnd) {
       // scalar block: each lane loads its two positions, then one pass in order
@@ -1188,14 +1195,19 @@ template <int NC>
 __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, int H) {
   constexpr int KW = NC > 2 ? NC : 2;
   const int lane = threadIdx.x & 31;
-  const uint32_t n = min(*s.n_live, s.n_max);
-  const uint32_t n_blocks = (n + kSeg - 1) / kSeg;
+  const uint32_t n0 = min(*s.n_live[0], s.n_max[0]), n1 = min(*s.n_live[1], s.n_max[1]);
+  const uint32_t nb0 = (n0 + kSeg - 1) / kSeg, nb1 = (n1 + kSeg - 1) / kSeg;
   const uint32_t gw = (uint32_t)((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
   const uint32_t n_warps = (uint32_t)((gridDim.x * blockDim.x) >> 5);
-  for (uint32_t ob = gw; ob + 1 < n_blocks; ob += n_warps) {  // a full block with a successor
+  for (uint32_t g = gw; g < nb0 + nb1; g += n_warps) {
+    const int sg = g < nb0 ? 0 : 1;
+    const uint32_t ob = sg ? g - nb0 : g, n_blocks = sg ? nb1 : nb0;
+    const uint32_t* keys = s.keys[sg];
+    const uint32_t sb = s.slot_base[sg];
+    if (ob + 1 >= n_blocks) continue;  // a full block with a successor
     const uint32_t base = ob * kSeg;
-    const uint32_t key = s.keys[base + kSeg - 1], kn = s.keys[base + kSeg], k0 = s.keys[base];
-    const uint32_t kp = base > 0 ? s.keys[base - 1] : 0xffffffffu;
+    const uint32_t key = keys[base + kSeg - 1], kn = keys[base + kSeg], k0 = keys[base];
+    const uint32_t kp = base > 0 ? keys[base - 1] : 0xffffffffu;
     if (key >= kKeyDrop || kn != key) continue;
     if (k0 == key && kp == key) continue;  // the run began in an earlier block
     // last block q of the run: the run continues into block q + 1 while that
@@ -1203,19 +1215,19 @@ __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, 
     uint32_t q = ob + 1;
     for (int round = 0; round < (1 << 20); ++round) {
       const uint32_t probe = q + 1 + (uint32_t)lane;
-      const bool cont = probe < n_blocks && s.keys[probe * kSeg] == key;
+      const bool cont = probe < n_blocks && keys[probe * kSeg] == key;
       const uint32_t bal = __ballot_sync(kFull, cont);
       const int lead = bal == kFull ? 32 : __ffs(~bal) - 1;
       q += (uint32_t)lead;
       if (lead < 32) break;
     }
-    const int W = 2 * q + 1 < A.part_slots ? key_width(key, H) : 0;
+    const int W = sb + 2 * q + 1 < A.part_slots ? key_width(key, H) : 0;
     if (W == 0 && lane == 0) check_failed(A, 12, q, A.part_slots);
     float sum[KW];
 #pragma unroll
     for (int k = 0; k < KW; ++k) {
       const int c = lane + 32 * k;
-      sum[k] = c < W ? A.part[(size_t)(2 * ob + 1) * A.row_w + c] : 0.f;
+      sum[k] = c < W ? A.part[(size_t)(sb + 2 * ob + 1) * A.row_w + c] : 0.f;
     }
     uint32_t b = ob + 1;
     for (; b + 4 <= q + 1; b += 4) {
@@ -1225,7 +1237,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, 
 #pragma unroll
         for (int k = 0; k < KW; ++k) {
           const int c = lane + 32 * k;
-          x[t][k] = c < W ? A.part[(size_t)(2 * (b + t)) * A.row_w + c] : 0.f;
+          x[t][k] = c < W ? A.part[(size_t)(sb + 2 * (b + t)) * A.row_w + c] : 0.f;
         }
 #pragma unroll
       for (int t = 0; t < 4; ++t)
@@ -1236,7 +1248,7 @@ __global__ void __launch_bounds__(256) combine_kernel(Grads G, Act A, Sorted s, 
 #pragma unroll
       for (int k = 0; k < KW; ++k) {
         const int c = lane + 32 * k;
-        if (c < W) sum[k] += A.part[(size_t)(2 * b) * A.row_w + c];
+        if (c < W) sum[k] += A.part[(size_t)(sb + 2 * b) * A.row_w + c];
       }
 #pragma unroll
     for (int k = 0; k < KW; ++k) {
@@ -1268,6 +1280,7 @@ struct RedProb {
 struct RedTable {
   RedProb p[kMaxProb];
   int n_prob, n_tiles, K;
+  int tile_base;  // this table's first tile in the partial and counter arrays
 };
 
 __device__ __forceinline__ float pair_of(const float* ta, int c) {
@@ -1336,17 +1349,18 @@ __device__ void tile_block(const RedTable& T, Act& A, int tile, int split) {
     }
     __syncthreads();
   }
-  float* part = A.tile_part + ((size_t)tile * kSplits + split) * (kTO * kTC) + tid * 4;
+  const int gt = T.tile_base + tile;  // the tile's slot among all of the step's tiles
+  float* part = A.tile_part + ((size_t)gt * kSplits + split) * (kTO * kTC) + tid * 4;
   *reinterpret_cast<float4*>(part) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   __threadfence();
   __syncthreads();
-  if (tid == 0) last = atomicAdd(A.tile_cnt + tile, 1u) == kSplits - 1;
+  if (tid == 0) last = atomicAdd(A.tile_cnt + gt, 1u) == kSplits - 1;
   __syncthreads();
   if (!last) return;
   __threadfence();
   float sum[4] = {0.f, 0.f, 0.f, 0.f};
   for (int sp = 0; sp < kSplits; ++sp) {
-    const float4 v = __ldcg(reinterpret_cast<const float4*>(A.tile_part + ((size_t)tile * kSplits + sp) * (kTO * kTC) +
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(A.tile_part + ((size_t)gt * kSplits + sp) * (kTO * kTC) +
                                                            tid * 4));
     sum[0] += v.x, sum[1] += v.y, sum[2] += v.z, sum[3] += v.w;
   }
@@ -1356,7 +1370,7 @@ __device__ void tile_block(const RedTable& T, Act& A, int tile, int split) {
     const int c = c0 + tc + v;
     if (o < q.O && c < q.C) q.out[(size_t)o * q.C + c] = sum[v];
   }
-  if (tid == 0) A.tile_cnt[tile] = 0;  // ready for the next step
+  if (tid == 0) A.tile_cnt[gt] = 0;  // ready for the next step
 }
 
 // The 30 metrics of compute_batch_loss (train_gpu_candle.rs:271-300), summed
@@ -1404,14 +1418,18 @@ __device__ void metrics_block(const Batch& bt, const Act& A, LossScale raw, cons
   }
 }
 
-// Blocks [0, n_tiles * kSplits): weight-gradient tiles; then the feature-row
-// gradient grad_trunk[r][c] += dpsp[r][c] (c < 32) + sum_j daf[r][j] W_acc[j][c]
-// for r < 1260 (one thread per element); the last block: metrics.
+// Blocks [0, n_tiles * kSplits): weight-gradient tiles; then (feature_rows)
+// the feature-row gradient grad_trunk[r][c] += dpsp[r][c] (c < 32) + sum_j
+// daf[r][j] W_acc[j][c] for r < 1260 (one thread per element) and the
+// metrics block.  The tiles that need only the per-board backward run as one
+// launch beside the table sums; the accumulator weights' tile (it also needs
+// the feature rows' gradients), the feature rows and the metrics after them.
 __global__ void __launch_bounds__(256) final_kernel(RedTable T, Params P, Grads G, Act A, Batch bt, int H,
-                                                    LossScale raw, const uint32_t* status, float* metrics) {
+                                                    LossScale raw, const uint32_t* status, float* metrics,
+                                                    int feature_rows) {
   const int tile_blocks = T.n_tiles * kSplits;
   const int64_t feat_elems = (int64_t)kInput * H;
-  const int feat_blocks = (int)((feat_elems + 255) / 256);
+  const int feat_blocks = feature_rows ? (int)((feat_elems + 255) / 256) : 0;
   if ((int)blockIdx.x < tile_blocks) {
     tile_block(T, A, blockIdx.x / kSplits, blockIdx.x % kSplits);
     return;
@@ -1458,7 +1476,7 @@ int64_t leaf_size(int leaf, int64_t H) {
 }
 
 struct Plan {
-  size_t small, keys, sort, part, tile_part;
+  size_t small, keys, sort, sort2, part, tile_part;
   size_t bp, hid, rms, vh, ta, ctx, vl, af, dl, mrow, frow, pay, dvl, dctx, cons, rec, dbp, dpre, dta, dvh;
   size_t small_bytes, total;
   int row_w, max_tiles;
@@ -1485,8 +1503,10 @@ Plan make_plan(int64_t H, int64_t B, int64_t F, int64_t M, int64_t T) {
   p.small_bytes = (kSmallCounters + kTileCounters) * 4 + (size_t)kInput * kFeatW * 4;
   p.small = take(p.small_bytes);
   p.keys = take((size_t)n * 4);
-  p.sort = take(scat::sort_bytes(n));
-  p.part = take((size_t)2 * ((n + kSeg - 1) / kSeg) * p.row_w * 4);
+  const int64_t n_rows = cb.sparse, n_scalars = n - cb.sparse;  // the two sorts' slots
+  p.sort = take(scat::sort_bytes(n_rows));
+  p.sort2 = take(scat::sort_bytes(n_scalars));
+  p.part = take((size_t)2 * ((n_rows + kSeg - 1) / kSeg + (n_scalars + kSeg - 1) / kSeg) * p.row_w * 4);
   p.tile_part = take((size_t)p.max_tiles * kSplits * kTO * kTC * 4);
   p.bp = take((size_t)B * H * 4);
   p.hid = take((size_t)B * H * 4);
@@ -1531,42 +1551,89 @@ void add_prob(RedTable& T, const float* a, int lda, int O, const float* x, int l
   T.n_tiles += tiles_for(O, C);
 }
 
+// The step's streams and events (one stream, no events, without an engine).
+struct Streams {
+  cudaStream_t main, side, side2;
+  cudaEvent_t join, join2, bwd, join3, comb, join4;
+  bool forked;
+};
+// The optional AdamW of a single-GPU step: the table leaves' ranges (final
+// after the table sums) and the dense leaves' (final after the last kernel).
+struct Optim {
+  float *params, *m, *v;
+  const float* grads;
+  cnnue_adamw_state* state;
+  AdamWRanges table, dense;
+};
+
 template <int NC>
 int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const Bases& cb, const Sorted& srt,
-                LossScale ls, LossScale raw, uint32_t* status, float* metrics, cudaStream_t s, cudaStream_t side,
-                cudaEvent_t join) {
+                LossScale ls, LossScale raw, uint32_t* status, float* metrics, const Streams& st,
+                const Optim* opt) {
   constexpr int H = 32 * NC;
+  const cudaStream_t s = st.main;
   const int board_blocks = (int)((bt.B + kWarps - 1) / kWarps);
   const int af_blocks = (kInput + kBW - 1) / kBW;
   fwd_kernel<NC><<<(unsigned)bt.B + af_blocks, 32 * kBW, (size_t)fwd_smem_words(bt.F, H) * 4, s>>>(
       P, bt, A, (int)bt.B, status);
-  if (int st = check_launch_error("azt forward")) return st;
+  if (int e = check_launch_error("azt forward")) return e;
   policy_kernel<<<(unsigned)bt.B, 32 * kBW, (size_t)bt.M * 4, s>>>(P, bt, A, H, ls, status);
-  if (int st = check_launch_error("azt policy")) return st;
+  if (int e = check_launch_error("azt policy")) return e;
   bwd_kernel<NC><<<board_blocks, 32 * kWarps, 0, s>>>(P, bt, A);
-  if (int st = check_launch_error("azt backward")) return st;
-  if (side != s) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, join, 0));
-  const int64_t seg_blocks = (srt.n_max + kSeg - 1) / kSeg;
+  if (int e = check_launch_error("azt backward")) return e;
+  // dense weight gradients: all but the accumulator weights need only the
+  // per-board backward, so they run beside the table sums
+  RedTable Te{}, Tl{};
+  Te.K = Tl.K = (int)bt.B;
+  add_prob(Te, bt.rule, kRule, kRule, A.dpre, H, H, 0, G.g[L_RULE]);
+  add_prob(Te, nullptr, 0, 1, A.dbp, H, H, 0, G.g[L_HB]);
+  add_prob(Te, A.dvh, kVH, kVH, A.hid, H, H, 0, G.g[L_VHH]);
+  add_prob(Te, nullptr, 0, 1, A.dvh, kVH, kVH, 0, G.g[L_VHB]);
+  add_prob(Te, A.dvl, 4, 3, A.vh, kVH, kVH, 0, G.g[L_VHO]);
+  add_prob(Te, A.dvl, 4, 3, A.ta, kTR, kPair, 1, G.g[L_VTO]);
+  add_prob(Te, A.dctx, kCtx, 16, A.ta, kTR, kPair, 1, G.g[L_PTC]);
+  add_prob(Te, A.dctx, kCtx, 16, A.hid, H, H, 0, G.g[L_PCH]);
+  add_prob(Te, nullptr, 0, 1, A.cons, kPsp, kPsp, 0, G.g[L_CONS]);
+  Tl.tile_base = Te.n_tiles;
+  add_prob(Tl, A.dctx + 16, kCtx, kAcc, A.bp, H, H, 0, G.g[L_PAH], A.pspaf + kPsp, kFeatW, P.p[L_FT], H, kInput);
+  const cudaStream_t early = st.forked ? st.side : s;
+  if (st.forked) {
+    CNNUE_CUDA_TRY(cudaEventRecord(st.bwd, s));
+    CNNUE_CUDA_TRY(cudaStreamWaitEvent(st.side, st.bwd, 0));
+  }
+  final_kernel<<<Te.n_tiles * kSplits, 256, 0, early>>>(Te, P, G, A, bt, H, raw, status, metrics, 0);
+  if (int e = check_launch_error("azt dense gradients")) return e;
+  if (st.forked) {
+    CNNUE_CUDA_TRY(cudaEventRecord(st.join3, st.side));
+    CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, st.join, 0));
+    CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, st.join2, 0));
+  }
+  const int64_t seg_blocks = ((int64_t)srt.n_max[0] + kSeg - 1) / kSeg + ((int64_t)srt.n_max[1] + kSeg - 1) / kSeg;
   const unsigned seg_grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((seg_blocks + 7) / 8, 148 * 32));
   seg_kernel<NC><<<seg_grid, 256, 0, s>>>(G, A, bt, srt, H);
-  if (int st = check_launch_error("azt segment sums")) return st;
+  if (int e = check_launch_error("azt segment sums")) return e;
   combine_kernel<NC><<<seg_grid, 256, 0, s>>>(G, A, srt, H);
-  if (int st = check_launch_error("azt run combine")) return st;
-  RedTable T{};
-  T.K = (int)bt.B;
-  add_prob(T, bt.rule, kRule, kRule, A.dpre, H, H, 0, G.g[L_RULE]);
-  add_prob(T, nullptr, 0, 1, A.dbp, H, H, 0, G.g[L_HB]);
-  add_prob(T, A.dvh, kVH, kVH, A.hid, H, H, 0, G.g[L_VHH]);
-  add_prob(T, nullptr, 0, 1, A.dvh, kVH, kVH, 0, G.g[L_VHB]);
-  add_prob(T, A.dvl, 4, 3, A.vh, kVH, kVH, 0, G.g[L_VHO]);
-  add_prob(T, A.dvl, 4, 3, A.ta, kTR, kPair, 1, G.g[L_VTO]);
-  add_prob(T, A.dctx, kCtx, 16, A.ta, kTR, kPair, 1, G.g[L_PTC]);
-  add_prob(T, A.dctx, kCtx, 16, A.hid, H, H, 0, G.g[L_PCH]);
-  add_prob(T, A.dctx + 16, kCtx, kAcc, A.bp, H, H, 0, G.g[L_PAH], A.pspaf + kPsp, kFeatW, P.p[L_FT], H, kInput);
-  add_prob(T, nullptr, 0, 1, A.cons, kPsp, kPsp, 0, G.g[L_CONS]);
+  if (int e = check_launch_error("azt run combine")) return e;
+  if (opt) {
+    // the table leaves' gradients are final: their AdamW runs beside the rest
+    if (int e = adamw_prepare(opt->state, s)) return e;
+    const cudaStream_t tab = st.forked ? st.side2 : s;
+    if (st.forked) {
+      CNNUE_CUDA_TRY(cudaEventRecord(st.comb, s));
+      CNNUE_CUDA_TRY(cudaStreamWaitEvent(st.side2, st.comb, 0));
+    }
+    if (int e = adamw_ranges(opt->params, opt->m, opt->v, opt->grads, opt->table, opt->state, tab)) return e;
+    if (st.forked) CNNUE_CUDA_TRY(cudaEventRecord(st.join4, st.side2));
+  }
   const int feat_blocks = (int)(((int64_t)kInput * H + 255) / 256);
-  final_kernel<<<T.n_tiles * kSplits + feat_blocks + 1, 256, 0, s>>>(T, P, G, A, bt, H, raw, status, metrics);
-  return check_launch_error("azt final");
+  final_kernel<<<Tl.n_tiles * kSplits + feat_blocks + 1, 256, 0, s>>>(Tl, P, G, A, bt, H, raw, status, metrics, 1);
+  if (int e = check_launch_error("azt final")) return e;
+  if (st.forked) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, st.join3, 0));
+  if (opt) {
+    if (int e = adamw_ranges(opt->params, opt->m, opt->v, opt->grads, opt->dense, opt->state, s)) return e;
+    if (st.forked) CNNUE_CUDA_TRY(cudaStreamWaitEvent(s, st.join4, 0));
+  }
+  return CNNUE_OK;
 }
 
 }  // namespace
@@ -1575,8 +1642,8 @@ int launch_main(const Params& P, const Grads& G, Act& A, const Batch& bt, const 
 
 struct cnnue_azt {
   int device;
-  cudaStream_t side;
-  cudaEvent_t fork, join;
+  cudaStream_t side, side2;  // the row-key sort then the early dense gradients; the scalar-key sort then AdamW
+  cudaEvent_t fork, keys, join, join2, bwd, join3, comb, join4;
 };
 
 using namespace cnnue;
@@ -1588,13 +1655,16 @@ int cnnue_azt_create(int device, cnnue_azt** out) {
   if (!out) return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_create: out is NULL");
   *out = nullptr;
   if (int st = use_device(device)) return st;
-  cnnue_azt* e = new cnnue_azt{device, nullptr, nullptr, nullptr};
+  cnnue_azt* e = new cnnue_azt{};
+  e->device = device;
   cudaError_t err = cudaStreamCreateWithFlags(&e->side, cudaStreamNonBlocking);
-  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->fork, cudaEventDisableTiming);
-  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&e->join, cudaEventDisableTiming);
+  if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&e->side2, cudaStreamNonBlocking);
+  for (cudaEvent_t* ev : {&e->fork, &e->keys, &e->join, &e->join2, &e->bwd, &e->join3, &e->comb, &e->join4})
+    if (err == cudaSuccess) err = cudaEventCreateWithFlags(ev, cudaEventDisableTiming);
   if (err != cudaSuccess) {
-    if (e->join) cudaEventDestroy(e->join);
-    if (e->fork) cudaEventDestroy(e->fork);
+    for (cudaEvent_t ev : {e->fork, e->keys, e->join, e->join2, e->bwd, e->join3, e->comb, e->join4})
+      if (ev) cudaEventDestroy(ev);
+    if (e->side2) cudaStreamDestroy(e->side2);
     if (e->side) cudaStreamDestroy(e->side);
     delete e;
     return cuda_error(err, "cnnue_azt_create");
@@ -1607,8 +1677,10 @@ int cnnue_azt_destroy(cnnue_azt* e) {
   if (!e) return CNNUE_OK;
   use_device(e->device);
   cudaStreamSynchronize(e->side);
-  cudaEventDestroy(e->join);
-  cudaEventDestroy(e->fork);
+  cudaStreamSynchronize(e->side2);
+  for (cudaEvent_t ev : {e->fork, e->keys, e->join, e->join2, e->bwd, e->join3, e->comb, e->join4})
+    cudaEventDestroy(ev);
+  cudaStreamDestroy(e->side2);
   cudaStreamDestroy(e->side);
   delete e;
   return CNNUE_OK;
@@ -1621,7 +1693,8 @@ size_t cnnue_azt_workspace_bytes(int64_t hidden, int64_t batch, int64_t features
 
 int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t n_grads, const int64_t* leaf_offsets,
                    int64_t hidden, const cnnue_azt_batch* batch, float value_weight, float policy_weight,
-                   float* d_metrics, uint32_t* d_status, void* d_ws, size_t ws_bytes, void* stream) {
+                   float* d_metrics, uint32_t* d_status, void* d_ws, size_t ws_bytes, const cnnue_azt_optim* optim,
+                   void* stream) {
   if (!d_params || !d_grads || !leaf_offsets || !batch || !d_metrics || !d_status || !d_ws)
     return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: NULL argument");
   const cnnue_azt_batch& b = *batch;
@@ -1681,7 +1754,7 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   A.row_w = pl.row_w;
   A.status = d_status;
   const Bases cb = bases(b.batch, b.features, b.moves, b.threats);
-  A.part_slots = (uint32_t)(2 * ((cb.n + kSeg - 1) / kSeg));
+  A.part_slots = (uint32_t)(2 * (((int64_t)cb.sparse + kSeg - 1) / kSeg + ((int64_t)cb.n - cb.sparse + kSeg - 1) / kSeg));
   const LossScale raw{std::max(value_weight, 0.f), std::max(policy_weight, 0.f)};
   const LossScale ls{raw.value / (float)b.batch, raw.policy / (float)b.batch};
 
@@ -1699,17 +1772,71 @@ int cnnue_azt_step(cnnue_azt* e, const float* d_params, float* d_grads, int64_t 
   keygen_kernel<<<pool_blocks + other_blocks, 256, 0, side>>>(bt, cb, A.keys, A.pay, A.counters, d_status,
                                                              pool_blocks);
   if (int st = check_launch_error("azt keys")) return st;
-  Sorted srt{nullptr, nullptr, A.counters + 1, cb.n};
-  if (int st = scat::radix_sort(A.keys, cb.n, kKeyDrop, w + pl.sort, side, &srt.keys, &srt.pay, A.counters + 1,
-                                kKeyDrop, A.pay))
+  // the row keys (2 passes, 16 bits) on the side stream, the scalar-table
+  // keys (3 passes) on the second one, both after the keys
+  cudaStream_t side2 = e ? e->side2 : s;
+  if (side != s) {
+    CNNUE_CUDA_TRY(cudaEventRecord(e->keys, side));
+    CNNUE_CUDA_TRY(cudaStreamWaitEvent(side2, e->keys, 0));
+  }
+  Sorted srt{};
+  srt.n_live[0] = A.counters;
+  srt.n_live[1] = A.counters + 1;
+  srt.n_max[0] = cb.sparse;
+  srt.n_max[1] = cb.n - cb.sparse;
+  srt.slot_base[0] = 0;
+  srt.slot_base[1] = (uint32_t)(2 * ((cb.sparse + kSeg - 1) / kSeg));
+  if (int st = scat::radix_sort(A.keys, cb.sparse, kKeyRowsEnd, w + pl.sort, side, &srt.keys[0], &srt.pay[0],
+                                A.counters, kKeyDrop, A.pay))
     return st;
-  if (side != s) CNNUE_CUDA_TRY(cudaEventRecord(e->join, side));
+  if (int st = scat::radix_sort(A.keys + cb.sparse, (int64_t)cb.n - cb.sparse, kKeyDrop, w + pl.sort2, side2,
+                                &srt.keys[1], &srt.pay[1], A.counters + 1, kKeyDrop, A.pay + cb.sparse))
+    return st;
+  if (side != s) {
+    CNNUE_CUDA_TRY(cudaEventRecord(e->join, side));
+    CNNUE_CUDA_TRY(cudaEventRecord(e->join2, side2));
+  }
+  Streams streams{s, side, side2, nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, side != s};
+  if (e) {
+    streams.join = e->join, streams.join2 = e->join2, streams.bwd = e->bwd;
+    streams.join3 = e->join3, streams.comb = e->comb, streams.join4 = e->join4;
+  }
+  Optim opt{};
+  if (optim) {
+    if (!optim->params || !optim->m || !optim->v || !optim->state || optim->params != d_params)
+      return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: optim needs params (= d_params), m, v and state");
+    for (int l = 0; l + 1 < kLeaves; ++l)
+      if (leaf_offsets[l + 1] < leaf_offsets[l] + leaf_size(l, hidden))
+        return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: the optimizer needs the leaves in order");
+    opt.params = optim->params, opt.m = optim->m, opt.v = optim->v, opt.state = optim->state;
+    opt.grads = d_grads;
+    const int64_t* o = leaf_offsets;
+    auto add = [](AdamWRanges& r, int64_t b, int64_t e) {
+      r.begin[r.n] = b;
+      r.len4[r.n] = (e - b + 3) / 4;  // into the leaf's padding (zeros: AdamW keeps them)
+      ++r.n;
+    };
+    // table leaves (final after the table sums) and the dense ones; the
+    // tactical table's constant zero (its last element) is not a parameter
+    add(opt.table, o[L_TE], o[L_VTO]);
+    add(opt.table, o[L_MB], o[L_CONS]);
+    add(opt.table, o[L_MC], o[L_PAH]);
+    add(opt.table, o[L_AM], o[L_TACT] + kTactLen - 1);
+    add(opt.dense, 0, o[L_TE]);
+    add(opt.dense, o[L_VTO], o[L_MB]);
+    add(opt.dense, o[L_CONS], o[L_MC]);
+    add(opt.dense, o[L_PAH], o[L_AM]);
+    if (o[L_FT] != 0 || ((o[L_TACT] + kTactLen - 1) & 3))
+      return set_error(CNNUE_ERR_INVALID_ARG, "cnnue_azt_step: the optimizer needs the trunk table first and the "
+                       "tactical table ending on a 4-element boundary");
+  }
+  const Optim* op = optim ? &opt : nullptr;
   switch (hidden) {
-    case 32: return launch_main<1>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
-    case 64: return launch_main<2>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
-    case 128: return launch_main<4>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
-    case 256: return launch_main<8>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
-    default: return launch_main<16>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, s, side, e ? e->join : nullptr);
+    case 32: return launch_main<1>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, streams, op);
+    case 64: return launch_main<2>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, streams, op);
+    case 128: return launch_main<4>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, streams, op);
+    case 256: return launch_main<8>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, streams, op);
+    default: return launch_main<16>(P, G, A, bt, cb, srt, ls, raw, d_status, d_metrics, streams, op);
   }
 }
 

@@ -24,6 +24,19 @@ int cuda_error(cudaError_t err, const char* what);
 
 // Maps a kernel status word (CNNUE_STATUS_* bits) to a CNNUE_ERR_* code and
 // records the detail as the thread's last error.
+// AdamW on the device state (cnnue_adamw_state, optim.cu): the step's
+// scalars once (advances the step), then any number of updates of disjoint
+// ranges of the flat buffers with them (float4 groups, 16-byte aligned).
+constexpr int kMaxAdamRanges = 8;
+struct AdamWRanges {
+  int64_t begin[kMaxAdamRanges];  // element offsets, multiples of 4
+  int64_t len4[kMaxAdamRanges];   // lengths in float4 groups
+  int n;
+};
+int adamw_prepare(cnnue_adamw_state* d_state, cudaStream_t s);
+int adamw_ranges(float* d_params, float* d_m, float* d_v, const float* d_grads, const AdamWRanges& r,
+                 const cnnue_adamw_state* d_state, cudaStream_t s);
+
 int status_from_word(uint32_t word);
 
 // Checks that `device` is the current device, switching to it if needed.

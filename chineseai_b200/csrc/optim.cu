@@ -152,8 +152,56 @@ int launch_adamw(float* d_params, float* d_m, float* d_v, const float* d_grads, 
   return CNNUE_OK;
 }
 
+// AdamW over up to kMaxRanges disjoint ranges of a flat buffer in one launch
+// (device-state scalars, scale 1): the ranges' float4 groups are one index
+// space; ranges start and end on 4-element boundaries.
+__global__ void __launch_bounds__(256) adamw_ranges_kernel(float* __restrict__ p, float* __restrict__ m,
+                                                           float* __restrict__ v, const float* __restrict__ g,
+                                                           AdamWRanges r, const AdamWScalars* kd) {
+  const AdamWScalars k = *kd;
+  int64_t total = 0;
+  for (int j = 0; j < r.n; ++j) total += r.len4[j];
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t q = i;
+    int j = 0;
+    while (j + 1 < r.n && q >= r.len4[j]) q -= r.len4[j++];
+    const int64_t e = r.begin[j] + 4 * q;
+    float4 pp = *(float4*)(p + e), mm = *(float4*)(m + e), vv = *(float4*)(v + e);
+    const float4 gg = __ldg((const float4*)(g + e));
+    adamw_one(pp.x, mm.x, vv.x, gg.x, k);
+    adamw_one(pp.y, mm.y, vv.y, gg.y, k);
+    adamw_one(pp.z, mm.z, vv.z, gg.z, k);
+    adamw_one(pp.w, mm.w, vv.w, gg.w, k);
+    *(float4*)(p + e) = pp;
+    *(float4*)(m + e) = mm;
+    *(float4*)(v + e) = vv;
+  }
+}
+
 }  // namespace
 }  // namespace opt
+
+int adamw_prepare(cnnue_adamw_state* d_state, cudaStream_t s) {
+  opt::adamw_prepare_kernel<<<1, 1, 0, s>>>(d_state, nullptr, 0);
+  return check_launch_error("adamw_prepare_kernel");
+}
+
+int adamw_ranges(float* d_params, float* d_m, float* d_v, const float* d_grads, const AdamWRanges& r,
+                 const cnnue_adamw_state* d_state, cudaStream_t s) {
+  int64_t total = 0;
+  for (int j = 0; j < r.n; ++j) {
+    if ((r.begin[j] & 3) || r.len4[j] < 0) return set_error(CNNUE_ERR_INVALID_ARG, "adamw range not aligned");
+    total += r.len4[j];
+  }
+  if (total == 0) return CNNUE_OK;
+  if (((uintptr_t)d_params | (uintptr_t)d_m | (uintptr_t)d_v | (uintptr_t)d_grads) & 15)
+    return set_error(CNNUE_ERR_INVALID_ARG, "adamw buffers not 16-byte aligned");
+  const unsigned blocks = (unsigned)std::min<int64_t>((total + 255) / 256, 148 * 8);
+  opt::adamw_ranges_kernel<<<blocks, 256, 0, s>>>(d_params, d_m, d_v, d_grads, r,
+                                                   (const opt::AdamWScalars*)d_state->scalars);
+  return check_launch_error("adamw_ranges_kernel");
+}
+
 }  // namespace cnnue
 
 using namespace cnnue;

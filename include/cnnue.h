@@ -642,10 +642,20 @@ int cnnue_azt_create(int device, cnnue_azt** out);
 int cnnue_azt_destroy(cnnue_azt* engine);
 /* Workspace of one step (0 for unsupported dims); 256-byte aligned. */
 size_t cnnue_azt_workspace_bytes(int64_t hidden, int64_t batch, int64_t features, int64_t moves, int64_t threats);
+/* Optional AdamW inside the step (single GPU): params must be d_params (then
+ * updated in place), m / v the moments in the same layout, state the device
+ * state of cnnue_adamw_device; the leaves must be in the order above from
+ * offset 0.  The table leaves are updated while the dense gradients finish. */
+typedef struct cnnue_azt_optim {
+  float* params;
+  float* m;
+  float* v;
+  cnnue_adamw_state* state;
+} cnnue_azt_optim;
 int cnnue_azt_step(cnnue_azt* engine, const float* d_params, float* d_grads, int64_t n_grads,
                    const int64_t* leaf_offsets, int64_t hidden, const cnnue_azt_batch* batch, float value_weight,
                    float policy_weight, float* d_metrics, uint32_t* d_status, void* d_ws, size_t ws_bytes,
-                   void* stream);
+                   const cnnue_azt_optim* optim, void* stream);
 
 /* Per-move records for the policy logits (the per-move inputs of
  * evaluate_prepared_hidden_with_context, src/az.rs:1766-1887), side to move

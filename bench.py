@@ -827,12 +827,13 @@ def run_fp32(args):
                        "l2": "flushed (256 MiB write) before each timed step"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": None,
+                         "kernel": "f_fused_kernel",
                          "scope": "whole forward (one kernel): gathered fp32 rows, indices, offsets, outputs, "
                                   "stack weights once; the 11.6 MB table is L2-resident after the first rows"},
             "e2e": {"value": world * F32_BATCH / (e2e_total / args.steps / 1e3), "unit": "evals/s",
                     "h2d_bytes_per_step": int(pos.indices.nbytes + pos.offsets.nbytes),
                     "d2h_bytes_per_step": F32_BATCH * 4},
-            "clocks": clocks, "gpu_launches": 2 * args.steps,  # f_gather_kernel + f_stack_kernel
+            "clocks": clocks, "gpu_launches": args.steps,  # f_fused_kernel
         }
         if not args.no_cpu_baseline:
             import oracle

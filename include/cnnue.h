@@ -254,8 +254,9 @@ typedef struct cnnue_f_weights {
 typedef struct cnnue_f_model cnnue_f_model;
 int cnnue_f_model_create(const cnnue_f_weights* weights, int device, cnnue_f_model** out);
 int cnnue_f_model_destroy(cnnue_f_model* model);
-/* Workspace of cnnue_f_forward for n positions: the status word and the
- * clipped FT outputs [n][512] fp32. */
+/* Workspace of cnnue_f_forward for n positions: the 512-byte header (status
+ * word and the kernel's counters, cleared by each call), the clipped FT
+ * outputs [n][512] fp32 and the per-bucket position lists [8][n]. */
 size_t cnnue_f_workspace_bytes(int64_t n_positions);
 /* fp32 forward: FT sum (bias + rows in index order), clipped ReLU [0,1] on the
  * concatenated 512, bucket = (n0-1)/4 (8 buckets), stack 512->16->32->1 with

@@ -27,7 +27,7 @@ def test_golden(fmodel):
     np.testing.assert_allclose(out, g["f_out"], rtol=RTOL, atol=ATOL)
 
 
-@pytest.mark.parametrize("n,seed", [(1, 2), (100, 3), (4096, 1)])
+@pytest.mark.parametrize("n,seed", [(1, 2), (100, 3), (4096, 1), (140_000, 5)])
 def test_random(fmodel, fweights, n, seed):
     pos = synth.positions(n, seed)
     out = fmodel.forward_positions(pos)

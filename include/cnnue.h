@@ -193,10 +193,12 @@ int cnnue_q_ctx_wait(cnnue_q_stream_ctx* ctx, uint64_t ticket, int* status);
  *     are rejected with CNNUE_ERR_INVALID_ARG (split them, or use
  *     cnnue_q_forward with a workspace).
  *   - The first call on a device looks up the scratch array's device address
- *     (once per device, with that device current); make that first call
- *     before any stream capture.  The address is kept for the life of the
- *     process: after cudaDeviceReset on that device the entry point must not
- *     be called again.
+ *     (once per device, with that device current).  The address is kept for
+ *     the life of the process: after cudaDeviceReset on that device the
+ *     entry point must not be called again.
+ *   - The call synchronises its stream to read the kernels' status, so it
+ *     cannot be captured into a CUDA graph (use cnnue_q_forward with a
+ *     workspace inside a capture).
  *   - Every call on a device shares the one scratch array, which keeps the
  *     previous call's contents; each call clears the part that must start at
  *     zero.  Calls whose GPU work overlaps (other threads, other streams)

@@ -778,6 +778,7 @@ __device__ __forceinline__ void ring_advance(ConsumerRing& r) {
 template <int kSR, int kNS>
 __device__ __forceinline__ void consume_list_fast(ConsumerRing& r, volatile int* abort, uint32_t cnt, int lane,
                                                   uint32_t* status, unsigned long long wait_ns, uint4& acc) {
+  static_assert((kSR & (kSR - 1)) == 0, "the tree of adds of a full stage needs a power-of-two stage");
   for (uint32_t first = 0; first < cnt; first += kSR) {
     const uint32_t rows = min((uint32_t)kSR, cnt - first);
     pipe::mbar_wait_addr(r.full, r.phase, abort, status, wait_ns);
@@ -955,10 +956,15 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 
 // ===========================================================================
 // Split evaluation, kernel 1 of 2: gather + pack.  Same ring protocol as the
-// fused kernel, on 6 stages x 4 rows per CTA and 4 CTAs per SM (measured per
-// 65,536 positions, gather + stacks: 0.486 ms with 12 x 4 rows and 2 CTAs per
-// SM, 0.404 with 8 x 4 and 3, 0.381 with 6 x 4 and 4, 0.406 with 4 x 4 and 5;
-// 4 producer warps per CTA beat 2, 3, 5, 6 and 8).  The four consumer warps own the 16-byte column chunks so that a
+// fused kernel, on 3 stages x 8 rows per CTA, 4 CTAs per SM and 3 producer
+// warps.  Every consumer warp waits on and releases every stage, so the ring's
+// handshakes cost instruction issue per stage: 8-row stages halve them per
+// row.  Measured per 65,536 positions with the L2 flushed (forward incl. the
+// bucket sort and stacks / update): 4 x 6 rows, 4 CTAs, 4 producers 358.5 /
+// 295.6 us; 8 x 3, 4, 3: 329.6 / 295.1 us; 8 x 3, 3, 3: 327.7 / 316.0 us;
+// 8 x 4, 3, 4: 334.1 / 302.9 us; 8 x 3, 4, 2: 389.9 / 294.0 us; 16-row
+// stages 453-455 / 518-592 us.  (Among 4-row rings, 12 x 4 with 2 CTAs per
+// SM, 8 x 4 with 3 and 4 x 4 with 5 were slower than 6 x 4 with 4.)  The four consumer warps own the 16-byte column chunks so that a
 // chunk's pack partner (columns j and j + 512) sits in the same warp: lane
 // l < 16 of warp w owns chunk 16w + l, lane l + 16 owns chunk 64 + 16w + l.
 // After a position's two perspectives are summed, partner lanes swap one
@@ -971,10 +977,10 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 // barrier joins the consumer warps; the bucket stacks run in kernel 2 over
 // the packed rows.
 // ===========================================================================
-constexpr int kGRows = 4;
-constexpr int kGStages = 6;
+constexpr int kGRows = 8;
+constexpr int kGStages = 3;
 constexpr int kGMinBlocks = 4;  // CTAs per SM (ring 48 KB each)
-constexpr int kGProducersEval = 4;
+constexpr int kGProducersEval = 3;
 constexpr int kGProducersUpdate = 2;
 constexpr int gproducers_of(bool update) { return update ? kGProducersUpdate : kGProducersEval; }
 constexpr int gather_threads(bool update) { return kBulkConsumers + 32 * gproducers_of(update); }

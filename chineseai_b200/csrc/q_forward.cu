@@ -804,6 +804,50 @@ __device__ __forceinline__ void consume_list_fast(ConsumerRing& r, volatile int*
   }
 }
 
+// Adds the rows of one forward list into two accumulators: the thread's
+// 16 bytes of every row at the ring slot (column chunk c) and 1 KB further
+// (chunk c + 64, its pack partner).
+template <int kSR, int kNS>
+__device__ __forceinline__ void consume_list_fast2(ConsumerRing& r, volatile int* abort, uint32_t cnt, int lane,
+                                                   uint32_t* status, unsigned long long wait_ns, uint4& acc_lo,
+                                                   uint4& acc_hi) {
+  static_assert((kSR & (kSR - 1)) == 0, "the tree of adds of a full stage needs a power-of-two stage");
+  for (uint32_t first = 0; first < cnt; first += kSR) {
+    const uint32_t rows = min((uint32_t)kSR, cnt - first);
+    pipe::mbar_wait_addr(r.full, r.phase, abort, status, wait_ns);
+    if (rows == (uint32_t)kSR) {
+      uint4 v[kSR];
+#pragma unroll
+      for (int j = 0; j < kSR; ++j) v[j] = pipe::lds128(r.slot + j * kRowBytes);
+#pragma unroll
+      for (int h = kSR / 2; h >= 1; h /= 2)
+#pragma unroll
+        for (int j = 0; j < h; ++j) v[j] = vadd(v[j], v[j + h]);
+      acc_lo = vadd(acc_lo, v[0]);
+#pragma unroll
+      for (int j = 0; j < kSR; ++j) v[j] = pipe::lds128(r.slot + 1024 + j * kRowBytes);
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive_addr(r.empty);
+#pragma unroll
+      for (int h = kSR / 2; h >= 1; h /= 2)
+#pragma unroll
+        for (int j = 0; j < h; ++j) v[j] = vadd(v[j], v[j + h]);
+      acc_hi = vadd(acc_hi, v[0]);
+    } else {
+      uint4 s = pipe::lds128(r.slot), t = pipe::lds128(r.slot + 1024);
+      for (uint32_t j = 1; j < rows; ++j) {
+        s = vadd(s, pipe::lds128(r.slot + j * kRowBytes));
+        t = vadd(t, pipe::lds128(r.slot + 1024 + j * kRowBytes));
+      }
+      __syncwarp();
+      if (lane == 0) pipe::mbar_arrive_addr(r.empty);
+      acc_lo = vadd(acc_lo, s);
+      acc_hi = vadd(acc_hi, t);
+    }
+    ring_advance<kSR, kNS>(r);
+  }
+}
+
 template <bool kUpdate, bool kWriteAcc>
 __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_kernel(const ForwardArgs a) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -959,19 +1003,23 @@ __global__ void __launch_bounds__(bulk_threads(kUpdate), kBulkMinBlocks) q_bulk_
 // fused kernel, on 3 stages x 8 rows per CTA, 4 CTAs per SM and 3 producer
 // warps.  Every consumer warp waits on and releases every stage, so the ring's
 // handshakes cost instruction issue per stage: 8-row stages halve them per
-// row.  Measured per 65,536 positions with the L2 flushed (forward incl. the
+// row, and the forward runs two consumer warps whose lanes own two 16-byte
+// chunks of every row (gather_forward_consumer; 331 -> 312 us per 65,536
+// positions), the update four.  Measured per 65,536 positions with the L2 flushed (forward incl. the
 // bucket sort and stacks / update): 4 x 6 rows, 4 CTAs, 4 producers 358.5 /
 // 295.6 us; 8 x 3, 4, 3: 329.6 / 295.1 us; 8 x 3, 3, 3: 327.7 / 316.0 us;
 // 8 x 4, 3, 4: 334.1 / 302.9 us; 8 x 3, 4, 2: 389.9 / 294.0 us; 16-row
 // stages 453-455 / 518-592 us.  (Among 4-row rings, 12 x 4 with 2 CTAs per
-// SM, 8 x 4 with 3 and 4 x 4 with 5 were slower than 6 x 4 with 4.)  The four consumer warps own the 16-byte column chunks so that a
+// SM, 8 x 4 with 3 and 4 x 4 with 5 were slower than 6 x 4 with 4.)  In the
+// update, the four consumer warps own the 16-byte column chunks so that a
 // chunk's pack partner (columns j and j + 512) sits in the same warp: lane
 // l < 16 of warp w owns chunk 16w + l, lane l + 16 owns chunk 64 + 16w + l.
 // After a position's two perspectives are summed, partner lanes swap one
 // perspective's chunk with a single 16-byte shuffle exchange, lane l < 16
 // packs perspective 0 and lane l + 16 perspective 1, and each lane stores its
-// 8 packed bytes: 1024 uint8 per position, written at the position's sorted
-// slot.  The CTAs walk positions in batch order (a CTA's index lists are
+// 8 packed bytes (in the forward a lane holds both chunks of a pair and packs
+// both perspectives itself): 1024 uint8 per position, written at the
+// position's sorted slot.  The CTAs walk positions in batch order (a CTA's index lists are
 // contiguous, which the producers' per-stage index loads find in L1; the
 // sorted order scatters them and measured ~110 us slower per 65,536).  No
 // barrier joins the consumer warps; the bucket stacks run in kernel 2 over
@@ -983,7 +1031,10 @@ constexpr int kGMinBlocks = 4;  // CTAs per SM (ring 48 KB each)
 constexpr int kGProducersEval = 3;
 constexpr int kGProducersUpdate = 2;
 constexpr int gproducers_of(bool update) { return update ? kGProducersUpdate : kGProducersEval; }
-constexpr int gather_threads(bool update) { return kBulkConsumers + 32 * gproducers_of(update); }
+// consumer warps: two in the forward (lane l of warp w owns column chunks
+// 32w + l and its pack partner 32w + l + 64), four in the update
+constexpr int gconsumers_of(bool update) { return update ? 4 : 2; }
+constexpr int gather_threads(bool update) { return 32 * gconsumers_of(update) + 32 * gproducers_of(update); }
 
 struct GatherSmem {
   uint8_t ring[kGRows * kGStages][kRowBytes];
@@ -992,6 +1043,61 @@ struct GatherSmem {
   uint32_t issued[kGStages];
   int abort;
 };
+
+// Forward consumers of the gather (two warps): lane l of warp w owns column
+// chunk c = 32w + l (columns [8c, 8c + 8)) and its pack partner c + 64
+// (columns j + 512) of every row, so each stage costs a warp one wait and one
+// release for 2 x 8 rows of 16 bytes, and the pack needs no exchange: lane l
+// packs both perspectives of chunk c and stores 8 bytes of each.
+template <bool kWriteAcc>
+__device__ __forceinline__ void gather_forward_consumer(GatherSmem& sm, const ForwardArgs& a, int64_t begin,
+                                                        int64_t end, int warp, int lane) {
+  const int c = 32 * warp + lane;
+  const uint4 bias_lo = __ldg((const uint4*)((const char*)a.w.bias + c * 16));
+  const uint4 bias_hi = __ldg((const uint4*)((const char*)a.w.bias + (c + 64) * 16));
+  ConsumerRing ring{pipe::smem_addr(&sm.full[0]), pipe::smem_addr(&sm.empty[0]),
+                    pipe::smem_addr(&sm.ring[0][0]) + (uint32_t)(c * 16), 0u, 0u};
+  PosDesc nxt;
+  if (begin < end) nxt = finish_desc<false>(a, load_raw<false>(a, (uint32_t)begin, 0));
+  // launched as a programmatic dependent of the bucket sort's scatter: the
+  // inverse order (written by it) is complete and visible only after this
+  // wait; the producers read only the batch's lists and never wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  uint32_t slot_n = begin < end ? a.inv[begin] : 0u;  // sorted slot of the next position
+  for (int64_t i = begin; i < end; ++i) {
+    const PosDesc d = nxt;
+    const uint32_t slot = slot_n;
+    const bool has_next = i + 1 < end;
+    RawDesc raw;
+    if (has_next) {
+      raw = load_raw<false>(a, (uint32_t)(i + 1), 0);
+      slot_n = a.inv[i + 1];
+    }
+    uint4 lo[2], hi[2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      lo[p] = bias_lo;
+      hi[p] = bias_hi;
+      consume_list_fast2<kGRows, kGStages>(ring, &sm.abort, d.add[p].cnt, lane, a.status, a.wait_ns, lo[p], hi[p]);
+    }
+    if (kWriteAcc) {
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        char* row = (char*)(a.acc_out + (2 * (int64_t)d.pos + p) * kCols);
+        *(uint4*)(row + c * 16) = lo[p];
+        *(uint4*)(row + (c + 64) * 16) = hi[p];
+      }
+    }
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      uint2 out;
+      out.x = pack_quad(lo[p].x, hi[p].x, lo[p].y, hi[p].y);
+      out.y = pack_quad(lo[p].z, hi[p].z, lo[p].w, hi[p].w);
+      *(uint2*)(a.packed + (size_t)slot * CNNUE_Q_PACKED + (p ? CNNUE_Q_HALF : 0) + 8 * c) = out;
+    }
+    if (has_next) nxt = finish_desc<false>(a, raw);
+  }
+}
 
 template <bool kUpdate, bool kWriteAcc>
 __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather_kernel(const ForwardArgs a) {
@@ -1005,7 +1111,7 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGStages; ++s) {
       pipe::mbar_init(&sm.full[s], 1);
-      pipe::mbar_init(&sm.empty[s], kBulkConsumers / 32);
+      pipe::mbar_init(&sm.empty[s], gconsumers_of(kUpdate));
       sm.issued[s] = 0xffffffffu;
     }
     sm.abort = 0;
@@ -1016,12 +1122,16 @@ __global__ void __launch_bounds__(gather_threads(kUpdate), kGMinBlocks) q_gather
   const int64_t begin = a.n * blockIdx.x / gridDim.x;
   const int64_t end = a.n * (blockIdx.x + 1) / gridDim.x;
 
-  if (warp >= kBulkConsumers / 32) {
+  if (warp >= gconsumers_of(kUpdate)) {
     if (kUpdate)
-      produce<true, gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32, lane);
+      produce<true, gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - gconsumers_of(kUpdate), lane);
     else
-      produce_forward_fast<gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - kBulkConsumers / 32,
+      produce_forward_fast<gproducers_of(kUpdate), kGRows, kGStages>(sm, a, begin, end, warp - gconsumers_of(kUpdate),
                                                                      lane);
+    return;
+  }
+  if (!kUpdate) {
+    gather_forward_consumer<kWriteAcc>(sm, a, begin, end, warp, lane);
     return;
   }
 

@@ -63,6 +63,10 @@ def test_workspace_sizes():
     assert 512 < a < b
     assert b >= 65536 * 6
     assert lib.cnnue_feature_pool_bwd_workspace_bytes(1024, 32, 128) > 1024 * 32 * 6 * 4
+    # fp32 forward: the 512-byte header, the clipped FT outputs [n][512] fp32
+    # and the bucket lists [8][n] u32
+    for n in (1, 4096, 140_000):
+        assert lib.cnnue_f_workspace_bytes(n) >= 512 + n * 512 * 4 + 8 * n * 4
 
 
 def test_splitmix64_matches_reference_definition():

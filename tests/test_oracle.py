@@ -166,6 +166,22 @@ def test_f_oracle(golden, fweights):
     np.testing.assert_allclose(out, ref, rtol=1e-4, atol=1e-6)
 
 
+def test_f_oracle_ft_sums_follow_the_scalar_order(fweights):
+    """The fp32 FT sums are bias first, then every row in index order, one
+    float32 add each: the order the GPU kernel keeps bit for bit."""
+    pos = synth.positions(64, 9)
+    st, _, acc = oracle.f_forward(fweights, pos, with_acc=True)
+    assert st == 0
+    acc = np.asarray(acc, np.float32).reshape(pos.n, 2, 256)
+    ft = np.asarray(fweights.ft_weight, np.float32)
+    for q in range(pos.n):
+        for p in range(2):
+            s = np.asarray(fweights.ft_bias, np.float32).copy()
+            for f in pos.indices[pos.offsets[2 * q + p]:pos.offsets[2 * q + p + 1]]:
+                s = (s + ft[int(f)]).astype(np.float32)
+            np.testing.assert_array_equal(acc[q, p], s)
+
+
 def test_feature_pool_oracle_on_reference_fixture(golden):
     from tests.golden.make_golden import pool_fixture
     tables, items = pool_fixture()
